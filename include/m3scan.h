@@ -1,0 +1,150 @@
+/*
+ * m3scan.h - C ABI of the B200 (sm_100a) Mamba-3 trapezoidal selective scan.
+ *
+ * Drop-in kernels for the hot path of PranavPrasannaV/RedPanda's Mamba-3
+ * backbone.  Every entry point takes plain device pointers, sizes and a CUDA
+ * stream (passed as void*), returns 0 or an M3_ERR_* code, never throws,
+ * never allocates and never frees: the caller owns every input, output and
+ * workspace buffer.  All pointers are device pointers to dense, row-major
+ * (contiguous) tensors.
+ *
+ * Interface map (reference file:line -> entry point):
+ *   redpanda/engine/triton_scan.py:248-281  _TrapezoidalScanFn.forward  -> m3_scan_fwd
+ *   redpanda/engine/triton_scan.py:283-315  _TrapezoidalScanFn.backward -> m3_scan_bwd
+ *   redpanda/engine/mamba.py:254-260        bidirectional scan pair     -> m3_scan_fwd/bwd with
+ *                                                                          M3_DIR_BIDIR
+ *   redpanda/engine/mamba.py:343,377-379    return_state (h_last, dBu_last) -> m3_scan_fwd h_last/dbu_last
+ *   redpanda/engine/mamba.py:466-493        Mamba3Block.step recurrence -> m3_step
+ *
+ * Shapes (B batch, L length, D = d_inner, N = d_state, n_rot rotational lanes,
+ * N - n_rot tracking lanes):
+ *   delta, u            (B, L, D)  dtype_du  (post-softplus delta, SSM input)
+ *   Bc, Cc              (B, L, N)  dtype_bc  (MIMO-contracted, BCNorm'ed B and C)
+ *   A_real_p, A_imag_p  (D, N)     float32   rotational eigenvalues in columns
+ *                                            [0, n_rot), zero elsewhere
+ *   track_p             (D, N)     float32   tanh(theta) in columns [n_rot, N)
+ *   (the padded parameter layout of triton_scan.py:325-335)
+ *   y                   (B, L, D)  float32   scan output WITHOUT the u*D skip
+ */
+#ifndef M3SCAN_H
+#define M3SCAN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define M3_API __attribute__((visibility("default")))
+#else
+#define M3_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+enum { M3_F32 = 0, M3_BF16 = 1 };
+
+/* scan directions.  M3_DIR_REV scans the sequence back to front, which equals
+ * flip(scan(flip(x))) of the reference (mamba.py:258-260); M3_DIR_BIDIR writes
+ * y_fwd + y_rev in one launch. */
+enum { M3_DIR_FWD = 0, M3_DIR_REV = 1, M3_DIR_BIDIR = 2 };
+
+/* status codes */
+enum {
+  M3_OK = 0,
+  M3_ERR_NULL = 1,         /* a required pointer is NULL */
+  M3_ERR_SHAPE = 2,        /* a size is out of range */
+  M3_ERR_DTYPE = 3,        /* unsupported element type */
+  M3_ERR_UNSUPPORTED = 4,  /* no kernel for this (d_state, n_rot) split */
+  M3_ERR_ALIGN = 5,        /* a pointer is not aligned to its element size */
+  M3_ERR_WORKSPACE = 6,    /* workspace missing or too small */
+  M3_ERR_LAUNCH = 7,       /* the CUDA launch failed (see cudaGetLastError) */
+  M3_ERR_DEVICE = 8,       /* a kernel recorded a device-side error */
+  M3_ERR_NO_DEVICE = 9     /* no CUDA device / the current device is not sm_100 */
+};
+
+typedef struct m3_scan_desc {
+  int32_t batch;      /* B >= 1 */
+  int32_t seqlen;     /* L >= 1 */
+  int32_t d_inner;    /* D >= 1 */
+  int32_t d_state;    /* N, 1..128 */
+  int32_t n_rot;      /* 0..N rotational lanes; N - n_rot tracking lanes */
+  int32_t dtype_du;   /* element type of delta and u (M3_F32 or M3_BF16) */
+  int32_t dtype_bc;   /* element type of Bc and Cc */
+  int32_t direction;  /* M3_DIR_FWD, M3_DIR_REV or M3_DIR_BIDIR */
+} m3_scan_desc;
+
+typedef struct m3_step_desc {
+  int32_t batch;      /* rows advanced in lockstep */
+  int32_t d_inner;
+  int32_t d_state;
+  int32_t n_rot;
+  int32_t dtype_du;
+  int32_t dtype_bc;
+} m3_step_desc;
+
+/* Human-readable text of a status code (static storage). */
+M3_API const char* m3_strerror(int code);
+
+/* ABI version: (major << 16) | minor. */
+M3_API int m3_version(void);
+
+/* Number of float32 elements of the forward checkpoint buffer the backward
+ * consumes (0 when L <= 16).  Replaces the hck/dck chunk checkpoints that
+ * triton_scan.py:261-262 allocates. */
+M3_API size_t m3_scan_ckpt_floats(const m3_scan_desc* desc);
+
+/* Forward scan.  Replaces _TrapezoidalScanFn.forward (triton_scan.py:248-281)
+ * and the return_state branch of _selective_scan_trapezoidal (mamba.py:377-379).
+ *   y         required, (B, L, D) float32
+ *   ckpt      optional (NULL = inference only); m3_scan_ckpt_floats() floats,
+ *             to be handed to m3_scan_bwd
+ *   h_last,   optional, (B, D, N) float32: state after the last token of the
+ *   dbu_last  scan direction (M3_DIR_FWD or M3_DIR_REV only) */
+M3_API int m3_scan_fwd(const m3_scan_desc* desc,
+                const void* delta, const void* u, const void* Bc, const void* Cc,
+                const float* A_real_p, const float* A_imag_p, const float* track_p,
+                float* y, float* ckpt, float* h_last, float* dbu_last,
+                void* stream);
+
+/* Workspace bytes m3_scan_bwd needs on the current device. */
+M3_API size_t m3_scan_bwd_workspace_bytes(const m3_scan_desc* desc);
+
+/* Analytic backward.  Replaces _TrapezoidalScanFn.backward
+ * (triton_scan.py:283-315) with deterministic reductions (no atomics).
+ *   dy        (B, L, D) of dtype_dy, the gradient of y
+ *   ckpt      the forward's checkpoint buffer (NULL allowed when L <= 16)
+ *   d_delta, d_u   (B, L, D) of dtype_du
+ *   d_Bc, d_Cc     (B, L, N) of dtype_bc
+ *   d_A_real_p, d_A_imag_p, d_track_p   (D, N) float32 in the padded layout
+ *   workspace      >= m3_scan_bwd_workspace_bytes(desc) bytes */
+M3_API int m3_scan_bwd(const m3_scan_desc* desc,
+                const void* delta, const void* u, const void* Bc, const void* Cc,
+                const float* A_real_p, const float* A_imag_p, const float* track_p,
+                const void* dy, int32_t dtype_dy, const float* ckpt,
+                void* d_delta, void* d_u, void* d_Bc, void* d_Cc,
+                float* d_A_real_p, float* d_A_imag_p, float* d_track_p,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/* O(1) recurrent step of B rows, in place.  Replaces the recurrence of
+ * Mamba3Block.step (mamba.py:466-493):
+ *   h, dbu    (B, D, N) float32, read and overwritten with the new state
+ *   delta, u  (B, D) of dtype_du;  Bc, Cc  (B, N) of dtype_bc
+ *   y         (B, D) float32, sum_n h*C without the u*D skip
+ * Bit-identical to m3_scan_fwd (M3_DIR_FWD) at every position when fed the
+ * same per-token inputs and the scan's state. */
+M3_API int m3_step(const m3_step_desc* desc, float* h, float* dbu,
+            const void* delta, const void* u, const void* Bc, const void* Cc,
+            const float* A_real_p, const float* A_imag_p, const float* track_p,
+            float* y, void* stream);
+
+/* Reads (and clears when clear != 0) the device-side error word of the
+ * current device; *code receives 0 or an M3_ERR_* value. */
+M3_API int m3_device_error(int32_t* code, int32_t clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M3SCAN_H */

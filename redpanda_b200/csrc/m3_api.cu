@@ -1,0 +1,297 @@
+// C ABI of the scan library: argument validation, tile selection, workspace
+// layout and kernel dispatch.  No allocation, no exceptions, no host sync.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "m3_common.cuh"
+#include "m3_internal.h"
+#include "m3_tiles.h"
+#include "m3scan.h"
+
+namespace m3 {
+
+__device__ int g_err_word = 0;
+
+int* device_err_ptr() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_err_word) != cudaSuccess) return nullptr;
+  return static_cast<int*>(p);
+}
+
+bool select_tile(int n_rot, int n_track, Tile* out) {
+  const int rr = (n_rot + 3) / 4, tt = (n_track + 3) / 4;
+  static const Tile kTiles[] = {
+#define M3_X(r, t, nd) {r, t, nd},
+      M3_TILE_LIST(M3_X)
+#undef M3_X
+  };
+  const Tile* best = nullptr;
+  for (const Tile& t : kTiles) {
+    if (t.R == rr && t.T == tt) { *out = t; return true; }
+  }
+  for (const Tile& t : kTiles) {
+    if (t.R >= rr && t.T >= tt && (!best || t.R + t.T < best->R + best->T)) best = &t;
+  }
+  if (!best) return false;
+  *out = *best;
+  return true;
+}
+
+namespace {
+
+constexpr int kMaxState = 128;
+
+int device_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  return sms;
+}
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return M3_ERR_NO_DEVICE; }
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return M3_ERR_NO_DEVICE;
+  }
+  return major == 10 ? M3_OK : M3_ERR_NO_DEVICE;
+}
+
+bool dtype_ok(int dt) { return dt == M3_F32 || dt == M3_BF16; }
+int dsize(int dt) { return dt == M3_BF16 ? 2 : 4; }
+bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_scan_desc(const m3_scan_desc* d, Tile* tile) {
+  if (!d) return M3_ERR_NULL;
+  if (d->batch < 1 || d->seqlen < 1 || d->d_inner < 1 || d->d_state < 1 ||
+      d->d_state > kMaxState || d->n_rot < 0 || d->n_rot > d->d_state)
+    return M3_ERR_SHAPE;
+  if (!dtype_ok(d->dtype_du) || !dtype_ok(d->dtype_bc)) return M3_ERR_DTYPE;
+  if (d->direction < M3_DIR_FWD || d->direction > M3_DIR_BIDIR) return M3_ERR_SHAPE;
+  if (!select_tile(d->n_rot, d->d_state - d->n_rot, tile)) return M3_ERR_UNSUPPORTED;
+  const long long g = (d->d_inner + tile->dt() - 1) / tile->dt();
+  if (g > 65535) return M3_ERR_SHAPE;
+  return M3_OK;
+}
+
+int nchunks(int L) { return (L + kCK - 1) / kCK; }
+
+size_t ckpt_floats(const m3_scan_desc* d, const Tile& t) {
+  const int nch = nchunks(d->seqlen);
+  if (nch <= 1) return 0;
+  const size_t ndirs = d->direction == M3_DIR_BIDIR ? 2 : 1;
+  return (size_t)d->batch * ndirs * (nch - 1) * d->d_inner * t.np();
+}
+
+struct BwdLayout {
+  int G, Bg;
+  size_t off_a, off_bc, off_du, total;
+};
+
+size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+bool bwd_layout(const m3_scan_desc* d, const Tile& t, BwdLayout* lay) {
+  const int sms = device_sms();
+  if (sms <= 0) return false;
+  lay->G = (d->d_inner + t.dt() - 1) / t.dt();
+  int bg = lay->G >= sms ? 1 : sms / lay->G;
+  if (bg > d->batch) bg = d->batch;
+  if (bg < 1) bg = 1;
+  lay->Bg = bg;
+  const size_t np = t.np();
+  const size_t a_bytes = (size_t)lay->Bg * 3 * d->d_inner * np * 4;
+  const size_t bc_bytes = (size_t)lay->G * d->batch * d->seqlen * 2 * np * 4;
+  const size_t du_bytes = d->direction == M3_DIR_BIDIR
+                              ? (size_t)lay->G * lay->Bg * d->seqlen * t.dt() * 2 * 4
+                              : 0;
+  lay->off_a = 0;
+  lay->off_bc = round256(a_bytes);
+  lay->off_du = lay->off_bc + round256(bc_bytes);
+  lay->total = lay->off_du + round256(du_bytes);
+  return true;
+}
+
+}  // namespace
+}  // namespace m3
+
+using namespace m3;
+
+extern "C" {
+
+const char* m3_strerror(int code) {
+  switch (code) {
+    case M3_OK: return "ok";
+    case M3_ERR_NULL: return "m3: a required pointer is NULL";
+    case M3_ERR_SHAPE: return "m3: a size argument is out of range";
+    case M3_ERR_DTYPE: return "m3: unsupported element type (float32 or bfloat16 only)";
+    case M3_ERR_UNSUPPORTED: return "m3: no compiled kernel for this (d_state, n_rot) split";
+    case M3_ERR_ALIGN: return "m3: a pointer is not aligned to its element size";
+    case M3_ERR_WORKSPACE: return "m3: workspace missing or too small";
+    case M3_ERR_LAUNCH: return "m3: CUDA kernel launch failed";
+    case M3_ERR_DEVICE: return "m3: a kernel recorded a device-side error";
+    case M3_ERR_NO_DEVICE: return "m3: no sm_100 CUDA device is current";
+    default: return "m3: unknown status code";
+  }
+}
+
+int m3_version(void) { return (1 << 16) | 0; }
+
+size_t m3_scan_ckpt_floats(const m3_scan_desc* desc) {
+  Tile t;
+  if (check_scan_desc(desc, &t) != M3_OK) return 0;
+  return ckpt_floats(desc, t);
+}
+
+int m3_scan_fwd(const m3_scan_desc* desc, const void* delta, const void* u, const void* Bc,
+                const void* Cc, const float* A_real_p, const float* A_imag_p,
+                const float* track_p, float* y, float* ckpt, float* h_last, float* dbu_last,
+                void* stream) {
+  Tile t;
+  int rc = check_scan_desc(desc, &t);
+  if (rc != M3_OK) return rc;
+  if (!delta || !u || !Bc || !Cc || !A_real_p || !A_imag_p || !track_p || !y) return M3_ERR_NULL;
+  if ((h_last == nullptr) != (dbu_last == nullptr)) return M3_ERR_NULL;
+  if (h_last && desc->direction == M3_DIR_BIDIR) return M3_ERR_SHAPE;
+  const int esd = dsize(desc->dtype_du), esb = dsize(desc->dtype_bc);
+  if (!aligned(delta, esd) || !aligned(u, esd) || !aligned(Bc, esb) || !aligned(Cc, esb) ||
+      !aligned(A_real_p, 4) || !aligned(A_imag_p, 4) || !aligned(track_p, 4) || !aligned(y, 4) ||
+      (ckpt && !aligned(ckpt, 4)) || (h_last && (!aligned(h_last, 4) || !aligned(dbu_last, 4))))
+    return M3_ERR_ALIGN;
+  if ((rc = check_device()) != M3_OK) return rc;
+
+  FwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.delta = delta; p.u = u; p.Bc = Bc; p.Cc = Cc;
+  p.Ar = A_real_p; p.Ai = A_imag_p; p.Tk = track_p;
+  p.y = y; p.ckpt = ckpt_floats(desc, t) ? ckpt : nullptr;
+  p.h_last = h_last; p.dbu_last = dbu_last;
+  p.B = desc->batch; p.L = desc->seqlen; p.D = desc->d_inner; p.N = desc->d_state;
+  p.NR = desc->n_rot; p.NT = desc->d_state - desc->n_rot;
+  p.dt_du = desc->dtype_du; p.dt_bc = desc->dtype_bc;
+  p.direction = desc->direction;
+  p.nch = nchunks(desc->seqlen);
+  p.async_ok = aligned(delta, 4) && aligned(u, 4) &&
+               (desc->dtype_du == M3_F32 || (desc->d_inner % 2) == 0);
+  p.err = device_err_ptr();
+  cudaError_t e = launch_scan_fwd(t, p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
+size_t m3_scan_bwd_workspace_bytes(const m3_scan_desc* desc) {
+  Tile t;
+  if (check_scan_desc(desc, &t) != M3_OK) return 0;
+  BwdLayout lay;
+  if (!bwd_layout(desc, t, &lay)) return 0;
+  return lay.total;
+}
+
+int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, const void* Bc,
+                const void* Cc, const float* A_real_p, const float* A_imag_p,
+                const float* track_p, const void* dy, int32_t dtype_dy, const float* ckpt,
+                void* d_delta, void* d_u, void* d_Bc, void* d_Cc, float* d_A_real_p,
+                float* d_A_imag_p, float* d_track_p, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  Tile t;
+  int rc = check_scan_desc(desc, &t);
+  if (rc != M3_OK) return rc;
+  if (!dtype_ok(dtype_dy)) return M3_ERR_DTYPE;
+  if (!delta || !u || !Bc || !Cc || !A_real_p || !A_imag_p || !track_p || !dy || !d_delta ||
+      !d_u || !d_Bc || !d_Cc || !d_A_real_p || !d_A_imag_p || !d_track_p)
+    return M3_ERR_NULL;
+  if (ckpt_floats(desc, t) > 0 && !ckpt) return M3_ERR_NULL;
+  const int esd = dsize(desc->dtype_du), esb = dsize(desc->dtype_bc), esy = dsize(dtype_dy);
+  if (!aligned(delta, esd) || !aligned(u, esd) || !aligned(d_delta, esd) || !aligned(d_u, esd) ||
+      !aligned(Bc, esb) || !aligned(Cc, esb) || !aligned(d_Bc, esb) || !aligned(d_Cc, esb) ||
+      !aligned(dy, esy) || !aligned(A_real_p, 4) || !aligned(A_imag_p, 4) ||
+      !aligned(track_p, 4) || !aligned(d_A_real_p, 4) || !aligned(d_A_imag_p, 4) ||
+      !aligned(d_track_p, 4) || (ckpt && !aligned(ckpt, 4)) || !aligned(workspace, 256))
+    return M3_ERR_ALIGN;
+  if ((rc = check_device()) != M3_OK) return rc;
+  BwdLayout lay;
+  if (!bwd_layout(desc, t, &lay)) return M3_ERR_NO_DEVICE;
+  if (!workspace || workspace_bytes < lay.total) return M3_ERR_WORKSPACE;
+
+  char* ws = static_cast<char*>(workspace);
+  BwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.delta = delta; p.u = u; p.Bc = Bc; p.Cc = Cc;
+  p.Ar = A_real_p; p.Ai = A_imag_p; p.Tk = track_p;
+  p.dy = dy; p.ckpt = ckpt;
+  p.d_delta = d_delta; p.d_u = d_u;
+  p.part_a = reinterpret_cast<float*>(ws + lay.off_a);
+  p.part_bc = reinterpret_cast<float*>(ws + lay.off_bc);
+  p.scratch_du =
+      desc->direction == M3_DIR_BIDIR ? reinterpret_cast<float*>(ws + lay.off_du) : nullptr;
+  p.B = desc->batch; p.L = desc->seqlen; p.D = desc->d_inner; p.N = desc->d_state;
+  p.NR = desc->n_rot; p.NT = desc->d_state - desc->n_rot;
+  p.dt_du = desc->dtype_du; p.dt_bc = desc->dtype_bc; p.dt_dy = dtype_dy;
+  p.direction = desc->direction;
+  p.nch = nchunks(desc->seqlen);
+  p.G = lay.G; p.Bg = lay.Bg;
+  p.err = device_err_ptr();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_scan_bwd(t, p, s);
+  if (e != cudaSuccess) return M3_ERR_LAUNCH;
+
+  ReduceParams r;
+  memset(&r, 0, sizeof(r));
+  r.part_bc = p.part_bc; r.part_a = p.part_a;
+  r.d_Bc = d_Bc; r.d_Cc = d_Cc;
+  r.dAr = d_A_real_p; r.dAi = d_A_imag_p; r.dTk = d_track_p;
+  r.B = p.B; r.L = p.L; r.D = p.D; r.N = p.N; r.NR = p.NR; r.NT = p.NT;
+  r.dt_bc = p.dt_bc; r.G = p.G; r.Bg = p.Bg;
+  e = launch_bwd_reduce(t, r, s);
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
+int m3_step(const m3_step_desc* desc, float* h, float* dbu, const void* delta, const void* u,
+            const void* Bc, const void* Cc, const float* A_real_p, const float* A_imag_p,
+            const float* track_p, float* y, void* stream) {
+  if (!desc) return M3_ERR_NULL;
+  if (desc->batch < 1 || desc->d_inner < 1 || desc->d_state < 1 || desc->d_state > kMaxState ||
+      desc->n_rot < 0 || desc->n_rot > desc->d_state)
+    return M3_ERR_SHAPE;
+  if (!dtype_ok(desc->dtype_du) || !dtype_ok(desc->dtype_bc)) return M3_ERR_DTYPE;
+  if (!h || !dbu || !delta || !u || !Bc || !Cc || !A_real_p || !A_imag_p || !track_p || !y)
+    return M3_ERR_NULL;
+  Tile t;
+  if (!select_tile(desc->n_rot, desc->d_state - desc->n_rot, &t)) return M3_ERR_UNSUPPORTED;
+  if ((desc->d_inner + 31) / 32 > 65535) return M3_ERR_SHAPE;
+  const int esd = dsize(desc->dtype_du), esb = dsize(desc->dtype_bc);
+  if (!aligned(h, 4) || !aligned(dbu, 4) || !aligned(delta, esd) || !aligned(u, esd) ||
+      !aligned(Bc, esb) || !aligned(Cc, esb) || !aligned(A_real_p, 4) || !aligned(A_imag_p, 4) ||
+      !aligned(track_p, 4) || !aligned(y, 4))
+    return M3_ERR_ALIGN;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  StepParams p;
+  memset(&p, 0, sizeof(p));
+  p.h = h; p.dbu = dbu; p.delta = delta; p.u = u; p.Bc = Bc; p.Cc = Cc;
+  p.Ar = A_real_p; p.Ai = A_imag_p; p.Tk = track_p; p.y = y;
+  p.B = desc->batch; p.D = desc->d_inner; p.N = desc->d_state;
+  p.NR = desc->n_rot; p.NT = desc->d_state - desc->n_rot;
+  p.dt_du = desc->dtype_du; p.dt_bc = desc->dtype_bc;
+  p.err = device_err_ptr();
+  cudaError_t e = launch_step(t, p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
+int m3_device_error(int32_t* code, int32_t clear) {
+  if (!code) return M3_ERR_NULL;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_err_word, sizeof(int)) != cudaSuccess) return M3_ERR_LAUNCH;
+  *code = v;
+  if (clear && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_err_word, &z, sizeof(int)) != cudaSuccess) return M3_ERR_LAUNCH;
+  }
+  return M3_OK;
+}
+
+}  // extern "C"

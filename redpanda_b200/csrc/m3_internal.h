@@ -1,0 +1,78 @@
+// Internal launch interface shared by the kernel translation units and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace m3 {
+
+// Per-thread lane tiling: R rotational + T tracking lanes per channel, ND
+// channels per thread, 4 threads per channel group, 128 threads per CTA.
+struct Tile {
+  int R, T, ND;
+  int nl() const { return R + T; }
+  int np() const { return 4 * (R + T); }   // padded state lanes per channel
+  int dt() const { return 32 * ND; }       // channels per CTA
+};
+
+// Tile chosen for a (n_rot, n_track) split; identical for scan, backward and
+// step so that their arithmetic (and the y reduction order) agrees.
+bool select_tile(int n_rot, int n_track, Tile* out);
+
+struct FwdParams {
+  const void* delta; const void* u; const void* Bc; const void* Cc;
+  const float* Ar; const float* Ai; const float* Tk;
+  float* y; float* ckpt; float* h_last; float* dbu_last;
+  int B, L, D, N, NR, NT;
+  int dt_du, dt_bc;
+  int direction;   // 0 fwd, 1 rev, 2 bidir
+  int nch;         // chunks of kCK steps
+  int async_ok;    // cp.async staging allowed (alignment checked on the host)
+  int* err;
+};
+
+struct BwdParams {
+  const void* delta; const void* u; const void* Bc; const void* Cc;
+  const float* Ar; const float* Ai; const float* Tk;
+  const void* dy; const float* ckpt;
+  void* d_delta; void* d_u;
+  float* part_bc;     // [G][B][L][2][NP]
+  float* part_a;      // [Bg][3][D][NP]
+  float* scratch_du;  // [G*Bg][L][DT][2]  (bidirectional only)
+  int B, L, D, N, NR, NT;
+  int dt_du, dt_bc, dt_dy;
+  int direction;
+  int nch;
+  int G, Bg;
+  int* err;
+};
+
+struct StepParams {
+  float* h; float* dbu;
+  const void* delta; const void* u; const void* Bc; const void* Cc;
+  const float* Ar; const float* Ai; const float* Tk;
+  float* y;
+  int B, D, N, NR, NT;
+  int dt_du, dt_bc;
+  int* err;
+};
+
+struct ReduceParams {
+  const float* part_bc; const float* part_a;
+  void* d_Bc; void* d_Cc;
+  float* dAr; float* dAi; float* dTk;
+  int B, L, D, N, NR, NT;
+  int dt_bc;
+  int G, Bg;
+};
+
+cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s);
+cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s);
+cudaError_t launch_bwd_reduce(const Tile& t, const ReduceParams& p, cudaStream_t s);
+cudaError_t launch_step(const Tile& t, const StepParams& p, cudaStream_t s);
+
+// device error word of the current device
+int* device_err_ptr();
+
+}  // namespace m3

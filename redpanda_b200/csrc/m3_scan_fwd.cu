@@ -1,0 +1,306 @@
+// K1/K3: forward trapezoidal scan (causal, reverse, or both directions fused
+// into one launch) with optional chunk checkpoints for the backward and the
+// final (h, dBu) state for the O(1) step.
+//
+// Replaces _fwd_kernel (redpanda/engine/triton_scan.py:44-98) and the two
+// flipped launches of the bidirectional Eval Mamba (redpanda/engine/mamba.py:254-260).
+//
+// CTA = 128 threads = 32 channel groups x 4 state-lane quarters.  A thread owns
+// ND consecutive channels x (R rotational + T tracking) state lanes and walks
+// the sequence in registers.  delta/u tiles of kCK timesteps are staged into
+// shared memory with cp.async (double-buffered, in their HBM dtype); B/C are
+// register-prefetched one chunk ahead, converted to fp32 and padded to the
+// thread lane layout.  y is reduced over the 4 lane quarters with shuffles.
+#include "m3_common.cuh"
+#include "m3_internal.h"
+#include "m3_tiles.h"
+
+namespace m3 {
+namespace {
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool valid) {
+  uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  int sz = valid ? 4 : 0;  // src-size 0 => zero fill
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(sz)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait1() {
+  asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait0() {
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+// Stage delta and u for processing steps [s0, s0 + kCK) of row b, channels
+// [d0, d0 + DT), in their HBM dtype, into one shared buffer pair.  Rows past the
+// sequence end and channels past D are zero-filled.
+template <int DT>
+__device__ __forceinline__ void stage_du(unsigned char* s_dl, unsigned char* s_u,
+                                         const FwdParams& p, int b, int d0, int s0,
+                                         int dir, int esz) {
+  if (p.async_ok) {
+    const int epw = 4 / esz;        // elements per 4-byte word
+    const int wpr = DT / epw;       // words per staged row
+    for (int i = threadIdx.x; i < kCK * wpr; i += kThreads) {
+      const int tt = i / wpr, w = i - tt * wpr;
+      const int s = s0 + tt, d = d0 + w * epw;
+      const bool ok = (s < p.L) && (d < p.D);
+      const int t = dir ? p.L - 1 - s : s;
+      const size_t gi = ok ? ((size_t)b * p.L + t) * p.D + d : 0;
+      cp_async4(s_dl + (size_t)i * 4, (const char*)p.delta + gi * esz, ok);
+      cp_async4(s_u + (size_t)i * 4, (const char*)p.u + gi * esz, ok);
+    }
+  } else {
+    for (int i = threadIdx.x; i < kCK * DT; i += kThreads) {
+      const int tt = i / DT, dd = i - tt * DT;
+      const int s = s0 + tt, d = d0 + dd;
+      const bool ok = (s < p.L) && (d < p.D);
+      const int t = dir ? p.L - 1 - s : s;
+      const size_t gi = ok ? ((size_t)b * p.L + t) * p.D + d : 0;
+      if (esz == 2) {
+        const uint16_t* a = (const uint16_t*)p.delta;
+        const uint16_t* c = (const uint16_t*)p.u;
+        ((uint16_t*)s_dl)[i] = ok ? a[gi] : 0;
+        ((uint16_t*)s_u)[i] = ok ? c[gi] : 0;
+      } else {
+        ((float*)s_dl)[i] = ok ? ((const float*)p.delta)[gi] : 0.f;
+        ((float*)s_u)[i] = ok ? ((const float*)p.u)[gi] : 0.f;
+      }
+    }
+  }
+}
+
+// ND channel values of one staged row, converted to fp32.
+template <int ND>
+__device__ __forceinline__ void read_chan(const unsigned char* base, bool bf16, float (&v)[ND]) {
+  if (bf16) {
+    if constexpr (ND % 2 == 0) {
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(base);
+#pragma unroll
+      for (int i = 0; i < ND / 2; ++i) {
+        float2 f = __bfloat1622float2(p2[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else {
+      const __nv_bfloat16* p1 = reinterpret_cast<const __nv_bfloat16*>(base);
+#pragma unroll
+      for (int i = 0; i < ND; ++i) v[i] = __bfloat162float(p1[i]);
+    }
+  } else {
+    const float* pf = reinterpret_cast<const float*>(base);
+    if constexpr (ND % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < ND / 4; ++i) {
+        float4 f = reinterpret_cast<const float4*>(pf)[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < ND; ++i) v[i] = pf[i];
+    }
+  }
+}
+
+template <int R, int T, int ND>
+__global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdParams p) {
+  using LM = LaneMap<R, T>;
+  constexpr int NL = R + T;
+  constexpr int NP = LM::NP;
+  constexpr int DT = 32 * ND;
+  constexpr int RR = R > 0 ? R : 1;
+  constexpr int TT = T > 0 ? T : 1;
+  constexpr int BCE = (kCK * NP + kThreads - 1) / kThreads;   // B/C prefetch per thread
+
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned char* s_dl = smem;                                 // [2][kCK*DT*4]
+  unsigned char* s_u = s_dl + 2 * kCK * DT * 4;               // [2][kCK*DT*4]
+  float* s_b = reinterpret_cast<float*>(s_u + 2 * kCK * DT * 4);  // [2][kCK][NP]
+  float* s_c = s_b + 2 * kCK * NP;
+
+  const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
+  const int b = blockIdx.x;
+  const int d0 = blockIdx.y * DT;
+  const int dbase = d0 + grp * ND;
+  const bool bf16 = p.dt_du == M3_BF16;
+  const int esz = bf16 ? 2 : 4;
+  const int L = p.L, D = p.D, N = p.N;
+
+  // Eigenvalues of this thread's cells (zero for virtual lanes / channels).
+  float ar[ND][RR], ai[ND][RR], tk[ND][TT];
+#pragma unroll
+  for (int k = 0; k < ND; ++k) {
+    const int d = dbase + k;
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int n = LM::mem_lane(q, j, p.NR, p.NT);
+      const bool ok = (d < D) && (n >= 0);
+      const size_t gi = ok ? (size_t)d * N + n : 0;
+      if (j < R) {
+        ar[k][j] = ok ? p.Ar[gi] : 0.f;
+        ai[k][j] = ok ? p.Ai[gi] : 0.f;
+      } else {
+        tk[k][j - R] = ok ? p.Tk[gi] : 0.f;
+      }
+    }
+  }
+
+  const int npass = p.direction == M3_DIR_BIDIR ? 2 : 1;
+  for (int pass = 0; pass < npass; ++pass) {
+    const int dir = p.direction == M3_DIR_BIDIR ? (pass == 0 ? 1 : 0) : p.direction;
+    const bool accumulate = p.direction == M3_DIR_BIDIR && pass == 1;
+    const int dslot = p.direction == M3_DIR_BIDIR ? dir : 0;
+    const int ndirs = p.direction == M3_DIR_BIDIR ? 2 : 1;
+
+    float P[ND][NL];
+#pragma unroll
+    for (int k = 0; k < ND; ++k)
+#pragma unroll
+      for (int j = 0; j < NL; ++j) P[k][j] = 0.f;
+
+    float rb[BCE], rc[BCE];
+    auto load_bc = [&](int s0) {
+#pragma unroll
+      for (int e = 0; e < BCE; ++e) {
+        const int i = tid + e * kThreads;
+        const int tt = i / NP, lane = i - tt * NP;
+        const int s = s0 + tt;
+        const int n = LM::mem_lane(lane / NL, lane % NL, p.NR, p.NT);
+        const bool ok = (i < kCK * NP) && (s < L) && (n >= 0);
+        const int t = dir ? L - 1 - s : s;
+        const size_t gi = ok ? ((size_t)b * L + t) * N + n : 0;
+        rb[e] = ok ? ld_f(p.Bc, gi, p.dt_bc) : 0.f;
+        rc[e] = ok ? ld_f(p.Cc, gi, p.dt_bc) : 0.f;
+      }
+    };
+    auto store_bc = [&](int buf) {
+#pragma unroll
+      for (int e = 0; e < BCE; ++e) {
+        const int i = tid + e * kThreads;
+        if (i < kCK * NP) {
+          s_b[buf * kCK * NP + i] = rb[e];
+          s_c[buf * kCK * NP + i] = rc[e];
+        }
+      }
+    };
+
+    // prologue: chunk 0 into buffer 0
+    stage_du<DT>(s_dl, s_u, p, b, d0, 0, dir, esz);
+    cp_async_commit();
+    load_bc(0);
+    store_bc(0);
+
+    for (int c = 0; c < p.nch; ++c) {
+      const int buf = c & 1;
+      const bool more = c + 1 < p.nch;
+      if (more)
+        stage_du<DT>(s_dl + (buf ^ 1) * kCK * DT * 4, s_u + (buf ^ 1) * kCK * DT * 4, p, b, d0,
+                     (c + 1) * kCK, dir, esz);
+      cp_async_commit();
+      if (more) load_bc((c + 1) * kCK);
+      cp_async_wait1();
+      __syncthreads();
+
+      // checkpoint of P = 2h + dBu before the first step of this chunk
+      if (c > 0 && p.ckpt != nullptr) {
+#pragma unroll
+        for (int k = 0; k < ND; ++k) {
+          const int d = dbase + k;
+          if (d < D) {
+            float* dst = p.ckpt +
+                ((((size_t)b * ndirs + dslot) * (p.nch - 1) + (c - 1)) * D + d) * NP + q * NL;
+#pragma unroll
+            for (int j = 0; j < NL; ++j) dst[j] = P[k][j];
+          }
+        }
+      }
+
+      const unsigned char* bdl = s_dl + buf * kCK * DT * 4;
+      const unsigned char* bu = s_u + buf * kCK * DT * 4;
+      const float* bb = s_b + buf * kCK * NP;
+      const float* bc = s_c + buf * kCK * NP;
+      const int ns = min(kCK, L - c * kCK);
+      for (int tt = 0; tt < ns; ++tt) {
+        const int s = c * kCK + tt;
+        const int t = dir ? L - 1 - s : s;
+        float dl[ND], uu[ND];
+        read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * esz, bf16, dl);
+        read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * esz, bf16, uu);
+        float Bv[NL], Cv[NL];
+#pragma unroll
+        for (int j = 0; j < NL; ++j) {
+          Bv[j] = bb[tt * NP + q * NL + j];
+          Cv[j] = bc[tt * NP + q * NL + j];
+        }
+        const bool last = (s == L - 1) && (p.h_last != nullptr);
+        float part[ND];
+#pragma unroll
+        for (int k = 0; k < ND; ++k) {
+          const float du = __fmul_rn(dl[k], uu[k]);
+          float H[NL];
+#pragma unroll
+          for (int j = 0; j < R; ++j)
+            H[j] = cell_update(rot_gate(dl[k], ar[k][j], ai[k][j]), P[k][j], du, Bv[j]);
+#pragma unroll
+          for (int j = R; j < NL; ++j) H[j] = cell_update(tk[k][j - R], P[k][j], du, Bv[j]);
+          part[k] = y_partial<NL>(H, Cv);
+          if (last) {
+            const int d = dbase + k;
+            if (d < D) {
+#pragma unroll
+              for (int j = 0; j < NL; ++j) {
+                const int n = LM::mem_lane(q, j, p.NR, p.NT);
+                if (n >= 0) {
+                  const size_t gi = ((size_t)b * D + d) * N + n;
+                  p.h_last[gi] = __fmul_rn(0.5f, H[j]);
+                  p.dbu_last[gi] = __fmul_rn(du, Bv[j]);
+                }
+              }
+            }
+          }
+        }
+        float* yrow = p.y + ((size_t)b * L + t) * D;
+#pragma unroll
+        for (int k = 0; k < ND; ++k) {
+          const float tot = __fmul_rn(0.5f, quad_sum(part[k]));
+          const int d = dbase + k;
+          if ((k & 3) == q && d < D) {
+            yrow[d] = accumulate ? __fadd_rn(tot, yrow[d]) : tot;
+          }
+        }
+      }
+      if (more) store_bc(buf ^ 1);
+      __syncthreads();
+    }
+  }
+  cp_async_wait0();
+}
+
+template <int R, int T, int ND>
+cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
+  constexpr int NP = 4 * (R + T);
+  constexpr int DT = 32 * ND;
+  const size_t smem = 2 * (2 * (size_t)kCK * DT * 4) + 2 * (2 * (size_t)kCK * NP * 4);
+  auto kern = scan_fwd_kernel<R, T, ND>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.B, (p.D + DT - 1) / DT);
+  kern<<<grid, kThreads, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
+#define M3_X(r, tt, nd) \
+  if (t.R == r && t.T == tt && t.ND == nd) return launch_fwd_impl<r, tt, nd>(p, s);
+  M3_TILE_LIST(M3_X)
+#undef M3_X
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace m3

@@ -1,0 +1,266 @@
+"""PyTorch operator surface of the sm_100a trapezoidal scan.
+
+Mirrors ``redpanda/engine/triton_scan.py`` so that it is a drop-in for the
+reference's fused-scan path:
+
+* ``HAS_M3`` (alias ``HAS_TRITON``) -- availability flag (triton_scan.py:30-37)
+* ``m3_trapezoidal_scan`` (alias ``triton_trapezoidal_scan``) -- same
+  arguments and result as triton_scan.py:318-337: y WITHOUT the ``u*D`` skip
+* ``_TrapezoidalScanFn`` -- the autograd Function (triton_scan.py:244-315),
+  analytic backward, grads cast to the input dtypes
+* ``m3_bidir_scan`` -- y_fwd + flip(scan(flip(x))) in one launch (mamba.py:254-260)
+* ``m3_scan_with_state`` -- the ``return_state`` scan (mamba.py:377-379)
+* ``m3_step_`` -- the in-place O(1) step recurrence (mamba.py:466-493)
+
+Installing this module as ``triton_scan`` (``redpanda_b200.integration``)
+routes the unmodified reference ``mamba.py`` through these kernels.  There is
+no CPU or PyTorch fallback: every op raises if the CUDA library is missing or a
+tensor is not on an sm_100 device.
+"""
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from ._lib import M3_BF16, M3_DIR_BIDIR, M3_DIR_FWD, M3_DIR_REV, M3_F32, ScanDesc, StepDesc
+
+CHUNK = 16  # checkpoint / backward recompute chunk (timesteps)
+
+
+def _has_m3():
+    if not _lib.available() or not torch.cuda.is_available():
+        return False
+    try:
+        return torch.cuda.get_device_capability()[0] == 10
+    except Exception:  # pragma: no cover - driver trouble
+        return False
+
+
+HAS_M3 = _has_m3()
+HAS_TRITON = HAS_M3   # name the reference's mamba.py:344 imports
+
+
+def _dt_code(dtype):
+    if dtype == torch.float32:
+        return M3_F32
+    if dtype == torch.bfloat16:
+        return M3_BF16
+    raise TypeError(f"unsupported dtype {dtype}")
+
+
+def _prep_pair(a, b):
+    """Contiguous copies of a tensor pair in one kernel dtype (f32 or bf16)."""
+    if a.dtype == b.dtype and a.dtype in (torch.float32, torch.bfloat16):
+        dt = a.dtype
+    else:
+        dt = torch.float32
+    return a.to(dt).contiguous(), b.to(dt).contiguous(), _dt_code(dt)
+
+
+def ctypes_ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require_cuda(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("m3 scan ops run on CUDA tensors only (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError("m3 scan ops need every tensor on one device")
+    return dev
+
+
+def pad_params(A_real, A_imag, track, n_rot, n_state, d_inner, device):
+    """(D, N) fp32 parameter tensors in the layout of triton_scan.py:325-335."""
+    if A_real is not None:
+        Ar_p = F.pad(A_real, (0, n_state - A_real.shape[-1]))
+        Ai_p = (F.pad(A_imag, (0, n_state - A_imag.shape[-1]))
+                if A_imag is not None else torch.zeros(d_inner, n_state, device=device))
+    else:
+        Ar_p = torch.zeros(d_inner, n_state, device=device)
+        Ai_p = torch.zeros(d_inner, n_state, device=device)
+    Tk_p = (F.pad(track, (n_rot, 0))
+            if track is not None else torch.zeros(d_inner, n_state, device=device))
+    return Ar_p, Ai_p, Tk_p
+
+
+class _TrapezoidalScanFn(torch.autograd.Function):
+    """y = trapezoidal selective scan; analytic, deterministic backward.
+
+    forward(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state)
+    returns (y, h_last, dbu_last); the state outputs are empty unless
+    ``want_state`` and are not differentiable.
+    """
+
+    @staticmethod
+    def forward(ctx, delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state):
+        lib = _lib.load()
+        dev = _require_cuda(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p)
+        dl, uu, dt_du = _prep_pair(delta, u)
+        bb, cc, dt_bc = _prep_pair(Bc, Cc)
+        ar, ai, tk = (x.detach().to(torch.float32).contiguous() for x in (Ar_p, Ai_p, Tk_p))
+        B, L, D = uu.shape
+        N = bb.shape[-1]
+        desc = ScanDesc(B, L, D, N, int(n_rot), dt_du, dt_bc, int(direction))
+        y = torch.empty(B, L, D, device=dev, dtype=torch.float32)
+        need_grad = any(ctx.needs_input_grad[:7])
+        nck = lib.m3_scan_ckpt_floats(desc) if need_grad else 0
+        ckpt = torch.empty(nck, device=dev, dtype=torch.float32) if nck else None
+        if want_state:
+            h = torch.empty(B, D, N, device=dev, dtype=torch.float32)
+            dbu = torch.empty_like(h)
+        else:
+            h = dbu = None
+        with torch.cuda.device(dev):
+            _lib.check(lib.m3_scan_fwd(desc, dl.data_ptr(), uu.data_ptr(), bb.data_ptr(),
+                                       cc.data_ptr(), ar.data_ptr(), ai.data_ptr(),
+                                       tk.data_ptr(), y.data_ptr(), ctypes_ptr(ckpt),
+                                       ctypes_ptr(h), ctypes_ptr(dbu), _stream(dev)))
+        empty = torch.empty(0, device=dev)
+        ctx.save_for_backward(dl, uu, bb, cc, ar, ai, tk, ckpt if ckpt is not None else empty)
+        ctx.has_ckpt = ckpt is not None
+        ctx.desc = (B, L, D, N, int(n_rot), dt_du, dt_bc, int(direction))
+        ctx.in_dtypes = (delta.dtype, u.dtype, Bc.dtype, Cc.dtype,
+                         Ar_p.dtype, Ai_p.dtype, Tk_p.dtype)
+        if want_state:
+            ctx.mark_non_differentiable(h, dbu)
+            return y, h, dbu
+        return y, empty, empty
+
+    @staticmethod
+    def backward(ctx, dy, _dh=None, _ddbu=None):
+        lib = _lib.load()
+        dl, uu, bb, cc, ar, ai, tk, ckpt = ctx.saved_tensors
+        dev = dl.device
+        desc = ScanDesc(*ctx.desc)
+        if dy.dtype not in (torch.float32, torch.bfloat16):
+            dy = dy.float()
+        dy = dy.contiguous()
+        dd = torch.empty_like(dl)
+        du = torch.empty_like(uu)
+        dB = torch.empty_like(bb)
+        dC = torch.empty_like(cc)
+        dAr = torch.empty_like(ar)
+        dAi = torch.empty_like(ai)
+        dTk = torch.empty_like(tk)
+        nws = lib.m3_scan_bwd_workspace_bytes(desc)
+        ws = torch.empty(max(nws, 1), device=dev, dtype=torch.uint8)
+        with torch.cuda.device(dev):
+            _lib.check(lib.m3_scan_bwd(
+                desc, dl.data_ptr(), uu.data_ptr(), bb.data_ptr(), cc.data_ptr(),
+                ar.data_ptr(), ai.data_ptr(), tk.data_ptr(), dy.data_ptr(), _dt_code(dy.dtype),
+                ckpt.data_ptr() if ctx.has_ckpt else None,
+                dd.data_ptr(), du.data_ptr(), dB.data_ptr(), dC.data_ptr(),
+                dAr.data_ptr(), dAi.data_ptr(), dTk.data_ptr(), ws.data_ptr(), nws,
+                _stream(dev)))
+        td, tu, tb, tc, tar, tai, ttk = ctx.in_dtypes
+        return (dd.to(td), du.to(tu), dB.to(tb), dC.to(tc), dAr.to(tar), dAi.to(tai),
+                dTk.to(ttk), None, None, None)
+
+
+def _apply(delta, u, Bc, Cc, A_real, A_imag, track, n_rot, n_state, direction, want_state):
+    d_inner = u.shape[-1]
+    Ar_p, Ai_p, Tk_p = pad_params(A_real, A_imag, track, n_rot, n_state, d_inner, u.device)
+    return _TrapezoidalScanFn.apply(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p,
+                                    n_rot, direction, want_state)
+
+
+def m3_trapezoidal_scan(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
+                        n_rot, n_state):
+    """Causal scan; drop-in for ``triton_trapezoidal_scan`` (triton_scan.py:318-337).
+
+    Returns fp32 y (B, L, D) without the ``u*D`` skip term.
+    """
+    return _apply(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
+                  n_rot, n_state, M3_DIR_FWD, False)[0]
+
+
+triton_trapezoidal_scan = m3_trapezoidal_scan
+
+
+def m3_reverse_scan(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
+                    n_rot, n_state):
+    """flip(scan(flip(x))) without materialising flipped copies."""
+    return _apply(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
+                  n_rot, n_state, M3_DIR_REV, False)[0]
+
+
+def m3_bidir_scan(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
+                  n_rot, n_state):
+    """Fused bidirectional scan: scan(x) + flip(scan(flip(x))) (mamba.py:254-260).
+
+    Skip terms excluded; the reference block adds ``u*D`` once per direction.
+    """
+    return _apply(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
+                  n_rot, n_state, M3_DIR_BIDIR, False)[0]
+
+
+def m3_scan_with_state(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
+                       n_rot, n_state):
+    """Causal scan returning ``(y, (h_last, dBu_last))`` (mamba.py:377-379).
+
+    y is differentiable; the state is not.
+    """
+    y, h, dbu = _apply(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
+                       n_rot, n_state, M3_DIR_FWD, True)
+    return y, (h, dbu)
+
+
+def m3_step_(h, dbu, delta_t, u_t, Bc_t, Cc_t, A_real, A_imag, track, n_rot, n_state):
+    """O(1) step of B rows, updating ``h`` and ``dbu`` IN PLACE; returns y (B, D).
+
+    h, dbu: (B, D, N) contiguous float32 CUDA tensors (the reference cache
+    pair, mamba.py:487-498).  delta_t, u_t: (B, D); Bc_t, Cc_t: (B, N).
+    The reference step is functional (mamba.py:489-498); callers that keep the
+    old state must clone it first (as mars_search.py:640 does).
+    """
+    lib = _lib.load()
+    dev = _require_cuda(h, dbu, delta_t, u_t, Bc_t, Cc_t)
+    if h.dtype != torch.float32 or dbu.dtype != torch.float32:
+        raise TypeError("m3_step_: the state must be float32")
+    if not (h.is_contiguous() and dbu.is_contiguous()):
+        raise ValueError("m3_step_: the state must be contiguous (it is updated in place)")
+    B, D, N = h.shape
+    dl, uu, dt_du = _prep_pair(delta_t, u_t)
+    bb, cc, dt_bc = _prep_pair(Bc_t, Cc_t)
+    Ar_p, Ai_p, Tk_p = pad_params(A_real, A_imag, track, n_rot, n_state, D, dev)
+    ar, ai, tk = (x.detach().to(torch.float32).contiguous() for x in (Ar_p, Ai_p, Tk_p))
+    y = torch.empty(B, D, device=dev, dtype=torch.float32)
+    desc = StepDesc(B, D, N, int(n_rot), dt_du, dt_bc)
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3_step(desc, h.data_ptr(), dbu.data_ptr(), dl.data_ptr(),
+                               uu.data_ptr(), bb.data_ptr(), cc.data_ptr(), ar.data_ptr(),
+                               ai.data_ptr(), tk.data_ptr(), y.data_ptr(), _stream(dev)))
+    return y
+
+
+def m3_step(state, delta_t, u_t, Bc_t, Cc_t, A_real, A_imag, track, n_rot, n_state):
+    """Functional step: returns (y, (h_new, dbu_new)); ``state`` may be None."""
+    B, D = u_t.shape
+    N = Bc_t.shape[-1]
+    if state is None:
+        h = torch.zeros(B, D, N, device=u_t.device, dtype=torch.float32)
+        dbu = torch.zeros_like(h)
+    else:
+        h, dbu = (s.detach().to(torch.float32).clone(memory_format=torch.contiguous_format)
+                  for s in state)
+    y = m3_step_(h, dbu, delta_t, u_t, Bc_t, Cc_t, A_real, A_imag, track, n_rot, n_state)
+    return y, (h, dbu)
+
+
+def device_error(clear=True):
+    """Device-side error word of the current device (0 = none)."""
+    import ctypes
+    lib = _lib.load()
+    code = ctypes.c_int32(0)
+    _lib.check(lib.m3_device_error(ctypes.byref(code), int(bool(clear))))
+    return code.value

@@ -1,0 +1,151 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference itself.
+
+Run in a container where the read-only reference checkout is present:
+
+    python tests/golden/make_golden.py [--ref /path/to/RedPanda]
+
+It imports ``redpanda/engine/mamba.py`` from that checkout, drives the
+reference's own ``Mamba3Block._selective_scan_trapezoidal`` (the PyTorch scan
+path, training mode with its default ``scan_checkpoint=True``) and the
+reference ``Mamba`` model (forward, ``step``, ``prime_cache``, parameter
+gradients), and stores inputs and outputs as small ``.pt`` files next to this
+script.  Nothing on the GPU box reads the reference; the fixtures travel
+instead.
+"""
+
+import argparse
+import os
+import sys
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+from redpanda_b200.synthetic import ScanShape, make_scan_inputs  # noqa: E402
+
+
+def _ref_block(M, shape, theta):
+    cfg = M.MambaConfig(d_model=shape.d_inner // 2, n_layer=1, vocab_size=64,
+                        d_state=shape.d_state, n_track_state=shape.n_track,
+                        mimo_p=1, scan_checkpoint=True, use_triton_scan=False)
+    blk = M.Mamba3Block(cfg).train()
+    if shape.n_track > 0:
+        with torch.no_grad():
+            blk.track_theta.copy_(theta)
+    return blk
+
+
+def scan_case(M, shape, seed, bidir):
+    """Reference scan (no skip term) + autograd grads for one seeded input set."""
+    inp = make_scan_inputs(shape, seed=seed)
+    blk = _ref_block(M, shape, inp["theta"])
+    leaves = {k: inp[k].clone().requires_grad_(True)
+              for k in ("delta", "u", "Bc", "Cc", "A_real", "A_imag") if inp[k] is not None}
+    D0 = torch.zeros(shape.d_inner)
+
+    def run(delta, u, Bc, Cc, Ar, Ai, return_state=False):
+        # p = 1 view so that the block's B.sum(-1) is the identity.
+        return blk._selective_scan_trapezoidal(u, delta, Ar, Ai, Bc.unsqueeze(-1),
+                                               Cc.unsqueeze(-1), D0,
+                                               return_state=return_state)
+
+    lv = leaves
+    y = run(lv["delta"], lv["u"], lv["Bc"], lv["Cc"], lv.get("A_real"), lv.get("A_imag"))
+    if bidir:
+        y = y + run(lv["delta"].flip(1), lv["u"].flip(1), lv["Bc"].flip(1),
+                    lv["Cc"].flip(1), lv.get("A_real"), lv.get("A_imag")).flip(1)
+    (y * inp["dy"]).sum().backward()
+    out = {"shape": tuple(shape.__dict__.values()), "seed": seed, "bidir": bidir,
+           "inputs": {k: (v if v is None else v.clone()) for k, v in inp.items()},
+           "y": y.detach().clone(),
+           "grads": {k: v.grad.clone() for k, v in leaves.items()}}
+    if shape.n_track > 0:
+        out["grads"]["theta"] = blk.track_theta.grad.clone()
+    if not bidir:
+        with torch.no_grad():
+            blk.eval()
+            _, (h, dbu) = run(inp["delta"], inp["u"], inp["Bc"], inp["Cc"],
+                              inp["A_real"], inp["A_imag"], return_state=True)
+        out["h_last"], out["dbu_last"] = h.clone(), dbu.clone()
+    return out
+
+
+def model_case(M, kw, seed, L, bidir):
+    """Reference Mamba: forward, step chain, prime_cache and parameter grads."""
+    torch.manual_seed(seed)
+    cfg = M.MambaConfig(vocab_size=64, bidirectional=bidir, scan_checkpoint=True,
+                        use_triton_scan=False, **kw)
+    m = M.Mamba(cfg)
+    ids = torch.randint(0, 64, (3, L))
+    out = {"kw": dict(kw), "bidir": bidir, "seed": seed, "ids": ids,
+           "state_dict": {k: v.clone() for k, v in m.state_dict().items()}}
+    m.train()
+    y = m(ids)
+    y.pow(2).mean().backward()
+    out["forward"] = y.detach().clone()
+    out["param_grads"] = {k: p.grad.clone() for k, p in m.named_parameters()
+                          if p.grad is not None}
+    m.zero_grad(set_to_none=True)
+    if not bidir:
+        m.eval()
+        with torch.no_grad():
+            cache = None
+            hs = []
+            for t in range(L):
+                h, cache = m.step(token_id=ids[:, t], cache=cache)
+                hs.append(h)
+            out["step_hidden"] = torch.stack(hs, 1)
+            out["step_cache_last"] = [(a.clone(), b.clone()) for a, b in cache]
+            k = max(1, L // 2)
+            fin, pc = m.prime_cache(ids[:, :k])
+            out["prime_k"] = k
+            out["prime_final"] = fin.clone()
+            out["prime_cache"] = [(a.clone(), b.clone()) for a, b in pc]
+            nxt, _ = m.step(token_id=ids[:, k], cache=pc)
+            out["prime_next"] = nxt.clone()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, os.path.join(args.ref, "redpanda", "engine"))
+    import mamba as M  # the reference module, read-only
+
+    torch.set_num_threads(1)
+    cases = {
+        # config-0 shapes with the batch cut to 2 (rows are independent)
+        "scan_c0_causal": scan_case(M, ScanShape(2, 64, 256, 16, 4, 4), 0, False),
+        "scan_c0_bidir": scan_case(M, ScanShape(2, 64, 256, 16, 4, 4), 1, True),
+        # ragged length (not a multiple of the 32-token chunk), no tracking lanes
+        "scan_l70_notrack": scan_case(M, ScanShape(2, 70, 64, 16, 0, 2), 2, False),
+        # length 1, mostly tracking lanes
+        "scan_l1": scan_case(M, ScanShape(3, 1, 32, 12, 8, 2), 3, False),
+        # config-1 state layout (16 rot + 16 track) at a tiny batch
+        "scan_c1_slice": scan_case(M, ScanShape(1, 33, 128, 32, 16, 4), 4, True),
+        # config-3 state layout (24 rot + 8 track)
+        "scan_c3_slice": scan_case(M, ScanShape(2, 40, 64, 32, 8, 2), 5, False),
+    }
+    for name, c in cases.items():
+        torch.save(c, os.path.join(HERE, name + ".pt"))
+    models = {
+        # the reference's own verify() configs (triton_scan.py:353-354)
+        "model_verify_trk": model_case(M, dict(d_model=32, n_layer=2, d_state=12,
+                                               n_track_state=4, mimo_p=2), 10, 33, False),
+        "model_verify_trk_bidir": model_case(M, dict(d_model=32, n_layer=2, d_state=12,
+                                                     n_track_state=4, mimo_p=2), 11, 33, True),
+        "model_verify_notrk": model_case(M, dict(d_model=48, n_layer=2, d_state=16,
+                                                 n_track_state=0, mimo_p=2), 12, 70, False),
+    }
+    for name, c in models.items():
+        torch.save(c, os.path.join(HERE, name + ".pt"))
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".pt"):
+            print(f, os.path.getsize(os.path.join(HERE, f)))
+
+
+if __name__ == "__main__":
+    main()
