@@ -1,0 +1,434 @@
+#!/usr/bin/env python
+"""Headline benchmark: bidirectional Mamba-3 trapezoidal scan, forward + backward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl m3|reference]
+
+One step = the fused bidirectional forward scan (with backward checkpoints) and
+the analytic backward over one batch of config-2 shaped synthetic input
+(B=1024 rows per GPU, L=64, d_inner=1536, d_state=32 with 16 rotational + 16
+tracking lanes, bf16 delta/u/B/C/dy, fp32 state), plus -- on more than one GPU
+-- one NCCL all-reduce of the scan-parameter gradients (the data-parallel
+exchange of config 4).  Per-GPU work is fixed as N grows ("weak" scaling).
+Inputs (~0.6 GB/GPU) exceed the 126 MB L2, so no flush is needed between steps.
+
+The JSON line also carries the end-to-end leg (host buffers, H2D/D2H copies in
+the timed region), the roofline of the dominant kernel (the backward), the CPU
+baseline (the oracle port of the reference algorithm on the host cores), the
+clocks sampled during the timed region, and the config-3 recurrent-step
+rollout measurement.
+
+``--impl reference`` times the reference algorithm (the CPU oracle port; the
+reference is pure Python/PyTorch and has no GPU path outside Triton) on the
+host cores, on rank 0 only.
+"""
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "scan fwd+bwd Gtokens/s (% HBM peak); recurrent-step rollout node-steps/s/GPU"
+UNIT = "Gtokens/s"
+# config 2 / 4 shape (per GPU)
+B_RANK, L, D, N, N_ROT, MIMO_P = 1024, 64, 1536, 32, 16, 4
+# algorithmic HBM bytes per token at this boundary (bf16 delta/u/B/C/dy, fp32 y)
+FWD_BYTES_PER_TOKEN = 2 * 2 * D + 2 * 2 * N + 4 * D            # 12416
+BWD_BYTES_PER_TOKEN = 3 * 2 * D + 2 * 2 * N + 2 * 2 * D + 2 * 2 * N  # 15616
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def _traffic_per_token():
+    """DRAM bytes/token of the backward kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "scan_bwd_c2_traffic.txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_token:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_scan_rate(rows, min_seconds, max_reps=None):
+    """Reference algorithm (oracle port, fp32 autograd) on the host: tokens/s."""
+    import torch
+    import oracle as O
+    from redpanda_b200.synthetic import ScanShape, make_scan_inputs
+    torch.set_num_threads(os.cpu_count() or 1)
+    inp = make_scan_inputs(ScanShape(rows, L, D, N, N - N_ROT, MIMO_P), seed=123)
+    def once():
+        O.scan_with_grads(inp["delta"], inp["u"], inp["Bc"], inp["Cc"], inp["A_real"],
+                          inp["A_imag"], inp["track"], inp["dy"], bidir=True)
+    once()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        once()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or (max_reps and reps >= max_reps):
+            break
+    return rows * L * reps / el, reps, el
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    from redpanda_b200.synthetic import ScanShape, make_scan_inputs
+    import oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = 4
+    inp = make_scan_inputs(ScanShape(rows, L, D, N, N - N_ROT, MIMO_P), seed=123)
+    def once():
+        O.scan_with_grads(inp["delta"], inp["u"], inp["Bc"], inp["Cc"], inp["A_real"],
+                          inp["A_imag"], inp["track"], inp["dy"], bidir=True)
+    for _ in range(args.warmup):
+        once()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        once()
+    el = time.perf_counter() - t0
+    v = rows * L * args.steps / el / 1e9
+    sample = (f"{rows} rows x L={L} of the config-2 shape per step (bidirectional fwd+bwd, "
+              f"fp32 PyTorch autograd of the reference chunked scan)")
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "c2 bidirectional scan fwd+bwd, CPU sample",
+                       "rows_per_step": rows, "seq_len": L, "d_inner": D, "d_state": N,
+                       "n_rot": N_ROT},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def make_inputs(dev, seed):
+    import torch
+    import torch.nn.functional as F
+    g = torch.Generator(dev).manual_seed(seed)
+    bf = torch.bfloat16
+    n_tr = N - N_ROT
+    x = {
+        "delta": F.softplus(torch.randn(B_RANK, L, D, device=dev, generator=g) * 0.5 - 2).to(bf),
+        "u": torch.randn(B_RANK, L, D, device=dev, generator=g).to(bf),
+    }
+    def bc():
+        raw = torch.randn(B_RANK, L, N * MIMO_P, device=dev, generator=g) / math.sqrt(N)
+        raw = raw * torch.rsqrt(raw.pow(2).mean(-1, keepdim=True) + 1e-5)
+        return raw.view(B_RANK, L, N, MIMO_P).sum(-1).to(bf)
+    x["Bc"], x["Cc"] = bc(), bc()
+    x["dy"] = torch.randn(B_RANK, L, D, device=dev, generator=g).to(bf)
+    ar = -torch.exp(torch.randn(D, N_ROT, device=dev, generator=g) * 0.5)
+    ai = (torch.rand(D, N_ROT, device=dev, generator=g) * 2 - 1) * math.pi
+    tk = torch.tanh(torch.randn(D, n_tr, device=dev, generator=g))
+    return x, ar, ai, tk
+
+
+def run_m3(args):
+    import torch
+    import torch.distributed as dist
+    from redpanda_b200 import scan as S
+    from redpanda_b200.scan import ScanPlan, pad_params
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    if not S.HAS_M3:
+        raise RuntimeError("m3 library or sm_100 device unavailable")
+
+    x, ar, ai, tk = make_inputs(dev, 1000 + rank)
+    Ar_p, Ai_p, Tk_p = (t.contiguous() for t in pad_params(ar, ai, tk, N_ROT, N, D, dev))
+    bf = torch.bfloat16
+    plan = ScanPlan(B_RANK, L, D, N, N_ROT, bf, bf, S.M3_DIR_BIDIR)
+    y = torch.empty(B_RANK, L, D, device=dev)
+    ckpt = torch.empty(plan.ckpt_floats(), device=dev)
+    ws = torch.empty(plan.workspace_bytes(), device=dev, dtype=torch.uint8)
+    gd, gu = torch.empty_like(x["delta"]), torch.empty_like(x["u"])
+    gB, gC = torch.empty_like(x["Bc"]), torch.empty_like(x["Cc"])
+    gflat = torch.empty(3, D, N, device=dev)   # dA_real, dA_imag, dtrack: one all-reduce
+    stream = torch.cuda.current_stream(dev)
+    bwd_events = []
+
+    def step(inputs, timed_bwd=False):
+        plan.forward(inputs["delta"], inputs["u"], inputs["Bc"], inputs["Cc"], Ar_p, Ai_p, Tk_p,
+                     y, ckpt)
+        if timed_bwd:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        plan.backward(inputs["delta"], inputs["u"], inputs["Bc"], inputs["Cc"], Ar_p, Ai_p, Tk_p,
+                      inputs["dy"], ckpt, gd, gu, gB, gC, gflat[0], gflat[1], gflat[2], ws)
+        if timed_bwd:
+            e1.record(stream)
+            bwd_events.append((e0, e1))
+        if world > 1:
+            dist.all_reduce(gflat)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident leg
+    for _ in range(args.warmup):
+        step(x)
+    barrier()
+    clk = ClockSampler(local)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(x, timed_bwd=True)
+    t1.record(stream)
+    barrier()
+    clocks = clk.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1))
+    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in bwd_events)
+    tokens = world * B_RANK * L * args.steps
+    value = tokens / (ms / 1e3) / 1e9
+
+    # ---- end-to-end leg: pinned host inputs copied in, parameter grads copied out
+    host = {k: v.cpu().pin_memory() for k, v in x.items()}
+    dbuf = {k: torch.empty_like(v) for k, v in x.items()}
+    gout = torch.empty(gflat.shape, dtype=gflat.dtype).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = gout.numel() * gout.element_size()
+
+    def e2e_step():
+        for k in host:
+            dbuf[k].copy_(host[k], non_blocking=True)
+        step(dbuf)
+        gout.copy_(gflat, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    t0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    t1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1))
+    e2e_value = tokens / (e2e_ms / 1e3) / 1e9
+
+    step_info = run_step_rollout(dev, args) if (args.rollout and rank == 0) else None
+
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        bwd_bytes = BWD_BYTES_PER_TOKEN * B_RANK * L
+        achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
+        tpt = _traffic_per_token()
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            rate, reps, el = cpu_scan_rate(4, args.cpu_seconds)
+            cpu = {"value": rate / 1e9, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"{reps} x 4 rows x L={L} of the config-2 shape, bidirectional "
+                             f"fwd+bwd, fp32 reference algorithm (oracle port), {el:.1f} s"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "c2: bidirectional scan fwd+bwd (config 2 shape; "
+                                   "config 4's data-parallel grad all-reduce when N>1)",
+                       "batch_per_gpu": B_RANK, "global_batch": B_RANK * world, "seq_len": L,
+                       "d_inner": D, "d_state": N, "n_rot": N_ROT, "mimo_p": MIMO_P,
+                       "parallelism": f"dp{world}", "l2": "inputs larger than L2 (no flush)",
+                       "compute": "fp32 state/accumulation, bf16 inputs and input grads"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps},
+            "gpu_launches": 4 * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "scan_bwd (m3_scan_bwd)",
+                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": (tpt * B_RANK * L) if tpt else None,
+                         "algorithmic_bytes": bwd_bytes, "ms_per_launch": bwd_ms,
+                         "note": "compute-bound (FP32/MUFU issue), see profiles/"},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        if step_info is not None:
+            line["step_rollout"] = step_info
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_step_rollout(dev, args):
+    """Config 3: 12-layer lockstep rollout of B=8192 states, 32 steps, re-anchored
+    every 8 steps by a full L=64 scan with return_state (recurrence kernels only;
+    per-layer token inputs are synthetic)."""
+    import torch
+    from redpanda_b200 import scan as S
+    from redpanda_b200.scan import ScanPlan, pad_params
+    layers, Bs, Ds, Ns, nr = 12, 8192, 1024, 32, 24
+    g = torch.Generator(dev).manual_seed(7)
+    params = []
+    for _ in range(layers):
+        ar = -torch.exp(torch.randn(Ds, nr, device=dev, generator=g) * 0.5)
+        ai = (torch.rand(Ds, nr, device=dev, generator=g) * 2 - 1) * math.pi
+        tk = torch.tanh(torch.randn(Ds, Ns - nr, device=dev, generator=g))
+        params.append(tuple(t.contiguous() for t in pad_params(ar, ai, tk, nr, Ns, Ds, dev)))
+    h = [torch.zeros(Bs, Ds, Ns, device=dev) for _ in range(layers)]
+    db = [torch.zeros(Bs, Ds, Ns, device=dev) for _ in range(layers)]
+    bf = torch.bfloat16
+    seq = {"delta": torch.nn.functional.softplus(
+               torch.randn(Bs, 64, Ds, device=dev, generator=g) * 0.5 - 2).to(bf),
+           "u": torch.randn(Bs, 64, Ds, device=dev, generator=g).to(bf),
+           "Bc": torch.randn(Bs, 64, Ns, device=dev, generator=g).to(bf),
+           "Cc": torch.randn(Bs, 64, Ns, device=dev, generator=g).to(bf)}
+    yseq = torch.empty(Bs, 64, Ds, device=dev)
+    tok = {k: v[:, 0].float().contiguous() for k, v in seq.items()}
+    ystep = torch.empty(Bs, Ds, device=dev)
+    plan = ScanPlan(Bs, 64, Ds, Ns, nr, bf, bf, S.M3_DIR_FWD)
+    lib = S._lib.load()
+    sdesc = S.StepDesc(Bs, Ds, Ns, nr, S.M3_F32, S.M3_F32)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def anchor():
+        for li in range(layers):
+            plan.forward(seq["delta"], seq["u"], seq["Bc"], seq["Cc"], *params[li], yseq,
+                         None, h[li], db[li])
+
+    def one_step():
+        for li in range(layers):
+            ar, ai, tk = params[li]
+            S._lib.check(lib.m3_step(sdesc, h[li].data_ptr(), db[li].data_ptr(),
+                                     tok["delta"].data_ptr(), tok["u"].data_ptr(),
+                                     tok["Bc"].data_ptr(), tok["Cc"].data_ptr(), ar.data_ptr(),
+                                     ai.data_ptr(), tk.data_ptr(), ystep.data_ptr(), sh))
+
+    def rollout():
+        for s in range(32):
+            if s % 8 == 0:
+                anchor()
+            one_step()
+
+    rollout()
+    torch.cuda.synchronize(dev)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record(stream)
+    rollout()
+    e[1].record(stream)
+    for _ in range(32):
+        one_step()
+    e[2].record(stream)
+    torch.cuda.synchronize(dev)
+    total_ms = e[0].elapsed_time(e[1])
+    steps_ms = e[1].elapsed_time(e[2])
+    peak, kind = _peaks()
+    state_bytes = layers * Bs * Ds * Ns * 16
+    return {
+        "workload": "c3: 12 layers, B=8192, D=1024, N=32 (24 rot + 8 track), 32 steps, "
+                    "re-anchor every 8 steps by an L=64 scan with return_state",
+        "node_steps_per_s": Bs * 32 / (total_ms / 1e3),
+        "ms_per_rollout": total_ms,
+        "step_only_node_steps_per_s": Bs * 32 / (steps_ms / 1e3),
+        "step_ms_per_node_step_batch": steps_ms / 32,
+        "step_hbm_gbs": state_bytes / (steps_ms / 32 / 1e3) / 1e9,
+        "step_hbm_frac": state_bytes / (steps_ms / 32 / 1e3) / 1e9 / peak,
+        "step_algorithmic_bytes": state_bytes,
+        "gpu_launches": 32 * layers + 4 * layers,
+        "note": "recurrence kernels only; the projection GEMMs of Mamba.step are not included",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["m3", "reference"], default="m3")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-rollout", dest="rollout", action="store_false",
+                    help="skip the config-3 step rollout measurement")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_m3(args)
+
+
+if __name__ == "__main__":
+    main()

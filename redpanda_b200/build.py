@@ -42,9 +42,9 @@ def _deps():
             if f.endswith((".cuh", ".h"))] + [os.path.join(INCLUDE, "m3scan.h")]
 
 
-def _compile(src, verbose):
-    obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
-    cmd = [_nvcc(), *ARCH, *FLAGS, "-c", src, "-o", obj]
+def _compile(src, verbose, build_dir, extra):
+    obj = os.path.join(build_dir, os.path.basename(src)[:-3] + ".o")
+    cmd = [_nvcc(), *ARCH, *FLAGS, *extra, "-c", src, "-o", obj]
     if verbose:
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -53,29 +53,34 @@ def _compile(src, verbose):
     return obj, r.stderr
 
 
-def build_library(force=False, jobs=None, verbose=False):
-    """Compile the library if any source is newer than it; return its path."""
+def build_library(force=False, jobs=None, verbose=False, out=LIB, extra_flags=(),
+                  build_dir=BUILD):
+    """Compile the library if any source is newer than it; return its path.
+
+    ``out``/``extra_flags``/``build_dir`` build a variant (e.g. ``-D`` tuning
+    macros) next to the default library without touching it.
+    """
     srcs = _sources()
-    if (not force and os.path.exists(LIB)
-            and os.path.getmtime(LIB) >= max(os.path.getmtime(f) for f in srcs + _deps())):
-        return LIB
-    os.makedirs(BUILD, exist_ok=True)
+    if (not force and os.path.exists(out)
+            and os.path.getmtime(out) >= max(os.path.getmtime(f) for f in srcs + _deps())):
+        return out
+    os.makedirs(build_dir, exist_ok=True)
     jobs = jobs or min(len(srcs), os.cpu_count() or 1)
     logs = []
     with cf.ThreadPoolExecutor(jobs) as ex:
         objs = []
-        for obj, log in ex.map(lambda s: _compile(s, verbose), srcs):
+        for obj, log in ex.map(lambda s: _compile(s, verbose, build_dir, list(extra_flags)), srcs):
             objs.append(obj)
             logs.append(log)
-    tmp = LIB + ".tmp"
+    tmp = out + ".tmp"
     cmd = [_nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, LIB)
+    os.replace(tmp, out)
     if verbose:
         sys.stderr.write("\n".join(logs))
-    return LIB
+    return out
 
 
 def main():

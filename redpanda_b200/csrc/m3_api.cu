@@ -22,7 +22,7 @@ int* device_err_ptr() {
 bool select_tile(int n_rot, int n_track, Tile* out) {
   const int rr = (n_rot + 3) / 4, tt = (n_track + 3) / 4;
   static const Tile kTiles[] = {
-#define M3_X(r, t, nd) {r, t, nd},
+#define M3_X(r, t, nd, ndb, nthb) {r, t, nd, ndb, nthb},
       M3_TILE_LIST(M3_X)
 #undef M3_X
   };
@@ -97,7 +97,7 @@ size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
 bool bwd_layout(const m3_scan_desc* d, const Tile& t, BwdLayout* lay) {
   const int sms = device_sms();
   if (sms <= 0) return false;
-  lay->G = (d->d_inner + t.dt() - 1) / t.dt();
+  lay->G = (d->d_inner + t.dt_bwd() - 1) / t.dt_bwd();
   int bg = lay->G >= sms ? 1 : sms / lay->G;
   if (bg > d->batch) bg = d->batch;
   if (bg < 1) bg = 1;
@@ -106,7 +106,7 @@ bool bwd_layout(const m3_scan_desc* d, const Tile& t, BwdLayout* lay) {
   const size_t a_bytes = (size_t)lay->Bg * 3 * d->d_inner * np * 4;
   const size_t bc_bytes = (size_t)lay->G * d->batch * d->seqlen * 2 * np * 4;
   const size_t du_bytes = d->direction == M3_DIR_BIDIR
-                              ? (size_t)lay->G * lay->Bg * d->seqlen * t.dt() * 2 * 4
+                              ? (size_t)lay->G * lay->Bg * d->seqlen * t.dt_bwd() * 2 * 4
                               : 0;
   lay->off_a = 0;
   lay->off_bc = round256(a_bytes);
@@ -232,6 +232,9 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   p.direction = desc->direction;
   p.nch = nchunks(desc->seqlen);
   p.G = lay.G; p.Bg = lay.Bg;
+  p.async_du = aligned(delta, 4) && aligned(u, 4) &&
+               (desc->dtype_du == M3_F32 || (desc->d_inner % 2) == 0);
+  p.async_dy = aligned(dy, 4) && (dtype_dy == M3_F32 || (desc->d_inner % 2) == 0);
   p.err = device_err_ptr();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = launch_scan_bwd(t, p, s);

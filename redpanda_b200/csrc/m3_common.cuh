@@ -25,6 +25,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "m3_math.cuh"
 #include "m3scan.h"
 
 namespace m3 {
@@ -67,13 +68,14 @@ struct LaneMap {
 };
 
 // ---------------------------------------------------------------- cell math
-// Rotational gate.  Accurate libm functions (not the MUFU approximations):
-// the gradient tolerance needs ~1-ulp gates.
-__device__ __forceinline__ float rot_gate(float dl, float ar, float ai) {
-  float e = expf(__fmul_rn(dl, ar));
-  float c = cosf(__fmul_rn(dl, ai));
-  return __fmul_rn(e, c);
+// Rotational gate exp(dl*A_real) * cos(dl*A_imag) from a2 = A_real*log2(e)
+// (m3_math.cuh: ~1e-7 absolute error, no MUFU cosine).
+__device__ __forceinline__ float rot_gate(float dl, float a2, float ai) {
+  return __fmul_rn(gate_exp(dl, a2), gate_cos(dl, ai));
 }
+
+// Per-cell constant of the exponential, computed identically by every kernel.
+__device__ __forceinline__ float exp_const(float ar) { return __fmul_rn(ar, kLog2e); }
 
 // One cell update: returns H = 2*h[t]; P becomes 2*h[t] + dBu[t].
 __device__ __forceinline__ float cell_update(float g, float& P, float du, float b) {

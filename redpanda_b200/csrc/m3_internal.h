@@ -10,10 +10,12 @@ namespace m3 {
 // Per-thread lane tiling: R rotational + T tracking lanes per channel, ND
 // channels per thread, 4 threads per channel group, 128 threads per CTA.
 struct Tile {
-  int R, T, ND;
+  int R, T, ND;      // ND: channels per thread in the forward and step kernels
+  int NDB, NTHB;     // backward: channels per thread, threads per CTA
   int nl() const { return R + T; }
-  int np() const { return 4 * (R + T); }   // padded state lanes per channel
-  int dt() const { return 32 * ND; }       // channels per CTA
+  int np() const { return 4 * (R + T); }       // padded state lanes per channel
+  int dt() const { return 32 * ND; }           // forward channels per CTA
+  int dt_bwd() const { return NTHB / 4 * NDB; }  // backward channels per CTA
 };
 
 // Tile chosen for a (n_rot, n_track) split; identical for scan, backward and
@@ -45,6 +47,7 @@ struct BwdParams {
   int direction;
   int nch;
   int G, Bg;
+  int async_du, async_dy;   // cp.async staging allowed for delta/u and dy
   int* err;
 };
 

@@ -23,6 +23,7 @@
 // a fixed order, so results are bitwise reproducible run to run.
 #include "m3_common.cuh"
 #include "m3_internal.h"
+#include "m3_stage.cuh"
 #include "m3_tiles.h"
 #include "m3_tmem.cuh"
 
@@ -35,36 +36,75 @@ constexpr int pow2ceil(int x) {
   return p;
 }
 
-template <int R, int T, int ND>
+template <int R, int T, int ND, int NTH>
 struct BwdCfg {
   static constexpr int NL = R + T;
   static constexpr int NP = 4 * NL;
-  static constexpr int DT = 32 * ND;
+  static constexpr int NW = NTH / 32;               // warps
+  static constexpr int DT = NTH / 4 * ND;           // channels per CTA
   static constexpr int C = ND * NL;                 // cells per thread
   static constexpr int CS = pow2ceil(C);            // TMEM columns per timestep
-  static constexpr int NCOLS = (kCK * CS < 32) ? 32 : kCK * CS;
-  static constexpr size_t smem_floats =
-      3 * (size_t)kCK * DT + 2 * (size_t)kCK * NP + (size_t)kCK * 4 * 2 * NP;
-  static constexpr size_t smem_bytes = smem_floats * 4 + 16;
+  static constexpr int WG_COLS = kCK * CS;          // TMEM columns per warpgroup
+  static constexpr int NCOLS = (NTH / 128) * WG_COLS < 32 ? 32 : (NTH / 128) * WG_COLS;
+  static constexpr size_t raw_bytes = (size_t)kCK * DT * 4;   // one staged (kCK x DT) tile
+  static constexpr size_t smem_bytes =
+      3 * 2 * raw_bytes                       // delta, u, dy (HBM dtype), double-buffered
+      + 2 * (size_t)DT * NP * 4               // checkpoint tile, double-buffered
+      + 2 * 2 * (size_t)kCK * NP * 4          // B, C (fp32), double-buffered
+      + (size_t)kCK * NW * 2 * NP * 4         // dB/dC warp partials
+      + 16;                                   // TMEM address slot
 };
 
-template <int R, int T, int ND>
-__global__ void __launch_bounds__(kThreads, 1) scan_bwd_kernel(const BwdParams p) {
+// Stage a (kCK x DT) tile of a (B, L, D) tensor for processing steps
+// [s0, s0 + kCK) in its HBM dtype; rows past L and channels past D read zero.
+template <int DT, int NTH>
+__device__ __forceinline__ void stage_tile(unsigned char* dst, const void* src, int esz,
+                                           bool async_ok, int b, int d0, int s0, int dir,
+                                           int L, int D) {
+  if (async_ok) {
+    const int epw = 4 / esz, wpr = DT / epw;
+    for (int i = threadIdx.x; i < kCK * wpr; i += NTH) {
+      const int tt = i / wpr, w = i - tt * wpr;
+      const int s = s0 + tt, d = d0 + w * epw;
+      const bool ok = (s < L) && (d < D);
+      const int t = dir ? L - 1 - s : s;
+      const size_t gi = ok ? ((size_t)b * L + t) * D + d : 0;
+      cp_async4(dst + (size_t)i * 4, (const char*)src + gi * esz, ok);
+    }
+  } else {
+    for (int i = threadIdx.x; i < kCK * DT; i += NTH) {
+      const int tt = i / DT, dd = i - tt * DT;
+      const int s = s0 + tt, d = d0 + dd;
+      const bool ok = (s < L) && (d < D);
+      const int t = dir ? L - 1 - s : s;
+      const size_t gi = ok ? ((size_t)b * L + t) * D + d : 0;
+      if (esz == 2) ((uint16_t*)dst)[i] = ok ? ((const uint16_t*)src)[gi] : (uint16_t)0;
+      else ((float*)dst)[i] = ok ? ((const float*)src)[gi] : 0.f;
+    }
+  }
+}
+
+template <int R, int T, int ND, int NTH>
+__global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
   using LM = LaneMap<R, T>;
-  using CF = BwdCfg<R, T, ND>;
-  constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS;
+  using CF = BwdCfg<R, T, ND, NTH>;
+  constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS, NW = CF::NW;
   constexpr int RR = R > 0 ? R : 1;
   constexpr int TT = T > 0 ? T : 1;
+  constexpr int BCE = (kCK * NP + NTH - 1) / NTH;
+  constexpr int V = 2 * NL;                  // dB + dC partials per thread per step
+  constexpr int V8 = (V + 7) / 8 * 8;        // padded to the 8-group butterfly
   static_assert(CF::NCOLS <= 512, "TMEM holds at most 512 columns");
 
-  extern __shared__ __align__(16) float sm[];
-  float* s_dl = sm;                          // [kCK][DT]
-  float* s_u = s_dl + kCK * DT;              // [kCK][DT]
-  float* s_dy = s_u + kCK * DT;              // [kCK][DT]
-  float* s_b = s_dy + kCK * DT;              // [kCK][NP]
-  float* s_c = s_b + kCK * NP;               // [kCK][NP]
-  float* s_red = s_c + kCK * NP;             // [kCK][4 warps][2][NP]
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_red + kCK * 4 * 2 * NP);
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned char* s_dl = smem;                                   // [2][raw]
+  unsigned char* s_u = s_dl + 2 * CF::raw_bytes;                // [2][raw]
+  unsigned char* s_dy = s_u + 2 * CF::raw_bytes;                // [2][raw]
+  float* s_ck = reinterpret_cast<float*>(s_dy + 2 * CF::raw_bytes);  // [2][DT][NP]
+  float* s_b = s_ck + 2 * DT * NP;                              // [2][kCK][NP]
+  float* s_c = s_b + 2 * kCK * NP;                              // [2][kCK][NP]
+  float* s_red = s_c + 2 * kCK * NP;                            // [kCK][NW][2][NP]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_red + kCK * NW * 2 * NP);
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
   const int warp = tid >> 5, lane = tid & 31;
@@ -73,12 +113,18 @@ __global__ void __launch_bounds__(kThreads, 1) scan_bwd_kernel(const BwdParams p
   const int B = p.B, L = p.L, D = p.D, N = p.N;
   const bool bidir = p.direction == M3_DIR_BIDIR;
   const int ndirs = bidir ? 2 : 1;
+  const int nch = p.nch;
+  const bool bf_du = p.dt_du == M3_BF16, bf_dy = p.dt_dy == M3_BF16;
+  const int es_du = bf_du ? 2 : 4, es_dy = bf_dy ? 2 : 4;
+  const bool async_du = p.async_du, async_dy = p.async_dy;
 
   if (warp == 0) tmem_alloc(s_tmem, CF::NCOLS);
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
-  const uint32_t tbase = *s_tmem + ((uint32_t)(warp * 32) << 16);
+  // warp w reads/writes TMEM lanes 32*(w%4).. of column block w/4
+  const uint32_t tbase =
+      *s_tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * CF::WG_COLS);
 
   float ar[ND][RR], ai[ND][RR], tk[ND][TT];
 #pragma unroll
@@ -110,207 +156,279 @@ __global__ void __launch_bounds__(kThreads, 1) scan_bwd_kernel(const BwdParams p
   const int cta = gt * p.Bg + bg;
   float* scratch = p.scratch_du ? p.scratch_du + (size_t)cta * L * DT * 2 : nullptr;
 
-  for (int b = bg; b < B; b += p.Bg) {
-    for (int pass = 0; pass < ndirs; ++pass) {
-      const int dir = bidir ? pass : p.direction;
-      const int dslot = bidir ? dir : 0;
-      const bool first_of_two = bidir && pass == 0;
-      const bool second_of_two = bidir && pass == 1;
+  // work items in processing order: rows b = bg, bg+Bg, ...; per row the
+  // directions; per direction the chunks from last to first
+  const int rows = bg < B ? (B - bg + p.Bg - 1) / p.Bg : 0;
+  const int per_row = ndirs * nch;
+  const int nitems = rows * per_row;
+  auto item = [&](int i, int& b, int& pass, int& c) {
+    const int r = i / per_row, rem = i - r * per_row;
+    b = bg + r * p.Bg;
+    pass = rem / nch;
+    c = nch - 1 - (rem - pass * nch);
+  };
+  auto dir_of = [&](int pass) { return bidir ? pass : p.direction; };
 
-      float qv[ND][NL], gn[ND][RR];
+  float rb[BCE], rc[BCE];
+  auto load_bc = [&](int b, int dir, int s0) {
+#pragma unroll
+    for (int e = 0; e < BCE; ++e) {
+      const int i = tid + e * NTH;
+      const int tt = i / NP, ln = i - tt * NP;
+      const int s = s0 + tt;
+      const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
+      const bool ok = (i < kCK * NP) && (s < L) && (n >= 0);
+      const int t = dir ? L - 1 - s : s;
+      const size_t gi = ok ? ((size_t)b * L + t) * N + n : 0;
+      rb[e] = ok ? ld_f(p.Bc, gi, p.dt_bc) : 0.f;
+      rc[e] = ok ? ld_f(p.Cc, gi, p.dt_bc) : 0.f;
+    }
+  };
+  auto store_bc = [&](int buf) {
+#pragma unroll
+    for (int e = 0; e < BCE; ++e) {
+      const int i = tid + e * NTH;
+      if (i < kCK * NP) {
+        s_b[buf * kCK * NP + i] = rb[e];
+        s_c[buf * kCK * NP + i] = rc[e];
+      }
+    }
+  };
+  auto stage = [&](int i, int buf) {
+    int b, pass, c;
+    item(i, b, pass, c);
+    const int dir = dir_of(pass), s0 = c * kCK;
+    stage_tile<DT, NTH>(s_dl + buf * CF::raw_bytes, p.delta, es_du, async_du, b, d0, s0, dir, L, D);
+    stage_tile<DT, NTH>(s_u + buf * CF::raw_bytes, p.u, es_du, async_du, b, d0, s0, dir, L, D);
+    stage_tile<DT, NTH>(s_dy + buf * CF::raw_bytes, p.dy, es_dy, async_dy, b, d0, s0, dir, L, D);
+    if (c > 0) {
+      const int dslot = bidir ? dir : 0;
+      const float* src = p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
+      float* dst = s_ck + buf * DT * NP;
+      for (int v = tid; v < DT * NP / 4; v += NTH) {
+        const bool ok = d0 + (v * 4) / NP < D;
+        cp_async16(dst + v * 4, ok ? src + v * 4 : p.ckpt, ok);
+      }
+    }
+  };
+
+  float qv[C], gn[ND * RR];
+  if (nitems > 0) {
+    stage(0, 0);
+    cp_async_commit();
+    {
+      int b, pass, c;
+      item(0, b, pass, c);
+      load_bc(b, dir_of(pass), c * kCK);
+      store_bc(0);
+    }
+  }
+  for (int it = 0; it < nitems; ++it) {
+    const int buf = it & 1;
+    int b, pass, c;
+    item(it, b, pass, c);
+    const int dir = dir_of(pass);
+    const bool first_of_two = bidir && pass == 0;
+    const bool second_of_two = bidir && pass == 1;
+    const int s0 = c * kCK;
+    const int ns = min(kCK, L - s0);
+    const bool more = it + 1 < nitems;
+    if (more) stage(it + 1, buf ^ 1);
+    cp_async_commit();
+    if (more) {
+      int b2, pass2, c2;
+      item(it + 1, b2, pass2, c2);
+      load_bc(b2, dir_of(pass2), c2 * kCK);
+    }
+    cp_async_wait1();
+    __syncthreads();
+
+    if (c == nch - 1) {   // first chunk of a direction pass: adjoint state starts at zero
+#pragma unroll
+      for (int i = 0; i < C; ++i) qv[i] = 0.f;
+#pragma unroll
+      for (int i = 0; i < ND * RR; ++i) gn[i] = 0.f;
+    }
+
+    const unsigned char* bdl = s_dl + buf * CF::raw_bytes;
+    const unsigned char* bu = s_u + buf * CF::raw_bytes;
+    const unsigned char* bdy = s_dy + buf * CF::raw_bytes;
+    const float* bb = s_b + buf * kCK * NP;
+    const float* bc = s_c + buf * kCK * NP;
+
+    // ---- forward recompute of the chunk; P[t-1] of every cell -> TMEM
+    float P[C];
+    {
+      const float* ck = s_ck + buf * DT * NP + grp * ND * NP + q * NL;
+#pragma unroll
+      for (int k = 0; k < ND; ++k)
+#pragma unroll
+        for (int j = 0; j < NL; ++j) P[k * NL + j] = c > 0 ? ck[k * NP + j] : 0.f;
+    }
+    for (int tt = 0; tt < ns; ++tt) {
+      tmem_store<C>(tbase + (uint32_t)(tt * CS), P);
+      float dl[ND], uu[ND];
+      read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
+      read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
+      const float* rbv = bb + tt * NP + q * NL;
 #pragma unroll
       for (int k = 0; k < ND; ++k) {
+        const float du = __fmul_rn(dl[k], uu[k]);
 #pragma unroll
-        for (int j = 0; j < NL; ++j) qv[k][j] = 0.f;
+        for (int j = 0; j < R; ++j)
+          cell_update(rot_gate(dl[k], exp_const(ar[k][j]), ai[k][j]), P[k * NL + j], du, rbv[j]);
 #pragma unroll
-        for (int j = 0; j < RR; ++j) gn[k][j] = 0.f;
+        for (int j = R; j < NL; ++j) cell_update(tk[k][j - R], P[k * NL + j], du, rbv[j]);
       }
+    }
+    tmem_wait_st();
 
-      for (int c = p.nch - 1; c >= 0; --c) {
-        const int s0 = c * kCK;
-        const int ns = min(kCK, L - s0);
-        __syncthreads();  // previous chunk's shared-memory readers are done
-        for (int i = tid; i < kCK * DT; i += kThreads) {
-          const int tt = i / DT, dd = i - tt * DT;
-          const int s = s0 + tt, d = d0 + dd;
-          const bool ok = (s < L) && (d < D);
-          const int t = dir ? L - 1 - s : s;
-          const size_t gi = ok ? ((size_t)b * L + t) * D + d : 0;
-          s_dl[i] = ok ? ld_f(p.delta, gi, p.dt_du) : 0.f;
-          s_u[i] = ok ? ld_f(p.u, gi, p.dt_du) : 0.f;
-          s_dy[i] = ok ? ld_f(p.dy, gi, p.dt_dy) : 0.f;
+    // ---- reverse recurrence
+    for (int tt = ns - 1; tt >= 0; --tt) {
+      float Pp[C];
+      tmem_load<C>(tbase + (uint32_t)(tt * CS), Pp);
+      const int s = s0 + tt;
+      const int t = dir ? L - 1 - s : s;
+      float dl[ND], uu[ND], dyv[ND];
+      read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
+      read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
+      read_chan<ND>(bdy + (size_t)(tt * DT + grp * ND) * es_dy, bf_dy, dyv);
+      const float* rbv = bb + tt * NP + q * NL;
+      const float* rcv = bc + tt * NP + q * NL;
+      float Bv[NL], Cv[NL], pB[NL], pC[NL];
+#pragma unroll
+      for (int j = 0; j < NL; ++j) {
+        Bv[j] = rbv[j];
+        Cv[j] = rcv[j];
+        pB[j] = 0.f;
+        pC[j] = 0.f;
+      }
+      tmem_wait_ld();
+      float gsum[ND], sbs[ND];
+#pragma unroll
+      for (int k = 0; k < ND; ++k) {
+        const float dlk = dl[k], dyk = dyv[k];
+        const float du = __fmul_rn(dlk, uu[k]);
+        float gs = 0.f, sB = 0.f;
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+          const float pp = Pp[k * NL + j];
+          const float e = gate_exp(dlk, exp_const(ar[k][j]));
+          float sn, cs;
+          gate_sincos(dlk, ai[k][j], sn, cs);
+          const float g = __fmul_rn(e, cs);
+          const float es = __fmul_rn(e, sn);
+          const float dbu = __fmul_rn(du, Bv[j]);
+          const float H = __fmaf_rn(g, pp, dbu);
+          const float dyC = __fmul_rn(dyk, Cv[j]);
+          const float qn = __fmaf_rn(gn[k * RR + j], qv[k * NL + j], dyC);
+          const float ddbu = __fmaf_rn(-0.5f, dyC, qn);
+          const float wp = __fmul_rn(qn, pp);
+          const float wg = __fmul_rn(wp, g);
+          const float ws = __fmul_rn(wp, es);
+          gAr[k][j] = __fmaf_rn(dlk, wg, gAr[k][j]);
+          gAi[k][j] = __fmaf_rn(-dlk, ws, gAi[k][j]);
+          gs = __fmaf_rn(ar[k][j], wg, gs);
+          gs = __fmaf_rn(-ai[k][j], ws, gs);
+          sB = __fmaf_rn(ddbu, Bv[j], sB);
+          pB[j] = __fmaf_rn(ddbu, du, pB[j]);
+          pC[j] = __fmaf_rn(dyk, H, pC[j]);
+          qv[k * NL + j] = qn;
+          gn[k * RR + j] = g;
         }
-        for (int i = tid; i < kCK * NP; i += kThreads) {
-          const int tt = i / NP, ln = i - tt * NP;
-          const int s = s0 + tt;
-          const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
-          const bool ok = (s < L) && (n >= 0);
-          const int t = dir ? L - 1 - s : s;
-          const size_t gi = ok ? ((size_t)b * L + t) * N + n : 0;
-          s_b[i] = ok ? ld_f(p.Bc, gi, p.dt_bc) : 0.f;
-          s_c[i] = ok ? ld_f(p.Cc, gi, p.dt_bc) : 0.f;
+#pragma unroll
+        for (int j = R; j < NL; ++j) {
+          const float pp = Pp[k * NL + j];
+          const float g = tk[k][j - R];
+          const float dbu = __fmul_rn(du, Bv[j]);
+          const float H = __fmaf_rn(g, pp, dbu);
+          const float dyC = __fmul_rn(dyk, Cv[j]);
+          const float qn = __fmaf_rn(g, qv[k * NL + j], dyC);
+          const float ddbu = __fmaf_rn(-0.5f, dyC, qn);
+          const float wp = __fmul_rn(qn, pp);
+          gTk[k][j - R] = __fadd_rn(gTk[k][j - R], wp);
+          sB = __fmaf_rn(ddbu, Bv[j], sB);
+          pB[j] = __fmaf_rn(ddbu, du, pB[j]);
+          pC[j] = __fmaf_rn(dyk, H, pC[j]);
+          qv[k * NL + j] = qn;
         }
-        float P[C];
+        gsum[k] = gs;
+        sbs[k] = sB;
+      }
+      // per-channel outputs: reduce over the 4 lane quarters
 #pragma unroll
-        for (int k = 0; k < ND; ++k) {
-          const int d = dbase + k;
-          const float* src =
-              (c > 0 && d < D)
-                  ? p.ckpt + ((((size_t)b * ndirs + dslot) * (p.nch - 1) + (c - 1)) * D + d) * NP +
-                        q * NL
-                  : nullptr;
-#pragma unroll
-          for (int j = 0; j < NL; ++j) P[k * NL + j] = src ? src[j] : 0.f;
-        }
-        __syncthreads();
-
-        // ---- forward recompute of the chunk; P[t-1] of every cell -> TMEM
-        for (int tt = 0; tt < ns; ++tt) {
-          tmem_store<C>(tbase + (uint32_t)(tt * CS), P);
-          const float* rdl = s_dl + tt * DT + grp * ND;
-          const float* ru = s_u + tt * DT + grp * ND;
-          const float* rb = s_b + tt * NP + q * NL;
-#pragma unroll
-          for (int k = 0; k < ND; ++k) {
-            const float dl = rdl[k];
-            const float du = __fmul_rn(dl, ru[k]);
-#pragma unroll
-            for (int j = 0; j < R; ++j)
-              cell_update(rot_gate(dl, ar[k][j], ai[k][j]), P[k * NL + j], du, rb[j]);
-#pragma unroll
-            for (int j = R; j < NL; ++j) cell_update(tk[k][j - R], P[k * NL + j], du, rb[j]);
-          }
-        }
-        tmem_wait_st();
-
-        // ---- reverse recurrence
-        for (int tt = ns - 1; tt >= 0; --tt) {
-          float Pp[C];
-          tmem_load<C>(tbase + (uint32_t)(tt * CS), Pp);
-          tmem_wait_ld();
-          const int s = s0 + tt;
-          const int t = dir ? L - 1 - s : s;
-          const float* rdl = s_dl + tt * DT + grp * ND;
-          const float* ru = s_u + tt * DT + grp * ND;
-          const float* rdy = s_dy + tt * DT + grp * ND;
-          const float* rb = s_b + tt * NP + q * NL;
-          const float* rc = s_c + tt * NP + q * NL;
-          float Bv[NL], Cv[NL], pB[NL], pC[NL];
-#pragma unroll
-          for (int j = 0; j < NL; ++j) {
-            Bv[j] = rb[j];
-            Cv[j] = rc[j];
-            pB[j] = 0.f;
-            pC[j] = 0.f;
-          }
-          float gsum[ND], sbs[ND];
-#pragma unroll
-          for (int k = 0; k < ND; ++k) {
-            const float dl = rdl[k], uu = ru[k], dyv = rdy[k];
-            const float du = __fmul_rn(dl, uu);
-            float gs = 0.f, sB = 0.f;
-#pragma unroll
-            for (int j = 0; j < R; ++j) {
-              const float pp = Pp[k * NL + j];
-              const float e = expf(__fmul_rn(dl, ar[k][j]));
-              float sn, cs;
-              sincosf(__fmul_rn(dl, ai[k][j]), &sn, &cs);
-              const float g = __fmul_rn(e, cs);
-              const float es = __fmul_rn(e, sn);
-              const float dbu = __fmul_rn(du, Bv[j]);
-              const float H = __fmaf_rn(g, pp, dbu);
-              const float dyC = __fmul_rn(dyv, Cv[j]);
-              const float qn = __fmaf_rn(gn[k][j], qv[k][j], dyC);
-              const float ddbu = __fmaf_rn(-0.5f, dyC, qn);
-              const float wp = __fmul_rn(qn, pp);
-              const float wg = __fmul_rn(wp, g);
-              const float ws = __fmul_rn(wp, es);
-              gAr[k][j] = __fmaf_rn(dl, wg, gAr[k][j]);
-              gAi[k][j] = __fmaf_rn(-dl, ws, gAi[k][j]);
-              gs = __fmaf_rn(ar[k][j], wg, gs);
-              gs = __fmaf_rn(-ai[k][j], ws, gs);
-              sB = __fmaf_rn(ddbu, Bv[j], sB);
-              pB[j] = __fmaf_rn(ddbu, du, pB[j]);
-              pC[j] = __fmaf_rn(dyv, H, pC[j]);
-              qv[k][j] = qn;
-              gn[k][j] = g;
+      for (int k = 0; k < ND; ++k) {
+        const float gsv = quad_sum(gsum[k]);
+        const float sBv = quad_sum(sbs[k]);
+        const int d = dbase + k;
+        if ((k & 3) == q && d < D) {
+          float ddl = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, uu[k]));
+          float ddu = __fmul_rn(sBv, dl[k]);
+          const size_t oi = ((size_t)b * L + t) * D + d;
+          float* sc = scratch ? scratch + ((size_t)t * DT + (d - d0)) * 2 : nullptr;
+          if (first_of_two) {
+            sc[0] = ddl;
+            sc[1] = ddu;
+          } else {
+            if (second_of_two) {
+              ddl = __fadd_rn(sc[0], ddl);
+              ddu = __fadd_rn(sc[1], ddu);
             }
-#pragma unroll
-            for (int j = R; j < NL; ++j) {
-              const float pp = Pp[k * NL + j];
-              const float g = tk[k][j - R];
-              const float dbu = __fmul_rn(du, Bv[j]);
-              const float H = __fmaf_rn(g, pp, dbu);
-              const float dyC = __fmul_rn(dyv, Cv[j]);
-              const float qn = __fmaf_rn(g, qv[k][j], dyC);
-              const float ddbu = __fmaf_rn(-0.5f, dyC, qn);
-              const float wp = __fmul_rn(qn, pp);
-              gTk[k][j - R] = __fadd_rn(gTk[k][j - R], wp);
-              sB = __fmaf_rn(ddbu, Bv[j], sB);
-              pB[j] = __fmaf_rn(ddbu, du, pB[j]);
-              pC[j] = __fmaf_rn(dyv, H, pC[j]);
-              qv[k][j] = qn;
-            }
-            gsum[k] = gs;
-            sbs[k] = sB;
-          }
-          // per-channel outputs: reduce over the 4 lane quarters
-#pragma unroll
-          for (int k = 0; k < ND; ++k) {
-            const float gsv = quad_sum(gsum[k]);
-            const float sBv = quad_sum(sbs[k]);
-            const int d = dbase + k;
-            if ((k & 3) == q && d < D) {
-              float ddl = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, ru[k]));
-              float ddu = __fmul_rn(sBv, rdl[k]);
-              const size_t oi = ((size_t)b * L + t) * D + d;
-              float* sc = scratch ? scratch + ((size_t)t * DT + (d - d0)) * 2 : nullptr;
-              if (first_of_two) {
-                sc[0] = ddl;
-                sc[1] = ddu;
-              } else {
-                if (second_of_two) {
-                  ddl = __fadd_rn(sc[0], ddl);
-                  ddu = __fadd_rn(sc[1], ddu);
-                }
-                st_f(p.d_delta, oi, p.dt_du, ddl);
-                st_f(p.d_u, oi, p.dt_du, ddu);
-              }
-            }
-          }
-          // dB/dC partial over this warp's 8 channel groups
-#pragma unroll
-          for (int j = 0; j < NL; ++j) {
-#pragma unroll
-            for (int m = 4; m < 32; m <<= 1) {
-              pB[j] = __fadd_rn(pB[j], __shfl_xor_sync(0xffffffffu, pB[j], m));
-              pC[j] = __fadd_rn(pC[j], __shfl_xor_sync(0xffffffffu, pC[j], m));
-            }
-          }
-          if (lane < 4) {
-            float* r0 = s_red + ((size_t)(tt * 4 + warp) * 2) * NP + q * NL;
-#pragma unroll
-            for (int j = 0; j < NL; ++j) {
-              r0[j] = pB[j];
-              r0[NP + j] = pC[j];
-            }
+            st_f(p.d_delta, oi, p.dt_du, ddl);
+            st_f(p.d_u, oi, p.dt_du, ddu);
           }
         }
-        __syncthreads();
-        // flush this chunk's dB/dC partials: fixed order over the 4 warps
-        for (int i = tid; i < ns * 2 * NP; i += kThreads) {
-          const int tt = i / (2 * NP), rem = i - tt * 2 * NP;
-          const int which = rem / NP, ln = rem - which * NP;
-          const float* r = s_red + ((size_t)tt * 4 * 2 + which) * NP + ln;
-          const float v = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[2 * NP]), r[4 * NP]), r[6 * NP]);
-          const int s = s0 + tt;
-          const int t = dir ? L - 1 - s : s;
-          float* dst = p.part_bc + ((((size_t)gt * B + b) * L + t) * 2 + which) * NP + ln;
-          *dst = second_of_two ? __fadd_rn(*dst, v) : v;
+      }
+      // dB/dC over this warp's 8 channel groups (lanes q, q+4, ..., q+28):
+      // transposed butterfly, after which each lane holds V8/8 fully reduced
+      // values; value i of lane l is original index
+      // ((l>>2)&1)*V8/2 + ((l>>3)&1)*V8/4 + ((l>>4)&1)*V8/8 + i.
+      {
+        float v[V8];
+#pragma unroll
+        for (int j = 0; j < NL; ++j) { v[j] = pB[j]; v[NL + j] = pC[j]; }
+#pragma unroll
+        for (int j = V; j < V8; ++j) v[j] = 0.f;
+#pragma unroll
+        for (int lvl = 0; lvl < 3; ++lvl) {
+          const int m = 4 << lvl;
+          const int half = V8 >> (lvl + 1);
+          const bool hi = (lane & m) != 0;
+#pragma unroll
+          for (int i = 0; i < half; ++i) {
+            const float send = hi ? v[i] : v[i + half];
+            const float keep = hi ? v[i + half] : v[i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+          }
+        }
+        const int obase = ((lane >> 2) & 1) * (V8 / 2) + ((lane >> 3) & 1) * (V8 / 4) +
+                          ((lane >> 4) & 1) * (V8 / 8);
+        float* r0 = s_red + (size_t)(tt * NW + warp) * 2 * NP + q * NL;
+#pragma unroll
+        for (int i = 0; i < V8 / 8; ++i) {
+          const int o = obase + i;
+          if (o < NL) r0[o] = v[i];
+          else if (o < V) r0[NP + (o - NL)] = v[i];
         }
       }
     }
+    __syncthreads();
+    // flush this chunk's dB/dC partials: fixed order over the 4 warps
+    for (int i = tid; i < ns * 2 * NP; i += NTH) {
+      const int tt = i / (2 * NP), rem = i - tt * 2 * NP;
+      const int which = rem / NP, ln = rem - which * NP;
+      const float* r = s_red + ((size_t)tt * NW * 2 + which) * NP + ln;
+      float v = r[0];
+#pragma unroll
+      for (int w = 1; w < NW; ++w) v = __fadd_rn(v, r[(size_t)w * 2 * NP]);
+      const int s = s0 + tt;
+      const int t = dir ? L - 1 - s : s;
+      float* dst = p.part_bc + ((((size_t)gt * B + b) * L + t) * 2 + which) * NP + ln;
+      *dst = second_of_two ? __fadd_rn(*dst, v) : v;
+    }
+    if (more) store_bc(buf ^ 1);
   }
+  cp_async_wait0();
 
   // dA partial of this batch group
 #pragma unroll
@@ -382,23 +500,23 @@ __global__ void reduce_a_kernel(const ReduceParams p, int R, int T) {
   }
 }
 
-template <int R, int T, int ND>
+template <int R, int T, int ND, int NTH>
 cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
-  using CF = BwdCfg<R, T, ND>;
-  auto kern = scan_bwd_kernel<R, T, ND>;
+  using CF = BwdCfg<R, T, ND, NTH>;
+  auto kern = scan_bwd_kernel<R, T, ND, NTH>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)CF::smem_bytes);
   if (e != cudaSuccess) return e;
   dim3 grid(p.Bg, p.G);
-  kern<<<grid, kThreads, CF::smem_bytes, stream>>>(p);
+  kern<<<grid, NTH, CF::smem_bytes, stream>>>(p);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s) {
-#define M3_X(r, tt, nd) \
-  if (t.R == r && t.T == tt && t.ND == nd) return launch_bwd_impl<r, tt, nd>(p, s);
+#define M3_X(r, tt, nd, ndb, nthb) \
+  if (t.R == r && t.T == tt && t.ND == nd) return launch_bwd_impl<r, tt, ndb, nthb>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;

@@ -13,26 +13,11 @@
 // thread lane layout.  y is reduced over the 4 lane quarters with shuffles.
 #include "m3_common.cuh"
 #include "m3_internal.h"
+#include "m3_stage.cuh"
 #include "m3_tiles.h"
 
 namespace m3 {
 namespace {
-
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool valid) {
-  uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  int sz = valid ? 4 : 0;  // src-size 0 => zero fill
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(sz)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
-}
-__device__ __forceinline__ void cp_async_wait1() {
-  asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-}
-__device__ __forceinline__ void cp_async_wait0() {
-  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-}
 
 // Stage delta and u for processing steps [s0, s0 + kCK) of row b, channels
 // [d0, d0 + DT), in their HBM dtype, into one shared buffer pair.  Rows past the
@@ -73,40 +58,27 @@ __device__ __forceinline__ void stage_du(unsigned char* s_dl, unsigned char* s_u
   }
 }
 
-// ND channel values of one staged row, converted to fp32.
-template <int ND>
-__device__ __forceinline__ void read_chan(const unsigned char* base, bool bf16, float (&v)[ND]) {
-  if (bf16) {
-    if constexpr (ND % 2 == 0) {
-      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(base);
-#pragma unroll
-      for (int i = 0; i < ND / 2; ++i) {
-        float2 f = __bfloat1622float2(p2[i]);
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
-      }
-    } else {
-      const __nv_bfloat16* p1 = reinterpret_cast<const __nv_bfloat16*>(base);
-#pragma unroll
-      for (int i = 0; i < ND; ++i) v[i] = __bfloat162float(p1[i]);
-    }
-  } else {
-    const float* pf = reinterpret_cast<const float*>(base);
-    if constexpr (ND % 4 == 0) {
-#pragma unroll
-      for (int i = 0; i < ND / 4; ++i) {
-        float4 f = reinterpret_cast<const float4*>(pf)[i];
-        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < ND; ++i) v[i] = pf[i];
-    }
+// Stage y (fp32) of processing steps [s0, s0 + kCK) for the second pass of the
+// bidirectional scan, which adds the first pass's output.
+template <int DT>
+__device__ __forceinline__ void stage_y(float* s_y, const FwdParams& p, int b, int d0, int s0,
+                                        int dir) {
+  for (int i = threadIdx.x; i < kCK * DT; i += kThreads) {
+    const int tt = i / DT, dd = i - tt * DT;
+    const int s = s0 + tt, d = d0 + dd;
+    const bool ok = (s < p.L) && (d < p.D);
+    const int t = dir ? p.L - 1 - s : s;
+    const size_t gi = ok ? ((size_t)b * p.L + t) * p.D + d : 0;
+    cp_async4(s_y + i, p.y + gi, ok);
   }
 }
 
+#ifndef M3_FWD_MIN_BLOCKS
+#define M3_FWD_MIN_BLOCKS 3
+#endif
+
 template <int R, int T, int ND>
-__global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdParams p) {
+__global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(const FwdParams p) {
   using LM = LaneMap<R, T>;
   constexpr int NL = R + T;
   constexpr int NP = LM::NP;
@@ -120,6 +92,7 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdParams p) {
   unsigned char* s_u = s_dl + 2 * kCK * DT * 4;               // [2][kCK*DT*4]
   float* s_b = reinterpret_cast<float*>(s_u + 2 * kCK * DT * 4);  // [2][kCK][NP]
   float* s_c = s_b + 2 * kCK * NP;
+  float* s_y = s_c + 2 * kCK * NP;                            // [2][kCK][DT] (bidir pass 2)
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
   const int b = blockIdx.x;
@@ -140,7 +113,7 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdParams p) {
       const bool ok = (d < D) && (n >= 0);
       const size_t gi = ok ? (size_t)d * N + n : 0;
       if (j < R) {
-        ar[k][j] = ok ? p.Ar[gi] : 0.f;
+        ar[k][j] = ok ? exp_const(p.Ar[gi]) : 0.f;   // A_real * log2(e)
         ai[k][j] = ok ? p.Ai[gi] : 0.f;
       } else {
         tk[k][j - R] = ok ? p.Tk[gi] : 0.f;
@@ -189,6 +162,7 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdParams p) {
 
     // prologue: chunk 0 into buffer 0
     stage_du<DT>(s_dl, s_u, p, b, d0, 0, dir, esz);
+    if (accumulate) stage_y<DT>(s_y, p, b, d0, 0, dir);
     cp_async_commit();
     load_bc(0);
     store_bc(0);
@@ -196,9 +170,11 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdParams p) {
     for (int c = 0; c < p.nch; ++c) {
       const int buf = c & 1;
       const bool more = c + 1 < p.nch;
-      if (more)
+      if (more) {
         stage_du<DT>(s_dl + (buf ^ 1) * kCK * DT * 4, s_u + (buf ^ 1) * kCK * DT * 4, p, b, d0,
                      (c + 1) * kCK, dir, esz);
+        if (accumulate) stage_y<DT>(s_y + (buf ^ 1) * kCK * DT, p, b, d0, (c + 1) * kCK, dir);
+      }
       cp_async_commit();
       if (more) load_bc((c + 1) * kCK);
       cp_async_wait1();
@@ -222,6 +198,7 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdParams p) {
       const unsigned char* bu = s_u + buf * kCK * DT * 4;
       const float* bb = s_b + buf * kCK * NP;
       const float* bc = s_c + buf * kCK * NP;
+      const float* by = s_y + buf * kCK * DT;
       const int ns = min(kCK, L - c * kCK);
       for (int tt = 0; tt < ns; ++tt) {
         const int s = c * kCK + tt;
@@ -268,7 +245,7 @@ __global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdParams p) {
           const float tot = __fmul_rn(0.5f, quad_sum(part[k]));
           const int d = dbase + k;
           if ((k & 3) == q && d < D) {
-            yrow[d] = accumulate ? __fadd_rn(tot, yrow[d]) : tot;
+            yrow[d] = accumulate ? __fadd_rn(tot, by[tt * DT + grp * ND + k]) : tot;
           }
         }
       }
@@ -283,7 +260,8 @@ template <int R, int T, int ND>
 cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
   constexpr int NP = 4 * (R + T);
   constexpr int DT = 32 * ND;
-  const size_t smem = 2 * (2 * (size_t)kCK * DT * 4) + 2 * (2 * (size_t)kCK * NP * 4);
+  const size_t smem = 2 * (2 * (size_t)kCK * DT * 4) + 2 * (2 * (size_t)kCK * NP * 4) +
+                      (p.direction == M3_DIR_BIDIR ? 2 * (size_t)kCK * DT * 4 : 0);
   auto kern = scan_fwd_kernel<R, T, ND>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
@@ -296,7 +274,7 @@ cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
-#define M3_X(r, tt, nd) \
+#define M3_X(r, tt, nd, ndb, nthb) \
   if (t.R == r && t.T == tt && t.ND == nd) return launch_fwd_impl<r, tt, nd>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X

@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kThreads) step_kernel(const StepParams p) {
     const size_t gp = (size_t)(dok ? d : 0) * N + (lane[j] >= 0 ? lane[j] : 0);
     float g;
     if (j < R) {
-      const float ar = lane[j] >= 0 ? p.Ar[gp] : 0.f;
+      const float ar = lane[j] >= 0 ? exp_const(p.Ar[gp]) : 0.f;
       const float ai = lane[j] >= 0 ? p.Ai[gp] : 0.f;
       g = rot_gate(dl, ar, ai);
     } else {
@@ -82,7 +82,7 @@ cudaError_t launch_step_impl(const StepParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_step(const Tile& t, const StepParams& p, cudaStream_t s) {
-#define M3_X(r, tt, nd) \
+#define M3_X(r, tt, nd, ndb, nthb) \
   if (t.R == r && t.T == tt) return launch_step_impl<r, tt>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X

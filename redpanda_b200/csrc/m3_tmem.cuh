@@ -55,19 +55,35 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
       : "memory");
 }
 
-// Store / load C consecutive 32-bit values (C a multiple of 8).
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const float* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+               "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3])
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+               : "r"(taddr)
+               : "memory");
+}
+
+// Store / load C consecutive 32-bit values (C a multiple of 4): 8-column
+// pieces, then one 4-column piece.
 template <int C>
 __device__ __forceinline__ void tmem_store(uint32_t taddr, const float (&v)[C]) {
-  static_assert(C % 8 == 0, "TMEM rows are written 8 columns at a time");
+  static_assert(C % 4 == 0, "TMEM rows are written 4 columns at a time");
 #pragma unroll
   for (int i = 0; i < C / 8; ++i) tmem_st8(taddr + 8 * i, &v[8 * i]);
+  if constexpr (C % 8 != 0) tmem_st4(taddr + 8 * (C / 8), &v[8 * (C / 8)]);
 }
 
 template <int C>
 __device__ __forceinline__ void tmem_load(uint32_t taddr, float (&v)[C]) {
-  static_assert(C % 8 == 0, "TMEM rows are read 8 columns at a time");
+  static_assert(C % 4 == 0, "TMEM rows are read 4 columns at a time");
 #pragma unroll
   for (int i = 0; i < C / 8; ++i) tmem_ld8(taddr + 8 * i, &v[8 * i]);
+  if constexpr (C % 8 != 0) tmem_ld4(taddr + 8 * (C / 8), &v[8 * (C / 8)]);
 }
 
 }  // namespace m3

@@ -93,6 +93,52 @@ def pad_params(A_real, A_imag, track, n_rot, n_state, d_inner, device):
     return Ar_p, Ai_p, Tk_p
 
 
+class ScanPlan:
+    """One scan shape bound to the C ABI; calls write into caller-owned buffers.
+
+    The layer below the autograd Function: no allocation per call, no dtype
+    conversion.  ``delta``/``u`` share ``dtype_du``, ``Bc``/``Cc`` share
+    ``dtype_bc`` (torch.float32 or torch.bfloat16); parameters are the (D, N)
+    fp32 padded tensors of :func:`pad_params`.
+    """
+
+    def __init__(self, batch, seqlen, d_inner, d_state, n_rot, dtype_du=torch.float32,
+                 dtype_bc=torch.float32, direction=M3_DIR_FWD):
+        self.shape = (batch, seqlen, d_inner, d_state)
+        self.n_rot = int(n_rot)
+        self.dtype_du, self.dtype_bc = dtype_du, dtype_bc
+        self.direction = int(direction)
+        self.desc = ScanDesc(batch, seqlen, d_inner, d_state, self.n_rot, _dt_code(dtype_du),
+                             _dt_code(dtype_bc), self.direction)
+        self._lib = _lib.load()
+
+    def ckpt_floats(self):
+        return int(self._lib.m3_scan_ckpt_floats(self.desc))
+
+    def workspace_bytes(self):
+        return int(self._lib.m3_scan_bwd_workspace_bytes(self.desc))
+
+    def forward(self, delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, y, ckpt=None, h_last=None,
+                dbu_last=None, stream=None):
+        dev = delta.device
+        s = _stream(dev) if stream is None else stream
+        _lib.check(self._lib.m3_scan_fwd(
+            self.desc, delta.data_ptr(), u.data_ptr(), Bc.data_ptr(), Cc.data_ptr(),
+            Ar_p.data_ptr(), Ai_p.data_ptr(), Tk_p.data_ptr(), y.data_ptr(), ctypes_ptr(ckpt),
+            ctypes_ptr(h_last), ctypes_ptr(dbu_last), s))
+
+    def backward(self, delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, dy, ckpt, d_delta, d_u, d_Bc,
+                 d_Cc, d_Ar, d_Ai, d_Tk, workspace, stream=None):
+        dev = delta.device
+        s = _stream(dev) if stream is None else stream
+        _lib.check(self._lib.m3_scan_bwd(
+            self.desc, delta.data_ptr(), u.data_ptr(), Bc.data_ptr(), Cc.data_ptr(),
+            Ar_p.data_ptr(), Ai_p.data_ptr(), Tk_p.data_ptr(), dy.data_ptr(),
+            _dt_code(dy.dtype), ctypes_ptr(ckpt), d_delta.data_ptr(), d_u.data_ptr(),
+            d_Bc.data_ptr(), d_Cc.data_ptr(), d_Ar.data_ptr(), d_Ai.data_ptr(),
+            d_Tk.data_ptr(), workspace.data_ptr(), workspace.numel(), s))
+
+
 class _TrapezoidalScanFn(torch.autograd.Function):
     """y = trapezoidal selective scan; analytic, deterministic backward.
 
