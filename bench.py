@@ -412,6 +412,7 @@ def run_step_rollout(dev, args):
 
 
 def main():
+    global B_RANK
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -421,9 +422,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-rollout", dest="rollout", action="store_false",
                     help="skip the config-3 step rollout measurement")
+    ap.add_argument("--batch", type=int, default=B_RANK,
+                    help="rows per GPU (default: the config-2 batch; smaller values are "
+                         "for profiler captures only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    B_RANK = args.batch
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -95,6 +95,7 @@ struct BwdLayout {
 size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 bool bwd_layout(const m3_scan_desc* d, const Tile& t, BwdLayout* lay) {
+  if (t.NDB == 0) return false;
   const int sms = device_sms();
   if (sms <= 0) return false;
   lay->G = (d->d_inner + t.dt_bwd() - 1) / t.dt_bwd();
@@ -198,6 +199,7 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   Tile t;
   int rc = check_scan_desc(desc, &t);
   if (rc != M3_OK) return rc;
+  if (t.NDB == 0) return M3_ERR_UNSUPPORTED;
   if (!dtype_ok(dtype_dy)) return M3_ERR_DTYPE;
   if (!delta || !u || !Bc || !Cc || !A_real_p || !A_imag_p || !track_p || !dy || !d_delta ||
       !d_u || !d_Bc || !d_Cc || !d_A_real_p || !d_A_imag_p || !d_track_p)

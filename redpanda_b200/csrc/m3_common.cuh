@@ -85,6 +85,15 @@ __device__ __forceinline__ float cell_update(float g, float& P, float du, float 
   return H;
 }
 
+// Two cells (channels k, k+1 of one state lane) in one packed update: the
+// lane-wise twin of cell_update().
+__device__ __forceinline__ float2 cell_update2(float2 g, float2& P, float2 du, float b) {
+  const float2 dbu = __fmul2_rn(du, f2(b));
+  const float2 H = __ffma2_rn(g, P, dbu);
+  P = __fadd2_rn(H, dbu);
+  return H;
+}
+
 // Sum of a per-thread partial over the kQ threads of a channel group
 // (fixed pairing: (s0+s1)+(s2+s3) on every lane).
 __device__ __forceinline__ float quad_sum(float s) {

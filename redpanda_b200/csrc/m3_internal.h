@@ -39,7 +39,7 @@ struct BwdParams {
   const float* Ar; const float* Ai; const float* Tk;
   const void* dy; const float* ckpt;
   void* d_delta; void* d_u;
-  float* part_bc;     // [G][B][L][2][NP]
+  float* part_bc;     // [G][B][L][2][NL][4 quarters]
   float* part_a;      // [Bg][3][D][NP]
   float* scratch_du;  // [G*Bg][L][DT][2]  (bidirectional only)
   int B, L, D, N, NR, NT;

@@ -10,11 +10,11 @@
 //   The multiple of pi (or pi/2) is subtracted from the EXACT product
 //   delta*A_imag inside an FMA, using a three-part split of pi whose leading
 //   part has 12 significant bits (so k*PI_A is exact for |k| < 2^12).
+//   The reduction is by pi (|r| <= pi/2); sin and cos share the sign (-1)^k.
 //   Polynomial coefficients are this project's own least-squares fits on
-//   Chebyshev nodes of the reduced interval (fp32 Horner evaluation included):
-//     cos on [-pi/2, pi/2], 6 terms in r^2:          max abs error  9.0e-8
-//     cos on [-pi/4, pi/4], 5 terms in r^2:          max abs error  5.2e-8
-//     sin on [-pi/4, pi/4], r * (5 terms in r^2):    max rel error  9.0e-8
+//   Chebyshev nodes of [-pi/2, pi/2] (errors include the fp32 Horner evaluation):
+//     cos: 6 terms in r^2,          max abs error 9.0e-8
+//     sin: r * (7 terms in r^2),    max rel error 1.0e-7
 //   Arguments beyond the reduction's exact range (|k| > 2048, i.e.
 //   |delta*A_imag| > ~6400) take the accurate libm path instead.
 #pragma once
@@ -25,7 +25,6 @@ namespace m3 {
 
 constexpr float kLog2e = 0x1.715476p+0f;        // log2(e) rounded to fp32
 constexpr float kInvPi = 0x1.45f306p-2f;        // 1/pi
-constexpr float kTwoOverPi = 0x1.45f306p-1f;    // 2/pi
 constexpr float kPiA = 0x1.922p+1f;             // 3217/1024: pi to 12 significant bits
 constexpr float kPiB = -0x1.2aeef4p-17f;        // pi - kPiA, rounded
 constexpr float kPiC = -0x1.73dcb4p-42f;        // pi - kPiA - kPiB, rounded
@@ -68,39 +67,103 @@ __device__ __forceinline__ float gate_cos(float dl, float ai) {
   return __uint_as_float(__float_as_uint(p) ^ odd);
 }
 
-// sin and cos of dl * ai: reduction by pi/2, |r| <= pi/4, quadrant rotation.
-__device__ __forceinline__ void gate_sincos(float dl, float ai, float& sn, float& cs) {
+// ---------------------------------------------------------------------------
+// Packed two-lane forms (sm_100 FFMA2/FMUL2/FADD2).  Each lane is rounded
+// exactly like the scalar intrinsic above, so packed and scalar code paths give
+// bit-identical results; only the instruction count differs.
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
+__device__ __forceinline__ float2 gate_exp2(float2 dl, float2 a2) {
+  const float2 x = __fmul2_rn(dl, a2);
+  return make_float2(ex2_approx(x.x), ex2_approx(x.y));
+}
+
+// cos(dl * ai) for two cells WITHOUT the large-argument check: the caller
+// guarantees |dl * ai| <= 6000 (so |k| < kMaxK), where it equals gate_cos().
+__device__ __forceinline__ float2 gate_cos2_nocheck(float2 dl, float2 ai) {
+  const float2 x = __fmul2_rn(dl, ai);
+  const float2 j = __ffma2_rn(x, f2(kInvPi), f2(kMagic));
+  const float2 k = __fadd2_rn(j, f2(-kMagic));
+  float2 r = __ffma2_rn(dl, ai, __fmul2_rn(k, f2(-kPiA)));
+  r = __ffma2_rn(k, f2(-kPiB), r);
+  r = __ffma2_rn(k, f2(-kPiC), r);
+  const float2 s = __fmul2_rn(r, r);
+  float2 p = f2(-0x1.181966p-22f);
+  p = __ffma2_rn(p, s, f2(0x1.9f720cp-16f));
+  p = __ffma2_rn(p, s, f2(-0x1.6c1396p-10f));
+  p = __ffma2_rn(p, s, f2(0x1.555548p-5f));
+  p = __ffma2_rn(p, s, f2(-0.5f));
+  p = __ffma2_rn(p, s, f2(1.0f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) ^ (__float_as_uint(j.x) << 31)),
+                     __uint_as_float(__float_as_uint(p.y) ^ (__float_as_uint(j.y) << 31)));
+}
+
+// sin and cos of dl*ai with the reduction by pi: both share the sign (-1)^k,
+// cos is computed exactly as gate_cos() (so the backward's gate equals the
+// forward's bit for bit) and sin uses a 7-term odd polynomial on [-pi/2, pi/2]
+// (this project's least-squares fit, max relative error 1.0e-7).
+__device__ __forceinline__ float sin_poly(float r, float s) {
+  float p = 0x1.5328dcp-33f;
+  p = __fmaf_rn(p, s, -0x1.ae0874p-26f);
+  p = __fmaf_rn(p, s, 0x1.71dd12p-19f);
+  p = __fmaf_rn(p, s, -0x1.a019fep-13f);
+  p = __fmaf_rn(p, s, 0x1.111112p-7f);
+  p = __fmaf_rn(p, s, -0x1.555556p-3f);
+  return __fmaf_rn(__fmul_rn(r, s), p, r);
+}
+
+__device__ __forceinline__ void gate_sincos_pi(float dl, float ai, float& sn, float& cs) {
   const float x = __fmul_rn(dl, ai);
-  const float j = __fmaf_rn(x, kTwoOverPi, kMagic);
+  const float j = __fmaf_rn(x, kInvPi, kMagic);
   const float k = __fsub_rn(j, kMagic);
-  if (fabsf(k) > 2.0f * kMaxK) {
+  if (fabsf(k) > kMaxK) {
     sincos_slow(dl, ai, &sn, &cs);
     return;
   }
-  // pi/2 split = half of the pi split (exact halving)
-  float r = __fmaf_rn(dl, ai, -__fmul_rn(k, 0.5f * kPiA));
-  r = __fmaf_rn(-k, 0.5f * kPiB, r);
-  r = __fmaf_rn(-k, 0.5f * kPiC, r);
+  float r = __fmaf_rn(dl, ai, -__fmul_rn(k, kPiA));
+  r = __fmaf_rn(-k, kPiB, r);
+  r = __fmaf_rn(-k, kPiC, r);
   const float s = __fmul_rn(r, r);
-  float pc = 0x1.994066p-16f;
-  pc = __fmaf_rn(pc, s, -0x1.6c08bep-10f);
-  pc = __fmaf_rn(pc, s, 0x1.55553ep-5f);
-  pc = __fmaf_rn(pc, s, -0.5f);
-  pc = __fmaf_rn(pc, s, 1.0f);
-  float ps = 0x1.6ce166p-19f;
-  ps = __fmaf_rn(ps, s, -0x1.a00fccp-13f);
-  ps = __fmaf_rn(ps, s, 0x1.111108p-7f);
-  ps = __fmaf_rn(ps, s, -0x1.555556p-3f);
-  ps = __fmaf_rn(__fmul_rn(r, s), ps, r);
-  const unsigned q = __float_as_uint(j);
-  // quadrant q: (sin, cos) = (s, c), (c, -s), (-s, -c), (-c, s)
-  const bool swap = q & 1u;
-  const float a = swap ? pc : ps;
-  const float b = swap ? ps : pc;
-  const unsigned sgn_s = (q & 2u) << 30;            // q = 2, 3 -> negative sin
-  const unsigned sgn_c = ((q + 1u) & 2u) << 30;     // q = 1, 2 -> negative cos
-  sn = __uint_as_float(__float_as_uint(a) ^ sgn_s);
-  cs = __uint_as_float(__float_as_uint(b) ^ sgn_c);
+  float p = -0x1.181966p-22f;
+  p = __fmaf_rn(p, s, 0x1.9f720cp-16f);
+  p = __fmaf_rn(p, s, -0x1.6c1396p-10f);
+  p = __fmaf_rn(p, s, 0x1.555548p-5f);
+  p = __fmaf_rn(p, s, -0.5f);
+  p = __fmaf_rn(p, s, 1.0f);
+  const unsigned odd = __float_as_uint(j) << 31;
+  cs = __uint_as_float(__float_as_uint(p) ^ odd);
+  sn = __uint_as_float(__float_as_uint(sin_poly(r, s)) ^ odd);
 }
+
+__device__ __forceinline__ void gate_sincos2_nocheck(float2 dl, float2 ai, float2& sn, float2& cs) {
+  const float2 x = __fmul2_rn(dl, ai);
+  const float2 j = __ffma2_rn(x, f2(kInvPi), f2(kMagic));
+  const float2 k = __fadd2_rn(j, f2(-kMagic));
+  float2 r = __ffma2_rn(dl, ai, __fmul2_rn(k, f2(-kPiA)));
+  r = __ffma2_rn(k, f2(-kPiB), r);
+  r = __ffma2_rn(k, f2(-kPiC), r);
+  const float2 s = __fmul2_rn(r, r);
+  float2 p = f2(-0x1.181966p-22f);
+  p = __ffma2_rn(p, s, f2(0x1.9f720cp-16f));
+  p = __ffma2_rn(p, s, f2(-0x1.6c1396p-10f));
+  p = __ffma2_rn(p, s, f2(0x1.555548p-5f));
+  p = __ffma2_rn(p, s, f2(-0.5f));
+  p = __ffma2_rn(p, s, f2(1.0f));
+  float2 q = f2(0x1.5328dcp-33f);
+  q = __ffma2_rn(q, s, f2(-0x1.ae0874p-26f));
+  q = __ffma2_rn(q, s, f2(0x1.71dd12p-19f));
+  q = __ffma2_rn(q, s, f2(-0x1.a019fep-13f));
+  q = __ffma2_rn(q, s, f2(0x1.111112p-7f));
+  q = __ffma2_rn(q, s, f2(-0x1.555556p-3f));
+  q = __ffma2_rn(__fmul2_rn(r, s), q, r);
+  const unsigned ox = __float_as_uint(j.x) << 31, oy = __float_as_uint(j.y) << 31;
+  cs = make_float2(__uint_as_float(__float_as_uint(p.x) ^ ox),
+                   __uint_as_float(__float_as_uint(p.y) ^ oy));
+  sn = make_float2(__uint_as_float(__float_as_uint(q.x) ^ ox),
+                   __uint_as_float(__float_as_uint(q.y) ^ oy));
+}
+
+// Largest |dl * ai| for which the packed no-check path is exact-equivalent.
+constexpr float kFastArgBound = 6000.0f;
 
 }  // namespace m3

@@ -21,6 +21,8 @@
 // dB/dC are reduced over the CTA's channels (warp shuffles + shared memory)
 // into one partial per channel tile.  A second kernel sums both partial sets in
 // a fixed order, so results are bitwise reproducible run to run.
+#include <type_traits>
+
 #include "m3_common.cuh"
 #include "m3_internal.h"
 #include "m3_stage.cuh"
@@ -36,22 +38,34 @@ constexpr int pow2ceil(int x) {
   return p;
 }
 
+// Backward tiling: NDP channel pairs per thread (packed FP32), NTH threads.
 template <int R, int T, int ND, int NTH>
 struct BwdCfg {
+  static_assert(ND % 2 == 0, "the backward processes channel pairs");
   static constexpr int NL = R + T;
   static constexpr int NP = 4 * NL;
   static constexpr int NW = NTH / 32;               // warps
-  static constexpr int DT = NTH / 4 * ND;           // channels per CTA
+  static constexpr int NG = NTH / 4;                // channel groups
+  static constexpr int DT = NG * ND;                // channels per CTA
+  static constexpr int NDP = ND / 2;                // channel pairs per thread
   static constexpr int C = ND * NL;                 // cells per thread
   static constexpr int CS = pow2ceil(C);            // TMEM columns per timestep
   static constexpr int WG_COLS = kCK * CS;          // TMEM columns per warpgroup
   static constexpr int NCOLS = (NTH / 128) * WG_COLS < 32 ? 32 : (NTH / 128) * WG_COLS;
+  static constexpr int FL = 4;                      // steps per dB/dC/ddelta flush
   static constexpr size_t raw_bytes = (size_t)kCK * DT * 4;   // one staged (kCK x DT) tile
+  // Reduction staging rows hold one value per thread (group-major, quarter-minor),
+  // so per-step stores are bank-conflict free; the row pitches are padded so
+  // the float4 reads of the flush hit distinct banks.
+  static constexpr int SR = NG * 4 + 16;                       // dB/dC row pitch
+  static constexpr int SG = NG * 4 + (16 / ND < 4 ? 4 : 16 / ND);  // ddelta row pitch
+  static constexpr size_t red_floats = (size_t)FL * 2 * NL * SR;   // [FL][2][NL][SR]
+  static constexpr size_t gs_floats = (size_t)FL * ND * 2 * SG;    // [FL][ND][2][SG]
   static constexpr size_t smem_bytes =
       3 * 2 * raw_bytes                       // delta, u, dy (HBM dtype), double-buffered
       + 2 * (size_t)DT * NP * 4               // checkpoint tile, double-buffered
       + 2 * 2 * (size_t)kCK * NP * 4          // B, C (fp32), double-buffered
-      + (size_t)kCK * NW * 2 * NP * 4         // dB/dC warp partials
+      + red_floats * 4 + gs_floats * 4
       + 16;                                   // TMEM address slot
 };
 
@@ -84,30 +98,36 @@ __device__ __forceinline__ void stage_tile(unsigned char* dst, const void* src, 
   }
 }
 
+// One element of a staged (kCK x DT) tile, converted to fp32.
+__device__ __forceinline__ float tile_at(const unsigned char* base, bool bf16, int idx) {
+  if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+  return reinterpret_cast<const float*>(base)[idx];
+}
+
 template <int R, int T, int ND, int NTH>
 __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
   using LM = LaneMap<R, T>;
   using CF = BwdCfg<R, T, ND, NTH>;
-  constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS, NW = CF::NW;
+  constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS;
+  constexpr int NG = CF::NG, NDP = CF::NDP, FL = CF::FL, SR = CF::SR, SG = CF::SG;
   constexpr int RR = R > 0 ? R : 1;
   constexpr int TT = T > 0 ? T : 1;
   constexpr int BCE = (kCK * NP + NTH - 1) / NTH;
-  constexpr int V = 2 * NL;                  // dB + dC partials per thread per step
-  constexpr int V8 = (V + 7) / 8 * 8;        // padded to the 8-group butterfly
   static_assert(CF::NCOLS <= 512, "TMEM holds at most 512 columns");
 
   extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* s_dl = smem;                                   // [2][raw]
-  unsigned char* s_u = s_dl + 2 * CF::raw_bytes;                // [2][raw]
-  unsigned char* s_dy = s_u + 2 * CF::raw_bytes;                // [2][raw]
+  unsigned char* s_dl = smem;                                        // [2][raw]
+  unsigned char* s_u = s_dl + 2 * CF::raw_bytes;                     // [2][raw]
+  unsigned char* s_dy = s_u + 2 * CF::raw_bytes;                     // [2][raw]
   float* s_ck = reinterpret_cast<float*>(s_dy + 2 * CF::raw_bytes);  // [2][DT][NP]
-  float* s_b = s_ck + 2 * DT * NP;                              // [2][kCK][NP]
-  float* s_c = s_b + 2 * kCK * NP;                              // [2][kCK][NP]
-  float* s_red = s_c + 2 * kCK * NP;                            // [kCK][NW][2][NP]
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_red + kCK * NW * 2 * NP);
+  float* s_b = s_ck + 2 * DT * NP;                                   // [2][kCK][NP]
+  float* s_c = s_b + 2 * kCK * NP;                                   // [2][kCK][NP]
+  float* s_red = s_c + 2 * kCK * NP;                                 // [FL][2][NL][SR]
+  float* s_gs = s_red + CF::red_floats;                              // [FL][ND][2][SG]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_gs + CF::gs_floats);
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
-  const int warp = tid >> 5, lane = tid & 31;
+  const int warp = tid >> 5;
   const int bg = blockIdx.x, gt = blockIdx.y;
   const int d0 = gt * DT, dbase = d0 + grp * ND;
   const int B = p.B, L = p.L, D = p.D, N = p.N;
@@ -126,7 +146,9 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
   const uint32_t tbase =
       *s_tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * CF::WG_COLS);
 
-  float ar[ND][RR], ai[ND][RR], tk[ND][TT];
+  // parameters of the thread's cells, as channel pairs (k, k+1)
+  float2 AR[NDP][RR], A2[NDP][RR], AI[NDP][RR], TK[NDP][TT];
+  float maxai = 0.f;
 #pragma unroll
   for (int k = 0; k < ND; ++k) {
     const int d = dbase + k;
@@ -136,21 +158,27 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
       const bool ok = (d < D) && (n >= 0);
       const size_t gi = ok ? (size_t)d * N + n : 0;
       if (j < R) {
-        ar[k][j] = ok ? p.Ar[gi] : 0.f;
-        ai[k][j] = ok ? p.Ai[gi] : 0.f;
+        const float ar = ok ? p.Ar[gi] : 0.f, ai = ok ? p.Ai[gi] : 0.f;
+        maxai = fmaxf(maxai, fabsf(ai));
+        float2& r_ = AR[k >> 1][j]; float2& e_ = A2[k >> 1][j]; float2& i_ = AI[k >> 1][j];
+        if (k & 1) { r_.y = ar; e_.y = exp_const(ar); i_.y = ai; }
+        else       { r_.x = ar; e_.x = exp_const(ar); i_.x = ai; }
       } else {
-        tk[k][j - R] = ok ? p.Tk[gi] : 0.f;
+        const float tv = ok ? p.Tk[gi] : 0.f;
+        if (k & 1) TK[k >> 1][j - R].y = tv; else TK[k >> 1][j - R].x = tv;
       }
     }
   }
 
-  float gAr[ND][RR], gAi[ND][RR], gTk[ND][TT];
+  // dA accumulators: sum_t dl*wp*gate, sum_t dl*wp*exp*sin, sum_t wp (x 0.5 at the end;
+  // the second carries the sign of dA_imag)
+  float2 gAr[NDP][RR], gAi[NDP][RR], gTk[NDP][TT];
 #pragma unroll
-  for (int k = 0; k < ND; ++k) {
+  for (int k = 0; k < NDP; ++k) {
 #pragma unroll
-    for (int j = 0; j < RR; ++j) { gAr[k][j] = 0.f; gAi[k][j] = 0.f; }
+    for (int j = 0; j < RR; ++j) { gAr[k][j] = f2(0.f); gAi[k][j] = f2(0.f); }
 #pragma unroll
-    for (int j = 0; j < TT; ++j) gTk[k][j] = 0.f;
+    for (int j = 0; j < TT; ++j) gTk[k][j] = f2(0.f);
   }
 
   const int cta = gt * p.Bg + bg;
@@ -212,16 +240,14 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     }
   };
 
-  float qv[C], gn[ND * RR];
+  float2 qv[NDP][NL], gn[NDP][RR];
   if (nitems > 0) {
     stage(0, 0);
     cp_async_commit();
-    {
-      int b, pass, c;
-      item(0, b, pass, c);
-      load_bc(b, dir_of(pass), c * kCK);
-      store_bc(0);
-    }
+    int b, pass, c;
+    item(0, b, pass, c);
+    load_bc(b, dir_of(pass), c * kCK);
+    store_bc(0);
   }
   for (int it = 0; it < nitems; ++it) {
     const int buf = it & 1;
@@ -245,9 +271,12 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
 
     if (c == nch - 1) {   // first chunk of a direction pass: adjoint state starts at zero
 #pragma unroll
-      for (int i = 0; i < C; ++i) qv[i] = 0.f;
+      for (int k = 0; k < NDP; ++k) {
 #pragma unroll
-      for (int i = 0; i < ND * RR; ++i) gn[i] = 0.f;
+        for (int j = 0; j < NL; ++j) qv[k][j] = f2(0.f);
+#pragma unroll
+        for (int j = 0; j < RR; ++j) gn[k][j] = f2(0.f);
+      }
     }
 
     const unsigned char* bdl = s_dl + buf * CF::raw_bytes;
@@ -257,174 +286,224 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     const float* bc = s_c + buf * kCK * NP;
 
     // ---- forward recompute of the chunk; P[t-1] of every cell -> TMEM
-    float P[C];
+    float2 P[NDP][NL];
     {
       const float* ck = s_ck + buf * DT * NP + grp * ND * NP + q * NL;
 #pragma unroll
       for (int k = 0; k < ND; ++k)
 #pragma unroll
-        for (int j = 0; j < NL; ++j) P[k * NL + j] = c > 0 ? ck[k * NP + j] : 0.f;
+        for (int j = 0; j < NL; ++j) {
+          const float v = c > 0 ? ck[k * NP + j] : 0.f;
+          if (k & 1) P[k >> 1][j].y = v; else P[k >> 1][j].x = v;
+        }
     }
     for (int tt = 0; tt < ns; ++tt) {
-      tmem_store<C>(tbase + (uint32_t)(tt * CS), P);
+      tmem_store<C>(tbase + (uint32_t)(tt * CS), reinterpret_cast<const float(&)[C]>(P));
       float dl[ND], uu[ND];
       read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
       read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
       const float* rbv = bb + tt * NP + q * NL;
+      float mdl = 0.f;
 #pragma unroll
-      for (int k = 0; k < ND; ++k) {
-        const float du = __fmul_rn(dl[k], uu[k]);
+      for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
+      // The fast/exact choice is made once per step (not per cell) so that the
+      // compiler emits two branch-free bodies instead of predicating both.
+      auto recompute = [&](auto fast_tag) {
+        constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
-        for (int j = 0; j < R; ++j)
-          cell_update(rot_gate(dl[k], exp_const(ar[k][j]), ai[k][j]), P[k * NL + j], du, rbv[j]);
+        for (int kp = 0; kp < NDP; ++kp) {
+          const float2 dl2 = make_float2(dl[2 * kp], dl[2 * kp + 1]);
+          const float2 du2 = __fmul2_rn(dl2, make_float2(uu[2 * kp], uu[2 * kp + 1]));
 #pragma unroll
-        for (int j = R; j < NL; ++j) cell_update(tk[k][j - R], P[k * NL + j], du, rbv[j]);
-      }
+          for (int j = 0; j < R; ++j) {
+            float2 g;
+            if constexpr (FAST) {
+              g = __fmul2_rn(gate_exp2(dl2, A2[kp][j]), gate_cos2_nocheck(dl2, AI[kp][j]));
+            } else {
+              g = make_float2(rot_gate(dl2.x, A2[kp][j].x, AI[kp][j].x),
+                              rot_gate(dl2.y, A2[kp][j].y, AI[kp][j].y));
+            }
+            cell_update2(g, P[kp][j], du2, rbv[j]);
+          }
+#pragma unroll
+          for (int j = R; j < NL; ++j) cell_update2(TK[kp][j - R], P[kp][j], du2, rbv[j]);
+        }
+      };
+      if (__fmul_rn(mdl, maxai) <= kFastArgBound) recompute(std::true_type{});
+      else recompute(std::false_type{});
     }
     tmem_wait_st();
 
-    // ---- reverse recurrence
+    // ---- reverse recurrence, flushing dB/dC and ddelta/du every FL steps
     for (int tt = ns - 1; tt >= 0; --tt) {
-      float Pp[C];
-      tmem_load<C>(tbase + (uint32_t)(tt * CS), Pp);
-      const int s = s0 + tt;
-      const int t = dir ? L - 1 - s : s;
+      const int slot = (ns - 1 - tt) % FL;
+      float2 Pp[NDP][NL];
+      tmem_load<C>(tbase + (uint32_t)(tt * CS), reinterpret_cast<float(&)[C]>(Pp));
       float dl[ND], uu[ND], dyv[ND];
       read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
       read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
       read_chan<ND>(bdy + (size_t)(tt * DT + grp * ND) * es_dy, bf_dy, dyv);
       const float* rbv = bb + tt * NP + q * NL;
       const float* rcv = bc + tt * NP + q * NL;
-      float Bv[NL], Cv[NL], pB[NL], pC[NL];
+      float Bv[NL], Cv[NL];
 #pragma unroll
-      for (int j = 0; j < NL; ++j) {
-        Bv[j] = rbv[j];
-        Cv[j] = rcv[j];
-        pB[j] = 0.f;
-        pC[j] = 0.f;
-      }
+      for (int j = 0; j < NL; ++j) { Bv[j] = rbv[j]; Cv[j] = rcv[j]; }
+      float mdl = 0.f;
+#pragma unroll
+      for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
       tmem_wait_ld();
-      float gsum[ND], sbs[ND];
+      float2 pB[NL], pC[NL];
+      float* gsrow = s_gs + (size_t)slot * ND * 2 * SG + grp * 4 + q;
+      auto reverse_cells = [&](auto fast_tag) {
+      constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
-      for (int k = 0; k < ND; ++k) {
-        const float dlk = dl[k], dyk = dyv[k];
-        const float du = __fmul_rn(dlk, uu[k]);
-        float gs = 0.f, sB = 0.f;
+      for (int kp = 0; kp < NDP; ++kp) {
+        const float2 dl2 = make_float2(dl[2 * kp], dl[2 * kp + 1]);
+        const float2 du2 = __fmul2_rn(dl2, make_float2(uu[2 * kp], uu[2 * kp + 1]));
+        const float2 dy2 = make_float2(dyv[2 * kp], dyv[2 * kp + 1]);
+        float2 gs = f2(0.f), gsi = f2(0.f), sB = f2(0.f);
 #pragma unroll
         for (int j = 0; j < R; ++j) {
-          const float pp = Pp[k * NL + j];
-          const float e = gate_exp(dlk, exp_const(ar[k][j]));
-          float sn, cs;
-          gate_sincos(dlk, ai[k][j], sn, cs);
-          const float g = __fmul_rn(e, cs);
-          const float es = __fmul_rn(e, sn);
-          const float dbu = __fmul_rn(du, Bv[j]);
-          const float H = __fmaf_rn(g, pp, dbu);
-          const float dyC = __fmul_rn(dyk, Cv[j]);
-          const float qn = __fmaf_rn(gn[k * RR + j], qv[k * NL + j], dyC);
-          const float ddbu = __fmaf_rn(-0.5f, dyC, qn);
-          const float wp = __fmul_rn(qn, pp);
-          const float wg = __fmul_rn(wp, g);
-          const float ws = __fmul_rn(wp, es);
-          gAr[k][j] = __fmaf_rn(dlk, wg, gAr[k][j]);
-          gAi[k][j] = __fmaf_rn(-dlk, ws, gAi[k][j]);
-          gs = __fmaf_rn(ar[k][j], wg, gs);
-          gs = __fmaf_rn(-ai[k][j], ws, gs);
-          sB = __fmaf_rn(ddbu, Bv[j], sB);
-          pB[j] = __fmaf_rn(ddbu, du, pB[j]);
-          pC[j] = __fmaf_rn(dyk, H, pC[j]);
-          qv[k * NL + j] = qn;
-          gn[k * RR + j] = g;
+          const float2 pp = Pp[kp][j];
+          const float2 e = gate_exp2(dl2, A2[kp][j]);
+          float2 sn, cs;
+          if constexpr (FAST) {
+            gate_sincos2_nocheck(dl2, AI[kp][j], sn, cs);
+          } else {
+            gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
+            gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
+          }
+          const float2 g = __fmul2_rn(e, cs);
+          const float2 es = __fmul2_rn(e, sn);
+          const float2 dbu = __fmul2_rn(du2, f2(Bv[j]));
+          const float2 H = __ffma2_rn(g, pp, dbu);
+          const float2 dyC = __fmul2_rn(dy2, f2(Cv[j]));
+          const float2 qn = __ffma2_rn(gn[kp][j], qv[kp][j], dyC);
+          const float2 ddbu = __ffma2_rn(f2(-0.5f), dyC, qn);
+          const float2 wp = __fmul2_rn(qn, pp);
+          const float2 wg = __fmul2_rn(wp, g);
+          const float2 ws = __fmul2_rn(wp, es);
+          gAr[kp][j] = __ffma2_rn(dl2, wg, gAr[kp][j]);
+          gAi[kp][j] = __ffma2_rn(dl2, ws, gAi[kp][j]);
+          gs = __ffma2_rn(AR[kp][j], wg, gs);
+          gsi = __ffma2_rn(AI[kp][j], ws, gsi);
+          sB = __ffma2_rn(ddbu, f2(Bv[j]), sB);
+          pB[j] = kp == 0 ? __fmul2_rn(ddbu, du2) : __ffma2_rn(ddbu, du2, pB[j]);
+          pC[j] = kp == 0 ? __fmul2_rn(dy2, H) : __ffma2_rn(dy2, H, pC[j]);
+          qv[kp][j] = qn;
+          gn[kp][j] = g;
         }
 #pragma unroll
         for (int j = R; j < NL; ++j) {
-          const float pp = Pp[k * NL + j];
-          const float g = tk[k][j - R];
-          const float dbu = __fmul_rn(du, Bv[j]);
-          const float H = __fmaf_rn(g, pp, dbu);
-          const float dyC = __fmul_rn(dyk, Cv[j]);
-          const float qn = __fmaf_rn(g, qv[k * NL + j], dyC);
-          const float ddbu = __fmaf_rn(-0.5f, dyC, qn);
-          const float wp = __fmul_rn(qn, pp);
-          gTk[k][j - R] = __fadd_rn(gTk[k][j - R], wp);
-          sB = __fmaf_rn(ddbu, Bv[j], sB);
-          pB[j] = __fmaf_rn(ddbu, du, pB[j]);
-          pC[j] = __fmaf_rn(dyk, H, pC[j]);
-          qv[k * NL + j] = qn;
+          const float2 pp = Pp[kp][j];
+          const float2 g = TK[kp][j - R];
+          const float2 dbu = __fmul2_rn(du2, f2(Bv[j]));
+          const float2 H = __ffma2_rn(g, pp, dbu);
+          const float2 dyC = __fmul2_rn(dy2, f2(Cv[j]));
+          const float2 qn = __ffma2_rn(g, qv[kp][j], dyC);
+          const float2 ddbu = __ffma2_rn(f2(-0.5f), dyC, qn);
+          const float2 wp = __fmul2_rn(qn, pp);
+          gTk[kp][j - R] = __fadd2_rn(gTk[kp][j - R], wp);
+          sB = __ffma2_rn(ddbu, f2(Bv[j]), sB);
+          pB[j] = kp == 0 ? __fmul2_rn(ddbu, du2) : __ffma2_rn(ddbu, du2, pB[j]);
+          pC[j] = kp == 0 ? __fmul2_rn(dy2, H) : __ffma2_rn(dy2, H, pC[j]);
+          qv[kp][j] = qn;
         }
-        gsum[k] = gs;
-        sbs[k] = sB;
+        // channel partials over this thread's lanes: gsum = sum(ar*wg) - sum(ai*ws), sB
+        const float2 gsum = __fadd2_rn(gs, __fmul2_rn(gsi, f2(-1.f)));
+        gsrow[(2 * (2 * kp) + 0) * SG] = gsum.x;
+        gsrow[(2 * (2 * kp) + 1) * SG] = sB.x;
+        gsrow[(2 * (2 * kp + 1) + 0) * SG] = gsum.y;
+        gsrow[(2 * (2 * kp + 1) + 1) * SG] = sB.y;
       }
-      // per-channel outputs: reduce over the 4 lane quarters
-#pragma unroll
-      for (int k = 0; k < ND; ++k) {
-        const float gsv = quad_sum(gsum[k]);
-        const float sBv = quad_sum(sbs[k]);
-        const int d = dbase + k;
-        if ((k & 3) == q && d < D) {
-          float ddl = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, uu[k]));
-          float ddu = __fmul_rn(sBv, dl[k]);
-          const size_t oi = ((size_t)b * L + t) * D + d;
-          float* sc = scratch ? scratch + ((size_t)t * DT + (d - d0)) * 2 : nullptr;
-          if (first_of_two) {
-            sc[0] = ddl;
-            sc[1] = ddu;
-          } else {
-            if (second_of_two) {
-              ddl = __fadd_rn(sc[0], ddl);
-              ddu = __fadd_rn(sc[1], ddu);
-            }
-            st_f(p.d_delta, oi, p.dt_du, ddl);
-            st_f(p.d_u, oi, p.dt_du, ddu);
-          }
-        }
-      }
-      // dB/dC over this warp's 8 channel groups (lanes q, q+4, ..., q+28):
-      // transposed butterfly, after which each lane holds V8/8 fully reduced
-      // values; value i of lane l is original index
-      // ((l>>2)&1)*V8/2 + ((l>>3)&1)*V8/4 + ((l>>4)&1)*V8/8 + i.
+      };
+      if (__fmul_rn(mdl, maxai) <= kFastArgBound) reverse_cells(std::true_type{});
+      else reverse_cells(std::false_type{});
+      // dB/dC partial of this thread's channels
       {
-        float v[V8];
+        float* r0 = s_red + (size_t)slot * 2 * NL * SR + grp * 4 + q;
 #pragma unroll
-        for (int j = 0; j < NL; ++j) { v[j] = pB[j]; v[NL + j] = pC[j]; }
-#pragma unroll
-        for (int j = V; j < V8; ++j) v[j] = 0.f;
-#pragma unroll
-        for (int lvl = 0; lvl < 3; ++lvl) {
-          const int m = 4 << lvl;
-          const int half = V8 >> (lvl + 1);
-          const bool hi = (lane & m) != 0;
-#pragma unroll
-          for (int i = 0; i < half; ++i) {
-            const float send = hi ? v[i] : v[i + half];
-            const float keep = hi ? v[i + half] : v[i];
-            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
-          }
-        }
-        const int obase = ((lane >> 2) & 1) * (V8 / 2) + ((lane >> 3) & 1) * (V8 / 4) +
-                          ((lane >> 4) & 1) * (V8 / 8);
-        float* r0 = s_red + (size_t)(tt * NW + warp) * 2 * NP + q * NL;
-#pragma unroll
-        for (int i = 0; i < V8 / 8; ++i) {
-          const int o = obase + i;
-          if (o < NL) r0[o] = v[i];
-          else if (o < V) r0[NP + (o - NL)] = v[i];
+        for (int j = 0; j < NL; ++j) {
+          r0[j * SR] = __fadd_rn(pB[j].x, pB[j].y);
+          r0[(NL + j) * SR] = __fadd_rn(pC[j].x, pC[j].y);
         }
       }
-    }
-    __syncthreads();
-    // flush this chunk's dB/dC partials: fixed order over the 4 warps
-    for (int i = tid; i < ns * 2 * NP; i += NTH) {
-      const int tt = i / (2 * NP), rem = i - tt * 2 * NP;
-      const int which = rem / NP, ln = rem - which * NP;
-      const float* r = s_red + ((size_t)tt * NW * 2 + which) * NP + ln;
-      float v = r[0];
+      if (slot == FL - 1 || tt == 0) {
+        __syncthreads();
+        const int nsl = slot + 1;                 // slots in this flush
+        const int tt_hi = tt + slot;              // step of slot 0
+        // dB/dC: each (slot, which, j) row holds one value per (group, quarter);
+        // 4 threads sum it over the groups as float4s of the 4 quarters, in a
+        // fixed order, and write lanes j*4 + q of the partial.
+        for (int base = 0; base < nsl * 2 * NL; base += NTH / 4) {
+          const int row = base + (tid >> 2), part = tid & 3;
+          const bool rok = row < nsl * 2 * NL;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (rok) {
+            const float* src = s_red + (size_t)row * SR;
+#pragma unroll 4
+            for (int g = part; g < NG; g += 4) {
+              const float4 v = *reinterpret_cast<const float4*>(src + g * 4);
+              acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
+              acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
+            }
+          }
 #pragma unroll
-      for (int w = 1; w < NW; ++w) v = __fadd_rn(v, r[(size_t)w * 2 * NP]);
-      const int s = s0 + tt;
-      const int t = dir ? L - 1 - s : s;
-      float* dst = p.part_bc + ((((size_t)gt * B + b) * L + t) * 2 + which) * NP + ln;
-      *dst = second_of_two ? __fadd_rn(*dst, v) : v;
+          for (int m = 1; m < 4; m <<= 1) {
+            acc.x = __fadd_rn(acc.x, __shfl_xor_sync(0xffffffffu, acc.x, m));
+            acc.y = __fadd_rn(acc.y, __shfl_xor_sync(0xffffffffu, acc.y, m));
+            acc.z = __fadd_rn(acc.z, __shfl_xor_sync(0xffffffffu, acc.z, m));
+            acc.w = __fadd_rn(acc.w, __shfl_xor_sync(0xffffffffu, acc.w, m));
+          }
+          if (rok && part == 0) {
+            const int sl = row / (2 * NL), rem = row - sl * 2 * NL;
+            const int which = rem / NL, j = rem - which * NL;
+            const int s = s0 + tt_hi - sl;
+            const int t = dir ? L - 1 - s : s;
+            float4* dst = reinterpret_cast<float4*>(
+                p.part_bc + ((((size_t)gt * B + b) * L + t) * 2 + which) * NP + j * 4);
+            if (second_of_two) {
+              const float4 o = *dst;
+              acc.x = __fadd_rn(o.x, acc.x); acc.y = __fadd_rn(o.y, acc.y);
+              acc.z = __fadd_rn(o.z, acc.z); acc.w = __fadd_rn(o.w, acc.w);
+            }
+            *dst = acc;
+          }
+        }
+        // ddelta / du per channel: sum the 4 lane-quarter partials
+        for (int i = tid; i < nsl * DT; i += NTH) {
+          const int sl = i / DT, dd = i - sl * DT;
+          const int d = d0 + dd;
+          if (d < D) {
+            const int tts = tt_hi - sl;
+            const float* g4p = s_gs + ((size_t)(sl * ND + dd % ND) * 2) * SG + (dd / ND) * 4;
+            const float4 g4 = *reinterpret_cast<const float4*>(g4p);
+            const float4 b4 = *reinterpret_cast<const float4*>(g4p + SG);
+            const float gsv = __fadd_rn(__fadd_rn(g4.x, g4.y), __fadd_rn(g4.z, g4.w));
+            const float sBv = __fadd_rn(__fadd_rn(b4.x, b4.y), __fadd_rn(b4.z, b4.w));
+            const float dlv = tile_at(bdl, bf_du, tts * DT + dd);
+            const float uv = tile_at(bu, bf_du, tts * DT + dd);
+            float ddl = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, uv));
+            float ddu = __fmul_rn(sBv, dlv);
+            const int s = s0 + tts;
+            const int t = dir ? L - 1 - s : s;
+            float* sc = scratch ? scratch + ((size_t)t * DT + dd) * 2 : nullptr;
+            if (first_of_two) {
+              sc[0] = ddl;
+              sc[1] = ddu;
+            } else {
+              if (second_of_two) {
+                ddl = __fadd_rn(sc[0], ddl);
+                ddu = __fadd_rn(sc[1], ddu);
+              }
+              const size_t oi = ((size_t)b * L + t) * D + d;
+              st_f(p.d_delta, oi, p.dt_du, ddl);
+              st_f(p.d_u, oi, p.dt_du, ddu);
+            }
+          }
+        }
+        __syncthreads();
+      }
     }
     if (more) store_bc(buf ^ 1);
   }
@@ -439,9 +518,17 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
       float* a1 = p.part_a + (((size_t)bg * 3 + 1) * D + d) * NP + q * NL;
       float* a2 = p.part_a + (((size_t)bg * 3 + 2) * D + d) * NP + q * NL;
 #pragma unroll
-      for (int j = 0; j < R; ++j) { a0[j] = gAr[k][j]; a1[j] = gAi[k][j]; a2[j] = 0.f; }
+      for (int j = 0; j < R; ++j) {
+        a0[j] = (k & 1) ? gAr[k >> 1][j].y : gAr[k >> 1][j].x;
+        a1[j] = -((k & 1) ? gAi[k >> 1][j].y : gAi[k >> 1][j].x);
+        a2[j] = 0.f;
+      }
 #pragma unroll
-      for (int j = R; j < NL; ++j) { a0[j] = 0.f; a1[j] = 0.f; a2[j] = gTk[k][j - R]; }
+      for (int j = R; j < NL; ++j) {
+        a0[j] = 0.f;
+        a1[j] = 0.f;
+        a2[j] = (k & 1) ? gTk[k >> 1][j - R].y : gTk[k >> 1][j - R].x;
+      }
     }
   }
 
@@ -459,6 +546,13 @@ __device__ __forceinline__ int pad_lane(int n, int NR, int R, int T) {
   return (k / T) * (R + T) + R + (k % T);
 }
 
+// Position (j*4 + q) of memory state lane n in the dB/dC partial rows.
+__device__ __forceinline__ int part_lane(int n, int NR, int R, int T) {
+  if (n < NR) return (n % R) * 4 + n / R;
+  const int k = n - NR;
+  return (R + k % T) * 4 + k / T;
+}
+
 __global__ void reduce_bc_kernel(const ReduceParams p, int R, int T) {
   const size_t total = (size_t)p.B * p.L * p.N;
   const int NP = 4 * (R + T);
@@ -466,7 +560,7 @@ __global__ void reduce_bc_kernel(const ReduceParams p, int R, int T) {
        i += (size_t)gridDim.x * blockDim.x) {
     const int n = (int)(i % p.N);
     const size_t bt = i / p.N;
-    const int ln = pad_lane(n, p.NR, R, T);
+    const int ln = part_lane(n, p.NR, R, T);
     float vb = 0.f, vc = 0.f;
     for (int g = 0; g < p.G; ++g) {
       const float* src = p.part_bc + (((size_t)g * p.B * p.L + bt) * 2) * NP + ln;
@@ -516,7 +610,8 @@ cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
 
 cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s) {
 #define M3_X(r, tt, nd, ndb, nthb) \
-  if (t.R == r && t.T == tt && t.ND == nd) return launch_bwd_impl<r, tt, ndb, nthb>(p, s);
+  if constexpr (ndb > 0)                                                    \
+    if (t.R == r && t.T == tt && t.ND == nd) return launch_bwd_impl<r, tt, ndb, nthb>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;

@@ -102,21 +102,29 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
   const int esz = bf16 ? 2 : 4;
   const int L = p.L, D = p.D, N = p.N;
 
-  // Eigenvalues of this thread's cells (zero for virtual lanes / channels).
-  float ar[ND][RR], ai[ND][RR], tk[ND][TT];
+  // Eigenvalues of this thread's cells (zero for virtual lanes / channels),
+  // held as channel pairs (k, k+1) so the packed FP32 path can use them.
+  constexpr int NDP = (ND + 1) / 2;
+  float2 A2[NDP][RR], AI[NDP][RR], TK[NDP][TT];
+  float maxai = 0.f;   // max |A_imag| over the thread's cells (fast-path bound)
 #pragma unroll
-  for (int k = 0; k < ND; ++k) {
+  for (int k = 0; k < 2 * NDP; ++k) {
     const int d = dbase + k;
 #pragma unroll
     for (int j = 0; j < NL; ++j) {
       const int n = LM::mem_lane(q, j, p.NR, p.NT);
-      const bool ok = (d < D) && (n >= 0);
+      const bool ok = (k < ND) && (d < D) && (n >= 0);
       const size_t gi = ok ? (size_t)d * N + n : 0;
       if (j < R) {
-        ar[k][j] = ok ? exp_const(p.Ar[gi]) : 0.f;   // A_real * log2(e)
-        ai[k][j] = ok ? p.Ai[gi] : 0.f;
+        const float a2 = ok ? exp_const(p.Ar[gi]) : 0.f;   // A_real * log2(e)
+        const float ai = ok ? p.Ai[gi] : 0.f;
+        maxai = fmaxf(maxai, fabsf(ai));
+        if (k & 1) { A2[k >> 1][j].y = a2; AI[k >> 1][j].y = ai; }
+        else       { A2[k >> 1][j].x = a2; AI[k >> 1][j].x = ai; }
       } else {
-        tk[k][j - R] = ok ? p.Tk[gi] : 0.f;
+        const float tv = ok ? p.Tk[gi] : 0.f;
+        if (k & 1) TK[k >> 1][j - R].y = tv;
+        else       TK[k >> 1][j - R].x = tv;
       }
     }
   }
@@ -128,11 +136,11 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
     const int dslot = p.direction == M3_DIR_BIDIR ? dir : 0;
     const int ndirs = p.direction == M3_DIR_BIDIR ? 2 : 1;
 
-    float P[ND][NL];
+    float2 P[NDP][NL];   // P = 2h + dBu of cells (k, j): component k&1 of P[k/2][j]
 #pragma unroll
-    for (int k = 0; k < ND; ++k)
+    for (int k = 0; k < NDP; ++k)
 #pragma unroll
-      for (int j = 0; j < NL; ++j) P[k][j] = 0.f;
+      for (int j = 0; j < NL; ++j) P[k][j] = make_float2(0.f, 0.f);
 
     float rb[BCE], rc[BCE];
     auto load_bc = [&](int s0) {
@@ -189,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
             float* dst = p.ckpt +
                 ((((size_t)b * ndirs + dslot) * (p.nch - 1) + (c - 1)) * D + d) * NP + q * NL;
 #pragma unroll
-            for (int j = 0; j < NL; ++j) dst[j] = P[k][j];
+            for (int j = 0; j < NL; ++j) dst[j] = (k & 1) ? P[k >> 1][j].y : P[k >> 1][j].x;
           }
         }
       }
@@ -213,27 +221,63 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
           Cv[j] = bc[tt * NP + q * NL + j];
         }
         const bool last = (s == L - 1) && (p.h_last != nullptr);
-        float part[ND];
+        float du[ND], mdl = 0.f;
 #pragma unroll
         for (int k = 0; k < ND; ++k) {
-          const float du = __fmul_rn(dl[k], uu[k]);
-          float H[NL];
+          du[k] = __fmul_rn(dl[k], uu[k]);
+          mdl = fmaxf(mdl, fabsf(dl[k]));
+        }
+        float part[2 * NDP];
+        if ((ND % 2 == 0) && !last && __fmul_rn(mdl, maxai) <= kFastArgBound) {
+          // packed path: channel pairs, no per-cell range checks
 #pragma unroll
-          for (int j = 0; j < R; ++j)
-            H[j] = cell_update(rot_gate(dl[k], ar[k][j], ai[k][j]), P[k][j], du, Bv[j]);
+          for (int kp = 0; kp < NDP; ++kp) {
+            const float2 dl2 = make_float2(dl[2 * kp], dl[(2 * kp + 1) % ND]);
+            const float2 du2 = make_float2(du[2 * kp], du[(2 * kp + 1) % ND]);
+            float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int j = R; j < NL; ++j) H[j] = cell_update(tk[k][j - R], P[k][j], du, Bv[j]);
-          part[k] = y_partial<NL>(H, Cv);
-          if (last) {
-            const int d = dbase + k;
-            if (d < D) {
+            for (int j = 0; j < R; ++j) {
+              const float2 g = __fmul2_rn(gate_exp2(dl2, A2[kp][j]), gate_cos2_nocheck(dl2, AI[kp][j]));
+              const float2 H = cell_update2(g, P[kp][j], du2, Bv[j]);
+              acc = __ffma2_rn(H, f2(Cv[j]), acc);
+            }
 #pragma unroll
-              for (int j = 0; j < NL; ++j) {
-                const int n = LM::mem_lane(q, j, p.NR, p.NT);
-                if (n >= 0) {
-                  const size_t gi = ((size_t)b * D + d) * N + n;
-                  p.h_last[gi] = __fmul_rn(0.5f, H[j]);
-                  p.dbu_last[gi] = __fmul_rn(du, Bv[j]);
+            for (int j = R; j < NL; ++j) {
+              const float2 H = cell_update2(TK[kp][j - R], P[kp][j], du2, Bv[j]);
+              acc = __ffma2_rn(H, f2(Cv[j]), acc);
+            }
+            part[2 * kp] = acc.x;
+            part[2 * kp + 1] = acc.y;
+          }
+        } else {
+          // scalar path: per-cell range checks (large arguments, the last step)
+#pragma unroll
+          for (int k = 0; k < ND; ++k) {
+            float H[NL];
+#pragma unroll
+            for (int j = 0; j < NL; ++j) {
+              float& Pk = (k & 1) ? P[k >> 1][j].y : P[k >> 1][j].x;
+              float g;
+              if (j < R) {
+                g = rot_gate(dl[k], (k & 1) ? A2[k >> 1][j].y : A2[k >> 1][j].x,
+                             (k & 1) ? AI[k >> 1][j].y : AI[k >> 1][j].x);
+              } else {
+                g = (k & 1) ? TK[k >> 1][j - R].y : TK[k >> 1][j - R].x;
+              }
+              H[j] = cell_update(g, Pk, du[k], Bv[j]);
+            }
+            part[k] = y_partial<NL>(H, Cv);
+            if (last) {
+              const int d = dbase + k;
+              if (d < D) {
+#pragma unroll
+                for (int j = 0; j < NL; ++j) {
+                  const int n = LM::mem_lane(q, j, p.NR, p.NT);
+                  if (n >= 0) {
+                    const size_t gi = ((size_t)b * D + d) * N + n;
+                    p.h_last[gi] = __fmul_rn(0.5f, H[j]);
+                    p.dbu_last[gi] = __fmul_rn(du[k], Bv[j]);
+                  }
                 }
               }
             }

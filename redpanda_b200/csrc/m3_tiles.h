@@ -2,6 +2,7 @@
 // channel (state lanes are split over 4 threads); NDF / NDB = channels per
 // thread in the forward/step and in the backward kernel; NTHB = backward CTA
 // size (256 = two warpgroups, each with its own half of Tensor Memory).
+// NDB = 0: forward and step only (the backward needs R + T <= 16).
 // Any (n_rot, n_track) split is served by the smallest tiling with
 // R >= ceil(n_rot/4) and T >= ceil(n_track/4); surplus lanes are virtual.
 #pragma once
@@ -15,7 +16,7 @@
   X(4, 0, 8, 4, 256)    /* N=16, no tracking                                  */ \
   X(2, 0, 8, 8, 256)    /* N=8, no tracking                                   */ \
   X(8, 0, 4, 2, 256)    /* N=32, no tracking                                  */ \
-  X(12, 4, 2, 1, 256)   /* N=64, 48 rot + 16 track                            */ \
-  X(16, 0, 2, 1, 256)   /* N=64, no tracking                                  */ \
-  X(8, 8, 2, 1, 256)    /* fallback: up to 32 rot + 32 track                  */ \
-  X(16, 16, 1, 1, 128)  /* fallback: up to 64 rot + 64 track                  */
+  X(12, 4, 2, 2, 128)   /* N=64, 48 rot + 16 track                            */ \
+  X(16, 0, 2, 2, 128)   /* N=64, no tracking                                  */ \
+  X(8, 8, 2, 2, 128)    /* fallback: up to 32 rot + 32 track                  */ \
+  X(16, 16, 1, 0, 128)  /* fallback: up to 64 rot + 64 track                  */
