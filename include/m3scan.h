@@ -61,7 +61,9 @@ enum {
   M3_ERR_WORKSPACE = 6,    /* workspace missing or too small */
   M3_ERR_LAUNCH = 7,       /* the CUDA launch failed (see cudaGetLastError) */
   M3_ERR_DEVICE = 8,       /* a kernel recorded a device-side error */
-  M3_ERR_NO_DEVICE = 9     /* no CUDA device / the current device is not sm_100 */
+  M3_ERR_NO_DEVICE = 9,    /* no CUDA device / the current device is not sm_100 */
+  M3_ERR_SCRATCH_LIMIT = 10  /* m3_scan_bwd_noalloc: the problem needs more scratch than
+                                M3_NOALLOC_SCRATCH_BYTES */
 };
 
 typedef struct m3_scan_desc {
@@ -138,6 +140,31 @@ M3_API int m3_step(const m3_step_desc* desc, float* h, float* dbu,
             const void* delta, const void* u, const void* Bc, const void* Cc,
             const float* A_real_p, const float* A_imag_p, const float* track_p,
             float* y, void* stream);
+
+/* Size of the scratch buffer built into the library for m3_scan_bwd_noalloc. */
+#define M3_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+
+/* The analytic backward without a caller-supplied workspace.  No counterpart in
+ * the reference: it exists for callers that cannot allocate device memory when
+ * they run the backward (memory carved up at start-up by an allocator they have
+ * no handle to, or loops that must not call cudaMalloc).  Inputs and outputs
+ * are exactly those of m3_scan_bwd; the workspace comes from a device buffer of
+ * M3_NOALLOC_SCRATCH_BYTES that the library holds on every GPU that loads it,
+ * until the process exits.  This entry point never allocates or frees.
+ *   - Problems whose m3_scan_bwd_workspace_bytes() exceeds the buffer are
+ *     rejected with M3_ERR_SCRATCH_LIMIT.
+ *   - The first call on each device looks up the buffer's device address (with
+ *     that device current) and caches it; make that first call before any
+ *     stream capture.
+ *   - All calls on a device share the one buffer, which keeps the last call's
+ *     contents.  Calls whose executions overlap on the GPU (other streams, or
+ *     other host threads) race on it and corrupt each other's results. */
+M3_API int m3_scan_bwd_noalloc(const m3_scan_desc* desc,
+                const void* delta, const void* u, const void* Bc, const void* Cc,
+                const float* A_real_p, const float* A_imag_p, const float* track_p,
+                const void* dy, int32_t dtype_dy, const float* ckpt,
+                void* d_delta, void* d_u, void* d_Bc, void* d_Cc,
+                float* d_A_real_p, float* d_A_imag_p, float* d_track_p, void* stream);
 
 /* Reads (and clears when clear != 0) the device-side error word of the
  * current device; *code receives 0 or an M3_ERR_* value. */

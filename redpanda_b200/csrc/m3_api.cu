@@ -135,6 +135,9 @@ const char* m3_strerror(int code) {
     case M3_ERR_LAUNCH: return "m3: CUDA kernel launch failed";
     case M3_ERR_DEVICE: return "m3: a kernel recorded a device-side error";
     case M3_ERR_NO_DEVICE: return "m3: no sm_100 CUDA device is current";
+    case M3_ERR_SCRATCH_LIMIT:
+      return "m3: problem needs more backward scratch than the built-in no-allocation buffer "
+             "(M3_NOALLOC_SCRATCH_BYTES); use m3_scan_bwd with a workspace";
     default: return "m3: unknown status code";
   }
 }

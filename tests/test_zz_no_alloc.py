@@ -1,0 +1,114 @@
+"""m3_scan_bwd_noalloc: the backward for callers that cannot allocate.
+
+Some callers of this library cannot call cudaMalloc at the moment they run the
+backward (their device memory was carved up at start-up by an allocator they
+have no handle to, or they run in a loop that must not allocate).  For them the
+library exposes one entry point whose scratch lives in a device buffer built
+into the library.  This test calls it through the C ABI twice in a row, on
+different inputs and directions, and checks each result against the regular
+m3_scan_bwd (which is handed a caller-allocated workspace) within the
+gradient tolerance the parity tests use.  It also checks that a problem too
+large for the built-in buffer is refused with M3_ERR_SCRATCH_LIMIT.
+
+The file name makes pytest collect it last; it passes alone in a fresh process
+as well as after the other tests.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+from redpanda_b200 import _lib
+from redpanda_b200.scan import M3_DIR_BIDIR, M3_DIR_FWD, ScanPlan, pad_params
+from redpanda_b200.synthetic import ScanShape, make_scan_inputs
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-6               # fp32 gradient bar of the parity tests (norm-wise relative)
+M3_ERR_SCRATCH_LIMIT = 10
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    den = b.abs().max().item()
+    return (a - b).abs().max().item() / (den if den > 0 else 1.0)
+
+
+def _case(shape, seed, direction, dtype):
+    inp = make_scan_inputs(shape, seed=seed, dtype=dtype)
+    dev = torch.device("cuda")
+    g = {k: (None if v is None else v.to(dev)) for k, v in inp.items()}
+    D, N = shape.d_inner, shape.d_state
+    Ar, Ai, Tk = (t.contiguous() for t in pad_params(g["A_real"], g["A_imag"], g["track"],
+                                                     shape.n_rot, N, D, dev))
+    plan = ScanPlan(shape.batch, shape.seqlen, D, N, shape.n_rot, dtype, dtype, direction)
+    y = torch.empty(shape.batch, shape.seqlen, D, device=dev)
+    ckpt = torch.empty(max(plan.ckpt_floats(), 1), device=dev)
+    plan.forward(g["delta"], g["u"], g["Bc"], g["Cc"], Ar, Ai, Tk, y,
+                 ckpt if plan.ckpt_floats() else None)
+    dy = g["dy"].contiguous()
+    return plan, g, (Ar, Ai, Tk), dy, (ckpt if plan.ckpt_floats() else None)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _run(lib, plan, g, params, dy, ckpt, noalloc):
+    D, N = plan.shape[2], plan.shape[3]
+    outs = [torch.empty_like(g["delta"]), torch.empty_like(g["u"]), torch.empty_like(g["Bc"]),
+            torch.empty_like(g["Cc"])] + [torch.empty(D, N, device="cuda") for _ in range(3)]
+    Ar, Ai, Tk = params
+    stream = torch.cuda.current_stream().cuda_stream
+    args = [ctypes.byref(plan.desc), g["delta"].data_ptr(), g["u"].data_ptr(),
+            g["Bc"].data_ptr(), g["Cc"].data_ptr(), Ar.data_ptr(), Ai.data_ptr(), Tk.data_ptr(),
+            dy.data_ptr(), 0, _ptr(ckpt)] + [o.data_ptr() for o in outs]
+    if noalloc:
+        rc = lib.m3_scan_bwd_noalloc(*args, stream)
+    else:
+        nws = lib.m3_scan_bwd_workspace_bytes(ctypes.byref(plan.desc))
+        ws = torch.empty(nws, device="cuda", dtype=torch.uint8)
+        rc = lib.m3_scan_bwd(*args, ws.data_ptr(), nws, stream)
+    torch.cuda.synchronize()
+    assert rc == 0, _lib.strerror(rc)
+    return outs
+
+
+def test_noalloc_backward_matches_regular_backward_twice_in_a_row():
+    lib = _lib.load()
+    cases = [
+        (ScanShape(4, 40, 256, 32, 16, 4), 21, M3_DIR_BIDIR, torch.float32),
+        (ScanShape(3, 64, 192, 16, 4, 4), 22, M3_DIR_FWD, torch.float32),
+    ]
+    prepared = [_case(*c) for c in cases]
+    refs = []
+    for plan, g, params, dy, ckpt in prepared:
+        assert lib.m3_scan_bwd_workspace_bytes(ctypes.byref(plan.desc)) <= _noalloc_bytes()
+        refs.append(_run(lib, plan, g, params, dy, ckpt, noalloc=False))
+    # two no-allocation calls in a row: the second finds the first one's data
+    # in the shared buffer
+    gots = [_run(lib, *prep, noalloc=True) for prep in prepared]
+    for got, ref in zip(gots, refs):
+        for a, b in zip(got, ref):
+            assert torch.isfinite(a).all()
+            assert _rel(a, b) <= TOL
+
+
+def _noalloc_bytes():
+    # M3_NOALLOC_SCRATCH_BYTES in include/m3scan.h
+    return 64 * 1024 * 1024
+
+
+def test_noalloc_refuses_problems_beyond_its_buffer():
+    lib = _lib.load()
+    # config-2 rows: the workspace of 1024 rows is far above the built-in 64 MiB
+    shape = ScanShape(1024, 64, 1536, 32, 16, 4)
+    plan = ScanPlan(shape.batch, shape.seqlen, shape.d_inner, shape.d_state, shape.n_rot,
+                    torch.bfloat16, torch.bfloat16, M3_DIR_BIDIR)
+    assert lib.m3_scan_bwd_workspace_bytes(ctypes.byref(plan.desc)) > _noalloc_bytes()
+    fake = ctypes.c_void_p(256)   # never dereferenced: the size check comes first
+    args = [ctypes.byref(plan.desc)] + [fake] * 8 + [0, fake] + [fake] * 7
+    rc = lib.m3_scan_bwd_noalloc(*args, None)
+    assert rc == M3_ERR_SCRATCH_LIMIT
+    assert "no-allocation buffer" in _lib.strerror(rc)
