@@ -1,0 +1,280 @@
+"""Mamba-3 backbone whose scan and recurrent step run on the sm_100a kernels.
+
+Host-side mirror of ``redpanda/engine/mamba.py`` (the reference's backbone)
+with the same class names, constructor arguments, parameter names and
+initialisation, so a reference ``state_dict`` loads unchanged.  The
+projections (``in_proj``, ``x_proj``, ``dt_proj``, ``out_proj``), BCNorm and the
+gating stay plain PyTorch (cuBLAS GEMMs), exactly as in the reference; the
+recurrences go through :mod:`redpanda_b200.scan`:
+
+* causal scan (``_selective_scan_trapezoidal``, mamba.py:318-380) ->
+  ``m3_trapezoidal_scan`` (forward + analytic backward)
+* ``return_state`` priming (mamba.py:377-379) -> ``m3_scan_with_state``
+* bidirectional pair (mamba.py:254-260) -> one fused ``m3_bidir_scan`` launch
+* ``Mamba3Block.step`` recurrence (mamba.py:466-493) -> ``m3_step``
+
+There is no CPU path: the scan ops raise on CPU tensors.
+"""
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import scan as S
+
+
+@dataclass
+class MambaConfig:
+    """Fields and defaults of the reference ``MambaConfig`` (mamba.py:24-62)."""
+    d_model: int = 512
+    n_layer: int = 16
+    vocab_size: int = 8192
+    d_state: int = 64
+    expand: int = 2
+    dt_rank: int = 'auto'
+    pad_vocab_size_multiple: int = 8
+    bias: bool = False
+    use_complex: bool = True
+    mimo_p: int = 4
+    use_bcnorm: bool = True
+    n_track_state: int = 0
+    bidirectional: bool = False
+    grad_checkpoint: bool = False
+    scan_checkpoint: bool = True     # accepted for compatibility; the kernels checkpoint themselves
+    use_triton_scan: bool = False    # accepted for compatibility; the kernels are always used
+
+    def __post_init__(self):
+        self.d_inner = int(self.expand * self.d_model)
+        if self.dt_rank == 'auto':
+            self.dt_rank = math.ceil(self.d_model / 16)
+        assert 0 <= self.n_track_state < self.d_state, "n_track_state must be < d_state"
+        self.n_rot_state = self.d_state - self.n_track_state
+        if self.vocab_size % self.pad_vocab_size_multiple != 0:
+            self.vocab_size += (self.pad_vocab_size_multiple
+                                - self.vocab_size % self.pad_vocab_size_multiple)
+
+
+class RMSNorm(nn.Module):
+    """x * rsqrt(mean(x^2) + eps) * weight (mamba.py:82-89)."""
+
+    def __init__(self, d: int, eps: float = 1e-5):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(d))
+
+    def forward(self, x):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
+
+
+class Mamba3Block(nn.Module):
+    """One Mamba-3 layer (mamba.py:141-498) with the recurrences on the kernels."""
+
+    def __init__(self, config: MambaConfig):
+        super().__init__()
+        self.config = config
+        d_inner, n = config.d_inner, config.d_state
+        n_rot, n_track, p = config.n_rot_state, config.n_track_state, config.mimo_p
+        self.in_proj = nn.Linear(config.d_model, d_inner * 2, bias=config.bias)
+        self.x_proj = nn.Linear(d_inner, config.dt_rank + n * p * 2, bias=True)
+        self.dt_proj = nn.Linear(config.dt_rank, d_inner, bias=True)
+        with torch.no_grad():
+            # dt bias: softplus^-1 of log-uniform timescales in [1e-3, 1e-1]
+            dt0 = torch.exp(torch.rand(d_inner) * (math.log(0.1) - math.log(0.001))
+                            + math.log(0.001))
+            self.dt_proj.bias.copy_(dt0 + torch.log(-torch.expm1(-dt0)))
+            self.dt_proj.bias._no_reinit = True
+        if n_rot > 0:
+            mags = torch.arange(1, n_rot + 1, dtype=torch.float32).repeat(d_inner, 1)
+            if config.use_complex:
+                self.A_log_mag = nn.Parameter(torch.log(mags))
+                self.A_phase = nn.Parameter(torch.zeros(d_inner, n_rot))
+            else:
+                self.A_log = nn.Parameter(torch.log(mags))
+        if n_track > 0:
+            theta = torch.atanh(torch.linspace(-0.95, 0.95, n_track).clamp(-0.999, 0.999))
+            self.track_theta = nn.Parameter(theta.unsqueeze(0).repeat(d_inner, 1))
+        if config.use_bcnorm:
+            self.b_norm = RMSNorm(n * p)
+            self.c_norm = RMSNorm(n * p)
+        self.D = nn.Parameter(torch.ones(d_inner))
+        self.out_proj = nn.Linear(d_inner, config.d_model, bias=config.bias)
+
+    # -- eigenvalues (mamba.py:211-229)
+    def _compute_A(self):
+        if self.config.n_rot_state == 0:
+            return None, None
+        if self.config.use_complex:
+            mag = -torch.exp(self.A_log_mag.float())
+            phase = self.A_phase.float()
+            return mag * torch.cos(phase), mag * torch.sin(phase)
+        return -torch.exp(self.A_log.float()), None
+
+    def _track_gate(self):
+        return torch.tanh(self.track_theta.float())
+
+    # -- projections (mamba.py:284-301)
+    def _ssm_proj(self, u):
+        cfg = self.config
+        n, p = cfg.d_state, cfg.mimo_p
+        x_dbl = self.x_proj(u)
+        dt_raw, B_raw, C_raw = x_dbl.split([cfg.dt_rank, n * p, n * p], dim=-1)
+        if cfg.use_bcnorm:
+            B_raw = self.b_norm(B_raw)
+            C_raw = self.c_norm(C_raw)
+        B = B_raw.view(*u.shape[:-1], n, p)
+        C = C_raw.view(*u.shape[:-1], n, p)
+        delta = F.softplus(self.dt_proj(dt_raw))
+        return delta, B, C
+
+    def _scan_args(self, delta, u, B, C):
+        cfg = self.config
+        track = self._track_gate() if cfg.n_track_state > 0 else None
+        A_real, A_imag = self._compute_A()
+        return (delta, u, B.sum(dim=-1), C.sum(dim=-1), A_real, A_imag, track,
+                cfg.n_rot_state, cfg.d_state)
+
+    def _selective_scan_trapezoidal(self, u, delta, A_real, A_imag, B, C, D,
+                                    return_state=False):
+        """Same contract as mamba.py:318-380: returns y + u*D (and the state)."""
+        cfg = self.config
+        track = self._track_gate() if cfg.n_track_state > 0 else None
+        args = (delta, u, B.sum(dim=-1), C.sum(dim=-1), A_real, A_imag, track,
+                cfg.n_rot_state, cfg.d_state)
+        if return_state:
+            y, state = S.m3_scan_with_state(*args)
+            return y + u * D, state
+        return S.m3_trapezoidal_scan(*args) + u * D
+
+    def ssm(self, u, return_state=False):
+        delta, B, C = self._ssm_proj(u)
+        A_real, A_imag = self._compute_A()
+        return self._selective_scan_trapezoidal(u, delta, A_real, A_imag, B, C, self.D,
+                                                return_state=return_state)
+
+    def forward(self, x):
+        """mamba.py:231-267; the bidirectional pair is one fused launch."""
+        x_branch, z = self.in_proj(x).chunk(2, dim=-1)
+        x_branch = F.silu(x_branch)
+        if not self.config.bidirectional:
+            y = self.ssm(x_branch)
+        else:
+            delta, B, C = self._ssm_proj(x_branch)
+            y = S.m3_bidir_scan(*self._scan_args(delta, x_branch, B, C)) \
+                + 2.0 * x_branch * self.D
+        return self.out_proj(y * F.silu(z))
+
+    def forward_with_state(self, x):
+        """mamba.py:269-282: output and the (h_last, dBu_last) state."""
+        x_branch, z = self.in_proj(x).chunk(2, dim=-1)
+        x_branch = F.silu(x_branch)
+        y, state = self.ssm(x_branch, return_state=True)
+        return self.out_proj(y * F.silu(z)), state
+
+    def _step_inputs(self, x_t):
+        x_branch, z = self.in_proj(x_t).chunk(2, dim=-1)
+        x_branch = F.silu(x_branch)
+        delta, B, C = self._ssm_proj(x_branch)
+        return x_branch, z, delta, B.sum(dim=-1), C.sum(dim=-1)
+
+    def step_(self, x_t, state):
+        """In-place O(1) step: advances ``state = (h, dBu)`` (float32, contiguous)."""
+        cfg = self.config
+        u, z, delta, Bc, Cc = self._step_inputs(x_t)
+        h, dbu = state
+        A_real, A_imag = self._compute_A()
+        track = self._track_gate() if cfg.n_track_state > 0 else None
+        y = S.m3_step_(h, dbu, delta, u, Bc, Cc, A_real, A_imag, track,
+                       cfg.n_rot_state, cfg.d_state)
+        y = y + u * self.D
+        return self.out_proj(y * F.silu(z)), state
+
+    def step(self, x_t, state=None):
+        """Functional O(1) step (mamba.py:427-498): returns (out, (h, dBu_t))."""
+        cfg = self.config
+        if state is None:
+            h = torch.zeros(x_t.shape[0], cfg.d_inner, cfg.d_state, device=x_t.device)
+            state = (h, torch.zeros_like(h))
+        else:
+            state = tuple(s.detach().to(torch.float32).clone(
+                memory_format=torch.contiguous_format) for s in state)
+        return self.step_(x_t, state)
+
+
+class Mamba(nn.Module):
+    """Embedding + Mamba3Block layers + final norm (mamba.py:503-620)."""
+
+    def __init__(self, config: MambaConfig):
+        super().__init__()
+        self.config = config
+        self.grad_checkpoint = getattr(config, "grad_checkpoint", False)
+        self.embedding = nn.Embedding(config.vocab_size, config.d_model)
+        self.layers = nn.ModuleList([
+            nn.ModuleDict({"mixer": Mamba3Block(config), "norm": RMSNorm(config.d_model)})
+            for _ in range(config.n_layer)
+        ])
+        self.norm_f = RMSNorm(config.d_model)
+        self.apply(self._init_weights)
+
+    def _init_weights(self, module):
+        if isinstance(module, nn.Linear):
+            nn.init.normal_(module.weight, mean=0.0, std=0.02)
+            if module.bias is not None and not getattr(module.bias, "_no_reinit", False):
+                nn.init.zeros_(module.bias)
+        elif isinstance(module, nn.Embedding):
+            nn.init.normal_(module.weight, mean=0.0, std=0.02)
+
+    def forward(self, input_ids, input_embeds=None):
+        x = input_embeds if input_embeds is not None else self.embedding(input_ids)
+        for layer in self.layers:
+            mixer, norm = layer["mixer"], layer["norm"]
+            if self.grad_checkpoint and self.training and x.requires_grad:
+                x = x + torch.utils.checkpoint.checkpoint(
+                    lambda inp, m=mixer, nm=norm: m(nm(inp)), x, use_reentrant=False)
+            else:
+                x = x + mixer(norm(x))
+        return self.norm_f(x)
+
+    def init_cache(self, batch_size, device):
+        return [None] * len(self.layers)
+
+    def _embed_step(self, token_id, input_embed):
+        if input_embed is not None:
+            return input_embed
+        if token_id.dim() == 2:
+            token_id = token_id.squeeze(1)
+        return self.embedding(token_id)
+
+    def step(self, token_id=None, cache=None, input_embed=None, apply_final_norm=True):
+        """mamba.py:564-601; returns (hidden, new_cache) without touching ``cache``."""
+        assert not self.config.bidirectional, "step() requires a causal model"
+        x = self._embed_step(token_id, input_embed)
+        cache = cache if cache is not None else [None] * len(self.layers)
+        new_cache = []
+        for i, layer in enumerate(self.layers):
+            delta, st = layer["mixer"].step(layer["norm"](x), cache[i])
+            x = x + delta
+            new_cache.append(st)
+        return (self.norm_f(x) if apply_final_norm else x), new_cache
+
+    def step_(self, token_id=None, cache=None, input_embed=None, apply_final_norm=True):
+        """In-place variant for lockstep rollouts: advances every (h, dBu) in ``cache``."""
+        assert not self.config.bidirectional, "step() requires a causal model"
+        x = self._embed_step(token_id, input_embed)
+        for i, layer in enumerate(self.layers):
+            delta, _ = layer["mixer"].step_(layer["norm"](x), cache[i])
+            x = x + delta
+        return (self.norm_f(x) if apply_final_norm else x), cache
+
+    def prime_cache(self, input_ids):
+        """mamba.py:603-620: full scan once, then (final_hidden, cache)."""
+        assert not self.config.bidirectional, "prime_cache() requires a causal model"
+        cur = self.embedding(input_ids)
+        cache = []
+        for layer in self.layers:
+            mixed, state = layer["mixer"].forward_with_state(layer["norm"](cur))
+            cur = cur + mixed
+            cache.append(state)
+        return self.norm_f(cur[:, -1, :]), cache

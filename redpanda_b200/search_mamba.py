@@ -1,0 +1,180 @@
+"""Search Mamba on the sm_100a kernels: the MARS node-evaluation surfaces.
+
+Mirror of ``redpanda/engine/search_mamba.py`` (same heads, parameter names and
+initialisation) over :class:`redpanda_b200.mamba.Mamba`.  The O(1) node step
+(``eval_step``, ``evaluate_lines_fast``, ``score_branch``) runs the recurrent
+step kernel; priming runs the scan with ``return_state``.
+``dynamics_rollout`` (the training rollout, search_mamba.py:252-273) uses the
+equivalent causal scan over the concatenated board + move tokens, so it is
+differentiable through the scan kernel's analytic backward.
+"""
+
+import json
+from dataclasses import asdict, fields as dc_fields
+
+import torch
+import torch.nn as nn
+
+from .mamba import Mamba, MambaConfig
+
+
+class SearchMambaConfig(MambaConfig):
+    """Mirrors the reference subclass (search_mamba.py:24-36).
+
+    Like the reference, the class is not re-decorated as a dataclass, so its
+    annotated defaults do not reach ``__init__``; callers pass shapes explicitly.
+    """
+    d_model: int = 384
+    n_layer: int = 12
+    d_state: int = 32
+    expand: int = 2
+    use_complex: bool = True
+    mimo_p: int = 2
+    use_bcnorm: bool = True
+
+
+class SearchMamba(nn.Module):
+    """Causal Mamba + value / continuation / consistency heads (search_mamba.py:39-101)."""
+
+    def __init__(self, config: SearchMambaConfig = None, vocab_size: int = 8192,
+                 eval_dim: int = 512):
+        super().__init__()
+        if config is None:
+            config = SearchMambaConfig(vocab_size=vocab_size)
+        config.bidirectional = False
+        self.config = config
+        self.eval_dim = eval_dim
+        self.backbone = Mamba(config)
+        d = config.d_model
+        self.line_value_head = nn.Sequential(
+            nn.Linear(d, d), nn.GELU(), nn.LayerNorm(d),
+            nn.Linear(d, d // 2), nn.GELU(), nn.Linear(d // 2, 1))
+        self.value_head = nn.Sequential(
+            nn.Linear(d, d), nn.GELU(), nn.LayerNorm(d), nn.Linear(d, 1))
+        self.continuation_head = nn.Sequential(
+            nn.Linear(d, d * 2), nn.GELU(), nn.LayerNorm(d * 2),
+            nn.Linear(d * 2, config.vocab_size))
+        self.consistency_proj = nn.Sequential(
+            nn.Linear(d, d), nn.GELU(), nn.Linear(d, eval_dim))
+        self.apply(self._init_weights)
+
+    def _init_weights(self, m):
+        if isinstance(m, nn.Linear):
+            nn.init.orthogonal_(m.weight, gain=1.0)
+            if m.bias is not None:
+                nn.init.constant_(m.bias, 0)
+
+    def _device(self):
+        return next(self.parameters()).device
+
+    # -- full-sequence scoring (search_mamba.py:103-158)
+    def forward(self, board_encoding, move_sequences):
+        hidden = self.backbone(torch.cat([board_encoding, move_sequences], dim=-1))
+        return self.line_value_head(hidden[:, -1, :]).squeeze(-1)
+
+    def evaluate_lines(self, board_encoding, move_sequences):
+        if board_encoding.dim() == 1:
+            board_encoding = board_encoding.unsqueeze(0)
+        return self.forward(board_encoding.expand(move_sequences.shape[0], -1), move_sequences)
+
+    def evaluate_with_continuation(self, board_encoding, move_sequences):
+        if board_encoding.dim() == 1:
+            board_encoding = board_encoding.unsqueeze(0)
+        full = torch.cat([board_encoding.expand(move_sequences.shape[0], -1), move_sequences], -1)
+        final = self.backbone(full)[:, -1, :]
+        return self.line_value_head(final).squeeze(-1), self.continuation_head(final)
+
+    # -- O(1) cached evaluation (search_mamba.py:162-291)
+    def prime_board(self, board_encoding):
+        if not torch.is_tensor(board_encoding):
+            board_encoding = torch.as_tensor(board_encoding, dtype=torch.long,
+                                             device=self._device())
+        if board_encoding.dim() == 1:
+            board_encoding = board_encoding.unsqueeze(0)
+        return self.backbone.prime_cache(board_encoding)
+
+    @staticmethod
+    def _expand_cache(cache, k):
+        """Broadcast a B=1 cache to B=k rows (contiguous copies, as the reference)."""
+        return [(h.expand(k, *h.shape[1:]).contiguous(), dbu.expand(k, *dbu.shape[1:]).contiguous())
+                for h, dbu in cache]
+
+    @torch.no_grad()
+    def evaluate_lines_fast(self, board_encoding, move_sequences, lengths=None):
+        device = self._device()
+        _, cache = self.prime_board(board_encoding.to(device))
+        K, L = move_sequences.shape
+        move_sequences = move_sequences.to(device)
+        cache = self._expand_cache(cache, K)
+        hiddens = []
+        for t in range(L):
+            hidden, cache = self.backbone.step_(token_id=move_sequences[:, t], cache=cache)
+            hiddens.append(hidden)
+        hiddens = torch.stack(hiddens, dim=1)
+        if lengths is not None:
+            idx = (lengths.to(device).clamp(min=1) - 1).view(K, 1, 1).expand(-1, 1, hiddens.shape[-1])
+            final = hiddens.gather(1, idx).squeeze(1)
+        else:
+            final = hiddens[:, -1, :]
+        return self.line_value_head(final).squeeze(-1)
+
+    @torch.no_grad()
+    def score_branch(self, board_cache, move_sequence):
+        device = self._device()
+        cache = self._expand_cache(board_cache, 1)
+        hidden = None
+        for tok in move_sequence:
+            hidden, cache = self.backbone.step_(
+                token_id=torch.tensor([int(tok)], device=device), cache=cache)
+        quality = self.line_value_head(hidden).squeeze(-1)
+        return quality.item(), self.continuation_head(hidden).squeeze(0)
+
+    @torch.no_grad()
+    def eval_step(self, cache, move_token):
+        """One O(1) node evaluation for MARS (search_mamba.py:275-291).
+
+        Returns (value, continuation logits, new cache); ``cache`` is not modified.
+        """
+        tok = torch.tensor([int(move_token)], device=self._device())
+        h, cache = self.backbone.step(token_id=tok, cache=cache)
+        value = torch.tanh(self.value_head(h)).squeeze(-1).item()
+        return value, self.continuation_head(h).squeeze(0), cache
+
+    def dynamics_rollout(self, board_encoding, move_tokens):
+        """Training rollout (search_mamba.py:252-273) as one causal scan.
+
+        Priming on the board and stepping through the moves is the same
+        recurrence as scanning the concatenated sequence; the hidden state
+        after move t is the scan output at position L_board + t.
+        """
+        Lb = board_encoding.shape[1]
+        hidden = self.backbone(torch.cat([board_encoding, move_tokens], dim=1))[:, Lb:]
+        values = torch.tanh(self.value_head(hidden)).squeeze(-1)
+        return values, self.continuation_head(hidden), self.consistency_proj(hidden)
+
+    # -- persistence (search_mamba.py:347-383)
+    def save_pretrained(self, path):
+        torch.save(self.state_dict(), path)
+        cfg_path = path.replace('.pt', '_config.json').replace('.pth', '_config.json')
+        if cfg_path == path:
+            cfg_path = path + '.config.json'
+        cfg = asdict(self.config)
+        cfg["eval_dim"] = self.eval_dim
+        with open(cfg_path, 'w') as f:
+            json.dump(cfg, f, indent=2)
+
+    @classmethod
+    def from_pretrained(cls, path, device='cpu', config=None):
+        eval_dim = 512
+        if config is None:
+            cfg_path = path.replace('.pt', '_config.json').replace('.pth', '_config.json')
+            if cfg_path == path:
+                cfg_path = path + '.config.json'
+            with open(cfg_path) as f:
+                cfg = json.load(f)
+            eval_dim = int(cfg.get("eval_dim", 512))
+            valid = {f.name for f in dc_fields(SearchMambaConfig)}
+            config = SearchMambaConfig(**{k: v for k, v in cfg.items() if k in valid})
+        model = cls(config, eval_dim=eval_dim)
+        model.load_state_dict(torch.load(path, map_location=device, weights_only=True))
+        return model

@@ -1,0 +1,160 @@
+"""Model-level parity: redpanda_b200.mamba / search_mamba against the reference.
+
+Golden fixtures (tests/golden/model_*.pt) hold a reference ``Mamba`` state dict,
+token ids and the reference's own forward output, parameter gradients of
+``y.pow(2).mean()`` (the loss of the reference's verify gate,
+triton_scan.py:374-384), the ``step`` chain and ``prime_cache`` results.  The
+mirror loads the same state dict and must reproduce them; the projections are
+fp32 cuBLAS GEMMs here and CPU GEMMs in the fixtures, so the bars are
+end-to-end model tolerances, tighter than the reference's own 2e-3 gate.
+"""
+
+import glob
+import os
+
+import pytest
+import torch
+
+from redpanda_b200.mamba import Mamba, MambaConfig
+from redpanda_b200.search_mamba import SearchMamba, SearchMambaConfig
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+FWD_TOL = 1e-5
+GRAD_TOL = 1e-4
+STEP_TOL = 1e-5
+
+
+def _rel(a, b):
+    a, b = a.detach().double().cpu(), b.detach().double().cpu()
+    den = b.abs().max().item()
+    return (a - b).abs().max().item() / (den if den > 0 else 1.0)
+
+
+def _load(name):
+    c = torch.load(os.path.join(GOLDEN, name + ".pt"))
+    cfg = MambaConfig(vocab_size=64, bidirectional=c["bidir"], **c["kw"])
+    m = Mamba(cfg).cuda()
+    m.load_state_dict(c["state_dict"])
+    return c, m
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+@pytest.mark.parametrize("name", sorted(os.path.basename(p)[:-3]
+                                        for p in glob.glob(os.path.join(GOLDEN, "model_*.pt"))))
+def test_forward_and_param_grads_match_reference(name):
+    c, m = _load(name)
+    m.train()
+    y = m(c["ids"].cuda())
+    y.pow(2).mean().backward()
+    assert _rel(y, c["forward"]) <= FWD_TOL
+    grads = dict(m.named_parameters())
+    for k, g in c["param_grads"].items():
+        assert grads[k].grad is not None, k
+        assert _rel(grads[k].grad, g) <= GRAD_TOL, k
+
+
+@pytest.mark.parametrize("name", ["model_verify_trk", "model_verify_notrk"])
+def test_step_chain_and_prime_match_reference(name):
+    c, m = _load(name)
+    m.eval()
+    ids = c["ids"].cuda()
+    with torch.no_grad():
+        cache, hs = None, []
+        for t in range(ids.shape[1]):
+            h, cache = m.step(token_id=ids[:, t], cache=cache)
+            hs.append(h)
+        assert _rel(torch.stack(hs, 1), c["step_hidden"]) <= STEP_TOL
+        for (h1, d1), (h2, d2) in zip(cache, c["step_cache_last"]):
+            assert _rel(h1, h2) <= STEP_TOL and _rel(d1, d2) <= STEP_TOL
+        k = c["prime_k"]
+        fin, pc = m.prime_cache(ids[:, :k])
+        assert _rel(fin, c["prime_final"]) <= STEP_TOL
+        nxt, _ = m.step(token_id=ids[:, k], cache=pc)
+        assert _rel(nxt, c["prime_next"]) <= STEP_TOL
+
+
+def test_step_matches_forward_reference_gate():
+    """test_v3.py:44-56 / test_v4.py:35-46: step over a sequence equals the forward."""
+    torch.manual_seed(0)
+    m = Mamba(MambaConfig(d_model=32, n_layer=3, d_state=12, n_track_state=4, mimo_p=2,
+                          vocab_size=500)).cuda().eval()
+    ids = torch.randint(0, 500, (2, 10), device="cuda")
+    with torch.no_grad():
+        full = m(ids)
+        cache, outs = None, []
+        for t in range(10):
+            h, cache = m.step(token_id=ids[:, t], cache=cache)
+            outs.append(h)
+    assert torch.allclose(full, torch.stack(outs, 1), atol=1e-5)
+    assert float(m.layers[0]["mixer"]._track_gate().detach().min()) < -0.5
+
+
+def test_inplace_step_equals_functional_step():
+    torch.manual_seed(1)
+    m = Mamba(MambaConfig(d_model=64, n_layer=2, d_state=32, n_track_state=8, mimo_p=2,
+                          vocab_size=256)).cuda().eval()
+    ids = torch.randint(0, 256, (5, 12), device="cuda")
+    with torch.no_grad():
+        _, cache = m.prime_cache(ids[:, :8])
+        cache_b = [(h.clone(), d.clone()) for h, d in cache]
+        for t in range(8, 12):
+            ha, cache = m.step(token_id=ids[:, t], cache=cache)
+            hb, cache_b = m.step_(token_id=ids[:, t], cache=cache_b)
+            assert torch.equal(ha, hb)
+        for (h1, d1), (h2, d2) in zip(cache, cache_b):
+            assert torch.equal(h1, h2) and torch.equal(d1, d2)
+
+
+def test_bidirectional_rejects_step_and_prime():
+    m = Mamba(MambaConfig(d_model=32, n_layer=2, d_state=8, mimo_p=2, vocab_size=64,
+                          bidirectional=True)).cuda()
+    ids = torch.randint(0, 64, (2, 10), device="cuda")
+    assert m(ids).shape == (2, 10, 32)
+    with pytest.raises(AssertionError):
+        m.prime_cache(ids)
+
+
+def test_search_mamba_fast_line_eval_equals_slow():
+    """test_v3.py:78-88: cached (prime + step) line scores equal the full forward."""
+    torch.manual_seed(2)
+    scfg = SearchMambaConfig(d_model=32, n_layer=2, d_state=8, mimo_p=2, vocab_size=300)
+    sm = SearchMamba(scfg, vocab_size=300).cuda().eval()
+    board = torch.randint(1, 300, (40,), device="cuda")
+    lines = torch.randint(1, 300, (6, 5), device="cuda")
+    with torch.no_grad():
+        slow = sm.evaluate_lines(board, lines)
+        fast = sm.evaluate_lines_fast(board, lines)
+    assert torch.allclose(slow, fast, atol=1e-4)
+
+
+def test_search_mamba_dynamics_and_eval_step():
+    """test_v4.py:61-78: rollout shapes, tanh bounds, differentiability, eval_step."""
+    torch.manual_seed(3)
+    scfg = SearchMambaConfig(d_model=24, n_layer=2, d_state=8, n_track_state=2, mimo_p=2,
+                             vocab_size=200)
+    sm = SearchMamba(scfg, vocab_size=200, eval_dim=32).cuda()
+    board = torch.randint(1, 200, (3, 20), device="cuda")
+    moves = torch.randint(1, 200, (3, 5), device="cuda")
+    v, c, f = sm.dynamics_rollout(board, moves)
+    assert v.shape == (3, 5) and c.shape == (3, 5, scfg.vocab_size) and f.shape == (3, 5, 32)
+    assert v.abs().max().item() <= 1.0001
+    (v.pow(2).mean() + c.mean() + f.pow(2).mean()).backward()
+    gsum = sum(p.grad.abs().sum().item() for p in sm.parameters() if p.grad is not None)
+    assert gsum > 0 and gsum == gsum
+    sm.eval()
+    _, cache = sm.prime_board(board[0])
+    val, cont, cache2 = sm.eval_step(cache, int(moves[0, 0]))
+    assert isinstance(val, float) and cont.shape[0] == scfg.vocab_size
+    # the rollout's per-move values equal prime + eval_step on the same line
+    with torch.no_grad():
+        vr, _, _ = sm.dynamics_rollout(board[:1], moves[:1, :1])
+    assert abs(vr.item() - val) < 1e-4
