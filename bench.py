@@ -382,7 +382,22 @@ def run_step_rollout(dev, args):
                 anchor()
             one_step()
 
+    # factored state: h in place, [delta*u | B] factors ping-ponged per layer
+    fac = [[torch.zeros(Bs, Ds + Ns, device=dev) for _ in range(2)] for _ in range(layers)]
+    fdesc = S.StepDesc(Bs, Ds, Ns, nr, S.M3_F32, S.M3_F32)
+
+    def one_step_factored(parity):
+        for li in range(layers):
+            ar, ai, tk = params[li]
+            S._lib.check(lib.m3_step_factored(
+                fdesc, h[li].data_ptr(), fac[li][parity].data_ptr(),
+                fac[li][parity ^ 1].data_ptr(), tok["delta"].data_ptr(), tok["u"].data_ptr(),
+                tok["Bc"].data_ptr(), tok["Cc"].data_ptr(), ar.data_ptr(), ai.data_ptr(),
+                tk.data_ptr(), ystep.data_ptr(), sh))
+
     rollout()
+    for s_ in range(4):
+        one_step_factored(s_ & 1)
     torch.cuda.synchronize(dev)
     e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     e[0].record(stream)
@@ -391,9 +406,13 @@ def run_step_rollout(dev, args):
     for _ in range(32):
         one_step()
     e[2].record(stream)
+    for s_ in range(32):
+        one_step_factored(s_ & 1)
+    e[3].record(stream)
     torch.cuda.synchronize(dev)
     total_ms = e[0].elapsed_time(e[1])
     steps_ms = e[1].elapsed_time(e[2])
+    fsteps_ms = e[2].elapsed_time(e[3])
     peak, kind = _peaks()
     state_bytes = layers * Bs * Ds * Ns * 16
     return {
@@ -406,6 +425,9 @@ def run_step_rollout(dev, args):
         "step_hbm_gbs": state_bytes / (steps_ms / 32 / 1e3) / 1e9,
         "step_hbm_frac": state_bytes / (steps_ms / 32 / 1e3) / 1e9 / peak,
         "step_algorithmic_bytes": state_bytes,
+        "factored_step_node_steps_per_s": Bs * 32 / (fsteps_ms / 1e3),
+        "factored_step_hbm_gbs": state_bytes / 2 / (fsteps_ms / 32 / 1e3) / 1e9,
+        "factored_step_hbm_frac": state_bytes / 2 / (fsteps_ms / 32 / 1e3) / 1e9 / peak,
         "gpu_launches": 32 * layers + 4 * layers,
         "note": "recurrence kernels only; the projection GEMMs of Mamba.step are not included",
     }

@@ -62,8 +62,9 @@ enum {
   M3_ERR_LAUNCH = 7,       /* the CUDA launch failed (see cudaGetLastError) */
   M3_ERR_DEVICE = 8,       /* a kernel recorded a device-side error */
   M3_ERR_NO_DEVICE = 9,    /* no CUDA device / the current device is not sm_100 */
-  M3_ERR_SCRATCH_LIMIT = 10  /* m3_scan_bwd_noalloc: the problem needs more scratch than
+  M3_ERR_SCRATCH_LIMIT = 10, /* m3_scan_bwd_noalloc: the problem needs more scratch than
                                 M3_NOALLOC_SCRATCH_BYTES */
+  M3_ERR_ALIAS = 11          /* two buffers that must be distinct overlap */
 };
 
 typedef struct m3_scan_desc {
@@ -138,6 +139,20 @@ M3_API int m3_scan_bwd(const m3_scan_desc* desc,
  * same per-token inputs and the scan's state. */
 M3_API int m3_step(const m3_step_desc* desc, float* h, float* dbu,
             const void* delta, const void* u, const void* Bc, const void* Cc,
+            const float* A_real_p, const float* A_imag_p, const float* track_p,
+            float* y, void* stream);
+
+/* O(1) step with the factored state: the same recurrence as m3_step with half
+ * its HBM traffic.  The state is h (B, D, N) fp32, updated in place, and the
+ * factors of the last token's input contribution, fac (B, D + N) fp32 =
+ * [delta*u (D) | B (N)], read from fac_prev and written to fac_next (distinct
+ * buffers; swap them between steps).  dBu = (delta*u)*B is rebuilt with the
+ * scan's own rounding, so the outputs equal m3_step's bit for bit.  The
+ * factors after a scan are [delta[L-1]*u[L-1] | Bc[L-1]] of its inputs.
+ * Extends the cache contract of Mamba3Block.step (mamba.py:487-498), whose
+ * dBu tensor it replaces by its two factors. */
+M3_API int m3_step_factored(const m3_step_desc* desc, float* h, const float* fac_prev,
+            float* fac_next, const void* delta, const void* u, const void* Bc, const void* Cc,
             const float* A_real_p, const float* A_imag_p, const float* track_p,
             float* y, void* stream);
 

@@ -44,6 +44,7 @@ SIGNATURES = {
     "m3_scan_bwd": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P,
                                    _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "m3_step": (ctypes.c_int, [_S, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "m3_step_factored": (ctypes.c_int, [_S, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "m3_scan_bwd_noalloc": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P,
                                            _P, _P, _P, _P, _P, _P, _P, _P]),
     "m3_device_error": (ctypes.c_int, [ctypes.POINTER(_I), _I]),

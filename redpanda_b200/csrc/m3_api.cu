@@ -135,6 +135,7 @@ const char* m3_strerror(int code) {
     case M3_ERR_LAUNCH: return "m3: CUDA kernel launch failed";
     case M3_ERR_DEVICE: return "m3: a kernel recorded a device-side error";
     case M3_ERR_NO_DEVICE: return "m3: no sm_100 CUDA device is current";
+    case M3_ERR_ALIAS: return "m3: two buffers that must be distinct overlap";
     case M3_ERR_SCRATCH_LIMIT:
       return "m3: problem needs more backward scratch than the built-in no-allocation buffer "
              "(M3_NOALLOC_SCRATCH_BYTES); use m3_scan_bwd with a workspace";
@@ -256,36 +257,66 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 
-int m3_step(const m3_step_desc* desc, float* h, float* dbu, const void* delta, const void* u,
-            const void* Bc, const void* Cc, const float* A_real_p, const float* A_imag_p,
-            const float* track_p, float* y, void* stream) {
+static int step_common(const m3_step_desc* desc, float* h, float* dbu, const float* fac_prev,
+                       float* fac_next, const void* delta, const void* u, const void* Bc,
+                       const void* Cc, const float* A_real_p, const float* A_imag_p,
+                       const float* track_p, float* y, void* stream) {
   if (!desc) return M3_ERR_NULL;
   if (desc->batch < 1 || desc->d_inner < 1 || desc->d_state < 1 || desc->d_state > kMaxState ||
       desc->n_rot < 0 || desc->n_rot > desc->d_state)
     return M3_ERR_SHAPE;
   if (!dtype_ok(desc->dtype_du) || !dtype_ok(desc->dtype_bc)) return M3_ERR_DTYPE;
-  if (!h || !dbu || !delta || !u || !Bc || !Cc || !A_real_p || !A_imag_p || !track_p || !y)
+  const bool factored = fac_next != nullptr;
+  if (!h || !delta || !u || !Bc || !Cc || !A_real_p || !A_imag_p || !track_p || !y)
     return M3_ERR_NULL;
+  if (factored ? !fac_prev : !dbu) return M3_ERR_NULL;
   Tile t;
   if (!select_tile(desc->n_rot, desc->d_state - desc->n_rot, &t)) return M3_ERR_UNSUPPORTED;
   if ((desc->d_inner + 31) / 32 > 65535) return M3_ERR_SHAPE;
   const int esd = dsize(desc->dtype_du), esb = dsize(desc->dtype_bc);
-  if (!aligned(h, 4) || !aligned(dbu, 4) || !aligned(delta, esd) || !aligned(u, esd) ||
+  if (!aligned(h, 16) || (dbu && !aligned(dbu, 16)) || (fac_prev && !aligned(fac_prev, 4)) ||
+      (fac_next && !aligned(fac_next, 4)) || !aligned(delta, esd) || !aligned(u, esd) ||
       !aligned(Bc, esb) || !aligned(Cc, esb) || !aligned(A_real_p, 4) || !aligned(A_imag_p, 4) ||
       !aligned(track_p, 4) || !aligned(y, 4))
     return M3_ERR_ALIGN;
+  if (factored) {
+    const size_t bytes = (size_t)desc->batch * (desc->d_inner + desc->d_state) * 4;
+    const char* a = reinterpret_cast<const char*>(fac_prev);
+    const char* b = reinterpret_cast<const char*>(fac_next);
+    if (a < b + bytes && b < a + bytes) return M3_ERR_ALIAS;
+  }
   int rc = check_device();
   if (rc != M3_OK) return rc;
   StepParams p;
   memset(&p, 0, sizeof(p));
-  p.h = h; p.dbu = dbu; p.delta = delta; p.u = u; p.Bc = Bc; p.Cc = Cc;
+  p.h = h; p.dbu = dbu; p.fac_in = fac_prev; p.fac_out = fac_next; p.factored = factored;
+  p.delta = delta; p.u = u; p.Bc = Bc; p.Cc = Cc;
   p.Ar = A_real_p; p.Ai = A_imag_p; p.Tk = track_p; p.y = y;
   p.B = desc->batch; p.D = desc->d_inner; p.N = desc->d_state;
   p.NR = desc->n_rot; p.NT = desc->d_state - desc->n_rot;
   p.dt_du = desc->dtype_du; p.dt_bc = desc->dtype_bc;
+  p.vec_bc = aligned(Bc, 16) && aligned(Cc, 16);
+  p.vec_fac = factored && aligned(fac_prev, 16) && aligned(fac_next, 16) &&
+              (desc->d_inner % 4) == 0;
   p.err = device_err_ptr();
   cudaError_t e = launch_step(t, p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
+int m3_step(const m3_step_desc* desc, float* h, float* dbu, const void* delta, const void* u,
+            const void* Bc, const void* Cc, const float* A_real_p, const float* A_imag_p,
+            const float* track_p, float* y, void* stream) {
+  return step_common(desc, h, dbu, nullptr, nullptr, delta, u, Bc, Cc, A_real_p, A_imag_p,
+                     track_p, y, stream);
+}
+
+int m3_step_factored(const m3_step_desc* desc, float* h, const float* fac_prev, float* fac_next,
+                     const void* delta, const void* u, const void* Bc, const void* Cc,
+                     const float* A_real_p, const float* A_imag_p, const float* track_p,
+                     float* y, void* stream) {
+  if (!fac_next) return M3_ERR_NULL;
+  return step_common(desc, h, nullptr, fac_prev, fac_next, delta, u, Bc, Cc, A_real_p, A_imag_p,
+                     track_p, y, stream);
 }
 
 int m3_device_error(int32_t* code, int32_t clear) {

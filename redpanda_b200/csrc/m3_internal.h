@@ -52,7 +52,11 @@ struct BwdParams {
 };
 
 struct StepParams {
-  float* h; float* dbu;
+  float* h; float* dbu;                       // full state (dbu unused when factored)
+  const float* fac_in; float* fac_out;        // factored state: [delta*u | B], (B, D + N)
+  int factored;
+  int vec_bc;                                 // Bc/Cc 16-byte aligned: vector row loads
+  int vec_fac;                                // factors 16-byte aligned, D % 4 == 0
   const void* delta; const void* u; const void* Bc; const void* Cc;
   const float* Ar; const float* Ai; const float* Tk;
   float* y;

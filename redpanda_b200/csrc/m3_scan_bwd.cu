@@ -29,8 +29,18 @@
 #include "m3_tiles.h"
 #include "m3_tmem.cuh"
 
+#ifndef M3_BWD_UNROLL_RECOMPUTE
+#define M3_BWD_UNROLL_RECOMPUTE 1
+#endif
+#ifndef M3_BWD_UNROLL_REVERSE
+#define M3_BWD_UNROLL_REVERSE 1
+#endif
+
 namespace m3 {
 namespace {
+
+constexpr int kUnrollRecompute = M3_BWD_UNROLL_RECOMPUTE;
+constexpr int kUnrollReverse = M3_BWD_UNROLL_REVERSE;
 
 constexpr int pow2ceil(int x) {
   int p = 1;
@@ -44,7 +54,6 @@ struct BwdCfg {
   static_assert(ND % 2 == 0, "the backward processes channel pairs");
   static constexpr int NL = R + T;
   static constexpr int NP = 4 * NL;
-  static constexpr int NW = NTH / 32;               // warps
   static constexpr int NG = NTH / 4;                // channel groups
   static constexpr int DT = NG * ND;                // channels per CTA
   static constexpr int NDP = ND / 2;                // channel pairs per thread
@@ -297,6 +306,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
           if (k & 1) P[k >> 1][j].y = v; else P[k >> 1][j].x = v;
         }
     }
+#pragma unroll kUnrollRecompute
     for (int tt = 0; tt < ns; ++tt) {
       tmem_store<C>(tbase + (uint32_t)(tt * CS), reinterpret_cast<const float(&)[C]>(P));
       float dl[ND], uu[ND];
@@ -335,6 +345,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     tmem_wait_st();
 
     // ---- reverse recurrence, flushing dB/dC and ddelta/du every FL steps
+#pragma unroll kUnrollReverse
     for (int tt = ns - 1; tt >= 0; --tt) {
       const int slot = (ns - 1 - tt) % FL;
       float2 Pp[NDP][NL];

@@ -73,6 +73,11 @@ __device__ __forceinline__ void stage_y(float* s_y, const FwdParams& p, int b, i
   }
 }
 
+#ifndef M3_FWD_UNROLL
+#define M3_FWD_UNROLL 1
+#endif
+constexpr int kFwdUnroll = M3_FWD_UNROLL;
+
 #ifndef M3_FWD_MIN_BLOCKS
 #define M3_FWD_MIN_BLOCKS 3
 #endif
@@ -208,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
       const float* bc = s_c + buf * kCK * NP;
       const float* by = s_y + buf * kCK * DT;
       const int ns = min(kCK, L - c * kCK);
+#pragma unroll kFwdUnroll
       for (int tt = 0; tt < ns; ++tt) {
         const int s = c * kCK + tt;
         const int t = dir ? L - 1 - s : s;

@@ -11,9 +11,12 @@ reference's fused-scan path:
 * ``m3_bidir_scan`` -- y_fwd + flip(scan(flip(x))) in one launch (mamba.py:254-260)
 * ``m3_scan_with_state`` -- the ``return_state`` scan (mamba.py:377-379)
 * ``m3_step_`` -- the in-place O(1) step recurrence (mamba.py:466-493)
+* ``m3_step_factored_`` -- the same step on the factored (h, [delta*u | B])
+  state, half the HBM traffic, bit-identical results
 
-Installing this module as ``triton_scan`` (``redpanda_b200.integration``)
-routes the unmodified reference ``mamba.py`` through these kernels.  There is
+Registering this module as ``triton_scan`` in ``sys.modules`` routes the
+unmodified reference ``mamba.py`` (with ``use_triton_scan=True``) through
+these kernels.  There is
 no CPU or PyTorch fallback: every op raises if the CUDA library is missing or a
 tensor is not on an sm_100 device.
 """
@@ -286,6 +289,42 @@ def m3_step_(h, dbu, delta_t, u_t, Bc_t, Cc_t, A_real, A_imag, track, n_rot, n_s
         _lib.check(lib.m3_step(desc, h.data_ptr(), dbu.data_ptr(), dl.data_ptr(),
                                uu.data_ptr(), bb.data_ptr(), cc.data_ptr(), ar.data_ptr(),
                                ai.data_ptr(), tk.data_ptr(), y.data_ptr(), _stream(dev)))
+    return y
+
+
+def factored_state(delta, u, Bc):
+    """Factors [delta*u | B] of the last token of a (B, L, .) sequence, (B, D + N) fp32.
+
+    Together with the scan's ``h_last`` this is the factored step state; the
+    product is the scan's own fp32 rounding of delta*u.
+    """
+    return torch.cat([delta[:, -1].float() * u[:, -1].float(), Bc[:, -1].float()], dim=-1)
+
+
+def m3_step_factored_(h, fac_prev, fac_next, delta_t, u_t, Bc_t, Cc_t, A_real, A_imag, track,
+                      n_rot, n_state):
+    """O(1) step on the factored state: h (B, D, N) in place, factors
+    fac_prev -> fac_next (B, D + N), returns y (B, D).  Equals :func:`m3_step_`
+    bit for bit with half its HBM traffic."""
+    lib = _lib.load()
+    dev = _require_cuda(h, fac_prev, fac_next, delta_t, u_t, Bc_t, Cc_t)
+    if h.dtype != torch.float32 or fac_prev.dtype != torch.float32 or \
+            fac_next.dtype != torch.float32:
+        raise TypeError("m3_step_factored_: the state must be float32")
+    if not (h.is_contiguous() and fac_prev.is_contiguous() and fac_next.is_contiguous()):
+        raise ValueError("m3_step_factored_: the state must be contiguous")
+    B, D, N = h.shape
+    dl, uu, dt_du = _prep_pair(delta_t, u_t)
+    bb, cc, dt_bc = _prep_pair(Bc_t, Cc_t)
+    Ar_p, Ai_p, Tk_p = pad_params(A_real, A_imag, track, n_rot, n_state, D, dev)
+    ar, ai, tk = (x.detach().to(torch.float32).contiguous() for x in (Ar_p, Ai_p, Tk_p))
+    y = torch.empty(B, D, device=dev, dtype=torch.float32)
+    desc = StepDesc(B, D, N, int(n_rot), dt_du, dt_bc)
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3_step_factored(desc, h.data_ptr(), fac_prev.data_ptr(),
+                                        fac_next.data_ptr(), dl.data_ptr(), uu.data_ptr(),
+                                        bb.data_ptr(), cc.data_ptr(), ar.data_ptr(),
+                                        ai.data_ptr(), tk.data_ptr(), y.data_ptr(), _stream(dev)))
     return y
 
 

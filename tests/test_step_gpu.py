@@ -99,3 +99,97 @@ def test_functional_step_does_not_mutate_input_state():
                             g["A_real"], g["A_imag"], g["track"], sh.n_rot, 16)
     assert torch.equal(h, hc) and torch.equal(d, dc)
     assert not torch.equal(h2, h)
+
+
+@pytest.mark.parametrize("sh", SHAPES, ids=lambda s: f"B{s.batch}L{s.seqlen}D{s.d_inner}N{s.d_state}")
+def test_factored_step_equals_full_step_and_scan(sh):
+    """The factored state (h, [delta*u | B]) reproduces the full-state step and
+    the scan bit for bit."""
+    g = to_cuda(make_scan_inputs(sh, seed=5))
+    k = max(1, sh.seqlen // 2)
+    pre = {key: (v[:, :k] if v is not None and v.dim() == 3 and v.shape[1] == sh.seqlen else v)
+           for key, v in g.items()}
+    y, (h, dbu) = S.m3_scan_with_state(g["delta"], g["u"], g["Bc"], g["Cc"], g["A_real"],
+                                       g["A_imag"], g["track"], sh.n_rot, sh.d_state)
+    _, (hk, dk) = S.m3_scan_with_state(pre["delta"], pre["u"], pre["Bc"], pre["Cc"],
+                                       g["A_real"], g["A_imag"], g["track"], sh.n_rot,
+                                       sh.d_state)
+    hf = hk.clone()
+    fa = S.factored_state(pre["delta"], pre["u"], pre["Bc"])
+    fb = torch.empty_like(fa)
+    hfull, dfull = hk.clone(), dk.clone()
+    for t in range(k, sh.seqlen):
+        args = (g["delta"][:, t], g["u"][:, t], g["Bc"][:, t], g["Cc"][:, t], g["A_real"],
+                g["A_imag"], g["track"], sh.n_rot, sh.d_state)
+        yf = S.m3_step_factored_(hf, fa, fb, *args)
+        ys = S.m3_step_(hfull, dfull, *args)
+        assert torch.equal(yf, ys)
+        assert torch.equal(yf, y[:, t])
+        fa, fb = fb, fa
+    assert torch.equal(hf, h) and torch.equal(hfull, h)
+    # the final factors rebuild the scan's dBu exactly
+    D = sh.d_inner
+    rebuilt = fa[:, :D, None] * fa[:, None, D:]
+    assert torch.equal(rebuilt, dbu)
+
+
+def test_factored_step_rejects_aliased_factors():
+    sh = ScanShape(2, 1, 64, 16, 4, 2)
+    g = to_cuda(make_scan_inputs(sh, seed=1))
+    h = torch.zeros(2, 64, 16, device="cuda")
+    fac = torch.zeros(2, 64 + 16, device="cuda")
+    with pytest.raises(RuntimeError, match="distinct"):
+        S.m3_step_factored_(h, fac, fac, g["delta"][:, 0], g["u"][:, 0], g["Bc"][:, 0],
+                            g["Cc"][:, 0], g["A_real"], g["A_imag"], g["track"], sh.n_rot, 16)
+
+
+@pytest.mark.parametrize("sh", SHAPES[:3], ids=lambda s: f"B{s.batch}D{s.d_inner}N{s.d_state}")
+def test_bf16_inputs_step_bit_exact_vs_scan(sh):
+    g = to_cuda(make_scan_inputs(sh, seed=13, dtype=torch.bfloat16))
+    y, (h, dbu) = S.m3_scan_with_state(g["delta"], g["u"], g["Bc"], g["Cc"], g["A_real"],
+                                       g["A_imag"], g["track"], sh.n_rot, sh.d_state)
+    ys, hs, ds = _step_all(g, sh)
+    assert torch.equal(ys, y) and torch.equal(hs, h) and torch.equal(ds, dbu)
+
+
+def _offset_copy(t, dtype=None):
+    """A copy of ``t`` whose data starts one element past a 16-byte boundary."""
+    t = t if dtype is None else t.to(dtype)
+    flat = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+    out = flat[1:].view(t.shape)
+    out.copy_(t)
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_unaligned_rows_take_the_scalar_path_with_equal_results(dtype):
+    """B/C rows and factors that are only element-aligned give the same bits."""
+    sh = ScanShape(4, 6, 256, 32, 8, 2)
+    g = to_cuda(make_scan_inputs(sh, seed=21, dtype=dtype))
+    B, D, N = sh.batch, sh.d_inner, sh.d_state
+    h0 = torch.randn(B, D, N, device="cuda") * 0.1
+    fa0 = torch.randn(B, D + N, device="cuda")
+    d0 = fa0[:, :D, None] * fa0[:, None, D:]
+    outs = []
+    for shift in (False, True):
+        h, dbu = h0.clone(), d0.clone()
+        hf, fa = h0.clone(), fa0.clone()
+        fb = torch.empty_like(fa)
+        if shift:
+            fa, fb = _offset_copy(fa), _offset_copy(fb)
+        ys = []
+        for t in range(sh.seqlen):
+            bc, cc = g["Bc"][:, t].contiguous(), g["Cc"][:, t].contiguous()
+            if shift:
+                bc, cc = _offset_copy(bc), _offset_copy(cc)
+                assert bc.data_ptr() % 16 != 0
+            args = (g["delta"][:, t], g["u"][:, t], bc, cc, g["A_real"], g["A_imag"],
+                    g["track"], sh.n_rot, N)
+            y1 = S.m3_step_(h, dbu, *args)
+            y2 = S.m3_step_factored_(hf, fa, fb, *args)
+            assert torch.equal(y1, y2)
+            ys.append(y1)
+            fa, fb = fb, fa
+        outs.append((torch.stack(ys, 1), h, dbu, hf))
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
