@@ -94,7 +94,9 @@ M3_API const char* m3_strerror(int code);
 M3_API int m3_version(void);
 
 /* Number of float32 elements of the forward checkpoint buffer the backward
- * consumes (0 when L <= 16).  Replaces the hck/dck chunk checkpoints that
+ * consumes: the state every 8 steps for the (16 rotational + 16 tracking)
+ * lane layout, every 16 steps otherwise; 0 when L fits one interval.  The
+ * buffer must be 16-byte aligned.  Replaces the hck/dck chunk checkpoints that
  * triton_scan.py:261-262 allocates. */
 M3_API size_t m3_scan_ckpt_floats(const m3_scan_desc* desc);
 
@@ -102,7 +104,7 @@ M3_API size_t m3_scan_ckpt_floats(const m3_scan_desc* desc);
  * and the return_state branch of _selective_scan_trapezoidal (mamba.py:377-379).
  *   y         required, (B, L, D) float32
  *   ckpt      optional (NULL = inference only); m3_scan_ckpt_floats() floats,
- *             to be handed to m3_scan_bwd
+ *             16-byte aligned, to be handed to m3_scan_bwd
  *   h_last,   optional, (B, D, N) float32: state after the last token of the
  *   dbu_last  scan direction (M3_DIR_FWD or M3_DIR_REV only) */
 M3_API int m3_scan_fwd(const m3_scan_desc* desc,
@@ -117,7 +119,8 @@ M3_API size_t m3_scan_bwd_workspace_bytes(const m3_scan_desc* desc);
 /* Analytic backward.  Replaces _TrapezoidalScanFn.backward
  * (triton_scan.py:283-315) with deterministic reductions (no atomics).
  *   dy        (B, L, D) of dtype_dy, the gradient of y
- *   ckpt      the forward's checkpoint buffer (NULL allowed when L <= 16)
+ *   ckpt      the forward's checkpoint buffer (NULL allowed when
+ *             m3_scan_ckpt_floats() is 0)
  *   d_delta, d_u   (B, L, D) of dtype_du
  *   d_Bc, d_Cc     (B, L, N) of dtype_bc
  *   d_A_real_p, d_A_imag_p, d_track_p   (D, N) float32 in the padded layout

@@ -2,6 +2,7 @@
 // layout and kernel dispatch.  No allocation, no exceptions, no host sync.
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "m3_common.cuh"
@@ -22,7 +23,7 @@ int* device_err_ptr() {
 bool select_tile(int n_rot, int n_track, Tile* out) {
   const int rr = (n_rot + 3) / 4, tt = (n_track + 3) / 4;
   static const Tile kTiles[] = {
-#define M3_X(r, t, nd, ndb, nthb) {r, t, nd, ndb, nthb},
+#define M3_X(r, t, nd, ndb, nthb, gs) {r, t, nd, ndb, nthb, gs},
       M3_TILE_LIST(M3_X)
 #undef M3_X
   };
@@ -78,10 +79,10 @@ int check_scan_desc(const m3_scan_desc* d, Tile* tile) {
   return M3_OK;
 }
 
-int nchunks(int L) { return (L + kCK - 1) / kCK; }
+int nchunks(int L, int len = kCK) { return (L + len - 1) / len; }
 
 size_t ckpt_floats(const m3_scan_desc* d, const Tile& t) {
-  const int nch = nchunks(d->seqlen);
+  const int nch = nchunks(d->seqlen, t.cki());
   if (nch <= 1) return 0;
   const size_t ndirs = d->direction == M3_DIR_BIDIR ? 2 : 1;
   return (size_t)d->batch * ndirs * (nch - 1) * d->d_inner * t.np();
@@ -164,7 +165,7 @@ int m3_scan_fwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   const int esd = dsize(desc->dtype_du), esb = dsize(desc->dtype_bc);
   if (!aligned(delta, esd) || !aligned(u, esd) || !aligned(Bc, esb) || !aligned(Cc, esb) ||
       !aligned(A_real_p, 4) || !aligned(A_imag_p, 4) || !aligned(track_p, 4) || !aligned(y, 4) ||
-      (ckpt && !aligned(ckpt, 4)) || (h_last && (!aligned(h_last, 4) || !aligned(dbu_last, 4))))
+      (ckpt && !aligned(ckpt, 16)) || (h_last && (!aligned(h_last, 4) || !aligned(dbu_last, 4))))
     return M3_ERR_ALIGN;
   if ((rc = check_device()) != M3_OK) return rc;
 
@@ -179,6 +180,8 @@ int m3_scan_fwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   p.dt_du = desc->dtype_du; p.dt_bc = desc->dtype_bc;
   p.direction = desc->direction;
   p.nch = nchunks(desc->seqlen);
+  p.cki = t.cki();
+  p.nck = nchunks(desc->seqlen, p.cki) - 1;
   p.async_ok = aligned(delta, 4) && aligned(u, 4) &&
                (desc->dtype_du == M3_F32 || (desc->d_inner % 2) == 0);
   p.err = device_err_ptr();
@@ -214,7 +217,7 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
       !aligned(Bc, esb) || !aligned(Cc, esb) || !aligned(d_Bc, esb) || !aligned(d_Cc, esb) ||
       !aligned(dy, esy) || !aligned(A_real_p, 4) || !aligned(A_imag_p, 4) ||
       !aligned(track_p, 4) || !aligned(d_A_real_p, 4) || !aligned(d_A_imag_p, 4) ||
-      !aligned(d_track_p, 4) || (ckpt && !aligned(ckpt, 4)) || !aligned(workspace, 256))
+      !aligned(d_track_p, 4) || (ckpt && !aligned(ckpt, 16)) || !aligned(workspace, 256))
     return M3_ERR_ALIGN;
   if ((rc = check_device()) != M3_OK) return rc;
   BwdLayout lay;
@@ -236,7 +239,7 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   p.NR = desc->n_rot; p.NT = desc->d_state - desc->n_rot;
   p.dt_du = desc->dtype_du; p.dt_bc = desc->dtype_bc; p.dt_dy = dtype_dy;
   p.direction = desc->direction;
-  p.nch = nchunks(desc->seqlen);
+  p.nch = nchunks(desc->seqlen, t.cki());
   p.G = lay.G; p.Bg = lay.Bg;
   p.async_du = aligned(delta, 4) && aligned(u, 4) &&
                (desc->dtype_du == M3_F32 || (desc->d_inner % 2) == 0);
@@ -298,6 +301,13 @@ static int step_common(const m3_step_desc* desc, float* h, float* dbu, const flo
   p.vec_bc = aligned(Bc, 16) && aligned(Cc, 16);
   p.vec_fac = factored && aligned(fac_prev, 16) && aligned(fac_next, 16) &&
               (desc->d_inner % 4) == 0;
+  // Pipelined kernel: dense lane tile (no virtual lanes), whole 32-channel tiles,
+  // and every staged row a 16-byte multiple at a 16-byte aligned address.
+  p.bulk = desc->n_rot == 4 * t.R && desc->d_state - desc->n_rot == 4 * t.T &&
+           (desc->d_inner % 32) == 0 && ((desc->d_state * esb) % 16) == 0 &&
+           aligned(delta, 16) && aligned(u, 16) && aligned(Bc, 16) && aligned(Cc, 16) &&
+           (!factored || (aligned(fac_prev, 16) && aligned(fac_next, 16))) &&
+           getenv("M3_STEP_NO_BULK") == nullptr;
   p.err = device_err_ptr();
   cudaError_t e = launch_step(t, p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;

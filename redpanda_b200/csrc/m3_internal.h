@@ -12,6 +12,8 @@ namespace m3 {
 struct Tile {
   int R, T, ND;      // ND: channels per thread in the forward and step kernels
   int NDB, NTHB;     // backward: channels per thread, threads per CTA
+  int GS;            // backward keeps the gates in Tensor Memory (8-step chunks)
+  int cki() const { return GS ? 8 : 16; }      // checkpoint interval = backward chunk
   int nl() const { return R + T; }
   int np() const { return 4 * (R + T); }       // padded state lanes per channel
   int dt() const { return 32 * ND; }           // forward channels per CTA
@@ -30,6 +32,7 @@ struct FwdParams {
   int dt_du, dt_bc;
   int direction;   // 0 fwd, 1 rev, 2 bidir
   int nch;         // chunks of kCK steps
+  int cki, nck;    // checkpoint interval (8 or 16 steps) and checkpoints per direction
   int async_ok;    // cp.async staging allowed (alignment checked on the host)
   int* err;
 };
@@ -45,7 +48,7 @@ struct BwdParams {
   int B, L, D, N, NR, NT;
   int dt_du, dt_bc, dt_dy;
   int direction;
-  int nch;
+  int nch;            // chunks of the tile's checkpoint interval
   int G, Bg;
   int async_du, async_dy;   // cp.async staging allowed for delta/u and dy
   int* err;
@@ -57,6 +60,7 @@ struct StepParams {
   int factored;
   int vec_bc;                                 // Bc/Cc 16-byte aligned: vector row loads
   int vec_fac;                                // factors 16-byte aligned, D % 4 == 0
+  int bulk;                                   // pipelined bulk-copy kernel eligible
   const void* delta; const void* u; const void* Bc; const void* Cc;
   const float* Ar; const float* Ai; const float* Tk;
   float* y;

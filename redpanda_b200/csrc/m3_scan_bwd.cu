@@ -13,7 +13,7 @@
 //   dB[t,n]  = sum_d ddBu*delta*u,   dC[t,n] = sum_d dy*h[t]
 //
 // Work split: CTA (batch group bg, channel tile g) walks its rows b = bg,
-// bg + Bg, ... and, per row and direction, the kCK-step chunks from last to
+// bg + Bg, ... and, per row and direction, the KC-step chunks from last to
 // first.  Each chunk restarts from the forward's checkpoint of P, recomputes
 // the chunk forward storing P[t-1] of every cell in Tensor Memory, then runs
 // the reverse recurrence reading P back.  dA_real/dA_imag/dtrack accumulate in
@@ -49,20 +49,25 @@ constexpr int pow2ceil(int x) {
 }
 
 // Backward tiling: NDP channel pairs per thread (packed FP32), NTH threads.
-template <int R, int T, int ND, int NTH>
+// GS: the recompute pass also keeps each step's rotational gates (exp*cos and
+// exp*sin) in Tensor Memory, so the reverse pass evaluates no transcendental;
+// the chunk is then KC = 8 steps so that state and gates fit.
+template <int R, int T, int ND, int NTH, bool GS>
 struct BwdCfg {
   static_assert(ND % 2 == 0, "the backward processes channel pairs");
+  static constexpr int KC = GS ? 8 : kCK;           // chunk length (= checkpoint interval)
   static constexpr int NL = R + T;
   static constexpr int NP = 4 * NL;
   static constexpr int NG = NTH / 4;                // channel groups
   static constexpr int DT = NG * ND;                // channels per CTA
   static constexpr int NDP = ND / 2;                // channel pairs per thread
   static constexpr int C = ND * NL;                 // cells per thread
-  static constexpr int CS = pow2ceil(C);            // TMEM columns per timestep
-  static constexpr int WG_COLS = kCK * CS;          // TMEM columns per warpgroup
+  static constexpr int CG = GS ? ND * R * 2 : 0;    // gate values per thread and step
+  static constexpr int CS = pow2ceil(C + CG);       // TMEM columns per timestep
+  static constexpr int WG_COLS = KC * CS;           // TMEM columns per warpgroup
   static constexpr int NCOLS = (NTH / 128) * WG_COLS < 32 ? 32 : (NTH / 128) * WG_COLS;
   static constexpr int FL = 4;                      // steps per dB/dC/ddelta flush
-  static constexpr size_t raw_bytes = (size_t)kCK * DT * 4;   // one staged (kCK x DT) tile
+  static constexpr size_t raw_bytes = (size_t)KC * DT * 4;    // one staged (KC x DT) tile
   // Reduction staging rows hold one value per thread (group-major, quarter-minor),
   // so per-step stores are bank-conflict free; the row pitches are padded so
   // the float4 reads of the flush hit distinct banks.
@@ -73,20 +78,20 @@ struct BwdCfg {
   static constexpr size_t smem_bytes =
       3 * 2 * raw_bytes                       // delta, u, dy (HBM dtype), double-buffered
       + 2 * (size_t)DT * NP * 4               // checkpoint tile, double-buffered
-      + 2 * 2 * (size_t)kCK * NP * 4          // B, C (fp32), double-buffered
+      + 2 * 2 * (size_t)KC * NP * 4           // B, C (fp32), double-buffered
       + red_floats * 4 + gs_floats * 4
       + 16;                                   // TMEM address slot
 };
 
-// Stage a (kCK x DT) tile of a (B, L, D) tensor for processing steps
-// [s0, s0 + kCK) in its HBM dtype; rows past L and channels past D read zero.
-template <int DT, int NTH>
+// Stage a (KC x DT) tile of a (B, L, D) tensor for processing steps
+// [s0, s0 + KC) in its HBM dtype; rows past L and channels past D read zero.
+template <int DT, int NTH, int KC>
 __device__ __forceinline__ void stage_tile(unsigned char* dst, const void* src, int esz,
                                            bool async_ok, int b, int d0, int s0, int dir,
                                            int L, int D) {
   if (async_ok) {
     const int epw = 4 / esz, wpr = DT / epw;
-    for (int i = threadIdx.x; i < kCK * wpr; i += NTH) {
+    for (int i = threadIdx.x; i < KC * wpr; i += NTH) {
       const int tt = i / wpr, w = i - tt * wpr;
       const int s = s0 + tt, d = d0 + w * epw;
       const bool ok = (s < L) && (d < D);
@@ -95,7 +100,7 @@ __device__ __forceinline__ void stage_tile(unsigned char* dst, const void* src, 
       cp_async4(dst + (size_t)i * 4, (const char*)src + gi * esz, ok);
     }
   } else {
-    for (int i = threadIdx.x; i < kCK * DT; i += NTH) {
+    for (int i = threadIdx.x; i < KC * DT; i += NTH) {
       const int tt = i / DT, dd = i - tt * DT;
       const int s = s0 + tt, d = d0 + dd;
       const bool ok = (s < L) && (d < D);
@@ -107,21 +112,22 @@ __device__ __forceinline__ void stage_tile(unsigned char* dst, const void* src, 
   }
 }
 
-// One element of a staged (kCK x DT) tile, converted to fp32.
+// One element of a staged (KC x DT) tile, converted to fp32.
 __device__ __forceinline__ float tile_at(const unsigned char* base, bool bf16, int idx) {
   if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
   return reinterpret_cast<const float*>(base)[idx];
 }
 
-template <int R, int T, int ND, int NTH>
+template <int R, int T, int ND, int NTH, bool GS>
 __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
   using LM = LaneMap<R, T>;
-  using CF = BwdCfg<R, T, ND, NTH>;
-  constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS;
+  using CF = BwdCfg<R, T, ND, NTH, GS>;
+  constexpr int KC = CF::KC;
+  constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS, CG = CF::CG;
   constexpr int NG = CF::NG, NDP = CF::NDP, FL = CF::FL, SR = CF::SR, SG = CF::SG;
   constexpr int RR = R > 0 ? R : 1;
   constexpr int TT = T > 0 ? T : 1;
-  constexpr int BCE = (kCK * NP + NTH - 1) / NTH;
+  constexpr int BCE = (KC * NP + NTH - 1) / NTH;
   static_assert(CF::NCOLS <= 512, "TMEM holds at most 512 columns");
 
   extern __shared__ __align__(16) unsigned char smem[];
@@ -129,9 +135,9 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
   unsigned char* s_u = s_dl + 2 * CF::raw_bytes;                     // [2][raw]
   unsigned char* s_dy = s_u + 2 * CF::raw_bytes;                     // [2][raw]
   float* s_ck = reinterpret_cast<float*>(s_dy + 2 * CF::raw_bytes);  // [2][DT][NP]
-  float* s_b = s_ck + 2 * DT * NP;                                   // [2][kCK][NP]
-  float* s_c = s_b + 2 * kCK * NP;                                   // [2][kCK][NP]
-  float* s_red = s_c + 2 * kCK * NP;                                 // [FL][2][NL][SR]
+  float* s_b = s_ck + 2 * DT * NP;                                   // [2][KC][NP]
+  float* s_c = s_b + 2 * KC * NP;                                    // [2][KC][NP]
+  float* s_red = s_c + 2 * KC * NP;                                  // [FL][2][NL][SR]
   float* s_gs = s_red + CF::red_floats;                              // [FL][ND][2][SG]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_gs + CF::gs_floats);
 
@@ -214,7 +220,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
       const int tt = i / NP, ln = i - tt * NP;
       const int s = s0 + tt;
       const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
-      const bool ok = (i < kCK * NP) && (s < L) && (n >= 0);
+      const bool ok = (i < KC * NP) && (s < L) && (n >= 0);
       const int t = dir ? L - 1 - s : s;
       const size_t gi = ok ? ((size_t)b * L + t) * N + n : 0;
       rb[e] = ok ? ld_f(p.Bc, gi, p.dt_bc) : 0.f;
@@ -225,19 +231,19 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
 #pragma unroll
     for (int e = 0; e < BCE; ++e) {
       const int i = tid + e * NTH;
-      if (i < kCK * NP) {
-        s_b[buf * kCK * NP + i] = rb[e];
-        s_c[buf * kCK * NP + i] = rc[e];
+      if (i < KC * NP) {
+        s_b[buf * KC * NP + i] = rb[e];
+        s_c[buf * KC * NP + i] = rc[e];
       }
     }
   };
   auto stage = [&](int i, int buf) {
     int b, pass, c;
     item(i, b, pass, c);
-    const int dir = dir_of(pass), s0 = c * kCK;
-    stage_tile<DT, NTH>(s_dl + buf * CF::raw_bytes, p.delta, es_du, async_du, b, d0, s0, dir, L, D);
-    stage_tile<DT, NTH>(s_u + buf * CF::raw_bytes, p.u, es_du, async_du, b, d0, s0, dir, L, D);
-    stage_tile<DT, NTH>(s_dy + buf * CF::raw_bytes, p.dy, es_dy, async_dy, b, d0, s0, dir, L, D);
+    const int dir = dir_of(pass), s0 = c * KC;
+    stage_tile<DT, NTH, KC>(s_dl + buf * CF::raw_bytes, p.delta, es_du, async_du, b, d0, s0, dir, L, D);
+    stage_tile<DT, NTH, KC>(s_u + buf * CF::raw_bytes, p.u, es_du, async_du, b, d0, s0, dir, L, D);
+    stage_tile<DT, NTH, KC>(s_dy + buf * CF::raw_bytes, p.dy, es_dy, async_dy, b, d0, s0, dir, L, D);
     if (c > 0) {
       const int dslot = bidir ? dir : 0;
       const float* src = p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
@@ -255,7 +261,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     cp_async_commit();
     int b, pass, c;
     item(0, b, pass, c);
-    load_bc(b, dir_of(pass), c * kCK);
+    load_bc(b, dir_of(pass), c * KC);
     store_bc(0);
   }
   for (int it = 0; it < nitems; ++it) {
@@ -265,15 +271,15 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     const int dir = dir_of(pass);
     const bool first_of_two = bidir && pass == 0;
     const bool second_of_two = bidir && pass == 1;
-    const int s0 = c * kCK;
-    const int ns = min(kCK, L - s0);
+    const int s0 = c * KC;
+    const int ns = min(KC, L - s0);
     const bool more = it + 1 < nitems;
     if (more) stage(it + 1, buf ^ 1);
     cp_async_commit();
     if (more) {
       int b2, pass2, c2;
       item(it + 1, b2, pass2, c2);
-      load_bc(b2, dir_of(pass2), c2 * kCK);
+      load_bc(b2, dir_of(pass2), c2 * KC);
     }
     cp_async_wait1();
     __syncthreads();
@@ -291,8 +297,8 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     const unsigned char* bdl = s_dl + buf * CF::raw_bytes;
     const unsigned char* bu = s_u + buf * CF::raw_bytes;
     const unsigned char* bdy = s_dy + buf * CF::raw_bytes;
-    const float* bb = s_b + buf * kCK * NP;
-    const float* bc = s_c + buf * kCK * NP;
+    const float* bb = s_b + buf * KC * NP;
+    const float* bc = s_c + buf * KC * NP;
 
     // ---- forward recompute of the chunk; P[t-1] of every cell -> TMEM
     float2 P[NDP][NL];
@@ -318,6 +324,8 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
       for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
       // The fast/exact choice is made once per step (not per cell) so that the
       // compiler emits two branch-free bodies instead of predicating both.
+      // GS: gates of this step, [channel pair][lane][exp*cos, exp*sin]
+      float2 GG[NDP][RR][2];
       auto recompute = [&](auto fast_tag) {
         constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
@@ -327,7 +335,19 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
 #pragma unroll
           for (int j = 0; j < R; ++j) {
             float2 g;
-            if constexpr (FAST) {
+            if constexpr (GS) {
+              const float2 e = gate_exp2(dl2, A2[kp][j]);
+              float2 sn, cs;
+              if constexpr (FAST) {
+                gate_sincos2_nocheck(dl2, AI[kp][j], sn, cs);
+              } else {
+                gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
+                gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
+              }
+              g = __fmul2_rn(e, cs);
+              GG[kp][j][0] = g;
+              GG[kp][j][1] = __fmul2_rn(e, sn);
+            } else if constexpr (FAST) {
               g = __fmul2_rn(gate_exp2(dl2, A2[kp][j]), gate_cos2_nocheck(dl2, AI[kp][j]));
             } else {
               g = make_float2(rot_gate(dl2.x, A2[kp][j].x, AI[kp][j].x),
@@ -341,6 +361,8 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
       };
       if (__fmul_rn(mdl, maxai) <= kFastArgBound) recompute(std::true_type{});
       else recompute(std::false_type{});
+      if constexpr (GS)
+        tmem_store<CG>(tbase + (uint32_t)(tt * CS + C), reinterpret_cast<const float(&)[CG]>(GG));
     }
     tmem_wait_st();
 
@@ -349,7 +371,10 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     for (int tt = ns - 1; tt >= 0; --tt) {
       const int slot = (ns - 1 - tt) % FL;
       float2 Pp[NDP][NL];
+      float2 GG[NDP][RR][2];
       tmem_load<C>(tbase + (uint32_t)(tt * CS), reinterpret_cast<float(&)[C]>(Pp));
+      if constexpr (GS)
+        tmem_load<CG>(tbase + (uint32_t)(tt * CS + C), reinterpret_cast<float(&)[CG]>(GG));
       float dl[ND], uu[ND], dyv[ND];
       read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
       read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
@@ -376,16 +401,22 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
 #pragma unroll
         for (int j = 0; j < R; ++j) {
           const float2 pp = Pp[kp][j];
-          const float2 e = gate_exp2(dl2, A2[kp][j]);
-          float2 sn, cs;
-          if constexpr (FAST) {
-            gate_sincos2_nocheck(dl2, AI[kp][j], sn, cs);
+          float2 g, es;
+          if constexpr (GS) {
+            g = GG[kp][j][0];
+            es = GG[kp][j][1];
           } else {
-            gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
-            gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
+            const float2 e = gate_exp2(dl2, A2[kp][j]);
+            float2 sn, cs;
+            if constexpr (FAST) {
+              gate_sincos2_nocheck(dl2, AI[kp][j], sn, cs);
+            } else {
+              gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
+              gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
+            }
+            g = __fmul2_rn(e, cs);
+            es = __fmul2_rn(e, sn);
           }
-          const float2 g = __fmul2_rn(e, cs);
-          const float2 es = __fmul2_rn(e, sn);
           const float2 dbu = __fmul2_rn(du2, f2(Bv[j]));
           const float2 H = __ffma2_rn(g, pp, dbu);
           const float2 dyC = __fmul2_rn(dy2, f2(Cv[j]));
@@ -428,7 +459,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
         gsrow[(2 * (2 * kp + 1) + 1) * SG] = sB.y;
       }
       };
-      if (__fmul_rn(mdl, maxai) <= kFastArgBound) reverse_cells(std::true_type{});
+      if (GS || __fmul_rn(mdl, maxai) <= kFastArgBound) reverse_cells(std::true_type{});
       else reverse_cells(std::false_type{});
       // dB/dC partial of this thread's channels
       {
@@ -605,10 +636,10 @@ __global__ void reduce_a_kernel(const ReduceParams p, int R, int T) {
   }
 }
 
-template <int R, int T, int ND, int NTH>
+template <int R, int T, int ND, int NTH, bool GS>
 cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
-  using CF = BwdCfg<R, T, ND, NTH>;
-  auto kern = scan_bwd_kernel<R, T, ND, NTH>;
+  using CF = BwdCfg<R, T, ND, NTH, GS>;
+  auto kern = scan_bwd_kernel<R, T, ND, NTH, GS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)CF::smem_bytes);
   if (e != cudaSuccess) return e;
@@ -620,9 +651,10 @@ cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s) {
-#define M3_X(r, tt, nd, ndb, nthb) \
-  if constexpr (ndb > 0)                                                    \
-    if (t.R == r && t.T == tt && t.ND == nd) return launch_bwd_impl<r, tt, ndb, nthb>(p, s);
+#define M3_X(r, tt, nd, ndb, nthb, gs)                                              \
+  if constexpr (ndb > 0)                                                            \
+    if (t.R == r && t.T == tt && t.ND == nd)                                        \
+      return launch_bwd_impl<r, tt, ndb, nthb, (gs != 0)>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;

@@ -193,20 +193,6 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
       cp_async_wait1();
       __syncthreads();
 
-      // checkpoint of P = 2h + dBu before the first step of this chunk
-      if (c > 0 && p.ckpt != nullptr) {
-#pragma unroll
-        for (int k = 0; k < ND; ++k) {
-          const int d = dbase + k;
-          if (d < D) {
-            float* dst = p.ckpt +
-                ((((size_t)b * ndirs + dslot) * (p.nch - 1) + (c - 1)) * D + d) * NP + q * NL;
-#pragma unroll
-            for (int j = 0; j < NL; ++j) dst[j] = (k & 1) ? P[k >> 1][j].y : P[k >> 1][j].x;
-          }
-        }
-      }
-
       const unsigned char* bdl = s_dl + buf * kCK * DT * 4;
       const unsigned char* bu = s_u + buf * kCK * DT * 4;
       const float* bb = s_b + buf * kCK * NP;
@@ -217,6 +203,30 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
       for (int tt = 0; tt < ns; ++tt) {
         const int s = c * kCK + tt;
         const int t = dir ? L - 1 - s : s;
+        // checkpoint of P = 2h + dBu before every p.cki-th processing step
+        // (the start of each backward chunk)
+        if (p.ckpt != nullptr && s > 0 && (s & (p.cki - 1)) == 0) {
+#pragma unroll
+          for (int k = 0; k < ND; ++k) {
+            const int d = dbase + k;
+            if (d < D) {
+              float* dst = p.ckpt +
+                  ((((size_t)b * ndirs + dslot) * p.nck + (s / p.cki - 1)) * D + d) * NP + q * NL;
+              if constexpr (NL % 4 == 0) {   // 16-byte aligned: NP*4 and NL*4 are multiples of 16
+#pragma unroll
+                for (int j = 0; j < NL; j += 4)
+                  *reinterpret_cast<float4*>(dst + j) =
+                      (k & 1) ? make_float4(P[k >> 1][j].y, P[k >> 1][j + 1].y,
+                                            P[k >> 1][j + 2].y, P[k >> 1][j + 3].y)
+                              : make_float4(P[k >> 1][j].x, P[k >> 1][j + 1].x,
+                                            P[k >> 1][j + 2].x, P[k >> 1][j + 3].x);
+              } else {
+#pragma unroll
+                for (int j = 0; j < NL; ++j) dst[j] = (k & 1) ? P[k >> 1][j].y : P[k >> 1][j].x;
+              }
+            }
+          }
+        }
         float dl[ND], uu[ND];
         read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * esz, bf16, dl);
         read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * esz, bf16, uu);
@@ -324,7 +334,7 @@ cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
-#define M3_X(r, tt, nd, ndb, nthb) \
+#define M3_X(r, tt, nd, ndb, nthb, gs) \
   if (t.R == r && t.T == tt && t.ND == nd) return launch_fwd_impl<r, tt, nd>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X

@@ -23,6 +23,7 @@
 //    overwritten while the step runs).
 #include "m3_common.cuh"
 #include "m3_internal.h"
+#include "m3_bulk.cuh"
 #include "m3_stage.cuh"
 #include "m3_tiles.h"
 
@@ -285,6 +286,278 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pipelined fast path for dense lane tiles (N == 4*(R+T), no virtual lanes),
+// D % 32 == 0 and 16-byte aligned rows.  A CTA owns one 32-channel tile for
+// the whole launch (eigenvalues loaded once) and a contiguous range of row
+// pairs.  Thread 0 streams each row pair's state tile (32 x N fp32 of h and of
+// dBu, or of h plus the [delta*u | B] factors) and its inputs into shared
+// memory with bulk asynchronous copies, kBulkStages pairs ahead of the
+// compute; completion is tracked per stage on an mbarrier.  The two rows of a
+// pair are computed as the two lanes of packed FP32 instructions, with the
+// rounding of the scalar cell functions, so outputs equal step_kernel's bit
+// for bit.  New state goes straight from registers to global memory.
+constexpr int kBulkRows = 2;   // rows per stage, one per packed lane
+// Stages in flight: the factored state moves half the bytes per row, so it
+// keeps more rows in flight to cover the same memory latency.
+constexpr int bulk_stages(bool fact) { return fact ? 5 : 3; }
+
+template <int NP, bool FACT>
+struct BulkStage {
+  static constexpr int kH = 32 * NP * 4;                        // h tile of one row
+  static constexpr int kS2 = FACT ? 32 * 4 + NP * 4 : kH;       // dBu tile, or [du | B]
+  static constexpr int kDL = 32 * 4;                            // delta or u (<= fp32)
+  static constexpr int kBC = NP * 4;                            // Bc or Cc (<= fp32)
+  static constexpr int oH = 0, oS2 = kH, oDL = kH + kS2, oU = oDL + kDL, oB = oU + kDL,
+                       oC = oB + kBC;
+  static constexpr int kRow = oC + kBC;
+  static constexpr int kBytes = kBulkRows * kRow;
+  static_assert(kS2 % 16 == 0 && kBC % 16 == 0, "bulk copy destinations are 16-byte aligned");
+};
+
+// n fp32 (dt == M3_F32) or bf16 values of a staged row, widened to fp32.
+template <int n>
+__device__ __forceinline__ void ld_staged(const unsigned char* base, int off, bool bf16, float* v) {
+  if (bf16) ld_vec_bf16<n>(reinterpret_cast<const __nv_bfloat16*>(base) + off, v);
+  else ld_vec<n, vec_width(n)>(reinterpret_cast<const float*>(base) + off, v);
+}
+
+template <int R, int T, bool FACT>
+__global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_bulk_kernel(const StepParams p,
+                                                                int pairs_per_cta) {
+  using LM = LaneMap<R, T>;
+  constexpr int NL = R + T;
+  constexpr int NP = LM::NP;
+  constexpr int RR = R > 0 ? R : 1;
+  constexpr int TT = T > 0 ? T : 1;
+  constexpr int VR = vec_width(RR), VT = vec_width(TT);
+  using SL = BulkStage<NP, FACT>;
+  constexpr int kBulkStages = bulk_stages(FACT);
+  extern __shared__ __align__(128) unsigned char smem[];
+  // stage buffers, then one mbarrier per stage
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBulkStages * SL::kBytes);
+
+  const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
+  const int D = p.D;
+  const int d0 = blockIdx.y * 32, d = d0 + grp;
+  const int npairs = (p.B + 1) / 2;
+  const int pair0 = blockIdx.x * pairs_per_cta;
+  const int n = min(pairs_per_cta, npairs - pair0);
+  const bool bf_du = p.dt_du == M3_BF16, bf_bc = p.dt_bc == M3_BF16;
+  const int esd = bf_du ? 2 : 4, esb = bf_bc ? 2 : 4;
+
+  float a2[RR], ai[RR], tk[TT];
+  float maxai = 0.f;
+#pragma unroll
+  for (int j = 0; j < NL; ++j) {
+    const int m = LM::mem_lane(q, j, p.NR, p.NT);   // dense tile: never virtual
+    const size_t gp = (size_t)d * NP + m;
+    if (j < R) {
+      a2[j] = exp_const(p.Ar[gp]);
+      ai[j] = p.Ai[gp];
+      maxai = fmaxf(maxai, fabsf(ai[j]));
+    } else {
+      tk[j - R] = p.Tk[gp];
+    }
+  }
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kBulkStages; ++s) mbar_init(&full[s], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  const uint32_t row_tx = SL::kH + (FACT ? 32 * 4 + NP * 4 : SL::kH) + 2 * 32 * esd +
+                          2 * NP * esb;
+  auto issue = [&](int i) {   // thread 0: stage the row pair pair0 + i
+    const int s = i % kBulkStages;
+    unsigned char* st = smem + s * SL::kBytes;
+    const int b0 = 2 * (pair0 + i);
+    const int nr = min(2, p.B - b0);
+    mbar_arrive_expect_tx(&full[s], nr * row_tx);
+    for (int r = 0; r < nr; ++r) {
+      const size_t b = (size_t)(b0 + r);
+      unsigned char* rs = st + r * SL::kRow;
+      bulk_g2s(rs + SL::oH, p.h + (b * D + d0) * NP, SL::kH, &full[s]);
+      if constexpr (FACT) {
+        const float* fac = p.fac_in + b * (D + NP);
+        bulk_g2s(rs + SL::oS2, fac + d0, 32 * 4, &full[s]);
+        bulk_g2s(rs + SL::oS2 + 32 * 4, fac + D, NP * 4, &full[s]);
+      } else {
+        bulk_g2s(rs + SL::oS2, p.dbu + (b * D + d0) * NP, SL::kH, &full[s]);
+      }
+      bulk_g2s(rs + SL::oDL, (const char*)p.delta + (b * D + d0) * esd, 32 * esd, &full[s]);
+      bulk_g2s(rs + SL::oU, (const char*)p.u + (b * D + d0) * esd, 32 * esd, &full[s]);
+      bulk_g2s(rs + SL::oB, (const char*)p.Bc + b * NP * esb, NP * esb, &full[s]);
+      bulk_g2s(rs + SL::oC, (const char*)p.Cc + b * NP * esb, NP * esb, &full[s]);
+    }
+  };
+
+  if (tid == 0) {
+    for (int i = 0; i < min(kBulkStages, n); ++i) issue(i);
+  }
+
+  int fail_at = -1;
+  for (int i = 0; i < n; ++i) {
+    const int s = i % kBulkStages;
+    const bool ok = mbar_wait(&full[s], (uint32_t)((i / kBulkStages) & 1));
+    const int b0 = 2 * (pair0 + i);
+    const bool two = b0 + 1 < p.B;
+
+    // ---- staged row pair -> registers (row 0 in .x, row 1 in .y)
+    float2 h2[NL], db2[NL], B2[NL], C2[NL], dl2, uu2;
+    {
+      float hv[2][NL], dv[2][NL], bv[2][NL], cv[2][NL], dlv[2], uv[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const unsigned char* rs = smem + s * SL::kBytes + r * SL::kRow;
+        if (r == 1 && !two) {
+#pragma unroll
+          for (int j = 0; j < NL; ++j) { hv[r][j] = 0.f; dv[r][j] = 0.f; bv[r][j] = 0.f; cv[r][j] = 0.f; }
+          dlv[r] = 0.f; uv[r] = 0.f;
+          continue;
+        }
+        const float* hs = reinterpret_cast<const float*>(rs + SL::oH) + grp * NP;
+        if constexpr (R > 0) ld_vec<R, VR>(hs + q * R, hv[r]);
+        if constexpr (T > 0) ld_vec<T, VT>(hs + 4 * R + q * T, hv[r] + R);
+        if constexpr (FACT) {
+          const float dup = reinterpret_cast<const float*>(rs + SL::oS2)[grp];
+          const float* bp = reinterpret_cast<const float*>(rs + SL::oS2 + 32 * 4);
+          float bf[NL];
+          if constexpr (R > 0) ld_vec<R, VR>(bp + q * R, bf);
+          if constexpr (T > 0) ld_vec<T, VT>(bp + 4 * R + q * T, bf + R);
+#pragma unroll
+          for (int j = 0; j < NL; ++j) dv[r][j] = __fmul_rn(dup, bf[j]);
+        } else {
+          const float* ds = reinterpret_cast<const float*>(rs + SL::oS2) + grp * NP;
+          if constexpr (R > 0) ld_vec<R, VR>(ds + q * R, dv[r]);
+          if constexpr (T > 0) ld_vec<T, VT>(ds + 4 * R + q * T, dv[r] + R);
+        }
+        dlv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(rs + SL::oDL)[grp])
+                       : reinterpret_cast<const float*>(rs + SL::oDL)[grp];
+        uv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(rs + SL::oU)[grp])
+                      : reinterpret_cast<const float*>(rs + SL::oU)[grp];
+        if constexpr (R > 0) {
+          ld_staged<R>(rs + SL::oB, q * R, bf_bc, bv[r]);
+          ld_staged<R>(rs + SL::oC, q * R, bf_bc, cv[r]);
+        }
+        if constexpr (T > 0) {
+          ld_staged<T>(rs + SL::oB, 4 * R + q * T, bf_bc, bv[r] + R);
+          ld_staged<T>(rs + SL::oC, 4 * R + q * T, bf_bc, cv[r] + R);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NL; ++j) {
+        h2[j] = make_float2(hv[0][j], hv[1][j]);
+        db2[j] = make_float2(dv[0][j], dv[1][j]);
+        B2[j] = make_float2(bv[0][j], bv[1][j]);
+        C2[j] = make_float2(cv[0][j], cv[1][j]);
+      }
+      dl2 = make_float2(dlv[0], dlv[1]);
+      uu2 = make_float2(uv[0], uv[1]);
+    }
+    // every thread has read stage s: it may be refilled (or the launch gives up)
+    if (__syncthreads_or(!ok)) { fail_at = i; break; }
+    if (tid == 0 && i + kBulkStages < n) issue(i + kBulkStages);
+
+    // ---- recurrence (the cell arithmetic of m3_common.cuh, two rows per instruction)
+    const float2 du2 = __fmul2_rn(dl2, uu2);
+    float2 H2[NL], ds2[NL];
+    const bool fast = __fmul_rn(fmaxf(fabsf(dl2.x), fabsf(dl2.y)), maxai) <= kFastArgBound;
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const float2 P = __fadd2_rn(__fmul2_rn(f2(2.f), h2[j]), db2[j]);
+      float2 g;
+      if (j < R) {
+        if (fast) {
+          g = __fmul2_rn(gate_exp2(dl2, f2(a2[j % RR])), gate_cos2_nocheck(dl2, f2(ai[j % RR])));
+        } else {
+          g = make_float2(rot_gate(dl2.x, a2[j % RR], ai[j % RR]),
+                          rot_gate(dl2.y, a2[j % RR], ai[j % RR]));
+        }
+      } else {
+        g = f2(tk[(j - R) % TT]);
+      }
+      ds2[j] = __fmul2_rn(du2, B2[j]);
+      H2[j] = __ffma2_rn(g, P, ds2[j]);
+    }
+    float2 acc = f2(0.f);
+#pragma unroll
+    for (int j = 0; j < NL; ++j) acc = __ffma2_rn(H2[j], C2[j], acc);
+    const float y0 = __fmul_rn(0.5f, quad_sum(acc.x));
+    const float y1 = __fmul_rn(0.5f, quad_sum(acc.y));
+
+    // ---- new state, factors and y
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if (r == 1 && !two) break;
+      const size_t b = (size_t)(b0 + r);
+      float hs[NL], dsv[NL];
+#pragma unroll
+      for (int j = 0; j < NL; ++j) {
+        const float2 hh = __fmul2_rn(f2(0.5f), H2[j]);
+        hs[j] = r ? hh.y : hh.x;
+        dsv[j] = r ? ds2[j].y : ds2[j].x;
+      }
+      float* ho = p.h + (b * D + d) * NP;
+      if constexpr (R > 0) st_vec<R, VR>(ho + q * R, hs);
+      if constexpr (T > 0) st_vec<T, VT>(ho + 4 * R + q * T, hs + R);
+      if constexpr (FACT) {
+        float* fac = p.fac_out + b * (D + NP);
+        if (q == 0) fac[d] = r ? du2.y : du2.x;
+        if (blockIdx.y == 0 && grp == 0) {
+          float bvv[NL];
+#pragma unroll
+          for (int j = 0; j < NL; ++j) bvv[j] = r ? B2[j].y : B2[j].x;
+          if constexpr (R > 0) st_vec<R, VR>(fac + D + q * R, bvv);
+          if constexpr (T > 0) st_vec<T, VT>(fac + D + 4 * R + q * T, bvv + R);
+        }
+      } else {
+        float* dout = p.dbu + (b * D + d) * NP;
+        if constexpr (R > 0) st_vec<R, VR>(dout + q * R, dsv);
+        if constexpr (T > 0) st_vec<T, VT>(dout + 4 * R + q * T, dsv + R);
+      }
+      if (q == 0) p.y[b * D + d] = r ? y1 : y0;
+    }
+  }
+
+  if (fail_at >= 0 && tid == 0) {
+    set_err(p.err, M3_ERR_DEVICE);
+    // let the copies still in flight land before the CTA's shared memory goes away
+    for (int i = fail_at; i < min(fail_at + kBulkStages, n); ++i)
+      mbar_wait(&full[i % kBulkStages], (uint32_t)((i / kBulkStages) & 1));
+  }
+}
+
+template <int R, int T, bool FACT>
+cudaError_t launch_step_bulk_impl(const StepParams& p, cudaStream_t stream) {
+  using SL = BulkStage<4 * (R + T), FACT>;
+  constexpr int kBulkStages = bulk_stages(FACT);
+  auto kern = step_bulk_kernel<R, T, FACT>;
+  const int smem = kBulkStages * SL::kBytes + kBulkStages * (int)sizeof(uint64_t);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0, occ = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return e;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem)) !=
+      cudaSuccess)
+    return e;
+  if (occ < 1) occ = 1;
+  const int tiles = p.D / 32;
+  const int npairs = (p.B + 1) / 2;
+  int g = (sms * occ) / tiles;          // one resident wave when the tiles allow it
+  if (g < 1) g = 1;
+  if (g > npairs) g = npairs;
+  const int per = (npairs + g - 1) / g;
+  g = (npairs + per - 1) / per;
+  dim3 grid(g, tiles);
+  kern<<<grid, kThreads, smem, stream>>>(p, per);
+  return cudaGetLastError();
+}
+
 template <int R, int T, bool FACT>
 cudaError_t launch_step_impl(const StepParams& p, cudaStream_t stream) {
   dim3 grid((p.B + kRowsPerCta - 1) / kRowsPerCta, (p.D + 31) / 32);
@@ -295,10 +568,14 @@ cudaError_t launch_step_impl(const StepParams& p, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_step(const Tile& t, const StepParams& p, cudaStream_t s) {
-#define M3_X(r, tt, nd, ndb, nthb)                                                 \
-  if (t.R == r && t.T == tt)                                                       \
+#define M3_X(r, tt, nd, ndb, nthb, gs)                                             \
+  if (t.R == r && t.T == tt) {                                                     \
+    if (p.bulk)                                                                    \
+      return p.factored ? launch_step_bulk_impl<r, tt, true>(p, s)                 \
+                        : launch_step_bulk_impl<r, tt, false>(p, s);               \
     return p.factored ? launch_step_impl<r, tt, true>(p, s)                        \
-                      : launch_step_impl<r, tt, false>(p, s);
+                      : launch_step_impl<r, tt, false>(p, s);                      \
+  }
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;

@@ -39,6 +39,11 @@ CASES = [
     ("bf16_odd_D", ScanShape(2, 20, 33, 16, 4, 2), torch.bfloat16, 0),
     ("all_tracking", ScanShape(2, 24, 64, 8, 8, 2), torch.float32, 0),
     ("no_rotation_verify_cfg", ScanShape(3, 70, 96, 16, 0, 2), torch.float32, 2),
+    # config-1 lane layout (gates kept in Tensor Memory, 8-step chunks): ragged
+    # last chunk, a single chunk, and a one-step last chunk
+    ("c1_layout_L37_bidir", ScanShape(3, 37, 96, 32, 16, 4), torch.float32, 2),
+    ("c1_layout_L8_causal", ScanShape(2, 8, 64, 32, 16, 4), torch.float32, 0),
+    ("c1_layout_L9_reverse_bf16", ScanShape(2, 9, 64, 32, 16, 4), torch.bfloat16, 1),
 ]
 
 _FN = {0: S.m3_trapezoidal_scan, 1: S.m3_reverse_scan, 2: S.m3_bidir_scan}

@@ -193,3 +193,40 @@ def test_unaligned_rows_take_the_scalar_path_with_equal_results(dtype):
         outs.append((torch.stack(ys, 1), h, dbu, hf))
     for a, b in zip(outs[0], outs[1]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("n_track", [8, 16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_pipelined_step_equals_register_path(n_track, dtype, monkeypatch):
+    """Aligned dense tiles go through the bulk-copy pipeline (several row pairs
+    per CTA, so every stage is reused, and an odd last row); the per-row
+    register path (M3_STEP_NO_BULK) must give the same bits, for the full and
+    the factored state, over several consecutive steps."""
+    B, D, N, steps = 301, 1024, 32, 5
+    gen = torch.Generator().manual_seed(31)
+    sh = ScanShape(B, steps, D, N, n_track, 2)
+    g = to_cuda(make_scan_inputs(sh, seed=17, dtype=dtype))
+    h0 = (torch.randn(B, D, N, generator=gen) * 0.1).cuda()
+    fa0 = torch.randn(B, D + N, generator=gen).cuda()
+    d0 = fa0[:, :D, None] * fa0[:, None, D:]
+    runs = []
+    for no_bulk in (False, True):
+        if no_bulk:
+            monkeypatch.setenv("M3_STEP_NO_BULK", "1")
+        else:
+            monkeypatch.delenv("M3_STEP_NO_BULK", raising=False)
+        h, dbu, hf, fa = h0.clone(), d0.clone(), h0.clone(), fa0.clone()
+        fb = torch.empty_like(fa)
+        ys, yfs = [], []
+        for t in range(steps):
+            args = (g["delta"][:, t], g["u"][:, t], g["Bc"][:, t], g["Cc"][:, t], g["A_real"],
+                    g["A_imag"], g["track"], sh.n_rot, N)
+            ys.append(S.m3_step_(h, dbu, *args))
+            yfs.append(S.m3_step_factored_(hf, fa, fb, *args))
+            fa, fb = fb, fa
+        torch.cuda.synchronize()
+        runs.append((torch.stack(ys), torch.stack(yfs), h, dbu, hf, fa))
+    for a, b in zip(runs[0], runs[1]):
+        assert torch.equal(a, b)
+    assert torch.equal(runs[0][0], runs[0][1])
+    assert S.device_error() == 0
