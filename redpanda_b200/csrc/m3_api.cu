@@ -106,7 +106,8 @@ bool bwd_layout(const m3_scan_desc* d, const Tile& t, BwdLayout* lay) {
   lay->Bg = bg;
   const size_t np = t.np();
   const size_t a_bytes = (size_t)lay->Bg * 3 * d->d_inner * np * 4;
-  const size_t bc_bytes = (size_t)lay->G * d->batch * d->seqlen * 2 * np * 4;
+  const size_t ndirs = d->direction == M3_DIR_BIDIR ? 2 : 1;
+  const size_t bc_bytes = (size_t)lay->G * ndirs * d->batch * d->seqlen * 2 * np * 4;
   const size_t du_bytes = d->direction == M3_DIR_BIDIR
                               ? (size_t)lay->G * lay->Bg * d->seqlen * t.dt_bwd() * 2 * 4
                               : 0;
@@ -184,6 +185,11 @@ int m3_scan_fwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   p.nck = nchunks(desc->seqlen, p.cki) - 1;
   p.async_ok = aligned(delta, 4) && aligned(u, 4) &&
                (desc->dtype_du == M3_F32 || (desc->d_inner % 2) == 0);
+  // bulk staging: whole channel tiles and 16-byte aligned rows of every input
+  p.bulk = (desc->d_inner % t.dt()) == 0 && ((desc->d_inner * esd) % 16) == 0 &&
+           ((desc->d_state * esb) % 16) == 0 && aligned(delta, 16) && aligned(u, 16) &&
+           aligned(Bc, 16) && aligned(Cc, 16) && aligned(y, 16) &&
+           getenv("M3_NO_BULK") == nullptr;
   p.err = device_err_ptr();
   cudaError_t e = launch_scan_fwd(t, p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
@@ -244,6 +250,11 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   p.async_du = aligned(delta, 4) && aligned(u, 4) &&
                (desc->dtype_du == M3_F32 || (desc->d_inner % 2) == 0);
   p.async_dy = aligned(dy, 4) && (dtype_dy == M3_F32 || (desc->d_inner % 2) == 0);
+  // bulk staging: whole channel tiles and 16-byte aligned rows of every input
+  p.bulk = (desc->d_inner % t.dt_bwd()) == 0 && ((desc->d_inner * esd) % 16) == 0 &&
+           ((desc->d_inner * esy) % 16) == 0 && ((desc->d_state * esb) % 16) == 0 &&
+           aligned(delta, 16) && aligned(u, 16) && aligned(dy, 16) && aligned(Bc, 16) &&
+           aligned(Cc, 16) && (!ckpt || aligned(ckpt, 16)) && getenv("M3_NO_BULK") == nullptr;
   p.err = device_err_ptr();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = launch_scan_bwd(t, p, s);
@@ -256,6 +267,7 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   r.dAr = d_A_real_p; r.dAi = d_A_imag_p; r.dTk = d_track_p;
   r.B = p.B; r.L = p.L; r.D = p.D; r.N = p.N; r.NR = p.NR; r.NT = p.NT;
   r.dt_bc = p.dt_bc; r.G = p.G; r.Bg = p.Bg;
+  r.ndirs = desc->direction == M3_DIR_BIDIR ? 2 : 1;
   e = launch_bwd_reduce(t, r, s);
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
@@ -307,7 +319,7 @@ static int step_common(const m3_step_desc* desc, float* h, float* dbu, const flo
            (desc->d_inner % 32) == 0 && ((desc->d_state * esb) % 16) == 0 &&
            aligned(delta, 16) && aligned(u, 16) && aligned(Bc, 16) && aligned(Cc, 16) &&
            (!factored || (aligned(fac_prev, 16) && aligned(fac_next, 16))) &&
-           getenv("M3_STEP_NO_BULK") == nullptr;
+           getenv("M3_NO_BULK") == nullptr;
   p.err = device_err_ptr();
   cudaError_t e = launch_step(t, p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;

@@ -34,6 +34,7 @@ struct FwdParams {
   int nch;         // chunks of kCK steps
   int cki, nck;    // checkpoint interval (8 or 16 steps) and checkpoints per direction
   int async_ok;    // cp.async staging allowed (alignment checked on the host)
+  int bulk;        // every staged row is a 16-byte aligned bulk copy
   int* err;
 };
 
@@ -42,7 +43,7 @@ struct BwdParams {
   const float* Ar; const float* Ai; const float* Tk;
   const void* dy; const float* ckpt;
   void* d_delta; void* d_u;
-  float* part_bc;     // [G][B][L][2][NL][4 quarters]
+  float* part_bc;     // [G][ndirs][B][L][2][NL][4 quarters]
   float* part_a;      // [Bg][3][D][NP]
   float* scratch_du;  // [G*Bg][L][DT][2]  (bidirectional only)
   int B, L, D, N, NR, NT;
@@ -51,6 +52,7 @@ struct BwdParams {
   int nch;            // chunks of the tile's checkpoint interval
   int G, Bg;
   int async_du, async_dy;   // cp.async staging allowed for delta/u and dy
+  int bulk;                 // every staged row is a 16-byte aligned bulk copy
   int* err;
 };
 
@@ -76,6 +78,7 @@ struct ReduceParams {
   int B, L, D, N, NR, NT;
   int dt_bc;
   int G, Bg;
+  int ndirs;          // direction slots of part_bc
 };
 
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s);

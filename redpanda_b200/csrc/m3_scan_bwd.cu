@@ -52,7 +52,7 @@ constexpr int pow2ceil(int x) {
 // GS: the recompute pass also keeps each step's rotational gates (exp*cos and
 // exp*sin) in Tensor Memory, so the reverse pass evaluates no transcendental;
 // the chunk is then KC = 8 steps so that state and gates fit.
-template <int R, int T, int ND, int NTH, bool GS>
+template <int R, int T, int ND, int NTH, bool GS, bool BULK>
 struct BwdCfg {
   static_assert(ND % 2 == 0, "the backward processes channel pairs");
   static constexpr int KC = GS ? 8 : kCK;           // chunk length (= checkpoint interval)
@@ -75,11 +75,17 @@ struct BwdCfg {
   static constexpr int SG = NG * 4 + (16 / ND < 4 ? 4 : 16 / ND);  // ddelta row pitch
   static constexpr size_t red_floats = (size_t)FL * 2 * NL * SR;   // [FL][2][NL][SR]
   static constexpr size_t gs_floats = (size_t)FL * ND * 2 * SG;    // [FL][ND][2][SG]
+  // BULK (16-byte staging): B/C rows land raw (HBM dtype, memory order) and
+  // are widened into the padded fp32 tiles after the copy; the bidirectional
+  // second pass stages the first pass's ddelta/du rows of the chunk.
+  static constexpr size_t braw_floats = BULK ? 2 * 2 * (size_t)KC * NP : 0;  // [2][B|C][KC][NP]
+  static constexpr size_t scr_floats = BULK ? (size_t)KC * DT * 2 : 0;       // [KC][DT][2]
   static constexpr size_t smem_bytes =
       3 * 2 * raw_bytes                       // delta, u, dy (HBM dtype), double-buffered
       + 2 * (size_t)DT * NP * 4               // checkpoint tile, double-buffered
       + 2 * 2 * (size_t)KC * NP * 4           // B, C (fp32), double-buffered
       + red_floats * 4 + gs_floats * 4
+      + braw_floats * 4 + scr_floats * 4
       + 16;                                   // TMEM address slot
 };
 
@@ -118,10 +124,10 @@ __device__ __forceinline__ float tile_at(const unsigned char* base, bool bf16, i
   return reinterpret_cast<const float*>(base)[idx];
 }
 
-template <int R, int T, int ND, int NTH, bool GS>
+template <int R, int T, int ND, int NTH, bool GS, bool BULK>
 __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
   using LM = LaneMap<R, T>;
-  using CF = BwdCfg<R, T, ND, NTH, GS>;
+  using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
   constexpr int KC = CF::KC;
   constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS, CG = CF::CG;
   constexpr int NG = CF::NG, NDP = CF::NDP, FL = CF::FL, SR = CF::SR, SG = CF::SG;
@@ -139,7 +145,9 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
   float* s_c = s_b + 2 * KC * NP;                                    // [2][KC][NP]
   float* s_red = s_c + 2 * KC * NP;                                  // [FL][2][NL][SR]
   float* s_gs = s_red + CF::red_floats;                              // [FL][ND][2][SG]
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_gs + CF::gs_floats);
+  float* s_braw = s_gs + CF::gs_floats;                              // [2][B|C][KC][NP] (BULK)
+  float* s_scr = s_braw + CF::braw_floats;                           // [KC][DT][2] (BULK)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_scr + CF::scr_floats);
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
   const int warp = tid >> 5;
@@ -255,14 +263,81 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     }
   };
 
+  // BULK staging of work item i into buffer buf with 16-byte cp.async and
+  // shift-only index math (rows of DT channels are powers of two of 16-byte
+  // pieces): delta/u/dy rows, the checkpoint tile, and the chunk's B and C rows
+  // as one contiguous block each (rows in memory order; widen_bc reorders).
+  const int es_bc = p.dt_bc == M3_BF16 ? 2 : 4;
+  const int lg_du = 31 - __clz(DT * es_du / 16), lg_dy = 31 - __clz(DT * es_dy / 16);
+  auto stage_vec = [&](int i, int buf) {
+    int b, pass, c;
+    item(i, b, pass, c);
+    const int dir = dir_of(pass), s0 = c * KC;
+    const int ns = min(KC, L - s0);
+    for (int v = tid; v < (3 * ns) << lg_du; v += NTH) {
+      // tensor k (delta, u) uses lg_du; dy rows are handled below when its size differs
+      const int r = v >> lg_du, w = v - (r << lg_du);
+      const int kind = r / ns, tt = r - kind * ns;
+      if (kind == 2 && lg_dy != lg_du) break;
+      const int s = s0 + tt;
+      const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
+      const int es = kind == 2 ? es_dy : es_du;
+      const void* src = kind == 0 ? p.delta : (kind == 1 ? p.u : p.dy);
+      unsigned char* dst = (kind == 0 ? s_dl : (kind == 1 ? s_u : s_dy)) + buf * CF::raw_bytes;
+      cp_async16(dst + (size_t)tt * DT * es + w * 16,
+                 (const char*)src + (row * D + d0) * es + w * 16, true);
+    }
+    if (lg_dy != lg_du) {
+      for (int v = tid; v < ns << lg_dy; v += NTH) {
+        const int tt = v >> lg_dy, w = v - (tt << lg_dy);
+        const int s = s0 + tt;
+        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
+        cp_async16(s_dy + buf * CF::raw_bytes + (size_t)tt * DT * es_dy + w * 16,
+                   (const char*)p.dy + (row * D + d0) * es_dy + w * 16, true);
+      }
+    }
+    if (c > 0) {
+      const int dslot = bidir ? dir : 0;
+      const float* src = p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
+      float* dst = s_ck + buf * DT * NP;
+      for (int v = tid; v < DT * NP / 4; v += NTH) cp_async16(dst + v * 4, src + v * 4, true);
+    }
+    const int t_lo = dir ? L - s0 - ns : s0;             // first memory row of the chunk
+    const int pieces = ns * N * es_bc / 16;
+    for (int v = tid; v < 2 * pieces; v += NTH) {
+      const int which = v >= pieces, w = v - which * pieces;
+      const char* src = (const char*)(which ? p.Cc : p.Bc) + ((size_t)b * L + t_lo) * N * es_bc;
+      float* dst = s_braw + ((size_t)(buf * 2 + which) * KC) * NP;
+      cp_async16(reinterpret_cast<char*>(dst) + w * 16, src + w * 16, true);
+    }
+  };
+  // widen the raw B/C rows of buffer buf into the padded fp32 lane layout
+  // (processing step tt is memory row tt, or ns-1-tt for the reversed scan)
+  auto widen_bc = [&](int buf, int ns, int dir) {
+    for (int i = tid; i < ns * NP; i += NTH) {
+      const int tt = i / NP, ln = i - tt * NP;
+      const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
+      const size_t r = (size_t)(dir ? ns - 1 - tt : tt) * N + (n >= 0 ? n : 0);
+      const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * KC) * NP;
+      const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * KC) * NP;
+      s_b[buf * KC * NP + i] = n >= 0 ? ld_f(rb0, r, p.dt_bc) : 0.f;
+      s_c[buf * KC * NP + i] = n >= 0 ? ld_f(rc0, r, p.dt_bc) : 0.f;
+    }
+  };
+
   float2 qv[NDP][NL], gn[NDP][RR];
   if (nitems > 0) {
-    stage(0, 0);
-    cp_async_commit();
-    int b, pass, c;
-    item(0, b, pass, c);
-    load_bc(b, dir_of(pass), c * KC);
-    store_bc(0);
+    if constexpr (BULK) {
+      stage_vec(0, 0);
+      cp_async_commit();
+    } else {
+      stage(0, 0);
+      cp_async_commit();
+      int b, pass, c;
+      item(0, b, pass, c);
+      load_bc(b, dir_of(pass), c * KC);
+      store_bc(0);
+    }
   }
   for (int it = 0; it < nitems; ++it) {
     const int buf = it & 1;
@@ -274,15 +349,36 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
     const int s0 = c * KC;
     const int ns = min(KC, L - s0);
     const bool more = it + 1 < nitems;
-    if (more) stage(it + 1, buf ^ 1);
-    cp_async_commit();
-    if (more) {
-      int b2, pass2, c2;
-      item(it + 1, b2, pass2, c2);
-      load_bc(b2, dir_of(pass2), c2 * KC);
+    if constexpr (BULK) {
+      // group 1: the first pass's ddelta/du rows of this chunk (written by this
+      // CTA before the previous barrier), needed from the first flush on
+      if (second_of_two) {
+        for (int v = tid; v < ns * (DT / 2); v += NTH) {
+          const int tt = v / (DT / 2), w = v - tt * (DT / 2);
+          const int s = s0 + tt;
+          const int t = dir ? L - 1 - s : s;
+          cp_async16(s_scr + (size_t)tt * DT * 2 + w * 4, scratch + (size_t)t * DT * 2 + w * 4, true);
+        }
+      }
+      cp_async_commit();
+      // group 2: the next work item
+      if (more) stage_vec(it + 1, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait_n<2>();   // this item's staging (committed one iteration ago)
+      __syncthreads();
+      widen_bc(buf, ns, dir);
+      __syncthreads();
+    } else {
+      if (more) stage(it + 1, buf ^ 1);
+      cp_async_commit();
+      if (more) {
+        int b2, pass2, c2;
+        item(it + 1, b2, pass2, c2);
+        load_bc(b2, dir_of(pass2), c2 * KC);
+      }
+      cp_async_wait1();
+      __syncthreads();
     }
-    cp_async_wait1();
-    __syncthreads();
 
     if (c == nch - 1) {   // first chunk of a direction pass: adjoint state starts at zero
 #pragma unroll
@@ -471,6 +567,9 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
         }
       }
       if (slot == FL - 1 || tt == 0) {
+        if constexpr (BULK) {
+          if (second_of_two) cp_async_wait_n<1>();   // the scratch group, not the prefetch
+        }
         __syncthreads();
         const int nsl = slot + 1;                 // slots in this flush
         const int tt_hi = tt + slot;              // step of slot 0
@@ -502,13 +601,11 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
             const int which = rem / NL, j = rem - which * NL;
             const int s = s0 + tt_hi - sl;
             const int t = dir ? L - 1 - s : s;
+            // one partial per (channel tile, direction): no read-modify-write
+            const int dslot = bidir ? dir : 0;
             float4* dst = reinterpret_cast<float4*>(
-                p.part_bc + ((((size_t)gt * B + b) * L + t) * 2 + which) * NP + j * 4);
-            if (second_of_two) {
-              const float4 o = *dst;
-              acc.x = __fadd_rn(o.x, acc.x); acc.y = __fadd_rn(o.y, acc.y);
-              acc.z = __fadd_rn(o.z, acc.z); acc.w = __fadd_rn(o.w, acc.w);
-            }
+                p.part_bc + (((((size_t)gt * ndirs + dslot) * B + b) * L + t) * 2 + which) * NP +
+                j * 4);
             *dst = acc;
           }
         }
@@ -535,8 +632,9 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
               sc[1] = ddu;
             } else {
               if (second_of_two) {
-                ddl = __fadd_rn(sc[0], ddl);
-                ddu = __fadd_rn(sc[1], ddu);
+                const float* scv = BULK ? s_scr + ((size_t)tts * DT + dd) * 2 : sc;
+                ddl = __fadd_rn(scv[0], ddl);
+                ddu = __fadd_rn(scv[1], ddu);
               }
               const size_t oi = ((size_t)b * L + t) * D + d;
               st_f(p.d_delta, oi, p.dt_du, ddl);
@@ -547,7 +645,9 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
         __syncthreads();
       }
     }
-    if (more) store_bc(buf ^ 1);
+    if constexpr (!BULK) {
+      if (more) store_bc(buf ^ 1);
+    }
   }
   cp_async_wait0();
 
@@ -604,7 +704,7 @@ __global__ void reduce_bc_kernel(const ReduceParams p, int R, int T) {
     const size_t bt = i / p.N;
     const int ln = part_lane(n, p.NR, R, T);
     float vb = 0.f, vc = 0.f;
-    for (int g = 0; g < p.G; ++g) {
+    for (int g = 0; g < p.G * p.ndirs; ++g) {   // channel tiles x directions, fixed order
       const float* src = p.part_bc + (((size_t)g * p.B * p.L + bt) * 2) * NP + ln;
       vb = __fadd_rn(vb, src[0]);
       vc = __fadd_rn(vc, src[NP]);
@@ -636,10 +736,15 @@ __global__ void reduce_a_kernel(const ReduceParams p, int R, int T) {
   }
 }
 
-template <int R, int T, int ND, int NTH, bool GS>
+// Largest dynamic shared memory of one CTA on sm_100 (227 KB); tiles whose
+// bulk-staging layout does not fit use the cp.async staging.
+constexpr size_t kMaxSmemPerCta = 227 * 1024;
+
+template <int R, int T, int ND, int NTH, bool GS, bool BULK>
 cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
-  using CF = BwdCfg<R, T, ND, NTH, GS>;
-  auto kern = scan_bwd_kernel<R, T, ND, NTH, GS>;
+  using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
+  static_assert(CF::smem_bytes <= kMaxSmemPerCta, "backward tile exceeds shared memory");
+  auto kern = scan_bwd_kernel<R, T, ND, NTH, GS, BULK>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)CF::smem_bytes);
   if (e != cudaSuccess) return e;
@@ -648,13 +753,23 @@ cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Bulk staging when the caller's layout allows it and the tile's bulk layout
+// fits in shared memory; cp.async staging otherwise.
+template <int R, int T, int ND, int NTH, bool GS>
+cudaError_t launch_bwd_tile(const BwdParams& p, cudaStream_t stream) {
+  if constexpr (BwdCfg<R, T, ND, NTH, GS, true>::smem_bytes <= kMaxSmemPerCta) {
+    if (p.bulk) return launch_bwd_impl<R, T, ND, NTH, GS, true>(p, stream);
+  }
+  return launch_bwd_impl<R, T, ND, NTH, GS, false>(p, stream);
+}
+
 }  // namespace
 
 cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s) {
 #define M3_X(r, tt, nd, ndb, nthb, gs)                                              \
   if constexpr (ndb > 0)                                                            \
     if (t.R == r && t.T == tt && t.ND == nd)                                        \
-      return launch_bwd_impl<r, tt, ndb, nthb, (gs != 0)>(p, s);
+      return launch_bwd_tile<r, tt, ndb, nthb, (gs != 0)>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;

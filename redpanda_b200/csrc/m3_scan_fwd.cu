@@ -11,6 +11,7 @@
 // shared memory with cp.async (double-buffered, in their HBM dtype); B/C are
 // register-prefetched one chunk ahead, converted to fp32 and padded to the
 // thread lane layout.  y is reduced over the 4 lane quarters with shuffles.
+#include "m3_bulk.cuh"
 #include "m3_common.cuh"
 #include "m3_internal.h"
 #include "m3_stage.cuh"
@@ -82,7 +83,19 @@ constexpr int kFwdUnroll = M3_FWD_UNROLL;
 #define M3_FWD_MIN_BLOCKS 3
 #endif
 
-template <int R, int T, int ND>
+// Shared memory of the forward kernel (bytes): delta, u (HBM dtype, 4 bytes
+// reserved per element), B, C (padded fp32), raw B/C rows and two mbarriers
+// (BULK staging), y of the first pass (bidirectional second pass only).
+template <int NP, int DT, bool BULK>
+struct FwdSmem {
+  static constexpr size_t du = (size_t)kCK * DT * 4;             // one buffer of delta or u
+  static constexpr size_t bc = (size_t)kCK * NP * 4;             // one buffer of B or C
+  static constexpr size_t braw = BULK ? 2 * 2 * bc : 0;          // [2][B|C][kCK][NP]
+  static constexpr size_t off_y = 2 * 2 * du + 2 * 2 * bc + braw + 16;
+  static size_t bytes(bool bidir) { return off_y + (bidir ? 2 * (size_t)kCK * DT * 4 : 0); }
+};
+
+template <int R, int T, int ND, bool BULK>
 __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(const FwdParams p) {
   using LM = LaneMap<R, T>;
   constexpr int NL = R + T;
@@ -92,12 +105,15 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
   constexpr int TT = T > 0 ? T : 1;
   constexpr int BCE = (kCK * NP + kThreads - 1) / kThreads;   // B/C prefetch per thread
 
+  using SM = FwdSmem<NP, DT, BULK>;
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* s_dl = smem;                                 // [2][kCK*DT*4]
   unsigned char* s_u = s_dl + 2 * kCK * DT * 4;               // [2][kCK*DT*4]
   float* s_b = reinterpret_cast<float*>(s_u + 2 * kCK * DT * 4);  // [2][kCK][NP]
   float* s_c = s_b + 2 * kCK * NP;
-  float* s_y = s_c + 2 * kCK * NP;                            // [2][kCK][DT] (bidir pass 2)
+  float* s_braw = s_c + 2 * kCK * NP;                         // [2][B|C][kCK][NP] (BULK)
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + SM::off_y - 16);   // [2] (BULK)
+  float* s_y = reinterpret_cast<float*>(smem + SM::off_y);    // [2][kCK][DT] (bidir pass 2)
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
   const int b = blockIdx.x;
@@ -134,8 +150,20 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
     }
   }
 
+  const int es_bc = p.dt_bc == M3_BF16 ? 2 : 4;
+  if constexpr (BULK) {
+    if (tid == 0) {
+      mbar_init(&s_bar[0], 1);
+      mbar_init(&s_bar[1], 1);
+      mbar_fence_init();
+    }
+    __syncthreads();
+  }
+  int phase[2] = {0, 0};   // completed uses of each staging buffer (BULK)
+  int fail = 0;
+
   const int npass = p.direction == M3_DIR_BIDIR ? 2 : 1;
-  for (int pass = 0; pass < npass; ++pass) {
+  for (int pass = 0; pass < npass && !fail; ++pass) {
     const int dir = p.direction == M3_DIR_BIDIR ? (pass == 0 ? 1 : 0) : p.direction;
     const bool accumulate = p.direction == M3_DIR_BIDIR && pass == 1;
     const int dslot = p.direction == M3_DIR_BIDIR ? dir : 0;
@@ -173,25 +201,93 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
       }
     };
 
+    // BULK: warp 0 stages chunk c (delta, u, B, C rows) with one bulk copy per
+    // row, lane 0 first registering the byte count on the buffer's mbarrier;
+    // the first pass's y rows (second pass) move with 16-byte cp.async.
+    auto stage_bulk = [&](int c, int buf) {
+      const int s0 = c * kCK, ns = min(kCK, L - s0);
+      const int lane = tid & 31;
+      if (lane == 0)
+        mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)ns * (uint32_t)(2 * DT * esz + 2 * N * es_bc));
+      __syncwarp();
+      for (int k = lane; k < 4 * ns; k += 32) {
+        const int tt = k >> 2, kind = k & 3;
+        const int s = s0 + tt;
+        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
+        if (kind < 2) {
+          unsigned char* dst = (kind == 0 ? s_dl : s_u) + buf * kCK * DT * 4 + (size_t)tt * DT * esz;
+          bulk_g2s(dst, (const char*)(kind == 0 ? p.delta : p.u) + (row * D + d0) * esz, DT * esz,
+                   &s_bar[buf]);
+        } else {
+          float* dst = s_braw + ((size_t)(buf * 2 + (kind - 2)) * kCK + tt) * NP;
+          bulk_g2s(dst, (const char*)(kind == 2 ? p.Bc : p.Cc) + row * N * es_bc, N * es_bc,
+                   &s_bar[buf]);
+        }
+      }
+    };
+    auto stage_y16 = [&](int c, int buf) {
+      const int s0 = c * kCK, ns = min(kCK, L - s0);
+      for (int v = tid; v < ns * (DT / 4); v += kThreads) {
+        const int tt = v / (DT / 4), w = v - tt * (DT / 4);
+        const int s = s0 + tt;
+        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
+        cp_async16(s_y + (size_t)(buf * kCK + tt) * DT + w * 4, p.y + row * D + d0 + w * 4, true);
+      }
+    };
+    auto widen_bc = [&](int buf, int ns) {
+      for (int i = tid; i < ns * NP; i += kThreads) {
+        const int tt = i / NP, ln = i - tt * NP;
+        const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
+        const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * kCK + tt) * NP;
+        const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * kCK + tt) * NP;
+        s_b[buf * kCK * NP + i] = n >= 0 ? ld_f(rb0, n, p.dt_bc) : 0.f;
+        s_c[buf * kCK * NP + i] = n >= 0 ? ld_f(rc0, n, p.dt_bc) : 0.f;
+      }
+    };
+
     // prologue: chunk 0 into buffer 0
-    stage_du<DT>(s_dl, s_u, p, b, d0, 0, dir, esz);
-    if (accumulate) stage_y<DT>(s_y, p, b, d0, 0, dir);
-    cp_async_commit();
-    load_bc(0);
-    store_bc(0);
+    if constexpr (BULK) {
+      if (tid < 32) stage_bulk(0, 0);
+      if (accumulate) stage_y16(0, 0);
+      cp_async_commit();
+    } else {
+      stage_du<DT>(s_dl, s_u, p, b, d0, 0, dir, esz);
+      if (accumulate) stage_y<DT>(s_y, p, b, d0, 0, dir);
+      cp_async_commit();
+      load_bc(0);
+      store_bc(0);
+    }
 
     for (int c = 0; c < p.nch; ++c) {
       const int buf = c & 1;
       const bool more = c + 1 < p.nch;
-      if (more) {
-        stage_du<DT>(s_dl + (buf ^ 1) * kCK * DT * 4, s_u + (buf ^ 1) * kCK * DT * 4, p, b, d0,
-                     (c + 1) * kCK, dir, esz);
-        if (accumulate) stage_y<DT>(s_y + (buf ^ 1) * kCK * DT, p, b, d0, (c + 1) * kCK, dir);
+      if constexpr (BULK) {
+        if (more) {
+          if (tid < 32) stage_bulk(c + 1, buf ^ 1);
+          if (accumulate) stage_y16(c + 1, buf ^ 1);
+        }
+        cp_async_commit();
+        const bool ok = mbar_wait(&s_bar[buf], (uint32_t)(phase[buf] & 1));
+        ++phase[buf];
+        cp_async_wait1();
+        if (ok) widen_bc(buf, min(kCK, L - c * kCK));
+        if (__syncthreads_or(!ok)) {
+          // give up: let a copy still in flight land before the CTA exits
+          if (tid == 0 && more) mbar_wait(&s_bar[buf ^ 1], (uint32_t)(phase[buf ^ 1] & 1));
+          fail = 1;
+          break;
+        }
+      } else {
+        if (more) {
+          stage_du<DT>(s_dl + (buf ^ 1) * kCK * DT * 4, s_u + (buf ^ 1) * kCK * DT * 4, p, b, d0,
+                       (c + 1) * kCK, dir, esz);
+          if (accumulate) stage_y<DT>(s_y + (buf ^ 1) * kCK * DT, p, b, d0, (c + 1) * kCK, dir);
+        }
+        cp_async_commit();
+        if (more) load_bc((c + 1) * kCK);
+        cp_async_wait1();
+        __syncthreads();
       }
-      cp_async_commit();
-      if (more) load_bc((c + 1) * kCK);
-      cp_async_wait1();
-      __syncthreads();
 
       const unsigned char* bdl = s_dl + buf * kCK * DT * 4;
       const unsigned char* bu = s_u + buf * kCK * DT * 4;
@@ -309,20 +405,22 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
           }
         }
       }
-      if (more) store_bc(buf ^ 1);
+      if constexpr (!BULK) {
+        if (more) store_bc(buf ^ 1);
+      }
       __syncthreads();
     }
   }
   cp_async_wait0();
+  if (fail) set_err(p.err, M3_ERR_DEVICE);
 }
 
-template <int R, int T, int ND>
+template <int R, int T, int ND, bool BULK>
 cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
   constexpr int NP = 4 * (R + T);
   constexpr int DT = 32 * ND;
-  const size_t smem = 2 * (2 * (size_t)kCK * DT * 4) + 2 * (2 * (size_t)kCK * NP * 4) +
-                      (p.direction == M3_DIR_BIDIR ? 2 * (size_t)kCK * DT * 4 : 0);
-  auto kern = scan_fwd_kernel<R, T, ND>;
+  const size_t smem = FwdSmem<NP, DT, BULK>::bytes(p.direction == M3_DIR_BIDIR);
+  auto kern = scan_fwd_kernel<R, T, ND, BULK>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
@@ -335,7 +433,8 @@ cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
 
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
 #define M3_X(r, tt, nd, ndb, nthb, gs) \
-  if (t.R == r && t.T == tt && t.ND == nd) return launch_fwd_impl<r, tt, nd>(p, s);
+  if (t.R == r && t.T == tt && t.ND == nd)                                  \
+    return p.bulk ? launch_fwd_impl<r, tt, nd, true>(p, s) : launch_fwd_impl<r, tt, nd, false>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;

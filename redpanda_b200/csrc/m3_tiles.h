@@ -18,7 +18,7 @@
   X(6, 2, 4, 2, 256, 0)    /* N=32, 24 rot + 8 track (config 3, Search Mamba) */ \
   X(2, 1, 8, 4, 256, 0)    /* N=12, 8 rot + 4 track; N=8, 6 rot + 2 track     */ \
   X(4, 0, 8, 4, 256, 0)    /* N=16, no tracking                               */ \
-  X(2, 0, 8, 8, 256, 0)    /* N=8, no tracking                                */ \
+  X(2, 0, 8, 4, 256, 0)    /* N=8, no tracking                                */ \
   X(8, 0, 4, 2, 256, 0)    /* N=32, no tracking                               */ \
   X(12, 4, 2, 2, 128, 0)   /* N=64, 48 rot + 16 track                         */ \
   X(16, 0, 2, 2, 128, 0)   /* N=64, no tracking                               */ \

@@ -44,6 +44,7 @@ CASES = [
     ("c1_layout_L37_bidir", ScanShape(3, 37, 96, 32, 16, 4), torch.float32, 2),
     ("c1_layout_L8_causal", ScanShape(2, 8, 64, 32, 16, 4), torch.float32, 0),
     ("c1_layout_L9_reverse_bf16", ScanShape(2, 9, 64, 32, 16, 4), torch.bfloat16, 1),
+    ("N8_no_track_bidir", ScanShape(2, 20, 256, 8, 0, 2), torch.float32, 2),
 ]
 
 _FN = {0: S.m3_trapezoidal_scan, 1: S.m3_reverse_scan, 2: S.m3_bidir_scan}
@@ -153,3 +154,32 @@ def test_backward_is_deterministic():
 
 def test_no_device_error_recorded():
     assert S.device_error(clear=True) == 0
+
+
+BULK_CASES = [
+    ("c1_layout_bidir_f32", ScanShape(3, 37, 256, 32, 16, 4), torch.float32, 2),
+    ("c1_layout_bidir_bf16", ScanShape(2, 64, 256, 32, 16, 4), torch.bfloat16, 2),
+    ("c3_layout_causal", ScanShape(2, 50, 256, 32, 8, 2), torch.float32, 0),
+    ("c0_layout_reverse", ScanShape(2, 20, 256, 16, 4, 4), torch.float32, 1),
+]
+
+
+@pytest.mark.parametrize("name,shape,dtype,direction", BULK_CASES, ids=[c[0] for c in BULK_CASES])
+def test_bulk_staging_equals_cp_async_staging(name, shape, dtype, direction, monkeypatch):
+    """Whole channel tiles with 16-byte aligned rows are staged with bulk
+    asynchronous copies; the element-wise cp.async path (M3_NO_BULK) must give
+    the same bits for the output and every gradient."""
+    inp = make_scan_inputs(shape, seed=19, dtype=dtype)
+    runs = []
+    for no_bulk in (False, True):
+        if no_bulk:
+            monkeypatch.setenv("M3_NO_BULK", "1")
+        else:
+            monkeypatch.delenv("M3_NO_BULK", raising=False)
+        runs.append(run_m3(inp, direction, dtype))
+    (y0, g0), (y1, g1) = runs
+    assert torch.equal(y0, y1)
+    for k in GRAD_KEYS:
+        if g0[k] is not None:
+            assert torch.equal(g0[k], g1[k]), k
+    assert S.device_error() == 0

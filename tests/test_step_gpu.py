@@ -200,7 +200,7 @@ def test_unaligned_rows_take_the_scalar_path_with_equal_results(dtype):
 def test_pipelined_step_equals_register_path(n_track, dtype, monkeypatch):
     """Aligned dense tiles go through the bulk-copy pipeline (several row pairs
     per CTA, so every stage is reused, and an odd last row); the per-row
-    register path (M3_STEP_NO_BULK) must give the same bits, for the full and
+    register path (M3_NO_BULK) must give the same bits, for the full and
     the factored state, over several consecutive steps."""
     B, D, N, steps = 301, 1024, 32, 5
     gen = torch.Generator().manual_seed(31)
@@ -212,9 +212,9 @@ def test_pipelined_step_equals_register_path(n_track, dtype, monkeypatch):
     runs = []
     for no_bulk in (False, True):
         if no_bulk:
-            monkeypatch.setenv("M3_STEP_NO_BULK", "1")
+            monkeypatch.setenv("M3_NO_BULK", "1")
         else:
-            monkeypatch.delenv("M3_STEP_NO_BULK", raising=False)
+            monkeypatch.delenv("M3_NO_BULK", raising=False)
         h, dbu, hf, fa = h0.clone(), d0.clone(), h0.clone(), fa0.clone()
         fb = torch.empty_like(fa)
         ys, yfs = [], []
