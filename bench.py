@@ -55,12 +55,12 @@ def _peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def _traffic_per_token():
-    """DRAM bytes/token of the backward kernel from the committed ncu summary."""
+def _profile_value(key):
+    """A figure of the committed ncu summary of the backward kernel (or None)."""
     path = os.path.join(REPO, "profiles", "scan_bwd_c2_traffic.txt")
     try:
         for line in open(path):
-            if line.startswith("dram_bytes_per_token:"):
+            if line.startswith(key + ":"):
                 return float(line.split(":")[1])
     except OSError:
         pass
@@ -68,8 +68,13 @@ def _traffic_per_token():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clock/throttle sampling (every 50 ms, timestamped).
+
+    Started before the warm-up so that it is running when the timed region
+    begins; ``stop(t0, t1)`` keeps only the samples whose timestamps fall in
+    the host wall-clock window [t0, t1] of the timed region.
+    """
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -78,12 +83,12 @@ class ClockSampler:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
 
-    def stop(self):
+    def stop(self, t0=None, t1=None):
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
@@ -93,24 +98,28 @@ class ClockSampler:
             self.p.kill()
         self.f.flush()
         self.f.seek(0)
-        sm, mx, reasons = [], [], set()
+        sm, mx, pw, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.f.read().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                if t0 is not None and not (t0 - 0.05 <= ts <= t1 + 0.05):
+                    continue
+                sm.append(float(parts[2]))
+                mx.append(float(parts[3]))
+                pw.append(float(parts[4]))
             except ValueError:
                 continue
-            for nm, v in zip(names, parts[5:9]):
+            for nm, v in zip(names, parts[6:10]):
                 if v.lower() == "active":
                     reasons.add(nm)
         os.unlink(self.f.name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "power_w_max": max(pw) if pw else None, "samples": len(sm)}
 
 
 def cpu_scan_rate(rows, min_seconds, max_reps=None):
@@ -219,19 +228,21 @@ def run_m3(args):
     gB, gC = torch.empty_like(x["Bc"]), torch.empty_like(x["Cc"])
     gflat = torch.empty(3, D, N, device=dev)   # dA_real, dA_imag, dtrack: one all-reduce
     stream = torch.cuda.current_stream(dev)
-    bwd_events = []
+    kernel_events = []
 
     def step(inputs, timed_bwd=False):
+        if timed_bwd:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record(stream)
         plan.forward(inputs["delta"], inputs["u"], inputs["Bc"], inputs["Cc"], Ar_p, Ai_p, Tk_p,
                      y, ckpt)
         if timed_bwd:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+            ev[1].record(stream)
         plan.backward(inputs["delta"], inputs["u"], inputs["Bc"], inputs["Cc"], Ar_p, Ai_p, Tk_p,
                       inputs["dy"], ckpt, gd, gu, gB, gC, gflat[0], gflat[1], gflat[2], ws)
         if timed_bwd:
-            e1.record(stream)
-            bwd_events.append((e0, e1))
+            ev[2].record(stream)
+            kernel_events.append(ev)
         if world > 1:
             dist.all_reduce(gflat)
 
@@ -248,19 +259,21 @@ def run_m3(args):
         return float(t.item())
 
     # ---- device-resident leg
+    clk = ClockSampler(local)
     for _ in range(args.warmup):
         step(x)
     barrier()
-    clk = ClockSampler(local)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
     t0.record(stream)
     for _ in range(args.steps):
         step(x, timed_bwd=True)
     t1.record(stream)
     barrier()
-    clocks = clk.stop()
+    clocks = clk.stop(wall0, time.time())
     ms = max_over_ranks(t0.elapsed_time(t1))
-    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in bwd_events)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in kernel_events)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in kernel_events)
     tokens = world * B_RANK * L * args.steps
     value = tokens / (ms / 1e3) / 1e9
 
@@ -314,7 +327,8 @@ def run_m3(args):
         peak, peak_kind = _peaks()
         bwd_bytes = BWD_BYTES_PER_TOKEN * B_RANK * L
         achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
-        tpt = _traffic_per_token()
+        tpt = _profile_value("dram_bytes_per_token")
+        fma = _profile_value("fma_pipe_active_pct")
         cpu = None
         if world == 1 and not args.no_cpu:
             rate, reps, el = cpu_scan_rate(4, args.cpu_seconds)
@@ -340,7 +354,11 @@ def run_m3(args):
                          "unit": "GB/s", "frac": achieved / peak,
                          "traffic": (tpt * B_RANK * L) if tpt else None,
                          "algorithmic_bytes": bwd_bytes, "ms_per_launch": bwd_ms,
-                         "note": "compute-bound (FP32/MUFU issue), see profiles/"},
+                         "fma_pipe_active_frac": (fma / 100.0) if fma is not None else None,
+                         "note": "compute-bound: the FP32 pipe, not HBM, limits the scan "
+                                 "(fma_pipe_active_frac from the ncu summary in profiles/)"},
+            "kernels_ms": {"scan_fwd_bidir": fwd_ms, "scan_bwd_bidir": bwd_ms,
+                           "tokens_per_launch": B_RANK * L},
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
@@ -358,7 +376,7 @@ def run_step_rollout(dev, args):
     import torch
     from redpanda_b200 import scan as S
     from redpanda_b200.scan import ScanPlan, pad_params
-    layers, Bs, Ds, Ns, nr = 12, 8192, 1024, 32, 24
+    layers, Bs, Ds, Ns, nr = args.rollout_layers, args.rollout_batch, 1024, 32, 24
     g = torch.Generator(dev).manual_seed(7)
     params = []
     for _ in range(layers):
@@ -436,7 +454,7 @@ def run_step_rollout(dev, args):
     peak, kind = _peaks()
     state_bytes = layers * Bs * Ds * Ns * 16
     return {
-        "workload": "c3: 12 layers, B=8192, D=1024, N=32 (24 rot + 8 track), 32 steps, "
+        "workload": f"c3: {layers} layers, B={Bs}, D=1024, N=32 (24 rot + 8 track), 32 steps, "
                     "re-anchor every 8 steps by an L=64 scan with return_state",
         "node_steps_per_s": Bs * 32 / (total_ms / 1e3),
         "ms_per_rollout": total_ms,
@@ -464,6 +482,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-rollout", dest="rollout", action="store_false",
                     help="skip the config-3 step rollout measurement")
+    ap.add_argument("--rollout-layers", type=int, default=12,
+                    help="layers of the config-3 rollout (default 12; fewer for profiler captures)")
+    ap.add_argument("--rollout-batch", type=int, default=8192,
+                    help="rollout rows (default 8192; fewer for profiler captures)")
     ap.add_argument("--batch", type=int, default=B_RANK,
                     help="rows per GPU (default: the config-2 batch; smaller values are "
                          "for profiler captures only)")
