@@ -2,9 +2,9 @@
 // bounded waits.  Used by the pipelined step kernel to stream whole state rows
 // into shared memory several rows ahead of the compute.
 //
-// No cluster multicast: every copy reads this GPU's own memory into this CTA's
-// own shared memory (a CTA-local shared address is a valid shared::cluster
-// address of the issuing CTA).
+// Every copy is the plain single-destination form: it reads this GPU's own
+// memory into the issuing CTA's own shared memory (a CTA-local shared address
+// is a valid shared::cluster address of the issuing CTA).
 #pragma once
 
 #include <stdint.h>
