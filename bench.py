@@ -322,6 +322,7 @@ def run_m3(args):
     e2e_value = tokens / (e2e_ms / 1e3) / 1e9
 
     step_info = run_step_rollout(dev, args) if (args.rollout and rank == 0) else None
+    model_info = run_model_rollout(dev, args) if (args.rollout and rank == 0) else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -364,6 +365,8 @@ def run_m3(args):
         }
         if step_info is not None:
             line["step_rollout"] = step_info
+        if model_info is not None:
+            line["model_rollout"] = model_info
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -469,6 +472,73 @@ def run_step_rollout(dev, args):
         "gpu_launches": 32 * layers + 4 * layers,
         "note": "recurrence kernels only; the projection GEMMs of Mamba.step are not included",
     }
+
+
+def run_model_rollout(dev, args):
+    """Config 3 at model level: a 12-layer Search-Mamba-shaped ``Mamba``
+    (d_model=512, d_inner=1024, d_state=32 with 8 tracking lanes, mimo_p=2,
+    vocab 8192, the reference initialisation with a random seed), B rollout
+    rows advanced 32 steps by the fused step layer (embedding, RMSNorm, cuBLAS
+    projections, one launch for softplus/BCNorm/MIMO fold, one for the
+    recurrence with the gated output, out_proj fused with the residual add),
+    re-anchored every 8 steps by ``prime_cache`` over a fresh L=64 token
+    sequence (scan with return_state).  Token ids are uniform over the
+    8192-move space.  GEMMs run in TF32; state and recurrence in fp32."""
+    import torch
+    from redpanda_b200.mamba import Mamba, MambaConfig
+    layers, Bs = args.rollout_layers, args.rollout_batch
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        torch.manual_seed(11)
+        cfg = MambaConfig(d_model=512, n_layer=layers, d_state=32, n_track_state=8, mimo_p=2,
+                          vocab_size=8192)
+        model = Mamba(cfg).to(dev).eval()
+        g = torch.Generator(dev).manual_seed(13)
+        boards = [torch.randint(0, 8192, (Bs, 64), device=dev, generator=g) for _ in range(4)]
+        moves = torch.randint(0, 8192, (32, Bs), device=dev, generator=g)
+        stream = torch.cuda.current_stream(dev)
+
+        def rollout(ev=None):
+            cache = None
+            for s_ in range(32):
+                if s_ % 8 == 0:
+                    if ev is not None:
+                        ev.append(("anchor0", torch.cuda.Event(enable_timing=True)))
+                        ev[-1][1].record(stream)
+                    _, cache = model.prime_cache(boards[s_ // 8])
+                    if ev is not None:
+                        ev.append(("anchor1", torch.cuda.Event(enable_timing=True)))
+                        ev[-1][1].record(stream)
+                x, cache = model.step_fused_(token_id=moves[s_], cache=cache)
+            return x
+
+        with torch.no_grad():
+            rollout()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev = []
+            e0.record(stream)
+            rollout(ev)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        total = e0.elapsed_time(e1)
+        anchor = sum(ev[i][1].elapsed_time(ev[i + 1][1]) for i in range(0, len(ev), 2))
+        steps_ms = total - anchor
+        return {
+            "workload": f"c3 model level: {layers}-layer Mamba (d_model=512, d_inner=1024, "
+                        f"d_state=32 with 8 tracking lanes, mimo_p=2, vocab 8192), B={Bs}, "
+                        "32 lockstep steps, prime_cache re-anchor over L=64 every 8 steps",
+            "node_steps_per_s": Bs * 32 / (total / 1e3),
+            "ms_per_rollout": total,
+            "anchor_ms": anchor,
+            "step_ms_per_node_step_batch": steps_ms / 32,
+            "step_only_node_steps_per_s": Bs * 32 / (steps_ms / 1e3),
+            "precision": "TF32 projections, fp32 state and recurrence",
+            "state": "reference (h, dBu) cache pair",
+        }
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old_tf32
 
 
 def main():

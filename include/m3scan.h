@@ -15,6 +15,8 @@
  *                                                                          M3_DIR_BIDIR
  *   redpanda/engine/mamba.py:343,377-379    return_state (h_last, dBu_last) -> m3_scan_fwd h_last/dbu_last
  *   redpanda/engine/mamba.py:466-493        Mamba3Block.step recurrence -> m3_step
+ *   redpanda/engine/mamba.py:455-469        step inputs (softplus, BCNorm, MIMO fold) -> m3_step_inputs
+ *   redpanda/engine/mamba.py:490-497        step + gated output (y + u*D) * silu(z) -> m3_step_gated
  *
  * Shapes (B batch, L length, D = d_inner, N = d_state, n_rot rotational lanes,
  * N - n_rot tracking lanes):
@@ -158,6 +160,35 @@ M3_API int m3_step_factored(const m3_step_desc* desc, float* h, const float* fac
             float* fac_next, const void* delta, const void* u, const void* Bc, const void* Cc,
             const float* A_real_p, const float* A_imag_p, const float* track_p,
             float* y, void* stream);
+
+/* The per-token step inputs from the layer's projection outputs, in one launch.
+ * Replaces the elementwise part of Mamba3Block.step (mamba.py:455-469):
+ *   delta (B, D)  = softplus(dt), torch's threshold 20
+ *   Bc, Cc (B, N) = sum over the p MIMO columns of BCNorm(B_raw), BCNorm(C_raw)
+ * with BCNorm(x) = x * rsqrt(mean(x^2) + eps) * w over the N*p vector
+ * (mamba.py:82-89, 297-299, 336-337).
+ *   dt     (B, ld_dt) float32: dt_proj(dt_raw) including its bias
+ *   xbc    (B, ld_x)  float32: rows of x_proj's output; B_raw starts at column
+ *          off_b and C_raw at off_c, N*p columns each
+ *   wb, wc (N*p,) float32 BCNorm weights, or both NULL (use_bcnorm=False: plain sum)
+ * desc->n_rot, dtype_du and dtype_bc are ignored; all outputs are float32. */
+M3_API int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p,
+            const float* dt, int64_t ld_dt, const float* xbc, int64_t ld_x,
+            int32_t off_b, int32_t off_c, const float* wb, const float* wc, float eps,
+            float* delta, float* Bc, float* Cc, void* stream);
+
+/* m3_step (dbu != NULL) or m3_step_factored (fac_prev, fac_next != NULL, dbu
+ * NULL) whose output is the layer's gated activation instead of y
+ * (mamba.py:493-497):
+ *   out (B, D) float32 = (y + u * d_skip) * silu(z),   silu(z) = z / (1 + exp(-z))
+ *   z       (B, ld_z) float32: the z half of in_proj's output (before silu)
+ *   d_skip  (D,) float32: the layer's skip weight D
+ * The state update is identical to m3_step / m3_step_factored. */
+M3_API int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu,
+            const float* fac_prev, float* fac_next, const void* delta, const void* u,
+            const void* Bc, const void* Cc, const float* A_real_p, const float* A_imag_p,
+            const float* track_p, const float* z, int64_t ld_z, const float* d_skip,
+            float* out, void* stream);
 
 /* Size of the scratch buffer built into the library for m3_scan_bwd_noalloc. */
 #define M3_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)

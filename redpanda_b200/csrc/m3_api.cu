@@ -275,7 +275,9 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
 static int step_common(const m3_step_desc* desc, float* h, float* dbu, const float* fac_prev,
                        float* fac_next, const void* delta, const void* u, const void* Bc,
                        const void* Cc, const float* A_real_p, const float* A_imag_p,
-                       const float* track_p, float* y, void* stream) {
+                       const float* track_p, float* y, void* stream,
+                       const float* z = nullptr, int64_t ld_z = 0,
+                       const float* d_skip = nullptr) {
   if (!desc) return M3_ERR_NULL;
   if (desc->batch < 1 || desc->d_inner < 1 || desc->d_state < 1 || desc->d_state > kMaxState ||
       desc->n_rot < 0 || desc->n_rot > desc->d_state)
@@ -320,6 +322,8 @@ static int step_common(const m3_step_desc* desc, float* h, float* dbu, const flo
            aligned(delta, 16) && aligned(u, 16) && aligned(Bc, 16) && aligned(Cc, 16) &&
            (!factored || (aligned(fac_prev, 16) && aligned(fac_next, 16))) &&
            getenv("M3_NO_BULK") == nullptr;
+  p.gated = z != nullptr;
+  p.z = z; p.ld_z = ld_z; p.d_skip = d_skip;
   p.err = device_err_ptr();
   cudaError_t e = launch_step(t, p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
@@ -339,6 +343,45 @@ int m3_step_factored(const m3_step_desc* desc, float* h, const float* fac_prev, 
   if (!fac_next) return M3_ERR_NULL;
   return step_common(desc, h, nullptr, fac_prev, fac_next, delta, u, Bc, Cc, A_real_p, A_imag_p,
                      track_p, y, stream);
+}
+
+int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu, const float* fac_prev,
+                  float* fac_next, const void* delta, const void* u, const void* Bc,
+                  const void* Cc, const float* A_real_p, const float* A_imag_p,
+                  const float* track_p, const float* z, int64_t ld_z, const float* d_skip,
+                  float* out, void* stream) {
+  if (!desc || !z || !d_skip) return M3_ERR_NULL;
+  if ((dbu != nullptr) == (fac_next != nullptr)) return M3_ERR_NULL;   // exactly one state form
+  if (ld_z < desc->d_inner) return M3_ERR_SHAPE;
+  if (!aligned(z, 4) || !aligned(d_skip, 4)) return M3_ERR_ALIGN;
+  return step_common(desc, h, dbu, fac_prev, fac_next, delta, u, Bc, Cc, A_real_p, A_imag_p,
+                     track_p, out, stream, z, ld_z, d_skip);
+}
+
+int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const float* dt, int64_t ld_dt,
+                   const float* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
+                   const float* wb, const float* wc, float eps, float* delta, float* Bc,
+                   float* Cc, void* stream) {
+  if (!desc) return M3_ERR_NULL;
+  const int64_t np = (int64_t)desc->d_state * mimo_p;
+  if (desc->batch < 1 || desc->d_inner < 1 || desc->d_state < 1 || mimo_p < 1 ||
+      ld_dt < desc->d_inner || off_b < 0 || off_c < 0 || off_b + np > ld_x ||
+      off_c + np > ld_x || !(eps >= 0.f))
+    return M3_ERR_SHAPE;
+  if (!dt || !xbc || !delta || !Bc || !Cc || ((wb == nullptr) != (wc == nullptr)))
+    return M3_ERR_NULL;
+  if (!aligned(dt, 4) || !aligned(xbc, 4) || !aligned(delta, 4) || !aligned(Bc, 4) ||
+      !aligned(Cc, 4) || (wb && (!aligned(wb, 4) || !aligned(wc, 4))))
+    return M3_ERR_ALIGN;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  InputsParams p;
+  memset(&p, 0, sizeof(p));
+  p.dt = dt; p.ld_dt = ld_dt; p.xbc = xbc; p.ld_x = ld_x; p.off_b = off_b; p.off_c = off_c;
+  p.wb = wb; p.wc = wc; p.eps = eps; p.delta = delta; p.Bc = Bc; p.Cc = Cc;
+  p.B = desc->batch; p.D = desc->d_inner; p.N = desc->d_state; p.P = mimo_p;
+  cudaError_t e = launch_step_inputs(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 
 int m3_device_error(int32_t* code, int32_t clear) {

@@ -63,6 +63,9 @@ struct StepParams {
   int vec_bc;                                 // Bc/Cc 16-byte aligned: vector row loads
   int vec_fac;                                // factors 16-byte aligned, D % 4 == 0
   int bulk;                                   // pipelined bulk-copy kernel eligible
+  int gated;                                  // y -> (y + u*d_skip) * silu(z)
+  const float* z; long long ld_z;             // (B, ld_z) pre-activation gate
+  const float* d_skip;                        // (D,) skip weight
   const void* delta; const void* u; const void* Bc; const void* Cc;
   const float* Ar; const float* Ai; const float* Tk;
   float* y;
@@ -85,6 +88,17 @@ cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s);
 cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s);
 cudaError_t launch_bwd_reduce(const Tile& t, const ReduceParams& p, cudaStream_t s);
 cudaError_t launch_step(const Tile& t, const StepParams& p, cudaStream_t s);
+
+struct InputsParams {
+  const float* dt; long long ld_dt;       // (B, ld_dt): dt_proj output before softplus
+  const float* xbc; long long ld_x;       // (B, ld_x): row of x_proj output
+  int off_b, off_c;                       // column offsets of B_raw and C_raw (N*p each)
+  const float* wb; const float* wc;       // (N*p,) BCNorm weights
+  float eps;
+  float* delta; float* Bc; float* Cc;     // (B, D), (B, N), (B, N)
+  int B, D, N, P;
+};
+cudaError_t launch_step_inputs(const InputsParams& p, cudaStream_t s);
 
 // device error word of the current device
 int* device_err_ptr();

@@ -97,6 +97,16 @@ __device__ __forceinline__ void ld_vec_bf16(const __nv_bfloat16* src, float* v) 
 
 constexpr int vec_width(int n) { return n % 4 == 0 ? 4 : (n % 2 == 0 ? 2 : 1); }
 
+// Output of one (row, channel): y, or with the gated epilogue of
+// Mamba3Block.step (mamba.py:493-497) (y + u*D) * silu(z), in that rounding order;
+// silu(z) = z / (1 + exp(-z)).
+__device__ __forceinline__ float step_out(const StepParams& p, float y, float u, float ds,
+                                          float z) {
+  if (!p.gated) return y;
+  const float sz = __fdiv_rn(z, __fadd_rn(1.0f, expf(-z)));
+  return __fmul_rn(__fadd_rn(y, __fmul_rn(u, ds)), sz);
+}
+
 template <int R, int T, bool FACT>
 __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_kernel(const StepParams p) {
   using LM = LaneMap<R, T>;
@@ -239,7 +249,9 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_kernel(
       H[j] = cell_update(tk[j - R], P, du, Bv[j]);
     }
     const float tot = __fmul_rn(0.5f, quad_sum(y_partial<NL>(H, Cv)));
-    if (q == 0 && dok) p.y[rd] = tot;
+    if (q == 0 && dok)
+      p.y[rd] = step_out(p, tot, uu, p.gated ? p.d_skip[d] : 0.f,
+                         p.gated ? p.z[(size_t)b * p.ld_z + d] : 0.f);
 
     float hs[NL], ds[NL];
 #pragma unroll
@@ -348,6 +360,7 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_bulk_ke
 
   float a2[RR], ai[RR], tk[TT];
   float maxai = 0.f;
+  const float dskip = p.gated ? p.d_skip[d] : 0.f;
 #pragma unroll
   for (int j = 0; j < NL; ++j) {
     const int m = LM::mem_lane(q, j, p.NR, p.NT);   // dense tile: never virtual
@@ -457,6 +470,12 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_bulk_ke
       dl2 = make_float2(dlv[0], dlv[1]);
       uu2 = make_float2(uv[0], uv[1]);
     }
+    // gated epilogue: z of the pair, loaded now, used after the recurrence
+    float zz[2] = {0.f, 0.f};
+    if (p.gated && q == 0) {
+      zz[0] = p.z[(size_t)b0 * p.ld_z + d];
+      if (two) zz[1] = p.z[(size_t)(b0 + 1) * p.ld_z + d];
+    }
     // every thread has read stage s: it may be refilled (or the launch gives up)
     if (__syncthreads_or(!ok)) { fail_at = i; break; }
     if (tid == 0 && i + kBulkStages < n) issue(i + kBulkStages);
@@ -518,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_bulk_ke
         if constexpr (R > 0) st_vec<R, VR>(dout + q * R, dsv);
         if constexpr (T > 0) st_vec<T, VT>(dout + 4 * R + q * T, dsv + R);
       }
-      if (q == 0) p.y[b * D + d] = r ? y1 : y0;
+      if (q == 0) p.y[b * D + d] = step_out(p, r ? y1 : y0, r ? uu2.y : uu2.x, dskip, zz[r]);
     }
   }
 

@@ -191,6 +191,50 @@ class Mamba3Block(nn.Module):
         y = y + u * self.D
         return self.out_proj(y * F.silu(z)), state
 
+    def step_params(self):
+        """Padded (A_real, A_imag, track) of the step kernels, cached until a
+        parameter changes (tensor version counters)."""
+        cfg = self.config
+        srcs = [t for t in (getattr(self, "A_log_mag", None), getattr(self, "A_phase", None),
+                            getattr(self, "A_log", None), getattr(self, "track_theta", None))
+                if t is not None]
+        key = tuple((t.data_ptr(), t._version) for t in srcs)
+        cached = getattr(self, "_step_params_cache", None)
+        if cached is None or cached[0] != key:
+            with torch.no_grad():
+                A_real, A_imag = self._compute_A()
+                track = self._track_gate() if cfg.n_track_state > 0 else None
+                dev = self.D.device
+                padded = tuple(t.to(torch.float32).contiguous() for t in S.pad_params(
+                    A_real, A_imag, track, cfg.n_rot_state, cfg.d_state, cfg.d_inner, dev))
+            cached = (key, padded)
+            self._step_params_cache = cached
+        return cached[1]
+
+    def step_fused_(self, x_t, state):
+        """O(1) step of the fused step layer, in place on ``state``.
+
+        ``state``: (h, dBu) (the reference cache pair) or (h, fac_prev, fac_next)
+        (the factored state; swap the factor buffers between steps).  The
+        projections are cuBLAS GEMMs; softplus, BCNorm and the MIMO fold run in
+        one launch (``m3_step_inputs``) and the recurrence with the gated output
+        (y + u*D) * silu(z) in another (``m3_step_gated_``).  Returns the
+        out_proj input (B, d_inner); the caller applies out_proj (mamba.py:497).
+        """
+        cfg = self.config
+        n, p = cfg.d_state, cfg.mimo_p
+        xz = self.in_proj(x_t)
+        u = F.silu(xz[:, :cfg.d_inner])
+        x_dbl = self.x_proj(u)
+        dt = self.dt_proj(x_dbl[:, :cfg.dt_rank])
+        bw = self.b_norm.weight if cfg.use_bcnorm else None
+        cw = self.c_norm.weight if cfg.use_bcnorm else None
+        eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
+        delta, bc, cc = S.m3_step_inputs(dt, x_dbl, cfg.dt_rank, cfg.dt_rank + n * p, bw, cw,
+                                         eps, n, p)
+        return S.m3_step_gated_(state, delta, u, bc, cc, self.step_params(), cfg.n_rot_state,
+                                xz[:, cfg.d_inner:], self.D)
+
     def step(self, x_t, state=None):
         """Functional O(1) step (mamba.py:427-498): returns (out, (h, dBu_t))."""
         cfg = self.config
@@ -266,6 +310,20 @@ class Mamba(nn.Module):
         for i, layer in enumerate(self.layers):
             delta, _ = layer["mixer"].step_(layer["norm"](x), cache[i])
             x = x + delta
+        return (self.norm_f(x) if apply_final_norm else x), cache
+
+    def step_fused_(self, token_id=None, cache=None, input_embed=None, apply_final_norm=True):
+        """Lockstep step of every layer on the fused step layer, in place on
+        ``cache`` (entries (h, dBu) or (h, fac_prev, fac_next)); out_proj and
+        the residual add are one GEMM (addmm).  Returns (hidden, cache)."""
+        assert not self.config.bidirectional, "step() requires a causal model"
+        x = self._embed_step(token_id, input_embed)
+        for i, layer in enumerate(self.layers):
+            mixer, norm = layer["mixer"], layer["norm"]
+            g = mixer.step_fused_(norm(x), cache[i])
+            op = mixer.out_proj
+            x = (torch.addmm(x, g, op.weight.t()) if op.bias is None
+                 else torch.addmm(x + op.bias, g, op.weight.t()))
         return (self.norm_f(x) if apply_final_norm else x), cache
 
     def prime_cache(self, input_ids):

@@ -13,6 +13,9 @@ reference's fused-scan path:
 * ``m3_step_`` -- the in-place O(1) step recurrence (mamba.py:466-493)
 * ``m3_step_factored_`` -- the same step on the factored (h, [delta*u | B])
   state, half the HBM traffic, bit-identical results
+* ``m3_step_inputs`` / ``m3_step_gated_`` -- the fused step layer: softplus,
+  BCNorm and MIMO fold in one launch (mamba.py:455-469), the recurrence with
+  the gated output (y + u*D) * silu(z) in another (mamba.py:490-497)
 
 Registering this module as ``triton_scan`` in ``sys.modules`` routes the
 unmodified reference ``mamba.py`` (with ``use_triton_scan=True``) through
@@ -326,6 +329,73 @@ def m3_step_factored_(h, fac_prev, fac_next, delta_t, u_t, Bc_t, Cc_t, A_real, A
                                         bb.data_ptr(), cc.data_ptr(), ar.data_ptr(),
                                         ai.data_ptr(), tk.data_ptr(), y.data_ptr(), _stream(dev)))
     return y
+
+
+def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mimo_p):
+    """softplus(dt) and the BCNorm'ed, MIMO-folded B and C of one token, one launch.
+
+    dt: (B, D) float32, dt_proj output with its bias; x_dbl: (B, K) float32 rows
+    of x_proj's output, B_raw at column ``off_b`` and C_raw at ``off_c``
+    (N*p columns each); b_weight / c_weight: BCNorm weights (N*p,) or None
+    (use_bcnorm=False).  Returns (delta (B, D), Bc (B, N), Cc (B, N)), float32:
+    mamba.py:455-469 and 336-337 for one token.
+    """
+    lib = _lib.load()
+    dev = _require_cuda(dt, x_dbl)
+    if dt.dtype != torch.float32 or x_dbl.dtype != torch.float32:
+        raise TypeError("m3_step_inputs: dt and x_dbl must be float32")
+    if dt.stride(-1) != 1 or x_dbl.stride(-1) != 1:
+        raise ValueError("m3_step_inputs: rows of dt and x_dbl must be contiguous")
+    B, D = dt.shape
+    wb = wc = None
+    if b_weight is not None:
+        wb = b_weight.detach().to(torch.float32).contiguous()
+        wc = c_weight.detach().to(torch.float32).contiguous()
+    delta = torch.empty(B, D, device=dev, dtype=torch.float32)
+    bc = torch.empty(B, n_state, device=dev, dtype=torch.float32)
+    cc = torch.empty_like(bc)
+    desc = StepDesc(B, D, n_state, 0, M3_F32, M3_F32)
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3_step_inputs(desc, int(mimo_p), dt.data_ptr(), dt.stride(0),
+                                      x_dbl.data_ptr(), x_dbl.stride(0), int(off_b), int(off_c),
+                                      ctypes_ptr(wb), ctypes_ptr(wc), float(eps),
+                                      delta.data_ptr(), bc.data_ptr(), cc.data_ptr(),
+                                      _stream(dev)))
+    return delta, bc, cc
+
+
+def m3_step_gated_(state, delta_t, u_t, Bc_t, Cc_t, params, n_rot, z, d_skip):
+    """In-place O(1) step whose output is the layer's gated activation
+    (y + u*D) * silu(z) (mamba.py:490-497), (B, D) float32.
+
+    ``state`` is (h, dbu) (the reference cache pair) or (h, fac_prev, fac_next)
+    (the factored state; the caller swaps the two factor buffers between steps).
+    ``params`` are the padded (A_real, A_imag, track) of :func:`pad_params`,
+    float32 and contiguous; ``z`` (B, D) may be a row-strided view.
+    """
+    lib = _lib.load()
+    h = state[0]
+    dev = _require_cuda(h, delta_t, u_t, Bc_t, Cc_t, z, d_skip)
+    B, D, N = h.shape
+    if z.stride(-1) != 1:
+        raise ValueError("m3_step_gated_: rows of z must be contiguous")
+    dl, uu, dt_du = _prep_pair(delta_t, u_t)
+    bb, cc, dt_bc = _prep_pair(Bc_t, Cc_t)
+    ar, ai, tk = params
+    ds = d_skip.detach().to(torch.float32).contiguous()
+    out = torch.empty(B, D, device=dev, dtype=torch.float32)
+    desc = StepDesc(B, D, N, int(n_rot), dt_du, dt_bc)
+    if len(state) == 2:
+        dbu, fa, fb = state[1], None, None
+    else:
+        dbu, fa, fb = None, state[1], state[2]
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3_step_gated(desc, h.data_ptr(), ctypes_ptr(dbu), ctypes_ptr(fa),
+                                     ctypes_ptr(fb), dl.data_ptr(), uu.data_ptr(),
+                                     bb.data_ptr(), cc.data_ptr(), ar.data_ptr(), ai.data_ptr(),
+                                     tk.data_ptr(), z.data_ptr(), z.stride(0), ds.data_ptr(),
+                                     out.data_ptr(), _stream(dev)))
+    return out
 
 
 def m3_step(state, delta_t, u_t, Bc_t, Cc_t, A_real, A_imag, track, n_rot, n_state):

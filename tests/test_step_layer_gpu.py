@@ -1,0 +1,129 @@
+"""The fused step layer: m3_step_inputs (softplus, BCNorm, MIMO fold in one
+launch) and m3_step_gated (the step with the gated output (y + u*D) * silu(z)),
+against the torch formulation of Mamba3Block.step (redpanda/engine/mamba.py:427-498)."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from redpanda_b200 import scan as S
+from redpanda_b200.mamba import Mamba, MambaConfig
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-6
+
+
+def _rel(a, b):
+    a, b = a.detach().double(), b.detach().double()
+    den = b.abs().max().item()
+    return (a - b).abs().max().item() / (den if den > 0 else 1.0)
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+@pytest.mark.parametrize("bcnorm", [True, False])
+@pytest.mark.parametrize("n,p", [(32, 2), (16, 4), (12, 2)])
+def test_step_inputs_match_torch(bcnorm, n, p):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    B, D, R = 37, 96, 8
+    dt = torch.randn(B, D, device="cuda", generator=g) * 8     # both softplus branches
+    x_dbl = torch.randn(B, R + 2 * n * p, device="cuda", generator=g)
+    wb = torch.rand(n * p, device="cuda", generator=g) + 0.5 if bcnorm else None
+    wc = torch.rand(n * p, device="cuda", generator=g) + 0.5 if bcnorm else None
+    eps = 1e-5
+    delta, bc, cc = S.m3_step_inputs(dt, x_dbl, R, R + n * p, wb, wc, eps, n, p)
+    ref_d = F.softplus(dt)
+    braw, craw = x_dbl[:, R:R + n * p], x_dbl[:, R + n * p:]
+    if bcnorm:
+        braw = braw * torch.rsqrt(braw.pow(2).mean(-1, keepdim=True) + eps) * wb
+        craw = craw * torch.rsqrt(craw.pow(2).mean(-1, keepdim=True) + eps) * wc
+    assert _rel(delta, ref_d) <= TOL
+    assert _rel(bc, braw.reshape(B, n, p).sum(-1)) <= TOL
+    assert _rel(cc, craw.reshape(B, n, p).sum(-1)) <= TOL
+
+
+@pytest.mark.parametrize("B,D,N,n_track", [(37, 256, 32, 8), (6, 40, 64, 16), (9, 128, 32, 16)])
+def test_gated_step_equals_step_and_torch_epilogue(B, D, N, n_track):
+    """Same state bits as m3_step_ / m3_step_factored_; output (y + u*D)*silu(z)."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    n_rot = N - n_track
+    A_real = -torch.exp(torch.randn(D, n_rot, device="cuda", generator=g) * 0.5)
+    A_imag = (torch.rand(D, n_rot, device="cuda", generator=g) * 2 - 1) * 3.14159
+    track = torch.tanh(torch.randn(D, n_track, device="cuda", generator=g))
+    params = tuple(t.contiguous() for t in S.pad_params(A_real, A_imag, track, n_rot, N, D,
+                                                        torch.device("cuda")))
+    h0 = torch.randn(B, D, N, device="cuda", generator=g) * 0.1
+    fa0 = torch.randn(B, D + N, device="cuda", generator=g)
+    d0 = fa0[:, :D, None] * fa0[:, None, D:]
+    d_skip = torch.randn(D, device="cuda", generator=g)
+    hr, dr = h0.clone(), d0.clone()
+    hg, dg = h0.clone(), d0.clone()
+    hf, fa = h0.clone(), fa0.clone()
+    fb = torch.empty_like(fa)
+    for _ in range(3):
+        delta = F.softplus(torch.randn(B, D, device="cuda", generator=g) * 0.5 - 2)
+        u = torch.randn(B, D, device="cuda", generator=g)
+        bc = torch.randn(B, N, device="cuda", generator=g)
+        cc = torch.randn(B, N, device="cuda", generator=g)
+        xz = torch.randn(B, 2 * D, device="cuda", generator=g)
+        z = xz[:, D:]                                          # row stride 2D
+        y = S.m3_step_(hr, dr, delta, u, bc, cc, A_real, A_imag, track, n_rot, N)
+        ref = (y + u * d_skip) * F.silu(z)
+        out = S.m3_step_gated_((hg, dg), delta, u, bc, cc, params, n_rot, z, d_skip)
+        outf = S.m3_step_gated_((hf, fa, fb), delta, u, bc, cc, params, n_rot, z, d_skip)
+        fa, fb = fb, fa
+        assert torch.equal(hg, hr) and torch.equal(dg, dr) and torch.equal(hf, hr)
+        assert torch.equal(out, outf)
+        assert _rel(out, ref) <= TOL
+    assert S.device_error() == 0
+
+
+def test_model_fused_step_matches_unfused_step_and_forward():
+    """Config-3-like layers: the fused step layer reproduces Mamba.step_ (torch
+    projections + m3_step_) and, from a primed cache, the full forward."""
+    torch.manual_seed(2)
+    cfg = MambaConfig(d_model=64, n_layer=2, d_state=32, n_track_state=8, mimo_p=2,
+                      vocab_size=256)
+    m = Mamba(cfg).cuda().eval()
+    ids = torch.randint(0, 256, (5, 12), device="cuda")
+    with torch.no_grad():
+        full = m(ids)
+        _, cache = m.prime_cache(ids[:, :8])
+        cache_u = [(h.clone(), d.clone()) for h, d in cache]
+        cache_f = [(h.clone(), d.clone()) for h, d in cache]
+        for t in range(8, 12):
+            hu, cache_u = m.step_(token_id=ids[:, t], cache=cache_u)
+            hf, cache_f = m.step_fused_(token_id=ids[:, t], cache=cache_f)
+            assert _rel(hf, hu) <= 1e-5
+            assert torch.allclose(hf, full[:, t], atol=1e-5)
+        for (h1, d1), (h2, d2) in zip(cache_u, cache_f):
+            assert _rel(h2, h1) <= 1e-5 and _rel(d2, d1) <= 1e-5
+
+
+def test_model_fused_step_factored_state_equals_full_state():
+    torch.manual_seed(4)
+    cfg = MambaConfig(d_model=64, n_layer=3, d_state=32, n_track_state=8, mimo_p=2,
+                      vocab_size=256)
+    m = Mamba(cfg).cuda().eval()
+    B, D, N = 6, cfg.d_inner, cfg.d_state
+    ids = torch.randint(0, 256, (B, 7), device="cuda")
+    full = [(torch.zeros(B, D, N, device="cuda"), torch.zeros(B, D, N, device="cuda"))
+            for _ in range(cfg.n_layer)]
+    fac = [[torch.zeros(B, D, N, device="cuda"), torch.zeros(B, D + N, device="cuda"),
+            torch.zeros(B, D + N, device="cuda")] for _ in range(cfg.n_layer)]
+    with torch.no_grad():
+        for t in range(7):
+            a, _ = m.step_fused_(token_id=ids[:, t], cache=full)
+            b, _ = m.step_fused_(token_id=ids[:, t], cache=fac)
+            for st in fac:
+                st[1], st[2] = st[2], st[1]
+            assert torch.equal(a, b)
+        for (h1, _), (h2, _, _) in zip(full, fac):
+            assert torch.equal(h1, h2)
