@@ -17,6 +17,7 @@
  *   redpanda/engine/mamba.py:466-493        Mamba3Block.step recurrence -> m3_step
  *   redpanda/engine/mamba.py:455-469        step inputs (softplus, BCNorm, MIMO fold) -> m3_step_inputs
  *   redpanda/engine/mamba.py:490-497        step + gated output (y + u*D) * silu(z) -> m3_step_gated
+ *   redpanda/engine/mamba.py:262-265        (y + u*D) * silu(z) after a scan -> m3_gate
  *
  * Shapes (B batch, L length, D = d_inner, N = d_state, n_rot rotational lanes,
  * N - n_rot tracking lanes):
@@ -188,6 +189,17 @@ M3_API int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu,
             const float* fac_prev, float* fac_next, const void* delta, const void* u,
             const void* Bc, const void* Cc, const float* A_real_p, const float* A_imag_p,
             const float* track_p, const float* z, int64_t ld_z, const float* d_skip,
+            float* out, void* stream);
+
+/* The layer's gated activation after a scan (mamba.py:262-265), elementwise
+ * over (rows, D) = (B*L, D):
+ *   out = (y + coef * (u * d_skip)) * silu(z),   silu(z) = z / (1 + exp(-z))
+ *   y (rows, D) float32 scan output; u (rows, D) of dtype_u (the SSM input);
+ *   z (rows, ld_z) float32, the z half of in_proj's output; d_skip (D,) float32;
+ *   coef 1 for one direction, 2 for the bidirectional pair (which adds u*D once
+ *   per direction, mamba.py:256-260).  out may equal y (in place). */
+M3_API int m3_gate(int64_t rows, int32_t d_inner, const float* y, const void* u,
+            int32_t dtype_u, const float* z, int64_t ld_z, const float* d_skip, float coef,
             float* out, void* stream);
 
 /* Size of the scratch buffer built into the library for m3_scan_bwd_noalloc. */

@@ -384,6 +384,25 @@ int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const float* dt, in
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 
+int m3_gate(int64_t rows, int32_t d_inner, const float* y, const void* u, int32_t dtype_u,
+            const float* z, int64_t ld_z, const float* d_skip, float coef, float* out,
+            void* stream) {
+  if (rows < 1 || d_inner < 1 || ld_z < d_inner) return M3_ERR_SHAPE;
+  if (!dtype_ok(dtype_u)) return M3_ERR_DTYPE;
+  if (!y || !u || !z || !d_skip || !out) return M3_ERR_NULL;
+  if (!aligned(y, 4) || !aligned(u, dsize(dtype_u)) || !aligned(z, 4) || !aligned(d_skip, 4) ||
+      !aligned(out, 4))
+    return M3_ERR_ALIGN;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  GateParams p;
+  memset(&p, 0, sizeof(p));
+  p.y = y; p.u = u; p.u_bf16 = dtype_u == M3_BF16; p.z = z; p.ld_z = ld_z;
+  p.d_skip = d_skip; p.coef = coef; p.out = out; p.rows = rows; p.D = d_inner;
+  cudaError_t e = launch_gate(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
 int m3_device_error(int32_t* code, int32_t clear) {
   if (!code) return M3_ERR_NULL;
   int rc = check_device();

@@ -100,6 +100,15 @@ struct InputsParams {
 };
 cudaError_t launch_step_inputs(const InputsParams& p, cudaStream_t s);
 
+struct GateParams {
+  const float* y; const void* u; int u_bf16;
+  const float* z; long long ld_z;
+  const float* d_skip; float coef;
+  float* out;
+  long long rows; int D;
+};
+cudaError_t launch_gate(const GateParams& p, cudaStream_t s);
+
 // device error word of the current device
 int* device_err_ptr();
 

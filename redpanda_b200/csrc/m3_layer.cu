@@ -8,6 +8,11 @@
 // RMSNorm(x) = x * rsqrt(mean(x^2) + eps) * w (mamba.py:82-89), applied per
 // element in that rounding order; softplus(x) = x for x > 20, else
 // log1p(exp(x)) (torch's threshold).  One warp normalises one row.
+//
+// Also the gated activation after a scan (mamba.py:262-265):
+//   out = (y + coef * u*D) * silu(z),  coef 1 (one direction) or 2 (the
+//   bidirectional pair adds u*D once per direction).
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include "m3_internal.h"
@@ -64,7 +69,36 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) step_inputs_kernel(const Inp
   }
 }
 
+// out = (y + coef*(u*d_skip)) * silu(z) over (rows, D), grid-stride over the
+// elements (consecutive threads take consecutive channels: coalesced rows).
+__global__ void gate_kernel(const GateParams p) {
+  const size_t D = (size_t)p.D;
+  const size_t total = (size_t)p.rows * D;
+  auto one = [&](size_t i) {
+    const size_t r = i / D, d = i - r * D;
+    const float u = p.u_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.u)[i])
+                             : static_cast<const float*>(p.u)[i];
+    const float z = p.z[r * p.ld_z + d];
+    const float sz = __fdiv_rn(z, __fadd_rn(1.0f, expf(-z)));
+    const float ud = __fmul_rn(p.coef, __fmul_rn(u, p.d_skip[d]));
+    p.out[i] = __fmul_rn(__fadd_rn(p.y[i], ud), sz);
+  };
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += stride) one(i);
+}
+
 }  // namespace
+
+cudaError_t launch_gate(const GateParams& p, cudaStream_t s) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t total = (size_t)p.rows * p.D;
+  size_t grid = (total + 255) / 256;
+  if (grid > (size_t)sms * 16) grid = (size_t)sms * 16;
+  gate_kernel<<<(unsigned)grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_step_inputs(const InputsParams& p, cudaStream_t s) {
   const int grid = (p.B + kRowsPerCta - 1) / kRowsPerCta;

@@ -66,6 +66,8 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(d))
 
     def forward(self, x):
+        if not torch.is_grad_enabled():   # inference: torch's fused kernel, same formula
+            return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
 
 
@@ -154,8 +156,44 @@ class Mamba3Block(nn.Module):
         return self._selective_scan_trapezoidal(u, delta, A_real, A_imag, B, C, self.D,
                                                 return_state=return_state)
 
+    def _forward_inference(self, x, return_state):
+        """No-grad layer forward on the fused kernels (mamba.py:231-282): after
+        the in_proj / x_proj / dt_proj GEMMs, softplus + BCNorm + MIMO fold of
+        every token is one launch (m3_step_inputs over B*L rows), the scan (or
+        the fused bidirectional pair) another, (y + u*D)*silu(z) a third
+        (m3_gate), then out_proj."""
+        cfg = self.config
+        n, p, d_in = cfg.d_state, cfg.mimo_p, cfg.d_inner
+        xz = self.in_proj(x)
+        u = F.silu(xz[..., :d_in])
+        x_dbl = self.x_proj(u)
+        dt = self.dt_proj(x_dbl[..., :cfg.dt_rank])
+        lead = u.shape[:-1]
+        rows = u.numel() // d_in
+        bw = self.b_norm.weight if cfg.use_bcnorm else None
+        cw = self.c_norm.weight if cfg.use_bcnorm else None
+        eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
+        delta, bc, cc = S.m3_step_inputs(dt.reshape(rows, d_in), x_dbl.reshape(rows, -1),
+                                         cfg.dt_rank, cfg.dt_rank + n * p, bw, cw, eps, n, p)
+        delta, bc, cc = delta.view(*lead, d_in), bc.view(*lead, n), cc.view(*lead, n)
+        track = self._track_gate() if cfg.n_track_state > 0 else None
+        A_real, A_imag = self._compute_A()
+        args = (delta, u, bc, cc, A_real, A_imag, track, cfg.n_rot_state, n)
+        state = None
+        if cfg.bidirectional:
+            y, coef = S.m3_bidir_scan(*args), 2.0
+        elif return_state:
+            (y, state), coef = S.m3_scan_with_state(*args), 1.0
+        else:
+            y, coef = S.m3_trapezoidal_scan(*args), 1.0
+        y = S.m3_gate(y, u, xz[..., d_in:], self.D, coef, out=y)
+        out = self.out_proj(y)
+        return (out, state) if return_state else out
+
     def forward(self, x):
         """mamba.py:231-267; the bidirectional pair is one fused launch."""
+        if not torch.is_grad_enabled():
+            return self._forward_inference(x, False)
         x_branch, z = self.in_proj(x).chunk(2, dim=-1)
         x_branch = F.silu(x_branch)
         if not self.config.bidirectional:
@@ -168,6 +206,8 @@ class Mamba3Block(nn.Module):
 
     def forward_with_state(self, x):
         """mamba.py:269-282: output and the (h_last, dBu_last) state."""
+        if not torch.is_grad_enabled():
+            return self._forward_inference(x, True)
         x_branch, z = self.in_proj(x).chunk(2, dim=-1)
         x_branch = F.silu(x_branch)
         y, state = self.ssm(x_branch, return_state=True)

@@ -219,9 +219,35 @@ class _TrapezoidalScanFn(torch.autograd.Function):
                 dTk.to(ttk), None, None, None)
 
 
+def _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state):
+    """Forward only (no autograd record, no checkpoints): the inference path."""
+    lib = _lib.load()
+    dev = _require_cuda(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p)
+    dl, uu, dt_du = _prep_pair(delta, u)
+    bb, cc, dt_bc = _prep_pair(Bc, Cc)
+    ar, ai, tk = (x.detach().to(torch.float32).contiguous() for x in (Ar_p, Ai_p, Tk_p))
+    B, L, D = uu.shape
+    N = bb.shape[-1]
+    desc = ScanDesc(B, L, D, N, int(n_rot), dt_du, dt_bc, int(direction))
+    y = torch.empty(B, L, D, device=dev, dtype=torch.float32)
+    empty = torch.empty(0, device=dev)
+    h = dbu = None
+    if want_state:
+        h = torch.empty(B, D, N, device=dev, dtype=torch.float32)
+        dbu = torch.empty_like(h)
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3_scan_fwd(desc, dl.data_ptr(), uu.data_ptr(), bb.data_ptr(),
+                                   cc.data_ptr(), ar.data_ptr(), ai.data_ptr(), tk.data_ptr(),
+                                   y.data_ptr(), None, ctypes_ptr(h), ctypes_ptr(dbu),
+                                   _stream(dev)))
+    return (y, h, dbu) if want_state else (y, empty, empty)
+
+
 def _apply(delta, u, Bc, Cc, A_real, A_imag, track, n_rot, n_state, direction, want_state):
     d_inner = u.shape[-1]
     Ar_p, Ai_p, Tk_p = pad_params(A_real, A_imag, track, n_rot, n_state, d_inner, u.device)
+    if not torch.is_grad_enabled():
+        return _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state)
     return _TrapezoidalScanFn.apply(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p,
                                     n_rot, direction, want_state)
 
@@ -362,6 +388,28 @@ def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mi
                                       delta.data_ptr(), bc.data_ptr(), cc.data_ptr(),
                                       _stream(dev)))
     return delta, bc, cc
+
+
+def m3_gate(y, u, z, d_skip, coef=1.0, out=None):
+    """(y + coef*u*D) * silu(z) in one launch (mamba.py:262-265); y: (..., D)
+    float32 contiguous, u: (..., D) float32/bf16 contiguous, z: (..., D) with
+    contiguous rows (a view of in_proj's output).  ``out`` may be ``y``."""
+    lib = _lib.load()
+    dev = _require_cuda(y, u, z, d_skip)
+    D = y.shape[-1]
+    rows = y.numel() // D
+    if not (y.is_contiguous() and u.is_contiguous()) or z.stride(-1) != 1:
+        raise ValueError("m3_gate: y and u must be contiguous, z row-contiguous")
+    zz = z.reshape(rows, D) if z.dim() > 2 else z
+    if zz.stride(-1) != 1:
+        raise ValueError("m3_gate: z rows must be contiguous")
+    out = torch.empty_like(y) if out is None else out
+    ds = d_skip.detach().to(torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3_gate(rows, D, y.data_ptr(), u.data_ptr(), _dt_code(u.dtype),
+                               zz.data_ptr(), zz.stride(0), ds.data_ptr(), float(coef),
+                               out.data_ptr(), _stream(dev)))
+    return out
 
 
 def m3_step_gated_(state, delta_t, u_t, Bc_t, Cc_t, params, n_rot, z, d_skip):

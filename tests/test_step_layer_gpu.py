@@ -127,3 +127,41 @@ def test_model_fused_step_factored_state_equals_full_state():
             assert torch.equal(a, b)
         for (h1, _), (h2, _, _) in zip(full, fac):
             assert torch.equal(h1, h2)
+
+
+@pytest.mark.parametrize("coef", [1.0, 2.0])
+@pytest.mark.parametrize("udtype", [torch.float32, torch.bfloat16])
+def test_gate_matches_torch(coef, udtype):
+    g = torch.Generator(device="cuda").manual_seed(9)
+    B, L, D = 3, 17, 96
+    y = torch.randn(B, L, D, device="cuda", generator=g)
+    u = torch.randn(B, L, D, device="cuda", generator=g).to(udtype)
+    xz = torch.randn(B, L, 2 * D, device="cuda", generator=g)
+    d_skip = torch.randn(D, device="cuda", generator=g)
+    out = S.m3_gate(y, u, xz[..., D:], d_skip, coef)
+    ref = (y + coef * (u.float() * d_skip)) * F.silu(xz[..., D:])
+    assert _rel(out, ref) <= TOL
+
+
+@pytest.mark.parametrize("bidir", [False, True])
+def test_inference_forward_equals_autograd_forward(bidir):
+    """The no-grad layer forward (m3_step_inputs over B*L rows, scan, m3_gate)
+    reproduces the training-path forward; prime_cache likewise."""
+    torch.manual_seed(6)
+    cfg = MambaConfig(d_model=64, n_layer=2, d_state=32, n_track_state=8, mimo_p=2,
+                      vocab_size=256, bidirectional=bidir)
+    m = Mamba(cfg).cuda().eval()
+    ids = torch.randint(0, 256, (4, 21), device="cuda")
+    with torch.enable_grad():
+        ref = m(ids)
+    with torch.no_grad():
+        out = m(ids)
+    assert _rel(out, ref) <= 1e-5
+    if not bidir:
+        with torch.enable_grad():
+            fr, cr = m.prime_cache(ids)
+        with torch.no_grad():
+            fi, ci = m.prime_cache(ids)
+        assert _rel(fi, fr) <= 1e-5
+        for (h1, d1), (h2, d2) in zip(ci, cr):
+            assert _rel(h1, h2) <= 1e-5 and _rel(d1, d2) <= 1e-5
