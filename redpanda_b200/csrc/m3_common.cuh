@@ -94,6 +94,14 @@ __device__ __forceinline__ float2 cell_update2(float2 g, float2& P, float2 du, f
   return H;
 }
 
+// The same packed update with B already held as a (b, b) pair.
+__device__ __forceinline__ float2 cell_update2p(float2 g, float2& P, float2 du, float2 b) {
+  const float2 dbu = __fmul2_rn(du, b);
+  const float2 H = __ffma2_rn(g, P, dbu);
+  P = __fadd2_rn(H, dbu);
+  return H;
+}
+
 // Sum of a per-thread partial over the kQ threads of a channel group
 // (fixed pairing: (s0+s1)+(s2+s3) on every lane).
 __device__ __forceinline__ float quad_sum(float s) {

@@ -17,6 +17,8 @@
 #include "m3_stage.cuh"
 #include "m3_tiles.h"
 
+#include <type_traits>
+
 namespace m3 {
 namespace {
 
@@ -75,7 +77,7 @@ __device__ __forceinline__ void stage_y(float* s_y, const FwdParams& p, int b, i
 }
 
 #ifndef M3_FWD_UNROLL
-#define M3_FWD_UNROLL 1
+#define M3_FWD_UNROLL 2
 #endif
 constexpr int kFwdUnroll = M3_FWD_UNROLL;
 
@@ -89,8 +91,8 @@ constexpr int kFwdUnroll = M3_FWD_UNROLL;
 template <int NP, int DT, bool BULK>
 struct FwdSmem {
   static constexpr size_t du = (size_t)kCK * DT * 4;             // one buffer of delta or u
-  static constexpr size_t bc = (size_t)kCK * NP * 4;             // one buffer of B or C
-  static constexpr size_t braw = BULK ? 2 * 2 * bc : 0;          // [2][B|C][kCK][NP]
+  static constexpr size_t bc = (size_t)kCK * NP * 8;             // one buffer of B or C pairs
+  static constexpr size_t braw = BULK ? 2 * 2 * (size_t)kCK * NP * 4 : 0;   // [2][B|C][kCK][NP]
   static constexpr size_t off_y = 2 * 2 * du + 2 * 2 * bc + braw + 16;
   static size_t bytes(bool bidir) { return off_y + (bidir ? 2 * (size_t)kCK * DT * 4 : 0); }
 };
@@ -109,9 +111,11 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* s_dl = smem;                                 // [2][kCK*DT*4]
   unsigned char* s_u = s_dl + 2 * kCK * DT * 4;               // [2][kCK*DT*4]
-  float* s_b = reinterpret_cast<float*>(s_u + 2 * kCK * DT * 4);  // [2][kCK][NP]
-  float* s_c = s_b + 2 * kCK * NP;
-  float* s_braw = s_c + 2 * kCK * NP;                         // [2][B|C][kCK][NP] (BULK)
+  // B and C of each staged step in the padded lane layout, as (b, b) pairs so
+  // that packed instructions take them without a broadcast
+  float2* s_b = reinterpret_cast<float2*>(s_u + 2 * kCK * DT * 4);  // [2][kCK][NP]
+  float2* s_c = s_b + 2 * kCK * NP;
+  float* s_braw = reinterpret_cast<float*>(s_c + 2 * kCK * NP);     // [2][B|C][kCK][NP] (BULK)
   uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + SM::off_y - 16);   // [2] (BULK)
   float* s_y = reinterpret_cast<float*>(smem + SM::off_y);    // [2][kCK][DT] (bidir pass 2)
 
@@ -195,8 +199,8 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
       for (int e = 0; e < BCE; ++e) {
         const int i = tid + e * kThreads;
         if (i < kCK * NP) {
-          s_b[buf * kCK * NP + i] = rb[e];
-          s_c[buf * kCK * NP + i] = rc[e];
+          s_b[buf * kCK * NP + i] = f2(rb[e]);
+          s_c[buf * kCK * NP + i] = f2(rc[e]);
         }
       }
     };
@@ -240,8 +244,8 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
         const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
         const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * kCK + tt) * NP;
         const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * kCK + tt) * NP;
-        s_b[buf * kCK * NP + i] = n >= 0 ? ld_f(rb0, n, p.dt_bc) : 0.f;
-        s_c[buf * kCK * NP + i] = n >= 0 ? ld_f(rc0, n, p.dt_bc) : 0.f;
+        s_b[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rb0, n, p.dt_bc) : 0.f);
+        s_c[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rc0, n, p.dt_bc) : 0.f);
       }
     };
 
@@ -291,56 +295,59 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
 
       const unsigned char* bdl = s_dl + buf * kCK * DT * 4;
       const unsigned char* bu = s_u + buf * kCK * DT * 4;
-      const float* bb = s_b + buf * kCK * NP;
-      const float* bc = s_c + buf * kCK * NP;
+      const float2* bb = s_b + buf * kCK * NP;
+      const float2* bc = s_c + buf * kCK * NP;
       const float* by = s_y + buf * kCK * DT;
       const int ns = min(kCK, L - c * kCK);
-#pragma unroll kFwdUnroll
-      for (int tt = 0; tt < ns; ++tt) {
-        const int s = c * kCK + tt;
-        const int t = dir ? L - 1 - s : s;
-        // checkpoint of P = 2h + dBu before every p.cki-th processing step
-        // (the start of each backward chunk)
-        if (p.ckpt != nullptr && s > 0 && (s & (p.cki - 1)) == 0) {
+      // checkpoint of P = 2h + dBu before processing step s (the start of a
+      // backward chunk: every p.cki steps)
+      auto write_ckpt = [&](int s) {
 #pragma unroll
-          for (int k = 0; k < ND; ++k) {
-            const int d = dbase + k;
-            if (d < D) {
-              float* dst = p.ckpt +
-                  ((((size_t)b * ndirs + dslot) * p.nck + (s / p.cki - 1)) * D + d) * NP + q * NL;
-              if constexpr (NL % 4 == 0) {   // 16-byte aligned: NP*4 and NL*4 are multiples of 16
+        for (int k = 0; k < ND; ++k) {
+          const int d = dbase + k;
+          if (d < D) {
+            float* dst = p.ckpt +
+                ((((size_t)b * ndirs + dslot) * p.nck + (s / p.cki - 1)) * D + d) * NP + q * NL;
+            if constexpr (NL % 4 == 0) {   // 16-byte aligned: NP*4 and NL*4 are multiples of 16
 #pragma unroll
-                for (int j = 0; j < NL; j += 4)
-                  *reinterpret_cast<float4*>(dst + j) =
-                      (k & 1) ? make_float4(P[k >> 1][j].y, P[k >> 1][j + 1].y,
-                                            P[k >> 1][j + 2].y, P[k >> 1][j + 3].y)
-                              : make_float4(P[k >> 1][j].x, P[k >> 1][j + 1].x,
-                                            P[k >> 1][j + 2].x, P[k >> 1][j + 3].x);
-              } else {
+              for (int j = 0; j < NL; j += 4)
+                *reinterpret_cast<float4*>(dst + j) =
+                    (k & 1) ? make_float4(P[k >> 1][j].y, P[k >> 1][j + 1].y,
+                                          P[k >> 1][j + 2].y, P[k >> 1][j + 3].y)
+                            : make_float4(P[k >> 1][j].x, P[k >> 1][j + 1].x,
+                                          P[k >> 1][j + 2].x, P[k >> 1][j + 3].x);
+            } else {
 #pragma unroll
-                for (int j = 0; j < NL; ++j) dst[j] = (k & 1) ? P[k >> 1][j].y : P[k >> 1][j].x;
-              }
+              for (int j = 0; j < NL; ++j) dst[j] = (k & 1) ? P[k >> 1][j].y : P[k >> 1][j].x;
             }
           }
         }
+      };
+      // One processing step.  FASTC: the caller proved |delta*A_imag| <=
+      // kFastArgBound for the whole chunk and that it holds no state output,
+      // so the packed path runs without a per-step check.
+      auto step = [&](int tt, auto fast_tag) {
+        constexpr bool FASTC = decltype(fast_tag)::value;
+        const int s = c * kCK + tt;
+        const int t = dir ? L - 1 - s : s;
         float dl[ND], uu[ND];
         read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * esz, bf16, dl);
         read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * esz, bf16, uu);
-        float Bv[NL], Cv[NL];
+        float2 Bv[NL], Cv[NL];   // B, C of the thread's lanes as (b, b) pairs
 #pragma unroll
         for (int j = 0; j < NL; ++j) {
           Bv[j] = bb[tt * NP + q * NL + j];
           Cv[j] = bc[tt * NP + q * NL + j];
         }
-        const bool last = (s == L - 1) && (p.h_last != nullptr);
+        const bool last = !FASTC && (s == L - 1) && (p.h_last != nullptr);
         float du[ND], mdl = 0.f;
 #pragma unroll
         for (int k = 0; k < ND; ++k) {
           du[k] = __fmul_rn(dl[k], uu[k]);
-          mdl = fmaxf(mdl, fabsf(dl[k]));
+          if constexpr (!FASTC) mdl = fmaxf(mdl, fabsf(dl[k]));
         }
         float part[2 * NDP];
-        if ((ND % 2 == 0) && !last && __fmul_rn(mdl, maxai) <= kFastArgBound) {
+        if (FASTC || ((ND % 2 == 0) && !last && __fmul_rn(mdl, maxai) <= kFastArgBound)) {
           // packed path: channel pairs, no per-cell range checks
 #pragma unroll
           for (int kp = 0; kp < NDP; ++kp) {
@@ -350,19 +357,22 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
 #pragma unroll
             for (int j = 0; j < R; ++j) {
               const float2 g = __fmul2_rn(gate_exp2(dl2, A2[kp][j]), gate_cos2_nocheck(dl2, AI[kp][j]));
-              const float2 H = cell_update2(g, P[kp][j], du2, Bv[j]);
-              acc = __ffma2_rn(H, f2(Cv[j]), acc);
+              const float2 H = cell_update2p(g, P[kp][j], du2, Bv[j]);
+              acc = __ffma2_rn(H, Cv[j], acc);
             }
 #pragma unroll
             for (int j = R; j < NL; ++j) {
-              const float2 H = cell_update2(TK[kp][j - R], P[kp][j], du2, Bv[j]);
-              acc = __ffma2_rn(H, f2(Cv[j]), acc);
+              const float2 H = cell_update2p(TK[kp][j - R], P[kp][j], du2, Bv[j]);
+              acc = __ffma2_rn(H, Cv[j], acc);
             }
             part[2 * kp] = acc.x;
             part[2 * kp + 1] = acc.y;
           }
         } else {
           // scalar path: per-cell range checks (large arguments, the last step)
+          float Cs[NL];
+#pragma unroll
+          for (int j = 0; j < NL; ++j) Cs[j] = Cv[j].x;
 #pragma unroll
           for (int k = 0; k < ND; ++k) {
             float H[NL];
@@ -376,9 +386,9 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
               } else {
                 g = (k & 1) ? TK[k >> 1][j - R].y : TK[k >> 1][j - R].x;
               }
-              H[j] = cell_update(g, Pk, du[k], Bv[j]);
+              H[j] = cell_update(g, Pk, du[k], Bv[j].x);
             }
-            part[k] = y_partial<NL>(H, Cv);
+            part[k] = y_partial<NL>(H, Cs);
             if (last) {
               const int d = dbase + k;
               if (d < D) {
@@ -388,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
                   if (n >= 0) {
                     const size_t gi = ((size_t)b * D + d) * N + n;
                     p.h_last[gi] = __fmul_rn(0.5f, H[j]);
-                    p.dbu_last[gi] = __fmul_rn(du[k], Bv[j]);
+                    p.dbu_last[gi] = __fmul_rn(du[k], Bv[j].x);
                   }
                 }
               }
@@ -403,6 +413,32 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
           if ((k & 3) == q && d < D) {
             yrow[d] = accumulate ? __fadd_rn(tot, by[tt * DT + grp * ND + k]) : tot;
           }
+        }
+      };
+      // the range decision once per chunk: max |delta| of the thread's channels
+      bool chunk_fast = false;
+      if constexpr (ND % 2 == 0) {
+        float mdl = 0.f;
+        for (int tt = 0; tt < ns; ++tt) {
+          float dl[ND];
+          read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * esz, bf16, dl);
+#pragma unroll
+          for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
+        }
+        const bool has_last = p.h_last != nullptr && c * kCK + ns == L;
+        chunk_fast = !has_last && __fmul_rn(mdl, maxai) <= kFastArgBound;
+      }
+      // segments between checkpoint positions (p.cki divides kCK)
+      const int seg_len = p.cki < kCK ? p.cki : kCK;
+      for (int seg = 0; seg < ns; seg += seg_len) {
+        const int send = min(ns, seg + seg_len);
+        const int s = c * kCK + seg;
+        if (p.ckpt != nullptr && s > 0 && (s & (p.cki - 1)) == 0) write_ckpt(s);
+        if (chunk_fast) {
+#pragma unroll kFwdUnroll
+          for (int tt = seg; tt < send; ++tt) step(tt, std::true_type{});
+        } else {
+          for (int tt = seg; tt < send; ++tt) step(tt, std::false_type{});
         }
       }
       if constexpr (!BULK) {
