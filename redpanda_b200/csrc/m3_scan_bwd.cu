@@ -66,14 +66,23 @@ struct BwdCfg {
   static constexpr int CS = pow2ceil(C + CG);       // TMEM columns per timestep
   static constexpr int WG_COLS = KC * CS;           // TMEM columns per warpgroup
   static constexpr int NCOLS = (NTH / 128) * WG_COLS < 32 ? 32 : (NTH / 128) * WG_COLS;
-  static constexpr int FL = 4;                      // steps per dB/dC/ddelta flush
+  // WR: dB/dC partials are first reduced over the 8 channel groups of a warp
+  // with a transposed shuffle butterfly (2*NL values halved over lane bits
+  // 4, 3, 2), leaving one value per (step, B|C, lane, warp, quarter) in shared
+  // memory; the flush then sums the warps once per chunk.  Otherwise every
+  // thread stores its partials and the flush sums all groups every 4 steps.
+  static constexpr bool WR = (2 * (R + T)) % 8 == 0;
+  static constexpr int NW = NTH / 32;               // warps
+  static constexpr int FL = WR ? (KC < 8 ? KC : 8) : 4;   // steps per dB/dC/ddelta flush
   static constexpr size_t raw_bytes = (size_t)KC * DT * 4;    // one staged (KC x DT) tile
   // Reduction staging rows hold one value per thread (group-major, quarter-minor),
   // so per-step stores are bank-conflict free; the row pitches are padded so
   // the float4 reads of the flush hit distinct banks.
   static constexpr int SR = NG * 4 + 16;                       // dB/dC row pitch
   static constexpr int SG = NG * 4 + (16 / ND < 4 ? 4 : 16 / ND);  // ddelta row pitch
-  static constexpr size_t red_floats = (size_t)FL * 2 * NL * SR;   // [FL][2][NL][SR]
+  static constexpr size_t red_floats =
+      WR ? (size_t)FL * 2 * NL * NW * 4                           // [FL][2*NL][NW][4]
+         : (size_t)FL * 2 * NL * SR;                              // [FL][2][NL][SR]
   static constexpr size_t gs_floats = (size_t)FL * ND * 2 * SG;    // [FL][ND][2][SG]
   // BULK (16-byte staging): B/C rows land raw (HBM dtype, memory order) and
   // are widened into the padded fp32 tiles after the copy; the bidirectional
@@ -143,7 +152,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
   float* s_ck = reinterpret_cast<float*>(s_dy + 2 * CF::raw_bytes);  // [2][DT][NP]
   float* s_b = s_ck + 2 * DT * NP;                                   // [2][KC][NP]
   float* s_c = s_b + 2 * KC * NP;                                    // [2][KC][NP]
-  float* s_red = s_c + 2 * KC * NP;                                  // [FL][2][NL][SR]
+  float* s_red = s_c + 2 * KC * NP;                                  // dB/dC staging (CF::WR)
   float* s_gs = s_red + CF::red_floats;                              // [FL][ND][2][SG]
   float* s_braw = s_gs + CF::gs_floats;                              // [2][B|C][KC][NP] (BULK)
   float* s_scr = s_braw + CF::braw_floats;                           // [KC][DT][2] (BULK)
@@ -558,7 +567,35 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
       if (GS || __fmul_rn(mdl, maxai) <= kFastArgBound) reverse_cells(std::true_type{});
       else reverse_cells(std::false_type{});
       // dB/dC partial of this thread's channels
-      {
+      if constexpr (CF::WR) {
+        // transposed butterfly over the warp's 8 channel groups (lane bits 4..2):
+        // each round keeps half of the values and adds the partner's copy of it
+        constexpr int V = 2 * NL;
+        float v[V];
+#pragma unroll
+        for (int j = 0; j < NL; ++j) {
+          v[j] = __fadd_rn(pB[j].x, pB[j].y);
+          v[NL + j] = __fadd_rn(pC[j].x, pC[j].y);
+        }
+        const int lane = tid & 31;
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+          const int m = 16 >> r, h = V >> (r + 1);
+          const bool up = (lane & m) != 0;
+#pragma unroll
+          for (int i = 0; i < h; ++i) {
+            const float keep = up ? v[h + i] : v[i];
+            const float send = up ? v[i] : v[h + i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+          }
+        }
+        // lane (g, q) now holds values base .. base + V/8 - 1 of its quarter q
+        const int g = lane >> 2;
+        const int base = ((g >> 2) & 1) * (V / 2) + ((g >> 1) & 1) * (V / 4) + (g & 1) * (V / 8);
+#pragma unroll
+        for (int i = 0; i < V / 8; ++i)
+          s_red[(((size_t)slot * V + base + i) * CF::NW + warp) * 4 + q] = v[i];
+      } else {
         float* r0 = s_red + (size_t)slot * 2 * NL * SR + grp * 4 + q;
 #pragma unroll
         for (int j = 0; j < NL; ++j) {
@@ -573,10 +610,33 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
         __syncthreads();
         const int nsl = slot + 1;                 // slots in this flush
         const int tt_hi = tt + slot;              // step of slot 0
+        if constexpr (CF::WR) {
+          // dB/dC: sum the warps' float4 (4 quarters) of each (slot, which, j)
+          // in warp order, write lanes j*4 + q of the partial
+          for (int row = tid; row < nsl * 2 * NL; row += NTH) {
+            const float4* src = reinterpret_cast<const float4*>(s_red) + (size_t)row * CF::NW;
+            float4 acc = src[0];
+#pragma unroll
+            for (int w = 1; w < CF::NW; ++w) {
+              const float4 v = src[w];
+              acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
+              acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
+            }
+            const int sl = row / (2 * NL), rem = row - sl * 2 * NL;
+            const int which = rem / NL, j = rem - which * NL;
+            const int s = s0 + tt_hi - sl;
+            const int t = dir ? L - 1 - s : s;
+            const int dslot = bidir ? dir : 0;
+            float4* dst = reinterpret_cast<float4*>(
+                p.part_bc + (((((size_t)gt * ndirs + dslot) * B + b) * L + t) * 2 + which) * NP +
+                j * 4);
+            *dst = acc;
+          }
+        }
         // dB/dC: each (slot, which, j) row holds one value per (group, quarter);
         // 4 threads sum it over the groups as float4s of the 4 quarters, in a
         // fixed order, and write lanes j*4 + q of the partial.
-        for (int base = 0; base < nsl * 2 * NL; base += NTH / 4) {
+        for (int base = 0; !CF::WR && base < nsl * 2 * NL; base += NTH / 4) {
           const int row = base + (tid >> 2), part = tid & 3;
           const bool rok = row < nsl * 2 * NL;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
