@@ -4,12 +4,13 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl m3|reference]
 
 One step = the fused bidirectional forward scan (with backward checkpoints) and
-the analytic backward over one batch of config-2 shaped synthetic input
-(B=1024 rows per GPU, L=64, d_inner=1536, d_state=32 with 16 rotational + 16
-tracking lanes, bf16 delta/u/B/C/dy, fp32 state), plus -- on more than one GPU
+the analytic backward of one layer of the config-4 stack (the config-1/2 layer
+shape: L=64, d_inner=1536, d_state=32 with 16 rotational + 16 tracking lanes,
+bf16 delta/u/B/C/dy, fp32 state) over config 4's global batch of 8192 rows
+split evenly across the N GPUs ("strong" scaling), plus -- on more than one GPU
 -- one NCCL all-reduce of the scan-parameter gradients (the data-parallel
-exchange of config 4).  Per-GPU work is fixed as N grows ("weak" scaling).
-Inputs (~0.6 GB/GPU) exceed the 126 MB L2, so no flush is needed between steps.
+exchange of config 4).  Inputs (>= 0.6 GB/GPU) exceed the 126 MB L2, so no
+flush is needed between steps.
 
 The JSON line also carries the end-to-end leg (host buffers, H2D/D2H copies in
 the timed region), the roofline of the dominant kernel (the backward), the CPU
@@ -39,7 +40,8 @@ sys.path.insert(0, REPO)
 METRIC = "scan fwd+bwd Gtokens/s (% HBM peak); recurrent-step rollout node-steps/s/GPU"
 UNIT = "Gtokens/s"
 # config 2 / 4 shape (per GPU)
-B_RANK, L, D, N, N_ROT, MIMO_P = 1024, 64, 1536, 32, 16, 4
+GLOBAL_B, L, D, N, N_ROT, MIMO_P = 8192, 64, 1536, 32, 16, 4
+B_RANK = GLOBAL_B     # rows per GPU; set from the world size in main()
 # algorithmic HBM bytes per token at this boundary (bf16 delta/u/B/C/dy, fp32 y)
 FWD_BYTES_PER_TOKEN = 2 * 2 * D + 2 * 2 * N + 4 * D            # 12416
 BWD_BYTES_PER_TOKEN = 3 * 2 * D + 2 * 2 * N + 2 * 2 * D + 2 * 2 * N  # 15616
@@ -209,6 +211,8 @@ def run_m3(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    global B_RANK
+    B_RANK = args.batch if args.batch else max(1, GLOBAL_B // world)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -323,6 +327,7 @@ def run_m3(args):
 
     step_info = run_step_rollout(dev, args) if (args.rollout and rank == 0) else None
     model_info = run_model_rollout(dev, args) if (args.rollout and rank == 0) else None
+    sweep_info = run_l_sweep(dev, args) if (args.sweep and rank == 0) else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -339,10 +344,12 @@ def run_m3(args):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong" if not args.batch else "weak",
+            "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": "c2: bidirectional scan fwd+bwd (config 2 shape; "
-                                   "config 4's data-parallel grad all-reduce when N>1)",
+            "config": {"workload": "c2/c4: bidirectional scan fwd+bwd of one layer of the "
+                                   "config-4 stack (config-2 layer shape), global batch split "
+                                   "over the GPUs, scan-parameter grad all-reduce when N>1",
                        "batch_per_gpu": B_RANK, "global_batch": B_RANK * world, "seq_len": L,
                        "d_inner": D, "d_state": N, "n_rot": N_ROT, "mimo_p": MIMO_P,
                        "parallelism": f"dp{world}", "l2": "inputs larger than L2 (no flush)",
@@ -367,6 +374,10 @@ def run_m3(args):
             line["step_rollout"] = step_info
         if model_info is not None:
             line["model_rollout"] = model_info
+        if sweep_info is not None:
+            line["l_sweep"] = {"workload": "c4 sequence-length sweep: bidirectional scan "
+                                           "fwd+bwd, c2 layer shape, bf16, 1 GPU",
+                               "points": sweep_info}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -474,6 +485,58 @@ def run_step_rollout(dev, args):
     }
 
 
+def run_l_sweep(dev, args):
+    """Config 4's sequence-length sweep on one GPU: the bidirectional scan fwd+bwd
+    (config-2 layer shape, bf16 inputs) at B=256 rows and L = 64 .. 4096;
+    tokens/s per length from CUDA events over a few steps."""
+    import torch
+    from redpanda_b200 import scan as S
+    from redpanda_b200.scan import ScanPlan, pad_params
+    out = []
+    Bs = args.sweep_batch
+    torch.cuda.empty_cache()
+    for Ls in (64, 256, 1024, 4096):
+        g = torch.Generator(dev).manual_seed(Ls)
+        bf = torch.bfloat16
+        x = {"delta": torch.nn.functional.softplus(
+                 torch.randn(Bs, Ls, D, device=dev, generator=g) * 0.5 - 2).to(bf),
+             "u": torch.randn(Bs, Ls, D, device=dev, generator=g).to(bf),
+             "Bc": torch.randn(Bs, Ls, N, device=dev, generator=g).to(bf),
+             "Cc": torch.randn(Bs, Ls, N, device=dev, generator=g).to(bf),
+             "dy": torch.randn(Bs, Ls, D, device=dev, generator=g).to(bf)}
+        ar = -torch.exp(torch.randn(D, N_ROT, device=dev, generator=g) * 0.5)
+        ai = (torch.rand(D, N_ROT, device=dev, generator=g) * 2 - 1) * math.pi
+        tk = torch.tanh(torch.randn(D, N - N_ROT, device=dev, generator=g))
+        P = [t.contiguous() for t in pad_params(ar, ai, tk, N_ROT, N, D, dev)]
+        plan = ScanPlan(Bs, Ls, D, N, N_ROT, bf, bf, S.M3_DIR_BIDIR)
+        y = torch.empty(Bs, Ls, D, device=dev)
+        ckpt = torch.empty(plan.ckpt_floats(), device=dev)
+        ws = torch.empty(plan.workspace_bytes(), device=dev, dtype=torch.uint8)
+        gd, gu = torch.empty_like(x["delta"]), torch.empty_like(x["u"])
+        gB, gC = torch.empty_like(x["Bc"]), torch.empty_like(x["Cc"])
+        ga = torch.empty(3, D, N, device=dev)
+
+        def once():
+            plan.forward(x["delta"], x["u"], x["Bc"], x["Cc"], *P, y, ckpt)
+            plan.backward(x["delta"], x["u"], x["Bc"], x["Cc"], *P, x["dy"], ckpt, gd, gu, gB,
+                          gC, ga[0], ga[1], ga[2], ws)
+        reps = max(2, 4096 // Ls)
+        once()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            once()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        out.append({"seq_len": Ls, "batch": Bs, "ms_per_step": ms,
+                    "gtokens_per_s": Bs * Ls / (ms / 1e3) / 1e9})
+        del x, y, ckpt, ws, gd, gu, gB, gC
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_model_rollout(dev, args):
     """Config 3 at model level: a 12-layer Search-Mamba-shaped ``Mamba``
     (d_model=512, d_inner=1024, d_state=32 with 8 tracking lanes, mimo_p=2,
@@ -542,7 +605,6 @@ def run_model_rollout(dev, args):
 
 
 def main():
-    global B_RANK
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -552,17 +614,19 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-rollout", dest="rollout", action="store_false",
                     help="skip the config-3 step rollout measurement")
+    ap.add_argument("--no-sweep", dest="sweep", action="store_false",
+                    help="skip the config-4 sequence-length sweep")
+    ap.add_argument("--sweep-batch", type=int, default=256)
     ap.add_argument("--rollout-layers", type=int, default=12,
                     help="layers of the config-3 rollout (default 12; fewer for profiler captures)")
     ap.add_argument("--rollout-batch", type=int, default=8192,
                     help="rollout rows (default 8192; fewer for profiler captures)")
-    ap.add_argument("--batch", type=int, default=B_RANK,
-                    help="rows per GPU (default: the config-2 batch; smaller values are "
-                         "for profiler captures only)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="rows per GPU (default: config 4's global 8192 rows split over "
+                         "the GPUs; smaller values are for profiler captures only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    B_RANK = args.batch
     if args.impl == "reference":
         run_reference(args)
     else:
