@@ -178,6 +178,27 @@ M3_API int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p,
             int32_t off_b, int32_t off_c, const float* wb, const float* wc, float eps,
             float* delta, float* Bc, float* Cc, void* stream);
 
+/* Workspace bytes of m3_step_inputs_bwd (the BCNorm weight-gradient partials). */
+M3_API size_t m3_step_inputs_bwd_workspace_bytes(const m3_step_desc* desc, int32_t mimo_p);
+
+/* Backward of m3_step_inputs over desc->batch rows (the training-path prologue:
+ * the gradients that torch's softplus, RMSNorm and sum backward give for
+ * mamba.py:284-301 and 336-337):
+ *   g_delta (rows, D), g_Bc, g_Cc (rows, N)  float32 upstream gradients
+ *   d_dt    (rows, D) float32 = g_delta * softplus'(dt)
+ *   d_xbc   (rows, ld_x) float32: columns [off_b, off_b + N*p) and
+ *           [off_c, off_c + N*p) are written (the gradients of B_raw, C_raw);
+ *           other columns are left untouched
+ *   d_wb, d_wc (N*p,) float32 BCNorm weight gradients, reduced over the rows in a
+ *           fixed order (bitwise reproducible); unused when wb == wc == NULL
+ *   workspace >= m3_step_inputs_bwd_workspace_bytes(desc, mimo_p) bytes */
+M3_API int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p,
+            const float* dt, int64_t ld_dt, const float* xbc, int64_t ld_x,
+            int32_t off_b, int32_t off_c, const float* wb, const float* wc, float eps,
+            const float* g_delta, const float* g_Bc, const float* g_Cc,
+            float* d_dt, float* d_xbc, float* d_wb, float* d_wc,
+            void* workspace, size_t workspace_bytes, void* stream);
+
 /* m3_step (dbu != NULL) or m3_step_factored (fac_prev, fac_next != NULL, dbu
  * NULL) whose output is the layer's gated activation instead of y
  * (mamba.py:493-497):

@@ -384,6 +384,46 @@ int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const float* dt, in
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 
+size_t m3_step_inputs_bwd_workspace_bytes(const m3_step_desc* desc, int32_t mimo_p) {
+  if (!desc || desc->batch < 1 || desc->d_state < 1 || mimo_p < 1) return 0;
+  const size_t np = (size_t)desc->d_state * mimo_p;
+  return (size_t)step_inputs_bwd_ctas(desc->batch) * 2 * np * sizeof(float);
+}
+
+int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p, const float* dt,
+                       int64_t ld_dt, const float* xbc, int64_t ld_x, int32_t off_b,
+                       int32_t off_c, const float* wb, const float* wc, float eps,
+                       const float* g_delta, const float* g_Bc, const float* g_Cc,
+                       float* d_dt, float* d_xbc, float* d_wb, float* d_wc, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (!desc) return M3_ERR_NULL;
+  const int64_t np = (int64_t)desc->d_state * mimo_p;
+  if (desc->batch < 1 || desc->d_inner < 1 || desc->d_state < 1 || mimo_p < 1 ||
+      ld_dt < desc->d_inner || off_b < 0 || off_c < 0 || off_b + np > ld_x ||
+      off_c + np > ld_x || !(eps >= 0.f) || np * 2 * 8 * 4 > 200 * 1024)
+    return M3_ERR_SHAPE;
+  if (!dt || !xbc || !g_delta || !g_Bc || !g_Cc || !d_dt || !d_xbc ||
+      ((wb == nullptr) != (wc == nullptr)) || (wb && (!d_wb || !d_wc)))
+    return M3_ERR_NULL;
+  if (!aligned(dt, 4) || !aligned(xbc, 4) || !aligned(g_delta, 4) || !aligned(g_Bc, 4) ||
+      !aligned(g_Cc, 4) || !aligned(d_dt, 4) || !aligned(d_xbc, 4) ||
+      (wb && (!aligned(wb, 4) || !aligned(wc, 4) || !aligned(d_wb, 4) || !aligned(d_wc, 4))))
+    return M3_ERR_ALIGN;
+  if (wb && (!workspace || workspace_bytes < m3_step_inputs_bwd_workspace_bytes(desc, mimo_p)))
+    return M3_ERR_WORKSPACE;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  InputsBwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.dt = dt; p.ld_dt = ld_dt; p.xbc = xbc; p.ld_x = ld_x; p.off_b = off_b; p.off_c = off_c;
+  p.wb = wb; p.wc = wc; p.eps = eps; p.g_delta = g_delta; p.g_Bc = g_Bc; p.g_Cc = g_Cc;
+  p.d_dt = d_dt; p.d_xbc = d_xbc; p.d_wb = d_wb; p.d_wc = d_wc;
+  p.part_w = static_cast<float*>(workspace);
+  p.rows = desc->batch; p.D = desc->d_inner; p.N = desc->d_state; p.P = mimo_p;
+  cudaError_t e = launch_step_inputs_bwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
 int m3_gate(int64_t rows, int32_t d_inner, const float* y, const void* u, int32_t dtype_u,
             const float* z, int64_t ld_z, const float* d_skip, float coef, float* out,
             void* stream) {

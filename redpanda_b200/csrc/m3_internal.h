@@ -100,6 +100,21 @@ struct InputsParams {
 };
 cudaError_t launch_step_inputs(const InputsParams& p, cudaStream_t s);
 
+struct InputsBwdParams {
+  const float* dt; long long ld_dt;
+  const float* xbc; long long ld_x;
+  int off_b, off_c;
+  const float* wb; const float* wc;
+  float eps;
+  const float* g_delta; const float* g_Bc; const float* g_Cc;   // (rows, D), (rows, N) x2
+  float* d_dt; float* d_xbc;                                    // (rows, D), (rows, ld_x)
+  float* d_wb; float* d_wc;                                     // (N*P,) each
+  float* part_w;                                                // [ctas][2][N*P]
+  long long rows; int D, N, P;
+};
+int step_inputs_bwd_ctas(long long rows);
+cudaError_t launch_step_inputs_bwd(const InputsBwdParams& p, cudaStream_t s);
+
 struct GateParams {
   const float* y; const void* u; int u_bf16;
   const float* z; long long ld_z;

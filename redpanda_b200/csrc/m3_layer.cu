@@ -87,7 +87,112 @@ __global__ void gate_kernel(const GateParams p) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += stride) one(i);
 }
 
+// Backward of step_inputs_kernel over `rows` rows:
+//   d_dt   = g_delta * softplus'(dt)  (1 above torch's threshold 20, else
+//            e/(e+1) with e = exp(dt), as torch's softplus backward)
+//   BCNorm with the MIMO fold, per row: y_i = (x_i*rs)*w_i, Bc[n] = sum_k y_{n*p+k},
+//   rs = (mean(x^2) + eps)^-1/2, so with gy_i = gBc[i/p], gx_i = gy_i*w_i:
+//     d_x_i = rs*gx_i - (rs^3/np) * x_i * sum_j gx_j*x_j
+//     d_w_i = sum over rows of gy_i * (x_i*rs)
+// One warp per row (grid-stride); the weight gradients accumulate per warp in
+// shared memory, are summed over the CTA's warps in warp order into one partial
+// per CTA, and reduce_w_kernel sums the partials in CTA order: deterministic.
+__global__ void __launch_bounds__(256) step_inputs_bwd_kernel(const InputsBwdParams p) {
+  extern __shared__ float s_w[];             // [8 warps][2][np]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int np = p.N * p.P;
+  float* wacc = s_w + (size_t)warp * 2 * np;
+  for (int i = lane; i < 2 * np; i += 32) wacc[i] = 0.f;
+  const long long nwarps = (long long)gridDim.x * 8;
+  for (long long r = (long long)blockIdx.x * 8 + warp; r < p.rows; r += nwarps) {
+    const size_t b = (size_t)r;
+    for (int d = lane; d < p.D; d += 32) {
+      const float x = p.dt[b * p.ld_dt + d];
+      const float g = p.g_delta[b * p.D + d];
+      float v = g;
+      if (!(x > 20.f)) {
+        const float e = expf(x);
+        v = __fdiv_rn(__fmul_rn(g, e), __fadd_rn(e, 1.f));
+      }
+      p.d_dt[b * p.D + d] = v;
+    }
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      const float* x = p.xbc + b * p.ld_x + (which ? p.off_c : p.off_b);
+      const float* gbc = (which ? p.g_Cc : p.g_Bc) + b * p.N;
+      const float* w = which ? p.wc : p.wb;
+      float* dx = p.d_xbc + b * p.ld_x + (which ? p.off_c : p.off_b);
+      if (w == nullptr) {   // no BCNorm: the fold is a plain sum
+        for (int i = lane; i < np; i += 32) dx[i] = gbc[i / p.P];
+        continue;
+      }
+      float ss = 0.f, sg = 0.f;
+      for (int i = lane; i < np; i += 32) {
+        const float xi = x[i];
+        ss = __fmaf_rn(xi, xi, ss);
+        sg = __fmaf_rn(__fmul_rn(gbc[i / p.P], w[i]), xi, sg);
+      }
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) {
+        ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, m));
+        sg = __fadd_rn(sg, __shfl_xor_sync(0xffffffffu, sg, m));
+      }
+      const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)np), p.eps));
+      const float coef = __fdiv_rn(__fmul_rn(__fmul_rn(rs, rs), rs), (float)np);
+      const float cs = __fmul_rn(coef, sg);
+      float* wa = wacc + which * np;
+      for (int i = lane; i < np; i += 32) {
+        const float xi = x[i], gy = gbc[i / p.P];
+        dx[i] = __fsub_rn(__fmul_rn(rs, __fmul_rn(gy, w[i])), __fmul_rn(cs, xi));
+        wa[i] = __fmaf_rn(gy, __fmul_rn(xi, rs), wa[i]);
+      }
+    }
+  }
+  __syncthreads();
+  if (p.wb != nullptr) {
+    for (int i = threadIdx.x; i < 2 * np; i += blockDim.x) {
+      float v = s_w[i];
+      for (int w = 1; w < 8; ++w) v = __fadd_rn(v, s_w[(size_t)w * 2 * np + i]);
+      p.part_w[(size_t)blockIdx.x * 2 * np + i] = v;
+    }
+  }
+}
+
+__global__ void reduce_w_kernel(const float* part, int nparts, int np, float* d_wb, float* d_wc) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 2 * np; i += gridDim.x * blockDim.x) {
+    float v = 0.f;
+    for (int g = 0; g < nparts; ++g) v = __fadd_rn(v, part[(size_t)g * 2 * np + i]);
+    if (i < np) d_wb[i] = v;
+    else d_wc[i - np] = v;
+  }
+}
+
 }  // namespace
+
+int step_inputs_bwd_ctas(long long rows) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  long long g = (rows + 7) / 8;
+  if (g > (long long)sms * 4) g = (long long)sms * 4;
+  return (int)(g < 1 ? 1 : g);
+}
+
+cudaError_t launch_step_inputs_bwd(const InputsBwdParams& p, cudaStream_t s) {
+  const int grid = step_inputs_bwd_ctas(p.rows);
+  const int np = p.N * p.P;
+  const size_t smem = (size_t)8 * 2 * np * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(step_inputs_bwd_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  step_inputs_bwd_kernel<<<grid, 256, smem, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || p.wb == nullptr) return e;
+  reduce_w_kernel<<<(2 * np + 255) / 256, 256, 0, s>>>(p.part_w, grid, np, p.d_wb, p.d_wc);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gate(const GateParams& p, cudaStream_t s) {
   int dev = 0, sms = 148;

@@ -131,6 +131,23 @@ class Mamba3Block(nn.Module):
         delta = F.softplus(self.dt_proj(dt_raw))
         return delta, B, C
 
+    def _ssm_inputs(self, u):
+        """(delta, Bc, Cc) of a sequence for the training path: the x_proj and
+        dt_proj GEMMs in torch, softplus + BCNorm + MIMO fold (and their
+        backward) in one launch each (m3_step_inputs / m3_step_inputs_bwd)."""
+        cfg = self.config
+        n, p = cfg.d_state, cfg.mimo_p
+        lead = u.shape[:-1]
+        x_dbl = self.x_proj(u)
+        dt = self.dt_proj(x_dbl[..., :cfg.dt_rank])
+        rows = u.numel() // cfg.d_inner
+        bw = self.b_norm.weight if cfg.use_bcnorm else None
+        cw = self.c_norm.weight if cfg.use_bcnorm else None
+        eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
+        delta, bc, cc = S.step_inputs(dt.reshape(rows, cfg.d_inner), x_dbl.reshape(rows, -1),
+                                      cfg.dt_rank, cfg.dt_rank + n * p, bw, cw, eps, n, p)
+        return delta.view(*lead, cfg.d_inner), bc.view(*lead, n), cc.view(*lead, n)
+
     def _scan_args(self, delta, u, B, C):
         cfg = self.config
         track = self._track_gate() if cfg.n_track_state > 0 else None
@@ -191,17 +208,22 @@ class Mamba3Block(nn.Module):
         return (out, state) if return_state else out
 
     def forward(self, x):
-        """mamba.py:231-267; the bidirectional pair is one fused launch."""
+        """mamba.py:231-267; the bidirectional pair is one fused launch; the
+        scan's prologue (softplus, BCNorm, MIMO fold) is one launch forward and
+        one backward (_ssm_inputs)."""
         if not torch.is_grad_enabled():
             return self._forward_inference(x, False)
+        cfg = self.config
         x_branch, z = self.in_proj(x).chunk(2, dim=-1)
         x_branch = F.silu(x_branch)
-        if not self.config.bidirectional:
-            y = self.ssm(x_branch)
+        delta, bc, cc = self._ssm_inputs(x_branch)
+        track = self._track_gate() if cfg.n_track_state > 0 else None
+        A_real, A_imag = self._compute_A()
+        args = (delta, x_branch, bc, cc, A_real, A_imag, track, cfg.n_rot_state, cfg.d_state)
+        if not cfg.bidirectional:
+            y = S.m3_trapezoidal_scan(*args) + x_branch * self.D
         else:
-            delta, B, C = self._ssm_proj(x_branch)
-            y = S.m3_bidir_scan(*self._scan_args(delta, x_branch, B, C)) \
-                + 2.0 * x_branch * self.D
+            y = S.m3_bidir_scan(*args) + 2.0 * x_branch * self.D
         return self.out_proj(y * F.silu(z))
 
     def forward_with_state(self, x):

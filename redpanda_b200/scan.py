@@ -390,6 +390,59 @@ def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mi
     return delta, bc, cc
 
 
+class _StepInputsFn(torch.autograd.Function):
+    """softplus(dt) and the BCNorm'ed, MIMO-folded B and C over rows, with the
+    analytic backward (m3_step_inputs / m3_step_inputs_bwd): the training-path
+    prologue of the scan (mamba.py:284-301, 336-337)."""
+
+    @staticmethod
+    def forward(ctx, dt, x_dbl, b_weight, c_weight, off_b, off_c, eps, n_state, mimo_p):
+        delta, bc, cc = m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps,
+                                       n_state, mimo_p)
+        ctx.save_for_backward(dt, x_dbl, b_weight if b_weight is not None else dt.new_empty(0),
+                              c_weight if c_weight is not None else dt.new_empty(0))
+        ctx.cfg = (off_b, off_c, float(eps), int(n_state), int(mimo_p), b_weight is not None)
+        return delta, bc, cc
+
+    @staticmethod
+    def backward(ctx, g_delta, g_bc, g_cc):
+        dt, x_dbl, wb, wc = ctx.saved_tensors
+        off_b, off_c, eps, n, p, has_w = ctx.cfg
+        lib = _lib.load()
+        dev = dt.device
+        rows, D = dt.shape
+        z = lambda g, shape: torch.zeros(shape, device=dev) if g is None else g.float().contiguous()  # noqa: E731
+        g_delta, g_bc, g_cc = z(g_delta, (rows, D)), z(g_bc, (rows, n)), z(g_cc, (rows, n))
+        d_dt = torch.empty(rows, D, device=dev, dtype=torch.float32)
+        d_x = torch.zeros_like(x_dbl)
+        desc = StepDesc(rows, D, n, 0, M3_F32, M3_F32)
+        d_wb = d_wc = ws = None
+        if has_w:
+            wb32, wc32 = wb.detach().float().contiguous(), wc.detach().float().contiguous()
+            d_wb, d_wc = torch.empty_like(wb32), torch.empty_like(wc32)
+            ws = torch.empty(max(1, lib.m3_step_inputs_bwd_workspace_bytes(desc, p)),
+                             device=dev, dtype=torch.uint8)
+        else:
+            wb32 = wc32 = None
+        with torch.cuda.device(dev):
+            _lib.check(lib.m3_step_inputs_bwd(
+                desc, p, dt.data_ptr(), dt.stride(0), x_dbl.data_ptr(), x_dbl.stride(0), off_b,
+                off_c, ctypes_ptr(wb32), ctypes_ptr(wc32), eps, g_delta.data_ptr(),
+                g_bc.data_ptr(), g_cc.data_ptr(), d_dt.data_ptr(), d_x.data_ptr(),
+                ctypes_ptr(d_wb), ctypes_ptr(d_wc), ctypes_ptr(ws),
+                0 if ws is None else ws.numel(), _stream(dev)))
+        return (d_dt, d_x, None if d_wb is None else d_wb.to(wb.dtype),
+                None if d_wc is None else d_wc.to(wc.dtype), None, None, None, None, None)
+
+
+def step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mimo_p):
+    """Differentiable :func:`m3_step_inputs` over (rows, .) float32 tensors."""
+    dt = dt.float().contiguous()
+    x_dbl = x_dbl.float().contiguous()
+    return _StepInputsFn.apply(dt, x_dbl, b_weight, c_weight, off_b, off_c, eps, n_state,
+                               mimo_p)
+
+
 def m3_gate(y, u, z, d_skip, coef=1.0, out=None):
     """(y + coef*u*D) * silu(z) in one launch (mamba.py:262-265); y: (..., D)
     float32 contiguous, u: (..., D) float32/bf16 contiguous, z: (..., D) with

@@ -165,3 +165,49 @@ def test_inference_forward_equals_autograd_forward(bidir):
         assert _rel(fi, fr) <= 1e-5
         for (h1, d1), (h2, d2) in zip(ci, cr):
             assert _rel(h1, h2) <= 1e-5 and _rel(d1, d2) <= 1e-5
+
+
+@pytest.mark.parametrize("bcnorm", [True, False])
+def test_step_inputs_backward_matches_torch_autograd(bcnorm):
+    """m3_step_inputs_bwd: the gradients torch's softplus / RMSNorm / sum give."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    rows, D, R, n, p = 300, 96, 8, 32, 4
+    dt = (torch.randn(rows, D, device="cuda", generator=g) * 8).requires_grad_(True)
+    x_dbl = torch.randn(rows, R + 2 * n * p, device="cuda", generator=g).requires_grad_(True)
+    wb = (torch.rand(n * p, device="cuda", generator=g) + 0.5).requires_grad_(bcnorm)
+    wc = (torch.rand(n * p, device="cuda", generator=g) + 0.5).requires_grad_(bcnorm)
+    gd = torch.randn(rows, D, device="cuda", generator=g)
+    gb = torch.randn(rows, n, device="cuda", generator=g)
+    gc = torch.randn(rows, n, device="cuda", generator=g)
+    eps = 1e-5
+
+    def torch_path():
+        delta = F.softplus(dt)
+        braw, craw = x_dbl[:, R:R + n * p], x_dbl[:, R + n * p:]
+        if bcnorm:
+            braw = braw * torch.rsqrt(braw.pow(2).mean(-1, keepdim=True) + eps) * wb
+            craw = craw * torch.rsqrt(craw.pow(2).mean(-1, keepdim=True) + eps) * wc
+        return delta, braw.reshape(rows, n, p).sum(-1), craw.reshape(rows, n, p).sum(-1)
+
+    outs = []
+    for fn in (torch_path, lambda: S.step_inputs(dt, x_dbl, R, R + n * p, wb if bcnorm else None,
+                                                 wc if bcnorm else None, eps, n, p)):
+        for t in (dt, x_dbl, wb, wc):
+            t.grad = None
+        d, b, c = fn()
+        ((d * gd).sum() + (b * gb).sum() + (c * gc).sum()).backward()
+        outs.append([t.grad.clone() if t.grad is not None else None for t in (dt, x_dbl, wb, wc)])
+    for a, r in zip(outs[1], outs[0]):
+        if r is None:
+            assert a is None
+        else:
+            assert _rel(a, r) <= 2e-6
+    # bitwise reproducible
+    for t in (dt, x_dbl, wb, wc):
+        t.grad = None
+    d, b, c = S.step_inputs(dt, x_dbl, R, R + n * p, wb if bcnorm else None,
+                            wc if bcnorm else None, eps, n, p)
+    ((d * gd).sum() + (b * gb).sum() + (c * gc).sum()).backward()
+    for t, prev in zip((dt, x_dbl, wb, wc), outs[1]):
+        if prev is not None:
+            assert torch.equal(t.grad, prev)
