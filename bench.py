@@ -328,6 +328,7 @@ def run_m3(args):
     step_info = run_step_rollout(dev, args) if (args.rollout and rank == 0) else None
     model_info = run_model_rollout(dev, args) if (args.rollout and rank == 0) else None
     sweep_info = run_l_sweep(dev, args) if (args.sweep and rank == 0) else None
+    train_info = run_model_train(dev, args) if (args.model_train and rank == 0) else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -374,6 +375,8 @@ def run_m3(args):
             line["step_rollout"] = step_info
         if model_info is not None:
             line["model_rollout"] = model_info
+        if train_info is not None:
+            line["model_train"] = train_info
         if sweep_info is not None:
             line["l_sweep"] = {"workload": "c4 sequence-length sweep: bidirectional scan "
                                            "fwd+bwd, c2 layer shape, bf16, 1 GPU",
@@ -537,6 +540,55 @@ def run_l_sweep(dev, args):
     return out
 
 
+def run_model_train(dev, args):
+    """Config 4 at model level: the 16-layer bidirectional Eval-Mamba stack of
+    config 1 (d_model=768, d_inner=1536, d_state=32 with 16 tracking lanes,
+    mimo_p=4, vocab 8192, the reference initialisation with a random seed), one
+    training step = forward, loss y.pow(2).mean() (the reference's verify-gate
+    loss), backward through the kernels (scan, prologue) and torch (GEMMs), and
+    a fused AdamW step; micro-batch of ``args.train_batch`` rows of L=64 random
+    token ids.  GEMMs in TF32, scan state and gradients in fp32."""
+    import torch
+    from redpanda_b200.mamba import Mamba, MambaConfig
+    Bs = args.train_batch
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        torch.manual_seed(17)
+        cfg = MambaConfig(d_model=768, n_layer=16, d_state=32, n_track_state=16, mimo_p=4,
+                          vocab_size=8192, bidirectional=True)
+        model = Mamba(cfg).to(dev).train()
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+        g = torch.Generator(dev).manual_seed(19)
+        ids = torch.randint(0, 8192, (Bs, 64), device=dev, generator=g)
+
+        def step():
+            opt.zero_grad(set_to_none=True)
+            loss = model(ids).pow(2).mean()
+            loss.backward()
+            opt.step()
+            return loss
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 5
+        e0.record()
+        for _ in range(n):
+            loss = step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / n
+        return {"workload": f"c4 model level: 16-layer bidirectional Mamba (d_model=768, "
+                            f"d_inner=1536, d_state=32 with 16 tracking lanes, mimo_p=4), "
+                            f"B={Bs} x L=64 per step, fwd + bwd + fused AdamW",
+                "ms_per_step": ms, "tokens_per_s": Bs * 64 / (ms / 1e3),
+                "loss": float(loss.item()),
+                "precision": "TF32 projections, fp32 scan state, activations and gradients"}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old_tf32
+
+
 def run_model_rollout(dev, args):
     """Config 3 at model level: a 12-layer Search-Mamba-shaped ``Mamba``
     (d_model=512, d_inner=1024, d_state=32 with 8 tracking lanes, mimo_p=2,
@@ -614,6 +666,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-rollout", dest="rollout", action="store_false",
                     help="skip the config-3 step rollout measurement")
+    ap.add_argument("--no-model-train", dest="model_train", action="store_false",
+                    help="skip the config-4 model-level training step")
+    ap.add_argument("--train-batch", type=int, default=256)
     ap.add_argument("--no-sweep", dest="sweep", action="store_false",
                     help="skip the config-4 sequence-length sweep")
     ap.add_argument("--sweep-batch", type=int, default=256)
