@@ -100,7 +100,8 @@ bool bwd_layout(const m3_scan_desc* d, const Tile& t, BwdLayout* lay) {
   const int sms = device_sms();
   if (sms <= 0) return false;
   lay->G = (d->d_inner + t.dt_bwd() - 1) / t.dt_bwd();
-  int bg = lay->G >= sms ? 1 : sms / lay->G;
+  const int slots = sms * t.bwd_ctas_per_sm();   // one resident wave
+  int bg = lay->G >= slots ? 1 : slots / lay->G;
   if (bg > d->batch) bg = d->batch;
   if (bg < 1) bg = 1;
   lay->Bg = bg;

@@ -14,6 +14,16 @@ struct Tile {
   int NDB, NTHB;     // backward: channels per thread, threads per CTA
   int GS;            // backward keeps the gates in Tensor Memory (8-step chunks)
   int cki() const { return GS ? 8 : 16; }      // checkpoint interval = backward chunk
+  // Tensor Memory columns of one backward CTA (the kernel's BwdCfg::NCOLS) and
+  // the backward CTAs that fit on one SM by Tensor Memory (512 columns)
+  int bwd_cols() const {
+    const int c = NDB * (R + T) + (GS ? NDB * R * 2 : 0);
+    int cs = 1;
+    while (cs < c) cs <<= 1;
+    const int cols = (NTHB / 128) * cki() * cs;
+    return cols < 32 ? 32 : cols;
+  }
+  int bwd_ctas_per_sm() const { const int n = 512 / bwd_cols(); return n < 1 ? 1 : n; }
   int nl() const { return R + T; }
   int np() const { return 4 * (R + T); }       // padded state lanes per channel
   int dt() const { return 32 * ND; }           // forward channels per CTA

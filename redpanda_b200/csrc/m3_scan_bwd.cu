@@ -66,6 +66,7 @@ struct BwdCfg {
   static constexpr int CS = pow2ceil(C + CG);       // TMEM columns per timestep
   static constexpr int WG_COLS = KC * CS;           // TMEM columns per warpgroup
   static constexpr int NCOLS = (NTH / 128) * WG_COLS < 32 ? 32 : (NTH / 128) * WG_COLS;
+  static constexpr int CPS = 512 / NCOLS < 1 ? 1 : 512 / NCOLS;   // CTAs per SM by TMEM
   // WR: dB/dC partials are first reduced over the 8 channel groups of a warp
   // with a transposed shuffle butterfly (2*NL values halved over lane bits
   // 4, 3, 2), leaving one value per (step, B|C, lane, warp, quarter) in shared
@@ -134,7 +135,8 @@ __device__ __forceinline__ float tile_at(const unsigned char* base, bool bf16, i
 }
 
 template <int R, int T, int ND, int NTH, bool GS, bool BULK>
-__global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const BwdParams p) {
+__global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
+    scan_bwd_kernel(const BwdParams p) {
   using LM = LaneMap<R, T>;
   using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
   constexpr int KC = CF::KC;

@@ -1,7 +1,10 @@
 // The compiled lane tilings.  R/T = rotational/tracking lanes per thread per
 // channel (state lanes are split over 4 threads); NDF / NDB = channels per
 // thread in the forward/step and in the backward kernel; NTHB = backward CTA
-// size (256 = two warpgroups, each with its own half of Tensor Memory).
+// size (128 = one warpgroup; 256 = two, each with its own half of Tensor
+// Memory).  A backward CTA that needs 256 or fewer TMEM columns shares its SM
+// with a second one, so the two CTAs' barriers and flushes overlap each
+// other's arithmetic.
 // NDB = 0: forward and step only (the backward needs R + T <= 16).
 // GS = 1: the backward keeps each step's rotational gates exp*cos and exp*sin
 // in Tensor Memory next to the state (so its reverse pass evaluates no
@@ -14,7 +17,7 @@
 // X(R, T, NDF, NDB, NTHB, GS)
 #define M3_TILE_LIST(X) \
   X(3, 1, 8, 4, 256, 0)    /* N=16, 12 rot + 4 track (config 0)               */ \
-  X(4, 4, 4, 2, 256, 1)    /* N=32, 16 rot + 16 track (configs 1, 2, 4)       */ \
+  X(4, 4, 4, 2, 128, 1)    /* N=32, 16 rot + 16 track (configs 1, 2, 4)       */ \
   X(6, 2, 4, 2, 256, 0)    /* N=32, 24 rot + 8 track (config 3, Search Mamba) */ \
   X(2, 1, 8, 4, 256, 0)    /* N=12, 8 rot + 4 track; N=8, 6 rot + 2 track     */ \
   X(4, 0, 8, 4, 256, 0)    /* N=16, no tracking                               */ \
