@@ -167,13 +167,21 @@ def run_reference(args):
     v = rows * L * args.steps / el / 1e9
     sample = (f"{rows} rows x L={L} of the config-2 shape per step (bidirectional fwd+bwd, "
               f"fp32 PyTorch autograd of the reference chunked scan)")
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "c2 bidirectional scan fwd+bwd, CPU sample",
-                       "rows_per_step": rows, "seq_len": L, "d_inner": D, "d_state": N,
-                       "n_rot": N_ROT},
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "c2/c4: bidirectional scan fwd+bwd of one layer of the "
+                                   "config-4 stack (config-2 layer shape), global batch split "
+                                   "over the GPUs, scan-parameter grad all-reduce when N>1",
+                       "batch_per_gpu": max(1, GLOBAL_B // max(1, world)),
+                       "global_batch": GLOBAL_B, "seq_len": L, "d_inner": D, "d_state": N,
+                       "n_rot": N_ROT, "mimo_p": MIMO_P,
+                       "reference_sample_rows_per_step": rows,
+                       "note": "the reference algorithm runs on the host cores on a bounded "
+                               "sample of the workload (tokens/s is a rate; rows are "
+                               "independent)"},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(),
                              "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
