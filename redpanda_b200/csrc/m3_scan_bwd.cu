@@ -30,7 +30,7 @@
 #include "m3_tmem.cuh"
 
 #ifndef M3_BWD_UNROLL_RECOMPUTE
-#define M3_BWD_UNROLL_RECOMPUTE 1
+#define M3_BWD_UNROLL_RECOMPUTE 2
 #endif
 #ifndef M3_BWD_UNROLL_REVERSE
 #define M3_BWD_UNROLL_REVERSE 1
