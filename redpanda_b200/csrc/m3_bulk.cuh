@@ -63,4 +63,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// A 2D tile of a tensor map (TMA) into shared memory, completion counted on
+// bar's transaction count; c0 is the inner coordinate (elements), c1 the outer.
+// The map must be a __grid_constant__ kernel parameter (its address is a
+// parameter-space address, valid as the tensor-map operand).
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
+}
+
 }  // namespace m3

@@ -21,6 +21,11 @@
 //    h is updated in place; the factors go from fac_in to a separate fac_out
 //    (every channel tile of a row reads the row's B factors, so they cannot be
 //    overwritten while the step runs).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdlib.h>
+#include <string.h>
+
 #include "m3_common.cuh"
 #include "m3_internal.h"
 #include "m3_bulk.cuh"
@@ -305,7 +310,10 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_kernel(
 // pairs.  Thread 0 streams each row pair's state tile (32 x N fp32 of h and of
 // dBu, or of h plus the [delta*u | B] factors) and its inputs into shared
 // memory with bulk asynchronous copies, kBulkStages pairs ahead of the
-// compute; completion is tracked per stage on an mbarrier.  The two rows of a
+// compute; completion is tracked per stage on an mbarrier.  For 32-lane tiles
+// the state tiles move as 2D TMA tiles with the 128-byte swizzle, so that the
+// warp's 8 channel rows (128 bytes apart) do not read the same shared-memory
+// banks; other tiles use 1D bulk copies of the contiguous 32 x N block.  The two rows of a
 // pair are computed as the two lanes of packed FP32 instructions, with the
 // rounding of the scalar cell functions, so outputs equal step_kernel's bit
 // for bit.  New state goes straight from registers to global memory.
@@ -314,18 +322,52 @@ constexpr int kBulkRows = 2;   // rows per stage, one per packed lane
 // keeps more rows in flight to cover the same memory latency.
 constexpr int bulk_stages(bool fact) { return fact ? 5 : 3; }
 
-template <int NP, bool FACT>
+// Stage layout of a row pair.  Unswizzled: row after row, [h | S2 | delta | u |
+// Bc | Cc].  Swizzled (SWZ, 32 lanes = 128-byte tile rows): the two h tiles,
+// then the two S2 parts, then the small rows, padded to 1 KB, so that every
+// state tile starts on the 1024-byte boundary the 128-byte swizzle needs.
+template <int NP, bool FACT, bool SWZ>
 struct BulkStage {
   static constexpr int kH = 32 * NP * 4;                        // h tile of one row
   static constexpr int kS2 = FACT ? 32 * 4 + NP * 4 : kH;       // dBu tile, or [du | B]
   static constexpr int kDL = 32 * 4;                            // delta or u (<= fp32)
   static constexpr int kBC = NP * 4;                            // Bc or Cc (<= fp32)
-  static constexpr int oH = 0, oS2 = kH, oDL = kH + kS2, oU = oDL + kDL, oB = oU + kDL,
-                       oC = oB + kBC;
-  static constexpr int kRow = oC + kBC;
-  static constexpr int kBytes = kBulkRows * kRow;
+  static constexpr int kSmall = 2 * kDL + 2 * kBC;
+  static constexpr int kRow = kH + kS2 + kSmall;
+  static constexpr int kBytes = SWZ ? (kBulkRows * kRow + 1023) / 1024 * 1024 : kBulkRows * kRow;
+  __device__ static constexpr int oH(int r) { return SWZ ? r * kH : r * kRow; }
+  __device__ static constexpr int oS2(int r) { return SWZ ? 2 * kH + r * kS2 : r * kRow + kH; }
+  __device__ static constexpr int oDL(int r) {
+    return SWZ ? 2 * (kH + kS2) + r * kSmall : r * kRow + kH + kS2;
+  }
+  __device__ static constexpr int oU(int r) { return oDL(r) + kDL; }
+  __device__ static constexpr int oB(int r) { return oDL(r) + 2 * kDL; }
+  __device__ static constexpr int oC(int r) { return oB(r) + kBC; }
   static_assert(kS2 % 16 == 0 && kBC % 16 == 0, "bulk copy destinations are 16-byte aligned");
+  static_assert(!SWZ || NP * 4 == 128, "the swizzled layout has 128-byte tile rows");
 };
+
+// n consecutive floats from float f0 of row `row` of a staged 32 x 32 fp32
+// tile written by a TMA copy with the 128-byte swizzle: the 16-byte chunk c of
+// tile row r lies at chunk c ^ (r & 7) (the tile starts on a 1 KB boundary).
+// Each VW-float piece is VW*4-byte aligned, so it stays inside one chunk.
+template <int n, int VW>
+__device__ __forceinline__ void ld_vec_swz(const unsigned char* tile, int row, int f0, float* v) {
+#pragma unroll
+  for (int i = 0; i < n / VW; ++i) {
+    const int byte = (f0 + i * VW) * 4;
+    const int phys = row * 128 + ((((byte >> 4) ^ (row & 7)) << 4) | (byte & 15));
+    if constexpr (VW == 4) {
+      const float4 x = *reinterpret_cast<const float4*>(tile + phys);
+      v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+    } else if constexpr (VW == 2) {
+      const float2 x = *reinterpret_cast<const float2*>(tile + phys);
+      v[2 * i] = x.x; v[2 * i + 1] = x.y;
+    } else {
+      v[i] = *reinterpret_cast<const float*>(tile + phys);
+    }
+  }
+}
 
 // n fp32 (dt == M3_F32) or bf16 values of a staged row, widened to fp32.
 template <int n>
@@ -334,19 +376,24 @@ __device__ __forceinline__ void ld_staged(const unsigned char* base, int off, bo
   else ld_vec<n, vec_width(n)>(reinterpret_cast<const float*>(base) + off, v);
 }
 
-template <int R, int T, bool FACT>
-__global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_bulk_kernel(const StepParams p,
-                                                                int pairs_per_cta) {
+template <int R, int T, bool FACT, bool SWZ>
+__global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
+    step_bulk_kernel(const StepParams p, int pairs_per_cta,
+                     const __grid_constant__ CUtensorMap tmap_h,
+                     const __grid_constant__ CUtensorMap tmap_d) {
   using LM = LaneMap<R, T>;
   constexpr int NL = R + T;
   constexpr int NP = LM::NP;
   constexpr int RR = R > 0 ? R : 1;
   constexpr int TT = T > 0 ? T : 1;
   constexpr int VR = vec_width(RR), VT = vec_width(TT);
-  using SL = BulkStage<NP, FACT>;
+  using SL = BulkStage<NP, FACT, SWZ>;
   constexpr int kBulkStages = bulk_stages(FACT);
-  extern __shared__ __align__(128) unsigned char smem[];
-  // stage buffers, then one mbarrier per stage
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  // stage buffers (from the first 1 KB boundary when swizzled), then one
+  // mbarrier per stage
+  unsigned char* smem =
+      SWZ ? smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u) : smem_raw;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBulkStages * SL::kBytes);
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
@@ -391,19 +438,24 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_bulk_ke
     mbar_arrive_expect_tx(&full[s], nr * row_tx);
     for (int r = 0; r < nr; ++r) {
       const size_t b = (size_t)(b0 + r);
-      unsigned char* rs = st + r * SL::kRow;
-      bulk_g2s(rs + SL::oH, p.h + (b * D + d0) * NP, SL::kH, &full[s]);
+      if constexpr (SWZ) {
+        tma_load_2d(st + SL::oH(r), &tmap_h, 0, (int)(b * D + d0), &full[s]);
+      } else {
+        bulk_g2s(st + SL::oH(r), p.h + (b * D + d0) * NP, SL::kH, &full[s]);
+      }
       if constexpr (FACT) {
         const float* fac = p.fac_in + b * (D + NP);
-        bulk_g2s(rs + SL::oS2, fac + d0, 32 * 4, &full[s]);
-        bulk_g2s(rs + SL::oS2 + 32 * 4, fac + D, NP * 4, &full[s]);
+        bulk_g2s(st + SL::oS2(r), fac + d0, 32 * 4, &full[s]);
+        bulk_g2s(st + SL::oS2(r) + 32 * 4, fac + D, NP * 4, &full[s]);
+      } else if constexpr (SWZ) {
+        tma_load_2d(st + SL::oS2(r), &tmap_d, 0, (int)(b * D + d0), &full[s]);
       } else {
-        bulk_g2s(rs + SL::oS2, p.dbu + (b * D + d0) * NP, SL::kH, &full[s]);
+        bulk_g2s(st + SL::oS2(r), p.dbu + (b * D + d0) * NP, SL::kH, &full[s]);
       }
-      bulk_g2s(rs + SL::oDL, (const char*)p.delta + (b * D + d0) * esd, 32 * esd, &full[s]);
-      bulk_g2s(rs + SL::oU, (const char*)p.u + (b * D + d0) * esd, 32 * esd, &full[s]);
-      bulk_g2s(rs + SL::oB, (const char*)p.Bc + b * NP * esb, NP * esb, &full[s]);
-      bulk_g2s(rs + SL::oC, (const char*)p.Cc + b * NP * esb, NP * esb, &full[s]);
+      bulk_g2s(st + SL::oDL(r), (const char*)p.delta + (b * D + d0) * esd, 32 * esd, &full[s]);
+      bulk_g2s(st + SL::oU(r), (const char*)p.u + (b * D + d0) * esd, 32 * esd, &full[s]);
+      bulk_g2s(st + SL::oB(r), (const char*)p.Bc + b * NP * esb, NP * esb, &full[s]);
+      bulk_g2s(st + SL::oC(r), (const char*)p.Cc + b * NP * esb, NP * esb, &full[s]);
     }
   };
 
@@ -424,40 +476,48 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_bulk_ke
       float hv[2][NL], dv[2][NL], bv[2][NL], cv[2][NL], dlv[2], uv[2];
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        const unsigned char* rs = smem + s * SL::kBytes + r * SL::kRow;
+        const unsigned char* st = smem + s * SL::kBytes;
         if (r == 1 && !two) {
 #pragma unroll
           for (int j = 0; j < NL; ++j) { hv[r][j] = 0.f; dv[r][j] = 0.f; bv[r][j] = 0.f; cv[r][j] = 0.f; }
           dlv[r] = 0.f; uv[r] = 0.f;
           continue;
         }
-        const float* hs = reinterpret_cast<const float*>(rs + SL::oH) + grp * NP;
-        if constexpr (R > 0) ld_vec<R, VR>(hs + q * R, hv[r]);
-        if constexpr (T > 0) ld_vec<T, VT>(hs + 4 * R + q * T, hv[r] + R);
+        if constexpr (SWZ) {
+          if constexpr (R > 0) ld_vec_swz<R, VR>(st + SL::oH(r), grp, q * R, hv[r]);
+          if constexpr (T > 0) ld_vec_swz<T, VT>(st + SL::oH(r), grp, 4 * R + q * T, hv[r] + R);
+        } else {
+          const float* hs = reinterpret_cast<const float*>(st + SL::oH(r)) + grp * NP;
+          if constexpr (R > 0) ld_vec<R, VR>(hs + q * R, hv[r]);
+          if constexpr (T > 0) ld_vec<T, VT>(hs + 4 * R + q * T, hv[r] + R);
+        }
         if constexpr (FACT) {
-          const float dup = reinterpret_cast<const float*>(rs + SL::oS2)[grp];
-          const float* bp = reinterpret_cast<const float*>(rs + SL::oS2 + 32 * 4);
+          const float dup = reinterpret_cast<const float*>(st + SL::oS2(r))[grp];
+          const float* bp = reinterpret_cast<const float*>(st + SL::oS2(r) + 32 * 4);
           float bf[NL];
           if constexpr (R > 0) ld_vec<R, VR>(bp + q * R, bf);
           if constexpr (T > 0) ld_vec<T, VT>(bp + 4 * R + q * T, bf + R);
 #pragma unroll
           for (int j = 0; j < NL; ++j) dv[r][j] = __fmul_rn(dup, bf[j]);
+        } else if constexpr (SWZ) {
+          if constexpr (R > 0) ld_vec_swz<R, VR>(st + SL::oS2(r), grp, q * R, dv[r]);
+          if constexpr (T > 0) ld_vec_swz<T, VT>(st + SL::oS2(r), grp, 4 * R + q * T, dv[r] + R);
         } else {
-          const float* ds = reinterpret_cast<const float*>(rs + SL::oS2) + grp * NP;
+          const float* ds = reinterpret_cast<const float*>(st + SL::oS2(r)) + grp * NP;
           if constexpr (R > 0) ld_vec<R, VR>(ds + q * R, dv[r]);
           if constexpr (T > 0) ld_vec<T, VT>(ds + 4 * R + q * T, dv[r] + R);
         }
-        dlv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(rs + SL::oDL)[grp])
-                       : reinterpret_cast<const float*>(rs + SL::oDL)[grp];
-        uv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(rs + SL::oU)[grp])
-                      : reinterpret_cast<const float*>(rs + SL::oU)[grp];
+        dlv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + SL::oDL(r))[grp])
+                       : reinterpret_cast<const float*>(st + SL::oDL(r))[grp];
+        uv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + SL::oU(r))[grp])
+                      : reinterpret_cast<const float*>(st + SL::oU(r))[grp];
         if constexpr (R > 0) {
-          ld_staged<R>(rs + SL::oB, q * R, bf_bc, bv[r]);
-          ld_staged<R>(rs + SL::oC, q * R, bf_bc, cv[r]);
+          ld_staged<R>(st + SL::oB(r), q * R, bf_bc, bv[r]);
+          ld_staged<R>(st + SL::oC(r), q * R, bf_bc, cv[r]);
         }
         if constexpr (T > 0) {
-          ld_staged<T>(rs + SL::oB, 4 * R + q * T, bf_bc, bv[r] + R);
-          ld_staged<T>(rs + SL::oC, 4 * R + q * T, bf_bc, cv[r] + R);
+          ld_staged<T>(st + SL::oB(r), 4 * R + q * T, bf_bc, bv[r] + R);
+          ld_staged<T>(st + SL::oC(r), 4 * R + q * T, bf_bc, cv[r] + R);
         }
       }
 #pragma unroll
@@ -549,12 +609,45 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T)) step_bulk_ke
   }
 }
 
-template <int R, int T, bool FACT>
-cudaError_t launch_step_bulk_impl(const StepParams& p, cudaStream_t stream) {
-  using SL = BulkStage<4 * (R + T), FACT>;
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (no link against the driver library); null if unavailable.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+            cudaSuccess || q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// A (rows, 32) fp32 state tensor as a 2D tensor map whose box is one 32-channel
+// tile (32 rows of 128 bytes) with the 128-byte swizzle.
+bool encode_state_map(CUtensorMap* map, const float* base, size_t rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {32, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {32 * sizeof(float)};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t elem[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+             box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <int R, int T, bool FACT, bool SWZ>
+cudaError_t launch_step_bulk_kernel(const StepParams& p, cudaStream_t stream,
+                                    const CUtensorMap& mh, const CUtensorMap& md) {
+  using SL = BulkStage<4 * (R + T), FACT, SWZ>;
   constexpr int kBulkStages = bulk_stages(FACT);
-  auto kern = step_bulk_kernel<R, T, FACT>;
-  const int smem = kBulkStages * SL::kBytes + kBulkStages * (int)sizeof(uint64_t);
+  auto kern = step_bulk_kernel<R, T, FACT, SWZ>;
+  const int smem = kBulkStages * SL::kBytes + kBulkStages * (int)sizeof(uint64_t) +
+                   (SWZ ? 1024 : 0);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 0, occ = 0;
@@ -573,8 +666,23 @@ cudaError_t launch_step_bulk_impl(const StepParams& p, cudaStream_t stream) {
   const int per = (npairs + g - 1) / g;
   g = (npairs + per - 1) / per;
   dim3 grid(g, tiles);
-  kern<<<grid, kThreads, smem, stream>>>(p, per);
+  kern<<<grid, kThreads, smem, stream>>>(p, per, mh, md);
   return cudaGetLastError();
+}
+
+
+template <int R, int T, bool FACT>
+cudaError_t launch_step_bulk_impl(const StepParams& p, cudaStream_t stream) {
+  CUtensorMap mh, md;
+  memset(&mh, 0, sizeof(mh));
+  memset(&md, 0, sizeof(md));
+  if constexpr (4 * (R + T) == 32) {
+    const size_t rows = (size_t)p.B * p.D;
+    if (getenv("M3_NO_SWIZZLE") == nullptr && encode_state_map(&mh, p.h, rows) &&
+        (FACT || encode_state_map(&md, p.dbu, rows)))
+      return launch_step_bulk_kernel<R, T, FACT, true>(p, stream, mh, md);
+  }
+  return launch_step_bulk_kernel<R, T, FACT, false>(p, stream, mh, md);
 }
 
 template <int R, int T, bool FACT>

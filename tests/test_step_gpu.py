@@ -199,9 +199,10 @@ def test_unaligned_rows_take_the_scalar_path_with_equal_results(dtype):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_pipelined_step_equals_register_path(n_track, dtype, monkeypatch):
     """Aligned dense tiles go through the bulk-copy pipeline (several row pairs
-    per CTA, so every stage is reused, and an odd last row); the per-row
-    register path (M3_NO_BULK) must give the same bits, for the full and
-    the factored state, over several consecutive steps."""
+    per CTA, so every stage is reused, and an odd last row), 32-lane tiles with
+    swizzled 2D TMA state tiles; the 1D bulk rows (M3_NO_SWIZZLE) and the
+    per-row register path (M3_NO_BULK) must give the same bits, for the full
+    and the factored state, over several consecutive steps."""
     B, D, N, steps = 301, 1024, 32, 5
     gen = torch.Generator().manual_seed(31)
     sh = ScanShape(B, steps, D, N, n_track, 2)
@@ -210,11 +211,14 @@ def test_pipelined_step_equals_register_path(n_track, dtype, monkeypatch):
     fa0 = torch.randn(B, D + N, generator=gen).cuda()
     d0 = fa0[:, :D, None] * fa0[:, None, D:]
     runs = []
-    for no_bulk in (False, True):
-        if no_bulk:
+    # TMA 2D with the 128-byte swizzle (32-lane tiles), 1D bulk rows, register path
+    for mode in ("swizzle", "bulk", "register"):
+        monkeypatch.delenv("M3_NO_BULK", raising=False)
+        monkeypatch.delenv("M3_NO_SWIZZLE", raising=False)
+        if mode != "swizzle":
+            monkeypatch.setenv("M3_NO_SWIZZLE", "1")
+        if mode == "register":
             monkeypatch.setenv("M3_NO_BULK", "1")
-        else:
-            monkeypatch.delenv("M3_NO_BULK", raising=False)
         h, dbu, hf, fa = h0.clone(), d0.clone(), h0.clone(), fa0.clone()
         fb = torch.empty_like(fa)
         ys, yfs = [], []
@@ -226,7 +230,8 @@ def test_pipelined_step_equals_register_path(n_track, dtype, monkeypatch):
             fa, fb = fb, fa
         torch.cuda.synchronize()
         runs.append((torch.stack(ys), torch.stack(yfs), h, dbu, hf, fa))
-    for a, b in zip(runs[0], runs[1]):
-        assert torch.equal(a, b)
+    for other in runs[1:]:
+        for a, b in zip(runs[0], other):
+            assert torch.equal(a, b)
     assert torch.equal(runs[0][0], runs[0][1])
     assert S.device_error() == 0
