@@ -425,9 +425,11 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
 #pragma unroll
           for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
         }
-        const bool has_last = p.h_last != nullptr && c * kCK + ns == L;
-        chunk_fast = !has_last && __fmul_rn(mdl, maxai) <= kFastArgBound;
+        chunk_fast = __fmul_rn(mdl, maxai) <= kFastArgBound;
       }
+      // the step that writes the final state (return_state) takes the checked path
+      const bool has_last = p.h_last != nullptr && c * kCK + ns == L;
+      const int nfast = has_last ? ns - 1 : ns;
       // segments between checkpoint positions (p.cki divides kCK)
       const int seg_len = p.cki < kCK ? p.cki : kCK;
       for (int seg = 0; seg < ns; seg += seg_len) {
@@ -435,8 +437,10 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
         const int s = c * kCK + seg;
         if (p.ckpt != nullptr && s > 0 && (s & (p.cki - 1)) == 0) write_ckpt(s);
         if (chunk_fast) {
+          const int fend = min(send, nfast);
 #pragma unroll kFwdUnroll
-          for (int tt = seg; tt < send; ++tt) step(tt, std::true_type{});
+          for (int tt = seg; tt < fend; ++tt) step(tt, std::true_type{});
+          for (int tt = fend; tt < send; ++tt) step(tt, std::false_type{});
         } else {
           for (int tt = seg; tt < send; ++tt) step(tt, std::false_type{});
         }
