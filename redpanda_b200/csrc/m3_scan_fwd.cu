@@ -97,7 +97,9 @@ struct FwdSmem {
   static size_t bytes(bool bidir) { return off_y + (bidir ? 2 * (size_t)kCK * DT * 4 : 0); }
 };
 
-template <int R, int T, int ND, bool BULK>
+// STATE: the launch writes the final (h, dBu) (return_state); compiled apart so
+// that launches without it carry no code for the state-writing last step.
+template <int R, int T, int ND, bool BULK, bool STATE>
 __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(const FwdParams p) {
   using LM = LaneMap<R, T>;
   constexpr int NL = R + T;
@@ -339,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
           Bv[j] = bb[tt * NP + q * NL + j];
           Cv[j] = bc[tt * NP + q * NL + j];
         }
-        const bool last = !FASTC && (s == L - 1) && (p.h_last != nullptr);
+        const bool last = STATE && !FASTC && (s == L - 1) && (p.h_last != nullptr);
         float du[ND], mdl = 0.f;
 #pragma unroll
         for (int k = 0; k < ND; ++k) {
@@ -428,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
         chunk_fast = __fmul_rn(mdl, maxai) <= kFastArgBound;
       }
       // the step that writes the final state (return_state) takes the checked path
-      const bool has_last = p.h_last != nullptr && c * kCK + ns == L;
+      const bool has_last = STATE && p.h_last != nullptr && c * kCK + ns == L;
       const int nfast = has_last ? ns - 1 : ns;
       // segments between checkpoint positions (p.cki divides kCK)
       const int seg_len = p.cki < kCK ? p.cki : kCK;
@@ -455,12 +457,12 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
   if (fail) set_err(p.err, M3_ERR_DEVICE);
 }
 
-template <int R, int T, int ND, bool BULK>
+template <int R, int T, int ND, bool BULK, bool STATE>
 cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
   constexpr int NP = 4 * (R + T);
   constexpr int DT = 32 * ND;
   const size_t smem = FwdSmem<NP, DT, BULK>::bytes(p.direction == M3_DIR_BIDIR);
-  auto kern = scan_fwd_kernel<R, T, ND, BULK>;
+  auto kern = scan_fwd_kernel<R, T, ND, BULK, STATE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
@@ -474,7 +476,10 @@ cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
 #define M3_X(r, tt, nd, ndb, nthb, gs) \
   if (t.R == r && t.T == tt && t.ND == nd)                                  \
-    return p.bulk ? launch_fwd_impl<r, tt, nd, true>(p, s) : launch_fwd_impl<r, tt, nd, false>(p, s);
+    return p.h_last ? (p.bulk ? launch_fwd_impl<r, tt, nd, true, true>(p, s)       \
+                              : launch_fwd_impl<r, tt, nd, false, true>(p, s))     \
+                    : (p.bulk ? launch_fwd_impl<r, tt, nd, true, false>(p, s)      \
+                              : launch_fwd_impl<r, tt, nd, false, false>(p, s));
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;
