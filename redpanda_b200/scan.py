@@ -13,6 +13,8 @@ reference's fused-scan path:
 * ``m3_step_`` -- the in-place O(1) step recurrence (mamba.py:466-493)
 * ``m3_step_factored_`` -- the same step on the factored (h, [delta*u | B])
   state, half the HBM traffic, bit-identical results
+* ``verify`` -- the correctness gate (triton_scan.py:340-398): forward and all
+  gradients against a float64 torch recurrence, raising on a mismatch
 * ``m3_step_inputs`` / ``m3_step_gated_`` -- the fused step layer: softplus,
   BCNorm and MIMO fold in one launch (mamba.py:455-469), the recurrence with
   the gated output (y + u*D) * silu(z) in another (mamba.py:490-497)
@@ -511,6 +513,13 @@ def m3_step(state, delta_t, u_t, Bc_t, Cc_t, A_real, A_imag, track, n_rot, n_sta
                   for s in state)
     y = m3_step_(h, dbu, delta_t, u_t, Bc_t, Cc_t, A_real, A_imag, track, n_rot, n_state)
     return y, (h, dbu)
+
+
+def verify(device="cuda", thorough=True, verbose=True):
+    """The correctness gate of triton_scan.py:340-398 for these kernels: forward
+    and all gradients against a float64 torch recurrence; raises on mismatch."""
+    from .verify import verify as _verify
+    return _verify(device=device, thorough=thorough, verbose=verbose)
 
 
 def device_error(clear=True):

@@ -106,3 +106,19 @@ def test_oracle_step_matches_scan_within_reference_tolerance():
         yt, h, dbu = O.step_cells(h, dbu, i["delta"][:, t], i["u"][:, t], i["Bc"][:, t],
                                   i["Cc"][:, t], i["A_real"], i["A_imag"], i["track"])
         assert torch.allclose(yt, y[:, t], atol=1e-4)
+
+
+def test_verify_gate_recurrence_matches_oracle():
+    """The float64 recurrence the verify gate compares the kernels with is the
+    oracle's scan (CPU, float64)."""
+    from redpanda_b200 import verify as V
+    from redpanda_b200.synthetic import ScanShape, make_scan_inputs
+    for sh in (ScanShape(2, 9, 16, 8, 2, 2), ScanShape(1, 33, 24, 12, 0, 2),
+               ScanShape(2, 5, 8, 4, 4, 2)):
+        inp = make_scan_inputs(sh, seed=1)
+        d = {k: (None if v is None else v.double()) for k, v in inp.items()}
+        y = V._torch_scan(d["delta"], d["u"], d["Bc"], d["Cc"], d["A_real"], d["A_imag"],
+                          d["track"])
+        yr, _ = O.scan_with_grads(d["delta"], d["u"], d["Bc"], d["Cc"], d["A_real"],
+                                  d["A_imag"], d["track"], d["dy"])
+        assert (y - yr).abs().max().item() <= 1e-12 * max(1.0, yr.abs().max().item())

@@ -183,3 +183,9 @@ def test_bulk_staging_equals_cp_async_staging(name, shape, dtype, direction, mon
         if g0[k] is not None:
             assert torch.equal(g0[k], g1[k]), k
     assert S.device_error() == 0
+
+
+def test_verify_gate_passes():
+    """The drop-in module's gate (triton_scan.verify's counterpart), thorough
+    configuration list: forward and all gradients vs the float64 recurrence."""
+    assert S.verify(device="cuda", thorough=True, verbose=False) is True
