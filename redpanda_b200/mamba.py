@@ -173,7 +173,7 @@ class Mamba3Block(nn.Module):
         return self._selective_scan_trapezoidal(u, delta, A_real, A_imag, B, C, self.D,
                                                 return_state=return_state)
 
-    def _forward_inference(self, x, return_state):
+    def _forward_inference(self, x, return_state, residual=None):
         """No-grad layer forward on the fused kernels (mamba.py:231-282): after
         the in_proj / x_proj / dt_proj GEMMs, softplus + BCNorm + MIMO fold of
         every token is one launch (m3_step_inputs over B*L rows), the scan (or
@@ -204,7 +204,13 @@ class Mamba3Block(nn.Module):
         else:
             y, coef = S.m3_trapezoidal_scan(*args), 1.0
         y = S.m3_gate(y, u, xz[..., d_in:], self.D, coef, out=y)
-        out = self.out_proj(y)
+        if residual is None:
+            out = self.out_proj(y)
+        else:   # residual + out_proj(y) as one GEMM
+            op = self.out_proj
+            r2 = residual.reshape(-1, residual.shape[-1])
+            r2 = r2 if op.bias is None else r2 + op.bias
+            out = torch.addmm(r2, y.reshape(-1, y.shape[-1]), op.weight.t()).view(residual.shape)
         return (out, state) if return_state else out
 
     def forward(self, x):
@@ -339,6 +345,8 @@ class Mamba(nn.Module):
             if self.grad_checkpoint and self.training and x.requires_grad:
                 x = x + torch.utils.checkpoint.checkpoint(
                     lambda inp, m=mixer, nm=norm: m(nm(inp)), x, use_reentrant=False)
+            elif not torch.is_grad_enabled():   # out_proj and the residual add in one GEMM
+                x = mixer._forward_inference(norm(x), False, residual=x)
             else:
                 x = x + mixer(norm(x))
         return self.norm_f(x)
@@ -394,7 +402,11 @@ class Mamba(nn.Module):
         cur = self.embedding(input_ids)
         cache = []
         for layer in self.layers:
-            mixed, state = layer["mixer"].forward_with_state(layer["norm"](cur))
-            cur = cur + mixed
+            if not torch.is_grad_enabled():   # out_proj and the residual add in one GEMM
+                cur, state = layer["mixer"]._forward_inference(layer["norm"](cur), True,
+                                                               residual=cur)
+            else:
+                mixed, state = layer["mixer"].forward_with_state(layer["norm"](cur))
+                cur = cur + mixed
             cache.append(state)
         return self.norm_f(cur[:, -1, :]), cache
