@@ -110,8 +110,11 @@ def model_case(M, kw, seed, L, bidir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("REDPANDA_REFERENCE"),
+                    help="checkout of PranavPrasannaV/RedPanda (or set REDPANDA_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("--ref (or REDPANDA_REFERENCE) must name a reference checkout")
     sys.path.insert(0, os.path.join(args.ref, "redpanda", "engine"))
     import mamba as M  # the reference module, read-only
 
