@@ -91,3 +91,60 @@ def test_ops_refuse_cpu_tensors(fn):
     A = torch.zeros(8, 2)
     with pytest.raises(RuntimeError, match="CUDA"):
         getattr(S, fn)(x, x, b, b, A, A, A, 2, 4)
+
+
+def test_checkpoint_interval_of_the_gate_storing_layout():
+    """The (16 rotational + 16 tracking) lane layout checkpoints every 8 steps
+    (its backward keeps the gates in Tensor Memory), others every 16."""
+    lib = _lib.load()
+    c1 = dict(d_state=32, n_rot=16, d_inner=1536)
+    assert lib.m3_scan_ckpt_floats(ctypes.byref(_desc(seqlen=8, **c1))) == 0
+    assert lib.m3_scan_ckpt_floats(ctypes.byref(_desc(seqlen=64, **c1))) == 2 * 7 * 1536 * 32
+    assert lib.m3_scan_ckpt_floats(ctypes.byref(_desc(seqlen=64, direction=2, **c1))) == \
+        2 * 2 * 7 * 1536 * 32
+    c3 = dict(d_state=32, n_rot=24, d_inner=1024)
+    assert lib.m3_scan_ckpt_floats(ctypes.byref(_desc(seqlen=64, **c3))) == 2 * 3 * 1024 * 32
+
+
+def _sdesc(**kw):
+    base = dict(batch=4, d_inner=64, d_state=16, n_rot=12, dtype_du=0, dtype_bc=0)
+    base.update(kw)
+    return _lib.StepDesc(**base)
+
+
+def test_layer_entry_points_validate_before_device_work():
+    """m3_step_inputs, m3_step_inputs_bwd, m3_gate and m3_step_gated reject bad
+    arguments with their status codes before touching a device."""
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.cast(buf, ctypes.c_void_p).value    # host memory: never dereferenced
+    d = _sdesc()
+    # m3_step_inputs(desc, p, dt, ld_dt, xbc, ld_x, off_b, off_c, wb, wc, eps, delta, Bc, Cc, s)
+    assert lib.m3_step_inputs(None, 2, p, 64, p, 72, 8, 40, None, None, 1e-5, p, p, p, None) == 1
+    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 32, p, 72, 8, 40, None, None, 1e-5, p, p, p,
+                              None) == 2          # ld_dt < d_inner
+    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 64, p, 60, 8, 40, None, None, 1e-5, p, p, p,
+                              None) == 2          # C_raw past the row
+    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 64, p, 72, 8, 40, p, None, 1e-5, p, p, p,
+                              None) == 1          # one BCNorm weight without the other
+    assert lib.m3_step_inputs(ctypes.byref(d), 0, p, 64, p, 72, 8, 40, None, None, 1e-5, p, p, p,
+                              None) == 2          # mimo_p = 0
+    # m3_step_inputs_bwd: a BCNorm backward without a workspace
+    args = [ctypes.byref(d), 2, p, 64, p, 72, 8, 40, p, p, 1e-5, p, p, p, p, p, p, p, None, 0,
+            None]
+    assert lib.m3_step_inputs_bwd(*args) == 6
+    assert lib.m3_step_inputs_bwd_workspace_bytes(ctypes.byref(d), 2) > 0
+    # m3_gate(rows, D, y, u, dtype_u, z, ld_z, d_skip, coef, out, s)
+    assert lib.m3_gate(0, 64, p, p, 0, p, 64, p, 1.0, p, None) == 2
+    assert lib.m3_gate(4, 64, p, p, 0, p, 32, p, 1.0, p, None) == 2    # ld_z < D
+    assert lib.m3_gate(4, 64, p, p, 9, p, 64, p, 1.0, p, None) == 3    # dtype
+    assert lib.m3_gate(4, 64, None, p, 0, p, 64, p, 1.0, p, None) == 1
+    # m3_step_gated: exactly one state form, a z row stride >= D
+    g = [ctypes.byref(d), p, p, p, p, p, p, p, p, p, p, p, p, 64, p, p, None]
+    assert lib.m3_step_gated(*g) == 1                                  # both forms given
+    g[2] = None
+    g[4] = None
+    assert lib.m3_step_gated(*g) == 1                                  # neither form
+    g[2] = p
+    g[13] = 32
+    assert lib.m3_step_gated(*g) == 2                                  # ld_z < D
