@@ -1,746 +1,24 @@
-// K2: analytic backward of the trapezoidal scan, causal / reverse / both
-// directions, with deterministic reductions.
-//
-// Replaces _bwd_kernel (redpanda/engine/triton_scan.py:100-241) and the
-// backward half of _TrapezoidalScanFn (triton_scan.py:283-315).  Gradients, per
-// cell, with q[t] = dL/dh[t] and P[t] = 2h[t] + dBu[t]:
-//   q[t]     = dy[t]*C[t] + gate[t+1]*q[t+1]
-//   dgate[t] = 0.5*q[t]*P[t-1]                  (= q*h[t-1] + 0.5*q*dBu[t-1])
-//   ddBu[t]  = 0.5*q[t] + 0.5*gate[t+1]*q[t+1]  (= q[t] - 0.5*dy[t]*C[t])
-//   dA_real += dgate*delta*gate,  dA_imag -= dgate*delta*exp*sin,  dtrack += dgate
-//   ddelta   = sum_n dgate*(A_real*gate - A_imag*exp*sin) + u*sum_n ddBu*B
-//   du       = delta*sum_n ddBu*B
-//   dB[t,n]  = sum_d ddBu*delta*u,   dC[t,n] = sum_d dy*h[t]
-//
-// Work split: CTA (batch group bg, channel tile g) walks its rows b = bg,
-// bg + Bg, ... and, per row and direction, the KC-step chunks from last to
-// first.  Each chunk restarts from the forward's checkpoint of P, recomputes
-// the chunk forward storing P[t-1] of every cell in Tensor Memory, then runs
-// the reverse recurrence reading P back.  dA_real/dA_imag/dtrack accumulate in
-// registers over the CTA's rows and land in one partial per batch group;
-// dB/dC are reduced over the CTA's channels (warp shuffles + shared memory)
-// into one partial per channel tile.  A second kernel sums both partial sets in
-// a fixed order, so results are bitwise reproducible run to run.
-#include <type_traits>
-
-#include "m3_common.cuh"
-#include "m3_internal.h"
-#include "m3_stage.cuh"
-#include "m3_tiles.h"
-#include "m3_tmem.cuh"
-
-#ifndef M3_BWD_UNROLL_RECOMPUTE
-#define M3_BWD_UNROLL_RECOMPUTE 2
-#endif
-#ifndef M3_BWD_UNROLL_REVERSE
-#define M3_BWD_UNROLL_REVERSE 1
-#endif
+// K2 dispatch: tile and element-type selection for the analytic backward, the
+// element-wise-staging variants (run-time element types) and the fixed-order
+// reductions of the partials.  The bulk-staged variants, one per combination
+// of delta/u and dy element types, are compiled in m3_scan_bwd_bulk_*.cu (in
+// parallel) from the kernel template in m3_scan_bwd.cuh.
+#include "m3_scan_bwd.cuh"
 
 namespace m3 {
+
+// defined in m3_scan_bwd_bulk_<du><dy>.cu: launch the bulk-staged kernel of
+// tile t; *handled is false when the tile's bulk layout does not fit
+cudaError_t launch_bwd_bulk_bf16_bf16(const Tile& t, const BwdParams& p, cudaStream_t s,
+                                      bool* handled);
+cudaError_t launch_bwd_bulk_bf16_f32(const Tile& t, const BwdParams& p, cudaStream_t s,
+                                     bool* handled);
+cudaError_t launch_bwd_bulk_f32_bf16(const Tile& t, const BwdParams& p, cudaStream_t s,
+                                     bool* handled);
+cudaError_t launch_bwd_bulk_f32_f32(const Tile& t, const BwdParams& p, cudaStream_t s,
+                                    bool* handled);
+
 namespace {
-
-constexpr int kUnrollRecompute = M3_BWD_UNROLL_RECOMPUTE;
-constexpr int kUnrollReverse = M3_BWD_UNROLL_REVERSE;
-
-constexpr int pow2ceil(int x) {
-  int p = 1;
-  while (p < x) p <<= 1;
-  return p;
-}
-
-// Backward tiling: NDP channel pairs per thread (packed FP32), NTH threads.
-// GS: the recompute pass also keeps each step's rotational gates (exp*cos and
-// exp*sin) in Tensor Memory, so the reverse pass evaluates no transcendental;
-// the chunk is then KC = 8 steps so that state and gates fit.
-template <int R, int T, int ND, int NTH, bool GS, bool BULK>
-struct BwdCfg {
-  static_assert(ND % 2 == 0, "the backward processes channel pairs");
-  static constexpr int KC = GS ? 8 : kCK;           // chunk length (= checkpoint interval)
-  static constexpr int NL = R + T;
-  static constexpr int NP = 4 * NL;
-  static constexpr int NG = NTH / 4;                // channel groups
-  static constexpr int DT = NG * ND;                // channels per CTA
-  static constexpr int NDP = ND / 2;                // channel pairs per thread
-  static constexpr int C = ND * NL;                 // cells per thread
-  static constexpr int CG = GS ? ND * R * 2 : 0;    // gate values per thread and step
-  static constexpr int CS = pow2ceil(C + CG);       // TMEM columns per timestep
-  static constexpr int WG_COLS = KC * CS;           // TMEM columns per warpgroup
-  static constexpr int NCOLS = (NTH / 128) * WG_COLS < 32 ? 32 : (NTH / 128) * WG_COLS;
-  static constexpr int CPS = 512 / NCOLS < 1 ? 1 : 512 / NCOLS;   // CTAs per SM by TMEM
-  // WR: dB/dC partials are first reduced over the 8 channel groups of a warp
-  // with a transposed shuffle butterfly (2*NL values halved over lane bits
-  // 4, 3, 2), leaving one value per (step, B|C, lane, warp, quarter) in shared
-  // memory; the flush then sums the warps once per chunk.  Otherwise every
-  // thread stores its partials and the flush sums all groups every 4 steps.
-  static constexpr bool WR = (2 * (R + T)) % 8 == 0;
-  static constexpr int NW = NTH / 32;               // warps
-  static constexpr int FL = WR ? (KC < 8 ? KC : 8) : 4;   // steps per dB/dC/ddelta flush
-  static constexpr size_t raw_bytes = (size_t)KC * DT * 4;    // one staged (KC x DT) tile
-  // Reduction staging rows hold one value per thread (group-major, quarter-minor),
-  // so per-step stores are bank-conflict free; the row pitches are padded so
-  // the float4 reads of the flush hit distinct banks.
-  static constexpr int SR = NG * 4 + 16;                       // dB/dC row pitch
-  static constexpr int SG = NG * 4 + (16 / ND < 4 ? 4 : 16 / ND);  // ddelta row pitch
-  static constexpr size_t red_floats =
-      WR ? (size_t)FL * 2 * NL * NW * 4                           // [FL][2*NL][NW][4]
-         : (size_t)FL * 2 * NL * SR;                              // [FL][2][NL][SR]
-  static constexpr size_t gs_floats = (size_t)FL * ND * 2 * SG;    // [FL][ND][2][SG]
-  // BULK (16-byte staging): B/C rows land raw (HBM dtype, memory order) and
-  // are widened into the padded fp32 tiles after the copy; the bidirectional
-  // second pass stages the first pass's ddelta/du rows of the chunk.
-  static constexpr size_t braw_floats = BULK ? 2 * 2 * (size_t)KC * NP : 0;  // [2][B|C][KC][NP]
-  static constexpr size_t scr_floats = BULK ? (size_t)KC * DT * 2 : 0;       // [KC][DT][2]
-  static constexpr size_t smem_bytes =
-      3 * 2 * raw_bytes                       // delta, u, dy (HBM dtype), double-buffered
-      + 2 * (size_t)DT * NP * 4               // checkpoint tile, double-buffered
-      + 2 * 2 * (size_t)KC * NP * 4           // B, C (fp32), double-buffered
-      + red_floats * 4 + gs_floats * 4
-      + braw_floats * 4 + scr_floats * 4
-      + 16;                                   // TMEM address slot
-};
-
-// Stage a (KC x DT) tile of a (B, L, D) tensor for processing steps
-// [s0, s0 + KC) in its HBM dtype; rows past L and channels past D read zero.
-template <int DT, int NTH, int KC>
-__device__ __forceinline__ void stage_tile(unsigned char* dst, const void* src, int esz,
-                                           bool async_ok, int b, int d0, int s0, int dir,
-                                           int L, int D) {
-  if (async_ok) {
-    const int epw = 4 / esz, wpr = DT / epw;
-    for (int i = threadIdx.x; i < KC * wpr; i += NTH) {
-      const int tt = i / wpr, w = i - tt * wpr;
-      const int s = s0 + tt, d = d0 + w * epw;
-      const bool ok = (s < L) && (d < D);
-      const int t = dir ? L - 1 - s : s;
-      const size_t gi = ok ? ((size_t)b * L + t) * D + d : 0;
-      cp_async4(dst + (size_t)i * 4, (const char*)src + gi * esz, ok);
-    }
-  } else {
-    for (int i = threadIdx.x; i < KC * DT; i += NTH) {
-      const int tt = i / DT, dd = i - tt * DT;
-      const int s = s0 + tt, d = d0 + dd;
-      const bool ok = (s < L) && (d < D);
-      const int t = dir ? L - 1 - s : s;
-      const size_t gi = ok ? ((size_t)b * L + t) * D + d : 0;
-      if (esz == 2) ((uint16_t*)dst)[i] = ok ? ((const uint16_t*)src)[gi] : (uint16_t)0;
-      else ((float*)dst)[i] = ok ? ((const float*)src)[gi] : 0.f;
-    }
-  }
-}
-
-// One element of a staged (KC x DT) tile, converted to fp32.
-__device__ __forceinline__ float tile_at(const unsigned char* base, bool bf16, int idx) {
-  if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
-  return reinterpret_cast<const float*>(base)[idx];
-}
-
-template <int R, int T, int ND, int NTH, bool GS, bool BULK>
-__global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
-    scan_bwd_kernel(const BwdParams p) {
-  using LM = LaneMap<R, T>;
-  using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
-  constexpr int KC = CF::KC;
-  constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS, CG = CF::CG;
-  constexpr int NG = CF::NG, NDP = CF::NDP, FL = CF::FL, SR = CF::SR, SG = CF::SG;
-  constexpr int RR = R > 0 ? R : 1;
-  constexpr int TT = T > 0 ? T : 1;
-  constexpr int BCE = (KC * NP + NTH - 1) / NTH;
-  static_assert(CF::NCOLS <= 512, "TMEM holds at most 512 columns");
-
-  extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* s_dl = smem;                                        // [2][raw]
-  unsigned char* s_u = s_dl + 2 * CF::raw_bytes;                     // [2][raw]
-  unsigned char* s_dy = s_u + 2 * CF::raw_bytes;                     // [2][raw]
-  float* s_ck = reinterpret_cast<float*>(s_dy + 2 * CF::raw_bytes);  // [2][DT][NP]
-  float* s_b = s_ck + 2 * DT * NP;                                   // [2][KC][NP]
-  float* s_c = s_b + 2 * KC * NP;                                    // [2][KC][NP]
-  float* s_red = s_c + 2 * KC * NP;                                  // dB/dC staging (CF::WR)
-  float* s_gs = s_red + CF::red_floats;                              // [FL][ND][2][SG]
-  float* s_braw = s_gs + CF::gs_floats;                              // [2][B|C][KC][NP] (BULK)
-  float* s_scr = s_braw + CF::braw_floats;                           // [KC][DT][2] (BULK)
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_scr + CF::scr_floats);
-
-  const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
-  const int warp = tid >> 5;
-  const int bg = blockIdx.x, gt = blockIdx.y;
-  const int d0 = gt * DT, dbase = d0 + grp * ND;
-  const int B = p.B, L = p.L, D = p.D, N = p.N;
-  const bool bidir = p.direction == M3_DIR_BIDIR;
-  const int ndirs = bidir ? 2 : 1;
-  const int nch = p.nch;
-  const bool bf_du = p.dt_du == M3_BF16, bf_dy = p.dt_dy == M3_BF16;
-  const int es_du = bf_du ? 2 : 4, es_dy = bf_dy ? 2 : 4;
-  const bool async_du = p.async_du, async_dy = p.async_dy;
-
-  if (warp == 0) tmem_alloc(s_tmem, CF::NCOLS);
-  tmem_fence_before();
-  __syncthreads();
-  tmem_fence_after();
-  // warp w reads/writes TMEM lanes 32*(w%4).. of column block w/4
-  const uint32_t tbase =
-      *s_tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * CF::WG_COLS);
-
-  // parameters of the thread's cells, as channel pairs (k, k+1)
-  float2 AR[NDP][RR], A2[NDP][RR], AI[NDP][RR], TK[NDP][TT];
-  float maxai = 0.f;
-#pragma unroll
-  for (int k = 0; k < ND; ++k) {
-    const int d = dbase + k;
-#pragma unroll
-    for (int j = 0; j < NL; ++j) {
-      const int n = LM::mem_lane(q, j, p.NR, p.NT);
-      const bool ok = (d < D) && (n >= 0);
-      const size_t gi = ok ? (size_t)d * N + n : 0;
-      if (j < R) {
-        const float ar = ok ? p.Ar[gi] : 0.f, ai = ok ? p.Ai[gi] : 0.f;
-        maxai = fmaxf(maxai, fabsf(ai));
-        float2& r_ = AR[k >> 1][j]; float2& e_ = A2[k >> 1][j]; float2& i_ = AI[k >> 1][j];
-        if (k & 1) { r_.y = ar; e_.y = exp_const(ar); i_.y = ai; }
-        else       { r_.x = ar; e_.x = exp_const(ar); i_.x = ai; }
-      } else {
-        const float tv = ok ? p.Tk[gi] : 0.f;
-        if (k & 1) TK[k >> 1][j - R].y = tv; else TK[k >> 1][j - R].x = tv;
-      }
-    }
-  }
-
-  // dA accumulators: sum_t dl*wp*gate, sum_t dl*wp*exp*sin, sum_t wp (x 0.5 at the end;
-  // the second carries the sign of dA_imag)
-  float2 gAr[NDP][RR], gAi[NDP][RR], gTk[NDP][TT];
-#pragma unroll
-  for (int k = 0; k < NDP; ++k) {
-#pragma unroll
-    for (int j = 0; j < RR; ++j) { gAr[k][j] = f2(0.f); gAi[k][j] = f2(0.f); }
-#pragma unroll
-    for (int j = 0; j < TT; ++j) gTk[k][j] = f2(0.f);
-  }
-
-  const int cta = gt * p.Bg + bg;
-  float* scratch = p.scratch_du ? p.scratch_du + (size_t)cta * L * DT * 2 : nullptr;
-
-  // work items in processing order: rows b = bg, bg+Bg, ...; per row the
-  // directions; per direction the chunks from last to first
-  const int rows = bg < B ? (B - bg + p.Bg - 1) / p.Bg : 0;
-  const int per_row = ndirs * nch;
-  const int nitems = rows * per_row;
-  auto item = [&](int i, int& b, int& pass, int& c) {
-    const int r = i / per_row, rem = i - r * per_row;
-    b = bg + r * p.Bg;
-    pass = rem / nch;
-    c = nch - 1 - (rem - pass * nch);
-  };
-  auto dir_of = [&](int pass) { return bidir ? pass : p.direction; };
-
-  float rb[BCE], rc[BCE];
-  auto load_bc = [&](int b, int dir, int s0) {
-#pragma unroll
-    for (int e = 0; e < BCE; ++e) {
-      const int i = tid + e * NTH;
-      const int tt = i / NP, ln = i - tt * NP;
-      const int s = s0 + tt;
-      const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
-      const bool ok = (i < KC * NP) && (s < L) && (n >= 0);
-      const int t = dir ? L - 1 - s : s;
-      const size_t gi = ok ? ((size_t)b * L + t) * N + n : 0;
-      rb[e] = ok ? ld_f(p.Bc, gi, p.dt_bc) : 0.f;
-      rc[e] = ok ? ld_f(p.Cc, gi, p.dt_bc) : 0.f;
-    }
-  };
-  auto store_bc = [&](int buf) {
-#pragma unroll
-    for (int e = 0; e < BCE; ++e) {
-      const int i = tid + e * NTH;
-      if (i < KC * NP) {
-        s_b[buf * KC * NP + i] = rb[e];
-        s_c[buf * KC * NP + i] = rc[e];
-      }
-    }
-  };
-  auto stage = [&](int i, int buf) {
-    int b, pass, c;
-    item(i, b, pass, c);
-    const int dir = dir_of(pass), s0 = c * KC;
-    stage_tile<DT, NTH, KC>(s_dl + buf * CF::raw_bytes, p.delta, es_du, async_du, b, d0, s0, dir, L, D);
-    stage_tile<DT, NTH, KC>(s_u + buf * CF::raw_bytes, p.u, es_du, async_du, b, d0, s0, dir, L, D);
-    stage_tile<DT, NTH, KC>(s_dy + buf * CF::raw_bytes, p.dy, es_dy, async_dy, b, d0, s0, dir, L, D);
-    if (c > 0) {
-      const int dslot = bidir ? dir : 0;
-      const float* src = p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
-      float* dst = s_ck + buf * DT * NP;
-      for (int v = tid; v < DT * NP / 4; v += NTH) {
-        const bool ok = d0 + (v * 4) / NP < D;
-        cp_async16(dst + v * 4, ok ? src + v * 4 : p.ckpt, ok);
-      }
-    }
-  };
-
-  // BULK staging of work item i into buffer buf with 16-byte cp.async and
-  // shift-only index math (rows of DT channels are powers of two of 16-byte
-  // pieces): delta/u/dy rows, the checkpoint tile, and the chunk's B and C rows
-  // as one contiguous block each (rows in memory order; widen_bc reorders).
-  const int es_bc = p.dt_bc == M3_BF16 ? 2 : 4;
-  const int lg_du = 31 - __clz(DT * es_du / 16), lg_dy = 31 - __clz(DT * es_dy / 16);
-  auto stage_vec = [&](int i, int buf) {
-    int b, pass, c;
-    item(i, b, pass, c);
-    const int dir = dir_of(pass), s0 = c * KC;
-    const int ns = min(KC, L - s0);
-    for (int v = tid; v < (3 * ns) << lg_du; v += NTH) {
-      // tensor k (delta, u) uses lg_du; dy rows are handled below when its size differs
-      const int r = v >> lg_du, w = v - (r << lg_du);
-      const int kind = r / ns, tt = r - kind * ns;
-      if (kind == 2 && lg_dy != lg_du) break;
-      const int s = s0 + tt;
-      const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
-      const int es = kind == 2 ? es_dy : es_du;
-      const void* src = kind == 0 ? p.delta : (kind == 1 ? p.u : p.dy);
-      unsigned char* dst = (kind == 0 ? s_dl : (kind == 1 ? s_u : s_dy)) + buf * CF::raw_bytes;
-      cp_async16(dst + (size_t)tt * DT * es + w * 16,
-                 (const char*)src + (row * D + d0) * es + w * 16, true);
-    }
-    if (lg_dy != lg_du) {
-      for (int v = tid; v < ns << lg_dy; v += NTH) {
-        const int tt = v >> lg_dy, w = v - (tt << lg_dy);
-        const int s = s0 + tt;
-        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
-        cp_async16(s_dy + buf * CF::raw_bytes + (size_t)tt * DT * es_dy + w * 16,
-                   (const char*)p.dy + (row * D + d0) * es_dy + w * 16, true);
-      }
-    }
-    if (c > 0) {
-      const int dslot = bidir ? dir : 0;
-      const float* src = p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
-      float* dst = s_ck + buf * DT * NP;
-      for (int v = tid; v < DT * NP / 4; v += NTH) cp_async16(dst + v * 4, src + v * 4, true);
-    }
-    const int t_lo = dir ? L - s0 - ns : s0;             // first memory row of the chunk
-    const int pieces = ns * N * es_bc / 16;
-    for (int v = tid; v < 2 * pieces; v += NTH) {
-      const int which = v >= pieces, w = v - which * pieces;
-      const char* src = (const char*)(which ? p.Cc : p.Bc) + ((size_t)b * L + t_lo) * N * es_bc;
-      float* dst = s_braw + ((size_t)(buf * 2 + which) * KC) * NP;
-      cp_async16(reinterpret_cast<char*>(dst) + w * 16, src + w * 16, true);
-    }
-  };
-  // widen the raw B/C rows of buffer buf into the padded fp32 lane layout
-  // (processing step tt is memory row tt, or ns-1-tt for the reversed scan)
-  auto widen_bc = [&](int buf, int ns, int dir) {
-    for (int i = tid; i < ns * NP; i += NTH) {
-      const int tt = i / NP, ln = i - tt * NP;
-      const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
-      const size_t r = (size_t)(dir ? ns - 1 - tt : tt) * N + (n >= 0 ? n : 0);
-      const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * KC) * NP;
-      const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * KC) * NP;
-      s_b[buf * KC * NP + i] = n >= 0 ? ld_f(rb0, r, p.dt_bc) : 0.f;
-      s_c[buf * KC * NP + i] = n >= 0 ? ld_f(rc0, r, p.dt_bc) : 0.f;
-    }
-  };
-
-  float2 qv[NDP][NL], gn[NDP][RR];
-  if (nitems > 0) {
-    if constexpr (BULK) {
-      stage_vec(0, 0);
-      cp_async_commit();
-    } else {
-      stage(0, 0);
-      cp_async_commit();
-      int b, pass, c;
-      item(0, b, pass, c);
-      load_bc(b, dir_of(pass), c * KC);
-      store_bc(0);
-    }
-  }
-  for (int it = 0; it < nitems; ++it) {
-    const int buf = it & 1;
-    int b, pass, c;
-    item(it, b, pass, c);
-    const int dir = dir_of(pass);
-    const bool first_of_two = bidir && pass == 0;
-    const bool second_of_two = bidir && pass == 1;
-    const int s0 = c * KC;
-    const int ns = min(KC, L - s0);
-    const bool more = it + 1 < nitems;
-    if constexpr (BULK) {
-      // group 1: the first pass's ddelta/du rows of this chunk (written by this
-      // CTA before the previous barrier), needed from the first flush on
-      if (second_of_two) {
-        for (int v = tid; v < ns * (DT / 2); v += NTH) {
-          const int tt = v / (DT / 2), w = v - tt * (DT / 2);
-          const int s = s0 + tt;
-          const int t = dir ? L - 1 - s : s;
-          cp_async16(s_scr + (size_t)tt * DT * 2 + w * 4, scratch + (size_t)t * DT * 2 + w * 4, true);
-        }
-      }
-      cp_async_commit();
-      // group 2: the next work item
-      if (more) stage_vec(it + 1, buf ^ 1);
-      cp_async_commit();
-      cp_async_wait_n<2>();   // this item's staging (committed one iteration ago)
-      __syncthreads();
-      widen_bc(buf, ns, dir);
-      __syncthreads();
-    } else {
-      if (more) stage(it + 1, buf ^ 1);
-      cp_async_commit();
-      if (more) {
-        int b2, pass2, c2;
-        item(it + 1, b2, pass2, c2);
-        load_bc(b2, dir_of(pass2), c2 * KC);
-      }
-      cp_async_wait1();
-      __syncthreads();
-    }
-
-    if (c == nch - 1) {   // first chunk of a direction pass: adjoint state starts at zero
-#pragma unroll
-      for (int k = 0; k < NDP; ++k) {
-#pragma unroll
-        for (int j = 0; j < NL; ++j) qv[k][j] = f2(0.f);
-#pragma unroll
-        for (int j = 0; j < RR; ++j) gn[k][j] = f2(0.f);
-      }
-    }
-
-    const unsigned char* bdl = s_dl + buf * CF::raw_bytes;
-    const unsigned char* bu = s_u + buf * CF::raw_bytes;
-    const unsigned char* bdy = s_dy + buf * CF::raw_bytes;
-    const float* bb = s_b + buf * KC * NP;
-    const float* bc = s_c + buf * KC * NP;
-
-    // ---- forward recompute of the chunk; P[t-1] of every cell -> TMEM
-    float2 P[NDP][NL];
-    {
-      const float* ck = s_ck + buf * DT * NP + grp * ND * NP + q * NL;
-#pragma unroll
-      for (int k = 0; k < ND; ++k)
-#pragma unroll
-        for (int j = 0; j < NL; ++j) {
-          const float v = c > 0 ? ck[k * NP + j] : 0.f;
-          if (k & 1) P[k >> 1][j].y = v; else P[k >> 1][j].x = v;
-        }
-    }
-#pragma unroll kUnrollRecompute
-    for (int tt = 0; tt < ns; ++tt) {
-      tmem_store<C>(tbase + (uint32_t)(tt * CS), reinterpret_cast<const float(&)[C]>(P));
-      float dl[ND], uu[ND];
-      read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
-      read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
-      const float* rbv = bb + tt * NP + q * NL;
-      float mdl = 0.f;
-#pragma unroll
-      for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
-      // The fast/exact choice is made once per step (not per cell) so that the
-      // compiler emits two branch-free bodies instead of predicating both.
-      // GS: gates of this step, [channel pair][lane][exp*cos, exp*sin]
-      float2 GG[NDP][RR][2];
-      auto recompute = [&](auto fast_tag) {
-        constexpr bool FAST = decltype(fast_tag)::value;
-#pragma unroll
-        for (int kp = 0; kp < NDP; ++kp) {
-          const float2 dl2 = make_float2(dl[2 * kp], dl[2 * kp + 1]);
-          const float2 du2 = __fmul2_rn(dl2, make_float2(uu[2 * kp], uu[2 * kp + 1]));
-#pragma unroll
-          for (int j = 0; j < R; ++j) {
-            float2 g;
-            if constexpr (GS) {
-              const float2 e = gate_exp2(dl2, A2[kp][j]);
-              float2 sn, cs;
-              if constexpr (FAST) {
-                gate_sincos2_nocheck(dl2, AI[kp][j], sn, cs);
-              } else {
-                gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
-                gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
-              }
-              g = __fmul2_rn(e, cs);
-              GG[kp][j][0] = g;
-              GG[kp][j][1] = __fmul2_rn(e, sn);
-            } else if constexpr (FAST) {
-              g = __fmul2_rn(gate_exp2(dl2, A2[kp][j]), gate_cos2_nocheck(dl2, AI[kp][j]));
-            } else {
-              g = make_float2(rot_gate(dl2.x, A2[kp][j].x, AI[kp][j].x),
-                              rot_gate(dl2.y, A2[kp][j].y, AI[kp][j].y));
-            }
-            cell_update2(g, P[kp][j], du2, rbv[j]);
-          }
-#pragma unroll
-          for (int j = R; j < NL; ++j) cell_update2(TK[kp][j - R], P[kp][j], du2, rbv[j]);
-        }
-      };
-      if (__fmul_rn(mdl, maxai) <= kFastArgBound) recompute(std::true_type{});
-      else recompute(std::false_type{});
-      if constexpr (GS)
-        tmem_store<CG>(tbase + (uint32_t)(tt * CS + C), reinterpret_cast<const float(&)[CG]>(GG));
-    }
-    tmem_wait_st();
-
-    // ---- reverse recurrence, flushing dB/dC and ddelta/du every FL steps
-#pragma unroll kUnrollReverse
-    for (int tt = ns - 1; tt >= 0; --tt) {
-      const int slot = (ns - 1 - tt) % FL;
-      float2 Pp[NDP][NL];
-      float2 GG[NDP][RR][2];
-      tmem_load<C>(tbase + (uint32_t)(tt * CS), reinterpret_cast<float(&)[C]>(Pp));
-      if constexpr (GS)
-        tmem_load<CG>(tbase + (uint32_t)(tt * CS + C), reinterpret_cast<float(&)[CG]>(GG));
-      float dl[ND], uu[ND], dyv[ND];
-      read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
-      read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
-      read_chan<ND>(bdy + (size_t)(tt * DT + grp * ND) * es_dy, bf_dy, dyv);
-      const float* rbv = bb + tt * NP + q * NL;
-      const float* rcv = bc + tt * NP + q * NL;
-      float Bv[NL], Cv[NL];
-#pragma unroll
-      for (int j = 0; j < NL; ++j) { Bv[j] = rbv[j]; Cv[j] = rcv[j]; }
-      float mdl = 0.f;
-#pragma unroll
-      for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
-      tmem_wait_ld();
-      float2 pB[NL], pC[NL];
-      float* gsrow = s_gs + (size_t)slot * ND * 2 * SG + grp * 4 + q;
-      auto reverse_cells = [&](auto fast_tag) {
-      constexpr bool FAST = decltype(fast_tag)::value;
-#pragma unroll
-      for (int kp = 0; kp < NDP; ++kp) {
-        const float2 dl2 = make_float2(dl[2 * kp], dl[2 * kp + 1]);
-        const float2 du2 = __fmul2_rn(dl2, make_float2(uu[2 * kp], uu[2 * kp + 1]));
-        const float2 dy2 = make_float2(dyv[2 * kp], dyv[2 * kp + 1]);
-        float2 gs = f2(0.f), gsi = f2(0.f), sB = f2(0.f);
-#pragma unroll
-        for (int j = 0; j < R; ++j) {
-          const float2 pp = Pp[kp][j];
-          float2 g, es;
-          if constexpr (GS) {
-            g = GG[kp][j][0];
-            es = GG[kp][j][1];
-          } else {
-            const float2 e = gate_exp2(dl2, A2[kp][j]);
-            float2 sn, cs;
-            if constexpr (FAST) {
-              gate_sincos2_nocheck(dl2, AI[kp][j], sn, cs);
-            } else {
-              gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
-              gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
-            }
-            g = __fmul2_rn(e, cs);
-            es = __fmul2_rn(e, sn);
-          }
-          const float2 dbu = __fmul2_rn(du2, f2(Bv[j]));
-          const float2 H = __ffma2_rn(g, pp, dbu);
-          const float2 dyC = __fmul2_rn(dy2, f2(Cv[j]));
-          const float2 qn = __ffma2_rn(gn[kp][j], qv[kp][j], dyC);
-          const float2 ddbu = __ffma2_rn(f2(-0.5f), dyC, qn);
-          const float2 wp = __fmul2_rn(qn, pp);
-          const float2 wg = __fmul2_rn(wp, g);
-          const float2 ws = __fmul2_rn(wp, es);
-          gAr[kp][j] = __ffma2_rn(dl2, wg, gAr[kp][j]);
-          gAi[kp][j] = __ffma2_rn(dl2, ws, gAi[kp][j]);
-          gs = __ffma2_rn(AR[kp][j], wg, gs);
-          gsi = __ffma2_rn(AI[kp][j], ws, gsi);
-          sB = __ffma2_rn(ddbu, f2(Bv[j]), sB);
-          pB[j] = kp == 0 ? __fmul2_rn(ddbu, du2) : __ffma2_rn(ddbu, du2, pB[j]);
-          pC[j] = kp == 0 ? __fmul2_rn(dy2, H) : __ffma2_rn(dy2, H, pC[j]);
-          qv[kp][j] = qn;
-          gn[kp][j] = g;
-        }
-#pragma unroll
-        for (int j = R; j < NL; ++j) {
-          const float2 pp = Pp[kp][j];
-          const float2 g = TK[kp][j - R];
-          const float2 dbu = __fmul2_rn(du2, f2(Bv[j]));
-          const float2 H = __ffma2_rn(g, pp, dbu);
-          const float2 dyC = __fmul2_rn(dy2, f2(Cv[j]));
-          const float2 qn = __ffma2_rn(g, qv[kp][j], dyC);
-          const float2 ddbu = __ffma2_rn(f2(-0.5f), dyC, qn);
-          const float2 wp = __fmul2_rn(qn, pp);
-          gTk[kp][j - R] = __fadd2_rn(gTk[kp][j - R], wp);
-          sB = __ffma2_rn(ddbu, f2(Bv[j]), sB);
-          pB[j] = kp == 0 ? __fmul2_rn(ddbu, du2) : __ffma2_rn(ddbu, du2, pB[j]);
-          pC[j] = kp == 0 ? __fmul2_rn(dy2, H) : __ffma2_rn(dy2, H, pC[j]);
-          qv[kp][j] = qn;
-        }
-        // channel partials over this thread's lanes: gsum = sum(ar*wg) - sum(ai*ws), sB
-        const float2 gsum = __fadd2_rn(gs, __fmul2_rn(gsi, f2(-1.f)));
-        gsrow[(2 * (2 * kp) + 0) * SG] = gsum.x;
-        gsrow[(2 * (2 * kp) + 1) * SG] = sB.x;
-        gsrow[(2 * (2 * kp + 1) + 0) * SG] = gsum.y;
-        gsrow[(2 * (2 * kp + 1) + 1) * SG] = sB.y;
-      }
-      };
-      if (GS || __fmul_rn(mdl, maxai) <= kFastArgBound) reverse_cells(std::true_type{});
-      else reverse_cells(std::false_type{});
-      // dB/dC partial of this thread's channels
-      if constexpr (CF::WR) {
-        // transposed butterfly over the warp's 8 channel groups (lane bits 4..2):
-        // each round keeps half of the values and adds the partner's copy of it
-        constexpr int V = 2 * NL;
-        float v[V];
-#pragma unroll
-        for (int j = 0; j < NL; ++j) {
-          v[j] = __fadd_rn(pB[j].x, pB[j].y);
-          v[NL + j] = __fadd_rn(pC[j].x, pC[j].y);
-        }
-        const int lane = tid & 31;
-#pragma unroll
-        for (int r = 0; r < 3; ++r) {
-          const int m = 16 >> r, h = V >> (r + 1);
-          const bool up = (lane & m) != 0;
-#pragma unroll
-          for (int i = 0; i < h; ++i) {
-            const float keep = up ? v[h + i] : v[i];
-            const float send = up ? v[i] : v[h + i];
-            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
-          }
-        }
-        // lane (g, q) now holds values base .. base + V/8 - 1 of its quarter q
-        const int g = lane >> 2;
-        const int base = ((g >> 2) & 1) * (V / 2) + ((g >> 1) & 1) * (V / 4) + (g & 1) * (V / 8);
-#pragma unroll
-        for (int i = 0; i < V / 8; ++i)
-          s_red[(((size_t)slot * V + base + i) * CF::NW + warp) * 4 + q] = v[i];
-      } else {
-        float* r0 = s_red + (size_t)slot * 2 * NL * SR + grp * 4 + q;
-#pragma unroll
-        for (int j = 0; j < NL; ++j) {
-          r0[j * SR] = __fadd_rn(pB[j].x, pB[j].y);
-          r0[(NL + j) * SR] = __fadd_rn(pC[j].x, pC[j].y);
-        }
-      }
-      if (slot == FL - 1 || tt == 0) {
-        if constexpr (BULK) {
-          if (second_of_two) cp_async_wait_n<1>();   // the scratch group, not the prefetch
-        }
-        __syncthreads();
-        const int nsl = slot + 1;                 // slots in this flush
-        const int tt_hi = tt + slot;              // step of slot 0
-        if constexpr (CF::WR) {
-          // dB/dC: sum the warps' float4 (4 quarters) of each (slot, which, j)
-          // in warp order, write lanes j*4 + q of the partial
-          for (int row = tid; row < nsl * 2 * NL; row += NTH) {
-            const float4* src = reinterpret_cast<const float4*>(s_red) + (size_t)row * CF::NW;
-            float4 acc = src[0];
-#pragma unroll
-            for (int w = 1; w < CF::NW; ++w) {
-              const float4 v = src[w];
-              acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
-              acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
-            }
-            const int sl = row / (2 * NL), rem = row - sl * 2 * NL;
-            const int which = rem / NL, j = rem - which * NL;
-            const int s = s0 + tt_hi - sl;
-            const int t = dir ? L - 1 - s : s;
-            const int dslot = bidir ? dir : 0;
-            float4* dst = reinterpret_cast<float4*>(
-                p.part_bc + (((((size_t)gt * ndirs + dslot) * B + b) * L + t) * 2 + which) * NP +
-                j * 4);
-            *dst = acc;
-          }
-        }
-        // dB/dC: each (slot, which, j) row holds one value per (group, quarter);
-        // 4 threads sum it over the groups as float4s of the 4 quarters, in a
-        // fixed order, and write lanes j*4 + q of the partial.
-        for (int base = 0; !CF::WR && base < nsl * 2 * NL; base += NTH / 4) {
-          const int row = base + (tid >> 2), part = tid & 3;
-          const bool rok = row < nsl * 2 * NL;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (rok) {
-            const float* src = s_red + (size_t)row * SR;
-#pragma unroll 4
-            for (int g = part; g < NG; g += 4) {
-              const float4 v = *reinterpret_cast<const float4*>(src + g * 4);
-              acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
-              acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
-            }
-          }
-#pragma unroll
-          for (int m = 1; m < 4; m <<= 1) {
-            acc.x = __fadd_rn(acc.x, __shfl_xor_sync(0xffffffffu, acc.x, m));
-            acc.y = __fadd_rn(acc.y, __shfl_xor_sync(0xffffffffu, acc.y, m));
-            acc.z = __fadd_rn(acc.z, __shfl_xor_sync(0xffffffffu, acc.z, m));
-            acc.w = __fadd_rn(acc.w, __shfl_xor_sync(0xffffffffu, acc.w, m));
-          }
-          if (rok && part == 0) {
-            const int sl = row / (2 * NL), rem = row - sl * 2 * NL;
-            const int which = rem / NL, j = rem - which * NL;
-            const int s = s0 + tt_hi - sl;
-            const int t = dir ? L - 1 - s : s;
-            // one partial per (channel tile, direction): no read-modify-write
-            const int dslot = bidir ? dir : 0;
-            float4* dst = reinterpret_cast<float4*>(
-                p.part_bc + (((((size_t)gt * ndirs + dslot) * B + b) * L + t) * 2 + which) * NP +
-                j * 4);
-            *dst = acc;
-          }
-        }
-        // ddelta / du per channel: sum the 4 lane-quarter partials
-        for (int i = tid; i < nsl * DT; i += NTH) {
-          const int sl = i / DT, dd = i - sl * DT;
-          const int d = d0 + dd;
-          if (d < D) {
-            const int tts = tt_hi - sl;
-            const float* g4p = s_gs + ((size_t)(sl * ND + dd % ND) * 2) * SG + (dd / ND) * 4;
-            const float4 g4 = *reinterpret_cast<const float4*>(g4p);
-            const float4 b4 = *reinterpret_cast<const float4*>(g4p + SG);
-            const float gsv = __fadd_rn(__fadd_rn(g4.x, g4.y), __fadd_rn(g4.z, g4.w));
-            const float sBv = __fadd_rn(__fadd_rn(b4.x, b4.y), __fadd_rn(b4.z, b4.w));
-            const float dlv = tile_at(bdl, bf_du, tts * DT + dd);
-            const float uv = tile_at(bu, bf_du, tts * DT + dd);
-            float ddl = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, uv));
-            float ddu = __fmul_rn(sBv, dlv);
-            const int s = s0 + tts;
-            const int t = dir ? L - 1 - s : s;
-            float* sc = scratch ? scratch + ((size_t)t * DT + dd) * 2 : nullptr;
-            if (first_of_two) {
-              sc[0] = ddl;
-              sc[1] = ddu;
-            } else {
-              if (second_of_two) {
-                const float* scv = BULK ? s_scr + ((size_t)tts * DT + dd) * 2 : sc;
-                ddl = __fadd_rn(scv[0], ddl);
-                ddu = __fadd_rn(scv[1], ddu);
-              }
-              const size_t oi = ((size_t)b * L + t) * D + d;
-              st_f(p.d_delta, oi, p.dt_du, ddl);
-              st_f(p.d_u, oi, p.dt_du, ddu);
-            }
-          }
-        }
-        __syncthreads();
-      }
-    }
-    if constexpr (!BULK) {
-      if (more) store_bc(buf ^ 1);
-    }
-  }
-  cp_async_wait0();
-
-  // dA partial of this batch group
-#pragma unroll
-  for (int k = 0; k < ND; ++k) {
-    const int d = dbase + k;
-    if (d < D) {
-      float* a0 = p.part_a + (((size_t)bg * 3 + 0) * D + d) * NP + q * NL;
-      float* a1 = p.part_a + (((size_t)bg * 3 + 1) * D + d) * NP + q * NL;
-      float* a2 = p.part_a + (((size_t)bg * 3 + 2) * D + d) * NP + q * NL;
-#pragma unroll
-      for (int j = 0; j < R; ++j) {
-        a0[j] = (k & 1) ? gAr[k >> 1][j].y : gAr[k >> 1][j].x;
-        a1[j] = -((k & 1) ? gAi[k >> 1][j].y : gAi[k >> 1][j].x);
-        a2[j] = 0.f;
-      }
-#pragma unroll
-      for (int j = R; j < NL; ++j) {
-        a0[j] = 0.f;
-        a1[j] = 0.f;
-        a2[j] = (k & 1) ? gTk[k >> 1][j - R].y : gTk[k >> 1][j - R].x;
-      }
-    }
-  }
-
-  tmem_fence_before();
-  __syncthreads();
-  tmem_fence_after();
-  if (warp == 0) tmem_dealloc(*s_tmem, CF::NCOLS);
-}
 
 // ---------------------------------------------------------------- reductions
 // Lane index (q*NL + j) of memory state lane n.
@@ -798,45 +76,26 @@ __global__ void reduce_a_kernel(const ReduceParams p, int R, int T) {
   }
 }
 
-// Largest dynamic shared memory of one CTA on sm_100 (227 KB); tiles whose
-// bulk-staging layout does not fit use the cp.async staging.
-constexpr size_t kMaxSmemPerCta = 227 * 1024;
-
-template <int R, int T, int ND, int NTH, bool GS, bool BULK>
-cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
-  using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
-  static_assert(CF::smem_bytes <= kMaxSmemPerCta, "backward tile exceeds shared memory");
-  auto kern = scan_bwd_kernel<R, T, ND, NTH, GS, BULK>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)CF::smem_bytes);
-  if (e != cudaSuccess) return e;
-  dim3 grid(p.Bg, p.G);
-  kern<<<grid, NTH, CF::smem_bytes, stream>>>(p);
-  return cudaGetLastError();
-}
-
-// Bulk staging when the caller's layout allows it and the tile's bulk layout
-// fits in shared memory; cp.async staging otherwise.
-template <int R, int T, int ND, int NTH, bool GS>
-cudaError_t launch_bwd_tile(const BwdParams& p, cudaStream_t stream) {
-  if constexpr (BwdCfg<R, T, ND, NTH, GS, true>::smem_bytes <= kMaxSmemPerCta) {
-    if (p.bulk) return launch_bwd_impl<R, T, ND, NTH, GS, true>(p, stream);
-  }
-  return launch_bwd_impl<R, T, ND, NTH, GS, false>(p, stream);
-}
-
 }  // namespace
 
 cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s) {
+  if (p.bulk) {
+    bool handled = false;
+    const bool du = p.dt_du == M3_BF16, dy = p.dt_dy == M3_BF16;
+    const cudaError_t e = du ? (dy ? launch_bwd_bulk_bf16_bf16(t, p, s, &handled)
+                                   : launch_bwd_bulk_bf16_f32(t, p, s, &handled))
+                             : (dy ? launch_bwd_bulk_f32_bf16(t, p, s, &handled)
+                                   : launch_bwd_bulk_f32_f32(t, p, s, &handled));
+    if (handled) return e;
+  }
 #define M3_X(r, tt, nd, ndb, nthb, gs)                                              \
   if constexpr (ndb > 0)                                                            \
     if (t.R == r && t.T == tt && t.ND == nd)                                        \
-      return launch_bwd_tile<r, tt, ndb, nthb, (gs != 0)>(p, s);
+      return bwd::launch_bwd_impl<r, tt, ndb, nthb, (gs != 0), false, -1, -1>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;
 }
-
 cudaError_t launch_bwd_reduce(const Tile& t, const ReduceParams& p, cudaStream_t s) {
   const int threads = 256;
   const size_t nbc = (size_t)p.B * p.L * p.N;

@@ -1,485 +1,28 @@
-// K1/K3: forward trapezoidal scan (causal, reverse, or both directions fused
-// into one launch) with optional chunk checkpoints for the backward and the
-// final (h, dBu) state for the O(1) step.
-//
-// Replaces _fwd_kernel (redpanda/engine/triton_scan.py:44-98) and the two
-// flipped launches of the bidirectional Eval Mamba (redpanda/engine/mamba.py:254-260).
-//
-// CTA = 128 threads = 32 channel groups x 4 state-lane quarters.  A thread owns
-// ND consecutive channels x (R rotational + T tracking) state lanes and walks
-// the sequence in registers.  delta/u tiles of kCK timesteps are staged into
-// shared memory with cp.async (double-buffered, in their HBM dtype); B/C are
-// register-prefetched one chunk ahead, converted to fp32 and padded to the
-// thread lane layout.  y is reduced over the 4 lane quarters with shuffles.
-#include "m3_bulk.cuh"
-#include "m3_common.cuh"
-#include "m3_internal.h"
-#include "m3_stage.cuh"
-#include "m3_tiles.h"
-
-#include <type_traits>
+// K1/K3 dispatch: tile, element-type and variant selection of the forward scan.
+// The element-wise-staging variants (run-time element type) are compiled here;
+// the bulk-staged variants, one translation unit per (delta/u element type,
+// return_state) pair, in m3_scan_fwd_bulk_*.cu from the kernel template in
+// m3_scan_fwd.cuh, so that the build compiles them in parallel.
+#include "m3_scan_fwd.cuh"
 
 namespace m3 {
-namespace {
 
-// Stage delta and u for processing steps [s0, s0 + kCK) of row b, channels
-// [d0, d0 + DT), in their HBM dtype, into one shared buffer pair.  Rows past the
-// sequence end and channels past D are zero-filled.
-template <int DT>
-__device__ __forceinline__ void stage_du(unsigned char* s_dl, unsigned char* s_u,
-                                         const FwdParams& p, int b, int d0, int s0,
-                                         int dir, int esz) {
-  if (p.async_ok) {
-    const int epw = 4 / esz;        // elements per 4-byte word
-    const int wpr = DT / epw;       // words per staged row
-    for (int i = threadIdx.x; i < kCK * wpr; i += kThreads) {
-      const int tt = i / wpr, w = i - tt * wpr;
-      const int s = s0 + tt, d = d0 + w * epw;
-      const bool ok = (s < p.L) && (d < p.D);
-      const int t = dir ? p.L - 1 - s : s;
-      const size_t gi = ok ? ((size_t)b * p.L + t) * p.D + d : 0;
-      cp_async4(s_dl + (size_t)i * 4, (const char*)p.delta + gi * esz, ok);
-      cp_async4(s_u + (size_t)i * 4, (const char*)p.u + gi * esz, ok);
-    }
-  } else {
-    for (int i = threadIdx.x; i < kCK * DT; i += kThreads) {
-      const int tt = i / DT, dd = i - tt * DT;
-      const int s = s0 + tt, d = d0 + dd;
-      const bool ok = (s < p.L) && (d < p.D);
-      const int t = dir ? p.L - 1 - s : s;
-      const size_t gi = ok ? ((size_t)b * p.L + t) * p.D + d : 0;
-      if (esz == 2) {
-        const uint16_t* a = (const uint16_t*)p.delta;
-        const uint16_t* c = (const uint16_t*)p.u;
-        ((uint16_t*)s_dl)[i] = ok ? a[gi] : 0;
-        ((uint16_t*)s_u)[i] = ok ? c[gi] : 0;
-      } else {
-        ((float*)s_dl)[i] = ok ? ((const float*)p.delta)[gi] : 0.f;
-        ((float*)s_u)[i] = ok ? ((const float*)p.u)[gi] : 0.f;
-      }
-    }
-  }
-}
-
-// Stage y (fp32) of processing steps [s0, s0 + kCK) for the second pass of the
-// bidirectional scan, which adds the first pass's output.
-template <int DT>
-__device__ __forceinline__ void stage_y(float* s_y, const FwdParams& p, int b, int d0, int s0,
-                                        int dir) {
-  for (int i = threadIdx.x; i < kCK * DT; i += kThreads) {
-    const int tt = i / DT, dd = i - tt * DT;
-    const int s = s0 + tt, d = d0 + dd;
-    const bool ok = (s < p.L) && (d < p.D);
-    const int t = dir ? p.L - 1 - s : s;
-    const size_t gi = ok ? ((size_t)b * p.L + t) * p.D + d : 0;
-    cp_async4(s_y + i, p.y + gi, ok);
-  }
-}
-
-#ifndef M3_FWD_UNROLL
-#define M3_FWD_UNROLL 2
-#endif
-constexpr int kFwdUnroll = M3_FWD_UNROLL;
-
-#ifndef M3_FWD_MIN_BLOCKS
-#define M3_FWD_MIN_BLOCKS 3
-#endif
-
-// Shared memory of the forward kernel (bytes): delta, u (HBM dtype, 4 bytes
-// reserved per element), B, C (padded fp32), raw B/C rows and two mbarriers
-// (BULK staging), y of the first pass (bidirectional second pass only).
-template <int NP, int DT, bool BULK>
-struct FwdSmem {
-  static constexpr size_t du = (size_t)kCK * DT * 4;             // one buffer of delta or u
-  static constexpr size_t bc = (size_t)kCK * NP * 8;             // one buffer of B or C pairs
-  static constexpr size_t braw = BULK ? 2 * 2 * (size_t)kCK * NP * 4 : 0;   // [2][B|C][kCK][NP]
-  static constexpr size_t off_y = 2 * 2 * du + 2 * 2 * bc + braw + 16;
-  static size_t bytes(bool bidir) { return off_y + (bidir ? 2 * (size_t)kCK * DT * 4 : 0); }
-};
-
-// STATE: the launch writes the final (h, dBu) (return_state); compiled apart so
-// that launches without it carry no code for the state-writing last step.
-template <int R, int T, int ND, bool BULK, bool STATE>
-__global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(const FwdParams p) {
-  using LM = LaneMap<R, T>;
-  constexpr int NL = R + T;
-  constexpr int NP = LM::NP;
-  constexpr int DT = 32 * ND;
-  constexpr int RR = R > 0 ? R : 1;
-  constexpr int TT = T > 0 ? T : 1;
-  constexpr int BCE = (kCK * NP + kThreads - 1) / kThreads;   // B/C prefetch per thread
-
-  using SM = FwdSmem<NP, DT, BULK>;
-  extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* s_dl = smem;                                 // [2][kCK*DT*4]
-  unsigned char* s_u = s_dl + 2 * kCK * DT * 4;               // [2][kCK*DT*4]
-  // B and C of each staged step in the padded lane layout, as (b, b) pairs so
-  // that packed instructions take them without a broadcast
-  float2* s_b = reinterpret_cast<float2*>(s_u + 2 * kCK * DT * 4);  // [2][kCK][NP]
-  float2* s_c = s_b + 2 * kCK * NP;
-  float* s_braw = reinterpret_cast<float*>(s_c + 2 * kCK * NP);     // [2][B|C][kCK][NP] (BULK)
-  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + SM::off_y - 16);   // [2] (BULK)
-  float* s_y = reinterpret_cast<float*>(smem + SM::off_y);    // [2][kCK][DT] (bidir pass 2)
-
-  const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
-  const int b = blockIdx.x;
-  const int d0 = blockIdx.y * DT;
-  const int dbase = d0 + grp * ND;
-  const bool bf16 = p.dt_du == M3_BF16;
-  const int esz = bf16 ? 2 : 4;
-  const int L = p.L, D = p.D, N = p.N;
-
-  // Eigenvalues of this thread's cells (zero for virtual lanes / channels),
-  // held as channel pairs (k, k+1) so the packed FP32 path can use them.
-  constexpr int NDP = (ND + 1) / 2;
-  float2 A2[NDP][RR], AI[NDP][RR], TK[NDP][TT];
-  float maxai = 0.f;   // max |A_imag| over the thread's cells (fast-path bound)
-#pragma unroll
-  for (int k = 0; k < 2 * NDP; ++k) {
-    const int d = dbase + k;
-#pragma unroll
-    for (int j = 0; j < NL; ++j) {
-      const int n = LM::mem_lane(q, j, p.NR, p.NT);
-      const bool ok = (k < ND) && (d < D) && (n >= 0);
-      const size_t gi = ok ? (size_t)d * N + n : 0;
-      if (j < R) {
-        const float a2 = ok ? exp_const(p.Ar[gi]) : 0.f;   // A_real * log2(e)
-        const float ai = ok ? p.Ai[gi] : 0.f;
-        maxai = fmaxf(maxai, fabsf(ai));
-        if (k & 1) { A2[k >> 1][j].y = a2; AI[k >> 1][j].y = ai; }
-        else       { A2[k >> 1][j].x = a2; AI[k >> 1][j].x = ai; }
-      } else {
-        const float tv = ok ? p.Tk[gi] : 0.f;
-        if (k & 1) TK[k >> 1][j - R].y = tv;
-        else       TK[k >> 1][j - R].x = tv;
-      }
-    }
-  }
-
-  const int es_bc = p.dt_bc == M3_BF16 ? 2 : 4;
-  if constexpr (BULK) {
-    if (tid == 0) {
-      mbar_init(&s_bar[0], 1);
-      mbar_init(&s_bar[1], 1);
-      mbar_fence_init();
-    }
-    __syncthreads();
-  }
-  int phase[2] = {0, 0};   // completed uses of each staging buffer (BULK)
-  int fail = 0;
-
-  const int npass = p.direction == M3_DIR_BIDIR ? 2 : 1;
-  for (int pass = 0; pass < npass && !fail; ++pass) {
-    const int dir = p.direction == M3_DIR_BIDIR ? (pass == 0 ? 1 : 0) : p.direction;
-    const bool accumulate = p.direction == M3_DIR_BIDIR && pass == 1;
-    const int dslot = p.direction == M3_DIR_BIDIR ? dir : 0;
-    const int ndirs = p.direction == M3_DIR_BIDIR ? 2 : 1;
-
-    float2 P[NDP][NL];   // P = 2h + dBu of cells (k, j): component k&1 of P[k/2][j]
-#pragma unroll
-    for (int k = 0; k < NDP; ++k)
-#pragma unroll
-      for (int j = 0; j < NL; ++j) P[k][j] = make_float2(0.f, 0.f);
-
-    float rb[BCE], rc[BCE];
-    auto load_bc = [&](int s0) {
-#pragma unroll
-      for (int e = 0; e < BCE; ++e) {
-        const int i = tid + e * kThreads;
-        const int tt = i / NP, lane = i - tt * NP;
-        const int s = s0 + tt;
-        const int n = LM::mem_lane(lane / NL, lane % NL, p.NR, p.NT);
-        const bool ok = (i < kCK * NP) && (s < L) && (n >= 0);
-        const int t = dir ? L - 1 - s : s;
-        const size_t gi = ok ? ((size_t)b * L + t) * N + n : 0;
-        rb[e] = ok ? ld_f(p.Bc, gi, p.dt_bc) : 0.f;
-        rc[e] = ok ? ld_f(p.Cc, gi, p.dt_bc) : 0.f;
-      }
-    };
-    auto store_bc = [&](int buf) {
-#pragma unroll
-      for (int e = 0; e < BCE; ++e) {
-        const int i = tid + e * kThreads;
-        if (i < kCK * NP) {
-          s_b[buf * kCK * NP + i] = f2(rb[e]);
-          s_c[buf * kCK * NP + i] = f2(rc[e]);
-        }
-      }
-    };
-
-    // BULK: warp 0 stages chunk c (delta, u, B, C rows) with one bulk copy per
-    // row, lane 0 first registering the byte count on the buffer's mbarrier;
-    // the first pass's y rows (second pass) move with 16-byte cp.async.
-    auto stage_bulk = [&](int c, int buf) {
-      const int s0 = c * kCK, ns = min(kCK, L - s0);
-      const int lane = tid & 31;
-      if (lane == 0)
-        mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)ns * (uint32_t)(2 * DT * esz + 2 * N * es_bc));
-      __syncwarp();
-      for (int k = lane; k < 4 * ns; k += 32) {
-        const int tt = k >> 2, kind = k & 3;
-        const int s = s0 + tt;
-        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
-        if (kind < 2) {
-          unsigned char* dst = (kind == 0 ? s_dl : s_u) + buf * kCK * DT * 4 + (size_t)tt * DT * esz;
-          bulk_g2s(dst, (const char*)(kind == 0 ? p.delta : p.u) + (row * D + d0) * esz, DT * esz,
-                   &s_bar[buf]);
-        } else {
-          float* dst = s_braw + ((size_t)(buf * 2 + (kind - 2)) * kCK + tt) * NP;
-          bulk_g2s(dst, (const char*)(kind == 2 ? p.Bc : p.Cc) + row * N * es_bc, N * es_bc,
-                   &s_bar[buf]);
-        }
-      }
-    };
-    auto stage_y16 = [&](int c, int buf) {
-      const int s0 = c * kCK, ns = min(kCK, L - s0);
-      for (int v = tid; v < ns * (DT / 4); v += kThreads) {
-        const int tt = v / (DT / 4), w = v - tt * (DT / 4);
-        const int s = s0 + tt;
-        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
-        cp_async16(s_y + (size_t)(buf * kCK + tt) * DT + w * 4, p.y + row * D + d0 + w * 4, true);
-      }
-    };
-    auto widen_bc = [&](int buf, int ns) {
-      for (int i = tid; i < ns * NP; i += kThreads) {
-        const int tt = i / NP, ln = i - tt * NP;
-        const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
-        const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * kCK + tt) * NP;
-        const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * kCK + tt) * NP;
-        s_b[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rb0, n, p.dt_bc) : 0.f);
-        s_c[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rc0, n, p.dt_bc) : 0.f);
-      }
-    };
-
-    // prologue: chunk 0 into buffer 0
-    if constexpr (BULK) {
-      if (tid < 32) stage_bulk(0, 0);
-      if (accumulate) stage_y16(0, 0);
-      cp_async_commit();
-    } else {
-      stage_du<DT>(s_dl, s_u, p, b, d0, 0, dir, esz);
-      if (accumulate) stage_y<DT>(s_y, p, b, d0, 0, dir);
-      cp_async_commit();
-      load_bc(0);
-      store_bc(0);
-    }
-
-    for (int c = 0; c < p.nch; ++c) {
-      const int buf = c & 1;
-      const bool more = c + 1 < p.nch;
-      if constexpr (BULK) {
-        if (more) {
-          if (tid < 32) stage_bulk(c + 1, buf ^ 1);
-          if (accumulate) stage_y16(c + 1, buf ^ 1);
-        }
-        cp_async_commit();
-        const bool ok = mbar_wait(&s_bar[buf], (uint32_t)(phase[buf] & 1));
-        ++phase[buf];
-        cp_async_wait1();
-        if (ok) widen_bc(buf, min(kCK, L - c * kCK));
-        if (__syncthreads_or(!ok)) {
-          // give up: let a copy still in flight land before the CTA exits
-          if (tid == 0 && more) mbar_wait(&s_bar[buf ^ 1], (uint32_t)(phase[buf ^ 1] & 1));
-          fail = 1;
-          break;
-        }
-      } else {
-        if (more) {
-          stage_du<DT>(s_dl + (buf ^ 1) * kCK * DT * 4, s_u + (buf ^ 1) * kCK * DT * 4, p, b, d0,
-                       (c + 1) * kCK, dir, esz);
-          if (accumulate) stage_y<DT>(s_y + (buf ^ 1) * kCK * DT, p, b, d0, (c + 1) * kCK, dir);
-        }
-        cp_async_commit();
-        if (more) load_bc((c + 1) * kCK);
-        cp_async_wait1();
-        __syncthreads();
-      }
-
-      const unsigned char* bdl = s_dl + buf * kCK * DT * 4;
-      const unsigned char* bu = s_u + buf * kCK * DT * 4;
-      const float2* bb = s_b + buf * kCK * NP;
-      const float2* bc = s_c + buf * kCK * NP;
-      const float* by = s_y + buf * kCK * DT;
-      const int ns = min(kCK, L - c * kCK);
-      // checkpoint of P = 2h + dBu before processing step s (the start of a
-      // backward chunk: every p.cki steps)
-      auto write_ckpt = [&](int s) {
-#pragma unroll
-        for (int k = 0; k < ND; ++k) {
-          const int d = dbase + k;
-          if (d < D) {
-            float* dst = p.ckpt +
-                ((((size_t)b * ndirs + dslot) * p.nck + (s / p.cki - 1)) * D + d) * NP + q * NL;
-            if constexpr (NL % 4 == 0) {   // 16-byte aligned: NP*4 and NL*4 are multiples of 16
-#pragma unroll
-              for (int j = 0; j < NL; j += 4)
-                *reinterpret_cast<float4*>(dst + j) =
-                    (k & 1) ? make_float4(P[k >> 1][j].y, P[k >> 1][j + 1].y,
-                                          P[k >> 1][j + 2].y, P[k >> 1][j + 3].y)
-                            : make_float4(P[k >> 1][j].x, P[k >> 1][j + 1].x,
-                                          P[k >> 1][j + 2].x, P[k >> 1][j + 3].x);
-            } else {
-#pragma unroll
-              for (int j = 0; j < NL; ++j) dst[j] = (k & 1) ? P[k >> 1][j].y : P[k >> 1][j].x;
-            }
-          }
-        }
-      };
-      // One processing step.  FASTC: the caller proved |delta*A_imag| <=
-      // kFastArgBound for the whole chunk and that it holds no state output,
-      // so the packed path runs without a per-step check.
-      auto step = [&](int tt, auto fast_tag) {
-        constexpr bool FASTC = decltype(fast_tag)::value;
-        const int s = c * kCK + tt;
-        const int t = dir ? L - 1 - s : s;
-        float dl[ND], uu[ND];
-        read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * esz, bf16, dl);
-        read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * esz, bf16, uu);
-        float2 Bv[NL], Cv[NL];   // B, C of the thread's lanes as (b, b) pairs
-#pragma unroll
-        for (int j = 0; j < NL; ++j) {
-          Bv[j] = bb[tt * NP + q * NL + j];
-          Cv[j] = bc[tt * NP + q * NL + j];
-        }
-        const bool last = STATE && !FASTC && (s == L - 1) && (p.h_last != nullptr);
-        float du[ND], mdl = 0.f;
-#pragma unroll
-        for (int k = 0; k < ND; ++k) {
-          du[k] = __fmul_rn(dl[k], uu[k]);
-          if constexpr (!FASTC) mdl = fmaxf(mdl, fabsf(dl[k]));
-        }
-        float part[2 * NDP];
-        if (FASTC || ((ND % 2 == 0) && !last && __fmul_rn(mdl, maxai) <= kFastArgBound)) {
-          // packed path: channel pairs, no per-cell range checks
-#pragma unroll
-          for (int kp = 0; kp < NDP; ++kp) {
-            const float2 dl2 = make_float2(dl[2 * kp], dl[(2 * kp + 1) % ND]);
-            const float2 du2 = make_float2(du[2 * kp], du[(2 * kp + 1) % ND]);
-            float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-            for (int j = 0; j < R; ++j) {
-              const float2 g = __fmul2_rn(gate_exp2(dl2, A2[kp][j]), gate_cos2_nocheck(dl2, AI[kp][j]));
-              const float2 H = cell_update2p(g, P[kp][j], du2, Bv[j]);
-              acc = __ffma2_rn(H, Cv[j], acc);
-            }
-#pragma unroll
-            for (int j = R; j < NL; ++j) {
-              const float2 H = cell_update2p(TK[kp][j - R], P[kp][j], du2, Bv[j]);
-              acc = __ffma2_rn(H, Cv[j], acc);
-            }
-            part[2 * kp] = acc.x;
-            part[2 * kp + 1] = acc.y;
-          }
-        } else {
-          // scalar path: per-cell range checks (large arguments, the last step)
-          float Cs[NL];
-#pragma unroll
-          for (int j = 0; j < NL; ++j) Cs[j] = Cv[j].x;
-#pragma unroll
-          for (int k = 0; k < ND; ++k) {
-            float H[NL];
-#pragma unroll
-            for (int j = 0; j < NL; ++j) {
-              float& Pk = (k & 1) ? P[k >> 1][j].y : P[k >> 1][j].x;
-              float g;
-              if (j < R) {
-                g = rot_gate(dl[k], (k & 1) ? A2[k >> 1][j].y : A2[k >> 1][j].x,
-                             (k & 1) ? AI[k >> 1][j].y : AI[k >> 1][j].x);
-              } else {
-                g = (k & 1) ? TK[k >> 1][j - R].y : TK[k >> 1][j - R].x;
-              }
-              H[j] = cell_update(g, Pk, du[k], Bv[j].x);
-            }
-            part[k] = y_partial<NL>(H, Cs);
-            if (last) {
-              const int d = dbase + k;
-              if (d < D) {
-#pragma unroll
-                for (int j = 0; j < NL; ++j) {
-                  const int n = LM::mem_lane(q, j, p.NR, p.NT);
-                  if (n >= 0) {
-                    const size_t gi = ((size_t)b * D + d) * N + n;
-                    p.h_last[gi] = __fmul_rn(0.5f, H[j]);
-                    p.dbu_last[gi] = __fmul_rn(du[k], Bv[j].x);
-                  }
-                }
-              }
-            }
-          }
-        }
-        float* yrow = p.y + ((size_t)b * L + t) * D;
-#pragma unroll
-        for (int k = 0; k < ND; ++k) {
-          const float tot = __fmul_rn(0.5f, quad_sum(part[k]));
-          const int d = dbase + k;
-          if ((k & 3) == q && d < D) {
-            yrow[d] = accumulate ? __fadd_rn(tot, by[tt * DT + grp * ND + k]) : tot;
-          }
-        }
-      };
-      // the range decision once per chunk: max |delta| of the thread's channels
-      bool chunk_fast = false;
-      if constexpr (ND % 2 == 0) {
-        float mdl = 0.f;
-        for (int tt = 0; tt < ns; ++tt) {
-          float dl[ND];
-          read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * esz, bf16, dl);
-#pragma unroll
-          for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
-        }
-        chunk_fast = __fmul_rn(mdl, maxai) <= kFastArgBound;
-      }
-      // the step that writes the final state (return_state) takes the checked path
-      const bool has_last = STATE && p.h_last != nullptr && c * kCK + ns == L;
-      const int nfast = has_last ? ns - 1 : ns;
-      // segments between checkpoint positions (p.cki divides kCK)
-      const int seg_len = p.cki < kCK ? p.cki : kCK;
-      for (int seg = 0; seg < ns; seg += seg_len) {
-        const int send = min(ns, seg + seg_len);
-        const int s = c * kCK + seg;
-        if (p.ckpt != nullptr && s > 0 && (s & (p.cki - 1)) == 0) write_ckpt(s);
-        if (chunk_fast) {
-          const int fend = min(send, nfast);
-#pragma unroll kFwdUnroll
-          for (int tt = seg; tt < fend; ++tt) step(tt, std::true_type{});
-          for (int tt = fend; tt < send; ++tt) step(tt, std::false_type{});
-        } else {
-          for (int tt = seg; tt < send; ++tt) step(tt, std::false_type{});
-        }
-      }
-      if constexpr (!BULK) {
-        if (more) store_bc(buf ^ 1);
-      }
-      __syncthreads();
-    }
-  }
-  cp_async_wait0();
-  if (fail) set_err(p.err, M3_ERR_DEVICE);
-}
-
-template <int R, int T, int ND, bool BULK, bool STATE>
-cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
-  constexpr int NP = 4 * (R + T);
-  constexpr int DT = 32 * ND;
-  const size_t smem = FwdSmem<NP, DT, BULK>::bytes(p.direction == M3_DIR_BIDIR);
-  auto kern = scan_fwd_kernel<R, T, ND, BULK, STATE>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid(p.B, (p.D + DT - 1) / DT);
-  kern<<<grid, kThreads, smem, stream>>>(p);
-  return cudaGetLastError();
-}
-
-}  // namespace
+// defined in m3_scan_fwd_bulk_<dtype>_<state>.cu: launch the bulk-staged kernel of tile t
+cudaError_t launch_fwd_bulk_bf16_state(const Tile& t, const FwdParams& p, cudaStream_t s);
+cudaError_t launch_fwd_bulk_bf16_nostate(const Tile& t, const FwdParams& p, cudaStream_t s);
+cudaError_t launch_fwd_bulk_f32_state(const Tile& t, const FwdParams& p, cudaStream_t s);
+cudaError_t launch_fwd_bulk_f32_nostate(const Tile& t, const FwdParams& p, cudaStream_t s);
 
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
-#define M3_X(r, tt, nd, ndb, nthb, gs) \
-  if (t.R == r && t.T == tt && t.ND == nd)                                  \
-    return p.h_last ? (p.bulk ? launch_fwd_impl<r, tt, nd, true, true>(p, s)       \
-                              : launch_fwd_impl<r, tt, nd, false, true>(p, s))     \
-                    : (p.bulk ? launch_fwd_impl<r, tt, nd, true, false>(p, s)      \
-                              : launch_fwd_impl<r, tt, nd, false, false>(p, s));
+  if (p.bulk) {
+    const bool bf = p.dt_du == M3_BF16, st = p.h_last != nullptr;
+    return bf ? (st ? launch_fwd_bulk_bf16_state(t, p, s) : launch_fwd_bulk_bf16_nostate(t, p, s))
+              : (st ? launch_fwd_bulk_f32_state(t, p, s) : launch_fwd_bulk_f32_nostate(t, p, s));
+  }
+#define M3_X(r, tt, nd, ndb, nthb, gs)                                              \
+  if (t.R == r && t.T == tt && t.ND == nd)                                        \
+    return p.h_last ? fwd::launch_fwd_impl<r, tt, nd, false, true, -1>(p, s)        \
+                    : fwd::launch_fwd_impl<r, tt, nd, false, false, -1>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;
