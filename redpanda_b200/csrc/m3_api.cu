@@ -252,10 +252,12 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
                (desc->dtype_du == M3_F32 || (desc->d_inner % 2) == 0);
   p.async_dy = aligned(dy, 4) && (dtype_dy == M3_F32 || (desc->d_inner % 2) == 0);
   // bulk staging: whole channel tiles and 16-byte aligned rows of every input
+  // and of d_delta/d_u (the flush writes 4 channels per vector store)
   p.bulk = (desc->d_inner % t.dt_bwd()) == 0 && ((desc->d_inner * esd) % 16) == 0 &&
            ((desc->d_inner * esy) % 16) == 0 && ((desc->d_state * esb) % 16) == 0 &&
            aligned(delta, 16) && aligned(u, 16) && aligned(dy, 16) && aligned(Bc, 16) &&
-           aligned(Cc, 16) && (!ckpt || aligned(ckpt, 16)) && getenv("M3_NO_BULK") == nullptr;
+           aligned(Cc, 16) && aligned(d_delta, 16) && aligned(d_u, 16) &&
+           (!ckpt || aligned(ckpt, 16)) && getenv("M3_NO_BULK") == nullptr;
   p.err = device_err_ptr();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = launch_scan_bwd(t, p, s);

@@ -1,6 +1,7 @@
 // Bulk asynchronous copies (global -> shared, completion on an mbarrier) with
 // bounded waits.  Used by the pipelined step kernel to stream whole state rows
-// into shared memory several rows ahead of the compute.
+// into shared memory several rows ahead of the compute, by the forward scan for
+// its input rows and by the backward for its checkpoint tiles.
 //
 // Every copy is the plain single-destination form: it reads this GPU's own
 // memory into the issuing CTA's own shared memory (a CTA-local shared address
@@ -33,6 +34,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
                "r"(bytes)
                : "memory");
+}
+
+// Arrives without expecting bytes (completes a phase that has no copy).
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 // Waits for phase `parity` of the barrier to complete; false after

@@ -24,6 +24,7 @@
 // a fixed order, so results are bitwise reproducible run to run.
 #include <type_traits>
 
+#include "m3_bulk.cuh"
 #include "m3_common.cuh"
 #include "m3_internal.h"
 #include "m3_stage.cuh"
@@ -98,7 +99,7 @@ struct BwdCfg {
       + 2 * 2 * (size_t)KC * NP * 4           // B, C (fp32), double-buffered
       + red_floats * 4 + gs_floats * 4
       + braw_floats * 4 + scr_floats * 4
-      + 16;                                   // TMEM address slot
+      + 32;                                   // TMEM address slot, 2 mbarriers (BULK)
 };
 
 // Stage a (KC x DT) tile of a (B, L, D) tensor for processing steps
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   float* s_braw = s_gs + CF::gs_floats;                              // [2][B|C][KC][NP] (BULK)
   float* s_scr = s_braw + CF::braw_floats;                           // [KC][DT][2] (BULK)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_scr + CF::scr_floats);
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(s_tmem) + 1;          // [2] (BULK)
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
   const int warp = tid >> 5;
@@ -177,6 +179,13 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   const int es_du = bf_du ? 2 : 4, es_dy = bf_dy ? 2 : 4;
   const bool async_du = p.async_du, async_dy = p.async_dy;
 
+  if constexpr (BULK) {
+    if (tid == 0) {   // checkpoint-tile completion, one barrier per staging buffer
+      mbar_init(&s_bar[0], 1);
+      mbar_init(&s_bar[1], 1);
+      mbar_fence_init();
+    }
+  }
   if (warp == 0) tmem_alloc(s_tmem, CF::NCOLS);
   tmem_fence_before();
   __syncthreads();
@@ -279,47 +288,44 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
     }
   };
 
-  // BULK staging of work item i into buffer buf with 16-byte cp.async and
-  // shift-only index math (rows of DT channels are powers of two of 16-byte
-  // pieces): delta/u/dy rows, the checkpoint tile, and the chunk's B and C rows
-  // as one contiguous block each (rows in memory order; widen_bc reorders).
+  // BULK staging of work item (b, pass, c) into buffer buf: the checkpoint
+  // tile (one contiguous block) by a single bulk copy completing on the
+  // buffer's mbarrier (every item arrives on it once, with or without a copy);
+  // delta/u/dy rows and the chunk's B and C rows (one contiguous block each,
+  // in memory order; widen_bc reorders) by 16-byte cp.async with shift-only
+  // index math (rows of DT channels are powers of two of 16-byte pieces).
   const int es_bc = p.dt_bc == M3_BF16 ? 2 : 4;
   const int lg_du = 31 - __clz(DT * es_du / 16), lg_dy = 31 - __clz(DT * es_dy / 16);
-  auto stage_vec = [&](int i, int buf) {
-    int b, pass, c;
-    item(i, b, pass, c);
+  auto stage_vec = [&](int b, int pass, int c, int buf) {
     const int dir = dir_of(pass), s0 = c * KC;
     const int ns = min(KC, L - s0);
-    for (int v = tid; v < (3 * ns) << lg_du; v += NTH) {
-      // tensor k (delta, u) uses lg_du; dy rows are handled below when its size differs
-      const int r = v >> lg_du, w = v - (r << lg_du);
-      const int kind = r / ns, tt = r - kind * ns;
-      if (kind == 2 && lg_dy != lg_du) break;
-      const int s = s0 + tt;
-      const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
-      const int es = kind == 2 ? es_dy : es_du;
-      const void* src = kind == 0 ? p.delta : (kind == 1 ? p.u : p.dy);
-      unsigned char* dst = (kind == 0 ? s_dl : (kind == 1 ? s_u : s_dy)) + buf * CF::raw_bytes;
-      cp_async16(dst + (size_t)tt * DT * es + w * 16,
-                 (const char*)src + (row * D + d0) * es + w * 16, true);
-    }
-    if (lg_dy != lg_du) {
-      for (int v = tid; v < ns << lg_dy; v += NTH) {
-        const int tt = v >> lg_dy, w = v - (tt << lg_dy);
-        const int s = s0 + tt;
-        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
-        cp_async16(s_dy + buf * CF::raw_bytes + (size_t)tt * DT * es_dy + w * 16,
-                   (const char*)p.dy + (row * D + d0) * es_dy + w * 16, true);
+    // memory row of processing step tt: row0 + tt (forward) or row0 - tt (reversed)
+    const long long row0 = (long long)b * L + (dir ? L - 1 - s0 : s0);
+    const int rstep = dir ? -1 : 1;
+    auto rows = [&](const void* src, unsigned char* dst, int es, int lg) {
+      for (int v = tid; v < (ns << lg); v += NTH) {
+        const int tt = v >> lg, w = v & ((1 << lg) - 1);
+        const long long row = row0 + rstep * tt;
+        cp_async16(dst + (size_t)tt * DT * es + w * 16,
+                   (const char*)src + (row * D + d0) * es + w * 16, true);
+      }
+    };
+    rows(p.delta, s_dl + buf * CF::raw_bytes, es_du, lg_du);
+    rows(p.u, s_u + buf * CF::raw_bytes, es_du, lg_du);
+    rows(p.dy, s_dy + buf * CF::raw_bytes, es_dy, lg_dy);
+    if (tid == 0) {
+      if (c > 0) {
+        const int dslot = bidir ? dir : 0;
+        const float* src =
+            p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
+        mbar_arrive_expect_tx(&s_bar[buf], DT * NP * 4);
+        bulk_g2s(s_ck + buf * DT * NP, src, DT * NP * 4, &s_bar[buf]);
+      } else {
+        mbar_arrive(&s_bar[buf]);
       }
     }
-    if (c > 0) {
-      const int dslot = bidir ? dir : 0;
-      const float* src = p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
-      float* dst = s_ck + buf * DT * NP;
-      for (int v = tid; v < DT * NP / 4; v += NTH) cp_async16(dst + v * 4, src + v * 4, true);
-    }
     const int t_lo = dir ? L - s0 - ns : s0;             // first memory row of the chunk
-    const int pieces = ns * N * es_bc / 16;
+    const int pieces = (ns * N * es_bc) >> 4;
     for (int v = tid; v < 2 * pieces; v += NTH) {
       const int which = v >= pieces, w = v - which * pieces;
       const char* src = (const char*)(which ? p.Cc : p.Bc) + ((size_t)b * L + t_lo) * N * es_bc;
@@ -328,23 +334,56 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
     }
   };
   // widen the raw B/C rows of buffer buf into the padded fp32 lane layout
-  // (processing step tt is memory row tt, or ns-1-tt for the reversed scan)
+  // (processing step tt is memory row tt, or ns-1-tt for the reversed scan).
+  // When NP divides the block, a thread always fills the same padded lane.
+  constexpr bool kFixedLane = NTH % NP == 0;
+  const int wl = tid % NP;
+  const int wn = LM::mem_lane(wl / NL, wl % NL, p.NR, p.NT);
+  const bool bc16 = p.dt_bc == M3_BF16;
   auto widen_bc = [&](int buf, int ns, int dir) {
-    for (int i = tid; i < ns * NP; i += NTH) {
-      const int tt = i / NP, ln = i - tt * NP;
-      const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
-      const size_t r = (size_t)(dir ? ns - 1 - tt : tt) * N + (n >= 0 ? n : 0);
-      const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * KC) * NP;
-      const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * KC) * NP;
-      s_b[buf * KC * NP + i] = n >= 0 ? ld_f(rb0, r, p.dt_bc) : 0.f;
-      s_c[buf * KC * NP + i] = n >= 0 ? ld_f(rc0, r, p.dt_bc) : 0.f;
+    const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * KC) * NP;
+    const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * KC) * NP;
+    if constexpr (kFixedLane) {
+      for (int tt = tid / NP; tt < ns; tt += NTH / NP) {
+        const int r = (dir ? ns - 1 - tt : tt) * N + (wn >= 0 ? wn : 0);
+        float bv = 0.f, cv = 0.f;
+        if (wn >= 0) {
+          if (bc16) {
+            bv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(rb0)[r]);
+            cv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(rc0)[r]);
+          } else {
+            bv = rb0[r];
+            cv = rc0[r];
+          }
+        }
+        s_b[buf * KC * NP + tt * NP + wl] = bv;
+        s_c[buf * KC * NP + tt * NP + wl] = cv;
+      }
+    } else {
+      for (int i = tid; i < ns * NP; i += NTH) {
+        const int tt = i / NP, ln = i - tt * NP;
+        const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
+        const size_t r = (size_t)(dir ? ns - 1 - tt : tt) * N + (n >= 0 ? n : 0);
+        s_b[buf * KC * NP + i] = n >= 0 ? ld_f(rb0, r, p.dt_bc) : 0.f;
+        s_c[buf * KC * NP + i] = n >= 0 ? ld_f(rc0, r, p.dt_bc) : 0.f;
+      }
     }
   };
 
   float2 qv[NDP][NL], gn[NDP][RR];
+  // the current work item, advanced without divisions: chunks from last to
+  // first, then the next direction, then the next row
+  int b = bg, pass = 0, c = nch - 1;
+  auto advance = [&](int& ib, int& ipass, int& ic) {
+    if (ic > 0) { --ic; return; }
+    ic = nch - 1;
+    if (++ipass < ndirs) return;
+    ipass = 0;
+    ib += p.Bg;
+  };
   if (nitems > 0) {
     if constexpr (BULK) {
-      stage_vec(0, 0);
+      stage_vec(b, pass, c, 0);
       cp_async_commit();
     } else {
       stage(0, 0);
@@ -355,10 +394,9 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
       store_bc(0);
     }
   }
-  for (int it = 0; it < nitems; ++it) {
+  bool fail = false;   // a checkpoint copy did not complete (BULK)
+  for (int it = 0; it < nitems; ++it, advance(b, pass, c)) {
     const int buf = it & 1;
-    int b, pass, c;
-    item(it, b, pass, c);
     const int dir = dir_of(pass);
     const bool first_of_two = bidir && pass == 0;
     const bool second_of_two = bidir && pass == 1;
@@ -378,10 +416,21 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
       }
       cp_async_commit();
       // group 2: the next work item
-      if (more) stage_vec(it + 1, buf ^ 1);
+      if (more) {
+        int b2 = b, pass2 = pass, c2 = c;
+        advance(b2, pass2, c2);
+        stage_vec(b2, pass2, c2, buf ^ 1);
+      }
       cp_async_commit();
       cp_async_wait_n<2>();   // this item's staging (committed one iteration ago)
-      __syncthreads();
+      // item it is use it/2 of its buffer's barrier
+      const bool ok = mbar_wait(&s_bar[buf], (uint32_t)((it >> 1) & 1));
+      if (__syncthreads_or(!ok)) {
+        // give up: let the next item's copy land before the CTA exits
+        if (tid == 0 && more) mbar_wait(&s_bar[buf ^ 1], (uint32_t)(((it + 1) >> 1) & 1));
+        fail = true;
+        break;
+      }
       widen_bc(buf, ns, dir);
       __syncthreads();
     } else {
@@ -677,36 +726,103 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
           }
         }
         // ddelta / du per channel: sum the 4 lane-quarter partials
-        for (int i = tid; i < nsl * DT; i += NTH) {
-          const int sl = i / DT, dd = i - sl * DT;
+        auto flush_du = [&](int sl, int dd) {
           const int d = d0 + dd;
-          if (d < D) {
+          if (d >= D) return;
+          const int tts = tt_hi - sl;
+          const float* g4p = s_gs + ((size_t)(sl * ND + dd % ND) * 2) * SG + (dd / ND) * 4;
+          const float4 g4 = *reinterpret_cast<const float4*>(g4p);
+          const float4 b4 = *reinterpret_cast<const float4*>(g4p + SG);
+          const float gsv = __fadd_rn(__fadd_rn(g4.x, g4.y), __fadd_rn(g4.z, g4.w));
+          const float sBv = __fadd_rn(__fadd_rn(b4.x, b4.y), __fadd_rn(b4.z, b4.w));
+          const float dlv = tile_at(bdl, bf_du, tts * DT + dd);
+          const float uv = tile_at(bu, bf_du, tts * DT + dd);
+          float ddl = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, uv));
+          float ddu = __fmul_rn(sBv, dlv);
+          const int s = s0 + tts;
+          const int t = dir ? L - 1 - s : s;
+          float* sc = scratch ? scratch + ((size_t)t * DT + dd) * 2 : nullptr;
+          if (first_of_two) {
+            *reinterpret_cast<float2*>(sc) = make_float2(ddl, ddu);
+          } else {
+            if (second_of_two) {
+              const float2 sv = *reinterpret_cast<const float2*>(
+                  BULK ? s_scr + ((size_t)tts * DT + dd) * 2 : sc);
+              ddl = __fadd_rn(sv.x, ddl);
+              ddu = __fadd_rn(sv.y, ddu);
+            }
+            const size_t oi = ((size_t)b * L + t) * D + d;
+            if (bf_du) {
+              reinterpret_cast<__nv_bfloat16*>(p.d_delta)[oi] = __float2bfloat16_rn(ddl);
+              reinterpret_cast<__nv_bfloat16*>(p.d_u)[oi] = __float2bfloat16_rn(ddu);
+            } else {
+              reinterpret_cast<float*>(p.d_delta)[oi] = ddl;
+              reinterpret_cast<float*>(p.d_u)[oi] = ddu;
+            }
+          }
+        };
+        if constexpr (BULK && DT % 4 == 0) {
+          // 4 consecutive channels of one step per thread (whole channel
+          // tiles and 16-byte aligned rows: vector loads and stores)
+          for (int i = tid; i < nsl * (DT / 4); i += NTH) {
+            const int sl = i / (DT / 4), dd0 = (i - sl * (DT / 4)) * 4;
             const int tts = tt_hi - sl;
-            const float* g4p = s_gs + ((size_t)(sl * ND + dd % ND) * 2) * SG + (dd / ND) * 4;
-            const float4 g4 = *reinterpret_cast<const float4*>(g4p);
-            const float4 b4 = *reinterpret_cast<const float4*>(g4p + SG);
-            const float gsv = __fadd_rn(__fadd_rn(g4.x, g4.y), __fadd_rn(g4.z, g4.w));
-            const float sBv = __fadd_rn(__fadd_rn(b4.x, b4.y), __fadd_rn(b4.z, b4.w));
-            const float dlv = tile_at(bdl, bf_du, tts * DT + dd);
-            const float uv = tile_at(bu, bf_du, tts * DT + dd);
-            float ddl = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, uv));
-            float ddu = __fmul_rn(sBv, dlv);
+            float dlv[4], uv[4], ddl[4], ddu[4];
+            read_chan<4>(bdl + (size_t)(tts * DT + dd0) * es_du, bf_du, dlv);
+            read_chan<4>(bu + (size_t)(tts * DT + dd0) * es_du, bf_du, uv);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int dd = dd0 + k;
+              const float* g4p = s_gs + ((size_t)(sl * ND + dd % ND) * 2) * SG + (dd / ND) * 4;
+              const float4 g4 = *reinterpret_cast<const float4*>(g4p);
+              const float4 b4 = *reinterpret_cast<const float4*>(g4p + SG);
+              const float gsv = __fadd_rn(__fadd_rn(g4.x, g4.y), __fadd_rn(g4.z, g4.w));
+              const float sBv = __fadd_rn(__fadd_rn(b4.x, b4.y), __fadd_rn(b4.z, b4.w));
+              ddl[k] = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, uv[k]));
+              ddu[k] = __fmul_rn(sBv, dlv[k]);
+            }
             const int s = s0 + tts;
             const int t = dir ? L - 1 - s : s;
-            float* sc = scratch ? scratch + ((size_t)t * DT + dd) * 2 : nullptr;
             if (first_of_two) {
-              sc[0] = ddl;
-              sc[1] = ddu;
+              float4* sc = reinterpret_cast<float4*>(scratch + ((size_t)t * DT + dd0) * 2);
+              sc[0] = make_float4(ddl[0], ddu[0], ddl[1], ddu[1]);
+              sc[1] = make_float4(ddl[2], ddu[2], ddl[3], ddu[3]);
             } else {
               if (second_of_two) {
-                const float* scv = BULK ? s_scr + ((size_t)tts * DT + dd) * 2 : sc;
-                ddl = __fadd_rn(scv[0], ddl);
-                ddu = __fadd_rn(scv[1], ddu);
+                const float4* sv = reinterpret_cast<const float4*>(s_scr + ((size_t)tts * DT + dd0) * 2);
+                const float4 v0 = sv[0], v1 = sv[1];
+                ddl[0] = __fadd_rn(v0.x, ddl[0]); ddu[0] = __fadd_rn(v0.y, ddu[0]);
+                ddl[1] = __fadd_rn(v0.z, ddl[1]); ddu[1] = __fadd_rn(v0.w, ddu[1]);
+                ddl[2] = __fadd_rn(v1.x, ddl[2]); ddu[2] = __fadd_rn(v1.y, ddu[2]);
+                ddl[3] = __fadd_rn(v1.z, ddl[3]); ddu[3] = __fadd_rn(v1.w, ddu[3]);
               }
-              const size_t oi = ((size_t)b * L + t) * D + d;
-              st_f(p.d_delta, oi, p.dt_du, ddl);
-              st_f(p.d_u, oi, p.dt_du, ddu);
+              const size_t oi = ((size_t)b * L + t) * D + d0 + dd0;
+              if (bf_du) {
+                auto pack = [](float x, float y) {
+                  const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+                  return *reinterpret_cast<const uint32_t*>(&h);
+                };
+                *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.d_delta) + oi) =
+                    make_uint2(pack(ddl[0], ddl[1]), pack(ddl[2], ddl[3]));
+                *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.d_u) + oi) =
+                    make_uint2(pack(ddu[0], ddu[1]), pack(ddu[2], ddu[3]));
+              } else {
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.d_delta) + oi) =
+                    make_float4(ddl[0], ddl[1], ddl[2], ddl[3]);
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.d_u) + oi) =
+                    make_float4(ddu[0], ddu[1], ddu[2], ddu[3]);
+              }
             }
+          }
+        } else if constexpr (NTH % DT == 0) {
+          // a thread keeps one channel; its steps are independent, so unroll
+          const int dd = tid % DT;
+#pragma unroll 4
+          for (int sl = tid / DT; sl < nsl; sl += NTH / DT) flush_du(sl, dd);
+        } else {
+          for (int i = tid; i < nsl * DT; i += NTH) {
+            const int sl = i / DT;
+            flush_du(sl, i - sl * DT);
           }
         }
         __syncthreads();
@@ -717,6 +833,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
     }
   }
   cp_async_wait0();
+  if (fail && tid == 0) set_err(p.err, M3_ERR_DEVICE);
 
   // dA partial of this batch group
 #pragma unroll

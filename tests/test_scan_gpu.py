@@ -189,3 +189,37 @@ def test_verify_gate_passes():
     """The drop-in module's gate (triton_scan.verify's counterpart), thorough
     configuration list: forward and all gradients vs the float64 recurrence."""
     assert S.verify(device="cuda", thorough=True, verbose=False) is True
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+def test_backward_grad_outputs_off_16_byte_boundary(dtype):
+    """d_delta/d_u that start off a 16-byte boundary (views into a larger
+    buffer) are written by the element-wise flush; the results equal those of
+    aligned outputs, which take the vector-store flush, bit for bit."""
+    from redpanda_b200.scan import ScanPlan, pad_params
+    B, L, D, N, NR = 2, 64, 256, 32, 16
+    sh = ScanShape(B, L, D, N, N - NR, 4)
+    inp = to_cuda(make_scan_inputs(sh, seed=23, dtype=dtype))
+    dev = inp["u"].device
+    Ar, Ai, Tk = (t.contiguous() for t in pad_params(inp["A_real"], inp["A_imag"],
+                                                     inp["track"], NR, N, D, dev))
+    plan = ScanPlan(B, L, D, N, NR, dtype, dtype, S.M3_DIR_BIDIR)
+    y = torch.empty(B, L, D, device=dev)
+    ckpt = torch.empty(plan.ckpt_floats(), device=dev)
+    args = (inp["delta"], inp["u"], inp["Bc"], inp["Cc"], Ar, Ai, Tk)
+    plan.forward(*args, y, ckpt)
+    dy = torch.randn(B, L, D, device=dev).to(dtype)
+    outs = []
+    for shift in (0, 1):   # elements: 2 or 4 bytes off the allocation's alignment
+        flat = torch.empty(2, B * L * D + 8, device=dev, dtype=dtype)
+        gd = flat[0, shift:shift + B * L * D].view(B, L, D)
+        gu = flat[1, shift:shift + B * L * D].view(B, L, D)
+        gB, gC = torch.empty_like(inp["Bc"]), torch.empty_like(inp["Cc"])
+        gA = torch.empty(3, D, N, device=dev)
+        ws = torch.empty(plan.workspace_bytes(), device=dev, dtype=torch.uint8)
+        plan.backward(*args, dy, ckpt, gd, gu, gB, gC, gA[0], gA[1], gA[2], ws)
+        outs.append((gd.clone(), gu.clone(), gB, gC, gA))
+    torch.cuda.synchronize()
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
+    assert S.device_error() == 0
