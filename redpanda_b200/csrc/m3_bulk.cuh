@@ -58,6 +58,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// Orders this thread's earlier generic-proxy view of global memory (including
+// writes by other threads made visible to it by a barrier) before its later
+// bulk copies, which read through the async proxy.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // bytes (a multiple of 16) from global src (16-byte aligned) to shared dst
 // (16-byte aligned); completion is counted on bar's transaction count.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,

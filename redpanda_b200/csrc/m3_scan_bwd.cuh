@@ -22,6 +22,8 @@
 // dB/dC are reduced over the CTA's channels (warp shuffles + shared memory)
 // into one partial per channel tile.  A second kernel sums both partial sets in
 // a fixed order, so results are bitwise reproducible run to run.
+#include <string.h>
+
 #include <type_traits>
 
 #include "m3_bulk.cuh"
@@ -29,6 +31,7 @@
 #include "m3_internal.h"
 #include "m3_stage.cuh"
 #include "m3_tiles.h"
+#include "m3_tma.h"
 #include "m3_tmem.cuh"
 
 #ifndef M3_BWD_UNROLL_RECOMPUTE
@@ -88,9 +91,10 @@ struct BwdCfg {
       WR ? (size_t)FL * 2 * NL * NW * 4                           // [FL][2*NL][NW][4]
          : (size_t)FL * 2 * NL * SR;                              // [FL][2][NL][SR]
   static constexpr size_t gs_floats = (size_t)FL * ND * 2 * SG;    // [FL][ND][2][SG]
-  // BULK (16-byte staging): B/C rows land raw (HBM dtype, memory order) and
-  // are widened into the padded fp32 tiles after the copy; the bidirectional
-  // second pass stages the first pass's ddelta/du rows of the chunk.
+  // BULK (copy-engine staging): the delta/u/dy tiles land in memory row order
+  // (TMA boxes of KC rows), B/C rows land raw (HBM dtype, memory order) and are
+  // widened into the padded fp32 tiles after the copy; the bidirectional second
+  // pass stages the first pass's ddelta/du rows of the chunk.
   static constexpr size_t braw_floats = BULK ? 2 * 2 * (size_t)KC * NP : 0;  // [2][B|C][KC][NP]
   static constexpr size_t scr_floats = BULK ? (size_t)KC * DT * 2 : 0;       // [KC][DT][2]
   static constexpr size_t smem_bytes =
@@ -99,7 +103,7 @@ struct BwdCfg {
       + 2 * 2 * (size_t)KC * NP * 4           // B, C (fp32), double-buffered
       + red_floats * 4 + gs_floats * 4
       + braw_floats * 4 + scr_floats * 4
-      + 32;                                   // TMEM address slot, 2 mbarriers (BULK)
+      + 32;                                   // TMEM address slot, 3 mbarriers (BULK)
 };
 
 // Stage a (KC x DT) tile of a (B, L, D) tensor for processing steps
@@ -141,7 +145,9 @@ __device__ __forceinline__ float tile_at(const unsigned char* base, bool bf16, i
 // 1 bf16), or -1 to read them from the parameters (element-wise staging path).
 template <int R, int T, int ND, int NTH, bool GS, bool BULK, int DU, int DY>
 __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
-    scan_bwd_kernel(const BwdParams p) {
+    scan_bwd_kernel(const BwdParams p, const __grid_constant__ CUtensorMap tm_dl,
+                    const __grid_constant__ CUtensorMap tm_u,
+                    const __grid_constant__ CUtensorMap tm_dy) {
   using LM = LaneMap<R, T>;
   using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
   constexpr int KC = CF::KC;
@@ -152,7 +158,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   constexpr int BCE = (KC * NP + NTH - 1) / NTH;
   static_assert(CF::NCOLS <= 512, "TMEM holds at most 512 columns");
 
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* s_dl = smem;                                        // [2][raw]
   unsigned char* s_u = s_dl + 2 * CF::raw_bytes;                     // [2][raw]
   unsigned char* s_dy = s_u + 2 * CF::raw_bytes;                     // [2][raw]
@@ -164,7 +170,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   float* s_braw = s_gs + CF::gs_floats;                              // [2][B|C][KC][NP] (BULK)
   float* s_scr = s_braw + CF::braw_floats;                           // [KC][DT][2] (BULK)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_scr + CF::scr_floats);
-  uint64_t* s_bar = reinterpret_cast<uint64_t*>(s_tmem) + 1;          // [2] (BULK)
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(s_tmem) + 1;          // [3] (BULK)
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
   const int warp = tid >> 5;
@@ -180,9 +186,16 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   const bool async_du = p.async_du, async_dy = p.async_dy;
 
   if constexpr (BULK) {
-    if (tid == 0) {   // checkpoint-tile completion, one barrier per staging buffer
+    // TMA boxes land at 128-byte aligned shared addresses (the raw tiles are
+    // multiples of 128 bytes, so the base decides); uniform over the CTA
+    if (smem_addr(smem) & 127u) {
+      if (tid == 0) set_err(p.err, M3_ERR_DEVICE);
+      return;
+    }
+    if (tid == 0) {   // one barrier per staging buffer, one for the scratch rows
       mbar_init(&s_bar[0], 1);
       mbar_init(&s_bar[1], 1);
+      mbar_init(&s_bar[2], 1);
       mbar_fence_init();
     }
   }
@@ -288,50 +301,37 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
     }
   };
 
-  // BULK staging of work item (b, pass, c) into buffer buf: the checkpoint
-  // tile (one contiguous block) by a single bulk copy completing on the
-  // buffer's mbarrier (every item arrives on it once, with or without a copy);
-  // delta/u/dy rows and the chunk's B and C rows (one contiguous block each,
-  // in memory order; widen_bc reorders) by 16-byte cp.async with shift-only
-  // index math (rows of DT channels are powers of two of 16-byte pieces).
+  // BULK staging of work item (b, pass, c) into buffer buf, all by thread 0
+  // on the copy engine, completing on the buffer's mbarrier: the delta/u/dy
+  // tiles as TMA boxes of KC memory rows x DT channels starting at the chunk's
+  // first memory row (rows past the chunk are never read; rows past the tensor
+  // are zero-filled), the checkpoint tile and the chunk's B and C rows as one
+  // contiguous block each (memory order).
   const int es_bc = p.dt_bc == M3_BF16 ? 2 : 4;
-  const int lg_du = 31 - __clz(DT * es_du / 16), lg_dy = 31 - __clz(DT * es_dy / 16);
   auto stage_vec = [&](int b, int pass, int c, int buf) {
+    if (tid != 0) return;
     const int dir = dir_of(pass), s0 = c * KC;
     const int ns = min(KC, L - s0);
-    // memory row of processing step tt: row0 + tt (forward) or row0 - tt (reversed)
-    const long long row0 = (long long)b * L + (dir ? L - 1 - s0 : s0);
-    const int rstep = dir ? -1 : 1;
-    auto rows = [&](const void* src, unsigned char* dst, int es, int lg) {
-      for (int v = tid; v < (ns << lg); v += NTH) {
-        const int tt = v >> lg, w = v & ((1 << lg) - 1);
-        const long long row = row0 + rstep * tt;
-        cp_async16(dst + (size_t)tt * DT * es + w * 16,
-                   (const char*)src + (row * D + d0) * es + w * 16, true);
-      }
-    };
-    rows(p.delta, s_dl + buf * CF::raw_bytes, es_du, lg_du);
-    rows(p.u, s_u + buf * CF::raw_bytes, es_du, lg_du);
-    rows(p.dy, s_dy + buf * CF::raw_bytes, es_dy, lg_dy);
-    if (tid == 0) {
-      if (c > 0) {
-        const int dslot = bidir ? dir : 0;
-        const float* src =
-            p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
-        mbar_arrive_expect_tx(&s_bar[buf], DT * NP * 4);
-        bulk_g2s(s_ck + buf * DT * NP, src, DT * NP * 4, &s_bar[buf]);
-      } else {
-        mbar_arrive(&s_bar[buf]);
-      }
-    }
     const int t_lo = dir ? L - s0 - ns : s0;             // first memory row of the chunk
-    const int pieces = (ns * N * es_bc) >> 4;
-    for (int v = tid; v < 2 * pieces; v += NTH) {
-      const int which = v >= pieces, w = v - which * pieces;
-      const char* src = (const char*)(which ? p.Cc : p.Bc) + ((size_t)b * L + t_lo) * N * es_bc;
-      float* dst = s_braw + ((size_t)(buf * 2 + which) * KC) * NP;
-      cp_async16(reinterpret_cast<char*>(dst) + w * 16, src + w * 16, true);
+    const uint32_t bc_bytes = (uint32_t)(ns * N * es_bc);
+    const uint32_t bytes = (uint32_t)(KC * DT * (2 * es_du + es_dy)) + 2 * bc_bytes +
+                           (c > 0 ? (uint32_t)(DT * NP * 4) : 0u);
+    mbar_arrive_expect_tx(&s_bar[buf], bytes);
+    const int y0 = b * L + t_lo;
+    tma_load_2d(s_dl + buf * CF::raw_bytes, &tm_dl, d0, y0, &s_bar[buf]);
+    tma_load_2d(s_u + buf * CF::raw_bytes, &tm_u, d0, y0, &s_bar[buf]);
+    tma_load_2d(s_dy + buf * CF::raw_bytes, &tm_dy, d0, y0, &s_bar[buf]);
+    if (c > 0) {
+      const int dslot = bidir ? dir : 0;
+      const float* src =
+          p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
+      bulk_g2s(s_ck + buf * DT * NP, src, DT * NP * 4, &s_bar[buf]);
     }
+    const size_t bc_off = ((size_t)b * L + t_lo) * N * es_bc;
+    bulk_g2s(s_braw + ((size_t)(buf * 2 + 0) * KC) * NP, (const char*)p.Bc + bc_off, bc_bytes,
+             &s_bar[buf]);
+    bulk_g2s(s_braw + ((size_t)(buf * 2 + 1) * KC) * NP, (const char*)p.Cc + bc_off, bc_bytes,
+             &s_bar[buf]);
   };
   // widen the raw B/C rows of buffer buf into the padded fp32 lane layout
   // (processing step tt is memory row tt, or ns-1-tt for the reversed scan).
@@ -384,7 +384,6 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   if (nitems > 0) {
     if constexpr (BULK) {
       stage_vec(b, pass, c, 0);
-      cp_async_commit();
     } else {
       stage(0, 0);
       cp_async_commit();
@@ -394,7 +393,8 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
       store_bc(0);
     }
   }
-  bool fail = false;   // a checkpoint copy did not complete (BULK)
+  bool fail = false;   // a staging copy did not complete (BULK)
+  int nscr = 0;        // scratch-row copies issued (BULK barrier 2 phases)
   for (int it = 0; it < nitems; ++it, advance(b, pass, c)) {
     const int buf = it & 1;
     const int dir = dir_of(pass);
@@ -403,31 +403,37 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
     const int s0 = c * KC;
     const int ns = min(KC, L - s0);
     const bool more = it + 1 < nitems;
+    // staged rows are in processing order (cp.async staging) or in memory
+    // order (BULK: processing step tt is memory row ns-1-tt when reversed)
+    const int mrow0 = (BULK && dir) ? ns - 1 : 0, mstep = (BULK && dir) ? -1 : 1;
+    [[maybe_unused]] const uint32_t scr_par = (uint32_t)(nscr & 1);
     if constexpr (BULK) {
-      // group 1: the first pass's ddelta/du rows of this chunk (written by this
-      // CTA before the previous barrier), needed from the first flush on
+      // the first pass's ddelta/du rows of this chunk, written by this CTA
+      // before the previous barrier (generic stores, hence the proxy fence),
+      // needed from the first flush on
       if (second_of_two) {
-        for (int v = tid; v < ns * (DT / 2); v += NTH) {
-          const int tt = v / (DT / 2), w = v - tt * (DT / 2);
-          const int s = s0 + tt;
-          const int t = dir ? L - 1 - s : s;
-          cp_async16(s_scr + (size_t)tt * DT * 2 + w * 4, scratch + (size_t)t * DT * 2 + w * 4, true);
+        if (tid == 0) {
+          const int t_lo = dir ? L - s0 - ns : s0;
+          fence_proxy_async_global();
+          mbar_arrive_expect_tx(&s_bar[2], (uint32_t)(ns * DT * 8));
+          bulk_g2s(s_scr, scratch + (size_t)t_lo * DT * 2, (uint32_t)(ns * DT * 8), &s_bar[2]);
         }
+        ++nscr;
       }
-      cp_async_commit();
-      // group 2: the next work item
-      if (more) {
+      if (more) {   // the next work item
         int b2 = b, pass2 = pass, c2 = c;
         advance(b2, pass2, c2);
         stage_vec(b2, pass2, c2, buf ^ 1);
       }
-      cp_async_commit();
-      cp_async_wait_n<2>();   // this item's staging (committed one iteration ago)
       // item it is use it/2 of its buffer's barrier
       const bool ok = mbar_wait(&s_bar[buf], (uint32_t)((it >> 1) & 1));
       if (__syncthreads_or(!ok)) {
-        // give up: let the next item's copy land before the CTA exits
-        if (tid == 0 && more) mbar_wait(&s_bar[buf ^ 1], (uint32_t)(((it + 1) >> 1) & 1));
+        // give up: let the copies still in flight land before the CTA exits
+        if (tid == 0) {
+          mbar_wait(&s_bar[buf], (uint32_t)((it >> 1) & 1));
+          if (more) mbar_wait(&s_bar[buf ^ 1], (uint32_t)(((it + 1) >> 1) & 1));
+          if (second_of_two) mbar_wait(&s_bar[2], scr_par);
+        }
         fail = true;
         break;
       }
@@ -477,8 +483,9 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
     for (int tt = 0; tt < ns; ++tt) {
       tmem_store<C>(tbase + (uint32_t)(tt * CS), reinterpret_cast<const float(&)[C]>(P));
       float dl[ND], uu[ND];
-      read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
-      read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
+      const int mr = mrow0 + mstep * tt;
+      read_chan<ND>(bdl + (size_t)(mr * DT + grp * ND) * es_du, bf_du, dl);
+      read_chan<ND>(bu + (size_t)(mr * DT + grp * ND) * es_du, bf_du, uu);
       const float* rbv = bb + tt * NP + q * NL;
       float mdl = 0.f;
 #pragma unroll
@@ -537,9 +544,10 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
       if constexpr (GS)
         tmem_load<CG>(tbase + (uint32_t)(tt * CS + C), reinterpret_cast<float(&)[CG]>(GG));
       float dl[ND], uu[ND], dyv[ND];
-      read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * es_du, bf_du, dl);
-      read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * es_du, bf_du, uu);
-      read_chan<ND>(bdy + (size_t)(tt * DT + grp * ND) * es_dy, bf_dy, dyv);
+      const int mr = mrow0 + mstep * tt;
+      read_chan<ND>(bdl + (size_t)(mr * DT + grp * ND) * es_du, bf_du, dl);
+      read_chan<ND>(bu + (size_t)(mr * DT + grp * ND) * es_du, bf_du, uu);
+      read_chan<ND>(bdy + (size_t)(mr * DT + grp * ND) * es_dy, bf_dy, dyv);
       const float* rbv = bb + tt * NP + q * NL;
       const float* rcv = bc + tt * NP + q * NL;
       float Bv[NL], Cv[NL];
@@ -660,10 +668,20 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
         }
       }
       if (slot == FL - 1 || tt == 0) {
+        bool okf = true;
         if constexpr (BULK) {
-          if (second_of_two) cp_async_wait_n<1>();   // the scratch group, not the prefetch
+          if (second_of_two) okf = mbar_wait(&s_bar[2], scr_par);
         }
-        __syncthreads();
+        if (__syncthreads_or(!okf)) {
+          // give up (leaves the step loop, then the item loop): let the copies
+          // still in flight land before the CTA exits
+          if (tid == 0) {
+            mbar_wait(&s_bar[2], scr_par);
+            if (more) mbar_wait(&s_bar[buf ^ 1], (uint32_t)(((it + 1) >> 1) & 1));
+          }
+          fail = true;
+          break;
+        }
         const int nsl = slot + 1;                 // slots in this flush
         const int tt_hi = tt + slot;              // step of slot 0
         if constexpr (CF::WR) {
@@ -735,8 +753,9 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
           const float4 b4 = *reinterpret_cast<const float4*>(g4p + SG);
           const float gsv = __fadd_rn(__fadd_rn(g4.x, g4.y), __fadd_rn(g4.z, g4.w));
           const float sBv = __fadd_rn(__fadd_rn(b4.x, b4.y), __fadd_rn(b4.z, b4.w));
-          const float dlv = tile_at(bdl, bf_du, tts * DT + dd);
-          const float uv = tile_at(bu, bf_du, tts * DT + dd);
+          const int mr = mrow0 + mstep * tts;
+          const float dlv = tile_at(bdl, bf_du, mr * DT + dd);
+          const float uv = tile_at(bu, bf_du, mr * DT + dd);
           float ddl = __fmaf_rn(0.5f, gsv, __fmul_rn(sBv, uv));
           float ddu = __fmul_rn(sBv, dlv);
           const int s = s0 + tts;
@@ -747,7 +766,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
           } else {
             if (second_of_two) {
               const float2 sv = *reinterpret_cast<const float2*>(
-                  BULK ? s_scr + ((size_t)tts * DT + dd) * 2 : sc);
+                  BULK ? s_scr + ((size_t)mr * DT + dd) * 2 : sc);
               ddl = __fadd_rn(sv.x, ddl);
               ddu = __fadd_rn(sv.y, ddu);
             }
@@ -768,8 +787,9 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
             const int sl = i / (DT / 4), dd0 = (i - sl * (DT / 4)) * 4;
             const int tts = tt_hi - sl;
             float dlv[4], uv[4], ddl[4], ddu[4];
-            read_chan<4>(bdl + (size_t)(tts * DT + dd0) * es_du, bf_du, dlv);
-            read_chan<4>(bu + (size_t)(tts * DT + dd0) * es_du, bf_du, uv);
+            const int mr = mrow0 + mstep * tts;
+            read_chan<4>(bdl + (size_t)(mr * DT + dd0) * es_du, bf_du, dlv);
+            read_chan<4>(bu + (size_t)(mr * DT + dd0) * es_du, bf_du, uv);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int dd = dd0 + k;
@@ -789,7 +809,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
               sc[1] = make_float4(ddl[2], ddu[2], ddl[3], ddu[3]);
             } else {
               if (second_of_two) {
-                const float4* sv = reinterpret_cast<const float4*>(s_scr + ((size_t)tts * DT + dd0) * 2);
+                const float4* sv = reinterpret_cast<const float4*>(s_scr + ((size_t)mr * DT + dd0) * 2);
                 const float4 v0 = sv[0], v1 = sv[1];
                 ddl[0] = __fadd_rn(v0.x, ddl[0]); ddu[0] = __fadd_rn(v0.y, ddu[0]);
                 ddl[1] = __fadd_rn(v0.z, ddl[1]); ddu[1] = __fadd_rn(v0.w, ddu[1]);
@@ -828,6 +848,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
         __syncthreads();
       }
     }
+    if (fail) break;
     if constexpr (!BULK) {
       if (more) store_bc(buf ^ 1);
     }
@@ -872,12 +893,25 @@ template <int R, int T, int ND, int NTH, bool GS, bool BULK, int DU, int DY>
 cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
   using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
   static_assert(CF::smem_bytes <= kMaxSmemPerCta, "backward tile exceeds shared memory");
+  // BULK: delta, u, dy as (B*L, D) row-major matrices with a (DT x KC) box;
+  // cudaErrorNotSupported (nothing launched) when the maps cannot be built
+  CUtensorMap maps[3];
+  memset(maps, 0, sizeof(maps));
+  if constexpr (BULK) {
+    static_assert(DU >= 0 && DY >= 0, "bulk staging needs compile-time element types");
+    const size_t rows = (size_t)p.B * p.L;
+    const int edu = DU == 1 ? 2 : 4, edy = DY == 1 ? 2 : 4;
+    if (!encode_rows_map(&maps[0], p.delta, edu, rows, p.D, CF::DT, CF::KC) ||
+        !encode_rows_map(&maps[1], p.u, edu, rows, p.D, CF::DT, CF::KC) ||
+        !encode_rows_map(&maps[2], p.dy, edy, rows, p.D, CF::DT, CF::KC))
+      return cudaErrorNotSupported;
+  }
   auto kern = scan_bwd_kernel<R, T, ND, NTH, GS, BULK, DU, DY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)CF::smem_bytes);
   if (e != cudaSuccess) return e;
   dim3 grid(p.Bg, p.G);
-  kern<<<grid, NTH, CF::smem_bytes, stream>>>(p);
+  kern<<<grid, NTH, CF::smem_bytes, stream>>>(p, maps[0], maps[1], maps[2]);
   return cudaGetLastError();
 }
 

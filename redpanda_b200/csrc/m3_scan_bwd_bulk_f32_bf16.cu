@@ -12,8 +12,9 @@ cudaError_t launch_bwd_bulk_f32_bf16(const Tile& t, const BwdParams& p, cudaStre
                 bwd::BwdCfg<r, tt, (ndb > 0 ? ndb : 2), nthb, (gs != 0), true>::smem_bytes <= \
                     bwd::kMaxSmemPerCta)                                                \
     if (t.R == r && t.T == tt && t.ND == nd) {                                          \
-      *handled = true;                                                                  \
-      return bwd::launch_bwd_impl<r, tt, ndb, nthb, (gs != 0), true, 0, 1>(p, s);    \
+      const cudaError_t e = bwd::launch_bwd_impl<r, tt, ndb, nthb, (gs != 0), true, 0, 1>(p, s);  \
+      *handled = e != cudaErrorNotSupported;                                      \
+      return e;                                                                     \
     }
   M3_TILE_LIST(M3_X)
 #undef M3_X

@@ -29,6 +29,7 @@
 #include "m3_common.cuh"
 #include "m3_internal.h"
 #include "m3_bulk.cuh"
+#include "m3_tma.h"
 #include "m3_stage.cuh"
 #include "m3_tiles.h"
 
@@ -607,22 +608,6 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
     for (int i = fail_at; i < min(fail_at + kBulkStages, n); ++i)
       mbar_wait(&full[i % kBulkStages], (uint32_t)((i / kBulkStages) & 1));
   }
-}
-
-// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
-// (no link against the driver library); null if unavailable.
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
-            cudaSuccess || q != cudaDriverEntryPointSuccess) {
-      cudaGetLastError();
-      return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
-    }
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  }();
-  return fn;
 }
 
 // A (rows, 32) fp32 state tensor as a 2D tensor map whose box is one 32-channel
