@@ -899,6 +899,9 @@ cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
   memset(maps, 0, sizeof(maps));
   if constexpr (BULK) {
     static_assert(DU >= 0 && DY >= 0, "bulk staging needs compile-time element types");
+    // TMA staging only for tiles of at most 128 channels (the configurations
+    // validated on the GPU); wider tiles take the element-wise staging
+    if constexpr (CF::DT > 128) return cudaErrorNotSupported;
     const size_t rows = (size_t)p.B * p.L;
     const int edu = DU == 1 ? 2 : 4, edy = DY == 1 ? 2 : 4;
     if (!encode_rows_map(&maps[0], p.delta, edu, rows, p.D, CF::DT, CF::KC) ||

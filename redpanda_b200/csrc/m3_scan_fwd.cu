@@ -16,8 +16,10 @@ cudaError_t launch_fwd_bulk_f32_nostate(const Tile& t, const FwdParams& p, cudaS
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
   if (p.bulk) {
     const bool bf = p.dt_du == M3_BF16, st = p.h_last != nullptr;
-    return bf ? (st ? launch_fwd_bulk_bf16_state(t, p, s) : launch_fwd_bulk_bf16_nostate(t, p, s))
-              : (st ? launch_fwd_bulk_f32_state(t, p, s) : launch_fwd_bulk_f32_nostate(t, p, s));
+    const cudaError_t e =
+        bf ? (st ? launch_fwd_bulk_bf16_state(t, p, s) : launch_fwd_bulk_bf16_nostate(t, p, s))
+           : (st ? launch_fwd_bulk_f32_state(t, p, s) : launch_fwd_bulk_f32_nostate(t, p, s));
+    if (e != cudaErrorNotSupported) return e;   // else: no tensor maps, element-wise staging
   }
 #define M3_X(r, tt, nd, ndb, nthb, gs)                                              \
   if (t.R == r && t.T == tt && t.ND == nd)                                        \

@@ -17,6 +17,9 @@
 #include "m3_internal.h"
 #include "m3_stage.cuh"
 #include "m3_tiles.h"
+#include "m3_tma.h"
+
+#include <string.h>
 
 #include <type_traits>
 
@@ -88,13 +91,15 @@ constexpr int kFwdUnroll = M3_FWD_UNROLL;
 
 // Shared memory of the forward kernel (bytes): delta, u (HBM dtype, 4 bytes
 // reserved per element), B, C (padded fp32), raw B/C rows and two mbarriers
-// (BULK staging), y of the first pass (bidirectional second pass only).
+// (BULK staging), y of the first pass (bidirectional second pass only).  The
+// tiles that TMA boxes land in (delta, u, y) start on 128-byte boundaries.
 template <int NP, int DT, bool BULK>
 struct FwdSmem {
   static constexpr size_t du = (size_t)kCK * DT * 4;             // one buffer of delta or u
   static constexpr size_t bc = (size_t)kCK * NP * 8;             // one buffer of B or C pairs
   static constexpr size_t braw = BULK ? 2 * 2 * (size_t)kCK * NP * 4 : 0;   // [2][B|C][kCK][NP]
-  static constexpr size_t off_y = 2 * 2 * du + 2 * 2 * bc + braw + 16;
+  static constexpr size_t off_bar = 2 * 2 * du + 2 * 2 * bc + braw;
+  static constexpr size_t off_y = off_bar + 128;
   static size_t bytes(bool bidir) { return off_y + (bidir ? 2 * (size_t)kCK * DT * 4 : 0); }
 };
 
@@ -102,8 +107,13 @@ struct FwdSmem {
 // that launches without it carry no code for the state-writing last step.
 // DU: element type of delta and u fixed at compile time (0 fp32, 1 bf16), or
 // -1 to read it from the parameters (the element-wise staging path).
+// BULK: delta, u and the first pass's y arrive as TMA boxes (tm_dl, tm_u, tm_y:
+// (B*L, D) row-major maps with a DT x kCK box), in memory row order.
 template <int R, int T, int ND, bool BULK, bool STATE, int DU>
-__global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(const FwdParams p) {
+__global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
+    scan_fwd_kernel(const FwdParams p, const __grid_constant__ CUtensorMap tm_dl,
+                    const __grid_constant__ CUtensorMap tm_u,
+                    const __grid_constant__ CUtensorMap tm_y) {
   using LM = LaneMap<R, T>;
   constexpr int NL = R + T;
   constexpr int NP = LM::NP;
@@ -113,7 +123,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
   constexpr int BCE = (kCK * NP + kThreads - 1) / kThreads;   // B/C prefetch per thread
 
   using SM = FwdSmem<NP, DT, BULK>;
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* s_dl = smem;                                 // [2][kCK*DT*4]
   unsigned char* s_u = s_dl + 2 * kCK * DT * 4;               // [2][kCK*DT*4]
   // B and C of each staged step in the padded lane layout, as (b, b) pairs so
@@ -121,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
   float2* s_b = reinterpret_cast<float2*>(s_u + 2 * kCK * DT * 4);  // [2][kCK][NP]
   float2* s_c = s_b + 2 * kCK * NP;
   float* s_braw = reinterpret_cast<float*>(s_c + 2 * kCK * NP);     // [2][B|C][kCK][NP] (BULK)
-  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + SM::off_y - 16);   // [2] (BULK)
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + SM::off_bar);   // [2] (BULK)
   float* s_y = reinterpret_cast<float*>(smem + SM::off_y);    // [2][kCK][DT] (bidir pass 2)
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
@@ -161,6 +171,11 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
 
   const int es_bc = p.dt_bc == M3_BF16 ? 2 : 4;
   if constexpr (BULK) {
+    // TMA boxes land at 128-byte aligned shared addresses; uniform over the CTA
+    if (smem_addr(smem) & 127u) {
+      if (tid == 0) set_err(p.err, M3_ERR_DEVICE);
+      return;
+    }
     if (tid == 0) {
       mbar_init(&s_bar[0], 1);
       mbar_init(&s_bar[1], 1);
@@ -210,55 +225,48 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
       }
     };
 
-    // BULK: warp 0 stages chunk c (delta, u, B, C rows) with one bulk copy per
-    // row, lane 0 first registering the byte count on the buffer's mbarrier;
-    // the first pass's y rows (second pass) move with 16-byte cp.async.
+    // BULK: thread 0 stages chunk c on the copy engine, completing on the
+    // buffer's mbarrier: delta, u (and, in the second pass, the first pass's
+    // y) as TMA boxes of kCK memory rows from the chunk's first memory row
+    // (rows past the chunk are never read; rows past the tensor read zero),
+    // the chunk's B and C rows as one contiguous block each.  y was written by
+    // this CTA's first pass with generic stores before an earlier barrier,
+    // hence the proxy fence.
     auto stage_bulk = [&](int c, int buf) {
       const int s0 = c * kCK, ns = min(kCK, L - s0);
-      const int lane = tid & 31;
-      if (lane == 0)
-        mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)ns * (uint32_t)(2 * DT * esz + 2 * N * es_bc));
-      __syncwarp();
-      for (int k = lane; k < 4 * ns; k += 32) {
-        const int tt = k >> 2, kind = k & 3;
-        const int s = s0 + tt;
-        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
-        if (kind < 2) {
-          unsigned char* dst = (kind == 0 ? s_dl : s_u) + buf * kCK * DT * 4 + (size_t)tt * DT * esz;
-          bulk_g2s(dst, (const char*)(kind == 0 ? p.delta : p.u) + (row * D + d0) * esz, DT * esz,
-                   &s_bar[buf]);
-        } else {
-          float* dst = s_braw + ((size_t)(buf * 2 + (kind - 2)) * kCK + tt) * NP;
-          bulk_g2s(dst, (const char*)(kind == 2 ? p.Bc : p.Cc) + row * N * es_bc, N * es_bc,
-                   &s_bar[buf]);
-        }
-      }
+      const int t_lo = dir ? L - s0 - ns : s0;
+      const uint32_t bcb = (uint32_t)(ns * N * es_bc);
+      const uint32_t bytes = (uint32_t)(2 * kCK * DT * esz) + 2 * bcb +
+                             (accumulate ? (uint32_t)(kCK * DT * 4) : 0u);
+      if (accumulate) fence_proxy_async_global();
+      mbar_arrive_expect_tx(&s_bar[buf], bytes);
+      const int y0 = b * L + t_lo;
+      tma_load_2d(s_dl + buf * kCK * DT * 4, &tm_dl, d0, y0, &s_bar[buf]);
+      tma_load_2d(s_u + buf * kCK * DT * 4, &tm_u, d0, y0, &s_bar[buf]);
+      const size_t bc_off = ((size_t)b * L + t_lo) * N * es_bc;
+      bulk_g2s(s_braw + (size_t)(buf * 2 + 0) * kCK * NP, (const char*)p.Bc + bc_off, bcb,
+               &s_bar[buf]);
+      bulk_g2s(s_braw + (size_t)(buf * 2 + 1) * kCK * NP, (const char*)p.Cc + bc_off, bcb,
+               &s_bar[buf]);
+      if (accumulate) tma_load_2d(s_y + (size_t)buf * kCK * DT, &tm_y, d0, y0, &s_bar[buf]);
     };
-    auto stage_y16 = [&](int c, int buf) {
-      const int s0 = c * kCK, ns = min(kCK, L - s0);
-      for (int v = tid; v < ns * (DT / 4); v += kThreads) {
-        const int tt = v / (DT / 4), w = v - tt * (DT / 4);
-        const int s = s0 + tt;
-        const size_t row = (size_t)b * L + (dir ? L - 1 - s : s);
-        cp_async16(s_y + (size_t)(buf * kCK + tt) * DT + w * 4, p.y + row * D + d0 + w * 4, true);
-      }
-    };
+    // raw B/C rows (memory order, N elements each) -> (b, b) pairs of the
+    // padded lane layout in processing order
     auto widen_bc = [&](int buf, int ns) {
       for (int i = tid; i < ns * NP; i += kThreads) {
         const int tt = i / NP, ln = i - tt * NP;
         const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
-        const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * kCK + tt) * NP;
-        const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * kCK + tt) * NP;
-        s_b[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rb0, n, p.dt_bc) : 0.f);
-        s_c[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rc0, n, p.dt_bc) : 0.f);
+        const size_t r = (size_t)(dir ? ns - 1 - tt : tt) * N + (n >= 0 ? n : 0);
+        const float* rb0 = s_braw + (size_t)(buf * 2 + 0) * kCK * NP;
+        const float* rc0 = s_braw + (size_t)(buf * 2 + 1) * kCK * NP;
+        s_b[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rb0, r, p.dt_bc) : 0.f);
+        s_c[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rc0, r, p.dt_bc) : 0.f);
       }
     };
 
     // prologue: chunk 0 into buffer 0
     if constexpr (BULK) {
-      if (tid < 32) stage_bulk(0, 0);
-      if (accumulate) stage_y16(0, 0);
-      cp_async_commit();
+      if (tid == 0) stage_bulk(0, 0);
     } else {
       stage_du<DT>(s_dl, s_u, p, b, d0, 0, dir, esz);
       if (accumulate) stage_y<DT>(s_y, p, b, d0, 0, dir);
@@ -271,14 +279,9 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
       const int buf = c & 1;
       const bool more = c + 1 < p.nch;
       if constexpr (BULK) {
-        if (more) {
-          if (tid < 32) stage_bulk(c + 1, buf ^ 1);
-          if (accumulate) stage_y16(c + 1, buf ^ 1);
-        }
-        cp_async_commit();
+        if (more && tid == 0) stage_bulk(c + 1, buf ^ 1);
         const bool ok = mbar_wait(&s_bar[buf], (uint32_t)(phase[buf] & 1));
         ++phase[buf];
-        cp_async_wait1();
         if (ok) widen_bc(buf, min(kCK, L - c * kCK));
         if (__syncthreads_or(!ok)) {
           // give up: let a copy still in flight land before the CTA exits
@@ -304,6 +307,9 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
       const float2* bc = s_c + buf * kCK * NP;
       const float* by = s_y + buf * kCK * DT;
       const int ns = min(kCK, L - c * kCK);
+      // staged delta/u/y rows: processing order (cp.async staging) or memory
+      // order (BULK: processing step tt is memory row ns-1-tt when reversed)
+      const int mrow0 = (BULK && dir) ? ns - 1 : 0, mstep = (BULK && dir) ? -1 : 1;
       // checkpoint of P = 2h + dBu before processing step s (the start of a
       // backward chunk: every p.cki steps)
       auto write_ckpt = [&](int s) {
@@ -335,9 +341,10 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
         constexpr bool FASTC = decltype(fast_tag)::value;
         const int s = c * kCK + tt;
         const int t = dir ? L - 1 - s : s;
+        const int mr = mrow0 + mstep * tt;
         float dl[ND], uu[ND];
-        read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * esz, bf16, dl);
-        read_chan<ND>(bu + (size_t)(tt * DT + grp * ND) * esz, bf16, uu);
+        read_chan<ND>(bdl + (size_t)(mr * DT + grp * ND) * esz, bf16, dl);
+        read_chan<ND>(bu + (size_t)(mr * DT + grp * ND) * esz, bf16, uu);
         float2 Bv[NL], Cv[NL];   // B, C of the thread's lanes as (b, b) pairs
 #pragma unroll
         for (int j = 0; j < NL; ++j) {
@@ -416,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS) scan_fwd_kernel(c
           const float tot = __fmul_rn(0.5f, quad_sum(part[k]));
           const int d = dbase + k;
           if ((k & 3) == q && d < D) {
-            yrow[d] = accumulate ? __fadd_rn(tot, by[tt * DT + grp * ND + k]) : tot;
+            yrow[d] = accumulate ? __fadd_rn(tot, by[mr * DT + grp * ND + k]) : tot;
           }
         }
       };
@@ -465,12 +472,28 @@ cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
   constexpr int NP = 4 * (R + T);
   constexpr int DT = 32 * ND;
   const size_t smem = FwdSmem<NP, DT, BULK>::bytes(p.direction == M3_DIR_BIDIR);
+  // BULK: delta, u, y as (B*L, D) row-major maps with a (DT x kCK) box;
+  // cudaErrorNotSupported (nothing launched) when the maps cannot be built
+  CUtensorMap maps[3];
+  memset(maps, 0, sizeof(maps));
+  if constexpr (BULK) {
+    static_assert(DU >= 0, "bulk staging needs a compile-time element type");
+    // TMA staging only for tiles of at most 128 channels (the configurations
+    // validated on the GPU); wider tiles take the element-wise staging
+    if constexpr (DT > 128) return cudaErrorNotSupported;
+    const size_t rows = (size_t)p.B * p.L;
+    const int edu = DU == 1 ? 2 : 4;
+    if (!encode_rows_map(&maps[0], p.delta, edu, rows, p.D, DT, kCK) ||
+        !encode_rows_map(&maps[1], p.u, edu, rows, p.D, DT, kCK) ||
+        !encode_rows_map(&maps[2], p.y, 4, rows, p.D, DT, kCK))
+      return cudaErrorNotSupported;
+  }
   auto kern = scan_fwd_kernel<R, T, ND, BULK, STATE, DU>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B, (p.D + DT - 1) / DT);
-  kern<<<grid, kThreads, smem, stream>>>(p);
+  kern<<<grid, kThreads, smem, stream>>>(p, maps[0], maps[1], maps[2]);
   return cudaGetLastError();
 }
 
