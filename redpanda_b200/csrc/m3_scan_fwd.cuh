@@ -264,9 +264,19 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
       }
     };
 
-    // prologue: chunk 0 into buffer 0
+    // prologue: chunk 0 into buffer 0 (BULK: landed and widened before the
+    // loop; each chunk then waits for and widens its successor at its end,
+    // under the barrier that closes it)
     if constexpr (BULK) {
       if (tid == 0) stage_bulk(0, 0);
+      const bool ok = mbar_wait(&s_bar[0], (uint32_t)(phase[0] & 1));
+      ++phase[0];
+      if (ok) widen_bc(0, min(kCK, L));
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) mbar_wait(&s_bar[0], (uint32_t)((phase[0] - 1) & 1));
+        fail = 1;
+        break;
+      }
     } else {
       stage_du<DT>(s_dl, s_u, p, b, d0, 0, dir, esz);
       if (accumulate) stage_y<DT>(s_y, p, b, d0, 0, dir);
@@ -280,15 +290,6 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
       const bool more = c + 1 < p.nch;
       if constexpr (BULK) {
         if (more && tid == 0) stage_bulk(c + 1, buf ^ 1);
-        const bool ok = mbar_wait(&s_bar[buf], (uint32_t)(phase[buf] & 1));
-        ++phase[buf];
-        if (ok) widen_bc(buf, min(kCK, L - c * kCK));
-        if (__syncthreads_or(!ok)) {
-          // give up: let a copy still in flight land before the CTA exits
-          if (tid == 0 && more) mbar_wait(&s_bar[buf ^ 1], (uint32_t)(phase[buf ^ 1] & 1));
-          fail = 1;
-          break;
-        }
       } else {
         if (more) {
           stage_du<DT>(s_dl + (buf ^ 1) * kCK * DT * 4, s_u + (buf ^ 1) * kCK * DT * 4, p, b, d0,
@@ -457,10 +458,23 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
           for (int tt = seg; tt < send; ++tt) step(tt, std::false_type{});
         }
       }
-      if constexpr (!BULK) {
+      if constexpr (BULK) {
+        bool ok = true;
+        if (more) {
+          ok = mbar_wait(&s_bar[buf ^ 1], (uint32_t)(phase[buf ^ 1] & 1));
+          ++phase[buf ^ 1];
+          if (ok) widen_bc(buf ^ 1, min(kCK, L - (c + 1) * kCK));
+        }
+        if (__syncthreads_or(!ok)) {
+          // give up: let the copy still in flight land before the CTA exits
+          if (tid == 0) mbar_wait(&s_bar[buf ^ 1], (uint32_t)((phase[buf ^ 1] - 1) & 1));
+          fail = 1;
+          break;
+        }
+      } else {
         if (more) store_bc(buf ^ 1);
+        __syncthreads();
       }
-      __syncthreads();
     }
   }
   cp_async_wait0();
