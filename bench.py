@@ -290,11 +290,21 @@ def run_m3(args):
     value = tokens / (ms / 1e3) / 1e9
 
     # ---- end-to-end leg: every step copies its inputs in from pinned host memory
-    # and its parameter grads out.  The copy of step i+1's inputs runs on a copy
-    # stream into the second of two device buffer sets while step i computes;
-    # all K copies are inside the timed region (the first one is not hidden).
+    # and its parameter grads out, streaming each step's rows in NSUB sub-batches
+    # through the same public calls (ScanPlan.forward/backward on row slices):
+    # the copy of sub-batch g+1 runs on a copy stream into the second of two
+    # device buffer sets while sub-batch g computes, the parameter grads of the
+    # sub-batches are summed on the device and read back once per step.  All
+    # copies are inside the timed region (the very first one is not hidden).
+    nsub = 4 if B_RANK % 4 == 0 and B_RANK >= 64 else 1
+    bsub = B_RANK // nsub
+    splan = plan if nsub == 1 else ScanPlan(bsub, L, D, N, N_ROT, bf, bf, S.M3_DIR_BIDIR)
+    sckpt = ckpt if nsub == 1 else torch.empty(splan.ckpt_floats(), device=dev)
+    sws = ws if nsub == 1 else torch.empty(splan.workspace_bytes(), device=dev, dtype=torch.uint8)
+    gsub = torch.empty_like(gflat)
     host = {k: v.cpu().pin_memory() for k, v in x.items()}
-    dbufs = [{k: torch.empty_like(v) for k, v in x.items()} for _ in range(2)]
+    dbufs = [{k: torch.empty((bsub,) + tuple(v.shape[1:]), dtype=v.dtype, device=dev)
+              for k, v in x.items()} for _ in range(2)]
     gout = torch.empty(gflat.shape, dtype=gflat.dtype).pin_memory()
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = gout.numel() * gout.element_size()
@@ -302,27 +312,43 @@ def run_m3(args):
     copied = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
 
-    def h2d_copy(i):
-        slot = i & 1
-        if i >= 2:
-            copy_stream.wait_event(consumed[slot])   # step i-2 is done with this buffer set
+    def h2d_copy(gi):
+        slot, j = gi & 1, gi % nsub
+        if gi >= 2:
+            copy_stream.wait_event(consumed[slot])   # sub-batch gi-2 is done with this set
         with torch.cuda.stream(copy_stream):
             for k in host:
-                dbufs[slot][k].copy_(host[k], non_blocking=True)
+                dbufs[slot][k].copy_(host[k][j * bsub:(j + 1) * bsub], non_blocking=True)
             copied[slot].record(copy_stream)
+
+    def sub_step(inp, j):
+        rows = slice(j * bsub, (j + 1) * bsub)
+        splan.forward(inp["delta"], inp["u"], inp["Bc"], inp["Cc"], Ar_p, Ai_p, Tk_p, y[rows],
+                      sckpt)
+        splan.backward(inp["delta"], inp["u"], inp["Bc"], inp["Cc"], Ar_p, Ai_p, Tk_p,
+                       inp["dy"], sckpt, gd[rows], gu[rows], gB[rows], gC[rows],
+                       gsub[0], gsub[1], gsub[2], sws)
+        if j == 0:
+            gflat.copy_(gsub)
+        else:
+            gflat.add_(gsub)
+        if j == nsub - 1 and world > 1:
+            dist.all_reduce(gflat)
 
     def e2e_run(k_steps, start_event=None):
         if start_event is not None:
             copy_stream.wait_event(start_event)
+        total = k_steps * nsub
         h2d_copy(0)
-        for i in range(k_steps):
-            slot = i & 1
-            if i + 1 < k_steps:
-                h2d_copy(i + 1)
+        for gi in range(total):
+            slot, j = gi & 1, gi % nsub
+            if gi + 1 < total:
+                h2d_copy(gi + 1)
             stream.wait_event(copied[slot])
-            step(dbufs[slot])
+            sub_step(dbufs[slot], j)
             consumed[slot].record(stream)
-            gout.copy_(gflat, non_blocking=True)
+            if j == nsub - 1:
+                gout.copy_(gflat, non_blocking=True)
 
     e2e_run(max(1, args.warmup))
     barrier()
@@ -364,7 +390,8 @@ def run_m3(args):
                        "parallelism": f"dp{world}", "l2": "inputs larger than L2 (no flush)",
                        "compute": "fp32 state/accumulation, bf16 inputs and input grads"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps},
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps,
+                    "sub_batches": nsub},
             "gpu_launches": 4 * args.steps,
             "roofline": {"bound": "hbm", "kernel": "scan_bwd (m3_scan_bwd)",
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
