@@ -16,7 +16,7 @@
 //   Polynomial coefficients are this project's own least-squares fits on
 //   Chebyshev nodes of [-pi/2, pi/2] (errors include the fp32 Horner evaluation):
 //     cos: 6 terms in r^2,          max abs error 9.0e-8
-//     sin: r * (7 terms in r^2),    max rel error 1.0e-7
+//     sin: r * (6 terms in r^2),    max rel error 1.1e-7
 //   Arguments beyond the reduction's exact range (|k| > 2048, i.e.
 //   |delta*A_imag| > ~6400) take the accurate libm path instead.
 #pragma once
@@ -99,14 +99,13 @@ __device__ __forceinline__ float2 gate_cos2_nocheck(float2 dl, float2 ai) {
 
 // sin and cos of dl*ai with the reduction by pi: both share the sign (-1)^k,
 // cos is computed exactly as gate_cos() (so the backward's gate equals the
-// forward's bit for bit) and sin uses a 7-term odd polynomial on [-pi/2, pi/2]
-// (this project's least-squares fit, max relative error 1.0e-7).
+// forward's bit for bit) and sin uses a 6-term odd polynomial on [-pi/2, pi/2]
+// (this project's least-squares fit, max relative error 1.1e-7).
 __device__ __forceinline__ float sin_poly(float r, float s) {
-  float p = 0x1.5328dcp-33f;
-  p = __fmaf_rn(p, s, -0x1.ae0874p-26f);
-  p = __fmaf_rn(p, s, 0x1.71dd12p-19f);
-  p = __fmaf_rn(p, s, -0x1.a019fep-13f);
-  p = __fmaf_rn(p, s, 0x1.111112p-7f);
+  float p = -0x1.9a6850p-26f;
+  p = __fmaf_rn(p, s, 0x1.71707ep-19f);
+  p = __fmaf_rn(p, s, -0x1.a017dap-13f);
+  p = __fmaf_rn(p, s, 0x1.11110cp-7f);
   p = __fmaf_rn(p, s, -0x1.555556p-3f);
   return __fmaf_rn(__fmul_rn(r, s), p, r);
 }
@@ -146,11 +145,10 @@ __device__ __forceinline__ void gate_sincos2_nocheck(float2 dl, float2 ai, float
   p = __ffma2_rn(p, s, f2(0x1.555548p-5f));
   p = __ffma2_rn(p, s, f2(-0.5f));
   p = __ffma2_rn(p, s, f2(1.0f));
-  float2 q = f2(0x1.5328dcp-33f);
-  q = __ffma2_rn(q, s, f2(-0x1.ae0874p-26f));
-  q = __ffma2_rn(q, s, f2(0x1.71dd12p-19f));
-  q = __ffma2_rn(q, s, f2(-0x1.a019fep-13f));
-  q = __ffma2_rn(q, s, f2(0x1.111112p-7f));
+  float2 q = f2(-0x1.9a6850p-26f);
+  q = __ffma2_rn(q, s, f2(0x1.71707ep-19f));
+  q = __ffma2_rn(q, s, f2(-0x1.a017dap-13f));
+  q = __ffma2_rn(q, s, f2(0x1.11110cp-7f));
   q = __ffma2_rn(q, s, f2(-0x1.555556p-3f));
   q = __ffma2_rn(__fmul2_rn(r, s), q, r);
   const unsigned ox = __float_as_uint(j.x) << 31, oy = __float_as_uint(j.y) << 31;
