@@ -47,6 +47,8 @@ namespace bwd {
 
 constexpr int kUnrollRecompute = M3_BWD_UNROLL_RECOMPUTE;
 constexpr int kUnrollReverse = M3_BWD_UNROLL_REVERSE;
+// BULK: warps whose lane 0 issues a share of each work item's copies
+constexpr int kStageWarps = 4;
 
 constexpr int pow2ceil(int x) {
   int p = 1;
@@ -157,6 +159,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   constexpr int TT = T > 0 ? T : 1;
   constexpr int BCE = (KC * NP + NTH - 1) / NTH;
   static_assert(CF::NCOLS <= 512, "TMEM holds at most 512 columns");
+  static_assert(!BULK || NTH / 32 >= kStageWarps, "bulk staging issues from 4 warps");
 
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* s_dl = smem;                                        // [2][raw]
@@ -193,8 +196,8 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
       return;
     }
     if (tid == 0) {   // one barrier per staging buffer, one for the scratch rows
-      mbar_init(&s_bar[0], 1);
-      mbar_init(&s_bar[1], 1);
+      mbar_init(&s_bar[0], kStageWarps);
+      mbar_init(&s_bar[1], kStageWarps);
       mbar_init(&s_bar[2], 1);
       mbar_fence_init();
     }
@@ -309,29 +312,40 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   // contiguous block each (memory order).
   const int es_bc = p.dt_bc == M3_BF16 ? 2 : 4;
   auto stage_vec = [&](int b, int pass, int c, int buf) {
-    if (tid != 0) return;
+    // lane 0 of warps 0..3 each registers its own bytes and issues its copies
+    // (an issuing thread waits on every copy instruction, so four issue in
+    // parallel); the buffer's barrier expects kStageWarps arrivals per item
+    const int w = tid >> 5;
+    if ((tid & 31) != 0 || w >= kStageWarps) return;
     const int dir = dir_of(pass), s0 = c * KC;
     const int ns = min(KC, L - s0);
     const int t_lo = dir ? L - s0 - ns : s0;             // first memory row of the chunk
-    const uint32_t bc_bytes = (uint32_t)(ns * N * es_bc);
-    const uint32_t bytes = (uint32_t)(KC * DT * (2 * es_du + es_dy)) + 2 * bc_bytes +
-                           (c > 0 ? (uint32_t)(DT * NP * 4) : 0u);
-    mbar_arrive_expect_tx(&s_bar[buf], bytes);
     const int y0 = b * L + t_lo;
-    tma_load_2d(s_dl + buf * CF::raw_bytes, &tm_dl, d0, y0, &s_bar[buf]);
-    tma_load_2d(s_u + buf * CF::raw_bytes, &tm_u, d0, y0, &s_bar[buf]);
-    tma_load_2d(s_dy + buf * CF::raw_bytes, &tm_dy, d0, y0, &s_bar[buf]);
-    if (c > 0) {
-      const int dslot = bidir ? dir : 0;
-      const float* src =
-          p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
-      bulk_g2s(s_ck + buf * DT * NP, src, DT * NP * 4, &s_bar[buf]);
+    if (w == 0) {
+      mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)(KC * DT * es_du));
+      tma_load_2d(s_dl + buf * CF::raw_bytes, &tm_dl, d0, y0, &s_bar[buf]);
+    } else if (w == 1) {
+      mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)(KC * DT * es_du));
+      tma_load_2d(s_u + buf * CF::raw_bytes, &tm_u, d0, y0, &s_bar[buf]);
+    } else if (w == 2) {
+      mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)(KC * DT * es_dy) +
+                                             (c > 0 ? (uint32_t)(DT * NP * 4) : 0u));
+      tma_load_2d(s_dy + buf * CF::raw_bytes, &tm_dy, d0, y0, &s_bar[buf]);
+      if (c > 0) {
+        const int dslot = bidir ? dir : 0;
+        const float* src =
+            p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
+        bulk_g2s(s_ck + buf * DT * NP, src, DT * NP * 4, &s_bar[buf]);
+      }
+    } else {
+      const uint32_t bc_bytes = (uint32_t)(ns * N * es_bc);
+      mbar_arrive_expect_tx(&s_bar[buf], 2 * bc_bytes);
+      const size_t bc_off = ((size_t)b * L + t_lo) * N * es_bc;
+      bulk_g2s(s_braw + ((size_t)(buf * 2 + 0) * KC) * NP, (const char*)p.Bc + bc_off, bc_bytes,
+               &s_bar[buf]);
+      bulk_g2s(s_braw + ((size_t)(buf * 2 + 1) * KC) * NP, (const char*)p.Cc + bc_off, bc_bytes,
+               &s_bar[buf]);
     }
-    const size_t bc_off = ((size_t)b * L + t_lo) * N * es_bc;
-    bulk_g2s(s_braw + ((size_t)(buf * 2 + 0) * KC) * NP, (const char*)p.Bc + bc_off, bc_bytes,
-             &s_bar[buf]);
-    bulk_g2s(s_braw + ((size_t)(buf * 2 + 1) * KC) * NP, (const char*)p.Cc + bc_off, bc_bytes,
-             &s_bar[buf]);
   };
   // widen the raw B/C rows of buffer buf into the padded fp32 lane layout
   // (processing step tt is memory row tt, or ns-1-tt for the reversed scan).
@@ -412,7 +426,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
       // before the previous barrier (generic stores, hence the proxy fence),
       // needed from the first flush on
       if (second_of_two) {
-        if (tid == 0) {
+        if (tid == 32) {   // lane 0 of warp 1, which issues one TMA box per item
           const int t_lo = dir ? L - s0 - ns : s0;
           fence_proxy_async_global();
           mbar_arrive_expect_tx(&s_bar[2], (uint32_t)(ns * DT * 8));
