@@ -161,6 +161,9 @@ BULK_CASES = [
     ("c1_layout_bidir_bf16", ScanShape(2, 64, 256, 32, 16, 4), torch.bfloat16, 2),
     ("c3_layout_causal", ScanShape(2, 50, 256, 32, 8, 2), torch.float32, 0),
     ("c0_layout_reverse", ScanShape(2, 20, 256, 16, 4, 4), torch.float32, 1),
+    # TMA boxes of the last, ragged chunk reach past the end of the tensor
+    ("c1_layout_bidir_bf16_ragged", ScanShape(3, 37, 256, 32, 16, 4), torch.bfloat16, 2),
+    ("c3_layout_reverse_bf16_ragged", ScanShape(3, 29, 256, 32, 8, 2), torch.bfloat16, 1),
 ]
 
 
