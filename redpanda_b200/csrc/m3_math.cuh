@@ -18,7 +18,13 @@
 //     cos: 6 terms in r^2,          max abs error 9.0e-8
 //     sin: r * (6 terms in r^2),    max rel error 1.1e-7
 //   Arguments beyond the reduction's exact range (|k| > 2048, i.e.
-//   |delta*A_imag| > ~6400) take the accurate libm path instead.
+//   |delta*A_imag| > ~6400) take a slow path in double precision: the product
+//   of two fp32 values is exact in fp64 (48 significant bits), and the CUDA
+//   double-precision cos/sin of it, rounded once to fp32, are within half an
+//   fp32 ulp or so of the true values.  All three paths (packed, scalar and
+//   slow) therefore evaluate the gate at the EXACT product delta*A_imag; an
+//   fp32 evaluation at the rounded product would be off by up to
+//   |x| * 2^-24 (~4e-4 at |x| = 6400) in the argument.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -43,9 +49,16 @@ __device__ __forceinline__ float gate_exp(float dl, float a2) {
   return ex2_approx(__fmul_rn(dl, a2));
 }
 
-static __device__ __noinline__ float cos_slow(float dl, float ai) { return cosf(__fmul_rn(dl, ai)); }
+// |k| > 2048: cos / sin of the exact product in double precision.  cos is
+// evaluated by the same call in both helpers, so the forward's and the
+// backward's gates agree bit for bit on this path too.
+static __device__ __noinline__ float cos_slow(float dl, float ai) {
+  return (float)cos((double)dl * (double)ai);
+}
 static __device__ __noinline__ void sincos_slow(float dl, float ai, float* s, float* c) {
-  sincosf(__fmul_rn(dl, ai), s, c);
+  const double x = (double)dl * (double)ai;
+  *c = (float)cos(x);
+  *s = (float)sin(x);
 }
 
 // cos(dl * ai): reduction by pi, |r| <= pi/2, sign from the parity of k.

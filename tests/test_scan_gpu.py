@@ -1,19 +1,32 @@
 """GPU parity of the sm_100a scan kernels against the CPU oracle.
 
-Bars (norm-wise relative error max|a-b| / max|ref|, against the reference's own
-fp32 numerics, i.e. the oracle run in float32):
-  * forward y: 1e-5
-  * fp32 gradients: 1e-6, with the fp64 oracle as tie-breaker: a gradient that
-    misses 1e-6 against the fp32 reference still passes when it is at least as
-    close to the fp64 result as the fp32 reference is
+Bars (norm-wise relative error max|a-b| / max|ref|):
+  * forward y: 1e-5 against the reference's own fp32 numerics (the oracle run
+    in float32)
+  * fp32 gradients: 1e-6 against the same fp32 reference.  A (case, key) pair
+    that misses it passes only when it is listed in GRAD_ALLOW below, with
+    its measured value and a bound, AND is at least as close to the float64
+    recurrence as the fp32 reference itself is (there the fp32 reference, not
+    the kernel, carries the larger error)
   * bf16 outputs (grads cast to the bf16 input dtype, as triton_scan.py:313-315
     does): within one bf16 ulp of the fp32 reference value
+Every measured error is recorded in helpers.PARITY_TABLE and printed as a
+table at the end of the pytest run (tests/conftest.py), so the figures behind
+these bars are part of the test output.
+
+The wide gate-argument cases (test_scan_parity_wide_gate_arguments) drive
+|delta*A_imag| far past the benchmark range (see helpers.wide_gate_inputs).
+There the reference's fp32 path evaluates cos at the fp32-ROUNDED product
+delta*A_imag and is itself 6e-6..6e-4 from the exact recurrence, so those
+cases are held to the same bars against the float64 recurrence, and the fp32
+reference's own distance is recorded beside them.
 """
 
 import pytest
 import torch
 
-from helpers import GRAD_KEYS, oracle_scan, rel_err, to_cuda
+from helpers import (GRAD_KEYS, PARITY_TABLE, WIDE_REGIMES, gate_arg_stats, oracle_scan,
+                     rel_err, to_cuda, wide_gate_inputs)
 from redpanda_b200 import scan as S
 from redpanda_b200.synthetic import ScanShape, make_scan_inputs
 
@@ -72,6 +85,38 @@ def _bf16_ok(a, ref):
     return bool(((a - ref).abs() <= ulp + 1e-6 * ref.abs().max()).all())
 
 
+# (case, gradient key) -> (error vs the fp32 reference measured on a B200, bound).
+# Each entry is a gradient whose fp32 rounding differs from the reference's
+# fp32 rounding by a little more than 1e-6 of its largest element while being
+# at least as close to the float64 recurrence as the reference is.
+GRAD_ALLOW = {}
+
+
+def _check_grads(name, g, g32, g64, failures):
+    """Record every gradient's errors and collect the ones that miss their bar."""
+    for k in GRAD_KEYS:
+        if g[k] is None:
+            continue
+        e32 = rel_err(g[k], g32[k])
+        e64 = rel_err(g[k], g64[k])
+        r64 = rel_err(g32[k], g64[k])
+        if g[k].dtype == torch.bfloat16:
+            ok = _bf16_ok(g[k], g32[k])
+            PARITY_TABLE.append((name, "d" + k, "bf16", e32, e64, r64,
+                                 "ok (1 bf16 ulp)" if ok else "FAIL"))
+            if not ok:
+                failures.append((k, "bf16 ulp"))
+            continue
+        if e32 <= GRAD_TOL:
+            verdict = "ok"
+        elif (name, k) in GRAD_ALLOW and e32 <= GRAD_ALLOW[(name, k)][1] and e64 <= max(r64, GRAD_TOL):
+            verdict = "allow-listed"
+        else:
+            verdict = "FAIL"
+            failures.append((k, e32))
+        PARITY_TABLE.append((name, "d" + k, "fp32", e32, e64, r64, verdict))
+
+
 @pytest.mark.parametrize("name,shape,dtype,direction", CASES, ids=[c[0] for c in CASES])
 def test_scan_parity(name, shape, dtype, direction):
     inp = make_scan_inputs(shape, seed=11, dtype=dtype)
@@ -80,16 +125,74 @@ def test_scan_parity(name, shape, dtype, direction):
     y32, g32 = oracle_scan(inp32, direction, torch.float32)
     y64, g64 = oracle_scan(inp32, direction, torch.float64)
     assert y.dtype == torch.float32
-    assert rel_err(y, y32) <= FWD_TOL
+    ey = rel_err(y, y32)
+    PARITY_TABLE.append((name, "y", "fp32", ey, rel_err(y, y64), rel_err(y32, y64),
+                         "ok" if ey <= FWD_TOL else "FAIL"))
+    failures = []
+    _check_grads(name, g, g32, g64, failures)
+    assert ey <= FWD_TOL
+    assert not failures, failures
+
+
+WIDE_CASES = [
+    # regime, shape, input dtype, direction
+    (r, sh, dt, d)
+    for r in WIDE_REGIMES
+    for (sh, dt, d) in (
+        (ScanShape(2, 64, 256, 32, 16, 4), torch.float32, 2),    # config-1 lane layout
+        (ScanShape(2, 64, 256, 32, 16, 4), torch.bfloat16, 2),
+        (ScanShape(2, 50, 256, 32, 8, 2), torch.float32, 0),     # config-3 lane layout
+        (ScanShape(2, 40, 256, 16, 4, 4), torch.float32, 1),     # config-0 lane layout
+        (ScanShape(2, 64, 128, 32, 16, 4), torch.bfloat16, 0),
+    )
+]
+
+
+@pytest.mark.parametrize("regime,shape,dtype,direction", WIDE_CASES,
+                         ids=[f"{c[0]}-N{c[1].d_state}T{c[1].n_track}-"
+                              f"{'bf16' if c[2] == torch.bfloat16 else 'f32'}-"
+                              f"{('causal', 'reverse', 'bidir')[c[3]]}" for c in WIDE_CASES])
+def test_scan_parity_wide_gate_arguments(regime, shape, dtype, direction):
+    """Forward and every gradient over the whole range of the gate's argument
+    reduction (2 <= |k| <= 2048 on the packed path, the checked per-step path,
+    and the double-precision slow path for |k| > 2048), against the float64
+    recurrence (mamba.py:396-401 evaluated exactly)."""
+    inp = wide_gate_inputs(shape, 41, regime, dtype=dtype)
+    xmax, kmax, frac_slow = gate_arg_stats(inp)
+    if regime == "k_mid":
+        assert 2 <= kmax <= 2048 and frac_slow == 0.0
+    elif regime == "mixed":
+        assert kmax > 2048 and 0.0 < frac_slow < 0.05
+    else:
+        assert frac_slow > 0.9
+    inp32 = {k: (None if v is None else v.float()) for k, v in inp.items()}
+    y, g = run_m3(inp, direction, dtype)
+    y32, g32 = oracle_scan(inp32, direction, torch.float32)
+    y64, g64 = oracle_scan(inp32, direction, torch.float64)
+    name = f"wide_{regime}_N{shape.d_state}T{shape.n_track}_dir{direction}_" + \
+        ("bf16" if dtype == torch.bfloat16 else "f32")
+    ey = rel_err(y, y64)
+    PARITY_TABLE.append((name, "y", "fp32", rel_err(y, y32), ey, rel_err(y32, y64),
+                         "ok" if ey <= FWD_TOL else "FAIL"))
+    failures = [("y", ey)] if ey > FWD_TOL else []
     for k in GRAD_KEYS:
         if g[k] is None:
             continue
+        e64 = rel_err(g[k], g64[k])
+        r64 = rel_err(g32[k], g64[k])
         if g[k].dtype == torch.bfloat16:
-            assert _bf16_ok(g[k], g32[k]), k
+            ok = _bf16_ok(g[k], g64[k])
+            PARITY_TABLE.append((name, "d" + k, "bf16", rel_err(g[k], g32[k]), e64, r64,
+                                 "ok (1 bf16 ulp of fp64)" if ok else "FAIL"))
+            if not ok:
+                failures.append((k, "bf16 ulp"))
             continue
-        e32 = rel_err(g[k], g32[k])
-        if e32 > GRAD_TOL:
-            assert rel_err(g[k], g64[k]) <= max(rel_err(g32[k], g64[k]), GRAD_TOL), (k, e32)
+        PARITY_TABLE.append((name, "d" + k, "fp32", rel_err(g[k], g32[k]), e64, r64,
+                             "ok" if e64 <= GRAD_TOL else "FAIL"))
+        if e64 > GRAD_TOL:
+            failures.append((k, e64))
+    assert not failures, (failures, xmax, kmax, frac_slow)
+    assert S.device_error() == 0
 
 
 def test_grad_dtypes_follow_inputs():

@@ -6,7 +6,7 @@ import pytest
 import torch
 
 import oracle as O
-from helpers import rel_err, to_cuda
+from helpers import WIDE_REGIMES, gate_arg_stats, rel_err, to_cuda, wide_gate_inputs
 from redpanda_b200 import scan as S
 from redpanda_b200.synthetic import ScanShape, make_scan_inputs
 
@@ -41,6 +41,45 @@ def test_step_bit_exact_vs_scan_every_position(sh):
     assert torch.equal(ys, y)
     assert torch.equal(hs, h)
     assert torch.equal(ds, dbu)
+
+
+WIDE_STEP_SHAPES = [
+    ScanShape(3, 40, 256, 32, 8, 2),     # config-3 state layout
+    ScanShape(2, 24, 128, 32, 16, 4),    # config-1 layout
+    ScanShape(2, 20, 96, 16, 4, 4),      # config-0 layout, D not a multiple of 64
+]
+
+
+@pytest.mark.parametrize("regime", WIDE_REGIMES)
+@pytest.mark.parametrize("sh", WIDE_STEP_SHAPES,
+                         ids=lambda s: f"B{s.batch}L{s.seqlen}D{s.d_inner}N{s.d_state}")
+def test_step_bit_exact_vs_scan_wide_gate_arguments(sh, regime):
+    """Step == scan at every position, bit for bit, when the gate arguments
+    |delta*A_imag| cover the packed path with |k| >= 2, the checked path and the
+    double-precision slow path (helpers.wide_gate_inputs); the factored step
+    too."""
+    inp = wide_gate_inputs(sh, 43, regime)
+    _, kmax, _ = gate_arg_stats(inp)
+    assert kmax >= 2
+    g = to_cuda(inp)
+    y, (h, dbu) = S.m3_scan_with_state(g["delta"], g["u"], g["Bc"], g["Cc"], g["A_real"],
+                                       g["A_imag"], g["track"], sh.n_rot, sh.d_state)
+    ys, hs, ds = _step_all(g, sh)
+    assert torch.equal(ys, y)
+    assert torch.equal(hs, h)
+    assert torch.equal(ds, dbu)
+    hf = torch.zeros_like(hs)
+    fa = torch.zeros(sh.batch, sh.d_inner + sh.d_state, device="cuda")
+    fb = torch.empty_like(fa)
+    for t in range(sh.seqlen):
+        yt = S.m3_step_factored_(hf, fa, fb, g["delta"][:, t], g["u"][:, t], g["Bc"][:, t],
+                                 g["Cc"][:, t], g["A_real"], g["A_imag"], g["track"], sh.n_rot,
+                                 sh.d_state)
+        assert torch.equal(yt, y[:, t]), t
+        fa, fb = fb, fa
+    assert torch.equal(hf, h)
+    assert torch.isfinite(y).all()
+    assert S.device_error() == 0
 
 
 def test_step_continues_a_primed_prefix_bit_exactly():
