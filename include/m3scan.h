@@ -237,7 +237,10 @@ M3_API int m3_gate(int64_t rows, int32_t d_inner, const float* y, const void* u,
  *     rejected with M3_ERR_SCRATCH_LIMIT.
  *   - The first call on each device looks up the buffer's device address (with
  *     that device current) and caches it; make that first call before any
- *     stream capture.
+ *     stream capture.  The cached address belongs to the device's current
+ *     context: after cudaDeviceReset (or any other reset of the primary
+ *     context) in the same process, this entry point must not be called
+ *     again, since it would hand the kernels the stale address.
  *   - All calls on a device share the one buffer, which keeps the last call's
  *     contents.  Calls whose executions overlap on the GPU (other streams, or
  *     other host threads) race on it and corrupt each other's results. */

@@ -14,7 +14,10 @@
 // Host code may not use the array's name as a device address (it is a host-side
 // stand-in), so the first call on each device looks the address up with
 // cudaGetSymbolAddress while that device is current, checks the result and
-// caches it; later calls on the device reuse the cached address.
+// caches it; later calls on the device reuse the cached address.  The cache is
+// never invalidated: after a reset of the device's primary context
+// (cudaDeviceReset) in the same process the cached address is stale, so the
+// entry point must not be used after such a reset.
 #include <cuda_runtime.h>
 
 #include <mutex>
