@@ -6,11 +6,11 @@ initialisation) over :class:`redpanda_b200.mamba.Mamba`.  The O(1) node step
 step kernel; priming runs the scan with ``return_state``.
 ``dynamics_rollout`` (the training rollout, search_mamba.py:252-273) uses the
 equivalent causal scan over the concatenated board + move tokens, so it is
-differentiable through the scan kernel's analytic backward.
+differentiable through the scan kernel's analytic backward.  Checkpoint I/O
+(search_mamba.py:347-383) is not part of the scan/step path and is not
+mirrored; the heads keep the reference's parameter names, so a state dict that
+the reference saved loads with ``load_state_dict``.
 """
-
-import json
-from dataclasses import asdict, fields as dc_fields
 
 import torch
 import torch.nn as nn
@@ -151,30 +151,3 @@ class SearchMamba(nn.Module):
         hidden = self.backbone(torch.cat([board_encoding, move_tokens], dim=1))[:, Lb:]
         values = torch.tanh(self.value_head(hidden)).squeeze(-1)
         return values, self.continuation_head(hidden), self.consistency_proj(hidden)
-
-    # -- persistence (search_mamba.py:347-383)
-    def save_pretrained(self, path):
-        torch.save(self.state_dict(), path)
-        cfg_path = path.replace('.pt', '_config.json').replace('.pth', '_config.json')
-        if cfg_path == path:
-            cfg_path = path + '.config.json'
-        cfg = asdict(self.config)
-        cfg["eval_dim"] = self.eval_dim
-        with open(cfg_path, 'w') as f:
-            json.dump(cfg, f, indent=2)
-
-    @classmethod
-    def from_pretrained(cls, path, device='cpu', config=None):
-        eval_dim = 512
-        if config is None:
-            cfg_path = path.replace('.pt', '_config.json').replace('.pth', '_config.json')
-            if cfg_path == path:
-                cfg_path = path + '.config.json'
-            with open(cfg_path) as f:
-                cfg = json.load(f)
-            eval_dim = int(cfg.get("eval_dim", 512))
-            valid = {f.name for f in dc_fields(SearchMambaConfig)}
-            config = SearchMambaConfig(**{k: v for k, v in cfg.items() if k in valid})
-        model = cls(config, eval_dim=eval_dim)
-        model.load_state_dict(torch.load(path, map_location=device, weights_only=True))
-        return model

@@ -72,12 +72,29 @@ def scan_case(M, shape, seed, bidir):
     return out
 
 
-def model_case(M, kw, seed, L, bidir):
+def _set_phases(layers, seed, bound=1.4):
+    """Draw every layer's A_phase from U(-bound, bound).  The reference
+    initialises it to zero (mamba.py:188), which leaves A_imag = 0 and the
+    rotation unused.  |phase| < pi/2 keeps A_real = -exp(A_log_mag)*cos(phase)
+    negative (decaying gates); a phase past pi/2 makes A_real positive, the
+    gates exceed 1 and the reference's own outputs overflow within a few dozen
+    tokens."""
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for layer in layers:
+            mixer = layer["mixer"]
+            if hasattr(mixer, "A_phase"):
+                mixer.A_phase.copy_((torch.rand(mixer.A_phase.shape, generator=g) * 2 - 1) * bound)
+
+
+def model_case(M, kw, seed, L, bidir, phases=False):
     """Reference Mamba: forward, step chain, prime_cache and parameter grads."""
     torch.manual_seed(seed)
     cfg = M.MambaConfig(vocab_size=64, bidirectional=bidir, scan_checkpoint=True,
                         use_triton_scan=False, **kw)
     m = M.Mamba(cfg)
+    if phases:
+        _set_phases(m.layers, seed + 100)
     ids = torch.randint(0, 64, (3, L))
     out = {"kw": dict(kw), "bidir": bidir, "seed": seed, "ids": ids,
            "state_dict": {k: v.clone() for k, v in m.state_dict().items()}}
@@ -108,6 +125,69 @@ def model_case(M, kw, seed, L, bidir):
     return out
 
 
+def search_case(SM, kw, seed, eval_dim=16, vocab=64):
+    """Reference SearchMamba: dynamics_rollout (values, continuation logits,
+    consistency features, parameter gradients), prime_board + eval_step chain,
+    evaluate_lines_fast with lengths, evaluate_lines and score_branch
+    (search_mamba.py:103-291), with non-zero rotation phases (see _set_phases)."""
+    torch.manual_seed(seed)
+    cfg = SM.SearchMambaConfig(vocab_size=vocab, scan_checkpoint=True, use_triton_scan=False,
+                               **kw)
+    sm = SM.SearchMamba(cfg, vocab_size=vocab, eval_dim=eval_dim)
+    _set_phases(sm.backbone.layers, seed + 100)
+    board = torch.randint(1, vocab, (2, 24))
+    moves = torch.randint(1, vocab, (2, 6))
+    lines = torch.randint(1, vocab, (5, 6))
+    lengths = torch.tensor([6, 3, 1, 5, 2])
+    out = {"kw": dict(kw), "seed": seed, "eval_dim": eval_dim, "vocab": vocab,
+           "board": board, "moves": moves, "lines": lines, "lengths": lengths,
+           "state_dict": {k: v.clone() for k, v in sm.state_dict().items()}}
+    sm.train()
+    v, c, f = sm.dynamics_rollout(board, moves)
+    (v.pow(2).mean() + 0.1 * c.pow(2).mean() + f.pow(2).mean()).backward()
+    out["rollout"] = (v.detach().clone(), c.detach().clone(), f.detach().clone())
+    out["rollout_param_grads"] = {k: p.grad.clone() for k, p in sm.named_parameters()
+                                  if p.grad is not None}
+    sm.zero_grad(set_to_none=True)
+    sm.eval()
+    with torch.no_grad():
+        _, cache = sm.prime_board(board[0])
+        vals, conts = [], []
+        for t in range(moves.shape[1]):
+            val, cont, cache = sm.eval_step(cache, int(moves[0, t]))
+            vals.append(val)
+            conts.append(cont.clone())
+        out["eval_values"] = torch.tensor(vals, dtype=torch.float64)
+        out["eval_cont"] = torch.stack(conts)
+        out["lines_fast"] = sm.evaluate_lines_fast(board[0], lines, lengths=lengths).clone()
+        out["lines_slow"] = sm.evaluate_lines(board[0], lines).clone()
+        _, bcache = sm.prime_board(board[1])
+        q, logits = sm.score_branch(bcache, moves[1])
+        out["branch"] = (float(q), logits.clone())
+    return out
+
+
+def dropin_callsite(ref):
+    """The reference's call into the fused-scan module, read from its source
+    (mamba.py:343-350): the module name, the names it imports from it, and the
+    keyword names of the scan call.  Stored as JSON so that the tests can check
+    the drop-in module against it without the reference checkout."""
+    import ast
+    src_path = os.path.join(ref, "redpanda", "engine", "mamba.py")
+    tree = ast.parse(open(src_path).read())
+    out = {"file": "redpanda/engine/mamba.py", "imports": [], "calls": []}
+    for node in ast.walk(tree):
+        if isinstance(node, ast.ImportFrom) and node.module == "triton_scan":
+            out["module"] = node.module
+            out["imports"] += [a.name for a in node.names]
+            out["import_line"] = node.lineno
+        if isinstance(node, ast.Call) and getattr(node.func, "id", None) == "triton_trapezoidal_scan":
+            out["calls"].append({"line": node.lineno, "n_positional": len(node.args),
+                                 "keywords": [k.arg for k in node.keywords]})
+    assert out["imports"] and out["calls"], "call site not found"
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("REDPANDA_REFERENCE"),
@@ -117,6 +197,7 @@ def main():
         ap.error("--ref (or REDPANDA_REFERENCE) must name a reference checkout")
     sys.path.insert(0, os.path.join(args.ref, "redpanda", "engine"))
     import mamba as M  # the reference module, read-only
+    import search_mamba as SM  # the reference module, read-only
 
     torch.set_num_threads(1)
     cases = {
@@ -142,9 +223,25 @@ def main():
                                                      n_track_state=4, mimo_p=2), 11, 33, True),
         "model_verify_notrk": model_case(M, dict(d_model=48, n_layer=2, d_state=16,
                                                  n_track_state=0, mimo_p=2), 12, 70, False),
+        # rotation phases drawn from U(-1.4, 1.4): A_imag != 0 in every rotational lane
+        "model_phase_trk": model_case(M, dict(d_model=32, n_layer=2, d_state=12,
+                                              n_track_state=4, mimo_p=2), 13, 33, False,
+                                      phases=True),
+        "model_phase_bidir": model_case(M, dict(d_model=32, n_layer=2, d_state=16,
+                                                n_track_state=4, mimo_p=2), 14, 40, True,
+                                        phases=True),
     }
     for name, c in models.items():
         torch.save(c, os.path.join(HERE, name + ".pt"))
+    searches = {
+        "search_phase": search_case(SM, dict(d_model=32, n_layer=2, d_state=12,
+                                             n_track_state=4, mimo_p=2), 20),
+    }
+    for name, c in searches.items():
+        torch.save(c, os.path.join(HERE, name + ".pt"))
+    import json
+    with open(os.path.join(HERE, "dropin_callsite.json"), "w") as f:
+        json.dump(dropin_callsite(args.ref), f, indent=1)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".pt"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -15,6 +15,8 @@ import os
 import pytest
 import torch
 
+from helpers import PARITY_TABLE
+
 from redpanda_b200.mamba import Mamba, MambaConfig
 from redpanda_b200.search_mamba import SearchMamba, SearchMambaConfig
 
@@ -55,14 +57,22 @@ def test_forward_and_param_grads_match_reference(name):
     m.train()
     y = m(c["ids"].cuda())
     y.pow(2).mean().backward()
-    assert _rel(y, c["forward"]) <= FWD_TOL
+    ey = _rel(y, c["forward"])
+    PARITY_TABLE.append((name, "forward", "model", ey, float("nan"), float("nan"),
+                         "ok" if ey <= FWD_TOL else "FAIL"))
+    assert ey <= FWD_TOL
     grads = dict(m.named_parameters())
+    worst = (0.0, "")
     for k, g in c["param_grads"].items():
         assert grads[k].grad is not None, k
-        assert _rel(grads[k].grad, g) <= GRAD_TOL, k
+        e = _rel(grads[k].grad, g)
+        worst = max(worst, (e, k))
+        assert e <= GRAD_TOL, k
+    PARITY_TABLE.append((name, "params", "model", worst[0], float("nan"), float("nan"),
+                         "ok (worst: %s)" % worst[1]))
 
 
-@pytest.mark.parametrize("name", ["model_verify_trk", "model_verify_notrk"])
+@pytest.mark.parametrize("name", ["model_verify_trk", "model_verify_notrk", "model_phase_trk"])
 def test_step_chain_and_prime_match_reference(name):
     c, m = _load(name)
     m.eval()
@@ -158,3 +168,57 @@ def test_search_mamba_dynamics_and_eval_step():
     with torch.no_grad():
         vr, _, _ = sm.dynamics_rollout(board[:1], moves[:1, :1])
     assert abs(vr.item() - val) < 1e-4
+
+
+def test_search_mamba_matches_reference_fixture():
+    """SearchMamba against the reference's own outputs (tests/golden/search_phase.pt,
+    written by the reference search_mamba.py with rotation phases drawn from
+    N(0, 2)): dynamics_rollout values / continuation logits / consistency
+    features and their parameter gradients (search_mamba.py:252-273), the
+    prime_board + eval_step chain (:162-187, :275-291), evaluate_lines_fast
+    with per-line lengths (:189-225), evaluate_lines (:124-143) and
+    score_branch (:227-250)."""
+    c = torch.load(os.path.join(GOLDEN, "search_phase.pt"))
+    cfg = SearchMambaConfig(vocab_size=c["vocab"], **c["kw"])
+    sm = SearchMamba(cfg, vocab_size=c["vocab"], eval_dim=c["eval_dim"]).cuda()
+    sm.load_state_dict(c["state_dict"])
+    board, moves = c["board"].cuda(), c["moves"].cuda()
+    sm.train()
+    v, cont, f = sm.dynamics_rollout(board, moves)
+    (v.pow(2).mean() + 0.1 * cont.pow(2).mean() + f.pow(2).mean()).backward()
+    for name, a, b in zip(("values", "cont", "feats"), (v, cont, f), c["rollout"]):
+        e = _rel(a, b)
+        PARITY_TABLE.append(("search_phase", "rollout_" + name, "model", e, float("nan"),
+                             float("nan"), "ok" if e <= FWD_TOL else "FAIL"))
+        assert e <= FWD_TOL, name
+    grads = dict(sm.named_parameters())
+    worst = (0.0, "")
+    for k, g in c["rollout_param_grads"].items():
+        assert grads[k].grad is not None, k
+        e = _rel(grads[k].grad, g)
+        worst = max(worst, (e, k))
+        assert e <= GRAD_TOL, k
+    PARITY_TABLE.append(("search_phase", "rollout_params", "model", worst[0], float("nan"),
+                         float("nan"), "ok (worst: %s)" % worst[1]))
+    sm.eval()
+    with torch.no_grad():
+        _, cache = sm.prime_board(board[0])
+        vals, conts = [], []
+        for t in range(moves.shape[1]):
+            val, cn, cache = sm.eval_step(cache, int(moves[0, t]))
+            vals.append(val)
+            conts.append(cn)
+        ev = _rel(torch.tensor(vals, dtype=torch.float64), c["eval_values"])
+        ec = _rel(torch.stack(conts), c["eval_cont"])
+        fast = sm.evaluate_lines_fast(board[0], c["lines"].cuda(), lengths=c["lengths"].cuda())
+        slow = sm.evaluate_lines(board[0], c["lines"].cuda())
+        _, bcache = sm.prime_board(board[1])
+        q, logits = sm.score_branch(bcache, moves[1])
+    ef, es = _rel(fast, c["lines_fast"]), _rel(slow, c["lines_slow"])
+    eq = abs(q - c["branch"][0]) / max(abs(c["branch"][0]), 1e-12)
+    eb = _rel(logits, c["branch"][1])
+    for out, e in (("eval_values", ev), ("eval_cont", ec), ("lines_fast", ef),
+                   ("lines_slow", es), ("branch_q", eq), ("branch_logits", eb)):
+        PARITY_TABLE.append(("search_phase", out, "model", e, float("nan"), float("nan"),
+                             "ok" if e <= STEP_TOL else "FAIL"))
+        assert e <= STEP_TOL, out
