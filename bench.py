@@ -210,6 +210,41 @@ def make_inputs(dev, seed):
     return x, ar, ai, tk
 
 
+class MultiRank:
+    """Barrier and max-over-ranks timing for the legs that every rank runs."""
+
+    def __init__(self, rank, world, local, dev):
+        self.rank, self.world, self.local, self.dev = rank, world, local, dev
+
+    def barrier(self):
+        import torch
+        import torch.distributed as dist
+        if self.world > 1:
+            dist.barrier(device_ids=[self.local])
+        torch.cuda.synchronize(self.dev)
+
+    def max(self, v):
+        import torch
+        import torch.distributed as dist
+        if self.world == 1:
+            return v
+        t = torch.tensor([v], device=self.dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(self, fn):
+        """ms of fn() on this rank's stream between barriers, max over ranks."""
+        import torch
+        stream = torch.cuda.current_stream(self.dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        self.barrier()
+        return self.max(e0.elapsed_time(e1))
+
+
 def run_m3(args):
     import torch
     import torch.distributed as dist
@@ -289,13 +324,17 @@ def run_m3(args):
     tokens = world * B_RANK * L * args.steps
     value = tokens / (ms / 1e3) / 1e9
 
-    # ---- end-to-end leg: every step copies its inputs in from pinned host memory
-    # and its parameter grads out, streaming each step's rows in NSUB sub-batches
-    # through the same public calls (ScanPlan.forward/backward on row slices):
-    # the copy of sub-batch g+1 runs on a copy stream into the second of two
-    # device buffer sets while sub-batch g computes, the parameter grads of the
-    # sub-batches are summed on the device and read back once per step.  All
-    # copies are inside the timed region (the very first one is not hidden).
+    # ---- end-to-end leg: the same calls on host buffers.  Every step copies its
+    # inputs in from pinned host memory and ALL of its results out -- y (fp32),
+    # d_delta and d_u (bf16), d_Bc and d_Cc (bf16) and the parameter grads --
+    # streaming the step's rows in NSUB sub-batches through the same public calls
+    # (ScanPlan.forward/backward on row slices).  The host->device copy of
+    # sub-batch g+1 runs on one copy stream into the second of two device buffer
+    # sets while sub-batch g computes; the device->host copies of sub-batch g's
+    # results run on a second copy stream behind its compute (PCIe is full
+    # duplex, so both directions overlap the compute and each other).  The
+    # parameter grads of the sub-batches are summed on the device and read back
+    # once per step.  All copies are inside the timed region.
     nsub = 4 if B_RANK % 4 == 0 and B_RANK >= 64 else 1
     bsub = B_RANK // nsub
     splan = plan if nsub == 1 else ScanPlan(bsub, L, D, N, N_ROT, bf, bf, S.M3_DIR_BIDIR)
@@ -305,12 +344,19 @@ def run_m3(args):
     host = {k: v.cpu().pin_memory() for k, v in x.items()}
     dbufs = [{k: torch.empty((bsub,) + tuple(v.shape[1:]), dtype=v.dtype, device=dev)
               for k, v in x.items()} for _ in range(2)]
+    outs_dev = {"y": y, "d_delta": gd, "d_u": gu, "d_Bc": gB, "d_Cc": gC}
+    outs_host = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in outs_dev.items()}
     gout = torch.empty(gflat.shape, dtype=gflat.dtype).pin_memory()
     h2d = sum(v.numel() * v.element_size() for v in host.values())
-    d2h = gout.numel() * gout.element_size()
+    d2h = sum(v.numel() * v.element_size() for v in outs_host.values()) + \
+        gout.numel() * gout.element_size()
     copy_stream = torch.cuda.Stream(dev)
+    out_stream = torch.cuda.Stream(dev)
     copied = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(nsub)]
+    returned = [torch.cuda.Event() for _ in range(nsub)]
+    returned_used = [False] * nsub
 
     def h2d_copy(gi):
         slot, j = gi & 1, gi % nsub
@@ -321,13 +367,25 @@ def run_m3(args):
                 dbufs[slot][k].copy_(host[k][j * bsub:(j + 1) * bsub], non_blocking=True)
             copied[slot].record(copy_stream)
 
+    def d2h_copy(j):
+        rows = slice(j * bsub, (j + 1) * bsub)
+        out_stream.wait_event(computed[j])
+        with torch.cuda.stream(out_stream):
+            for k, v in outs_dev.items():
+                outs_host[k][rows].copy_(v[rows], non_blocking=True)
+            returned[j].record(out_stream)
+        returned_used[j] = True
+
     def sub_step(inp, j):
         rows = slice(j * bsub, (j + 1) * bsub)
+        if returned_used[j]:
+            stream.wait_event(returned[j])   # the previous step's rows j are on the host
         splan.forward(inp["delta"], inp["u"], inp["Bc"], inp["Cc"], Ar_p, Ai_p, Tk_p, y[rows],
                       sckpt)
         splan.backward(inp["delta"], inp["u"], inp["Bc"], inp["Cc"], Ar_p, Ai_p, Tk_p,
                        inp["dy"], sckpt, gd[rows], gu[rows], gB[rows], gC[rows],
                        gsub[0], gsub[1], gsub[2], sws)
+        computed[j].record(stream)
         if j == 0:
             gflat.copy_(gsub)
         else:
@@ -338,6 +396,7 @@ def run_m3(args):
     def e2e_run(k_steps, start_event=None):
         if start_event is not None:
             copy_stream.wait_event(start_event)
+            out_stream.wait_event(start_event)
         total = k_steps * nsub
         h2d_copy(0)
         for gi in range(total):
@@ -347,8 +406,11 @@ def run_m3(args):
             stream.wait_event(copied[slot])
             sub_step(dbufs[slot], j)
             consumed[slot].record(stream)
+            d2h_copy(j)
             if j == nsub - 1:
                 gout.copy_(gflat, non_blocking=True)
+        for j in range(nsub):   # the timed region ends when every result is on the host
+            stream.wait_event(returned[j])
 
     e2e_run(max(1, args.warmup))
     barrier()
@@ -358,17 +420,30 @@ def run_m3(args):
     barrier()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1))
     e2e_value = tokens / (e2e_ms / 1e3) / 1e9
+    # the host copies hold the device results bit for bit (last step's rows)
+    e2e_check = all(torch.equal(outs_host[k], v.cpu()) for k, v in outs_dev.items())
 
-    step_info = run_step_rollout(dev, args) if (args.rollout and rank == 0) else None
-    model_info = run_model_rollout(dev, args) if (args.rollout and rank == 0) else None
+    # every rank runs the config-3 rollouts on its share of the rows and the
+    # config-4 model-level training step on its share of the global batch (in
+    # the same order, so their barriers and collectives pair up); the
+    # one-GPU configurations (the sequence-length sweep, the per-config lines)
+    # run on rank 0 alone afterwards, with no collective
+    mp = MultiRank(rank, world, local, dev)
+    step_info = run_step_rollout(dev, args, mp) if args.rollout else None
+    model_info = run_model_rollout(dev, args, mp) if args.rollout else None
+    train_info = run_model_train(dev, args, mp) if args.model_train else None
     sweep_info = run_l_sweep(dev, args) if (args.sweep and rank == 0) else None
-    train_info = run_model_train(dev, args) if (args.model_train and rank == 0) else None
+    configs_info = run_configs(dev, args, clocks) if (args.configs and rank == 0) else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
         bwd_bytes = BWD_BYTES_PER_TOKEN * B_RANK * L
         achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
         tpt = _profile_value("dram_bytes_per_token")
+        ipt = _inst_per_token().get("c2_bwd_bidir")
+        mhz = clocks.get("sm_mhz") or 1965.0
+        issue_frac = (ipt * B_RANK * L / (bwd_ms / 1e3) / (SMS * SCHEDULERS * mhz * 1e6)
+                      if ipt else None)
         fma = _profile_value("fma_pipe_active_pct")
         cpu = None
         if world == 1 and not args.no_cpu:
@@ -391,7 +466,9 @@ def run_m3(args):
                        "compute": "fp32 state/accumulation, bf16 inputs and input grads"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps,
-                    "sub_batches": nsub},
+                    "sub_batches": nsub,
+                    "returned": "y (fp32), d_delta, d_u, d_Bc, d_Cc (bf16), parameter grads",
+                    "host_results_equal_device": e2e_check},
             "gpu_launches": 4 * args.steps,
             "roofline": {"bound": "hbm", "kernel": "scan_bwd (m3_scan_bwd)",
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
@@ -399,8 +476,11 @@ def run_m3(args):
                          "traffic": (tpt * B_RANK * L) if tpt else None,
                          "algorithmic_bytes": bwd_bytes, "ms_per_launch": bwd_ms,
                          "fma_pipe_active_frac": (fma / 100.0) if fma is not None else None,
-                         "note": "compute-bound: the FP32 pipe, not HBM, limits the scan "
-                                 "(fma_pipe_active_frac from the ncu summary in profiles/)"},
+                         "issue_frac": issue_frac,
+                         "note": "compute-bound: instruction issue, not HBM, limits the scan; "
+                                 "issue_frac = the backward's warp instructions per token (ncu, "
+                                 "profiles/scan_inst_per_token.txt) x tokens / its event time / "
+                                 "(148 SMs x 4 schedulers x the sampled SM clock)"},
             "kernels_ms": {"scan_fwd_bidir": fwd_ms, "scan_bwd_bidir": bwd_ms,
                            "tokens_per_launch": B_RANK * L},
             "cpu_baseline": cpu,
@@ -412,6 +492,8 @@ def run_m3(args):
             line["model_rollout"] = model_info
         if train_info is not None:
             line["model_train"] = train_info
+        if configs_info is not None:
+            line["configs"] = configs_info
         if sweep_info is not None:
             line["l_sweep"] = {"workload": "c4 sequence-length sweep: bidirectional scan "
                                            "fwd+bwd, c2 layer shape, bf16, 1 GPU",
@@ -421,15 +503,18 @@ def run_m3(args):
         dist.destroy_process_group()
 
 
-def run_step_rollout(dev, args):
+def run_step_rollout(dev, args, mp):
     """Config 3: 12-layer lockstep rollout of B=8192 states, 32 steps, re-anchored
     every 8 steps by a full L=64 scan with return_state (recurrence kernels only;
-    per-layer token inputs are synthetic)."""
+    per-layer token inputs are synthetic).  The rows are split evenly over the
+    ranks (independent rollouts, no communication); times are max over ranks."""
     import torch
     from redpanda_b200 import scan as S
     from redpanda_b200.scan import ScanPlan, pad_params
-    layers, Bs, Ds, Ns, nr = args.rollout_layers, args.rollout_batch, 1024, 32, 24
-    g = torch.Generator(dev).manual_seed(7)
+    layers, Ds, Ns, nr = args.rollout_layers, 1024, 32, 24
+    Bg = args.rollout_batch
+    Bs = max(1, Bg // mp.world)
+    g = torch.Generator(dev).manual_seed(7 + mp.rank)
     params = []
     for _ in range(layers):
         ar = -torch.exp(torch.randn(Ds, nr, device=dev, generator=g) * 0.5)
@@ -485,42 +570,189 @@ def run_step_rollout(dev, args):
                 tok["Bc"].data_ptr(), tok["Cc"].data_ptr(), ar.data_ptr(), ai.data_ptr(),
                 tk.data_ptr(), ystep.data_ptr(), sh))
 
+    def steps32():
+        for _ in range(32):
+            one_step()
+
+    def fsteps32():
+        for s_ in range(32):
+            one_step_factored(s_ & 1)
+
     rollout()
-    for s_ in range(4):
-        one_step_factored(s_ & 1)
-    torch.cuda.synchronize(dev)
-    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    e[0].record(stream)
-    rollout()
-    e[1].record(stream)
-    for _ in range(32):
-        one_step()
-    e[2].record(stream)
-    for s_ in range(32):
-        one_step_factored(s_ & 1)
-    e[3].record(stream)
-    torch.cuda.synchronize(dev)
-    total_ms = e[0].elapsed_time(e[1])
-    steps_ms = e[1].elapsed_time(e[2])
-    fsteps_ms = e[2].elapsed_time(e[3])
+    fsteps32()
+    total_ms = mp.timed(rollout)
+    steps_ms = mp.timed(steps32)
+    fsteps_ms = mp.timed(fsteps32)
     peak, kind = _peaks()
-    state_bytes = layers * Bs * Ds * Ns * 16
+    rows = Bs * mp.world
+    state_bytes = layers * Bs * Ds * Ns * 16          # per rank and node-step batch
+    gbs = state_bytes / (steps_ms / 32 / 1e3) / 1e9
+    fgbs = state_bytes / 2 / (fsteps_ms / 32 / 1e3) / 1e9
     return {
-        "workload": f"c3: {layers} layers, B={Bs}, D=1024, N=32 (24 rot + 8 track), 32 steps, "
-                    "re-anchor every 8 steps by an L=64 scan with return_state",
-        "node_steps_per_s": Bs * 32 / (total_ms / 1e3),
+        "workload": f"c3: {layers} layers, B={rows} ({Bs} per GPU), D=1024, N=32 (24 rot + 8 "
+                    "track), 32 steps, re-anchor every 8 steps by an L=64 scan with return_state",
+        "n_gpus": mp.world,
+        "node_steps_per_s": rows * 32 / (total_ms / 1e3),
         "ms_per_rollout": total_ms,
-        "step_only_node_steps_per_s": Bs * 32 / (steps_ms / 1e3),
+        "step_only_node_steps_per_s": rows * 32 / (steps_ms / 1e3),
         "step_ms_per_node_step_batch": steps_ms / 32,
-        "step_hbm_gbs": state_bytes / (steps_ms / 32 / 1e3) / 1e9,
-        "step_hbm_frac": state_bytes / (steps_ms / 32 / 1e3) / 1e9 / peak,
-        "step_algorithmic_bytes": state_bytes,
-        "factored_step_node_steps_per_s": Bs * 32 / (fsteps_ms / 1e3),
-        "factored_step_hbm_gbs": state_bytes / 2 / (fsteps_ms / 32 / 1e3) / 1e9,
-        "factored_step_hbm_frac": state_bytes / 2 / (fsteps_ms / 32 / 1e3) / 1e9 / peak,
+        "step_hbm_gbs_per_gpu": gbs,
+        "step_hbm_frac": gbs / peak,
+        "step_algorithmic_bytes_per_gpu": state_bytes,
+        "factored_step_node_steps_per_s": rows * 32 / (fsteps_ms / 1e3),
+        "factored_step_hbm_gbs_per_gpu": fgbs,
+        "factored_step_hbm_frac": fgbs / peak,
         "gpu_launches": 32 * layers + 4 * layers,
-        "note": "recurrence kernels only; the projection GEMMs of Mamba.step are not included",
+        "note": "recurrence kernels only; the projection GEMMs of Mamba.step are not included; "
+                "times are max over ranks",
     }
+
+
+# Issue roofline of the scan kernels: 148 SMs x 4 warp schedulers, one warp
+# instruction per scheduler and clock.  The per-token warp-instruction counts
+# come from the committed ncu summary (smsp__inst_executed.sum of each kernel
+# variant / tokens of its launch).
+SMS, SCHEDULERS = 148, 4
+
+
+def _inst_per_token():
+    out = {}
+    path = os.path.join(REPO, "profiles", "scan_inst_per_token.txt")
+    try:
+        for line in open(path):
+            if ":" in line and not line.startswith("#"):
+                k, v = line.split(":", 1)
+                out[k.strip()] = float(v)
+    except OSError:
+        pass
+    return out
+
+
+def run_configs(dev, args, clocks):
+    """One line per BASELINE configuration on one GPU (device-resident inputs,
+    CUDA events, a few warm-up launches):
+      c0         causal fwd+bwd, fp32, B=8, L=64, D=256, N=16 (12 rot + 4 track),
+                 with the reference algorithm on the host cores on the same
+                 inputs (config 0 is the reference's CPU-runnable case)
+      c1_fwd     bidirectional forward only (inference, no checkpoints), bf16,
+                 B=1024, L=64, D=1536, N=32 (16 rot + 16 track)
+      c2_bidir   bidirectional fwd (with checkpoints) + bwd + reductions, c1 shape
+      c2_causal  causal fwd + bwd + reductions, c1 shape
+    Each line: tokens/s, ms per step, the HBM fraction of its algorithmic bytes
+    and, where the ncu instruction counts are committed, the fraction of the
+    issue roofline (148 SMs x 4 schedulers x the median SM clock sampled in
+    the timed region of the headline)."""
+    import torch
+    from redpanda_b200 import scan as S
+    from redpanda_b200.scan import ScanPlan, pad_params
+    from redpanda_b200.synthetic import ScanShape, make_scan_inputs
+    peak, _ = _peaks()
+    ipt = _inst_per_token()
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    issue_peak = SMS * SCHEDULERS * mhz * 1e6
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+
+    def bench(fn, reps):
+        fn()
+        fn()
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    def setup(sh, dtype, direction, seed):
+        inp = make_scan_inputs(sh, seed=seed, dtype=dtype)
+        g = {k: (None if v is None else v.to(dev)) for k, v in inp.items()}
+        D_, N_ = sh.d_inner, sh.d_state
+        P = [t.contiguous() for t in pad_params(g["A_real"], g["A_imag"], g["track"], sh.n_rot,
+                                                N_, D_, dev)]
+        plan = ScanPlan(sh.batch, sh.seqlen, D_, N_, sh.n_rot, dtype, dtype, direction)
+        bufs = {"y": torch.empty(sh.batch, sh.seqlen, D_, device=dev),
+                "ckpt": torch.empty(max(1, plan.ckpt_floats()), device=dev),
+                "ws": torch.empty(max(1, plan.workspace_bytes()), device=dev, dtype=torch.uint8),
+                "gd": torch.empty_like(g["delta"]), "gu": torch.empty_like(g["u"]),
+                "gB": torch.empty_like(g["Bc"]), "gC": torch.empty_like(g["Cc"]),
+                "gA": torch.empty(3, D_, N_, device=dev), "dy": g["dy"].to(dtype).contiguous()}
+        return inp, g, P, plan, bufs
+
+    def fwd_bwd(g, P, plan, b):
+        ck = b["ckpt"] if plan.ckpt_floats() else None
+        plan.forward(g["delta"], g["u"], g["Bc"], g["Cc"], *P, b["y"], ck)
+        plan.backward(g["delta"], g["u"], g["Bc"], g["Cc"], *P, b["dy"], ck, b["gd"], b["gu"],
+                      b["gB"], b["gC"], b["gA"][0], b["gA"][1], b["gA"][2], b["ws"])
+
+    def line(name, sh, ms, bytes_per_token, kernels, extra=None):
+        tok = sh.batch * sh.seqlen
+        gbs = bytes_per_token * tok / (ms / 1e3) / 1e9
+        d = {"tokens_per_s": tok / (ms / 1e3), "ms_per_step": ms, "tokens_per_step": tok,
+             "hbm_gbs": gbs, "hbm_frac": gbs / peak, "algorithmic_bytes_per_token": bytes_per_token}
+        if all(k in ipt for k in kernels):
+            inst = sum(ipt[k] for k in kernels) * tok
+            d["issue_frac"] = inst / (ms / 1e3) / issue_peak
+            d["warp_inst_per_token"] = sum(ipt[k] for k in kernels)
+        if extra:
+            d.update(extra)
+        out[name] = d
+
+    # c0: the reference's CPU-runnable case, fp32
+    sh0 = ScanShape(8, 64, 256, 16, 4, 4)
+    inp0, g0, P0, plan0, b0 = setup(sh0, torch.float32, S.M3_DIR_FWD, 0)
+    ms0 = bench(lambda: fwd_bwd(g0, P0, plan0, b0), 200)
+    c0_bytes = (2 * 4 * 256 + 2 * 4 * 16 + 4 * 256) + (3 * 4 * 256 + 2 * 4 * 16 + 2 * 4 * 256
+                                                      + 2 * 4 * 16)
+    cpu0 = None
+    if not args.no_cpu:
+        import oracle as O
+        torch.set_num_threads(os.cpu_count() or 1)
+        def ref0():
+            O.scan_with_grads(inp0["delta"], inp0["u"], inp0["Bc"], inp0["Cc"], inp0["A_real"],
+                              inp0["A_imag"], inp0["track"], inp0["dy"])
+        ref0()
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 3.0:
+            ref0()
+            reps += 1
+        el = time.perf_counter() - t0
+        cpu0 = {"tokens_per_s": sh0.batch * sh0.seqlen * reps / el, "cores": os.cpu_count(),
+                "kind": "port", "sample": f"the full config-0 batch, {reps} fwd+bwd in {el:.1f} s"}
+    line("c0", sh0, ms0, c0_bytes, ["c0_fwd", "c0_bwd"],
+         {"workload": "c0: causal scan fwd+bwd, fp32, B=8, L=64, D=256, N=16 (12 rot + 4 "
+                      "track); launch-bound (512 tokens)",
+          "reference_cpu": cpu0})
+    del g0, b0
+
+    cb = args.config_batch
+    sh1 = ScanShape(cb, 64, 1536, 32, 16, 4)
+    bf = torch.bfloat16
+    # c1: bidirectional forward, inference (no checkpoints)
+    _, g1, P1, plan1, b1 = setup(sh1, bf, S.M3_DIR_BIDIR, 1)
+    ms1 = bench(lambda: plan1.forward(g1["delta"], g1["u"], g1["Bc"], g1["Cc"], *P1, b1["y"]), 10)
+    line("c1_fwd", sh1, ms1, FWD_BYTES_PER_TOKEN, ["c1_fwd_bidir"],
+         {"workload": f"c1: bidirectional forward scan (inference), bf16 inputs, fp32 state and "
+                      f"y, B={cb}, L=64, D=1536, N=32 (16 rot + 16 track)"})
+    # c2: fwd (with checkpoints) + bwd, bidirectional and causal
+    ms2 = bench(lambda: fwd_bwd(g1, P1, plan1, b1), 5)
+    line("c2_bidir", sh1, ms2, FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN,
+         ["c2_fwd_bidir", "c2_bwd_bidir"],
+         {"workload": f"c2: bidirectional scan fwd + analytic bwd + reductions, bf16, B={cb}"})
+    del g1, b1
+    torch.cuda.empty_cache()
+    _, g2, P2, plan2, b2 = setup(sh1, bf, S.M3_DIR_FWD, 2)
+    ms3 = bench(lambda: fwd_bwd(g2, P2, plan2, b2), 5)
+    line("c2_causal", sh1, ms3, FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN,
+         ["c2_fwd_causal", "c2_bwd_causal"],
+         {"workload": f"c2: causal scan fwd + analytic bwd + reductions, bf16, B={cb}"})
+    del g2, b2
+    torch.cuda.empty_cache()
+    out["issue_peak_warp_inst_per_s"] = issue_peak
+    out["sm_mhz_assumed"] = mhz
+    return out
 
 
 def run_l_sweep(dev, args):
@@ -575,68 +807,86 @@ def run_l_sweep(dev, args):
     return out
 
 
-def run_model_train(dev, args):
+def run_model_train(dev, args, mp):
     """Config 4 at model level: the 16-layer bidirectional Eval-Mamba stack of
     config 1 (d_model=768, d_inner=1536, d_state=32 with 16 tracking lanes,
-    mimo_p=4, vocab 8192, the reference initialisation with a random seed), one
-    training step = forward, loss y.pow(2).mean() (the reference's verify-gate
-    loss), backward through the kernels (scan, prologue) and torch (GEMMs), and
-    a fused AdamW step; micro-batch of ``args.train_batch`` rows of L=64 random
-    token ids.  GEMMs in TF32, scan state and gradients in fp32."""
+    mimo_p=4, vocab 8192, the reference initialisation), one training step =
+    forward, loss y.pow(2).mean() (the reference's verify-gate loss), backward
+    through the kernels (scan, prologue) and torch (GEMMs), and a fused AdamW
+    step.  The global batch (``args.train_global`` rows of L=64 random token
+    ids) is split evenly over the ranks and run in micro-batches of
+    ``args.train_batch`` rows with gradient accumulation; on more than one GPU
+    every parameter gradient (the scan parameters A, theta, dt bias and BCNorm
+    weights among them) is all-reduced over NCCL in buckets started from the
+    backward of the last micro-batch, overlapping the rest of it.  GEMMs in
+    TF32, scan state and gradients in fp32."""
     import torch
+    from redpanda_b200.distributed import OverlappedGradAllReducer
     from redpanda_b200.mamba import Mamba, MambaConfig
-    Bs = args.train_batch
+    mb = args.train_batch
+    per_rank = max(mb, args.train_global // mp.world)
+    accum = max(1, per_rank // mb)
     old_tf32 = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = True
     try:
-        torch.manual_seed(17)
+        torch.manual_seed(17)   # the same initial weights on every rank
         cfg = MambaConfig(d_model=768, n_layer=16, d_state=32, n_track_state=16, mimo_p=4,
                           vocab_size=8192, bidirectional=True)
         model = Mamba(cfg).to(dev).train()
         opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
-        g = torch.Generator(dev).manual_seed(19)
-        ids = torch.randint(0, 8192, (Bs, 64), device=dev, generator=g)
+        red = OverlappedGradAllReducer(model) if mp.world > 1 else None
+        g = torch.Generator(dev).manual_seed(19 + mp.rank)
+        ids = [torch.randint(0, 8192, (mb, 64), device=dev, generator=g) for _ in range(accum)]
+        last = {}
 
         def step():
             opt.zero_grad(set_to_none=True)
-            loss = model(ids).pow(2).mean()
-            loss.backward()
+            for i in range(accum):
+                if red is not None and i == accum - 1:
+                    red.arm()
+                loss = model(ids[i]).pow(2).mean() / accum
+                loss.backward()
+            if red is not None:
+                red.finish()
             opt.step()
-            return loss
-        for _ in range(2):
-            step()
-        torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n = 5
-        e0.record()
-        for _ in range(n):
-            loss = step()
-        e1.record()
-        torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / n
+            last["loss"] = loss
+
+        def steps(n):
+            def run():
+                for _ in range(n):
+                    step()
+            return run
+        steps(2)()
+        n = 3
+        ms = mp.timed(steps(n)) / n
+        rows = per_rank * mp.world
         return {"workload": f"c4 model level: 16-layer bidirectional Mamba (d_model=768, "
-                            f"d_inner=1536, d_state=32 with 16 tracking lanes, mimo_p=4), "
-                            f"B={Bs} x L=64 per step, fwd + bwd + fused AdamW",
-                "ms_per_step": ms, "tokens_per_s": Bs * 64 / (ms / 1e3),
-                "loss": float(loss.item()),
+                            f"d_inner=1536, d_state=32 with 16 tracking lanes, mimo_p=4), global "
+                            f"B={rows} x L=64 per step ({per_rank} rows per GPU in {accum} "
+                            f"micro-batches of {mb}), fwd + bwd + fused AdamW",
+                "n_gpus": mp.world, "ms_per_step": ms, "tokens_per_s": rows * 64 / (ms / 1e3),
+                "loss": float(last["loss"].item()) * accum,
+                "allreduce": ("every parameter gradient, NCCL, buckets of ~8 MB started during "
+                              "the last micro-batch's backward" if mp.world > 1 else "none (1 GPU)"),
                 "precision": "TF32 projections, fp32 scan state, activations and gradients"}
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old_tf32
 
 
-def run_model_rollout(dev, args):
+def run_model_rollout(dev, args, mp):
     """Config 3 at model level: a 12-layer Search-Mamba-shaped ``Mamba``
     (d_model=512, d_inner=1024, d_state=32 with 8 tracking lanes, mimo_p=2,
-    vocab 8192, the reference initialisation with a random seed), B rollout
-    rows advanced 32 steps by the fused step layer (embedding, RMSNorm, cuBLAS
-    projections, one launch for softplus/BCNorm/MIMO fold, one for the
-    recurrence with the gated output, out_proj fused with the residual add),
-    re-anchored every 8 steps by ``prime_cache`` over a fresh L=64 token
-    sequence (scan with return_state).  Token ids are uniform over the
-    8192-move space.  GEMMs run in TF32; state and recurrence in fp32."""
+    vocab 8192, the reference initialisation), B rollout rows (split evenly
+    over the ranks, no communication) advanced 32 steps by the fused step layer
+    (embedding, RMSNorm, cuBLAS projections, one launch for softplus/BCNorm/MIMO
+    fold, one for the recurrence with the gated output, out_proj fused with the
+    residual add), re-anchored every 8 steps by ``prime_cache`` over a fresh
+    L=64 token sequence (scan with return_state).  Token ids are uniform over
+    the 8192-move space.  GEMMs run in TF32; state and recurrence in fp32."""
     import torch
     from redpanda_b200.mamba import Mamba, MambaConfig
-    layers, Bs = args.rollout_layers, args.rollout_batch
+    layers = args.rollout_layers
+    Bs = max(1, args.rollout_batch // mp.world)
     old_tf32 = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = True
     try:
@@ -644,46 +894,43 @@ def run_model_rollout(dev, args):
         cfg = MambaConfig(d_model=512, n_layer=layers, d_state=32, n_track_state=8, mimo_p=2,
                           vocab_size=8192)
         model = Mamba(cfg).to(dev).eval()
-        g = torch.Generator(dev).manual_seed(13)
+        g = torch.Generator(dev).manual_seed(13 + mp.rank)
         boards = [torch.randint(0, 8192, (Bs, 64), device=dev, generator=g) for _ in range(4)]
         moves = torch.randint(0, 8192, (32, Bs), device=dev, generator=g)
         stream = torch.cuda.current_stream(dev)
+        ev = []
 
-        def rollout(ev=None):
+        def rollout(record=False):
             cache = None
             for s_ in range(32):
                 if s_ % 8 == 0:
-                    if ev is not None:
-                        ev.append(("anchor0", torch.cuda.Event(enable_timing=True)))
-                        ev[-1][1].record(stream)
+                    if record:
+                        ev.append(torch.cuda.Event(enable_timing=True))
+                        ev[-1].record(stream)
                     _, cache = model.prime_cache(boards[s_ // 8])
-                    if ev is not None:
-                        ev.append(("anchor1", torch.cuda.Event(enable_timing=True)))
-                        ev[-1][1].record(stream)
+                    if record:
+                        ev.append(torch.cuda.Event(enable_timing=True))
+                        ev[-1].record(stream)
                 x, cache = model.step_fused_(token_id=moves[s_], cache=cache)
             return x
 
         with torch.no_grad():
             rollout()
-            torch.cuda.synchronize(dev)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ev = []
-            e0.record(stream)
-            rollout(ev)
-            e1.record(stream)
-            torch.cuda.synchronize(dev)
-        total = e0.elapsed_time(e1)
-        anchor = sum(ev[i][1].elapsed_time(ev[i + 1][1]) for i in range(0, len(ev), 2))
+            total = mp.timed(lambda: rollout(record=True))
+        anchor = mp.max(sum(ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2)))
         steps_ms = total - anchor
+        rows = Bs * mp.world
         return {
             "workload": f"c3 model level: {layers}-layer Mamba (d_model=512, d_inner=1024, "
-                        f"d_state=32 with 8 tracking lanes, mimo_p=2, vocab 8192), B={Bs}, "
-                        "32 lockstep steps, prime_cache re-anchor over L=64 every 8 steps",
-            "node_steps_per_s": Bs * 32 / (total / 1e3),
+                        f"d_state=32 with 8 tracking lanes, mimo_p=2, vocab 8192), B={rows} "
+                        f"({Bs} per GPU), 32 lockstep steps, prime_cache re-anchor over L=64 "
+                        "every 8 steps",
+            "n_gpus": mp.world,
+            "node_steps_per_s": rows * 32 / (total / 1e3),
             "ms_per_rollout": total,
             "anchor_ms": anchor,
             "step_ms_per_node_step_batch": steps_ms / 32,
-            "step_only_node_steps_per_s": Bs * 32 / (steps_ms / 1e3),
+            "step_only_node_steps_per_s": rows * 32 / (steps_ms / 1e3),
             "precision": "TF32 projections, fp32 state and recurrence",
             "state": "reference (h, dBu) cache pair",
         }
@@ -703,10 +950,17 @@ def main():
                     help="skip the config-3 step rollout measurement")
     ap.add_argument("--no-model-train", dest="model_train", action="store_false",
                     help="skip the config-4 model-level training step")
-    ap.add_argument("--train-batch", type=int, default=256)
+    ap.add_argument("--train-batch", type=int, default=256,
+                    help="micro-batch rows of the config-4 model-level training step")
+    ap.add_argument("--train-global", type=int, default=2048,
+                    help="global rows per training step, split over the GPUs")
     ap.add_argument("--no-sweep", dest="sweep", action="store_false",
                     help="skip the config-4 sequence-length sweep")
     ap.add_argument("--sweep-batch", type=int, default=256)
+    ap.add_argument("--no-configs", dest="configs", action="store_false",
+                    help="skip the per-configuration lines (c0, c1 forward, c2 causal/bidir)")
+    ap.add_argument("--config-batch", type=int, default=1024,
+                    help="rows of the c1/c2 lines (default 1024, the configs' batch)")
     ap.add_argument("--rollout-layers", type=int, default=12,
                     help="layers of the config-3 rollout (default 12; fewer for profiler captures)")
     ap.add_argument("--rollout-batch", type=int, default=8192,

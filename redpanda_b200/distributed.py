@@ -81,6 +81,105 @@ class ScanGradAllReducer:
         return self.bucket
 
 
+class OverlappedGradAllReducer:
+    """Bucketed all-reduce of parameter gradients, launched during the backward.
+
+    Parameters are grouped into buckets of about ``bucket_bytes`` in reverse
+    registration order (roughly the order the backward produces their
+    gradients: last layer first).  A post-accumulate-grad hook on every
+    parameter counts down its bucket; when the bucket's last gradient has
+    landed, the bucket is packed and its all-reduce is started asynchronously
+    (NCCL runs it on its own stream behind the compute already queued), so it
+    overlaps the rest of the backward.  :meth:`finish` waits for the buckets,
+    averages and unpacks them into ``.grad``; buckets that were never completed
+    (a parameter without a gradient this step) are reduced there, with zeros
+    standing in for missing gradients, so every rank issues the same
+    collectives in the same order.
+
+    With gradient accumulation, call :meth:`arm` before the backward of the
+    last micro-batch only; the hooks do nothing while disarmed.
+    """
+
+    def __init__(self, module=None, params=None, bucket_bytes=8 << 20, group=None,
+                 average=True):
+        plist = list(params) if params is not None else \
+            [p for p in module.parameters() if p.requires_grad]
+        if not plist:
+            raise ValueError("no parameters to reduce")
+        self.group = group
+        self.average = average
+        self.buckets = []
+        cur, size = [], 0
+        for p in reversed(plist):
+            cur.append(p)
+            size += p.numel() * 4
+            if size >= bucket_bytes:
+                self.buckets.append(cur)
+                cur, size = [], 0
+        if cur:
+            self.buckets.append(cur)
+        self.bucket_of = {}
+        for bi, b in enumerate(self.buckets):
+            for p in b:
+                self.bucket_of[p] = bi
+                p.register_post_accumulate_grad_hook(self._hook)
+        self.armed = False
+        self._reset()
+
+    def _reset(self):
+        self.pending = [len(b) for b in self.buckets]
+        self.started = {}
+
+    def arm(self):
+        self._reset()
+        self.armed = True
+
+    def _pack(self, bi):
+        return torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1)
+                          .to(torch.float32) for p in self.buckets[bi]])
+
+    def _start(self, bi):
+        flat = self._pack(bi)
+        work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        self.started[bi] = (flat, work)
+
+    def _hook(self, p):
+        if not self.armed:
+            return
+        bi = self.bucket_of[p]
+        self.pending[bi] -= 1
+        # buckets start in index order, so every rank issues the same sequence
+        # of collectives even when its backward finishes buckets in another order
+        if self.pending[bi] == 0:
+            nxt = len(self.started)
+            while nxt < len(self.buckets) and self.pending[nxt] == 0:
+                self._start(nxt)
+                nxt += 1
+
+    def finish(self):
+        """Wait for every bucket, average, and write the results into ``.grad``."""
+        for bi in range(len(self.buckets)):
+            if bi not in self.started:
+                self._start(bi)
+        world = dist.get_world_size(self.group)
+        for bi, b in enumerate(self.buckets):
+            flat, work = self.started[bi]
+            work.wait()
+            if self.average:
+                flat.div_(world)
+            off = 0
+            for p in b:
+                n = p.numel()
+                g = flat[off:off + n].view_as(p).to(p.dtype)
+                if p.grad is None:
+                    p.grad = g.clone()
+                else:
+                    p.grad.copy_(g)
+                off += n
+        self.armed = False
+        self._reset()
+
+
 def init_from_env(backend=None, timeout_s=300):
     """init_process_group from torchrun's environment with a bounded timeout.
 

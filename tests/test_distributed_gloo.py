@@ -17,7 +17,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from redpanda_b200.distributed import ScanGradAllReducer, SCAN_PARAM_SUFFIXES, shard_rows
+from redpanda_b200.distributed import (OverlappedGradAllReducer, ScanGradAllReducer,
+                                       SCAN_PARAM_SUFFIXES, shard_rows)
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
@@ -78,6 +79,52 @@ def test_two_rank_allreduce_equals_full_batch():
     assert set(r0) == set(r1) and len(r0) == 2 * 6   # 2 layers x 6 scan parameters
     for k in r0:
         assert torch.equal(r0[k], r1[k]), k          # every rank holds the same result
+        assert torch.allclose(r0[k], full[k].grad, rtol=1e-5, atol=1e-8), k
+
+
+def _overlap_worker(rank, world, port, out_dir):
+    """Two micro-batches per rank; the bucketed all-reduce of every parameter
+    gradient is armed for the second backward only (gradient accumulation)."""
+    from oracle import model_oracle as MO
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    torch.manual_seed(0)
+    c = torch.load(os.path.join(GOLDEN, "model_verify_trk.pt"))
+    ids = torch.randint(0, 64, (4, 17))
+    a, b = shard_rows(ids.shape[0], rank, world)
+    cfg = MO.OracleConfig(vocab_size=64, bidirectional=False, **c["kw"])
+    p = {k: v.clone().requires_grad_(v.is_floating_point()) for k, v in c["state_dict"].items()}
+    red = OverlappedGradAllReducer(params=[v for v in p.values() if v.requires_grad],
+                                   bucket_bytes=16 << 10)
+    assert len(red.buckets) > 2
+    rows = list(range(a, b))
+    for i, r in enumerate(rows):
+        if i == len(rows) - 1:
+            red.arm()
+        y = MO.model_forward(p, cfg, ids[r:r + 1])
+        (y.pow(2).mean(dim=(1, 2)).sum() / len(rows)).backward()
+    red.finish()
+    torch.save({k: v.grad for k, v in p.items() if v.requires_grad},
+               os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_overlapped_bucketed_allreduce_with_accumulation_equals_full_batch():
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_overlap_worker, args=(2, port, d), nprocs=2, join=True,
+                           start_method="spawn")
+        r0 = torch.load(os.path.join(d, "rank0.pt"))
+        r1 = torch.load(os.path.join(d, "rank1.pt"))
+    torch.manual_seed(0)
+    c = torch.load(os.path.join(GOLDEN, "model_verify_trk.pt"))
+    ids = torch.randint(0, 64, (4, 17))
+    full = _model_grads(ids, c["state_dict"], c["kw"])
+    assert set(r0) == set(r1) and len(r0) > 12
+    for k in r0:
+        assert torch.equal(r0[k], r1[k]), k
         assert torch.allclose(r0[k], full[k].grad, rtol=1e-5, atol=1e-8), k
 
 
