@@ -99,24 +99,12 @@ struct BwdCfg {
   // pass stages the first pass's ddelta/du rows of the chunk.
   static constexpr size_t braw_floats = BULK ? 2 * 2 * (size_t)KC * NP : 0;  // [2][B|C][KC][NP]
   static constexpr size_t scr_floats = BULK ? (size_t)KC * DT * 2 : 0;       // [KC][DT][2]
-  static constexpr size_t base_bytes =
+  static constexpr size_t smem_bytes =
       3 * 2 * raw_bytes                       // delta, u, dy (HBM dtype), double-buffered
       + 2 * (size_t)DT * NP * 4               // checkpoint tile, double-buffered
       + 2 * 2 * (size_t)KC * NP * 4           // B, C (fp32), double-buffered
       + red_floats * 4 + gs_floats * 4
-      + braw_floats * 4 + scr_floats * 4;
-  // dA/dtrack totals: each thread's fp32 register sums of one KC-step chunk
-  // are folded into its own float64 totals here once per work item, so the
-  // parameter gradients carry the rounding of an 8- or 16-term fp32 sum
-  // instead of one sequential fp32 sum over every (row, step) of the CTA
-  // (tens of thousands of terms at large batch).  [pair][thread] double2
-  // layout (conflict-free 16-byte accesses).  Tilings whose shared memory
-  // cannot hold it keep the fp32 register sums.
-  static constexpr int NPAIR = NDP * (2 * (R > 0 ? R : 1) + (T > 0 ? T : 1));
-  static constexpr size_t acc_bytes = (size_t)NPAIR * NTH * 16;
-  static constexpr bool F64ACC = base_bytes + acc_bytes + 32 <= 227 * 1024;
-  static constexpr size_t smem_bytes =
-      base_bytes + (F64ACC ? acc_bytes : 0)
+      + braw_floats * 4 + scr_floats * 4
       + 32;                                   // TMEM address slot, 3 mbarriers (BULK)
 };
 
@@ -184,9 +172,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   float* s_gs = s_red + CF::red_floats;                              // [FL][ND][2][SG]
   float* s_braw = s_gs + CF::gs_floats;                              // [2][B|C][KC][NP] (BULK)
   float* s_scr = s_braw + CF::braw_floats;                           // [KC][DT][2] (BULK)
-  double2* s_acc = reinterpret_cast<double2*>(s_scr + CF::scr_floats);   // [NPAIR][NTH] (F64ACC)
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(
-      reinterpret_cast<unsigned char*>(s_acc) + (CF::F64ACC ? CF::acc_bytes : 0));
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_scr + CF::scr_floats);
   uint64_t* s_bar = reinterpret_cast<uint64_t*>(s_tmem) + 1;          // [3] (BULK)
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
@@ -257,32 +243,6 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
     for (int j = 0; j < RR; ++j) { gAr[k][j] = f2(0.f); gAi[k][j] = f2(0.f); }
 #pragma unroll
     for (int j = 0; j < TT; ++j) gTk[k][j] = f2(0.f);
-  }
-
-  // the thread's accumulator pairs in a fixed order: gAr, gAi, gTk
-  auto acc_pair = [&](int i) -> float2& {
-    constexpr int NR2 = NDP * RR;
-    if (i < NR2) return gAr[i / RR][i % RR];
-    if (i < 2 * NR2) return gAi[(i - NR2) / RR][(i - NR2) % RR];
-    return gTk[(i - 2 * NR2) / TT][(i - 2 * NR2) % TT];
-  };
-  // add the fp32 chunk sums to the float64 totals and restart them from zero
-  auto fold_acc = [&]() {
-    if constexpr (CF::F64ACC) {
-#pragma unroll
-      for (int i = 0; i < CF::NPAIR; ++i) {
-        float2& a = acc_pair(i);
-        double2 t = s_acc[i * NTH + tid];
-        t.x += (double)a.x;
-        t.y += (double)a.y;
-        s_acc[i * NTH + tid] = t;
-        a = f2(0.f);
-      }
-    }
-  };
-  if constexpr (CF::F64ACC) {
-#pragma unroll
-    for (int i = 0; i < CF::NPAIR; ++i) s_acc[i * NTH + tid] = make_double2(0.0, 0.0);
   }
 
   const int cta = gt * p.Bg + bg;
@@ -903,7 +863,6 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
       }
     }
     if (fail) break;
-    fold_acc();
     if constexpr (!BULK) {
       if (more) store_bc(buf ^ 1);
     }
@@ -911,14 +870,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   cp_async_wait0();
   if (fail && tid == 0) set_err(p.err, M3_ERR_DEVICE);
 
-  // dA partial of this batch group (F64ACC: the float64 totals, rounded once)
-  if constexpr (CF::F64ACC) {
-#pragma unroll
-    for (int i = 0; i < CF::NPAIR; ++i) {
-      const double2 t = s_acc[i * NTH + tid];
-      acc_pair(i) = make_float2((float)t.x, (float)t.y);
-    }
-  }
+  // dA partial of this batch group
 #pragma unroll
   for (int k = 0; k < ND; ++k) {
     const int d = dbase + k;
