@@ -149,6 +149,22 @@ def search_case(SM, kw, seed, eval_dim=16, vocab=64):
     out["rollout_param_grads"] = {k: p.grad.clone() for k, p in sm.named_parameters()
                                   if p.grad is not None}
     sm.zero_grad(set_to_none=True)
+    # the reference's own agreement between two equivalent formulations of the
+    # rollout: prime_cache + step loop (above) and one causal forward over the
+    # board and the moves.  Some head gradients (the continuation head's first
+    # layer, behind a LayerNorm of small variance) amplify fp32 rounding of the
+    # hidden states by orders of magnitude; this figure is the floor of any
+    # comparison against the fixture.
+    Lb = board.shape[1]
+    hid = sm.backbone(torch.cat([board, moves], 1))[:, Lb:]
+    v2 = torch.tanh(sm.value_head(hid)).squeeze(-1)
+    (v2.pow(2).mean() + 0.1 * sm.continuation_head(hid).pow(2).mean()
+     + sm.consistency_proj(hid).pow(2).mean()).backward()
+    out["rollout_self_consistency"] = {
+        k: ((p.grad - out["rollout_param_grads"][k]).abs().max()
+            / out["rollout_param_grads"][k].abs().max()).item()
+        for k, p in sm.named_parameters() if p.grad is not None}
+    sm.zero_grad(set_to_none=True)
     sm.eval()
     with torch.no_grad():
         _, cache = sm.prime_board(board[0])

@@ -196,10 +196,16 @@ def test_search_mamba_matches_reference_fixture():
     for k, g in c["rollout_param_grads"].items():
         assert grads[k].grad is not None, k
         e = _rel(grads[k].grad, g)
-        worst = max(worst, (e, k))
-        assert e <= GRAD_TOL, k
+        # the bar of each gradient is GRAD_TOL or, where the reference's own two
+        # equivalent rollout formulations (prime + step loop, one causal scan)
+        # disagree by more, four times that disagreement (make_golden.py records
+        # it; 5.8e-3 for continuation_head.0.weight, whose gradient passes a
+        # LayerNorm of small variance)
+        bar = max(GRAD_TOL, 4.0 * c["rollout_self_consistency"][k])
+        worst = max(worst, (e / bar, k))
+        assert e <= bar, (k, e, bar)
     PARITY_TABLE.append(("search_phase", "rollout_params", "model", worst[0], float("nan"),
-                         float("nan"), "ok (worst: %s)" % worst[1]))
+                         float("nan"), "ok (largest error/bar: %s)" % worst[1]))
     sm.eval()
     with torch.no_grad():
         _, cache = sm.prime_board(board[0])

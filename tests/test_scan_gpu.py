@@ -134,6 +134,19 @@ def test_scan_parity(name, shape, dtype, direction):
     assert not failures, failures
 
 
+# Wide-regime (case, gradient key) -> (error vs float64 measured on a B200, bound).
+# dA_real of the config-1 lane layout at D=128, bf16 inputs, causal: the
+# kernel's fp32 value misses 1e-6 of float64 while the reference's own fp32
+# path is further from float64 still (2.4e-6 and 1.1e-4 in the two regimes);
+# folding the chunk sums into float64 totals left it unchanged, so it is the
+# fp32 rounding of the per-cell terms, not the summation order.  The test
+# also requires the kernel to stay at least as close to float64 as the
+# fp32 reference.
+WIDE_GRAD_ALLOW = {
+    ("wide_k_mid_N32T16_dir0_bf16", "A_real"): (1.67e-6, 3e-6),
+    ("wide_mixed_N32T16_dir0_bf16", "A_real"): (2.20e-6, 4e-6),
+}
+
 WIDE_CASES = [
     # regime, shape, input dtype, direction
     (r, sh, dt, d)
@@ -187,10 +200,15 @@ def test_scan_parity_wide_gate_arguments(regime, shape, dtype, direction):
             if not ok:
                 failures.append((k, "bf16 ulp"))
             continue
-        PARITY_TABLE.append((name, "d" + k, "fp32", rel_err(g[k], g32[k]), e64, r64,
-                             "ok" if e64 <= GRAD_TOL else "FAIL"))
-        if e64 > GRAD_TOL:
+        if e64 <= GRAD_TOL:
+            verdict = "ok"
+        elif ((name, k) in WIDE_GRAD_ALLOW and e64 <= WIDE_GRAD_ALLOW[(name, k)][1]
+              and e64 <= r64):
+            verdict = "allow-listed"
+        else:
+            verdict = "FAIL"
             failures.append((k, e64))
+        PARITY_TABLE.append((name, "d" + k, "fp32", rel_err(g[k], g32[k]), e64, r64, verdict))
     assert not failures, (failures, xmax, kmax, frac_slow)
     assert S.device_error() == 0
 
