@@ -434,6 +434,7 @@ def run_m3(args):
     train_info = run_model_train(dev, args, mp) if args.model_train else None
     sweep_info = run_l_sweep(dev, args) if (args.sweep and rank == 0) else None
     configs_info = run_configs(dev, args, clocks) if (args.configs and rank == 0) else None
+    eval_info = run_model_eval(dev, args) if (args.model_train and rank == 0) else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -494,6 +495,8 @@ def run_m3(args):
             line["model_train"] = train_info
         if configs_info is not None:
             line["configs"] = configs_info
+        if eval_info is not None:
+            line["model_eval"] = eval_info
         if sweep_info is not None:
             line["l_sweep"] = {"workload": "c4 sequence-length sweep: bidirectional scan "
                                            "fwd+bwd, c2 layer shape, bf16, 1 GPU",
@@ -844,7 +847,9 @@ def run_model_train(dev, args, mp):
             for i in range(accum):
                 if red is not None and i == accum - 1:
                     red.arm()
-                loss = model(ids[i]).pow(2).mean() / accum
+                # bf16 mixed precision, as the reference trains (train.py:268)
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    loss = model(ids[i]).float().pow(2).mean() / accum
                 loss.backward()
             if red is not None:
                 red.finish()
@@ -868,9 +873,51 @@ def run_model_train(dev, args, mp):
                 "loss": float(last["loss"].item()) * accum,
                 "allreduce": ("every parameter gradient, NCCL, buckets of ~8 MB started during "
                               "the last micro-batch's backward" if mp.world > 1 else "none (1 GPU)"),
-                "precision": "TF32 projections, fp32 scan state, activations and gradients"}
+                "precision": "torch.autocast bf16 (the reference's mixed precision): bf16 "
+                             "projections on the tensor cores, the kernels' bf16 configuration "
+                             "(bf16 delta/u/Bc/Cc and y, fp32 state and accumulation), fp32 "
+                             "parameters, residual stream and optimizer"}
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old_tf32
+
+
+def run_model_eval(dev, args):
+    """The Eval-Mamba stack forward in bf16 (model.py:110-132 / mamba.py:231-267 at
+    config 1): the 16-layer bidirectional Mamba of config 4 (d_model=768,
+    d_inner=1536, d_state=32 with 16 tracking lanes, mimo_p=4), inference
+    (no grad) under torch.autocast bf16, B=``args.config_batch`` rows x L=64:
+    bf16 projections, softplus/BCNorm/MIMO fold in one launch, the fused
+    bidirectional scan writing bf16 y, the gate (y + 2uD)*silu(z) in bf16, the
+    bf16 out_proj.  One GPU."""
+    import torch
+    from redpanda_b200.mamba import Mamba, MambaConfig
+    Bs = args.config_batch
+    torch.manual_seed(23)
+    cfg = MambaConfig(d_model=768, n_layer=16, d_state=32, n_track_state=16, mimo_p=4,
+                      vocab_size=8192, bidirectional=True)
+    model = Mamba(cfg).to(dev).eval()
+    g = torch.Generator(dev).manual_seed(29)
+    ids = torch.randint(0, 8192, (Bs, 64), device=dev, generator=g)
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        for _ in range(2):
+            model(ids)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 5
+        e0.record(stream)
+        for _ in range(n):
+            out = model(ids)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / n
+    del model, out
+    torch.cuda.empty_cache()
+    return {"workload": f"c1 model level: 16-layer bidirectional Mamba forward (d_model=768, "
+                        f"d_inner=1536, d_state=32 with 16 tracking lanes, mimo_p=4), inference, "
+                        f"B={Bs} x L=64",
+            "ms_per_forward": ms, "tokens_per_s": Bs * 64 / (ms / 1e3),
+            "precision": "torch.autocast bf16; scan state and accumulation fp32"}
 
 
 def run_model_rollout(dev, args, mp):

@@ -116,6 +116,42 @@ M3_API int m3_scan_fwd(const m3_scan_desc* desc,
                 float* y, float* ckpt, float* h_last, float* dbu_last,
                 void* stream);
 
+/* m3_scan_fwd with the element type of y chosen by dtype_y (M3_F32 or
+ * M3_BF16); the state and every accumulation stay fp32 and only the stored y
+ * is rounded.  Replaces the same _TrapezoidalScanFn.forward
+ * (triton_scan.py:248-281) for a bf16 layer (the reference's autocast
+ * training, train.py:268, and the bf16 Eval-Mamba forward of model.py:110-132).
+ * With M3_DIR_BIDIR and a bf16 y the first direction's partial is stored in
+ * bf16 and the second adds to it in fp32 before rounding again (at most one
+ * bf16 ulp more than a single rounding). */
+M3_API int m3_scan_fwd_typed(const m3_scan_desc* desc,
+                const void* delta, const void* u, const void* Bc, const void* Cc,
+                const float* A_real_p, const float* A_imag_p, const float* track_p,
+                void* y, int32_t dtype_y, float* ckpt, float* h_last, float* dbu_last,
+                void* stream);
+
+/* Forward scan with the layer's prologue fused into its staging
+ * (mamba.py:284-301 and 336-337, the projections' softplus, BCNorm and MIMO
+ * fold that otherwise run before the scan).  bf16 inputs only (the
+ * config-1/2 element types; desc->dtype_du must be M3_BF16, dtype_bc is
+ * ignored):
+ *   dt      (B, L, D) bf16: dt_proj output including its bias, before softplus
+ *   xbc     (B*L, ld_x) bf16: x_proj output rows; B_raw = columns
+ *           [off_b, off_b + N*mimo_p), C_raw = [off_c, off_c + N*mimo_p)
+ *   wb, wc  (N*mimo_p,) float32 BCNorm weights, or both NULL (use_bcnorm=False)
+ *   u       (B, L, D) bf16
+ * The scan sees delta = bf16(softplus(dt)) and Bc, Cc = bf16 of the fold of
+ * BCNorm(B_raw), BCNorm(C_raw) (computed in fp32 as m3_step_inputs does), so
+ * y and ckpt equal those of m3_step_inputs + casts to bf16 + m3_scan_fwd_typed
+ * bit for bit.  Shapes the staging cannot take (column offsets off 8-element
+ * boundaries, N*mimo_p above 256, channel counts off the tile) return
+ * M3_ERR_UNSUPPORTED: run the unfused pair then. */
+M3_API int m3_scan_fwd_fused(const m3_scan_desc* desc, int32_t mimo_p, const void* dt,
+                const void* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
+                const float* wb, const float* wc, float eps, const void* u,
+                const float* A_real_p, const float* A_imag_p, const float* track_p,
+                void* y, int32_t dtype_y, float* ckpt, void* stream);
+
 /* Workspace bytes m3_scan_bwd needs on the current device. */
 M3_API size_t m3_scan_bwd_workspace_bytes(const m3_scan_desc* desc);
 
@@ -222,6 +258,14 @@ M3_API int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu,
 M3_API int m3_gate(int64_t rows, int32_t d_inner, const float* y, const void* u,
             int32_t dtype_u, const float* z, int64_t ld_z, const float* d_skip, float coef,
             float* out, void* stream);
+
+/* m3_gate with an element type per operand (M3_F32 or M3_BF16): y, u, z and
+ * out of a bf16 layer (mamba.py:262-265 under the reference's autocast,
+ * train.py:268; the bf16 Eval-Mamba forward, model.py:110-132).  Arithmetic is
+ * fp32; out is rounded once.  out may equal y only when dtype_out == dtype_y. */
+M3_API int m3_gate_typed(int64_t rows, int32_t d_inner, const void* y, int32_t dtype_y,
+            const void* u, int32_t dtype_u, const void* z, int32_t dtype_z, int64_t ld_z,
+            const float* d_skip, float coef, void* out, int32_t dtype_out, void* stream);
 
 /* Size of the scratch buffer built into the library for m3_scan_bwd_noalloc. */
 #define M3_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)

@@ -40,6 +40,10 @@ SIGNATURES = {
     "m3_version": (ctypes.c_int, []),
     "m3_scan_ckpt_floats": (_Z, [_D]),
     "m3_scan_fwd": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "m3_scan_fwd_typed": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P,
+                                         _P]),
+    "m3_scan_fwd_fused": (ctypes.c_int, [_D, _I, _P, _P, ctypes.c_int64, _I, _I, _P, _P,
+                                         ctypes.c_float, _P, _P, _P, _P, _P, _I, _P, _P]),
     "m3_scan_bwd_workspace_bytes": (_Z, [_D]),
     "m3_scan_bwd": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P,
                                    _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
@@ -56,6 +60,8 @@ SIGNATURES = {
                                           _P, _P, _Z, _P]),
     "m3_gate": (ctypes.c_int, [ctypes.c_int64, _I, _P, _P, _I, _P, ctypes.c_int64, _P,
                                ctypes.c_float, _P, _P]),
+    "m3_gate_typed": (ctypes.c_int, [ctypes.c_int64, _I, _P, _I, _P, _I, _P, _I,
+                                     ctypes.c_int64, _P, ctypes.c_float, _P, _I, _P]),
     "m3_step_gated": (ctypes.c_int, [_S, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                      ctypes.c_int64, _P, _P, _P]),
 }

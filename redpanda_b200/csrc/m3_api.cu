@@ -146,7 +146,7 @@ const char* m3_strerror(int code) {
   }
 }
 
-int m3_version(void) { return (1 << 16) | 0; }
+int m3_version(void) { return (1 << 16) | 1; }
 
 size_t m3_scan_ckpt_floats(const m3_scan_desc* desc) {
   Tile t;
@@ -158,6 +158,73 @@ int m3_scan_fwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
                 const void* Cc, const float* A_real_p, const float* A_imag_p,
                 const float* track_p, float* y, float* ckpt, float* h_last, float* dbu_last,
                 void* stream) {
+  return m3_scan_fwd_typed(desc, delta, u, Bc, Cc, A_real_p, A_imag_p, track_p, y, M3_F32, ckpt,
+                           h_last, dbu_last, stream);
+}
+
+static int fwd_common(const m3_scan_desc* desc, const void* delta, const void* u,
+                      const void* Bc, const void* Cc, const float* A_real_p,
+                      const float* A_imag_p, const float* track_p, void* y, int32_t dtype_y,
+                      float* ckpt, float* h_last, float* dbu_last, const void* pro_args,
+                      void* stream);
+
+namespace {
+// the fused prologue's inputs (m3_scan_fwd_fused / m3_scan_bwd_fused)
+struct ProArgs {
+  int32_t mimo_p; const void* xbc; int64_t ld_x; int32_t off_b, off_c;
+  const float* wb; const float* wc; float eps;
+};
+
+// Shapes the fused-prologue kernels take: bf16 delta/u rows and x_proj rows
+// that TMA can stage (16-byte aligned bases, strides and box rows; column
+// offsets on 8-element boundaries), whole channel tiles of at most 128
+// channels, and raw B/C rows that fit the staging buffer of the padded lanes.
+int check_pro(const m3_scan_desc* d, const Tile& t, const ProArgs& a, const void* dt,
+              const void* u, int dt_tile) {
+  const int64_t np = (int64_t)d->d_state * a.mimo_p;
+  if (a.mimo_p < 1 || a.off_b < 0 || a.off_c < 0 || a.off_b + np > a.ld_x ||
+      a.off_c + np > a.ld_x || !(a.eps >= 0.f))
+    return M3_ERR_SHAPE;
+  if (!a.xbc || ((a.wb == nullptr) != (a.wc == nullptr))) return M3_ERR_NULL;
+  if (d->dtype_du != M3_BF16) return M3_ERR_DTYPE;
+  if (!aligned(dt, 16) || !aligned(u, 16) || !aligned(a.xbc, 16) ||
+      (a.wb && (!aligned(a.wb, 4) || !aligned(a.wc, 4))))
+    return M3_ERR_ALIGN;
+  if ((d->d_inner % dt_tile) != 0 || dt_tile > 128 || (d->d_inner % 8) != 0 ||
+      ((a.ld_x * 2) % 16) != 0 || (a.off_b % 8) != 0 || (a.off_c % 8) != 0 ||
+      (np % 8) != 0 || np > 256 || np > 4 * t.np() || getenv("M3_NO_BULK") != nullptr)
+    return M3_ERR_UNSUPPORTED;
+  return M3_OK;
+}
+}  // namespace
+
+int m3_scan_fwd_typed(const m3_scan_desc* desc, const void* delta, const void* u,
+                      const void* Bc, const void* Cc, const float* A_real_p,
+                      const float* A_imag_p, const float* track_p, void* y, int32_t dtype_y,
+                      float* ckpt, float* h_last, float* dbu_last, void* stream) {
+  return fwd_common(desc, delta, u, Bc, Cc, A_real_p, A_imag_p, track_p, y, dtype_y, ckpt,
+                    h_last, dbu_last, nullptr, stream);
+}
+
+int m3_scan_fwd_fused(const m3_scan_desc* desc, int32_t mimo_p, const void* dt,
+                      const void* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
+                      const float* wb, const float* wc, float eps, const void* u,
+                      const float* A_real_p, const float* A_imag_p, const float* track_p,
+                      void* y, int32_t dtype_y, float* ckpt, void* stream) {
+  const ProArgs a{mimo_p, xbc, ld_x, off_b, off_c, wb, wc, eps};
+  // Bc/Cc are not read: pass xbc so that the shared checks see valid pointers
+  return fwd_common(desc, dt, u, xbc, xbc, A_real_p, A_imag_p, track_p, y, dtype_y, ckpt,
+                    nullptr, nullptr, &a, stream);
+}
+
+static int fwd_common(const m3_scan_desc* desc, const void* delta, const void* u,
+                      const void* Bc, const void* Cc, const float* A_real_p,
+                      const float* A_imag_p, const float* track_p, void* y, int32_t dtype_y,
+                      float* ckpt, float* h_last, float* dbu_last, const void* pro_args,
+                      void* stream) {
+  const ProArgs* pro = static_cast<const ProArgs*>(pro_args);
+  if (dtype_y != M3_F32 && dtype_y != M3_BF16) return M3_ERR_DTYPE;
+  const int esy = dtype_y == M3_BF16 ? 2 : 4;
   Tile t;
   int rc = check_scan_desc(desc, &t);
   if (rc != M3_OK) return rc;
@@ -166,16 +233,18 @@ int m3_scan_fwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   if (h_last && desc->direction == M3_DIR_BIDIR) return M3_ERR_SHAPE;
   const int esd = dsize(desc->dtype_du), esb = dsize(desc->dtype_bc);
   if (!aligned(delta, esd) || !aligned(u, esd) || !aligned(Bc, esb) || !aligned(Cc, esb) ||
-      !aligned(A_real_p, 4) || !aligned(A_imag_p, 4) || !aligned(track_p, 4) || !aligned(y, 4) ||
-      (ckpt && !aligned(ckpt, 16)) || (h_last && (!aligned(h_last, 4) || !aligned(dbu_last, 4))))
+      !aligned(A_real_p, 4) || !aligned(A_imag_p, 4) || !aligned(track_p, 4) ||
+      !aligned(y, esy) || (ckpt && !aligned(ckpt, 16)) ||
+      (h_last && (!aligned(h_last, 4) || !aligned(dbu_last, 4))))
     return M3_ERR_ALIGN;
+  if (pro && (rc = check_pro(desc, t, *pro, delta, u, t.dt())) != M3_OK) return rc;
   if ((rc = check_device()) != M3_OK) return rc;
 
   FwdParams p;
   memset(&p, 0, sizeof(p));
   p.delta = delta; p.u = u; p.Bc = Bc; p.Cc = Cc;
   p.Ar = A_real_p; p.Ai = A_imag_p; p.Tk = track_p;
-  p.y = y; p.ckpt = ckpt_floats(desc, t) ? ckpt : nullptr;
+  p.y = y; p.y_bf16 = dtype_y == M3_BF16; p.ckpt = ckpt_floats(desc, t) ? ckpt : nullptr;
   p.h_last = h_last; p.dbu_last = dbu_last;
   p.B = desc->batch; p.L = desc->seqlen; p.D = desc->d_inner; p.N = desc->d_state;
   p.NR = desc->n_rot; p.NT = desc->d_state - desc->n_rot;
@@ -190,7 +259,12 @@ int m3_scan_fwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   p.bulk = (desc->d_inner % t.dt()) == 0 && ((desc->d_inner * esd) % 16) == 0 &&
            ((desc->d_state * esb) % 16) == 0 && aligned(delta, 16) && aligned(u, 16) &&
            aligned(Bc, 16) && aligned(Cc, 16) && aligned(y, 16) &&
-           getenv("M3_NO_BULK") == nullptr;
+           ((desc->d_inner * esy) % 16) == 0 && getenv("M3_NO_BULK") == nullptr;
+  if (pro) {
+    if (!p.bulk) return M3_ERR_UNSUPPORTED;
+    p.pro = 1; p.xbc = pro->xbc; p.ld_x = pro->ld_x; p.off_b = pro->off_b;
+    p.off_c = pro->off_c; p.P = pro->mimo_p; p.wb = pro->wb; p.wc = pro->wc; p.eps = pro->eps;
+  }
   p.err = device_err_ptr();
   cudaError_t e = launch_scan_fwd(t, p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
@@ -430,18 +504,32 @@ int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p, const float* dt
 int m3_gate(int64_t rows, int32_t d_inner, const float* y, const void* u, int32_t dtype_u,
             const float* z, int64_t ld_z, const float* d_skip, float coef, float* out,
             void* stream) {
+  return m3_gate_typed(rows, d_inner, y, M3_F32, u, dtype_u, z, M3_F32, ld_z, d_skip, coef,
+                       out, M3_F32, stream);
+}
+
+int m3_gate_typed(int64_t rows, int32_t d_inner, const void* y, int32_t dtype_y, const void* u,
+                  int32_t dtype_u, const void* z, int32_t dtype_z, int64_t ld_z,
+                  const float* d_skip, float coef, void* out, int32_t dtype_out, void* stream) {
   if (rows < 1 || d_inner < 1 || ld_z < d_inner) return M3_ERR_SHAPE;
-  if (!dtype_ok(dtype_u)) return M3_ERR_DTYPE;
+  if (!dtype_ok(dtype_y) || !dtype_ok(dtype_u) || !dtype_ok(dtype_z) || !dtype_ok(dtype_out))
+    return M3_ERR_DTYPE;
   if (!y || !u || !z || !d_skip || !out) return M3_ERR_NULL;
-  if (!aligned(y, 4) || !aligned(u, dsize(dtype_u)) || !aligned(z, 4) || !aligned(d_skip, 4) ||
-      !aligned(out, 4))
+  if (!aligned(y, dsize(dtype_y)) || !aligned(u, dsize(dtype_u)) || !aligned(z, dsize(dtype_z)) ||
+      !aligned(d_skip, 4) || !aligned(out, dsize(dtype_out)))
     return M3_ERR_ALIGN;
+  // out may alias y only when both have the same element type (in place)
+  if (out == y && dtype_out != dtype_y) return M3_ERR_ALIAS;
   int rc = check_device();
   if (rc != M3_OK) return rc;
   GateParams p;
   memset(&p, 0, sizeof(p));
-  p.y = y; p.u = u; p.u_bf16 = dtype_u == M3_BF16; p.z = z; p.ld_z = ld_z;
-  p.d_skip = d_skip; p.coef = coef; p.out = out; p.rows = rows; p.D = d_inner;
+  p.y = y; p.y_bf16 = dtype_y == M3_BF16;
+  p.u = u; p.u_bf16 = dtype_u == M3_BF16;
+  p.z = z; p.z_bf16 = dtype_z == M3_BF16; p.ld_z = ld_z;
+  p.d_skip = d_skip; p.coef = coef;
+  p.out = out; p.out_bf16 = dtype_out == M3_BF16;
+  p.rows = rows; p.D = d_inner;
   cudaError_t e = launch_gate(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }

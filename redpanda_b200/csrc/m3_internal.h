@@ -37,7 +37,8 @@ bool select_tile(int n_rot, int n_track, Tile* out);
 struct FwdParams {
   const void* delta; const void* u; const void* Bc; const void* Cc;
   const float* Ar; const float* Ai; const float* Tk;
-  float* y; float* ckpt; float* h_last; float* dbu_last;
+  void* y; float* ckpt; float* h_last; float* dbu_last;
+  int y_bf16;      // y is bf16 (else fp32); fp32 state and accumulation either way
   int B, L, D, N, NR, NT;
   int dt_du, dt_bc;
   int direction;   // 0 fwd, 1 rev, 2 bidir
@@ -45,6 +46,13 @@ struct FwdParams {
   int cki, nck;    // checkpoint interval (8 or 16 steps) and checkpoints per direction
   int async_ok;    // cp.async staging allowed (alignment checked on the host)
   int bulk;        // every staged row is a 16-byte aligned bulk copy
+  // fused prologue (pro != 0, bf16 bulk path only): delta points at dt, the
+  // dt_proj output before softplus, and Bc/Cc are unused; B_raw and C_raw are
+  // columns [off_b, off_b + N*P) and [off_c, off_c + N*P) of the bf16 rows xbc
+  // (B*L, ld_x); delta = bf16(softplus(dt)), Bc/Cc = bf16(MIMO fold of BCNorm)
+  int pro;
+  const void* xbc; long long ld_x; int off_b, off_c, P;
+  const float* wb; const float* wc; float eps;
   int* err;
 };
 
@@ -111,13 +119,14 @@ struct InputsParams {
 cudaError_t launch_step_inputs(const InputsParams& p, cudaStream_t s);
 
 struct InputsBwdParams {
-  const float* dt; long long ld_dt;
-  const float* xbc; long long ld_x;
+  const float* dt; long long ld_dt;       // nullptr: skip the softplus part
+  const void* xbc; long long ld_x;        // float, or bf16 when x_bf16
+  int x_bf16;
   int off_b, off_c;
   const float* wb; const float* wc;
   float eps;
   const float* g_delta; const float* g_Bc; const float* g_Cc;   // (rows, D), (rows, N) x2
-  float* d_dt; float* d_xbc;                                    // (rows, D), (rows, ld_x)
+  float* d_dt; void* d_xbc;                                     // (rows, D), (rows, ld_x)
   float* d_wb; float* d_wc;                                     // (N*P,) each
   float* part_w;                                                // [ctas][2][N*P]
   long long rows; int D, N, P;
@@ -126,10 +135,11 @@ int step_inputs_bwd_ctas(long long rows);
 cudaError_t launch_step_inputs_bwd(const InputsBwdParams& p, cudaStream_t s);
 
 struct GateParams {
-  const float* y; const void* u; int u_bf16;
-  const float* z; long long ld_z;
+  const void* y; int y_bf16;
+  const void* u; int u_bf16;
+  const void* z; int z_bf16; long long ld_z;
   const float* d_skip; float coef;
-  float* out;
+  void* out; int out_bf16;
   long long rows; int D;
 };
 cudaError_t launch_gate(const GateParams& p, cudaStream_t s);

@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "m3_internal.h"
+#include "m3_prologue.cuh"
 
 namespace m3 {
 namespace {
@@ -28,49 +29,23 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) step_inputs_kernel(const Inp
   const int r0 = blockIdx.x * kRowsPerCta;
   const int rows = min(kRowsPerCta, p.B - r0);
   if (warp >= rows) return;
-  // softplus of this warp's row
-  {
-    const size_t b = (size_t)(r0 + warp);
+  const size_t b = (size_t)(r0 + warp);
+  {   // softplus of this warp's row
     const float* dt = p.dt + b * p.ld_dt;
     float* delta = p.delta + b * p.D;
-    for (int d = lane; d < p.D; d += 32) {
-      const float x = dt[d];
-      delta[d] = x > 20.f ? x : log1pf(expf(x));
-    }
+    for (int d = lane; d < p.D; d += 32) delta[d] = softplus20(dt[d]);
   }
-  const size_t b = (size_t)(r0 + warp);
   const int np = p.N * p.P;
   const float* xb = p.xbc + b * p.ld_x + p.off_b;
   const float* xc = p.xbc + b * p.ld_x + p.off_c;
-  float rb = 1.f, rc = 1.f;
-  if (p.wb != nullptr) {
-    float sb = 0.f, sc = 0.f;
-    for (int k = lane; k < np; k += 32) {
-      sb = __fmaf_rn(xb[k], xb[k], sb);
-      sc = __fmaf_rn(xc[k], xc[k], sc);
-    }
-#pragma unroll
-    for (int m = 16; m > 0; m >>= 1) {
-      sb = __fadd_rn(sb, __shfl_xor_sync(0xffffffffu, sb, m));
-      sc = __fadd_rn(sc, __shfl_xor_sync(0xffffffffu, sc, m));
-    }
-    rb = rsqrtf(__fadd_rn(__fdiv_rn(sb, (float)np), p.eps));
-    rc = rsqrtf(__fadd_rn(__fdiv_rn(sc, (float)np), p.eps));
-  }
+  const bool has_w = p.wb != nullptr;
+  auto ldb = [&](int k) { return xb[k]; };
+  auto ldc = [&](int k) { return xc[k]; };
+  const float rb = bcnorm_scale(ldb, np, p.eps, has_w, lane);
+  const float rc = bcnorm_scale(ldc, np, p.eps, has_w, lane);
   for (int n = lane; n < p.N; n += 32) {
-    float ab = 0.f, ac = 0.f;
-    for (int k = 0; k < p.P; ++k) {
-      const int i = n * p.P + k;
-      float vb = xb[i], vc = xc[i];
-      if (p.wb != nullptr) {
-        vb = __fmul_rn(__fmul_rn(vb, rb), p.wb[i]);
-        vc = __fmul_rn(__fmul_rn(vc, rc), p.wc[i]);
-      }
-      ab = k == 0 ? vb : __fadd_rn(ab, vb);
-      ac = k == 0 ? vc : __fadd_rn(ac, vc);
-    }
-    p.Bc[b * p.N + n] = ab;
-    p.Cc[b * p.N + n] = ac;
+    p.Bc[b * p.N + n] = bcnorm_fold(ldb, n, p.P, rb, p.wb);
+    p.Cc[b * p.N + n] = bcnorm_fold(ldc, n, p.P, rc, p.wc);
   }
 }
 
@@ -89,13 +64,13 @@ __global__ void gate_kernel(const GateParams p) {
   for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < p.rows;
        r += warps) {
     const size_t row = (size_t)r * p.D;
-    const float* z = p.z + (size_t)r * p.ld_z;
     if constexpr (VEC) {
-      const float4* y4 = reinterpret_cast<const float4*>(p.y + row);
+      const float* z = static_cast<const float*>(p.z) + (size_t)r * p.ld_z;
+      const float4* y4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.y) + row);
       const float4* u4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.u) + row);
       const float4* z4 = reinterpret_cast<const float4*>(z);
       const float4* d4 = reinterpret_cast<const float4*>(p.d_skip);
-      float4* o4 = reinterpret_cast<float4*>(p.out + row);
+      float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row);
       for (int c = lane; c < p.D / 4; c += 32) {
         const float4 y = y4[c], u = u4[c], zz = z4[c], ds = d4[c];
         o4[c] = make_float4(gate_one(y.x, u.x, zz.x, ds.x, p.coef),
@@ -104,10 +79,17 @@ __global__ void gate_kernel(const GateParams p) {
                             gate_one(y.w, u.w, zz.w, ds.w, p.coef));
       }
     } else {
+      // element types per operand: fp32 or bf16 (a bf16 layer's y, z and out)
+      auto ld = [](const void* base, size_t i, int bf) {
+        return bf ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
+                  : static_cast<const float*>(base)[i];
+      };
+      const size_t zrow = (size_t)r * p.ld_z;
       for (int d = lane; d < p.D; d += 32) {
-        const float u = p.u_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.u)[row + d])
-                                 : static_cast<const float*>(p.u)[row + d];
-        p.out[row + d] = gate_one(p.y[row + d], u, z[d], p.d_skip[d], p.coef);
+        const float v = gate_one(ld(p.y, row + d, p.y_bf16), ld(p.u, row + d, p.u_bf16),
+                                 ld(p.z, zrow + d, p.z_bf16), p.d_skip[d], p.coef);
+        if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[row + d] = __float2bfloat16_rn(v);
+        else static_cast<float*>(p.out)[row + d] = v;
       }
     }
   }
@@ -123,38 +105,49 @@ __global__ void gate_kernel(const GateParams p) {
 // One warp per row (grid-stride); the weight gradients accumulate per warp in
 // shared memory, are summed over the CTA's warps in warp order into one partial
 // per CTA, and reduce_w_kernel sums the partials in CTA order: deterministic.
+// XT: element type of the x_proj rows xbc and their gradient d_xbc (float, or
+// __nv_bfloat16 for the fused bf16 scan, whose rows are bf16); every
+// computation is fp32 and d_xbc is rounded once.  p.dt == nullptr skips the
+// softplus part (the fused scan backward applies it in its own flush).
+template <class XT>
+__device__ __forceinline__ float ldx(const XT* x, size_t i) {
+  if constexpr (sizeof(XT) == 2) return __bfloat162float(x[i]);
+  else return x[i];
+}
+template <class XT>
+__device__ __forceinline__ void stx(XT* x, size_t i, float v) {
+  if constexpr (sizeof(XT) == 2) x[i] = __float2bfloat16_rn(v);
+  else x[i] = v;
+}
+
+template <class XT>
 __global__ void __launch_bounds__(256) step_inputs_bwd_kernel(const InputsBwdParams p) {
   extern __shared__ float s_w[];             // [8 warps][2][np]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int np = p.N * p.P;
+  const XT* xbc = static_cast<const XT*>(p.xbc);
+  XT* d_xbc = static_cast<XT*>(p.d_xbc);
   float* wacc = s_w + (size_t)warp * 2 * np;
   for (int i = lane; i < 2 * np; i += 32) wacc[i] = 0.f;
   const long long nwarps = (long long)gridDim.x * 8;
   for (long long r = (long long)blockIdx.x * 8 + warp; r < p.rows; r += nwarps) {
     const size_t b = (size_t)r;
-    for (int d = lane; d < p.D; d += 32) {
-      const float x = p.dt[b * p.ld_dt + d];
-      const float g = p.g_delta[b * p.D + d];
-      float v = g;
-      if (!(x > 20.f)) {
-        const float e = expf(x);
-        v = __fdiv_rn(__fmul_rn(g, e), __fadd_rn(e, 1.f));
-      }
-      p.d_dt[b * p.D + d] = v;
+    if (p.dt != nullptr) {
+      for (int d = lane; d < p.D; d += 32)
+        p.d_dt[b * p.D + d] = softplus20_grad(p.g_delta[b * p.D + d], p.dt[b * p.ld_dt + d]);
     }
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
-      const float* x = p.xbc + b * p.ld_x + (which ? p.off_c : p.off_b);
+      const size_t x0 = b * p.ld_x + (which ? p.off_c : p.off_b);
       const float* gbc = (which ? p.g_Cc : p.g_Bc) + b * p.N;
       const float* w = which ? p.wc : p.wb;
-      float* dx = p.d_xbc + b * p.ld_x + (which ? p.off_c : p.off_b);
       if (w == nullptr) {   // no BCNorm: the fold is a plain sum
-        for (int i = lane; i < np; i += 32) dx[i] = gbc[i / p.P];
+        for (int i = lane; i < np; i += 32) stx(d_xbc, x0 + i, gbc[i / p.P]);
         continue;
       }
       float ss = 0.f, sg = 0.f;
       for (int i = lane; i < np; i += 32) {
-        const float xi = x[i];
+        const float xi = ldx(xbc, x0 + i);
         ss = __fmaf_rn(xi, xi, ss);
         sg = __fmaf_rn(__fmul_rn(gbc[i / p.P], w[i]), xi, sg);
       }
@@ -168,8 +161,8 @@ __global__ void __launch_bounds__(256) step_inputs_bwd_kernel(const InputsBwdPar
       const float cs = __fmul_rn(coef, sg);
       float* wa = wacc + which * np;
       for (int i = lane; i < np; i += 32) {
-        const float xi = x[i], gy = gbc[i / p.P];
-        dx[i] = __fsub_rn(__fmul_rn(rs, __fmul_rn(gy, w[i])), __fmul_rn(cs, xi));
+        const float xi = ldx(xbc, x0 + i), gy = gbc[i / p.P];
+        stx(d_xbc, x0 + i, __fsub_rn(__fmul_rn(rs, __fmul_rn(gy, w[i])), __fmul_rn(cs, xi)));
         wa[i] = __fmaf_rn(gy, __fmul_rn(xi, rs), wa[i]);
       }
     }
@@ -208,12 +201,13 @@ cudaError_t launch_step_inputs_bwd(const InputsBwdParams& p, cudaStream_t s) {
   const int grid = step_inputs_bwd_ctas(p.rows);
   const int np = p.N * p.P;
   const size_t smem = (size_t)8 * 2 * np * sizeof(float);
+  auto kern = p.x_bf16 ? step_inputs_bwd_kernel<__nv_bfloat16> : step_inputs_bwd_kernel<float>;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(step_inputs_bwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
     if (e != cudaSuccess) return e;
   }
-  step_inputs_bwd_kernel<<<grid, 256, smem, s>>>(p);
+  kern<<<grid, 256, smem, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.wb == nullptr) return e;
   reduce_w_kernel<<<(2 * np + 255) / 256, 256, 0, s>>>(p.part_w, grid, np, p.d_wb, p.d_wc);
@@ -227,7 +221,8 @@ cudaError_t launch_gate(const GateParams& p, cudaStream_t s) {
   long long grid = (p.rows + 7) / 8;   // 8 warps (rows) per CTA
   if (grid > (long long)sms * 16) grid = (long long)sms * 16;
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  const bool vec = !p.u_bf16 && (p.D % 4) == 0 && (p.ld_z % 4) == 0 && a16(p.y) && a16(p.u) &&
+  const bool vec = !p.u_bf16 && !p.y_bf16 && !p.z_bf16 && !p.out_bf16 && (p.D % 4) == 0 &&
+                   (p.ld_z % 4) == 0 && a16(p.y) && a16(p.u) &&
                    a16(p.z) && a16(p.d_skip) && a16(p.out);
   if (vec) gate_kernel<true><<<(unsigned)grid, 256, 0, s>>>(p);
   else gate_kernel<false><<<(unsigned)grid, 256, 0, s>>>(p);

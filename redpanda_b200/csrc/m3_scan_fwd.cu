@@ -13,7 +13,12 @@ cudaError_t launch_fwd_bulk_bf16_nostate(const Tile& t, const FwdParams& p, cuda
 cudaError_t launch_fwd_bulk_f32_state(const Tile& t, const FwdParams& p, cudaStream_t s);
 cudaError_t launch_fwd_bulk_f32_nostate(const Tile& t, const FwdParams& p, cudaStream_t s);
 
+cudaError_t launch_fwd_bulk_pro(const Tile& t, const FwdParams& p, cudaStream_t s);
+
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
+  // the fused prologue exists only as a bf16 bulk-staged kernel (the C ABI
+  // checks eligibility first; no fallback)
+  if (p.pro) return launch_fwd_bulk_pro(t, p, s);
   if (p.bulk) {
     const bool bf = p.dt_du == M3_BF16, st = p.h_last != nullptr;
     const cudaError_t e =
@@ -23,8 +28,8 @@ cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
   }
 #define M3_X(r, tt, nd, ndb, nthb, gs)                                              \
   if (t.R == r && t.T == tt && t.ND == nd)                                        \
-    return p.h_last ? fwd::launch_fwd_impl<r, tt, nd, false, true, -1>(p, s)        \
-                    : fwd::launch_fwd_impl<r, tt, nd, false, false, -1>(p, s);
+    return p.h_last ? fwd::launch_fwd_impl<r, tt, nd, false, true, -1, -1>(p, s)    \
+                    : fwd::launch_fwd_impl<r, tt, nd, false, false, -1, -1>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;

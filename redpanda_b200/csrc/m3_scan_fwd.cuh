@@ -15,6 +15,7 @@
 #include "m3_bulk.cuh"
 #include "m3_common.cuh"
 #include "m3_internal.h"
+#include "m3_prologue.cuh"
 #include "m3_stage.cuh"
 #include "m3_tiles.h"
 #include "m3_tma.h"
@@ -65,8 +66,9 @@ __device__ __forceinline__ void stage_du(unsigned char* s_dl, unsigned char* s_u
   }
 }
 
-// Stage y (fp32) of processing steps [s0, s0 + kCK) for the second pass of the
-// bidirectional scan, which adds the first pass's output.
+// Stage y of processing steps [s0, s0 + kCK) for the second pass of the
+// bidirectional scan, which adds the first pass's output; the tile is fp32
+// in processing order (a bf16 y is widened by plain loads).
 template <int DT>
 __device__ __forceinline__ void stage_y(float* s_y, const FwdParams& p, int b, int d0, int s0,
                                         int dir) {
@@ -76,7 +78,10 @@ __device__ __forceinline__ void stage_y(float* s_y, const FwdParams& p, int b, i
     const bool ok = (s < p.L) && (d < p.D);
     const int t = dir ? p.L - 1 - s : s;
     const size_t gi = ok ? ((size_t)b * p.L + t) * p.D + d : 0;
-    cp_async4(s_y + i, p.y + gi, ok);
+    if (p.y_bf16)
+      s_y[i] = ok ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.y)[gi]) : 0.f;
+    else
+      cp_async4(s_y + i, static_cast<const float*>(p.y) + gi, ok);
   }
 }
 
@@ -109,11 +114,20 @@ struct FwdSmem {
 // -1 to read it from the parameters (the element-wise staging path).
 // BULK: delta, u and the first pass's y arrive as TMA boxes (tm_dl, tm_u, tm_y:
 // (B*L, D) row-major maps with a DT x kCK box), in memory row order.
-template <int R, int T, int ND, bool BULK, bool STATE, int DU>
+// YB: y stored as bf16 (1) or fp32 (0) fixed at compile time, or -1 to read it
+// from the parameters (the element-wise staging path).
+// PRO: the layer's prologue is fused into the staging (BULK, bf16 only): tm_dl
+// maps dt, the dt_proj output before softplus, and tm_x the bf16 x_proj rows;
+// each landed chunk is turned into delta = bf16(softplus(dt)) in place and
+// into the padded B/C pairs by BCNorm + MIMO fold (m3_prologue.cuh), the same
+// values the standalone prologue followed by a cast to bf16 gives.
+template <int R, int T, int ND, bool BULK, bool STATE, int DU, int YB, bool PRO = false>
 __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
     scan_fwd_kernel(const FwdParams p, const __grid_constant__ CUtensorMap tm_dl,
                     const __grid_constant__ CUtensorMap tm_u,
-                    const __grid_constant__ CUtensorMap tm_y) {
+                    const __grid_constant__ CUtensorMap tm_y,
+                    const __grid_constant__ CUtensorMap tm_x) {
+  static_assert(!PRO || (BULK && DU == 1), "the fused prologue is a bf16 bulk-staging variant");
   using LM = LaneMap<R, T>;
   constexpr int NL = R + T;
   constexpr int NP = LM::NP;
@@ -139,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
   const int d0 = blockIdx.y * DT;
   const int dbase = d0 + grp * ND;
   const bool bf16 = DU < 0 ? p.dt_du == M3_BF16 : DU == 1;
+  const bool ybf = YB < 0 ? p.y_bf16 != 0 : YB == 1;
   const int esz = bf16 ? 2 : 4;
   const int L = p.L, D = p.D, N = p.N;
 
@@ -235,24 +250,59 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
     auto stage_bulk = [&](int c, int buf) {
       const int s0 = c * kCK, ns = min(kCK, L - s0);
       const int t_lo = dir ? L - s0 - ns : s0;
-      const uint32_t bcb = (uint32_t)(ns * N * es_bc);
+      const uint32_t bcb = PRO ? (uint32_t)(kCK * N * p.P * 2) : (uint32_t)(ns * N * es_bc);
       const uint32_t bytes = (uint32_t)(2 * kCK * DT * esz) + 2 * bcb +
-                             (accumulate ? (uint32_t)(kCK * DT * 4) : 0u);
+                             (accumulate ? (uint32_t)(kCK * DT * (ybf ? 2 : 4)) : 0u);
       if (accumulate) fence_proxy_async_global();
       mbar_arrive_expect_tx(&s_bar[buf], bytes);
       const int y0 = b * L + t_lo;
       tma_load_2d(s_dl + buf * kCK * DT * 4, &tm_dl, d0, y0, &s_bar[buf]);
       tma_load_2d(s_u + buf * kCK * DT * 4, &tm_u, d0, y0, &s_bar[buf]);
-      const size_t bc_off = ((size_t)b * L + t_lo) * N * es_bc;
-      bulk_g2s(s_braw + (size_t)(buf * 2 + 0) * kCK * NP, (const char*)p.Bc + bc_off, bcb,
-               &s_bar[buf]);
-      bulk_g2s(s_braw + (size_t)(buf * 2 + 1) * kCK * NP, (const char*)p.Cc + bc_off, bcb,
-               &s_bar[buf]);
+      if constexpr (PRO) {
+        // B_raw and C_raw boxes (kCK rows x N*P bf16) into the single raw
+        // buffer: the previous chunk's raw rows were widened before the
+        // barrier that precedes this issue
+        __nv_bfloat16* raw = reinterpret_cast<__nv_bfloat16*>(s_braw);
+        tma_load_2d(raw, &tm_x, p.off_b, y0, &s_bar[buf]);
+        tma_load_2d(raw + (size_t)kCK * N * p.P, &tm_x, p.off_c, y0, &s_bar[buf]);
+      } else {
+        const size_t bc_off = ((size_t)b * L + t_lo) * N * es_bc;
+        bulk_g2s(s_braw + (size_t)(buf * 2 + 0) * kCK * NP, (const char*)p.Bc + bc_off, bcb,
+                 &s_bar[buf]);
+        bulk_g2s(s_braw + (size_t)(buf * 2 + 1) * kCK * NP, (const char*)p.Cc + bc_off, bcb,
+                 &s_bar[buf]);
+      }
       if (accumulate) tma_load_2d(s_y + (size_t)buf * kCK * DT, &tm_y, d0, y0, &s_bar[buf]);
     };
     // raw B/C rows (memory order, N elements each) -> (b, b) pairs of the
     // padded lane layout in processing order
     auto widen_bc = [&](int buf, int ns) {
+      if constexpr (PRO) {
+        // delta = bf16(softplus(dt)) in place over the landed dt tile
+        __nv_bfloat16* dlt = reinterpret_cast<__nv_bfloat16*>(s_dl + buf * kCK * DT * 4);
+        for (int i = tid; i < kCK * DT; i += kThreads)
+          dlt[i] = __float2bfloat16_rn(softplus20(__bfloat162float(dlt[i])));
+        // BCNorm + MIMO fold of each staged row, one warp per (step, B|C)
+        const int np = N * p.P, lane = tid & 31;
+        const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(s_braw);
+        for (int r = tid >> 5; r < 2 * ns; r += kThreads / 32) {
+          const int which = r & 1, tt = r >> 1;
+          const int mr = dir ? ns - 1 - tt : tt;   // raw rows are in memory order
+          const __nv_bfloat16* x = raw + ((size_t)which * kCK + mr) * np;
+          auto ld = [&](int k) { return __bfloat162float(x[k]); };
+          const float* w = which ? p.wc : p.wb;
+          const float rs = bcnorm_scale(ld, np, p.eps, w != nullptr, lane);
+          float2* dst = (which ? s_c : s_b) + buf * kCK * NP + tt * NP;
+          for (int ln = lane; ln < NP; ln += 32) {
+            const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
+            const float v = n >= 0 ? __bfloat162float(__float2bfloat16_rn(
+                                         bcnorm_fold(ld, n, p.P, rs, w)))
+                                   : 0.f;
+            dst[ln] = f2(v);
+          }
+        }
+        return;
+      }
       for (int i = tid; i < ns * NP; i += kThreads) {
         const int tt = i / NP, ln = i - tt * NP;
         const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
@@ -418,13 +468,22 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
             }
           }
         }
-        float* yrow = p.y + ((size_t)b * L + t) * D;
+        const size_t yrow = ((size_t)b * L + t) * D;
 #pragma unroll
         for (int k = 0; k < ND; ++k) {
           const float tot = __fmul_rn(0.5f, quad_sum(part[k]));
           const int d = dbase + k;
           if ((k & 3) == q && d < D) {
-            yrow[d] = accumulate ? __fadd_rn(tot, by[mr * DT + grp * ND + k]) : tot;
+            float v = tot;
+            if (accumulate) {
+              // BULK with a bf16 y: the staged first-pass rows are bf16
+              const int si = mr * DT + grp * ND + k;
+              v = __fadd_rn(tot, (BULK && ybf)
+                                     ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(by)[si])
+                                     : by[si]);
+            }
+            if (ybf) static_cast<__nv_bfloat16*>(p.y)[yrow + d] = __float2bfloat16_rn(v);
+            else static_cast<float*>(p.y)[yrow + d] = v;
           }
         }
       };
@@ -481,17 +540,22 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
   if (fail) set_err(p.err, M3_ERR_DEVICE);
 }
 
-template <int R, int T, int ND, bool BULK, bool STATE, int DU>
+template <int R, int T, int ND, bool BULK, bool STATE, int DU, int YB, bool PRO = false>
 cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
   constexpr int NP = 4 * (R + T);
   constexpr int DT = 32 * ND;
   const size_t smem = FwdSmem<NP, DT, BULK>::bytes(p.direction == M3_DIR_BIDIR);
   // BULK: delta, u, y as (B*L, D) row-major maps with a (DT x kCK) box;
   // cudaErrorNotSupported (nothing launched) when the maps cannot be built
-  CUtensorMap maps[3];
+  CUtensorMap maps[4];
   memset(maps, 0, sizeof(maps));
   if constexpr (BULK) {
     static_assert(DU >= 0, "bulk staging needs a compile-time element type");
+    if constexpr (PRO) {   // the bf16 x_proj rows, a (kCK x N*P) box per B/C load
+      if (!encode_rows_map(&maps[3], p.xbc, 2, (size_t)p.B * p.L, (size_t)p.ld_x,
+                           p.N * p.P, kCK))
+        return cudaErrorNotSupported;
+    }
     // TMA staging only for tiles of at most 128 channels (the configurations
     // validated on the GPU); wider tiles take the element-wise staging
     if constexpr (DT > 128) return cudaErrorNotSupported;
@@ -499,15 +563,15 @@ cudaError_t launch_fwd_impl(const FwdParams& p, cudaStream_t stream) {
     const int edu = DU == 1 ? 2 : 4;
     if (!encode_rows_map(&maps[0], p.delta, edu, rows, p.D, DT, kCK) ||
         !encode_rows_map(&maps[1], p.u, edu, rows, p.D, DT, kCK) ||
-        !encode_rows_map(&maps[2], p.y, 4, rows, p.D, DT, kCK))
+        !encode_rows_map(&maps[2], p.y, p.y_bf16 ? 2 : 4, rows, p.D, DT, kCK))
       return cudaErrorNotSupported;
   }
-  auto kern = scan_fwd_kernel<R, T, ND, BULK, STATE, DU>;
+  auto kern = scan_fwd_kernel<R, T, ND, BULK, STATE, DU, YB, PRO>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.B, (p.D + DT - 1) / DT);
-  kern<<<grid, kThreads, smem, stream>>>(p, maps[0], maps[1], maps[2]);
+  kern<<<grid, kThreads, smem, stream>>>(p, maps[0], maps[1], maps[2], maps[3]);
   return cudaGetLastError();
 }
 

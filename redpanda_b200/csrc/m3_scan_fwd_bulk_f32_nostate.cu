@@ -7,7 +7,8 @@ namespace m3 {
 cudaError_t launch_fwd_bulk_f32_nostate(const Tile& t, const FwdParams& p, cudaStream_t s) {
 #define M3_X(r, tt, nd, ndb, nthb, gs)                                              \
   if (t.R == r && t.T == tt && t.ND == nd)                                        \
-    return fwd::launch_fwd_impl<r, tt, nd, true, false, 0>(p, s);
+    return p.y_bf16 ? fwd::launch_fwd_impl<r, tt, nd, true, false, 0, 1>(p, s)     \
+                    : fwd::launch_fwd_impl<r, tt, nd, true, false, 0, 0>(p, s);
   M3_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;

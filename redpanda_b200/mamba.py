@@ -71,6 +71,16 @@ class RMSNorm(nn.Module):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
 
 
+def _bf16_layer():
+    """True under torch.autocast("cuda", dtype=torch.bfloat16), the reference's
+    mixed-precision training (train.py:268): the layer then runs the bf16
+    configuration of the kernels -- bf16 delta, u, Bc, Cc into the scan (the
+    config-1/2 element types), a bf16 y with fp32 state and accumulation, and
+    the gated output in bf16 for the bf16 out_proj GEMM."""
+    return (torch.is_autocast_enabled("cuda")
+            and torch.get_autocast_dtype("cuda") == torch.bfloat16)
+
+
 class Mamba3Block(nn.Module):
     """One Mamba-3 layer (mamba.py:141-498) with the recurrences on the kernels."""
 
@@ -193,19 +203,28 @@ class Mamba3Block(nn.Module):
         delta, bc, cc = S.m3_step_inputs(dt.reshape(rows, d_in), x_dbl.reshape(rows, -1),
                                          cfg.dt_rank, cfg.dt_rank + n * p, bw, cw, eps, n, p)
         delta, bc, cc = delta.view(*lead, d_in), bc.view(*lead, n), cc.view(*lead, n)
+        bf16 = _bf16_layer()
+        if bf16:
+            bf = torch.bfloat16
+            delta, u, bc, cc = delta.to(bf), u.to(bf), bc.to(bf), cc.to(bf)
+        yd = torch.bfloat16 if bf16 else None
         track = self._track_gate() if cfg.n_track_state > 0 else None
         A_real, A_imag = self._compute_A()
         args = (delta, u, bc, cc, A_real, A_imag, track, cfg.n_rot_state, n)
         state = None
         if cfg.bidirectional:
-            y, coef = S.m3_bidir_scan(*args), 2.0
+            y, coef = S.m3_bidir_scan(*args, y_dtype=yd), 2.0
         elif return_state:
             (y, state), coef = S.m3_scan_with_state(*args), 1.0
         else:
-            y, coef = S.m3_trapezoidal_scan(*args), 1.0
-        y = S.m3_gate(y, u, xz[..., d_in:], self.D, coef, out=y)
+            y, coef = S.m3_trapezoidal_scan(*args, y_dtype=yd), 1.0
+        y = S.m3_gate(y, u, xz[..., d_in:], self.D, coef,
+                      out=None if (bf16 and y.dtype != torch.bfloat16) else y,
+                      out_dtype=torch.bfloat16 if bf16 else None)
         if residual is None:
             out = self.out_proj(y)
+        elif bf16:   # bf16 out_proj; the residual stream stays in its own (fp32) dtype
+            out = residual + self.out_proj(y)
         else:   # residual + out_proj(y) as one GEMM
             op = self.out_proj
             r2 = residual.reshape(-1, residual.shape[-1])
@@ -223,13 +242,18 @@ class Mamba3Block(nn.Module):
         x_branch, z = self.in_proj(x).chunk(2, dim=-1)
         x_branch = F.silu(x_branch)
         delta, bc, cc = self._ssm_inputs(x_branch)
+        yd = None
+        if _bf16_layer():   # the kernels' bf16 configuration (autograd casts the grads back)
+            bf = torch.bfloat16
+            delta, bc, cc, yd = delta.to(bf), bc.to(bf), cc.to(bf), bf
+            x_branch = x_branch.to(bf)
         track = self._track_gate() if cfg.n_track_state > 0 else None
         A_real, A_imag = self._compute_A()
         args = (delta, x_branch, bc, cc, A_real, A_imag, track, cfg.n_rot_state, cfg.d_state)
         if not cfg.bidirectional:
-            y = S.m3_trapezoidal_scan(*args) + x_branch * self.D
+            y = S.m3_trapezoidal_scan(*args, y_dtype=yd) + x_branch * self.D
         else:
-            y = S.m3_bidir_scan(*args) + 2.0 * x_branch * self.D
+            y = S.m3_bidir_scan(*args, y_dtype=yd) + 2.0 * x_branch * self.D
         return self.out_proj(y * F.silu(z))
 
     def forward_with_state(self, x):

@@ -128,12 +128,13 @@ class ScanPlan:
 
     def forward(self, delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, y, ckpt=None, h_last=None,
                 dbu_last=None, stream=None):
+        """y is float32 or bfloat16 (its element type selects the stored y)."""
         dev = delta.device
         s = _stream(dev) if stream is None else stream
-        _lib.check(self._lib.m3_scan_fwd(
+        _lib.check(self._lib.m3_scan_fwd_typed(
             self.desc, delta.data_ptr(), u.data_ptr(), Bc.data_ptr(), Cc.data_ptr(),
-            Ar_p.data_ptr(), Ai_p.data_ptr(), Tk_p.data_ptr(), y.data_ptr(), ctypes_ptr(ckpt),
-            ctypes_ptr(h_last), ctypes_ptr(dbu_last), s))
+            Ar_p.data_ptr(), Ai_p.data_ptr(), Tk_p.data_ptr(), y.data_ptr(), _dt_code(y.dtype),
+            ctypes_ptr(ckpt), ctypes_ptr(h_last), ctypes_ptr(dbu_last), s))
 
     def backward(self, delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, dy, ckpt, d_delta, d_u, d_Bc,
                  d_Cc, d_Ar, d_Ai, d_Tk, workspace, stream=None):
@@ -150,13 +151,15 @@ class ScanPlan:
 class _TrapezoidalScanFn(torch.autograd.Function):
     """y = trapezoidal selective scan; analytic, deterministic backward.
 
-    forward(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state)
-    returns (y, h_last, dbu_last); the state outputs are empty unless
-    ``want_state`` and are not differentiable.
+    forward(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state, y_dtype)
+    returns (y, h_last, dbu_last); y is float32 (the reference) or bfloat16 (a
+    bf16 layer; state and accumulation stay fp32); the state outputs are empty
+    unless ``want_state`` and are not differentiable.
     """
 
     @staticmethod
-    def forward(ctx, delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state):
+    def forward(ctx, delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state,
+                y_dtype=torch.float32):
         lib = _lib.load()
         dev = _require_cuda(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p)
         dl, uu, dt_du = _prep_pair(delta, u)
@@ -165,7 +168,7 @@ class _TrapezoidalScanFn(torch.autograd.Function):
         B, L, D = uu.shape
         N = bb.shape[-1]
         desc = ScanDesc(B, L, D, N, int(n_rot), dt_du, dt_bc, int(direction))
-        y = torch.empty(B, L, D, device=dev, dtype=torch.float32)
+        y = torch.empty(B, L, D, device=dev, dtype=y_dtype)
         need_grad = any(ctx.needs_input_grad[:7])
         nck = lib.m3_scan_ckpt_floats(desc) if need_grad else 0
         ckpt = torch.empty(nck, device=dev, dtype=torch.float32) if nck else None
@@ -175,10 +178,11 @@ class _TrapezoidalScanFn(torch.autograd.Function):
         else:
             h = dbu = None
         with torch.cuda.device(dev):
-            _lib.check(lib.m3_scan_fwd(desc, dl.data_ptr(), uu.data_ptr(), bb.data_ptr(),
-                                       cc.data_ptr(), ar.data_ptr(), ai.data_ptr(),
-                                       tk.data_ptr(), y.data_ptr(), ctypes_ptr(ckpt),
-                                       ctypes_ptr(h), ctypes_ptr(dbu), _stream(dev)))
+            _lib.check(lib.m3_scan_fwd_typed(desc, dl.data_ptr(), uu.data_ptr(), bb.data_ptr(),
+                                             cc.data_ptr(), ar.data_ptr(), ai.data_ptr(),
+                                             tk.data_ptr(), y.data_ptr(), _dt_code(y_dtype),
+                                             ctypes_ptr(ckpt), ctypes_ptr(h), ctypes_ptr(dbu),
+                                             _stream(dev)))
         empty = torch.empty(0, device=dev)
         ctx.save_for_backward(dl, uu, bb, cc, ar, ai, tk, ckpt if ckpt is not None else empty)
         ctx.has_ckpt = ckpt is not None
@@ -218,10 +222,11 @@ class _TrapezoidalScanFn(torch.autograd.Function):
                 _stream(dev)))
         td, tu, tb, tc, tar, tai, ttk = ctx.in_dtypes
         return (dd.to(td), du.to(tu), dB.to(tb), dC.to(tc), dAr.to(tar), dAi.to(tai),
-                dTk.to(ttk), None, None, None)
+                dTk.to(ttk), None, None, None, None)
 
 
-def _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state):
+def _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state,
+                 y_dtype=torch.float32):
     """Forward only (no autograd record, no checkpoints): the inference path."""
     lib = _lib.load()
     dev = _require_cuda(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p)
@@ -231,57 +236,64 @@ def _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_stat
     B, L, D = uu.shape
     N = bb.shape[-1]
     desc = ScanDesc(B, L, D, N, int(n_rot), dt_du, dt_bc, int(direction))
-    y = torch.empty(B, L, D, device=dev, dtype=torch.float32)
+    y = torch.empty(B, L, D, device=dev, dtype=y_dtype)
     empty = torch.empty(0, device=dev)
     h = dbu = None
     if want_state:
         h = torch.empty(B, D, N, device=dev, dtype=torch.float32)
         dbu = torch.empty_like(h)
     with torch.cuda.device(dev):
-        _lib.check(lib.m3_scan_fwd(desc, dl.data_ptr(), uu.data_ptr(), bb.data_ptr(),
-                                   cc.data_ptr(), ar.data_ptr(), ai.data_ptr(), tk.data_ptr(),
-                                   y.data_ptr(), None, ctypes_ptr(h), ctypes_ptr(dbu),
-                                   _stream(dev)))
+        _lib.check(lib.m3_scan_fwd_typed(desc, dl.data_ptr(), uu.data_ptr(), bb.data_ptr(),
+                                         cc.data_ptr(), ar.data_ptr(), ai.data_ptr(),
+                                         tk.data_ptr(), y.data_ptr(), _dt_code(y_dtype), None,
+                                         ctypes_ptr(h), ctypes_ptr(dbu), _stream(dev)))
     return (y, h, dbu) if want_state else (y, empty, empty)
 
 
-def _apply(delta, u, Bc, Cc, A_real, A_imag, track, n_rot, n_state, direction, want_state):
+def _apply(delta, u, Bc, Cc, A_real, A_imag, track, n_rot, n_state, direction, want_state,
+           y_dtype=None):
     d_inner = u.shape[-1]
+    y_dtype = torch.float32 if y_dtype is None else y_dtype
+    if y_dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"y_dtype must be float32 or bfloat16, not {y_dtype}")
     Ar_p, Ai_p, Tk_p = pad_params(A_real, A_imag, track, n_rot, n_state, d_inner, u.device)
     if not torch.is_grad_enabled():
-        return _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state)
+        return _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state,
+                            y_dtype)
     return _TrapezoidalScanFn.apply(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p,
-                                    n_rot, direction, want_state)
+                                    n_rot, direction, want_state, y_dtype)
 
 
 def m3_trapezoidal_scan(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
-                        n_rot, n_state):
+                        n_rot, n_state, *, y_dtype=None):
     """Causal scan; drop-in for ``triton_trapezoidal_scan`` (triton_scan.py:318-337).
 
-    Returns fp32 y (B, L, D) without the ``u*D`` skip term.
+    Returns y (B, L, D) without the ``u*D`` skip term: float32 as the
+    reference, or bfloat16 with ``y_dtype=torch.bfloat16`` (a bf16 layer; the
+    state and every accumulation stay fp32).
     """
     return _apply(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
-                  n_rot, n_state, M3_DIR_FWD, False)[0]
+                  n_rot, n_state, M3_DIR_FWD, False, y_dtype)[0]
 
 
 triton_trapezoidal_scan = m3_trapezoidal_scan
 
 
 def m3_reverse_scan(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
-                    n_rot, n_state):
+                    n_rot, n_state, *, y_dtype=None):
     """flip(scan(flip(x))) without materialising flipped copies."""
     return _apply(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
-                  n_rot, n_state, M3_DIR_REV, False)[0]
+                  n_rot, n_state, M3_DIR_REV, False, y_dtype)[0]
 
 
 def m3_bidir_scan(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
-                  n_rot, n_state):
+                  n_rot, n_state, *, y_dtype=None):
     """Fused bidirectional scan: scan(x) + flip(scan(flip(x))) (mamba.py:254-260).
 
     Skip terms excluded; the reference block adds ``u*D`` once per direction.
     """
     return _apply(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
-                  n_rot, n_state, M3_DIR_BIDIR, False)[0]
+                  n_rot, n_state, M3_DIR_BIDIR, False, y_dtype)[0]
 
 
 def m3_scan_with_state(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
@@ -370,8 +382,12 @@ def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mi
     """
     lib = _lib.load()
     dev = _require_cuda(dt, x_dbl)
-    if dt.dtype != torch.float32 or x_dbl.dtype != torch.float32:
-        raise TypeError("m3_step_inputs: dt and x_dbl must be float32")
+    # a bf16 layer's projections are widened first: the prologue computes in
+    # fp32, as torch autocast runs softplus and the RMSNorm (train.py:268)
+    if dt.dtype != torch.float32:
+        dt = dt.float()
+    if x_dbl.dtype != torch.float32:
+        x_dbl = x_dbl.float()
     if dt.stride(-1) != 1 or x_dbl.stride(-1) != 1:
         raise ValueError("m3_step_inputs: rows of dt and x_dbl must be contiguous")
     B, D = dt.shape
@@ -445,10 +461,13 @@ def step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mimo_
                                mimo_p)
 
 
-def m3_gate(y, u, z, d_skip, coef=1.0, out=None):
-    """(y + coef*u*D) * silu(z) in one launch (mamba.py:262-265); y: (..., D)
-    float32 contiguous, u: (..., D) float32/bf16 contiguous, z: (..., D) with
-    contiguous rows (a view of in_proj's output).  ``out`` may be ``y``."""
+def m3_gate(y, u, z, d_skip, coef=1.0, out=None, out_dtype=None):
+    """(y + coef*u*D) * silu(z) in one launch (mamba.py:262-265).
+
+    y, u: (..., D) contiguous, float32 or bfloat16; z: (..., D) float32 or
+    bfloat16 with contiguous rows (a view of in_proj's output); arithmetic in
+    fp32.  ``out`` (or a new tensor of ``out_dtype``, default y's dtype) may be
+    ``y`` itself."""
     lib = _lib.load()
     dev = _require_cuda(y, u, z, d_skip)
     D = y.shape[-1]
@@ -458,12 +477,14 @@ def m3_gate(y, u, z, d_skip, coef=1.0, out=None):
     zz = z.reshape(rows, D) if z.dim() > 2 else z
     if zz.stride(-1) != 1:
         raise ValueError("m3_gate: z rows must be contiguous")
-    out = torch.empty_like(y) if out is None else out
+    if out is None:
+        out = torch.empty(y.shape, device=dev, dtype=y.dtype if out_dtype is None else out_dtype)
     ds = d_skip.detach().to(torch.float32).contiguous()
     with torch.cuda.device(dev):
-        _lib.check(lib.m3_gate(rows, D, y.data_ptr(), u.data_ptr(), _dt_code(u.dtype),
-                               zz.data_ptr(), zz.stride(0), ds.data_ptr(), float(coef),
-                               out.data_ptr(), _stream(dev)))
+        _lib.check(lib.m3_gate_typed(rows, D, y.data_ptr(), _dt_code(y.dtype), u.data_ptr(),
+                                     _dt_code(u.dtype), zz.data_ptr(), _dt_code(zz.dtype),
+                                     zz.stride(0), ds.data_ptr(), float(coef), out.data_ptr(),
+                                     _dt_code(out.dtype), _stream(dev)))
     return out
 
 
@@ -480,6 +501,8 @@ def m3_step_gated_(state, delta_t, u_t, Bc_t, Cc_t, params, n_rot, z, d_skip):
     h = state[0]
     dev = _require_cuda(h, delta_t, u_t, Bc_t, Cc_t, z, d_skip)
     B, D, N = h.shape
+    if z.dtype != torch.float32:   # a bf16 layer's in_proj output (the step computes in fp32)
+        z = z.float()
     if z.stride(-1) != 1:
         raise ValueError("m3_step_gated_: rows of z must be contiguous")
     dl, uu, dt_du = _prep_pair(delta_t, u_t)

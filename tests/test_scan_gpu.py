@@ -347,3 +347,76 @@ def test_backward_grad_outputs_off_16_byte_boundary(dtype):
     for a, b in zip(outs[0], outs[1]):
         assert torch.equal(a, b)
     assert S.device_error() == 0
+
+
+BF16_Y_CASES = [
+    ("bulk_bidir", ScanShape(2, 37, 256, 32, 16, 4), torch.bfloat16, 2),
+    ("bulk_causal", ScanShape(2, 40, 256, 32, 8, 2), torch.bfloat16, 0),
+    ("bulk_reverse_f32_inputs", ScanShape(2, 29, 256, 32, 16, 4), torch.float32, 1),
+    ("elementwise_bidir_odd_D", ScanShape(2, 20, 40, 16, 4, 2), torch.float32, 2),
+]
+
+
+@pytest.mark.parametrize("name,shape,dtype,direction", BF16_Y_CASES,
+                         ids=[c[0] for c in BF16_Y_CASES])
+def test_bf16_y_output(name, shape, dtype, direction, monkeypatch):
+    """y stored in bf16 (m3_scan_fwd_typed): one direction rounds the same fp32
+    value the fp32 output holds; the bidirectional pair rounds the first
+    direction's partial and then the sum (at most one bf16 ulp more); the
+    gradients are those of the fp32-y scan fed the same (bf16) dy."""
+    inp = make_scan_inputs(shape, seed=29, dtype=dtype)
+    g = to_cuda(inp)
+    nr = shape.n_rot
+    fn = _FN[direction]
+    args = (g["delta"], g["u"], g["Bc"], g["Cc"], g["A_real"], g["A_imag"], g["track"], nr,
+            shape.d_state)
+    with torch.no_grad():
+        y32 = fn(*args)
+        y16 = fn(*args, y_dtype=torch.bfloat16)
+    assert y16.dtype == torch.bfloat16
+    if direction != 2:
+        assert torch.equal(y16, y32.to(torch.bfloat16))
+    else:
+        # the first pass (the reverse direction) is rounded to bf16, then the
+        # sum: |err| <= half a bf16 ulp of each (ulp(x) = 2^(floor(log2|x|) - 7))
+        with torch.no_grad():
+            yrev = S.m3_reverse_scan(*args)
+        def half_ulp(x):
+            return torch.pow(2.0, torch.floor(torch.log2(x.abs().clamp(min=1e-30))) - 8)
+        bound = half_ulp(yrev) + half_ulp(y32) + 1e-6 * y32.abs().max()
+        assert bool(((y16.float() - y32).abs() <= bound).all())
+    # gradients with a bf16 y equal the fp32-y scan's for the same dy
+    dy = g["dy"].to(torch.bfloat16)
+    grads = []
+    for yd in (torch.float32, torch.bfloat16):
+        lv = {k: g[k].clone().requires_grad_(True) for k in ("delta", "u", "Bc", "Cc")}
+        y = fn(lv["delta"], lv["u"], lv["Bc"], lv["Cc"], g["A_real"], g["A_imag"], g["track"],
+               nr, shape.d_state, y_dtype=yd)
+        y.backward(dy.to(yd))
+        grads.append([lv[k].grad for k in ("delta", "u", "Bc", "Cc")])
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)
+    assert S.device_error() == 0
+
+
+@pytest.mark.parametrize("types", [("f32", "bf16", "bf16", "bf16"), ("bf16", "bf16", "bf16", "bf16"),
+                                   ("f32", "f32", "bf16", "f32"), ("bf16", "f32", "f32", "f32")])
+def test_gate_typed_matches_torch(types):
+    """(y + c*u*D) * silu(z) with an element type per operand, against the
+    same formula in fp32 torch on the widened operands (out rounded once)."""
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16}
+    ty, tu, tz, to = (dt[t] for t in types)
+    rows, D = 300, 136
+    gen = torch.Generator("cuda").manual_seed(3)
+    y = torch.randn(rows, D, device="cuda", generator=gen).to(ty)
+    u = torch.randn(rows, D, device="cuda", generator=gen).to(tu)
+    zf = torch.randn(rows, 2 * D, device="cuda", generator=gen).to(tz)
+    z = zf[:, D:]                                   # row-strided view, as in the layer
+    ds = torch.randn(D, device="cuda", generator=gen)
+    out = S.m3_gate(y, u, z, ds, 2.0, out_dtype=to)
+    ref = (y.float() + 2.0 * (u.float() * ds)) * (z.float() / (1 + torch.exp(-z.float())))
+    assert out.dtype == to
+    if to == torch.float32:
+        assert rel_err(out, ref) <= 1e-6
+    else:
+        assert _bf16_ok(out, ref)
