@@ -753,6 +753,57 @@ def run_configs(dev, args, clocks):
          {"workload": f"c2: causal scan fwd + analytic bwd + reductions, bf16, B={cb}"})
     del g2, b2
     torch.cuda.empty_cache()
+    # c2 with the layer's prologue fused into both kernels: raw bf16 dt and
+    # x_proj rows in, softplus/BCNorm/MIMO fold applied while staging, d dt,
+    # d B_raw, d C_raw and the BCNorm weight gradients out -- the 12 800 (fwd)
+    # and 29 184 (fwd+bwd) B/token boundary of the raw projections
+    import ctypes
+    lib = S._lib.load()
+    g3 = torch.Generator(dev).manual_seed(3)
+    dt_rank, p4 = 48, 4
+    ld_x = dt_rank + 2 * N * p4
+    fx = {"dt": (torch.randn(cb, 64, 1536, device=dev, generator=g3) * 0.5 - 4.0).to(bf),
+          "x": torch.randn(cb, 64, ld_x, device=dev, generator=g3).to(bf),
+          "u": torch.randn(cb, 64, 1536, device=dev, generator=g3).to(bf),
+          "dy": torch.randn(cb, 64, 1536, device=dev, generator=g3).to(bf)}
+    wbc = [1 + 0.1 * torch.randn(N * p4, device=dev, generator=g3) for _ in range(2)]
+    Pf = [t.contiguous() for t in pad_params(
+        -torch.exp(torch.randn(1536, N_ROT, device=dev, generator=g3) * 0.5),
+        (torch.rand(1536, N_ROT, device=dev, generator=g3) * 2 - 1) * math.pi,
+        torch.tanh(torch.randn(1536, N - N_ROT, device=dev, generator=g3)), N_ROT, N, 1536, dev)]
+    planf = ScanPlan(cb, 64, 1536, N, N_ROT, bf, bf, S.M3_DIR_BIDIR)
+    yf = torch.empty(cb, 64, 1536, device=dev)
+    ckf = torch.empty(planf.ckpt_floats(), device=dev)
+    od = {"ddt": torch.empty_like(fx["dt"]), "du": torch.empty_like(fx["u"]),
+          "dx": torch.zeros_like(fx["x"]), "dw": torch.empty(2, N * p4, device=dev),
+          "dA": torch.empty(3, 1536, N, device=dev)}
+    nwsf = lib.m3_scan_bwd_fused_workspace_bytes(ctypes.byref(planf.desc), p4)
+    wsf = torch.empty(nwsf, device=dev, dtype=torch.uint8)
+    sh = stream.cuda_stream
+
+    def fused_step():
+        S._lib.check(lib.m3_scan_fwd_fused(
+            ctypes.byref(planf.desc), p4, fx["dt"].data_ptr(), fx["x"].data_ptr(), ld_x, dt_rank,
+            dt_rank + N * p4, wbc[0].data_ptr(), wbc[1].data_ptr(), 1e-5, fx["u"].data_ptr(),
+            Pf[0].data_ptr(), Pf[1].data_ptr(), Pf[2].data_ptr(), yf.data_ptr(), 0,
+            ckf.data_ptr(), sh))
+        S._lib.check(lib.m3_scan_bwd_fused(
+            ctypes.byref(planf.desc), p4, fx["dt"].data_ptr(), fx["x"].data_ptr(), ld_x, dt_rank,
+            dt_rank + N * p4, wbc[0].data_ptr(), wbc[1].data_ptr(), 1e-5, fx["u"].data_ptr(),
+            Pf[0].data_ptr(), Pf[1].data_ptr(), Pf[2].data_ptr(), fx["dy"].data_ptr(), 1,
+            ckf.data_ptr(), od["ddt"].data_ptr(), od["du"].data_ptr(), od["dx"].data_ptr(),
+            od["dw"][0].data_ptr(), od["dw"][1].data_ptr(), od["dA"][0].data_ptr(),
+            od["dA"][1].data_ptr(), od["dA"][2].data_ptr(), wsf.data_ptr(), nwsf, sh))
+    msf = bench(fused_step, 5)
+    raw_bc = 2 * N * p4 * 2
+    line("c2_fused_prologue_bidir", sh1, msf, (2 * 2 * 1536 + raw_bc + 4 * 1536) +
+         (3 * 2 * 1536 + raw_bc + 2 * 2 * 1536 + raw_bc), ["c2_fwd_bidir", "c2_bwd_bidir"],
+         {"workload": f"c2 with the prologue fused: bidirectional fwd + bwd from raw bf16 dt and "
+                      f"x_proj rows (softplus, BCNorm, MIMO fold and their backward inside the "
+                      f"scan kernels), B={cb}, y fp32",
+          "note": "issue_frac uses the unfused kernels' instruction counts"})
+    del fx, od, wsf, yf, ckf
+    torch.cuda.empty_cache()
     out["issue_peak_warp_inst_per_s"] = issue_peak
     out["sm_mhz_assumed"] = mhz
     return out

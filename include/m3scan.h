@@ -172,6 +172,31 @@ M3_API int m3_scan_bwd(const m3_scan_desc* desc,
                 float* d_A_real_p, float* d_A_imag_p, float* d_track_p,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* Workspace bytes of m3_scan_bwd_fused on the current device. */
+M3_API size_t m3_scan_bwd_fused_workspace_bytes(const m3_scan_desc* desc, int32_t mimo_p);
+
+/* Analytic backward of m3_scan_fwd_fused: the scan's backward with the
+ * prologue's backward fused in (the gradients torch's softplus, RMSNorm and
+ * sum give for mamba.py:284-301 and 336-337).  Inputs as m3_scan_fwd_fused,
+ * plus dy (B, L, D) of dtype_dy and the forward's ckpt.  Outputs:
+ *   d_dt    (B, L, D) bf16: softplus'(dt) times the bf16-rounded d delta
+ *   d_u     (B, L, D) bf16
+ *   d_xbc   (B*L, ld_x) bf16: the B_raw and C_raw columns are written; the
+ *           caller zero-fills the rest (the dt_raw columns get their gradient
+ *           through dt_proj)
+ *   d_wb, d_wc (N*mimo_p,) float32 BCNorm weight gradients (fixed-order sums)
+ *   d_A_real_p, d_A_imag_p, d_track_p  as m3_scan_bwd
+ * Every output equals, bit for bit, what the unfused bf16 layer's backward
+ * (m3_scan_bwd on the bf16 delta/Bc/Cc, then m3_step_inputs_bwd on the fp32
+ * values of their bf16 gradients) produces. */
+M3_API int m3_scan_bwd_fused(const m3_scan_desc* desc, int32_t mimo_p, const void* dt,
+                const void* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
+                const float* wb, const float* wc, float eps, const void* u,
+                const float* A_real_p, const float* A_imag_p, const float* track_p,
+                const void* dy, int32_t dtype_dy, const float* ckpt, void* d_dt, void* d_u,
+                void* d_xbc, float* d_wb, float* d_wc, float* d_A_real_p, float* d_A_imag_p,
+                float* d_track_p, void* workspace, size_t workspace_bytes, void* stream);
+
 /* O(1) recurrent step of B rows, in place.  Replaces the recurrence of
  * Mamba3Block.step (mamba.py:466-493):
  *   h, dbu    (B, D, N) float32, read and overwritten with the new state

@@ -45,6 +45,10 @@ SIGNATURES = {
     "m3_scan_fwd_fused": (ctypes.c_int, [_D, _I, _P, _P, ctypes.c_int64, _I, _I, _P, _P,
                                          ctypes.c_float, _P, _P, _P, _P, _P, _I, _P, _P]),
     "m3_scan_bwd_workspace_bytes": (_Z, [_D]),
+    "m3_scan_bwd_fused_workspace_bytes": (_Z, [_D, _I]),
+    "m3_scan_bwd_fused": (ctypes.c_int, [_D, _I, _P, _P, ctypes.c_int64, _I, _I, _P, _P,
+                                         ctypes.c_float, _P, _P, _P, _P, _P, _I, _P, _P, _P,
+                                         _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "m3_scan_bwd": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P,
                                    _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "m3_step": (ctypes.c_int, [_S, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),

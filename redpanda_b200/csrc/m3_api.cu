@@ -413,6 +413,112 @@ int m3_step(const m3_step_desc* desc, float* h, float* dbu, const void* delta, c
                      track_p, y, stream);
 }
 
+// workspace of the fused backward: the regular backward's, then the fp32 B/C
+// gradients (rows, N) x 2 and the BCNorm weight-gradient partials
+static bool fused_bwd_layout(const m3_scan_desc* d, const Tile& t, int32_t mimo_p,
+                             BwdLayout* lay, size_t* off_g, size_t* off_w, size_t* total) {
+  if (!bwd_layout(d, t, lay)) return false;
+  const long long rows = (long long)d->batch * d->seqlen;
+  *off_g = lay->total;
+  *off_w = *off_g + round256((size_t)rows * d->d_state * 4 * 2);
+  *total = *off_w + round256((size_t)step_inputs_bwd_ctas(rows) * 2 * d->d_state * mimo_p * 4);
+  return true;
+}
+
+size_t m3_scan_bwd_fused_workspace_bytes(const m3_scan_desc* desc, int32_t mimo_p) {
+  Tile t;
+  if (check_scan_desc(desc, &t) != M3_OK || mimo_p < 1) return 0;
+  BwdLayout lay;
+  size_t og, ow, total;
+  if (!fused_bwd_layout(desc, t, mimo_p, &lay, &og, &ow, &total)) return 0;
+  return total;
+}
+
+int m3_scan_bwd_fused(const m3_scan_desc* desc, int32_t mimo_p, const void* dt,
+                      const void* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
+                      const float* wb, const float* wc, float eps, const void* u,
+                      const float* A_real_p, const float* A_imag_p, const float* track_p,
+                      const void* dy, int32_t dtype_dy, const float* ckpt, void* d_dt,
+                      void* d_u, void* d_xbc, float* d_wb, float* d_wc, float* d_A_real_p,
+                      float* d_A_imag_p, float* d_track_p, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  Tile t;
+  int rc = check_scan_desc(desc, &t);
+  if (rc != M3_OK) return rc;
+  if (t.NDB == 0) return M3_ERR_UNSUPPORTED;
+  if (!dtype_ok(dtype_dy)) return M3_ERR_DTYPE;
+  if (!dt || !u || !A_real_p || !A_imag_p || !track_p || !dy || !d_dt || !d_u || !d_xbc ||
+      !d_A_real_p || !d_A_imag_p || !d_track_p || (wb && (!d_wb || !d_wc)))
+    return M3_ERR_NULL;
+  if (ckpt_floats(desc, t) > 0 && !ckpt) return M3_ERR_NULL;
+  const ProArgs a{mimo_p, xbc, ld_x, off_b, off_c, wb, wc, eps};
+  if ((rc = check_pro(desc, t, a, dt, u, t.dt_bwd())) != M3_OK) return rc;
+  const int esy = dsize(dtype_dy);
+  if (!aligned(dy, 16) || ((desc->d_inner * esy) % 16) != 0 || !aligned(d_dt, 16) ||
+      !aligned(d_u, 16) || !aligned(d_xbc, 2) || !aligned(A_real_p, 4) ||
+      !aligned(A_imag_p, 4) || !aligned(track_p, 4) || !aligned(d_A_real_p, 4) ||
+      !aligned(d_A_imag_p, 4) || !aligned(d_track_p, 4) || (ckpt && !aligned(ckpt, 16)) ||
+      !aligned(workspace, 256) || (d_wb && (!aligned(d_wb, 4) || !aligned(d_wc, 4))))
+    return M3_ERR_ALIGN;
+  if ((rc = check_device()) != M3_OK) return rc;
+  BwdLayout lay;
+  size_t off_g, off_w, total;
+  if (!fused_bwd_layout(desc, t, mimo_p, &lay, &off_g, &off_w, &total)) return M3_ERR_NO_DEVICE;
+  if (!workspace || workspace_bytes < total) return M3_ERR_WORKSPACE;
+
+  char* ws = static_cast<char*>(workspace);
+  const long long rows = (long long)desc->batch * desc->seqlen;
+  float* gB = reinterpret_cast<float*>(ws + off_g);
+  float* gC = gB + (size_t)rows * desc->d_state;
+  BwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.delta = dt; p.u = u; p.Bc = xbc; p.Cc = xbc;
+  p.Ar = A_real_p; p.Ai = A_imag_p; p.Tk = track_p;
+  p.dy = dy; p.ckpt = ckpt;
+  p.d_delta = d_dt; p.d_u = d_u;
+  p.part_a = reinterpret_cast<float*>(ws + lay.off_a);
+  p.part_bc = reinterpret_cast<float*>(ws + lay.off_bc);
+  p.scratch_du =
+      desc->direction == M3_DIR_BIDIR ? reinterpret_cast<float*>(ws + lay.off_du) : nullptr;
+  p.B = desc->batch; p.L = desc->seqlen; p.D = desc->d_inner; p.N = desc->d_state;
+  p.NR = desc->n_rot; p.NT = desc->d_state - desc->n_rot;
+  p.dt_du = M3_BF16; p.dt_bc = M3_BF16; p.dt_dy = dtype_dy;
+  p.direction = desc->direction;
+  p.nch = nchunks(desc->seqlen, t.cki());
+  p.G = lay.G; p.Bg = lay.Bg;
+  p.async_du = 1; p.async_dy = 1; p.bulk = 1;
+  p.pro = 1; p.xbc = xbc; p.ld_x = ld_x; p.off_b = off_b; p.off_c = off_c; p.P = mimo_p;
+  p.wb = wb; p.wc = wc; p.eps = eps;
+  p.err = device_err_ptr();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_scan_bwd(t, p, s);
+  if (e == cudaErrorNotSupported) return M3_ERR_UNSUPPORTED;
+  if (e != cudaSuccess) return M3_ERR_LAUNCH;
+
+  ReduceParams r;
+  memset(&r, 0, sizeof(r));
+  r.part_bc = p.part_bc; r.part_a = p.part_a;
+  r.d_Bc = gB; r.d_Cc = gC; r.bc_f32_of_bf16 = 1;
+  r.dAr = d_A_real_p; r.dAi = d_A_imag_p; r.dTk = d_track_p;
+  r.B = p.B; r.L = p.L; r.D = p.D; r.N = p.N; r.NR = p.NR; r.NT = p.NT;
+  r.dt_bc = M3_F32; r.G = p.G; r.Bg = p.Bg;
+  r.ndirs = desc->direction == M3_DIR_BIDIR ? 2 : 1;
+  e = launch_bwd_reduce(t, r, s);
+  if (e != cudaSuccess) return M3_ERR_LAUNCH;
+
+  // BCNorm + MIMO-fold backward over the bf16 rows (the dt part was applied in
+  // the scan's flush)
+  InputsBwdParams q;
+  memset(&q, 0, sizeof(q));
+  q.dt = nullptr; q.xbc = xbc; q.x_bf16 = 1; q.ld_x = ld_x; q.off_b = off_b; q.off_c = off_c;
+  q.wb = wb; q.wc = wc; q.eps = eps; q.g_Bc = gB; q.g_Cc = gC;
+  q.d_xbc = d_xbc; q.d_wb = d_wb; q.d_wc = d_wc;
+  q.part_w = reinterpret_cast<float*>(ws + off_w);
+  q.rows = rows; q.D = desc->d_inner; q.N = desc->d_state; q.P = mimo_p;
+  e = launch_step_inputs_bwd(q, s);
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
 int m3_step_factored(const m3_step_desc* desc, float* h, const float* fac_prev, float* fac_next,
                      const void* delta, const void* u, const void* Bc, const void* Cc,
                      const float* A_real_p, const float* A_imag_p, const float* track_p,

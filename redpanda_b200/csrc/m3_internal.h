@@ -71,6 +71,11 @@ struct BwdParams {
   int G, Bg;
   int async_du, async_dy;   // cp.async staging allowed for delta/u and dy
   int bulk;                 // every staged row is a 16-byte aligned bulk copy
+  // fused prologue (pro != 0; bf16 bulk path only): delta points at dt and
+  // d_delta receives d dt; Bc/Cc are unused (see FwdParams)
+  int pro;
+  const void* xbc; long long ld_x; int off_b, off_c, P;
+  const float* wb; const float* wc; float eps;
   int* err;
 };
 
@@ -100,6 +105,7 @@ struct ReduceParams {
   int dt_bc;
   int G, Bg;
   int ndirs;          // direction slots of part_bc
+  int bc_f32_of_bf16; // d_Bc/d_Cc are fp32 buffers receiving the bf16-rounded sums
 };
 
 cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s);

@@ -49,8 +49,13 @@ __global__ void reduce_bc_kernel(const ReduceParams p, int R, int T) {
       vb = __fadd_rn(vb, src[0]);
       vc = __fadd_rn(vc, src[NP]);
     }
-    st_f(p.d_Bc, i, p.dt_bc, vb);
-    st_f(p.d_Cc, i, p.dt_bc, __fmul_rn(0.5f, vc));
+    if (p.bc_f32_of_bf16) {   // the fused prologue's backward reads them (fp32 of the bf16 grads)
+      static_cast<float*>(p.d_Bc)[i] = __bfloat162float(__float2bfloat16_rn(vb));
+      static_cast<float*>(p.d_Cc)[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(0.5f, vc)));
+    } else {
+      st_f(p.d_Bc, i, p.dt_bc, vb);
+      st_f(p.d_Cc, i, p.dt_bc, __fmul_rn(0.5f, vc));
+    }
   }
 }
 
@@ -78,7 +83,15 @@ __global__ void reduce_a_kernel(const ReduceParams p, int R, int T) {
 
 }  // namespace
 
+cudaError_t launch_bwd_bulk_pro(const Tile& t, const BwdParams& p, cudaStream_t s,
+                                bool* handled);
+
 cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s) {
+  if (p.pro) {   // bf16 bulk-staged kernels only (the C ABI checks eligibility first)
+    bool handled = false;
+    const cudaError_t e = launch_bwd_bulk_pro(t, p, s, &handled);
+    return handled ? e : cudaErrorNotSupported;
+  }
   if (p.bulk) {
     bool handled = false;
     const bool du = p.dt_du == M3_BF16, dy = p.dt_dy == M3_BF16;

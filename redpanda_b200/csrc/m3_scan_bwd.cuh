@@ -29,6 +29,7 @@
 #include "m3_bulk.cuh"
 #include "m3_common.cuh"
 #include "m3_internal.h"
+#include "m3_prologue.cuh"
 #include "m3_stage.cuh"
 #include "m3_tiles.h"
 #include "m3_tma.h"
@@ -60,7 +61,10 @@ constexpr int pow2ceil(int x) {
 // GS: the recompute pass also keeps each step's rotational gates (exp*cos and
 // exp*sin) in Tensor Memory, so the reverse pass evaluates no transcendental;
 // the chunk is then KC = 8 steps so that state and gates fit.
-template <int R, int T, int ND, int NTH, bool GS, bool BULK>
+// PRO: the layer's prologue fused into the staging (bf16 bulk variant): raw dt
+// tiles and raw B/C rows are staged besides the delta and B/C tiles the math
+// reads (m3_prologue.cuh).
+template <int R, int T, int ND, int NTH, bool GS, bool BULK, bool PRO = false>
 struct BwdCfg {
   static_assert(ND % 2 == 0, "the backward processes channel pairs");
   static constexpr int KC = GS ? 8 : kCK;           // chunk length (= checkpoint interval)
@@ -99,7 +103,12 @@ struct BwdCfg {
   // pass stages the first pass's ddelta/du rows of the chunk.
   static constexpr size_t braw_floats = BULK ? 2 * 2 * (size_t)KC * NP : 0;  // [2][B|C][KC][NP]
   static constexpr size_t scr_floats = BULK ? (size_t)KC * DT * 2 : 0;       // [KC][DT][2]
+  // PRO: [2][KC][DT] bf16 raw dt, [2][B|C][KC][4*NP] bf16 raw x_proj rows
+  // (the host admits N*p <= 4*NP)
+  static constexpr size_t dtr_bytes = PRO ? 2 * (size_t)KC * DT * 2 : 0;
+  static constexpr size_t xraw_bytes = PRO ? 2 * 2 * (size_t)KC * 4 * NP * 2 : 0;
   static constexpr size_t smem_bytes =
+      dtr_bytes + xraw_bytes +
       3 * 2 * raw_bytes                       // delta, u, dy (HBM dtype), double-buffered
       + 2 * (size_t)DT * NP * 4               // checkpoint tile, double-buffered
       + 2 * 2 * (size_t)KC * NP * 4           // B, C (fp32), double-buffered
@@ -145,13 +154,15 @@ __device__ __forceinline__ float tile_at(const unsigned char* base, bool bf16, i
 
 // DU, DY: element types of delta/u and of dy fixed at compile time (0 fp32,
 // 1 bf16), or -1 to read them from the parameters (element-wise staging path).
-template <int R, int T, int ND, int NTH, bool GS, bool BULK, int DU, int DY>
-__global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
+template <int R, int T, int ND, int NTH, bool GS, bool BULK, int DU, int DY, bool PRO = false>
+__global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK, PRO>::CPS)
     scan_bwd_kernel(const BwdParams p, const __grid_constant__ CUtensorMap tm_dl,
                     const __grid_constant__ CUtensorMap tm_u,
-                    const __grid_constant__ CUtensorMap tm_dy) {
+                    const __grid_constant__ CUtensorMap tm_dy,
+                    const __grid_constant__ CUtensorMap tm_x) {
   using LM = LaneMap<R, T>;
-  using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
+  using CF = BwdCfg<R, T, ND, NTH, GS, BULK, PRO>;
+  static_assert(!PRO || (BULK && DU == 1), "the fused prologue is a bf16 bulk-staging variant");
   constexpr int KC = CF::KC;
   constexpr int NL = CF::NL, NP = CF::NP, DT = CF::DT, C = CF::C, CS = CF::CS, CG = CF::CG;
   constexpr int NG = CF::NG, NDP = CF::NDP, FL = CF::FL, SR = CF::SR, SG = CF::SG;
@@ -162,7 +173,10 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   static_assert(!BULK || NTH / 32 >= kStageWarps, "bulk staging issues from 4 warps");
 
   extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char* s_dl = smem;                                        // [2][raw]
+  // PRO staging first: raw dt [2][KC][DT] bf16, raw x_proj rows [2][B|C][KC][4*NP] bf16
+  __nv_bfloat16* s_dtr = reinterpret_cast<__nv_bfloat16*>(smem);
+  __nv_bfloat16* s_xraw = reinterpret_cast<__nv_bfloat16*>(smem + CF::dtr_bytes);
+  unsigned char* s_dl = smem + CF::dtr_bytes + CF::xraw_bytes;       // [2][raw]
   unsigned char* s_u = s_dl + 2 * CF::raw_bytes;                     // [2][raw]
   unsigned char* s_dy = s_u + 2 * CF::raw_bytes;                     // [2][raw]
   float* s_ck = reinterpret_cast<float*>(s_dy + 2 * CF::raw_bytes);  // [2][DT][NP]
@@ -323,7 +337,10 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
     const int y0 = b * L + t_lo;
     if (w == 0) {
       mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)(KC * DT * es_du));
-      tma_load_2d(s_dl + buf * CF::raw_bytes, &tm_dl, d0, y0, &s_bar[buf]);
+      // PRO: the raw dt tile; the widen step writes delta into s_dl
+      tma_load_2d(PRO ? static_cast<void*>(s_dtr + (size_t)buf * KC * DT)
+                      : static_cast<void*>(s_dl + buf * CF::raw_bytes),
+                  &tm_dl, d0, y0, &s_bar[buf]);
     } else if (w == 1) {
       mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)(KC * DT * es_du));
       tma_load_2d(s_u + buf * CF::raw_bytes, &tm_u, d0, y0, &s_bar[buf]);
@@ -337,6 +354,13 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
             p.ckpt + ((((size_t)b * ndirs + dslot) * (nch - 1) + (c - 1)) * D + d0) * NP;
         bulk_g2s(s_ck + buf * DT * NP, src, DT * NP * 4, &s_bar[buf]);
       }
+    } else if (PRO) {
+      // raw B_raw / C_raw boxes (KC rows x N*p bf16) of the x_proj rows
+      const int npr = N * p.P;
+      mbar_arrive_expect_tx(&s_bar[buf], (uint32_t)(2 * KC * npr * 2));
+      __nv_bfloat16* raw = s_xraw + (size_t)buf * 2 * KC * 4 * NP;
+      tma_load_2d(raw, &tm_x, p.off_b, y0, &s_bar[buf]);
+      tma_load_2d(raw + (size_t)KC * 4 * NP, &tm_x, p.off_c, y0, &s_bar[buf]);
     } else {
       const uint32_t bc_bytes = (uint32_t)(ns * N * es_bc);
       mbar_arrive_expect_tx(&s_bar[buf], 2 * bc_bytes);
@@ -355,6 +379,34 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
   const int wn = LM::mem_lane(wl / NL, wl % NL, p.NR, p.NT);
   const bool bc16 = p.dt_bc == M3_BF16;
   auto widen_bc = [&](int buf, int ns, int dir) {
+    if constexpr (PRO) {
+      // delta = bf16(softplus(dt)) over the tile (memory order, as TMA left it)
+      __nv_bfloat16* dlt = reinterpret_cast<__nv_bfloat16*>(s_dl + buf * CF::raw_bytes);
+      const __nv_bfloat16* dtr = s_dtr + (size_t)buf * KC * DT;
+      for (int i = tid; i < KC * DT; i += NTH)
+        dlt[i] = __float2bfloat16_rn(softplus20(__bfloat162float(dtr[i])));
+      // BCNorm + MIMO fold of each staged row, one warp per (step, B|C); the
+      // fold is rounded to bf16 as the unfused bf16 layer's cast does
+      const int np = N * p.P, lane = tid & 31;
+      const __nv_bfloat16* raw = s_xraw + (size_t)buf * 2 * KC * 4 * NP;
+      for (int r = tid >> 5; r < 2 * ns; r += NTH / 32) {
+        const int which = r & 1, tt = r >> 1;
+        const int mr = dir ? ns - 1 - tt : tt;
+        // box rows are packed at a pitch of np elements
+        const __nv_bfloat16* x = raw + (size_t)which * KC * 4 * NP + (size_t)mr * np;
+        auto ld = [&](int k) { return __bfloat162float(x[k]); };
+        const float* w = which ? p.wc : p.wb;
+        const float rs = bcnorm_scale(ld, np, p.eps, w != nullptr, lane);
+        float* dst = (which ? s_c : s_b) + buf * KC * NP + tt * NP;
+        for (int ln = lane; ln < NP; ln += 32) {
+          const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
+          dst[ln] = n >= 0 ? __bfloat162float(__float2bfloat16_rn(
+                                 bcnorm_fold(ld, n, p.P, rs, w)))
+                           : 0.f;
+        }
+      }
+      return;
+    }
     const float* rb0 = s_braw + ((size_t)(buf * 2 + 0) * KC) * NP;
     const float* rc0 = s_braw + ((size_t)(buf * 2 + 1) * KC) * NP;
     if constexpr (kFixedLane) {
@@ -784,6 +836,10 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
               ddl = __fadd_rn(sv.x, ddl);
               ddu = __fadd_rn(sv.y, ddu);
             }
+            if constexpr (PRO) {   // d dt = softplus'(dt) * (d delta rounded as the bf16 grad)
+              ddl = softplus20_grad(__bfloat162float(__float2bfloat16_rn(ddl)),
+                                    __bfloat162float(s_dtr[(size_t)buf * KC * DT + mr * DT + dd]));
+            }
             const size_t oi = ((size_t)b * L + t) * D + d;
             if (bf_du) {
               reinterpret_cast<__nv_bfloat16*>(p.d_delta)[oi] = __float2bfloat16_rn(ddl);
@@ -829,6 +885,13 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
                 ddl[1] = __fadd_rn(v0.z, ddl[1]); ddu[1] = __fadd_rn(v0.w, ddu[1]);
                 ddl[2] = __fadd_rn(v1.x, ddl[2]); ddu[2] = __fadd_rn(v1.y, ddu[2]);
                 ddl[3] = __fadd_rn(v1.z, ddl[3]); ddu[3] = __fadd_rn(v1.w, ddu[3]);
+              }
+              if constexpr (PRO) {   // d dt = softplus'(dt) * (d delta rounded as the bf16 grad)
+                const __nv_bfloat16* dtr = s_dtr + (size_t)buf * KC * DT + (size_t)mr * DT + dd0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  ddl[k] = softplus20_grad(__bfloat162float(__float2bfloat16_rn(ddl[k])),
+                                           __bfloat162float(dtr[k]));
               }
               const size_t oi = ((size_t)b * L + t) * D + d0 + dd0;
               if (bf_du) {
@@ -903,16 +966,21 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK>::CPS)
 // bulk-staging layout does not fit use the cp.async staging.
 constexpr size_t kMaxSmemPerCta = 227 * 1024;
 
-template <int R, int T, int ND, int NTH, bool GS, bool BULK, int DU, int DY>
+template <int R, int T, int ND, int NTH, bool GS, bool BULK, int DU, int DY, bool PRO = false>
 cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
-  using CF = BwdCfg<R, T, ND, NTH, GS, BULK>;
+  using CF = BwdCfg<R, T, ND, NTH, GS, BULK, PRO>;
   static_assert(CF::smem_bytes <= kMaxSmemPerCta, "backward tile exceeds shared memory");
   // BULK: delta, u, dy as (B*L, D) row-major matrices with a (DT x KC) box;
   // cudaErrorNotSupported (nothing launched) when the maps cannot be built
-  CUtensorMap maps[3];
+  CUtensorMap maps[4];
   memset(maps, 0, sizeof(maps));
   if constexpr (BULK) {
     static_assert(DU >= 0 && DY >= 0, "bulk staging needs compile-time element types");
+    if constexpr (PRO) {   // the bf16 x_proj rows, a (KC x N*P) box per B/C load
+      if (!encode_rows_map(&maps[3], p.xbc, 2, (size_t)p.B * p.L, (size_t)p.ld_x, p.N * p.P,
+                           CF::KC))
+        return cudaErrorNotSupported;
+    }
     // TMA staging only for tiles of at most 128 channels (the configurations
     // validated on the GPU); wider tiles take the element-wise staging
     if constexpr (CF::DT > 128) return cudaErrorNotSupported;
@@ -923,12 +991,12 @@ cudaError_t launch_bwd_impl(const BwdParams& p, cudaStream_t stream) {
         !encode_rows_map(&maps[2], p.dy, edy, rows, p.D, CF::DT, CF::KC))
       return cudaErrorNotSupported;
   }
-  auto kern = scan_bwd_kernel<R, T, ND, NTH, GS, BULK, DU, DY>;
+  auto kern = scan_bwd_kernel<R, T, ND, NTH, GS, BULK, DU, DY, PRO>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)CF::smem_bytes);
   if (e != cudaSuccess) return e;
   dim3 grid(p.Bg, p.G);
-  kern<<<grid, NTH, CF::smem_bytes, stream>>>(p, maps[0], maps[1], maps[2]);
+  kern<<<grid, NTH, CF::smem_bytes, stream>>>(p, maps[0], maps[1], maps[2], maps[3]);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,27 @@
+// Bulk-staged analytic backward kernels with the layer's prologue fused into
+// their staging and flush (bf16 dt, x_proj rows and u; dy in bf16 or fp32), one
+// per tile of m3_tiles.h whose bulk layout fits in shared memory.
+#include "m3_scan_bwd.cuh"
+
+namespace m3 {
+
+cudaError_t launch_bwd_bulk_pro(const Tile& t, const BwdParams& p, cudaStream_t s,
+                                bool* handled) {
+  *handled = false;
+#define M3_X(r, tt, nd, ndb, nthb, gs)                                                        \
+  if constexpr (ndb > 0 && bwd::BwdCfg<r, tt, (ndb > 0 ? ndb : 2), nthb, (gs != 0), true,     \
+                                       true>::smem_bytes <= bwd::kMaxSmemPerCta)               \
+    if (t.R == r && t.T == tt && t.ND == nd) {                                                \
+      const cudaError_t e =                                                                   \
+          p.dt_dy == M3_BF16                                                                  \
+              ? bwd::launch_bwd_impl<r, tt, ndb, nthb, (gs != 0), true, 1, 1, true>(p, s)      \
+              : bwd::launch_bwd_impl<r, tt, ndb, nthb, (gs != 0), true, 1, 0, true>(p, s);     \
+      *handled = e != cudaErrorNotSupported;                                                  \
+      return e;                                                                               \
+    }
+  M3_TILE_LIST(M3_X)
+#undef M3_X
+  return cudaSuccess;
+}
+
+}  // namespace m3

@@ -321,7 +321,8 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
       if (tid == 0) stage_bulk(0, 0);
       const bool ok = mbar_wait(&s_bar[0], (uint32_t)(phase[0] & 1));
       ++phase[0];
-      if (ok) widen_bc(0, min(kCK, L));
+      // (the fused widen uses warp shuffles: enter it warp-uniformly)
+      if (PRO ? __all_sync(0xffffffffu, ok) : ok) widen_bc(0, min(kCK, L));
       if (__syncthreads_or(!ok)) {
         if (tid == 0) mbar_wait(&s_bar[0], (uint32_t)((phase[0] - 1) & 1));
         fail = 1;
@@ -522,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
         if (more) {
           ok = mbar_wait(&s_bar[buf ^ 1], (uint32_t)(phase[buf ^ 1] & 1));
           ++phase[buf ^ 1];
-          if (ok) widen_bc(buf ^ 1, min(kCK, L - (c + 1) * kCK));
+          if (PRO ? __all_sync(0xffffffffu, ok) : ok) widen_bc(buf ^ 1, min(kCK, L - (c + 1) * kCK));
         }
         if (__syncthreads_or(!ok)) {
           // give up: let the copy still in flight land before the CTA exits

@@ -84,6 +84,9 @@ def _bf16_layer():
 class Mamba3Block(nn.Module):
     """One Mamba-3 layer (mamba.py:141-498) with the recurrences on the kernels."""
 
+    # bf16 layers run the scan with its prologue fused in (identical results)
+    fuse_prologue = True
+
     def __init__(self, config: MambaConfig):
         super().__init__()
         self.config = config
@@ -141,15 +144,41 @@ class Mamba3Block(nn.Module):
         delta = F.softplus(self.dt_proj(dt_raw))
         return delta, B, C
 
-    def _ssm_inputs(self, u):
+    def _projections(self, u):
+        """x_proj output and dt = dt_proj(dt_raw) (mamba.py:287-300)."""
+        x_dbl = self.x_proj(u)
+        return x_dbl, self.dt_proj(x_dbl[..., :self.config.dt_rank])
+
+    def _fused_scan(self, u, x_dbl, dt, direction):
+        """The bf16 layer's scan with its prologue fused into the kernels
+        (m3_scan_fwd_fused / m3_scan_bwd_fused), or None when it does not apply
+        (fuse_prologue off, non-bf16 projections, a shape the staging cannot
+        take): the caller then runs m3_step_inputs and the scan."""
+        cfg = self.config
+        if not self.fuse_prologue or not (x_dbl.dtype == dt.dtype == u.dtype == torch.bfloat16):
+            return None
+        n, p = cfg.d_state, cfg.mimo_p
+        bw = self.b_norm.weight if cfg.use_bcnorm else None
+        cw = self.c_norm.weight if cfg.use_bcnorm else None
+        eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
+        track = self._track_gate() if cfg.n_track_state > 0 else None
+        A_real, A_imag = self._compute_A()
+        try:
+            return S.m3_fused_scan(dt, x_dbl, bw, cw, eps, u, A_real, A_imag, track,
+                                   cfg.n_rot_state, n, p, cfg.dt_rank, cfg.dt_rank + n * p,
+                                   direction, y_dtype=torch.bfloat16)
+        except S.FusedUnsupported:
+            return None
+
+    def _ssm_inputs(self, u, x_dbl=None, dt=None):
         """(delta, Bc, Cc) of a sequence for the training path: the x_proj and
         dt_proj GEMMs in torch, softplus + BCNorm + MIMO fold (and their
         backward) in one launch each (m3_step_inputs / m3_step_inputs_bwd)."""
         cfg = self.config
         n, p = cfg.d_state, cfg.mimo_p
         lead = u.shape[:-1]
-        x_dbl = self.x_proj(u)
-        dt = self.dt_proj(x_dbl[..., :cfg.dt_rank])
+        if x_dbl is None:
+            x_dbl, dt = self._projections(u)
         rows = u.numel() // cfg.d_inner
         bw = self.b_norm.weight if cfg.use_bcnorm else None
         cw = self.c_norm.weight if cfg.use_bcnorm else None
@@ -200,24 +229,31 @@ class Mamba3Block(nn.Module):
         bw = self.b_norm.weight if cfg.use_bcnorm else None
         cw = self.c_norm.weight if cfg.use_bcnorm else None
         eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
-        delta, bc, cc = S.m3_step_inputs(dt.reshape(rows, d_in), x_dbl.reshape(rows, -1),
-                                         cfg.dt_rank, cfg.dt_rank + n * p, bw, cw, eps, n, p)
-        delta, bc, cc = delta.view(*lead, d_in), bc.view(*lead, n), cc.view(*lead, n)
         bf16 = _bf16_layer()
+        coef = 2.0 if cfg.bidirectional else 1.0
+        state = y = None
         if bf16:
-            bf = torch.bfloat16
-            delta, u, bc, cc = delta.to(bf), u.to(bf), bc.to(bf), cc.to(bf)
-        yd = torch.bfloat16 if bf16 else None
-        track = self._track_gate() if cfg.n_track_state > 0 else None
-        A_real, A_imag = self._compute_A()
-        args = (delta, u, bc, cc, A_real, A_imag, track, cfg.n_rot_state, n)
-        state = None
-        if cfg.bidirectional:
-            y, coef = S.m3_bidir_scan(*args, y_dtype=yd), 2.0
-        elif return_state:
-            (y, state), coef = S.m3_scan_with_state(*args), 1.0
-        else:
-            y, coef = S.m3_trapezoidal_scan(*args, y_dtype=yd), 1.0
+            u = u.to(torch.bfloat16)
+            if not return_state:   # the prologue fused into the scan
+                y = self._fused_scan(u, x_dbl, dt,
+                                     S.M3_DIR_BIDIR if cfg.bidirectional else S.M3_DIR_FWD)
+        if y is None:
+            delta, bc, cc = S.m3_step_inputs(dt.reshape(rows, d_in), x_dbl.reshape(rows, -1),
+                                             cfg.dt_rank, cfg.dt_rank + n * p, bw, cw, eps, n, p)
+            delta, bc, cc = delta.view(*lead, d_in), bc.view(*lead, n), cc.view(*lead, n)
+            if bf16:
+                bf = torch.bfloat16
+                delta, bc, cc = delta.to(bf), bc.to(bf), cc.to(bf)
+            yd = torch.bfloat16 if bf16 else None
+            track = self._track_gate() if cfg.n_track_state > 0 else None
+            A_real, A_imag = self._compute_A()
+            args = (delta, u, bc, cc, A_real, A_imag, track, cfg.n_rot_state, n)
+            if cfg.bidirectional:
+                y = S.m3_bidir_scan(*args, y_dtype=yd)
+            elif return_state:
+                y, state = S.m3_scan_with_state(*args)
+            else:
+                y = S.m3_trapezoidal_scan(*args, y_dtype=yd)
         y = S.m3_gate(y, u, xz[..., d_in:], self.D, coef,
                       out=None if (bf16 and y.dtype != torch.bfloat16) else y,
                       out_dtype=torch.bfloat16 if bf16 else None)
@@ -241,20 +277,27 @@ class Mamba3Block(nn.Module):
         cfg = self.config
         x_branch, z = self.in_proj(x).chunk(2, dim=-1)
         x_branch = F.silu(x_branch)
-        delta, bc, cc = self._ssm_inputs(x_branch)
+        coef = 2.0 if cfg.bidirectional else 1.0
+        x_dbl, dt = self._projections(x_branch)
+        if _bf16_layer():
+            x_branch = x_branch.to(torch.bfloat16)
+            y = self._fused_scan(x_branch, x_dbl, dt,
+                                 S.M3_DIR_BIDIR if cfg.bidirectional else S.M3_DIR_FWD)
+            if y is not None:
+                return self.out_proj((y + coef * x_branch * self.D) * F.silu(z))
+        delta, bc, cc = self._ssm_inputs(x_branch, x_dbl, dt)
         yd = None
         if _bf16_layer():   # the kernels' bf16 configuration (autograd casts the grads back)
             bf = torch.bfloat16
             delta, bc, cc, yd = delta.to(bf), bc.to(bf), cc.to(bf), bf
-            x_branch = x_branch.to(bf)
         track = self._track_gate() if cfg.n_track_state > 0 else None
         A_real, A_imag = self._compute_A()
         args = (delta, x_branch, bc, cc, A_real, A_imag, track, cfg.n_rot_state, cfg.d_state)
         if not cfg.bidirectional:
-            y = S.m3_trapezoidal_scan(*args, y_dtype=yd) + x_branch * self.D
+            y = S.m3_trapezoidal_scan(*args, y_dtype=yd)
         else:
-            y = S.m3_bidir_scan(*args, y_dtype=yd) + 2.0 * x_branch * self.D
-        return self.out_proj(y * F.silu(z))
+            y = S.m3_bidir_scan(*args, y_dtype=yd)
+        return self.out_proj((y + coef * x_branch * self.D) * F.silu(z))
 
     def forward_with_state(self, x):
         """mamba.py:269-282: output and the (h_last, dBu_last) state."""

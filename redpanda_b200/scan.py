@@ -225,6 +225,110 @@ class _TrapezoidalScanFn(torch.autograd.Function):
                 dTk.to(ttk), None, None, None, None)
 
 
+class FusedUnsupported(RuntimeError):
+    """The fused-prologue kernels cannot stage this shape; run the unfused pair."""
+
+
+M3_ERR_UNSUPPORTED = 4
+
+
+class _FusedScanFn(torch.autograd.Function):
+    """The scan with the layer's prologue fused in (m3_scan_fwd_fused /
+    m3_scan_bwd_fused): y from the raw projections dt (B, L, D) and x_dbl
+    (B, L, K) -- softplus, BCNorm and MIMO fold (mamba.py:284-301, 336-337)
+    applied as each chunk is staged.  bf16 inputs; equal bit for bit to
+    m3_step_inputs + casts to bf16 + the scan, forward and backward.
+
+    forward(dt, x_dbl, b_weight, c_weight, u, Ar_p, Ai_p, Tk_p, cfg) with
+    cfg = (n_rot, n_state, mimo_p, off_b, off_c, eps, direction, y_dtype, want_ckpt).
+    """
+
+    @staticmethod
+    def forward(ctx, dt, x_dbl, wb, wc, u, Ar_p, Ai_p, Tk_p, cfg):
+        n_rot, N, P, off_b, off_c, eps, direction, y_dtype, want_ckpt = cfg
+        lib = _lib.load()
+        dev = _require_cuda(dt, x_dbl, u, Ar_p, Ai_p, Tk_p)
+        if not (dt.dtype == x_dbl.dtype == u.dtype == torch.bfloat16):
+            raise FusedUnsupported("the fused prologue takes bf16 dt, x_dbl and u")
+        dt, x_dbl, u = dt.contiguous(), x_dbl.contiguous(), u.contiguous()
+        ar, ai, tk = (x.detach().to(torch.float32).contiguous() for x in (Ar_p, Ai_p, Tk_p))
+        w32 = [None if w is None else w.detach().to(torch.float32).contiguous() for w in (wb, wc)]
+        B, L, D = u.shape
+        desc = ScanDesc(B, L, D, N, int(n_rot), M3_BF16, M3_BF16, int(direction))
+        y = torch.empty(B, L, D, device=dev, dtype=y_dtype)
+        nck = lib.m3_scan_ckpt_floats(desc) if want_ckpt else 0
+        ckpt = torch.empty(nck, device=dev) if nck else None
+        with torch.cuda.device(dev):
+            rc = lib.m3_scan_fwd_fused(desc, int(P), dt.data_ptr(), x_dbl.data_ptr(),
+                                       x_dbl.shape[-1], int(off_b), int(off_c),
+                                       ctypes_ptr(w32[0]), ctypes_ptr(w32[1]), float(eps),
+                                       u.data_ptr(), ar.data_ptr(), ai.data_ptr(), tk.data_ptr(),
+                                       y.data_ptr(), _dt_code(y_dtype), ctypes_ptr(ckpt),
+                                       _stream(dev))
+        if rc == M3_ERR_UNSUPPORTED:
+            raise FusedUnsupported(_lib.strerror(rc))
+        _lib.check(rc)
+        empty = torch.empty(0, device=dev)
+        ctx.save_for_backward(dt, x_dbl, u, ar, ai, tk, ckpt if ckpt is not None else empty,
+                              *(w if w is not None else empty for w in w32))
+        ctx.cfg = cfg
+        ctx.has = (ckpt is not None, w32[0] is not None)
+        ctx.w_dtypes = (None if wb is None else wb.dtype, None if wc is None else wc.dtype)
+        ctx.p_dtypes = (Ar_p.dtype, Ai_p.dtype, Tk_p.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        lib = _lib.load()
+        dt, x_dbl, u, ar, ai, tk, ckpt, wb, wc = ctx.saved_tensors
+        n_rot, N, P, off_b, off_c, eps, direction, _, _ = ctx.cfg
+        has_ck, has_w = ctx.has
+        dev = dt.device
+        B, L, D = u.shape
+        desc = ScanDesc(B, L, D, N, int(n_rot), M3_BF16, M3_BF16, int(direction))
+        if dy.dtype not in (torch.float32, torch.bfloat16):
+            dy = dy.float()
+        dy = dy.contiguous()
+        d_dt, d_u = torch.empty_like(dt), torch.empty_like(u)
+        d_x = torch.zeros_like(x_dbl)
+        d_wb = torch.empty_like(wb) if has_w else None
+        d_wc = torch.empty_like(wc) if has_w else None
+        dAr, dAi, dTk = torch.empty_like(ar), torch.empty_like(ai), torch.empty_like(tk)
+        nws = lib.m3_scan_bwd_fused_workspace_bytes(desc, int(P))
+        ws = torch.empty(max(nws, 1), device=dev, dtype=torch.uint8)
+        with torch.cuda.device(dev):
+            _lib.check(lib.m3_scan_bwd_fused(
+                desc, int(P), dt.data_ptr(), x_dbl.data_ptr(), x_dbl.shape[-1], int(off_b),
+                int(off_c), ctypes_ptr(wb if has_w else None), ctypes_ptr(wc if has_w else None),
+                float(eps), u.data_ptr(), ar.data_ptr(), ai.data_ptr(), tk.data_ptr(),
+                dy.data_ptr(), _dt_code(dy.dtype), ckpt.data_ptr() if has_ck else None,
+                d_dt.data_ptr(), d_u.data_ptr(), d_x.data_ptr(), ctypes_ptr(d_wb),
+                ctypes_ptr(d_wc), dAr.data_ptr(), dAi.data_ptr(), dTk.data_ptr(),
+                ws.data_ptr(), nws, _stream(dev)))
+        wdt = ctx.w_dtypes
+        ta, ti, tt = ctx.p_dtypes
+        return (d_dt, d_x, None if d_wb is None else d_wb.to(wdt[0]),
+                None if d_wc is None else d_wc.to(wdt[1]), d_u, dAr.to(ta), dAi.to(ti),
+                dTk.to(tt), None)
+
+
+def m3_fused_scan(dt, x_dbl, b_weight, c_weight, eps, u, A_real, A_imag, track, n_rot, n_state,
+                  mimo_p, off_b, off_c, direction=M3_DIR_FWD, y_dtype=torch.bfloat16):
+    """y (without the u*D skip) of the scan whose prologue -- softplus(dt),
+    BCNorm of B_raw / C_raw (columns off_b / off_c of x_dbl, N*p each) and the
+    MIMO fold -- is fused into its staging; differentiable w.r.t. dt, x_dbl, the
+    BCNorm weights, u and the eigenvalues.  Raises FusedUnsupported when the
+    kernels cannot stage the shape."""
+    Ar_p, Ai_p, Tk_p = pad_params(A_real, A_imag, track, n_rot, n_state, u.shape[-1], u.device)
+    # checkpoints only when a backward can follow
+    want = torch.is_grad_enabled() and any(
+        t is not None and t.requires_grad
+        for t in (dt, x_dbl, b_weight, c_weight, u, Ar_p, Ai_p, Tk_p))
+    cfg = (int(n_rot), int(n_state), int(mimo_p), int(off_b), int(off_c), float(eps),
+           int(direction), y_dtype, bool(want))
+    return _FusedScanFn.apply(dt, x_dbl, b_weight, c_weight, u, Ar_p, Ai_p, Tk_p, cfg)
+
+
 def _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state,
                  y_dtype=torch.float32):
     """Forward only (no autograd record, no checkpoints): the inference path."""
