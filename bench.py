@@ -695,7 +695,7 @@ def run_configs(dev, args, clocks):
         gbs = bytes_per_token * tok / (ms / 1e3) / 1e9
         d = {"tokens_per_s": tok / (ms / 1e3), "ms_per_step": ms, "tokens_per_step": tok,
              "hbm_gbs": gbs, "hbm_frac": gbs / peak, "algorithmic_bytes_per_token": bytes_per_token}
-        if all(k in ipt for k in kernels):
+        if kernels and all(k in ipt for k in kernels):
             inst = sum(ipt[k] for k in kernels) * tok
             d["issue_frac"] = inst / (ms / 1e3) / issue_peak
             d["warp_inst_per_token"] = sum(ipt[k] for k in kernels)
@@ -753,12 +753,12 @@ def run_configs(dev, args, clocks):
          {"workload": f"c2: causal scan fwd + analytic bwd + reductions, bf16, B={cb}"})
     del g2, b2
     torch.cuda.empty_cache()
-    # c2 with the layer's prologue fused into both kernels: raw bf16 dt and
-    # x_proj rows in, softplus/BCNorm/MIMO fold applied while staging, d dt,
-    # d B_raw, d C_raw and the BCNorm weight gradients out -- the 12 800 (fwd)
-    # and 29 184 (fwd+bwd) B/token boundary of the raw projections
-    import ctypes
-    lib = S._lib.load()
+    # c2 from the raw projections -- bf16 dt before softplus and the x_proj rows
+    # holding B_raw/C_raw, the 12 800 (fwd) and 29 184 (fwd+bwd) B/token
+    # boundary -- two ways, both through autograd with the same dy: (a) the
+    # prologue fused into both scan kernels (m3_fused_scan), (b) the prologue as
+    # its own launch (m3_step_inputs, fp32) + casts to bf16 + the scan (the
+    # layer's default).  Both give the same bits (tests/test_fused_prologue_gpu.py).
     g3 = torch.Generator(dev).manual_seed(3)
     dt_rank, p4 = 48, 4
     ld_x = dt_rank + 2 * N * p4
@@ -767,42 +767,43 @@ def run_configs(dev, args, clocks):
           "u": torch.randn(cb, 64, 1536, device=dev, generator=g3).to(bf),
           "dy": torch.randn(cb, 64, 1536, device=dev, generator=g3).to(bf)}
     wbc = [1 + 0.1 * torch.randn(N * p4, device=dev, generator=g3) for _ in range(2)]
-    Pf = [t.contiguous() for t in pad_params(
-        -torch.exp(torch.randn(1536, N_ROT, device=dev, generator=g3) * 0.5),
-        (torch.rand(1536, N_ROT, device=dev, generator=g3) * 2 - 1) * math.pi,
-        torch.tanh(torch.randn(1536, N - N_ROT, device=dev, generator=g3)), N_ROT, N, 1536, dev)]
-    planf = ScanPlan(cb, 64, 1536, N, N_ROT, bf, bf, S.M3_DIR_BIDIR)
-    yf = torch.empty(cb, 64, 1536, device=dev)
-    ckf = torch.empty(planf.ckpt_floats(), device=dev)
-    od = {"ddt": torch.empty_like(fx["dt"]), "du": torch.empty_like(fx["u"]),
-          "dx": torch.zeros_like(fx["x"]), "dw": torch.empty(2, N * p4, device=dev),
-          "dA": torch.empty(3, 1536, N, device=dev)}
-    nwsf = lib.m3_scan_bwd_fused_workspace_bytes(ctypes.byref(planf.desc), p4)
-    wsf = torch.empty(nwsf, device=dev, dtype=torch.uint8)
-    sh = stream.cuda_stream
+    ar_f = -torch.exp(torch.randn(1536, N_ROT, device=dev, generator=g3) * 0.5)
+    ai_f = (torch.rand(1536, N_ROT, device=dev, generator=g3) * 2 - 1) * math.pi
+    tk_f = torch.tanh(torch.randn(1536, N - N_ROT, device=dev, generator=g3))
+    leaves = {k: v.requires_grad_(True) for k, v in fx.items() if k != "dy"}
+    rows = cb * 64
 
-    def fused_step():
-        S._lib.check(lib.m3_scan_fwd_fused(
-            ctypes.byref(planf.desc), p4, fx["dt"].data_ptr(), fx["x"].data_ptr(), ld_x, dt_rank,
-            dt_rank + N * p4, wbc[0].data_ptr(), wbc[1].data_ptr(), 1e-5, fx["u"].data_ptr(),
-            Pf[0].data_ptr(), Pf[1].data_ptr(), Pf[2].data_ptr(), yf.data_ptr(), 0,
-            ckf.data_ptr(), sh))
-        S._lib.check(lib.m3_scan_bwd_fused(
-            ctypes.byref(planf.desc), p4, fx["dt"].data_ptr(), fx["x"].data_ptr(), ld_x, dt_rank,
-            dt_rank + N * p4, wbc[0].data_ptr(), wbc[1].data_ptr(), 1e-5, fx["u"].data_ptr(),
-            Pf[0].data_ptr(), Pf[1].data_ptr(), Pf[2].data_ptr(), fx["dy"].data_ptr(), 1,
-            ckf.data_ptr(), od["ddt"].data_ptr(), od["du"].data_ptr(), od["dx"].data_ptr(),
-            od["dw"][0].data_ptr(), od["dw"][1].data_ptr(), od["dA"][0].data_ptr(),
-            od["dA"][1].data_ptr(), od["dA"][2].data_ptr(), wsf.data_ptr(), nwsf, sh))
-    msf = bench(fused_step, 5)
+    def chain(fused):
+        def run():
+            for v in leaves.values():
+                v.grad = None
+            if fused:
+                y = S.m3_fused_scan(leaves["dt"], leaves["x"], wbc[0], wbc[1], 1e-5, leaves["u"],
+                                    ar_f, ai_f, tk_f, N_ROT, N, p4, dt_rank, dt_rank + N * p4,
+                                    S.M3_DIR_BIDIR, y_dtype=torch.float32)
+            else:
+                dl, bc_, cc_ = S.step_inputs(leaves["dt"].float().reshape(rows, 1536),
+                                             leaves["x"].float().reshape(rows, ld_x), dt_rank,
+                                             dt_rank + N * p4, wbc[0], wbc[1], 1e-5, N, p4)
+                y = S.m3_bidir_scan(dl.view(cb, 64, 1536).to(bf), leaves["u"],
+                                    bc_.view(cb, 64, N).to(bf), cc_.view(cb, 64, N).to(bf),
+                                    ar_f, ai_f, tk_f, N_ROT, N)
+            y.backward(fx["dy"].float())
+        return run
+    msf = bench(chain(True), 5)
+    msu = bench(chain(False), 5)
     raw_bc = 2 * N * p4 * 2
-    line("c2_fused_prologue_bidir", sh1, msf, (2 * 2 * 1536 + raw_bc + 4 * 1536) +
-         (3 * 2 * 1536 + raw_bc + 2 * 2 * 1536 + raw_bc), ["c2_fwd_bidir", "c2_bwd_bidir"],
-         {"workload": f"c2 with the prologue fused: bidirectional fwd + bwd from raw bf16 dt and "
-                      f"x_proj rows (softplus, BCNorm, MIMO fold and their backward inside the "
-                      f"scan kernels), B={cb}, y fp32",
-          "note": "issue_frac uses the unfused kernels' instruction counts"})
-    del fx, od, wsf, yf, ckf
+    pro_bytes = (2 * 2 * 1536 + raw_bc + 4 * 1536) + (3 * 2 * 1536 + raw_bc + 2 * 2 * 1536 + raw_bc)
+    line("c2_fused_prologue_bidir", sh1, msf, pro_bytes, [],
+         {"workload": f"c2 from the raw projections with the prologue fused into the scan "
+                      f"kernels: bidirectional fwd + bwd from raw bf16 dt and x_proj rows "
+                      f"(softplus, BCNorm, MIMO fold and their backward inside the kernels), "
+                      f"B={cb}, y fp32, through autograd"})
+    line("c2_unfused_prologue_bidir", sh1, msu, pro_bytes, [],
+         {"workload": f"the same computation with the prologue as its own launch "
+                      f"(m3_step_inputs, fp32) + casts to bf16 + the scan, B={cb}, through "
+                      f"autograd (the bf16 layer's default)"})
+    del fx, leaves
     torch.cuda.empty_cache()
     out["issue_peak_warp_inst_per_s"] = issue_peak
     out["sm_mhz_assumed"] = mhz

@@ -9,7 +9,10 @@ import ctypes
 import os
 import threading
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libm3scan.so")
+# M3_LIBRARY names another build of the same library (e.g. one compiled with a
+# tuning macro by build.build_library(out=..., extra_flags=[...])).
+LIB_PATH = os.environ.get("M3_LIBRARY") or os.path.join(
+    os.path.dirname(os.path.abspath(__file__)), "libm3scan.so")
 
 M3_F32, M3_BF16 = 0, 1
 M3_DIR_FWD, M3_DIR_REV, M3_DIR_BIDIR = 0, 1, 2
@@ -101,7 +104,7 @@ def available():
     try:
         load()
         return True
-    except (RuntimeError, OSError):
+    except (RuntimeError, OSError, AttributeError):   # AttributeError: a stale build
         return False
 
 

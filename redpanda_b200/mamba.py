@@ -84,8 +84,14 @@ def _bf16_layer():
 class Mamba3Block(nn.Module):
     """One Mamba-3 layer (mamba.py:141-498) with the recurrences on the kernels."""
 
-    # bf16 layers run the scan with its prologue fused in (identical results)
-    fuse_prologue = True
+    # bf16 layers can run the scan with its prologue fused into the kernels
+    # (m3_scan_fwd_fused / m3_scan_bwd_fused; identical results).  Off by
+    # default: measured on a B200 the fused pair is slower than the separate
+    # HBM-bound prologue launch plus the scans, because the scan kernels are
+    # issue-bound and the fused staging repeats softplus per direction and the
+    # BCNorm per channel tile on their critical path (bench.py, configs line
+    # c2_fused_prologue_bidir).
+    fuse_prologue = False
 
     def __init__(self, config: MambaConfig):
         super().__init__()
