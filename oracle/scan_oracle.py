@@ -113,7 +113,7 @@ def scan_chunked(delta, u, Bc, Cc, A_real, A_imag, track, return_state=False,
     """
     nb, L, d = u.shape
     n = Bc.shape[-1]
-    h = torch.zeros(nb, d, n, dtype=delta.dtype)
+    h = torch.zeros(nb, d, n, dtype=delta.dtype, device=delta.device)
     carry = None
     ys = []
     for s in range(0, L, chunk):
@@ -151,9 +151,9 @@ def scan_sequential(delta, u, Bc, Cc, A_real, A_imag, track, reverse=False):
     """
     nb, L, d = u.shape
     n = Bc.shape[-1]
-    h = torch.zeros(nb, d, n, dtype=delta.dtype)
-    dbu_prev = torch.zeros(nb, d, n, dtype=delta.dtype)
-    y = torch.zeros(nb, L, d, dtype=delta.dtype)
+    h = torch.zeros(nb, d, n, dtype=delta.dtype, device=delta.device)
+    dbu_prev = torch.zeros(nb, d, n, dtype=delta.dtype, device=delta.device)
+    y = torch.zeros(nb, L, d, dtype=delta.dtype, device=delta.device)
     order = range(L - 1, -1, -1) if reverse else range(L)
     for t in order:
         g = _gates(delta[:, t:t + 1], A_real, A_imag, track)[:, 0]

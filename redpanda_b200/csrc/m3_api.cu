@@ -45,9 +45,12 @@ constexpr int kMaxState = 128;
 
 int device_sms() {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return -1; }
   int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
   return sms;
 }
 
@@ -74,6 +77,18 @@ int check_scan_desc(const m3_scan_desc* d, Tile* tile) {
   if (!dtype_ok(d->dtype_du) || !dtype_ok(d->dtype_bc)) return M3_ERR_DTYPE;
   if (d->direction < M3_DIR_FWD || d->direction > M3_DIR_BIDIR) return M3_ERR_SHAPE;
   if (!select_tile(d->n_rot, d->d_state - d->n_rot, tile)) return M3_ERR_UNSUPPORTED;
+  // fewer forward CTAs than SMs: the small-batch tiling of the same lane split
+  // (same bits, 4x the CTAs of the config-0 tile)
+  const int sms = device_sms();
+  if (sms > 0 && (long long)d->batch * ((d->d_inner + tile->dt() - 1) / tile->dt()) < sms) {
+    static const Tile kSmall[] = {
+#define M3_X(r, t, nd, ndb, nthb, gs) {r, t, nd, ndb, nthb, gs},
+        M3_SMALL_TILE_LIST(M3_X)
+#undef M3_X
+    };
+    for (const Tile& s : kSmall)
+      if (s.R == tile->R && s.T == tile->T) { *tile = s; break; }
+  }
   const long long g = (d->d_inner + tile->dt() - 1) / tile->dt();
   if (g > 65535) return M3_ERR_SHAPE;
   return M3_OK;

@@ -106,6 +106,7 @@ cudaError_t launch_scan_bwd(const Tile& t, const BwdParams& p, cudaStream_t s) {
     if (t.R == r && t.T == tt && t.ND == nd)                                        \
       return bwd::launch_bwd_impl<r, tt, ndb, nthb, (gs != 0), false, -1, -1>(p, s);
   M3_TILE_LIST(M3_X)
+  M3_SMALL_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;
 }

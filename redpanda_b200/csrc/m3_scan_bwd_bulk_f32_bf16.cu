@@ -17,6 +17,7 @@ cudaError_t launch_bwd_bulk_f32_bf16(const Tile& t, const BwdParams& p, cudaStre
       return e;                                                                     \
     }
   M3_TILE_LIST(M3_X)
+  M3_SMALL_TILE_LIST(M3_X)
 #undef M3_X
   return cudaSuccess;
 }

@@ -20,6 +20,7 @@ cudaError_t launch_bwd_bulk_pro(const Tile& t, const BwdParams& p, cudaStream_t 
       return e;                                                                               \
     }
   M3_TILE_LIST(M3_X)
+  M3_SMALL_TILE_LIST(M3_X)
 #undef M3_X
   return cudaSuccess;
 }

@@ -31,6 +31,7 @@ cudaError_t launch_scan_fwd(const Tile& t, const FwdParams& p, cudaStream_t s) {
     return p.h_last ? fwd::launch_fwd_impl<r, tt, nd, false, true, -1, -1>(p, s)    \
                     : fwd::launch_fwd_impl<r, tt, nd, false, false, -1, -1>(p, s);
   M3_TILE_LIST(M3_X)
+  M3_SMALL_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;
 }

@@ -10,6 +10,7 @@ cudaError_t launch_fwd_bulk_f32_state(const Tile& t, const FwdParams& p, cudaStr
     return p.y_bf16 ? fwd::launch_fwd_impl<r, tt, nd, true, true, 0, 1>(p, s)     \
                     : fwd::launch_fwd_impl<r, tt, nd, true, true, 0, 0>(p, s);
   M3_TILE_LIST(M3_X)
+  M3_SMALL_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;
 }

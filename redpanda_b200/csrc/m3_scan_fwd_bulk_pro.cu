@@ -11,6 +11,7 @@ cudaError_t launch_fwd_bulk_pro(const Tile& t, const FwdParams& p, cudaStream_t 
     return p.y_bf16 ? fwd::launch_fwd_impl<r, tt, nd, true, false, 1, 1, true>(p, s)       \
                     : fwd::launch_fwd_impl<r, tt, nd, true, false, 1, 0, true>(p, s);
   M3_TILE_LIST(M3_X)
+  M3_SMALL_TILE_LIST(M3_X)
 #undef M3_X
   return cudaErrorInvalidValue;
 }

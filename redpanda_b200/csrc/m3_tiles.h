@@ -27,3 +27,17 @@
   X(16, 0, 2, 2, 128, 0)   /* N=64, no tracking                               */ \
   X(8, 8, 2, 2, 128, 0)    /* fallback: up to 32 rot + 32 track               */ \
   X(16, 16, 1, 0, 128, 0)  /* fallback: up to 64 rot + 64 track               */
+
+// Small-batch tilings: the same lane splits with 2 channels per thread in the
+// forward (64-channel tiles) and 128-thread backward CTAs, used when the
+// regular tiling would give the scan fewer CTAs than the GPU has SMs (config 0
+// at B=8; a search priming one board).  A cell's arithmetic and the y / dΔ /
+// du reductions depend only on the lane split (R, T), so y, the checkpoints,
+// the final state, dΔ and du are the same bits under both tilings; dB/dC
+// (summed over channel tiles) and dA (over batch groups) follow the tiling's
+// partition and agree within rounding.  Same X(R, T, NDF, NDB, NTHB, GS)
+// fields as M3_TILE_LIST.
+#define M3_SMALL_TILE_LIST(X) \
+  X(3, 1, 2, 2, 128, 0)    /* N=16, 12 rot + 4 track (config 0)               */ \
+  X(4, 4, 2, 2, 128, 1)    /* N=32, 16 rot + 16 track                         */ \
+  X(6, 2, 2, 2, 128, 0)    /* N=32, 24 rot + 8 track (config 3)               */
