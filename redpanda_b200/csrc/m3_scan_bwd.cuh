@@ -107,13 +107,27 @@ struct BwdCfg {
   // (the host admits N*p <= 4*NP)
   static constexpr size_t dtr_bytes = PRO ? 2 * (size_t)KC * DT * 2 : 0;
   static constexpr size_t xraw_bytes = PRO ? 2 * 2 * (size_t)KC * 4 * NP * 2 : 0;
-  static constexpr size_t smem_bytes =
+  static constexpr size_t base_bytes =
       dtr_bytes + xraw_bytes +
       3 * 2 * raw_bytes                       // delta, u, dy (HBM dtype), double-buffered
       + 2 * (size_t)DT * NP * 4               // checkpoint tile, double-buffered
       + 2 * 2 * (size_t)KC * NP * 4           // B, C (fp32), double-buffered
       + red_floats * 4 + gs_floats * 4
-      + braw_floats * 4 + scr_floats * 4
+      + braw_floats * 4 + scr_floats * 4;
+  // dA/dtrack totals: each thread's fp32 register sums of one row (both
+  // directions, every step) are folded into its own float64 totals here when
+  // the CTA moves to its next row, so the parameter gradients carry the
+  // rounding of one row's fp32 sum instead of one sequential fp32 sum over
+  // every (row, step) of the CTA (tens of thousands of terms at large batch;
+  // measured at B=2048: 1.2-1.4e-6 of float64 without it).  Once per row
+  // costs ~0.2 % of the kernel; once per chunk measured 7 %.  [pair][thread]
+  // double2 layout (conflict-free 16-byte accesses).  Tilings whose shared
+  // memory cannot hold it keep the fp32 register sums.
+  static constexpr int NPAIR = NDP * (2 * (R > 0 ? R : 1) + (T > 0 ? T : 1));
+  static constexpr size_t acc_bytes = (size_t)NPAIR * NTH * 16;
+  static constexpr bool F64ACC = base_bytes + acc_bytes + 32 <= 227 * 1024;
+  static constexpr size_t smem_bytes =
+      base_bytes + (F64ACC ? acc_bytes : 0)
       + 32;                                   // TMEM address slot, 3 mbarriers (BULK)
 };
 
@@ -186,7 +200,9 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK, PRO>::CPS
   float* s_gs = s_red + CF::red_floats;                              // [FL][ND][2][SG]
   float* s_braw = s_gs + CF::gs_floats;                              // [2][B|C][KC][NP] (BULK)
   float* s_scr = s_braw + CF::braw_floats;                           // [KC][DT][2] (BULK)
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_scr + CF::scr_floats);
+  double2* s_acc = reinterpret_cast<double2*>(s_scr + CF::scr_floats);   // [NPAIR][NTH] (F64ACC)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(
+      reinterpret_cast<unsigned char*>(s_acc) + (CF::F64ACC ? CF::acc_bytes : 0));
   uint64_t* s_bar = reinterpret_cast<uint64_t*>(s_tmem) + 1;          // [3] (BULK)
 
   const int tid = threadIdx.x, q = tid & 3, grp = tid >> 2;
@@ -257,6 +273,32 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK, PRO>::CPS
     for (int j = 0; j < RR; ++j) { gAr[k][j] = f2(0.f); gAi[k][j] = f2(0.f); }
 #pragma unroll
     for (int j = 0; j < TT; ++j) gTk[k][j] = f2(0.f);
+  }
+
+  // the thread's accumulator pairs in a fixed order: gAr, gAi, gTk
+  auto acc_pair = [&](int i) -> float2& {
+    constexpr int NR2 = NDP * RR;
+    if (i < NR2) return gAr[i / RR][i % RR];
+    if (i < 2 * NR2) return gAi[(i - NR2) / RR][(i - NR2) % RR];
+    return gTk[(i - 2 * NR2) / TT][(i - 2 * NR2) % TT];
+  };
+  // add the fp32 chunk sums to the float64 totals and restart them from zero
+  auto fold_acc = [&]() {
+    if constexpr (CF::F64ACC) {
+#pragma unroll
+      for (int i = 0; i < CF::NPAIR; ++i) {
+        float2& a = acc_pair(i);
+        double2 t = s_acc[i * NTH + tid];
+        t.x += (double)a.x;
+        t.y += (double)a.y;
+        s_acc[i * NTH + tid] = t;
+        a = f2(0.f);
+      }
+    }
+  };
+  if constexpr (CF::F64ACC) {
+#pragma unroll
+    for (int i = 0; i < CF::NPAIR; ++i) s_acc[i * NTH + tid] = make_double2(0.0, 0.0);
   }
 
   const int cta = gt * p.Bg + bg;
@@ -926,6 +968,7 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK, PRO>::CPS
       }
     }
     if (fail) break;
+    if (c == 0 && pass == ndirs - 1) fold_acc();   // the row's last work item
     if constexpr (!BULK) {
       if (more) store_bc(buf ^ 1);
     }
@@ -933,7 +976,14 @@ __global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK, PRO>::CPS
   cp_async_wait0();
   if (fail && tid == 0) set_err(p.err, M3_ERR_DEVICE);
 
-  // dA partial of this batch group
+  // dA partial of this batch group (F64ACC: the float64 totals, rounded once)
+  if constexpr (CF::F64ACC) {
+#pragma unroll
+    for (int i = 0; i < CF::NPAIR; ++i) {
+      const double2 t = s_acc[i * NTH + tid];
+      acc_pair(i) = make_float2((float)t.x, (float)t.y);
+    }
+  }
 #pragma unroll
   for (int k = 0; k < ND; ++k) {
     const int d = dbase + k;
