@@ -5,6 +5,17 @@
 #include <stddef.h>
 #include <stdint.h>
 
+// M3_GS_CHUNK: steps per backward chunk (= forward checkpoint interval) of the
+// tilings that keep the gates in Tensor Memory; M3_BWD_MIN_BLOCKS caps the
+// backward's CTAs per SM the compiler budgets registers for (0: as many as
+// Tensor Memory allows).  Tuning knobs; the defaults are the measured best.
+#ifndef M3_GS_CHUNK
+#define M3_GS_CHUNK 8
+#endif
+#ifndef M3_BWD_MIN_BLOCKS
+#define M3_BWD_MIN_BLOCKS 0
+#endif
+
 namespace m3 {
 
 // Per-thread lane tiling: R rotational + T tracking lanes per channel, ND
@@ -13,7 +24,7 @@ struct Tile {
   int R, T, ND;      // ND: channels per thread in the forward and step kernels
   int NDB, NTHB;     // backward: channels per thread, threads per CTA
   int GS;            // backward keeps the gates in Tensor Memory (8-step chunks)
-  int cki() const { return GS ? 8 : 16; }      // checkpoint interval = backward chunk
+  int cki() const { return GS ? M3_GS_CHUNK : 16; }   // checkpoint interval = backward chunk
   // Tensor Memory columns of one backward CTA (the kernel's BwdCfg::NCOLS) and
   // the backward CTAs that fit on one SM by Tensor Memory (512 columns)
   int bwd_cols() const {

@@ -67,7 +67,7 @@ constexpr int pow2ceil(int x) {
 template <int R, int T, int ND, int NTH, bool GS, bool BULK, bool PRO = false>
 struct BwdCfg {
   static_assert(ND % 2 == 0, "the backward processes channel pairs");
-  static constexpr int KC = GS ? 8 : kCK;           // chunk length (= checkpoint interval)
+  static constexpr int KC = GS ? M3_GS_CHUNK : kCK; // chunk length (= checkpoint interval)
   static constexpr int NL = R + T;
   static constexpr int NP = 4 * NL;
   static constexpr int NG = NTH / 4;                // channel groups
@@ -169,7 +169,10 @@ __device__ __forceinline__ float tile_at(const unsigned char* base, bool bf16, i
 // DU, DY: element types of delta/u and of dy fixed at compile time (0 fp32,
 // 1 bf16), or -1 to read them from the parameters (element-wise staging path).
 template <int R, int T, int ND, int NTH, bool GS, bool BULK, int DU, int DY, bool PRO = false>
-__global__ void __launch_bounds__(NTH, BwdCfg<R, T, ND, NTH, GS, BULK, PRO>::CPS)
+__global__ void __launch_bounds__(
+    NTH, (M3_BWD_MIN_BLOCKS > 0 && M3_BWD_MIN_BLOCKS < BwdCfg<R, T, ND, NTH, GS, BULK, PRO>::CPS)
+             ? M3_BWD_MIN_BLOCKS
+             : BwdCfg<R, T, ND, NTH, GS, BULK, PRO>::CPS)
     scan_bwd_kernel(const BwdParams p, const __grid_constant__ CUtensorMap tm_dl,
                     const __grid_constant__ CUtensorMap tm_u,
                     const __grid_constant__ CUtensorMap tm_dy,
