@@ -335,23 +335,32 @@ def run_m3(args):
     # duplex, so both directions overlap the compute and each other).  The
     # parameter grads of the sub-batches are summed on the device and read back
     # once per step.  All copies are inside the timed region.
-    nsub = 4 if B_RANK % 4 == 0 and B_RANK >= 64 else 1
+    nsub = args.e2e_sub if B_RANK % args.e2e_sub == 0 and B_RANK >= 16 * args.e2e_sub else 1
     bsub = B_RANK // nsub
     splan = plan if nsub == 1 else ScanPlan(bsub, L, D, N, N_ROT, bf, bf, S.M3_DIR_BIDIR)
     sckpt = ckpt if nsub == 1 else torch.empty(splan.ckpt_floats(), device=dev)
     sws = ws if nsub == 1 else torch.empty(splan.workspace_bytes(), device=dev, dtype=torch.uint8)
     gsub = torch.empty_like(gflat)
+    # the parameter grads of a step are summed into one of two device buffers
+    # (alternating steps) and read back on a stream of their own, so the
+    # compute stream never queues behind a device->host copy
+    gsum = [torch.empty_like(gflat) for _ in range(2)]
     host = {k: v.cpu().pin_memory() for k, v in x.items()}
     dbufs = [{k: torch.empty((bsub,) + tuple(v.shape[1:]), dtype=v.dtype, device=dev)
               for k, v in x.items()} for _ in range(2)]
     outs_dev = {"y": y, "d_delta": gd, "d_u": gu, "d_Bc": gB, "d_Cc": gC}
     outs_host = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in outs_dev.items()}
-    gout = torch.empty(gflat.shape, dtype=gflat.dtype).pin_memory()
+    gout = [torch.empty(gflat.shape, dtype=gflat.dtype).pin_memory() for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = sum(v.numel() * v.element_size() for v in outs_host.values()) + \
-        gout.numel() * gout.element_size()
+        gout[0].numel() * gout[0].element_size()
     copy_stream = torch.cuda.Stream(dev)
     out_stream = torch.cuda.Stream(dev)
+    grad_stream = torch.cuda.Stream(dev)
+    summed = [torch.cuda.Event() for _ in range(2)]
+    gread = [torch.cuda.Event() for _ in range(2)]
+    gread_used = [False, False]
+    nstep = [0]
     copied = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     computed = [torch.cuda.Event() for _ in range(nsub)]
@@ -386,12 +395,24 @@ def run_m3(args):
                        inp["dy"], sckpt, gd[rows], gu[rows], gB[rows], gC[rows],
                        gsub[0], gsub[1], gsub[2], sws)
         computed[j].record(stream)
+        par = nstep[0] & 1
+        acc = gsum[par]
         if j == 0:
-            gflat.copy_(gsub)
+            if gread_used[par]:
+                stream.wait_event(gread[par])   # read back two steps ago
+            acc.copy_(gsub)
         else:
-            gflat.add_(gsub)
-        if j == nsub - 1 and world > 1:
-            dist.all_reduce(gflat)
+            acc.add_(gsub)
+        if j == nsub - 1:
+            if world > 1:
+                dist.all_reduce(acc)
+            summed[par].record(stream)
+            grad_stream.wait_event(summed[par])
+            with torch.cuda.stream(grad_stream):
+                gout[par].copy_(acc, non_blocking=True)
+                gread[par].record(grad_stream)
+            gread_used[par] = True
+            nstep[0] += 1
 
     def e2e_run(k_steps, start_event=None):
         if start_event is not None:
@@ -407,10 +428,11 @@ def run_m3(args):
             sub_step(dbufs[slot], j)
             consumed[slot].record(stream)
             d2h_copy(j)
-            if j == nsub - 1:
-                gout.copy_(gflat, non_blocking=True)
         for j in range(nsub):   # the timed region ends when every result is on the host
             stream.wait_event(returned[j])
+        for par in range(2):
+            if gread_used[par]:
+                stream.wait_event(gread[par])
 
     e2e_run(max(1, args.warmup))
     barrier()
@@ -421,7 +443,9 @@ def run_m3(args):
     e2e_ms = max_over_ranks(t0.elapsed_time(t1))
     e2e_value = tokens / (e2e_ms / 1e3) / 1e9
     # the host copies hold the device results bit for bit (last step's rows)
-    e2e_check = all(torch.equal(outs_host[k], v.cpu()) for k, v in outs_dev.items())
+    last = (nstep[0] - 1) & 1
+    e2e_check = (all(torch.equal(outs_host[k], v.cpu()) for k, v in outs_dev.items())
+                 and torch.equal(gout[last], gsum[last].cpu()))
 
     # every rank runs the config-3 rollouts on its share of the rows and the
     # config-4 model-level training step on its share of the global batch (in
@@ -1064,6 +1088,10 @@ def main():
                     help="layers of the config-3 rollout (default 12; fewer for profiler captures)")
     ap.add_argument("--rollout-batch", type=int, default=8192,
                     help="rollout rows (default 8192; fewer for profiler captures)")
+    ap.add_argument("--e2e-sub", type=int, default=16,
+                    help="sub-batches the end-to-end leg streams each step's rows in "
+                         "(default 16: measured 130 ms/step at 8192 rows against 147 with 4 "
+                         "and 137 with 8; the copies then run near the PCIe limit)")
     ap.add_argument("--batch", type=int, default=0,
                     help="rows per GPU (default: config 4's global 8192 rows split over "
                          "the GPUs; smaller values are for profiler captures only)")
