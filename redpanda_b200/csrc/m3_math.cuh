@@ -49,6 +49,14 @@ __device__ __forceinline__ float gate_exp(float dl, float a2) {
   return ex2_approx(__fmul_rn(dl, a2));
 }
 
+// v with its sign flipped when k = j - kMagic is odd.  The low mantissa bit of
+// j is the parity of k, so adding (bits(j) << 31) to the bits of v flips the
+// sign bit exactly when k is odd (the carry out of bit 31 is dropped): a
+// single shift-add.
+__device__ __forceinline__ float flip_odd(float v, float j) {
+  return __uint_as_float(__float_as_uint(v) + (__float_as_uint(j) << 31));
+}
+
 // |k| > 2048: cos / sin of the exact product in double precision.  cos is
 // evaluated by the same call in both helpers, so the forward's and the
 // backward's gates agree bit for bit on this path too.
@@ -76,8 +84,7 @@ __device__ __forceinline__ float gate_cos(float dl, float ai) {
   p = __fmaf_rn(p, s, 0x1.555548p-5f);
   p = __fmaf_rn(p, s, -0.5f);
   p = __fmaf_rn(p, s, 1.0f);
-  const unsigned odd = __float_as_uint(j) << 31;   // k odd -> negate
-  return __uint_as_float(__float_as_uint(p) ^ odd);
+  return flip_odd(p, j);   // k odd -> negate
 }
 
 // ---------------------------------------------------------------------------
@@ -106,8 +113,7 @@ __device__ __forceinline__ float2 gate_cos2_nocheck(float2 dl, float2 ai) {
   p = __ffma2_rn(p, s, f2(0x1.555548p-5f));
   p = __ffma2_rn(p, s, f2(-0.5f));
   p = __ffma2_rn(p, s, f2(1.0f));
-  return make_float2(__uint_as_float(__float_as_uint(p.x) ^ (__float_as_uint(j.x) << 31)),
-                     __uint_as_float(__float_as_uint(p.y) ^ (__float_as_uint(j.y) << 31)));
+  return make_float2(flip_odd(p.x, j.x), flip_odd(p.y, j.y));
 }
 
 // sin and cos of dl*ai with the reduction by pi: both share the sign (-1)^k,
@@ -140,35 +146,54 @@ __device__ __forceinline__ void gate_sincos_pi(float dl, float ai, float& sn, fl
   p = __fmaf_rn(p, s, 0x1.555548p-5f);
   p = __fmaf_rn(p, s, -0.5f);
   p = __fmaf_rn(p, s, 1.0f);
-  const unsigned odd = __float_as_uint(j) << 31;
-  cs = __uint_as_float(__float_as_uint(p) ^ odd);
-  sn = __uint_as_float(__float_as_uint(sin_poly(r, s)) ^ odd);
+  cs = flip_odd(p, j);
+  sn = flip_odd(sin_poly(r, s), j);
 }
 
-__device__ __forceinline__ void gate_sincos2_nocheck(float2 dl, float2 ai, float2& sn, float2& cs) {
+// Reduction by pi and both polynomials for two cells, before the sign:
+// cos(dl*ai) = (-1)^k p and sin(dl*ai) = (-1)^k q, k's parity in the low bit of j.
+__device__ __forceinline__ void sincos_reduced2(float2 dl, float2 ai, float2& j, float2& p,
+                                                float2& q) {
   const float2 x = __fmul2_rn(dl, ai);
-  const float2 j = __ffma2_rn(x, f2(kInvPi), f2(kMagic));
+  j = __ffma2_rn(x, f2(kInvPi), f2(kMagic));
   const float2 k = __fadd2_rn(j, f2(-kMagic));
   float2 r = __ffma2_rn(dl, ai, __fmul2_rn(k, f2(-kPiA)));
   r = __ffma2_rn(k, f2(-kPiB), r);
   const float2 s = __fmul2_rn(r, r);
-  float2 p = f2(-0x1.181966p-22f);
+  p = f2(-0x1.181966p-22f);
   p = __ffma2_rn(p, s, f2(0x1.9f720cp-16f));
   p = __ffma2_rn(p, s, f2(-0x1.6c1396p-10f));
   p = __ffma2_rn(p, s, f2(0x1.555548p-5f));
   p = __ffma2_rn(p, s, f2(-0.5f));
   p = __ffma2_rn(p, s, f2(1.0f));
-  float2 q = f2(-0x1.9a6850p-26f);
+  q = f2(-0x1.9a6850p-26f);
   q = __ffma2_rn(q, s, f2(0x1.71707ep-19f));
   q = __ffma2_rn(q, s, f2(-0x1.a017dap-13f));
   q = __ffma2_rn(q, s, f2(0x1.11110cp-7f));
   q = __ffma2_rn(q, s, f2(-0x1.555556p-3f));
   q = __ffma2_rn(__fmul2_rn(r, s), q, r);
-  const unsigned ox = __float_as_uint(j.x) << 31, oy = __float_as_uint(j.y) << 31;
-  cs = make_float2(__uint_as_float(__float_as_uint(p.x) ^ ox),
-                   __uint_as_float(__float_as_uint(p.y) ^ oy));
-  sn = make_float2(__uint_as_float(__float_as_uint(q.x) ^ ox),
-                   __uint_as_float(__float_as_uint(q.y) ^ oy));
+}
+
+// The backward's two gate values of two cells, g = exp(dl*ar)*cos(dl*ai) and
+// es = exp(dl*ar)*sin(dl*ai), without the large-argument check (|dl*ai| <=
+// kFastArgBound).  The sign (-1)^k is put on the exponential once instead of
+// on both polynomials; round-to-nearest is symmetric in the sign, so g equals
+// gate_exp2(dl, a2) * gate_cos2_nocheck(dl, ai) bit for bit.
+__device__ __forceinline__ void gate_es2_nocheck(float2 dl, float2 a2, float2 ai, float2& g,
+                                                 float2& es) {
+  float2 j, p, q;
+  sincos_reduced2(dl, ai, j, p, q);
+  const float2 e = gate_exp2(dl, a2);
+  const float2 se = make_float2(flip_odd(e.x, j.x), flip_odd(e.y, j.y));
+  g = __fmul2_rn(se, p);
+  es = __fmul2_rn(se, q);
+}
+
+__device__ __forceinline__ void gate_sincos2_nocheck(float2 dl, float2 ai, float2& sn, float2& cs) {
+  float2 j, p, q;
+  sincos_reduced2(dl, ai, j, p, q);
+  cs = make_float2(flip_odd(p.x, j.x), flip_odd(p.y, j.y));
+  sn = make_float2(flip_odd(q.x, j.x), flip_odd(q.y, j.y));
 }
 
 // Largest |dl * ai| for which the packed no-check path is exact-equivalent.

@@ -615,17 +615,17 @@ __global__ void __launch_bounds__(
           for (int j = 0; j < R; ++j) {
             float2 g;
             if constexpr (GS) {
-              const float2 e = gate_exp2(dl2, A2[kp][j]);
-              float2 sn, cs;
               if constexpr (FAST) {
-                gate_sincos2_nocheck(dl2, AI[kp][j], sn, cs);
+                gate_es2_nocheck(dl2, A2[kp][j], AI[kp][j], g, GG[kp][j][1]);
               } else {
+                const float2 e = gate_exp2(dl2, A2[kp][j]);
+                float2 sn, cs;
                 gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
                 gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
+                g = __fmul2_rn(e, cs);
+                GG[kp][j][1] = __fmul2_rn(e, sn);
               }
-              g = __fmul2_rn(e, cs);
               GG[kp][j][0] = g;
-              GG[kp][j][1] = __fmul2_rn(e, sn);
             } else if constexpr (FAST) {
               g = __fmul2_rn(gate_exp2(dl2, A2[kp][j]), gate_cos2_nocheck(dl2, AI[kp][j]));
             } else {
@@ -685,15 +685,13 @@ __global__ void __launch_bounds__(
           if constexpr (GS) {
             g = GG[kp][j][0];
             es = GG[kp][j][1];
+          } else if constexpr (FAST) {
+            gate_es2_nocheck(dl2, A2[kp][j], AI[kp][j], g, es);
           } else {
             const float2 e = gate_exp2(dl2, A2[kp][j]);
             float2 sn, cs;
-            if constexpr (FAST) {
-              gate_sincos2_nocheck(dl2, AI[kp][j], sn, cs);
-            } else {
-              gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
-              gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
-            }
+            gate_sincos_pi(dl2.x, AI[kp][j].x, sn.x, cs.x);
+            gate_sincos_pi(dl2.y, AI[kp][j].y, sn.y, cs.y);
             g = __fmul2_rn(e, cs);
             es = __fmul2_rn(e, sn);
           }
