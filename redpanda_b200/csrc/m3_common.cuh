@@ -110,6 +110,33 @@ __device__ __forceinline__ float quad_sum(float s) {
   return s;
 }
 
+// quad_sum() of ND channel partials at once, transposed: each round keeps
+// the channels of its own lane bit and adds the partner's copy of them, so
+// quarter q ends with the totals of its channels k = 4i + q in v[i] (ND >= 4;
+// ND = 2: quarters 0/2 hold channel 0 and 1/3 channel 1 in v[0]).  Every total
+// is summed in quad_sum()'s order (s0+s1)+(s2+s3), so the bits are the same.
+template <int ND>
+__device__ __forceinline__ void quad_sum_t(float (&v)[ND], int q) {
+  static_assert(ND % 2 == 0, "channel pairs");
+  const int b0 = q & 1, b1 = (q >> 1) & 1;
+#pragma unroll
+  for (int i = 0; i < ND / 2; ++i) {
+    const float keep = b0 ? v[2 * i + 1] : v[2 * i];
+    const float send = b0 ? v[2 * i] : v[2 * i + 1];
+    v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 1));
+  }
+  if constexpr (ND >= 4) {
+#pragma unroll
+    for (int i = 0; i < ND / 4; ++i) {
+      const float keep = b1 ? v[2 * i + 1] : v[2 * i];
+      const float send = b1 ? v[2 * i] : v[2 * i + 1];
+      v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+    }
+  } else {
+    v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], 2));
+  }
+}
+
 // Per-thread channel partial of y: sum_j H_j * C_j over the thread's lanes in
 // the fixed order rotational lanes first, then tracking lanes.
 template <int NL>

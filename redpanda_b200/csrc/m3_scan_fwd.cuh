@@ -470,11 +470,16 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
           }
         }
         const size_t yrow = ((size_t)b * L + t) * D;
+        // channel totals over the 4 quarters; quarter q writes channels k = 4i + q
+        constexpr int NY = ND >= 4 ? ND / 4 : 1;   // channels written per thread
+        if constexpr (ND % 2 == 0) quad_sum_t<ND>(reinterpret_cast<float(&)[ND]>(part), q);
+        else part[0] = quad_sum(part[0]);
 #pragma unroll
-        for (int k = 0; k < ND; ++k) {
-          const float tot = __fmul_rn(0.5f, quad_sum(part[k]));
+        for (int i = 0; i < NY; ++i) {
+          const int k = ND >= 4 ? 4 * i + q : q;
+          const float tot = __fmul_rn(0.5f, part[i]);
           const int d = dbase + k;
-          if ((k & 3) == q && d < D) {
+          if (k < ND && d < D) {
             float v = tot;
             if (accumulate) {
               // BULK with a bf16 y: the staged first-pass rows are bf16
