@@ -303,12 +303,12 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
         }
         return;
       }
+      const float* rb0 = s_braw + (size_t)(buf * 2 + 0) * kCK * NP;
+      const float* rc0 = s_braw + (size_t)(buf * 2 + 1) * kCK * NP;
       for (int i = tid; i < ns * NP; i += kThreads) {
         const int tt = i / NP, ln = i - tt * NP;
         const int n = LM::mem_lane(ln / NL, ln % NL, p.NR, p.NT);
         const size_t r = (size_t)(dir ? ns - 1 - tt : tt) * N + (n >= 0 ? n : 0);
-        const float* rb0 = s_braw + (size_t)(buf * 2 + 0) * kCK * NP;
-        const float* rc0 = s_braw + (size_t)(buf * 2 + 1) * kCK * NP;
         s_b[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rb0, r, p.dt_bc) : 0.f);
         s_c[buf * kCK * NP + i] = f2(n >= 0 ? ld_f(rc0, r, p.dt_bc) : 0.f);
       }
@@ -404,11 +404,10 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
           Cv[j] = bc[tt * NP + q * NL + j];
         }
         const bool last = STATE && !FASTC && (s == L - 1) && (p.h_last != nullptr);
-        float du[ND], mdl = 0.f;
+        float mdl = 0.f;
+        if constexpr (!FASTC) {
 #pragma unroll
-        for (int k = 0; k < ND; ++k) {
-          du[k] = __fmul_rn(dl[k], uu[k]);
-          if constexpr (!FASTC) mdl = fmaxf(mdl, fabsf(dl[k]));
+          for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
         }
         float part[2 * NDP];
         if (FASTC || ((ND % 2 == 0) && !last && __fmul_rn(mdl, maxai) <= kFastArgBound)) {
@@ -416,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
 #pragma unroll
           for (int kp = 0; kp < NDP; ++kp) {
             const float2 dl2 = make_float2(dl[2 * kp], dl[(2 * kp + 1) % ND]);
-            const float2 du2 = make_float2(du[2 * kp], du[(2 * kp + 1) % ND]);
+            const float2 du2 = __fmul2_rn(dl2, make_float2(uu[2 * kp], uu[(2 * kp + 1) % ND]));
             float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
             for (int j = 0; j < R; ++j) {
@@ -434,6 +433,9 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
           }
         } else {
           // scalar path: per-cell range checks (large arguments, the last step)
+          float du[ND];
+#pragma unroll
+          for (int k = 0; k < ND; ++k) du[k] = __fmul_rn(dl[k], uu[k]);
           float Cs[NL];
 #pragma unroll
           for (int j = 0; j < NL; ++j) Cs[j] = Cv[j].x;
@@ -497,11 +499,25 @@ __global__ void __launch_bounds__(kThreads, M3_FWD_MIN_BLOCKS)
       bool chunk_fast = false;
       if constexpr (ND % 2 == 0) {
         float mdl = 0.f;
-        for (int tt = 0; tt < ns; ++tt) {
-          float dl[ND];
-          read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * esz, bf16, dl);
+        if (bf16) {
+          // bf16 rows: |x| orders like the unsigned bits x & 0x7fff, so the
+          // maximum is taken on packed 16-bit halves of the raw words (a NaN
+          // sorts above every number and selects the checked path)
+          uint32_t m = 0;
+          for (int tt = 0; tt < ns; ++tt) {
+            const uint32_t* w =
+                reinterpret_cast<const uint32_t*>(bdl + (size_t)(tt * DT + grp * ND) * 2);
 #pragma unroll
-          for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
+            for (int i = 0; i < ND / 2; ++i) m = max_u16x2(m, w[i] & 0x7fff7fffu);
+          }
+          mdl = __uint_as_float(max(m & 0xffffu, m >> 16) << 16);
+        } else {
+          for (int tt = 0; tt < ns; ++tt) {
+            float dl[ND];
+            read_chan<ND>(bdl + (size_t)(tt * DT + grp * ND) * 4, false, dl);
+#pragma unroll
+            for (int k = 0; k < ND; ++k) mdl = fmaxf(mdl, fabsf(dl[k]));
+          }
         }
         chunk_fast = __fmul_rn(mdl, maxai) <= kFastArgBound;
       }

@@ -33,6 +33,13 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool va
                : "memory");
 }
 
+// Lane-wise maximum of two pairs of unsigned 16-bit integers.
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // ND channel values of one staged row, converted to fp32.
 template <int ND>
 __device__ __forceinline__ void read_chan(const unsigned char* base, bool bf16, float (&v)[ND]) {
