@@ -459,6 +459,7 @@ def run_m3(args):
     sweep_info = run_l_sweep(dev, args) if (args.sweep and rank == 0) else None
     configs_info = run_configs(dev, args, clocks) if (args.configs and rank == 0) else None
     eval_info = run_model_eval(dev, args) if (args.model_train and rank == 0) else None
+    node_info = run_search_nodes(dev, args) if (args.rollout and rank == 0) else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -521,6 +522,8 @@ def run_m3(args):
             line["configs"] = configs_info
         if eval_info is not None:
             line["model_eval"] = eval_info
+        if node_info is not None:
+            line["search_nodes"] = node_info
         if sweep_info is not None:
             line["l_sweep"] = {"workload": "c4 sequence-length sweep: bidirectional scan "
                                            "fwd+bwd, c2 layer shape, bf16, 1 GPU",
@@ -957,6 +960,94 @@ def run_model_train(dev, args, mp):
         torch.backends.cuda.matmul.allow_tf32 = old_tf32
 
 
+def run_search_nodes(dev, args):
+    """Search node evaluation at batch 1 (SearchMamba.eval_step,
+    search_mamba.py:275-291, as MARS calls it per node): a config-3-shaped
+    SearchMamba (12 layers, d_model=512, d_inner=1024, d_state=32 with 8
+    tracking lanes, mimo_p=2, vocab 8192) primed on a 64-token board, then a
+    chain of single-move evaluations, each returning the value as a Python
+    float (a host sync per node, as the reference's ``.item()``).  Eager
+    (``eval_step``: the stack's launches one by one) against the stack and both
+    heads replayed as one CUDA graph (``eval_step_graphed``).  TF32 projections."""
+    import torch
+    from redpanda_b200.search_mamba import SearchMamba, SearchMambaConfig
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        torch.manual_seed(31)
+        scfg = SearchMambaConfig(d_model=512, n_layer=12, d_state=32, n_track_state=8,
+                                 mimo_p=2, vocab_size=8192)
+        sm = SearchMamba(scfg, vocab_size=8192).to(dev).eval()
+        g = torch.Generator(dev).manual_seed(37)
+        board = torch.randint(0, 8192, (64,), device=dev, generator=g)
+        moves = torch.randint(0, 8192, (64,), generator=torch.Generator().manual_seed(41)).tolist()
+        out = {}
+        with torch.no_grad():
+            _, cache0 = sm.prime_board(board)
+            for name, fn in (("eager", sm.eval_step), ("graph", sm.eval_step_graphed)):
+                cache = cache0
+                for mv in moves[:8]:   # warm-up (captures the graph)
+                    _, _, cache = fn(cache, mv)
+                torch.cuda.synchronize(dev)
+                t0 = time.perf_counter()
+                cache = cache0
+                for mv in moves:
+                    _, _, cache = fn(cache, mv)
+                torch.cuda.synchronize(dev)
+                dt = time.perf_counter() - t0
+                out[name] = {"us_per_node": dt / len(moves) * 1e6,
+                             "nodes_per_s": len(moves) / dt}
+        sm.release_graphs()
+        # the backbone's step graph alone by batch, with the prologue inside the
+        # step kernel and as its own launch (Mamba3Block.fuse_step)
+        from redpanda_b200.graphs import StepGraph
+        from redpanda_b200.mamba import Mamba3Block
+        sweep = {}
+        try:
+            for B in (1, 64, 256, 1024, 4096):
+                ids = torch.randint(0, 8192, (B, 16), device=dev, generator=g)
+                mv = torch.randint(0, 8192, (B,), device=dev, generator=g)
+                for fuse in (True, False):
+                    Mamba3Block.fuse_step = fuse
+                    old_max = Mamba3Block.fuse_step_max_batch
+                    Mamba3Block.fuse_step_max_batch = 1 << 30
+                    with torch.no_grad():
+                        gr = StepGraph(sm.backbone, B)
+                        sm.backbone.prime_cache(ids, out=gr.cache)
+                        for _ in range(3):
+                            gr.step(mv)
+                        torch.cuda.synchronize(dev)
+                        e0 = torch.cuda.Event(enable_timing=True)
+                        e1 = torch.cuda.Event(enable_timing=True)
+                        n = 30 if B <= 1024 else 10
+                        e0.record()
+                        for _ in range(n):
+                            gr.step(mv)
+                        e1.record()
+                        torch.cuda.synchronize(dev)
+                    Mamba3Block.fuse_step_max_batch = old_max
+                    sweep[f"B{B}_{'fused' if fuse else 'two_launch'}"] = \
+                        e0.elapsed_time(e1) / n * 1e3
+                    del gr
+        finally:
+            Mamba3Block.fuse_step = True
+        del sm
+        torch.cuda.empty_cache()
+        out["workload"] = ("a10 search node evaluation: 12-layer SearchMamba (d_model=512, "
+                           "d_inner=1024, d_state=32 with 8 tracking lanes, mimo_p=2), batch 1, "
+                           "64 chained eval_step calls after a 64-token prime, value read "
+                           "back per node; host wall clock (each node ends in a host sync)")
+        out["speedup"] = out["eager"]["us_per_node"] / out["graph"]["us_per_node"]
+        out["graph_step_us_by_batch"] = sweep
+        out["graph_step_note"] = ("the backbone's 12-layer step as one CUDA graph, us per step "
+                                  "(CUDA events), prologue inside the step kernel vs its own "
+                                  "launch; step_fused_ takes the fused kernel up to "
+                                  "Mamba3Block.fuse_step_max_batch rows")
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old_tf32
+
+
 def run_model_eval(dev, args):
     """The Eval-Mamba stack forward in bf16 (model.py:110-132 / mamba.py:231-267 at
     config 1): the 16-layer bidirectional Mamba of config 4 (d_model=768,
@@ -1042,6 +1133,51 @@ def run_model_rollout(dev, args, mp):
             total = mp.timed(lambda: rollout(record=True))
         anchor = mp.max(sum(ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2)))
         steps_ms = total - anchor
+
+        # the same eager rollout with the step prologue fused into the step
+        # kernel (m3_step_gated_fused; by default only batches of at most
+        # Mamba3Block.fuse_step_max_batch rows take it)
+        from redpanda_b200.mamba import Mamba3Block
+        ev.clear()
+        old_max = Mamba3Block.fuse_step_max_batch
+        Mamba3Block.fuse_step_max_batch = 1 << 30
+        try:
+            with torch.no_grad():
+                rollout()
+                total_u = mp.timed(lambda: rollout(record=True))
+        finally:
+            Mamba3Block.fuse_step_max_batch = old_max
+        anchor_u = mp.max(sum(ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2)))
+        steps_u = total_u - anchor_u
+
+        # the same rollout with the 12-layer step replayed as one CUDA graph
+        # (redpanda_b200.graphs.StepGraph) and each re-anchor primed straight
+        # into the graph's static state
+        from redpanda_b200.graphs import StepGraph
+        ev.clear()
+        torch.cuda.empty_cache()
+        with torch.no_grad():
+            graph = StepGraph(model, Bs)
+
+            def rollout_graph(record=False):
+                for s_ in range(32):
+                    if s_ % 8 == 0:
+                        if record:
+                            ev.append(torch.cuda.Event(enable_timing=True))
+                            ev[-1].record(stream)
+                        model.prime_cache(boards[s_ // 8], out=graph.cache)
+                        if record:
+                            ev.append(torch.cuda.Event(enable_timing=True))
+                            ev[-1].record(stream)
+                    x = graph.step(moves[s_])[0]
+                return x
+
+            rollout_graph()
+            total_g = mp.timed(lambda: rollout_graph(record=True))
+        anchor_g = mp.max(sum(ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2)))
+        steps_g = total_g - anchor_g
+        del graph
+        torch.cuda.empty_cache()
         rows = Bs * mp.world
         return {
             "workload": f"c3 model level: {layers}-layer Mamba (d_model=512, d_inner=1024, "
@@ -1056,6 +1192,16 @@ def run_model_rollout(dev, args, mp):
             "step_only_node_steps_per_s": rows * 32 / (steps_ms / 1e3),
             "precision": "TF32 projections, fp32 state and recurrence",
             "state": "reference (h, dBu) cache pair",
+            "step_ms_fused_prologue": steps_u / 32,
+            "graph": {
+                "node_steps_per_s": rows * 32 / (total_g / 1e3),
+                "ms_per_rollout": total_g,
+                "anchor_ms": anchor_g,
+                "step_ms_per_node_step_batch": steps_g / 32,
+                "launches_per_step": 1,
+                "note": "the 12-layer fused step captured once as a CUDA graph; re-anchors "
+                        "prime into the graph's static state",
+            },
         }
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old_tf32

@@ -17,6 +17,8 @@
  *   redpanda/engine/mamba.py:466-493        Mamba3Block.step recurrence -> m3_step
  *   redpanda/engine/mamba.py:455-469        step inputs (softplus, BCNorm, MIMO fold) -> m3_step_inputs
  *   redpanda/engine/mamba.py:490-497        step + gated output (y + u*D) * silu(z) -> m3_step_gated
+ *   redpanda/engine/mamba.py:455-497        step inputs + step + gated output in one launch
+ *                                           -> m3_step_gated_fused
  *   redpanda/engine/mamba.py:262-265        (y + u*D) * silu(z) after a scan -> m3_gate
  *
  * Shapes (B batch, L length, D = d_inner, N = d_state, n_rot rotational lanes,
@@ -272,6 +274,29 @@ M3_API int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu,
             const void* Bc, const void* Cc, const float* A_real_p, const float* A_imag_p,
             const float* track_p, const float* z, int64_t ld_z, const float* d_skip,
             float* out, void* stream);
+
+/* m3_step_gated with the step's prologue in the same launch (mamba.py:455-497:
+ * softplus(dt_proj), BCNorm of B_raw / C_raw, the MIMO fold, the recurrence and
+ * the gated output): the kernel stages each row's dt and raw x_proj rows and
+ * computes delta, Bc and Cc itself with the arithmetic of m3_step_inputs, so
+ * the state and out are bit-identical to m3_step_inputs followed by
+ * m3_step_gated.
+ *   dt      (B, ld_dt) float32: dt_proj output (bias included), before softplus
+ *   xbc     (B, ld_x) float32: x_proj output; B_raw at column off_b, C_raw at
+ *           off_c, N * mimo_p values each
+ *   wb, wc  (N * mimo_p,) float32 BCNorm weights, or both NULL (plain fold)
+ *   u       (B, D) of desc->dtype_du; desc->dtype_bc must be M3_F32
+ * Served by the pipelined step kernel for dense 32-lane states (N = 32, no
+ * virtual lanes) with D % 32 == 0, mimo_p <= 2, and 16-byte aligned rows of dt,
+ * xbc (ld_x, off_b, off_c multiples of 4), u and the state; any other shape
+ * returns M3_ERR_UNSUPPORTED with nothing launched (run m3_step_inputs and
+ * m3_step_gated instead). */
+M3_API int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* h, float* dbu,
+            const float* fac_prev, float* fac_next, const float* dt, int64_t ld_dt,
+            const float* xbc, int64_t ld_x, int32_t off_b, int32_t off_c, const float* wb,
+            const float* wc, float eps, const void* u, const float* A_real_p,
+            const float* A_imag_p, const float* track_p, const float* z, int64_t ld_z,
+            const float* d_skip, float* out, void* stream);
 
 /* The layer's gated activation after a scan (mamba.py:262-265), elementwise
  * over (rows, D) = (B*L, D):

@@ -71,6 +71,9 @@ SIGNATURES = {
                                      ctypes.c_int64, _P, ctypes.c_float, _P, _I, _P]),
     "m3_step_gated": (ctypes.c_int, [_S, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                      ctypes.c_int64, _P, _P, _P]),
+    "m3_step_gated_fused": (ctypes.c_int, [_S, _I, _P, _P, _P, _P, _P, ctypes.c_int64, _P,
+                                           ctypes.c_int64, _I, _I, _P, _P, ctypes.c_float,
+                                           _P, _P, _P, _P, _P, ctypes.c_int64, _P, _P, _P]),
 }
 
 _lock = threading.Lock()

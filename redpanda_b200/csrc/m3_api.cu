@@ -364,12 +364,21 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 
+// Arguments of the fused prologue (m3_step_gated_fused).
+struct StepPro {
+  const float* dt; int64_t ld_dt;
+  const float* xbc; int64_t ld_x;
+  int32_t off_b, off_c, P;
+  const float* wb; const float* wc;
+  float eps;
+};
+
 static int step_common(const m3_step_desc* desc, float* h, float* dbu, const float* fac_prev,
                        float* fac_next, const void* delta, const void* u, const void* Bc,
                        const void* Cc, const float* A_real_p, const float* A_imag_p,
                        const float* track_p, float* y, void* stream,
                        const float* z = nullptr, int64_t ld_z = 0,
-                       const float* d_skip = nullptr) {
+                       const float* d_skip = nullptr, const StepPro* pro = nullptr) {
   if (!desc) return M3_ERR_NULL;
   if (desc->batch < 1 || desc->d_inner < 1 || desc->d_state < 1 || desc->d_state > kMaxState ||
       desc->n_rot < 0 || desc->n_rot > desc->d_state)
@@ -417,7 +426,15 @@ static int step_common(const m3_step_desc* desc, float* h, float* dbu, const flo
   p.gated = z != nullptr;
   p.z = z; p.ld_z = ld_z; p.d_skip = d_skip;
   p.err = device_err_ptr();
+  if (pro) {   // the fused prologue needs the pipelined kernel on a 32-lane tile
+    if (!p.bulk || desc->d_state != 32) return M3_ERR_UNSUPPORTED;
+    p.pro = 1;
+    p.dt = pro->dt; p.ld_dt = pro->ld_dt; p.xbc = pro->xbc; p.ld_x = pro->ld_x;
+    p.off_b = pro->off_b; p.off_c = pro->off_c; p.P = pro->P;
+    p.wb = pro->wb; p.wc = pro->wc; p.eps = pro->eps;
+  }
   cudaError_t e = launch_step(t, p, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported) return M3_ERR_UNSUPPORTED;
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 
@@ -554,6 +571,35 @@ int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu, const float* f
   if (!aligned(z, 4) || !aligned(d_skip, 4)) return M3_ERR_ALIGN;
   return step_common(desc, h, dbu, fac_prev, fac_next, delta, u, Bc, Cc, A_real_p, A_imag_p,
                      track_p, out, stream, z, ld_z, d_skip);
+}
+
+int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* h, float* dbu,
+                        const float* fac_prev, float* fac_next, const float* dt, int64_t ld_dt,
+                        const float* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
+                        const float* wb, const float* wc, float eps, const void* u,
+                        const float* A_real_p, const float* A_imag_p, const float* track_p,
+                        const float* z, int64_t ld_z, const float* d_skip, float* out,
+                        void* stream) {
+  if (!desc || !z || !d_skip || !dt || !xbc) return M3_ERR_NULL;
+  if ((dbu != nullptr) == (fac_next != nullptr)) return M3_ERR_NULL;   // exactly one state form
+  if ((wb == nullptr) != (wc == nullptr)) return M3_ERR_NULL;
+  if (desc->dtype_bc != M3_F32) return M3_ERR_DTYPE;
+  const int64_t np = (int64_t)desc->d_state * mimo_p;
+  if (ld_z < desc->d_inner || ld_dt < desc->d_inner || mimo_p < 1 || off_b < 0 || off_c < 0 ||
+      off_b + np > ld_x || off_c + np > ld_x || !(eps >= 0.f))
+    return M3_ERR_SHAPE;
+  if (!aligned(z, 4) || !aligned(d_skip, 4) || !aligned(dt, 4) || !aligned(xbc, 4) ||
+      (wb && (!aligned(wb, 4) || !aligned(wc, 4))))
+    return M3_ERR_ALIGN;
+  // every staged row a 16-byte multiple at a 16-byte aligned address
+  if (mimo_p > 2 || np % 4 != 0 || !aligned(dt, 16) || ld_dt % 4 != 0 || !aligned(xbc, 16) ||
+      ld_x % 4 != 0 || off_b % 4 != 0 || off_c % 4 != 0)
+    return M3_ERR_UNSUPPORTED;
+  const StepPro pro{dt, ld_dt, xbc, ld_x, off_b, off_c, mimo_p, wb, wc, eps};
+  // delta/Bc/Cc are not read under the fused prologue; dt and xbc stand in
+  // for the pointer checks (both 16-byte aligned)
+  return step_common(desc, h, dbu, fac_prev, fac_next, dt, u, xbc, xbc, A_real_p, A_imag_p,
+                     track_p, out, stream, z, ld_z, d_skip, &pro);
 }
 
 int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const float* dt, int64_t ld_dt,

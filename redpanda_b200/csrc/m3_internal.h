@@ -106,6 +106,16 @@ struct StepParams {
   int B, D, N, NR, NT;
   int dt_du, dt_bc;
   int* err;
+  // pro: the step's prologue fused into the pipelined kernel -- delta =
+  // softplus(dt) and Bc/Cc = BCNorm + MIMO fold of the raw x_proj rows, with
+  // the device functions of step_inputs_kernel (m3_prologue.cuh); fp32 dt and
+  // rows; `delta`, `Bc`, `Cc` are unused then
+  int pro;
+  const float* dt; long long ld_dt;
+  const float* xbc; long long ld_x;
+  int off_b, off_c, P;
+  const float* wb; const float* wc;
+  float eps;
 };
 
 struct ReduceParams {

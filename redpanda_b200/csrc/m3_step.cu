@@ -29,6 +29,7 @@
 #include "m3_common.cuh"
 #include "m3_internal.h"
 #include "m3_bulk.cuh"
+#include "m3_prologue.cuh"
 #include "m3_tma.h"
 #include "m3_stage.cuh"
 #include "m3_tiles.h"
@@ -327,13 +328,19 @@ constexpr int bulk_stages(bool fact) { return fact ? 5 : 3; }
 // Bc | Cc].  Swizzled (SWZ, 32 lanes = 128-byte tile rows): the two h tiles,
 // then the two S2 parts, then the small rows, padded to 1 KB, so that every
 // state tile starts on the 1024-byte boundary the 128-byte swizzle needs.
-template <int NP, bool FACT, bool SWZ>
+// PRO (prologue fused): the delta slot holds dt, and each row also stages its
+// raw B and C rows of x_proj (N*p fp32 each, p <= 2) after Cc; Bc and Cc are
+// then written by the CTA from the raw rows.  Sized so that the 32-lane tile
+// keeps 4 CTAs per SM (3 stages of 18 KB): a larger stage costs a resident CTA
+// and with it a quarter of the bytes in flight.
+template <int NP, bool FACT, bool SWZ, bool PRO = false>
 struct BulkStage {
   static constexpr int kH = 32 * NP * 4;                        // h tile of one row
   static constexpr int kS2 = FACT ? 32 * 4 + NP * 4 : kH;       // dBu tile, or [du | B]
   static constexpr int kDL = 32 * 4;                            // delta or u (<= fp32)
   static constexpr int kBC = NP * 4;                            // Bc or Cc (<= fp32)
-  static constexpr int kSmall = 2 * kDL + 2 * kBC;
+  static constexpr int kRaw = PRO ? 2 * NP * 4 : 0;             // raw B or C row (fp32)
+  static constexpr int kSmall = 2 * kDL + 2 * kBC + 2 * kRaw;
   static constexpr int kRow = kH + kS2 + kSmall;
   static constexpr int kBytes = SWZ ? (kBulkRows * kRow + 1023) / 1024 * 1024 : kBulkRows * kRow;
   __device__ static constexpr int oH(int r) { return SWZ ? r * kH : r * kRow; }
@@ -344,6 +351,8 @@ struct BulkStage {
   __device__ static constexpr int oU(int r) { return oDL(r) + kDL; }
   __device__ static constexpr int oB(int r) { return oDL(r) + 2 * kDL; }
   __device__ static constexpr int oC(int r) { return oB(r) + kBC; }
+  __device__ static constexpr int oRB(int r) { return oC(r) + kBC; }
+  __device__ static constexpr int oRC(int r) { return oRB(r) + kRaw; }
   static_assert(kS2 % 16 == 0 && kBC % 16 == 0, "bulk copy destinations are 16-byte aligned");
   static_assert(!SWZ || NP * 4 == 128, "the swizzled layout has 128-byte tile rows");
 };
@@ -377,7 +386,7 @@ __device__ __forceinline__ void ld_staged(const unsigned char* base, int off, bo
   else ld_vec<n, vec_width(n)>(reinterpret_cast<const float*>(base) + off, v);
 }
 
-template <int R, int T, bool FACT, bool SWZ>
+template <int R, int T, bool FACT, bool SWZ, bool PRO>
 __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
     step_bulk_kernel(const StepParams p, int pairs_per_cta,
                      const __grid_constant__ CUtensorMap tmap_h,
@@ -388,7 +397,8 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
   constexpr int RR = R > 0 ? R : 1;
   constexpr int TT = T > 0 ? T : 1;
   constexpr int VR = vec_width(RR), VT = vec_width(TT);
-  using SL = BulkStage<NP, FACT, SWZ>;
+  using SL = BulkStage<NP, FACT, SWZ, PRO>;
+  static_assert(!PRO || kThreads == 128, "the fused prologue uses one warp per (row, B|C)");
   constexpr int kBulkStages = bulk_stages(FACT);
   extern __shared__ __align__(128) unsigned char smem_raw[];
   // stage buffers (from the first 1 KB boundary when swizzled), then one
@@ -403,8 +413,9 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
   const int npairs = (p.B + 1) / 2;
   const int pair0 = blockIdx.x * pairs_per_cta;
   const int n = min(pairs_per_cta, npairs - pair0);
-  const bool bf_du = p.dt_du == M3_BF16, bf_bc = p.dt_bc == M3_BF16;
+  const bool bf_du = p.dt_du == M3_BF16, bf_bc = !PRO && p.dt_bc == M3_BF16;
   const int esd = bf_du ? 2 : 4, esb = bf_bc ? 2 : 4;
+  const int np_raw = PRO ? p.N * p.P : 0;   // raw B/C row length (PRO)
 
   float a2[RR], ai[RR], tk[TT];
   float maxai = 0.f;
@@ -429,8 +440,10 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
   }
   __syncthreads();
 
-  const uint32_t row_tx = SL::kH + (FACT ? 32 * 4 + NP * 4 : SL::kH) + 2 * 32 * esd +
-                          2 * NP * esb;
+  // PRO: dt (fp32) and u, then the raw B and C rows instead of Bc and Cc
+  const uint32_t row_tx = SL::kH + (FACT ? 32 * 4 + NP * 4 : SL::kH) +
+                          (PRO ? 32 * 4 + 32 * esd + 2 * np_raw * 4
+                               : 2 * 32 * esd + 2 * NP * esb);
   auto issue = [&](int i) {   // thread 0: stage the row pair pair0 + i
     const int s = i % kBulkStages;
     unsigned char* st = smem + s * SL::kBytes;
@@ -453,10 +466,18 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
       } else {
         bulk_g2s(st + SL::oS2(r), p.dbu + (b * D + d0) * NP, SL::kH, &full[s]);
       }
-      bulk_g2s(st + SL::oDL(r), (const char*)p.delta + (b * D + d0) * esd, 32 * esd, &full[s]);
-      bulk_g2s(st + SL::oU(r), (const char*)p.u + (b * D + d0) * esd, 32 * esd, &full[s]);
-      bulk_g2s(st + SL::oB(r), (const char*)p.Bc + b * NP * esb, NP * esb, &full[s]);
-      bulk_g2s(st + SL::oC(r), (const char*)p.Cc + b * NP * esb, NP * esb, &full[s]);
+      if constexpr (PRO) {
+        bulk_g2s(st + SL::oDL(r), p.dt + b * p.ld_dt + d0, 32 * 4, &full[s]);
+        bulk_g2s(st + SL::oU(r), (const char*)p.u + (b * D + d0) * esd, 32 * esd, &full[s]);
+        bulk_g2s(st + SL::oRB(r), p.xbc + b * p.ld_x + p.off_b, np_raw * 4, &full[s]);
+        bulk_g2s(st + SL::oRC(r), p.xbc + b * p.ld_x + p.off_c, np_raw * 4, &full[s]);
+      } else {
+        bulk_g2s(st + SL::oDL(r), (const char*)p.delta + (b * D + d0) * esd, 32 * esd,
+                 &full[s]);
+        bulk_g2s(st + SL::oU(r), (const char*)p.u + (b * D + d0) * esd, 32 * esd, &full[s]);
+        bulk_g2s(st + SL::oB(r), (const char*)p.Bc + b * NP * esb, NP * esb, &full[s]);
+        bulk_g2s(st + SL::oC(r), (const char*)p.Cc + b * NP * esb, NP * esb, &full[s]);
+      }
     }
   };
 
@@ -470,6 +491,23 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
     const bool ok = mbar_wait(&full[s], (uint32_t)((i / kBulkStages) & 1));
     const int b0 = 2 * (pair0 + i);
     const bool two = b0 + 1 < p.B;
+    if constexpr (PRO) {
+      // Bc / Cc of the pair from the staged raw rows: warp w normalises and
+      // folds (row w/2, B or C) exactly as step_inputs_kernel does (one warp
+      // per row, the same lane order), so the values equal the unfused
+      // chain's; the whole warp takes part (warp-uniform condition)
+      const int w = tid >> 5, lane = tid & 31, r = w >> 1;
+      if (r == 0 || two) {
+        unsigned char* st = smem + s * SL::kBytes;
+        const float* x = reinterpret_cast<const float*>(st + ((w & 1) ? SL::oRC(r) : SL::oRB(r)));
+        const float* wv = (w & 1) ? p.wc : p.wb;
+        auto ld = [&](int k) { return x[k]; };
+        const float rs = bcnorm_scale(ld, np_raw, p.eps, wv != nullptr, lane);
+        float* dst = reinterpret_cast<float*>(st + ((w & 1) ? SL::oC(r) : SL::oB(r)));
+        for (int nn = lane; nn < NP; nn += 32) dst[nn] = bcnorm_fold(ld, nn, p.P, rs, wv);
+      }
+      __syncthreads();
+    }
 
     // ---- staged row pair -> registers (row 0 in .x, row 1 in .y)
     float2 h2[NL], db2[NL], B2[NL], C2[NL], dl2, uu2;
@@ -508,8 +546,12 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
           if constexpr (R > 0) ld_vec<R, VR>(ds + q * R, dv[r]);
           if constexpr (T > 0) ld_vec<T, VT>(ds + 4 * R + q * T, dv[r] + R);
         }
-        dlv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + SL::oDL(r))[grp])
-                       : reinterpret_cast<const float*>(st + SL::oDL(r))[grp];
+        if constexpr (PRO) {   // delta = softplus(dt), as step_inputs_kernel
+          dlv[r] = softplus20(reinterpret_cast<const float*>(st + SL::oDL(r))[grp]);
+        } else {
+          dlv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + SL::oDL(r))[grp])
+                         : reinterpret_cast<const float*>(st + SL::oDL(r))[grp];
+        }
         uv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + SL::oU(r))[grp])
                       : reinterpret_cast<const float*>(st + SL::oU(r))[grp];
         if constexpr (R > 0) {
@@ -625,12 +667,12 @@ bool encode_state_map(CUtensorMap* map, const float* base, size_t rows) {
          CUDA_SUCCESS;
 }
 
-template <int R, int T, bool FACT, bool SWZ>
+template <int R, int T, bool FACT, bool SWZ, bool PRO>
 cudaError_t launch_step_bulk_kernel(const StepParams& p, cudaStream_t stream,
                                     const CUtensorMap& mh, const CUtensorMap& md) {
-  using SL = BulkStage<4 * (R + T), FACT, SWZ>;
+  using SL = BulkStage<4 * (R + T), FACT, SWZ, PRO>;
   constexpr int kBulkStages = bulk_stages(FACT);
-  auto kern = step_bulk_kernel<R, T, FACT, SWZ>;
+  auto kern = step_bulk_kernel<R, T, FACT, SWZ, PRO>;
   const int smem = kBulkStages * SL::kBytes + kBulkStages * (int)sizeof(uint64_t) +
                    (SWZ ? 1024 : 0);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -656,8 +698,8 @@ cudaError_t launch_step_bulk_kernel(const StepParams& p, cudaStream_t stream,
 }
 
 
-template <int R, int T, bool FACT>
-cudaError_t launch_step_bulk_impl(const StepParams& p, cudaStream_t stream) {
+template <int R, int T, bool FACT, bool PRO>
+cudaError_t launch_step_bulk_pro(const StepParams& p, cudaStream_t stream) {
   CUtensorMap mh, md;
   memset(&mh, 0, sizeof(mh));
   memset(&md, 0, sizeof(md));
@@ -665,9 +707,21 @@ cudaError_t launch_step_bulk_impl(const StepParams& p, cudaStream_t stream) {
     const size_t rows = (size_t)p.B * p.D;
     if (getenv("M3_NO_SWIZZLE") == nullptr && encode_state_map(&mh, p.h, rows) &&
         (FACT || encode_state_map(&md, p.dbu, rows)))
-      return launch_step_bulk_kernel<R, T, FACT, true>(p, stream, mh, md);
+      return launch_step_bulk_kernel<R, T, FACT, true, PRO>(p, stream, mh, md);
   }
-  return launch_step_bulk_kernel<R, T, FACT, false>(p, stream, mh, md);
+  return launch_step_bulk_kernel<R, T, FACT, false, PRO>(p, stream, mh, md);
+}
+
+// The fused prologue is compiled for the 32-lane tiles (the Search-Mamba and
+// Eval-Mamba shapes); other tiles report cudaErrorNotSupported (nothing is
+// launched) and the caller runs the prologue kernel and the step separately.
+template <int R, int T, bool FACT>
+cudaError_t launch_step_bulk_impl(const StepParams& p, cudaStream_t stream) {
+  if (p.pro) {
+    if constexpr (4 * (R + T) == 32) return launch_step_bulk_pro<R, T, FACT, true>(p, stream);
+    return cudaErrorNotSupported;
+  }
+  return launch_step_bulk_pro<R, T, FACT, false>(p, stream);
 }
 
 template <int R, int T, bool FACT>
@@ -682,6 +736,7 @@ cudaError_t launch_step_impl(const StepParams& p, cudaStream_t stream) {
 cudaError_t launch_step(const Tile& t, const StepParams& p, cudaStream_t s) {
 #define M3_X(r, tt, nd, ndb, nthb, gs)                                             \
   if (t.R == r && t.T == tt) {                                                     \
+    if (p.pro && !p.bulk) return cudaErrorNotSupported;                            \
     if (p.bulk)                                                                    \
       return p.factored ? launch_step_bulk_impl<r, tt, true>(p, s)                 \
                         : launch_step_bulk_impl<r, tt, false>(p, s);               \

@@ -1,0 +1,112 @@
+"""The lockstep recurrent step of a whole Mamba stack as one CUDA graph.
+
+A rollout (the MARS batched lines, redpanda/engine/mars_search.py:440-446) and
+a search node evaluation (``SearchMamba.eval_step``,
+redpanda/engine/search_mamba.py:275-291) advance the same state one token per
+call through every layer: embedding, per layer RMSNorm, the in_proj / x_proj /
+dt_proj GEMMs, the fused step kernels and out_proj with the residual add, then
+the final norm (``Mamba.step_fused_``).  That is about ten launches per layer;
+for a batch-1 node the GPU work of each is a few microseconds, so the CPU's
+launch rate sets the node rate.  ``StepGraph`` records the stack once with
+``torch.cuda.CUDAGraph`` and replays it as a single launch per token.
+
+The graph reads fixed addresses: its own token buffer, its static state
+(``cache``), the model's parameters and the padded step parameters cached at
+capture.  So: capture after the weights are final (capture again after they
+change); load a state by priming into ``cache``
+(``model.prime_cache(ids, out=graph.cache)``), by ``load_`` (a copy), or by
+stepping from the zero state; read ``hidden`` (and the head outputs) before the
+next replay, which overwrites them.  The whole state lives in one flat buffer,
+so copying a cache in or out is a single copy.
+"""
+
+import torch
+
+
+class StepGraph:
+    """``Mamba.step_fused_`` over every layer, captured for ``batch`` rows.
+
+    ``head``: optional callable on the step's hidden state (B, d_model) whose
+    outputs are captured too (e.g. a search's value and continuation heads);
+    they are returned by :meth:`step` after the hidden state.
+    """
+
+    def __init__(self, model, batch, apply_final_norm=True, head=None, warmup=2):
+        cfg = model.config
+        if cfg.bidirectional:
+            raise ValueError("StepGraph: the step needs a causal model")
+        dev = model.embedding.weight.device
+        if dev.type != "cuda":
+            raise RuntimeError("StepGraph: the model must be on a CUDA device")
+        n_layer, d, n = len(model.layers), cfg.d_inner, cfg.d_state
+        self.model = model
+        self.batch = batch
+        self._per = batch * d * n
+        self.flat = torch.zeros(n_layer * 2 * self._per, device=dev, dtype=torch.float32)
+        self.cache = self._views(self.flat)
+        self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+
+        def run(cache):
+            h, _ = model.step_fused_(token_id=self.tokens, cache=cache,
+                                     apply_final_norm=apply_final_norm)
+            extra = head(h) if head is not None else ()
+            return (h, *extra) if isinstance(extra, tuple) else (h, extra)
+
+        # warm-up on a scratch state (cuBLAS handles, the library's kernel
+        # attributes and the padded step parameters are set up here, outside
+        # the capture) so the caller's state is not advanced
+        scratch = self._views(self.flat.clone())
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.no_grad(), torch.cuda.stream(side):
+            for _ in range(warmup):
+                run(scratch)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        del scratch
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            self.outputs = run(self.cache)
+        self.hidden = self.outputs[0]
+
+    def _views(self, flat):
+        """(h, dBu) views of each layer's slice of a flat state buffer."""
+        d, n = self.model.config.d_inner, self.model.config.d_state
+        per, b = self._per, self.batch
+        return [(flat[(2 * i) * per:(2 * i + 1) * per].view(b, d, n),
+                 flat[(2 * i + 1) * per:(2 * i + 2) * per].view(b, d, n))
+                for i in range(len(self.model.layers))]
+
+    def load_(self, cache):
+        """Copy a cache ((h, dBu) per layer, ``batch`` rows) into the static state."""
+        src = getattr(cache, "flat", None)
+        if src is not None and src.numel() == self.flat.numel():
+            self.flat.copy_(src)
+            return
+        if len(cache) != len(self.cache):
+            raise ValueError("load_: one (h, dBu) entry per layer")
+        dst = [t for pair in self.cache for t in pair]
+        torch._foreach_copy_(dst, [t for pair in cache for t in pair[:2]])
+
+    def snapshot(self):
+        """A copy of the static state as a new cache (one copy of the flat buffer)."""
+        flat = self.flat.clone()
+        out = FlatCache(self._views(flat))
+        out.flat = flat
+        return out
+
+    def reset_(self):
+        """Zero state (the reference's ``init_cache``: no prefix)."""
+        self.flat.zero_()
+
+    def step(self, token_id):
+        """Advance the static state by one token per row; returns the captured
+        outputs (hidden state first), valid until the next call."""
+        tok = token_id if torch.is_tensor(token_id) else torch.as_tensor(token_id)
+        self.tokens.copy_(tok.reshape(-1).to(self.tokens.device), non_blocking=True)
+        self.graph.replay()
+        return self.outputs
+
+
+class FlatCache(list):
+    """A cache list whose (h, dBu) tensors are views of one buffer, ``flat``."""
+    flat = None

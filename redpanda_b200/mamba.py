@@ -92,6 +92,18 @@ class Mamba3Block(nn.Module):
     # BCNorm per channel tile on their critical path (bench.py, configs line
     # c2_fused_prologue_bidir).
     fuse_prologue = False
+    # the fused step layer (step_fused_) computes softplus, BCNorm and the MIMO
+    # fold inside the step kernel (m3_step_gated_fused, bit-identical to the
+    # two launches) for batches of at most fuse_step_max_batch rows, and runs
+    # m3_step_inputs + m3_step_gated_ above that.  Measured on a B200 (the
+    # 12-layer config-3 stack replayed as a CUDA graph, per step): 340 vs 485 us
+    # at B=1, 825 vs 971 us at B=256, 1.80 vs 1.85 ms at B=1024, but 5.78 vs
+    # 5.54 ms at B=4096 and 11.4 vs 10.8 ms at B=8192 -- small batches are
+    # launch-latency-bound and gain a launch per layer, large ones are
+    # HBM-bound and lose more to the per-row-pair BCNorm and barrier in every
+    # channel-tile CTA than the delta/Bc/Cc round trip costs.
+    fuse_step = True
+    fuse_step_max_batch = 2048
 
     def __init__(self, config: MambaConfig):
         super().__init__()
@@ -218,12 +230,13 @@ class Mamba3Block(nn.Module):
         return self._selective_scan_trapezoidal(u, delta, A_real, A_imag, B, C, self.D,
                                                 return_state=return_state)
 
-    def _forward_inference(self, x, return_state, residual=None):
+    def _forward_inference(self, x, return_state, residual=None, state_out=None):
         """No-grad layer forward on the fused kernels (mamba.py:231-282): after
         the in_proj / x_proj / dt_proj GEMMs, softplus + BCNorm + MIMO fold of
         every token is one launch (m3_step_inputs over B*L rows), the scan (or
         the fused bidirectional pair) another, (y + u*D)*silu(z) a third
-        (m3_gate), then out_proj."""
+        (m3_gate), then out_proj.  ``state_out``: (h, dBu) tensors that receive
+        the final state (with ``return_state``)."""
         cfg = self.config
         n, p, d_in = cfg.d_state, cfg.mimo_p, cfg.d_inner
         xz = self.in_proj(x)
@@ -257,7 +270,7 @@ class Mamba3Block(nn.Module):
             if cfg.bidirectional:
                 y = S.m3_bidir_scan(*args, y_dtype=yd)
             elif return_state:
-                y, state = S.m3_scan_with_state(*args)
+                y, state = S.m3_scan_with_state(*args, state_out=state_out)
             else:
                 y = S.m3_trapezoidal_scan(*args, y_dtype=yd)
         y = S.m3_gate(y, u, xz[..., d_in:], self.D, coef,
@@ -357,10 +370,13 @@ class Mamba3Block(nn.Module):
 
         ``state``: (h, dBu) (the reference cache pair) or (h, fac_prev, fac_next)
         (the factored state; swap the factor buffers between steps).  The
-        projections are cuBLAS GEMMs; softplus, BCNorm and the MIMO fold run in
-        one launch (``m3_step_inputs``) and the recurrence with the gated output
-        (y + u*D) * silu(z) in another (``m3_step_gated_``).  Returns the
-        out_proj input (B, d_inner); the caller applies out_proj (mamba.py:497).
+        projections are cuBLAS GEMMs; softplus, BCNorm, the MIMO fold, the
+        recurrence and the gated output (y + u*D) * silu(z) run in one launch
+        (``m3_step_gated_fused_``) for batches up to ``fuse_step_max_batch``
+        where its kernel serves the shape, else in two (``m3_step_inputs``,
+        ``m3_step_gated_``), with identical results.
+        Returns the out_proj input (B, d_inner); the caller applies out_proj
+        (mamba.py:497).
         """
         cfg = self.config
         n, p = cfg.d_state, cfg.mimo_p
@@ -371,6 +387,12 @@ class Mamba3Block(nn.Module):
         bw = self.b_norm.weight if cfg.use_bcnorm else None
         cw = self.c_norm.weight if cfg.use_bcnorm else None
         eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
+        if self.fuse_step and x_t.shape[0] <= self.fuse_step_max_batch:
+            out = S.m3_step_gated_fused_(state, dt, x_dbl, cfg.dt_rank, cfg.dt_rank + n * p,
+                                         bw, cw, eps, p, u, self.step_params(),
+                                         cfg.n_rot_state, xz[:, cfg.d_inner:], self.D)
+            if out is not None:
+                return out
         delta, bc, cc = S.m3_step_inputs(dt, x_dbl, cfg.dt_rank, cfg.dt_rank + n * p, bw, cw,
                                          eps, n, p)
         return S.m3_step_gated_(state, delta, u, bc, cc, self.step_params(), cfg.n_rot_state,
@@ -386,6 +408,13 @@ class Mamba3Block(nn.Module):
             state = tuple(s.detach().to(torch.float32).clone(
                 memory_format=torch.contiguous_format) for s in state)
         return self.step_(x_t, state)
+
+
+def _state_pair(entry):
+    """An (h, dBu) cache entry as a tuple (the factored state is not primed in place)."""
+    if len(entry) != 2:
+        raise ValueError("prime_cache(out=...) takes (h, dBu) cache entries")
+    return tuple(entry)
 
 
 class Mamba(nn.Module):
@@ -469,15 +498,22 @@ class Mamba(nn.Module):
                  else torch.addmm(x + op.bias, g, op.weight.t()))
         return (self.norm_f(x) if apply_final_norm else x), cache
 
-    def prime_cache(self, input_ids):
-        """mamba.py:603-620: full scan once, then (final_hidden, cache)."""
+    def prime_cache(self, input_ids, out=None):
+        """mamba.py:603-620: full scan once, then (final_hidden, cache).
+
+        ``out`` (no-grad only): an existing cache, (h, dBu) per layer, that
+        receives the primed state in place (a captured step graph's static
+        state); it is also the returned cache."""
         assert not self.config.bidirectional, "prime_cache() requires a causal model"
+        if out is not None and torch.is_grad_enabled():
+            raise ValueError("prime_cache(out=...) is an inference option (autograd disabled)")
         cur = self.embedding(input_ids)
         cache = []
-        for layer in self.layers:
+        for i, layer in enumerate(self.layers):
             if not torch.is_grad_enabled():   # out_proj and the residual add in one GEMM
-                cur, state = layer["mixer"]._forward_inference(layer["norm"](cur), True,
-                                                               residual=cur)
+                cur, state = layer["mixer"]._forward_inference(
+                    layer["norm"](cur), True, residual=cur,
+                    state_out=None if out is None else _state_pair(out[i]))
             else:
                 mixed, state = layer["mixer"].forward_with_state(layer["norm"](cur))
                 cur = cur + mixed

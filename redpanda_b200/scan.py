@@ -330,8 +330,12 @@ def m3_fused_scan(dt, x_dbl, b_weight, c_weight, eps, u, A_real, A_imag, track, 
 
 
 def _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state,
-                 y_dtype=torch.float32):
-    """Forward only (no autograd record, no checkpoints): the inference path."""
+                 y_dtype=torch.float32, state_out=None):
+    """Forward only (no autograd record, no checkpoints): the inference path.
+
+    ``state_out``: (h, dbu) float32 contiguous (B, D, N) tensors that receive
+    the final state instead of new ones (a captured step graph's static cache).
+    """
     lib = _lib.load()
     dev = _require_cuda(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p)
     dl, uu, dt_du = _prep_pair(delta, u)
@@ -343,7 +347,14 @@ def _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_stat
     y = torch.empty(B, L, D, device=dev, dtype=y_dtype)
     empty = torch.empty(0, device=dev)
     h = dbu = None
-    if want_state:
+    if want_state and state_out is not None:
+        h, dbu = state_out
+        for t in (h, dbu):
+            if (t.shape != (B, D, N) or t.dtype != torch.float32 or not t.is_contiguous()
+                    or t.device != dev):
+                raise ValueError("state_out: (B, D, N) contiguous float32 tensors on the "
+                                 "scan's device")
+    elif want_state:
         h = torch.empty(B, D, N, device=dev, dtype=torch.float32)
         dbu = torch.empty_like(h)
     with torch.cuda.device(dev):
@@ -355,7 +366,7 @@ def _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_stat
 
 
 def _apply(delta, u, Bc, Cc, A_real, A_imag, track, n_rot, n_state, direction, want_state,
-           y_dtype=None):
+           y_dtype=None, state_out=None):
     d_inner = u.shape[-1]
     y_dtype = torch.float32 if y_dtype is None else y_dtype
     if y_dtype not in (torch.float32, torch.bfloat16):
@@ -363,7 +374,9 @@ def _apply(delta, u, Bc, Cc, A_real, A_imag, track, n_rot, n_state, direction, w
     Ar_p, Ai_p, Tk_p = pad_params(A_real, A_imag, track, n_rot, n_state, d_inner, u.device)
     if not torch.is_grad_enabled():
         return _scan_nograd(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p, n_rot, direction, want_state,
-                            y_dtype)
+                            y_dtype, state_out)
+    if state_out is not None:
+        raise ValueError("state_out is an inference option (autograd disabled)")
     return _TrapezoidalScanFn.apply(delta, u, Bc, Cc, Ar_p, Ai_p, Tk_p,
                                     n_rot, direction, want_state, y_dtype)
 
@@ -401,13 +414,14 @@ def m3_bidir_scan(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
 
 
 def m3_scan_with_state(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
-                       n_rot, n_state):
+                       n_rot, n_state, state_out=None):
     """Causal scan returning ``(y, (h_last, dBu_last))`` (mamba.py:377-379).
 
-    y is differentiable; the state is not.
+    y is differentiable; the state is not.  ``state_out`` (inference only):
+    existing (h, dBu) tensors to write the state into.
     """
     y, h, dbu = _apply(delta, u, B_contracted, C_contracted, A_real, A_imag, track,
-                       n_rot, n_state, M3_DIR_FWD, True)
+                       n_rot, n_state, M3_DIR_FWD, True, state_out=state_out)
     return y, (h, dbu)
 
 
@@ -625,6 +639,58 @@ def m3_step_gated_(state, delta_t, u_t, Bc_t, Cc_t, params, n_rot, z, d_skip):
                                      bb.data_ptr(), cc.data_ptr(), ar.data_ptr(), ai.data_ptr(),
                                      tk.data_ptr(), z.data_ptr(), z.stride(0), ds.data_ptr(),
                                      out.data_ptr(), _stream(dev)))
+    return out
+
+
+M3_ERR_UNSUPPORTED = 4
+
+
+def m3_step_gated_fused_(state, dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, mimo_p,
+                         u_t, params, n_rot, z, d_skip):
+    """:func:`m3_step_inputs` + :func:`m3_step_gated_` in ONE launch
+    (mamba.py:455-497): the step kernel computes delta = softplus(dt) and the
+    BCNorm'ed, MIMO-folded Bc/Cc of each row from the raw projections itself,
+    with the same arithmetic, so state and output are bit-identical to the two
+    launches.  ``dt`` (B, D) and ``x_dbl`` (B, ld) float32 rows (x_dbl may be
+    the full x_proj output, B_raw / C_raw at columns off_b / off_c).
+
+    Returns the gated output (B, D) float32, or None when the fused kernel does
+    not serve this shape or layout (nothing launched; the caller runs the two
+    launches)."""
+    lib = _lib.load()
+    h = state[0]
+    dev = _require_cuda(h, dt, x_dbl, u_t, z, d_skip)
+    B, D, N = h.shape
+    if dt.dtype != torch.float32 or x_dbl.dtype != torch.float32:
+        return None
+    if dt.stride(-1) != 1 or x_dbl.stride(-1) != 1 or z.stride(-1) != 1:
+        return None
+    if z.dtype != torch.float32:
+        z = z.float()
+    uu = u_t if u_t.is_contiguous() else u_t.contiguous()
+    dt_du = _dt_code(uu.dtype)
+    ar, ai, tk = params
+    ds = d_skip.detach().to(torch.float32).contiguous()
+    if (b_weight is None) != (c_weight is None):
+        raise ValueError("m3_step_gated_fused_: both BCNorm weights or neither")
+    wb = None if b_weight is None else b_weight.detach().to(torch.float32).contiguous()
+    wc = None if c_weight is None else c_weight.detach().to(torch.float32).contiguous()
+    out = torch.empty(B, D, device=dev, dtype=torch.float32)
+    desc = StepDesc(B, D, N, int(n_rot), dt_du, M3_F32)
+    if len(state) == 2:
+        dbu, fa, fb = state[1], None, None
+    else:
+        dbu, fa, fb = None, state[1], state[2]
+    with torch.cuda.device(dev):
+        rc = lib.m3_step_gated_fused(desc, int(mimo_p), h.data_ptr(), ctypes_ptr(dbu),
+                                     ctypes_ptr(fa), ctypes_ptr(fb), dt.data_ptr(), dt.stride(0),
+                                     x_dbl.data_ptr(), x_dbl.stride(0), int(off_b), int(off_c),
+                                     ctypes_ptr(wb), ctypes_ptr(wc), float(eps), uu.data_ptr(),
+                                     ar.data_ptr(), ai.data_ptr(), tk.data_ptr(), z.data_ptr(),
+                                     z.stride(0), ds.data_ptr(), out.data_ptr(), _stream(dev))
+    if rc == M3_ERR_UNSUPPORTED:
+        return None
+    _lib.check(rc)
     return out
 
 

@@ -15,6 +15,7 @@ the reference saved loads with ``load_state_dict``.
 import torch
 import torch.nn as nn
 
+from .graphs import StepGraph
 from .mamba import Mamba, MambaConfig
 
 
@@ -57,6 +58,7 @@ class SearchMamba(nn.Module):
         self.consistency_proj = nn.Sequential(
             nn.Linear(d, d), nn.GELU(), nn.Linear(d, eval_dim))
         self.apply(self._init_weights)
+        self._node_graph = None
 
     def _init_weights(self, m):
         if isinstance(m, nn.Linear):
@@ -139,6 +141,29 @@ class SearchMamba(nn.Module):
         h, cache = self.backbone.step(token_id=tok, cache=cache)
         value = torch.tanh(self.value_head(h)).squeeze(-1).item()
         return value, self.continuation_head(h).squeeze(0), cache
+
+    @torch.no_grad()
+    def eval_step_graphed(self, cache, move_token):
+        """``eval_step`` with the whole node step -- every layer of the backbone
+        and the value and continuation heads -- replayed as one captured CUDA
+        graph (:class:`redpanda_b200.graphs.StepGraph`).  Same contract: returns
+        (value, continuation logits, new cache) and leaves ``cache`` unchanged;
+        the new cache's tensors share one buffer, so the next call loads it with
+        a single copy.  The graph is captured on first use from the current
+        weights; call ``release_graphs`` after changing them."""
+        g = self._node_graph
+        if g is None:
+            g = self._node_graph = StepGraph(
+                self.backbone, 1,
+                head=lambda h: (torch.tanh(self.value_head(h)).squeeze(-1),
+                                self.continuation_head(h).squeeze(0)))
+        g.load_(cache)
+        _, value, logits = g.step(int(move_token))
+        return value.item(), logits.clone(), g.snapshot()
+
+    def release_graphs(self):
+        """Drop the captured node graph (it is captured again on next use)."""
+        self._node_graph = None
 
     def dynamics_rollout(self, board_encoding, move_tokens):
         """Training rollout (search_mamba.py:252-273) as one causal scan.

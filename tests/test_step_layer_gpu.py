@@ -85,6 +85,107 @@ def test_gated_step_equals_step_and_torch_epilogue(B, D, N, n_track):
     assert S.device_error() == 0
 
 
+@pytest.mark.parametrize("B,D,n_track,p,bcnorm", [(37, 256, 8, 2, True), (8, 1024, 16, 2, True),
+                                                  (5, 64, 8, 2, False), (1, 128, 8, 1, True)])
+def test_step_gated_fused_equals_inputs_then_gated(B, D, n_track, p, bcnorm):
+    """m3_step_gated_fused (softplus, BCNorm, MIMO fold, recurrence and gated
+    output in one launch) gives the bits of m3_step_inputs + m3_step_gated, for
+    both state forms, odd batches (the last row pair half empty) and dt values
+    on both sides of softplus' threshold."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    N, R = 32, 16
+    n_rot = N - n_track
+    A_real = -torch.exp(torch.randn(D, n_rot, device="cuda", generator=g) * 0.5)
+    A_imag = (torch.rand(D, n_rot, device="cuda", generator=g) * 2 - 1) * 3.14159
+    track = torch.tanh(torch.randn(D, n_track, device="cuda", generator=g))
+    params = tuple(t.contiguous() for t in S.pad_params(A_real, A_imag, track, n_rot, N, D,
+                                                        torch.device("cuda")))
+    wb = torch.rand(N * p, device="cuda", generator=g) + 0.5 if bcnorm else None
+    wc = torch.rand(N * p, device="cuda", generator=g) + 0.5 if bcnorm else None
+    d_skip = torch.randn(D, device="cuda", generator=g)
+    h0 = torch.randn(B, D, N, device="cuda", generator=g) * 0.1
+    fa0 = torch.randn(B, D + N, device="cuda", generator=g)
+    d0 = fa0[:, :D, None] * fa0[:, None, D:]
+    hu, du_ = h0.clone(), d0.clone()
+    hf, df = h0.clone(), d0.clone()
+    hfa, fa, fb = h0.clone(), fa0.clone(), torch.empty_like(fa0)
+    hua, ua, ub = h0.clone(), fa0.clone(), torch.empty_like(fa0)
+    for _ in range(3):
+        dt = torch.randn(B, D, device="cuda", generator=g) * 2 - 3
+        dt[:, ::17] += 24.0                                     # above the threshold
+        x_dbl = torch.randn(B, R + 2 * N * p, device="cuda", generator=g)
+        u = torch.randn(B, D, device="cuda", generator=g)
+        z = torch.randn(B, 2 * D, device="cuda", generator=g)[:, D:]
+        delta, bc, cc = S.m3_step_inputs(dt, x_dbl, R, R + N * p, wb, wc, 1e-5, N, p)
+        ref = S.m3_step_gated_((hu, du_), delta, u, bc, cc, params, n_rot, z, d_skip)
+        out = S.m3_step_gated_fused_((hf, df), dt, x_dbl, R, R + N * p, wb, wc, 1e-5, p, u,
+                                     params, n_rot, z, d_skip)
+        assert out is not None, "the fused step kernel should serve this shape"
+        assert torch.equal(out, ref) and torch.equal(hf, hu) and torch.equal(df, du_)
+        ref_f = S.m3_step_gated_((hua, ua, ub), delta, u, bc, cc, params, n_rot, z, d_skip)
+        out_f = S.m3_step_gated_fused_((hfa, fa, fb), dt, x_dbl, R, R + N * p, wb, wc, 1e-5, p,
+                                       u, params, n_rot, z, d_skip)
+        assert torch.equal(out_f, ref_f) and torch.equal(hfa, hua) and torch.equal(fb, ub)
+        fa, fb = fb, fa
+        ua, ub = ub, ua
+    assert S.device_error() == 0
+
+
+def test_step_gated_fused_declines_unserved_shapes():
+    """Shapes outside the fused kernel (a 16-lane state, a misaligned B_raw
+    column, mimo_p 4) return None with nothing launched; the model then runs
+    the two launches."""
+    g = torch.Generator(device="cuda").manual_seed(1)
+    B, D, N = 4, 64, 16
+    params = tuple(t.contiguous() for t in S.pad_params(
+        -torch.ones(D, 12, device="cuda"), torch.zeros(D, 12, device="cuda"),
+        torch.zeros(D, 4, device="cuda"), 12, N, D, torch.device("cuda")))
+    st = (torch.zeros(B, D, N, device="cuda"), torch.zeros(B, D, N, device="cuda"))
+    dt = torch.randn(B, D, device="cuda", generator=g)
+    x = torch.randn(B, 8 + 2 * N * 2, device="cuda", generator=g)
+    u, z = torch.randn(B, D, device="cuda"), torch.randn(B, D, device="cuda")
+    ds = torch.zeros(D, device="cuda")
+    assert S.m3_step_gated_fused_(st, dt, x, 8, 8 + 2 * N, None, None, 0.0, 2, u, params, 12,
+                                  z, ds) is None
+    st32 = (torch.zeros(B, D, 32, device="cuda"), torch.zeros(B, D, 32, device="cuda"))
+    p32 = tuple(t.contiguous() for t in S.pad_params(
+        -torch.ones(D, 24, device="cuda"), torch.zeros(D, 24, device="cuda"),
+        torch.zeros(D, 8, device="cuda"), 24, 32, D, torch.device("cuda")))
+    x32 = torch.randn(B, 7 + 2 * 64, device="cuda", generator=g)
+    assert S.m3_step_gated_fused_(st32, dt, x32, 7, 7 + 64, None, None, 0.0, 2, u, p32, 24,
+                                  z, ds) is None
+    x4 = torch.randn(B, 8 + 2 * 128, device="cuda", generator=g)
+    assert S.m3_step_gated_fused_(st32, dt, x4, 8, 8 + 128, None, None, 0.0, 4, u, p32, 24,
+                                  z, ds) is None
+    assert S.device_error() == 0
+
+
+def test_model_step_prologue_in_kernel_equals_two_launches():
+    """Mamba.step_fused_ with the prologue inside the step kernel and with it as
+    its own launch (Mamba3Block.fuse_step) give the same bits, state and output."""
+    from redpanda_b200.mamba import Mamba3Block
+    torch.manual_seed(7)
+    cfg = MambaConfig(d_model=64, n_layer=2, d_state=32, n_track_state=8, mimo_p=2,
+                      vocab_size=256)
+    m = Mamba(cfg).cuda().eval()
+    ids = torch.randint(0, 256, (7, 9), device="cuda")
+    with torch.no_grad():
+        _, cache = m.prime_cache(ids[:, :5])
+        ca = [(h.clone(), d.clone()) for h, d in cache]
+        cb = [(h.clone(), d.clone()) for h, d in cache]
+        try:
+            for t in range(5, 9):
+                Mamba3Block.fuse_step = True
+                ha, ca = m.step_fused_(token_id=ids[:, t], cache=ca)
+                Mamba3Block.fuse_step = False
+                hb, cb = m.step_fused_(token_id=ids[:, t], cache=cb)
+                assert torch.equal(ha, hb)
+        finally:
+            Mamba3Block.fuse_step = True
+        for (h1, d1), (h2, d2) in zip(ca, cb):
+            assert torch.equal(h1, h2) and torch.equal(d1, d2)
+
+
 def test_model_fused_step_matches_unfused_step_and_forward():
     """Config-3-like layers: the fused step layer reproduces Mamba.step_ (torch
     projections + m3_step_) and, from a primed cache, the full forward."""
