@@ -20,6 +20,7 @@
  *   redpanda/engine/mamba.py:455-497        step inputs + step + gated output in one launch
  *                                           -> m3_step_gated_fused
  *   redpanda/engine/mamba.py:262-265        (y + u*D) * silu(z) after a scan -> m3_gate
+ *   redpanda/engine/mamba.py:243, 452       u = silu(x half of in_proj) -> m3_silu
  *
  * Shapes (B batch, L length, D = d_inner, N = d_state, n_rot rotational lanes,
  * N - n_rot tracking lanes):
@@ -231,15 +232,23 @@ M3_API int m3_step_factored(const m3_step_desc* desc, float* h, const float* fac
  *   Bc, Cc (B, N) = sum over the p MIMO columns of BCNorm(B_raw), BCNorm(C_raw)
  * with BCNorm(x) = x * rsqrt(mean(x^2) + eps) * w over the N*p vector
  * (mamba.py:82-89, 297-299, 336-337).
- *   dt     (B, ld_dt) float32: dt_proj(dt_raw) including its bias
- *   xbc    (B, ld_x)  float32: rows of x_proj's output; B_raw starts at column
- *          off_b and C_raw at off_c, N*p columns each
- *   wb, wc (N*p,) float32 BCNorm weights, or both NULL (use_bcnorm=False: plain sum)
+ *   dt      (B, ld_dt) float32: dt_proj(dt_raw), with its bias or without it
+ *   dt_bias (D,) float32 dt_proj bias, added to dt first (one fp32 rounding, as
+ *           torch's matmul-then-add), or NULL when dt includes it
+ *   xbc     (B, ld_x)  float32: rows of x_proj's output; B_raw starts at column
+ *           off_b and C_raw at off_c, N*p columns each
+ *   wb, wc  (N*p,) float32 BCNorm weights, or both NULL (use_bcnorm=False: plain sum)
  * desc->n_rot, dtype_du and dtype_bc are ignored; all outputs are float32. */
 M3_API int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p,
-            const float* dt, int64_t ld_dt, const float* xbc, int64_t ld_x,
-            int32_t off_b, int32_t off_c, const float* wb, const float* wc, float eps,
-            float* delta, float* Bc, float* Cc, void* stream);
+            const float* dt, int64_t ld_dt, const float* dt_bias, const float* xbc,
+            int64_t ld_x, int32_t off_b, int32_t off_c, const float* wb, const float* wc,
+            float eps, float* delta, float* Bc, float* Cc, void* stream);
+
+/* u = silu(x) = x / (1 + exp(-x)) over (rows, d) of a row-strided x: the x half
+ * of in_proj's output (mamba.py:243, 452), read in place; out (rows, d) float32
+ * contiguous. */
+M3_API int m3_silu(int64_t rows, int32_t d, const float* x, int64_t ld_x, float* out,
+            void* stream);
 
 /* Workspace bytes of m3_step_inputs_bwd (the BCNorm weight-gradient partials). */
 M3_API size_t m3_step_inputs_bwd_workspace_bytes(const m3_step_desc* desc, int32_t mimo_p);
@@ -281,7 +290,8 @@ M3_API int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu,
  * computes delta, Bc and Cc itself with the arithmetic of m3_step_inputs, so
  * the state and out are bit-identical to m3_step_inputs followed by
  * m3_step_gated.
- *   dt      (B, ld_dt) float32: dt_proj output (bias included), before softplus
+ *   dt      (B, ld_dt) float32: dt_proj output, before softplus; dt_bias (D,) or
+ *           NULL as for m3_step_inputs
  *   xbc     (B, ld_x) float32: x_proj output; B_raw at column off_b, C_raw at
  *           off_c, N * mimo_p values each
  *   wb, wc  (N * mimo_p,) float32 BCNorm weights, or both NULL (plain fold)
@@ -293,10 +303,10 @@ M3_API int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu,
  * m3_step_gated instead). */
 M3_API int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* h, float* dbu,
             const float* fac_prev, float* fac_next, const float* dt, int64_t ld_dt,
-            const float* xbc, int64_t ld_x, int32_t off_b, int32_t off_c, const float* wb,
-            const float* wc, float eps, const void* u, const float* A_real_p,
-            const float* A_imag_p, const float* track_p, const float* z, int64_t ld_z,
-            const float* d_skip, float* out, void* stream);
+            const float* dt_bias, const float* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
+            const float* wb, const float* wc, float eps, const void* u,
+            const float* A_real_p, const float* A_imag_p, const float* track_p,
+            const float* z, int64_t ld_z, const float* d_skip, float* out, void* stream);
 
 /* The layer's gated activation after a scan (mamba.py:262-265), elementwise
  * over (rows, D) = (B*L, D):

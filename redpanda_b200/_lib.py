@@ -59,8 +59,9 @@ SIGNATURES = {
     "m3_scan_bwd_noalloc": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P,
                                            _P, _P, _P, _P, _P, _P, _P, _P]),
     "m3_device_error": (ctypes.c_int, [ctypes.POINTER(_I), _I]),
-    "m3_step_inputs": (ctypes.c_int, [_S, _I, _P, ctypes.c_int64, _P, ctypes.c_int64, _I, _I,
-                                      _P, _P, ctypes.c_float, _P, _P, _P, _P]),
+    "m3_step_inputs": (ctypes.c_int, [_S, _I, _P, ctypes.c_int64, _P, _P, ctypes.c_int64, _I,
+                                      _I, _P, _P, ctypes.c_float, _P, _P, _P, _P]),
+    "m3_silu": (ctypes.c_int, [ctypes.c_int64, _I, _P, ctypes.c_int64, _P, _P]),
     "m3_step_inputs_bwd_workspace_bytes": (_Z, [_S, _I]),
     "m3_step_inputs_bwd": (ctypes.c_int, [_S, _I, _P, ctypes.c_int64, _P, ctypes.c_int64, _I,
                                           _I, _P, _P, ctypes.c_float, _P, _P, _P, _P, _P, _P,
@@ -71,7 +72,7 @@ SIGNATURES = {
                                      ctypes.c_int64, _P, ctypes.c_float, _P, _I, _P]),
     "m3_step_gated": (ctypes.c_int, [_S, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                      ctypes.c_int64, _P, _P, _P]),
-    "m3_step_gated_fused": (ctypes.c_int, [_S, _I, _P, _P, _P, _P, _P, ctypes.c_int64, _P,
+    "m3_step_gated_fused": (ctypes.c_int, [_S, _I, _P, _P, _P, _P, _P, ctypes.c_int64, _P, _P,
                                            ctypes.c_int64, _I, _I, _P, _P, ctypes.c_float,
                                            _P, _P, _P, _P, _P, ctypes.c_int64, _P, _P, _P]),
 }

@@ -367,6 +367,7 @@ int m3_scan_bwd(const m3_scan_desc* desc, const void* delta, const void* u, cons
 // Arguments of the fused prologue (m3_step_gated_fused).
 struct StepPro {
   const float* dt; int64_t ld_dt;
+  const float* dt_bias;
   const float* xbc; int64_t ld_x;
   int32_t off_b, off_c, P;
   const float* wb; const float* wc;
@@ -429,7 +430,8 @@ static int step_common(const m3_step_desc* desc, float* h, float* dbu, const flo
   if (pro) {   // the fused prologue needs the pipelined kernel on a 32-lane tile
     if (!p.bulk || desc->d_state != 32) return M3_ERR_UNSUPPORTED;
     p.pro = 1;
-    p.dt = pro->dt; p.ld_dt = pro->ld_dt; p.xbc = pro->xbc; p.ld_x = pro->ld_x;
+    p.dt = pro->dt; p.ld_dt = pro->ld_dt; p.dt_bias = pro->dt_bias;
+    p.xbc = pro->xbc; p.ld_x = pro->ld_x;
     p.off_b = pro->off_b; p.off_c = pro->off_c; p.P = pro->P;
     p.wb = pro->wb; p.wc = pro->wc; p.eps = pro->eps;
   }
@@ -575,7 +577,8 @@ int m3_step_gated(const m3_step_desc* desc, float* h, float* dbu, const float* f
 
 int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* h, float* dbu,
                         const float* fac_prev, float* fac_next, const float* dt, int64_t ld_dt,
-                        const float* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
+                        const float* dt_bias, const float* xbc, int64_t ld_x, int32_t off_b,
+                        int32_t off_c,
                         const float* wb, const float* wc, float eps, const void* u,
                         const float* A_real_p, const float* A_imag_p, const float* track_p,
                         const float* z, int64_t ld_z, const float* d_skip, float* out,
@@ -589,13 +592,13 @@ int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* h, floa
       off_b + np > ld_x || off_c + np > ld_x || !(eps >= 0.f))
     return M3_ERR_SHAPE;
   if (!aligned(z, 4) || !aligned(d_skip, 4) || !aligned(dt, 4) || !aligned(xbc, 4) ||
-      (wb && (!aligned(wb, 4) || !aligned(wc, 4))))
+      (wb && (!aligned(wb, 4) || !aligned(wc, 4))) || (dt_bias && !aligned(dt_bias, 4)))
     return M3_ERR_ALIGN;
   // every staged row a 16-byte multiple at a 16-byte aligned address
   if (mimo_p > 2 || np % 4 != 0 || !aligned(dt, 16) || ld_dt % 4 != 0 || !aligned(xbc, 16) ||
       ld_x % 4 != 0 || off_b % 4 != 0 || off_c % 4 != 0)
     return M3_ERR_UNSUPPORTED;
-  const StepPro pro{dt, ld_dt, xbc, ld_x, off_b, off_c, mimo_p, wb, wc, eps};
+  const StepPro pro{dt, ld_dt, dt_bias, xbc, ld_x, off_b, off_c, mimo_p, wb, wc, eps};
   // delta/Bc/Cc are not read under the fused prologue; dt and xbc stand in
   // for the pointer checks (both 16-byte aligned)
   return step_common(desc, h, dbu, fac_prev, fac_next, dt, u, xbc, xbc, A_real_p, A_imag_p,
@@ -603,9 +606,9 @@ int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* h, floa
 }
 
 int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const float* dt, int64_t ld_dt,
-                   const float* xbc, int64_t ld_x, int32_t off_b, int32_t off_c,
-                   const float* wb, const float* wc, float eps, float* delta, float* Bc,
-                   float* Cc, void* stream) {
+                   const float* dt_bias, const float* xbc, int64_t ld_x, int32_t off_b,
+                   int32_t off_c, const float* wb, const float* wc, float eps, float* delta,
+                   float* Bc, float* Cc, void* stream) {
   if (!desc) return M3_ERR_NULL;
   const int64_t np = (int64_t)desc->d_state * mimo_p;
   if (desc->batch < 1 || desc->d_inner < 1 || desc->d_state < 1 || mimo_p < 1 ||
@@ -615,16 +618,34 @@ int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const float* dt, in
   if (!dt || !xbc || !delta || !Bc || !Cc || ((wb == nullptr) != (wc == nullptr)))
     return M3_ERR_NULL;
   if (!aligned(dt, 4) || !aligned(xbc, 4) || !aligned(delta, 4) || !aligned(Bc, 4) ||
-      !aligned(Cc, 4) || (wb && (!aligned(wb, 4) || !aligned(wc, 4))))
+      !aligned(Cc, 4) || (wb && (!aligned(wb, 4) || !aligned(wc, 4))) ||
+      (dt_bias && !aligned(dt_bias, 4)))
     return M3_ERR_ALIGN;
   int rc = check_device();
   if (rc != M3_OK) return rc;
   InputsParams p;
   memset(&p, 0, sizeof(p));
-  p.dt = dt; p.ld_dt = ld_dt; p.xbc = xbc; p.ld_x = ld_x; p.off_b = off_b; p.off_c = off_c;
+  p.dt = dt; p.ld_dt = ld_dt; p.dt_bias = dt_bias;
+  p.xbc = xbc; p.ld_x = ld_x; p.off_b = off_b; p.off_c = off_c;
   p.wb = wb; p.wc = wc; p.eps = eps; p.delta = delta; p.Bc = Bc; p.Cc = Cc;
   p.B = desc->batch; p.D = desc->d_inner; p.N = desc->d_state; p.P = mimo_p;
+  p.vec4 = (desc->d_inner % 4) == 0 && ld_dt % 4 == 0 && aligned(dt, 16) &&
+           aligned(delta, 16) && (!dt_bias || aligned(dt_bias, 16));
   cudaError_t e = launch_step_inputs(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
+int m3_silu(int64_t rows, int32_t d, const float* x, int64_t ld_x, float* out, void* stream) {
+  if (rows < 1 || d < 1 || ld_x < d) return M3_ERR_SHAPE;
+  if (!x || !out) return M3_ERR_NULL;
+  if (!aligned(x, 4) || !aligned(out, 4)) return M3_ERR_ALIGN;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  SiluParams p;
+  memset(&p, 0, sizeof(p));
+  p.x = x; p.ld_x = ld_x; p.out = out; p.rows = rows; p.D = d;
+  p.vec4 = d % 4 == 0 && ld_x % 4 == 0 && aligned(x, 16) && aligned(out, 16);
+  cudaError_t e = launch_silu(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 

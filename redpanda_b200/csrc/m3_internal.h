@@ -112,6 +112,7 @@ struct StepParams {
   // rows; `delta`, `Bc`, `Cc` are unused then
   int pro;
   const float* dt; long long ld_dt;
+  const float* dt_bias;                       // (D,) or nullptr: delta = softplus(dt + bias)
   const float* xbc; long long ld_x;
   int off_b, off_c, P;
   const float* wb; const float* wc;
@@ -136,6 +137,8 @@ cudaError_t launch_step(const Tile& t, const StepParams& p, cudaStream_t s);
 
 struct InputsParams {
   const float* dt; long long ld_dt;       // (B, ld_dt): dt_proj output before softplus
+  const float* dt_bias;                   // (D,) dt_proj bias added first, or nullptr
+  int vec4;                               // dt rows, bias and delta as float4 (aligned, D % 4 == 0)
   const float* xbc; long long ld_x;       // (B, ld_x): row of x_proj output
   int off_b, off_c;                       // column offsets of B_raw and C_raw (N*p each)
   const float* wb; const float* wc;       // (N*p,) BCNorm weights
@@ -144,6 +147,14 @@ struct InputsParams {
   int B, D, N, P;
 };
 cudaError_t launch_step_inputs(const InputsParams& p, cudaStream_t s);
+
+struct SiluParams {
+  const float* x; long long ld_x;         // (rows, ld_x)
+  float* out;                             // (rows, D) contiguous
+  long long rows; int D;
+  int vec4;                               // x rows and out as float4
+};
+cudaError_t launch_silu(const SiluParams& p, cudaStream_t s);
 
 struct InputsBwdParams {
   const float* dt; long long ld_dt;       // nullptr: skip the softplus part

@@ -30,10 +30,27 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) step_inputs_kernel(const Inp
   const int rows = min(kRowsPerCta, p.B - r0);
   if (warp >= rows) return;
   const size_t b = (size_t)(r0 + warp);
-  {   // softplus of this warp's row
+  {   // softplus of this warp's row (after the dt_proj bias, when given)
     const float* dt = p.dt + b * p.ld_dt;
     float* delta = p.delta + b * p.D;
-    for (int d = lane; d < p.D; d += 32) delta[d] = softplus20(dt[d]);
+    const float* bias = p.dt_bias;
+    if (p.vec4) {
+      const float4* dt4 = reinterpret_cast<const float4*>(dt);
+      const float4* b4 = reinterpret_cast<const float4*>(bias);
+      float4* de4 = reinterpret_cast<float4*>(delta);
+      for (int c = lane; c < p.D / 4; c += 32) {
+        float4 x = dt4[c];
+        if (b4 != nullptr) {
+          const float4 bb = b4[c];
+          x = make_float4(__fadd_rn(x.x, bb.x), __fadd_rn(x.y, bb.y), __fadd_rn(x.z, bb.z),
+                          __fadd_rn(x.w, bb.w));
+        }
+        de4[c] = make_float4(softplus20(x.x), softplus20(x.y), softplus20(x.z), softplus20(x.w));
+      }
+    } else {
+      for (int d = lane; d < p.D; d += 32)
+        delta[d] = softplus20(bias != nullptr ? __fadd_rn(dt[d], bias[d]) : dt[d]);
+    }
   }
   const int np = p.N * p.P;
   const float* xb = p.xbc + b * p.ld_x + p.off_b;
@@ -226,6 +243,43 @@ cudaError_t launch_gate(const GateParams& p, cudaStream_t s) {
                    a16(p.z) && a16(p.d_skip) && a16(p.out);
   if (vec) gate_kernel<true><<<(unsigned)grid, 256, 0, s>>>(p);
   else gate_kernel<false><<<(unsigned)grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+// u = silu(x) over (rows, D) of a row-strided x (the x half of in_proj's
+// output, mamba.py:243/452): z / (1 + exp(-z)) in that rounding order; each
+// warp walks rows (grid-stride), its lanes the channels, four at a time when
+// vec4.
+__global__ void silu_kernel(const SiluParams p) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  auto silu = [](float z) { return __fdiv_rn(z, __fadd_rn(1.0f, expf(-z))); };
+  for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < p.rows;
+       r += warps) {
+    const float* x = p.x + (size_t)r * p.ld_x;
+    float* o = p.out + (size_t)r * p.D;
+    if (p.vec4) {
+      const float4* x4 = reinterpret_cast<const float4*>(x);
+      float4* o4 = reinterpret_cast<float4*>(o);
+      for (int c = lane; c < p.D / 4; c += 32) {
+        const float4 v = x4[c];
+        o4[c] = make_float4(silu(v.x), silu(v.y), silu(v.z), silu(v.w));
+      }
+    } else {
+      for (int d = lane; d < p.D; d += 32) o[d] = silu(x[d]);
+    }
+  }
+}
+
+cudaError_t launch_silu(const SiluParams& p, cudaStream_t s) {
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return e;
+  const long long want = (p.rows + 7) / 8;
+  const int grid = (int)(want < (long long)sms * 8 ? (want > 0 ? want : 1) : (long long)sms * 8);
+  silu_kernel<<<grid, 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 

@@ -546,8 +546,9 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
           if constexpr (R > 0) ld_vec<R, VR>(ds + q * R, dv[r]);
           if constexpr (T > 0) ld_vec<T, VT>(ds + 4 * R + q * T, dv[r] + R);
         }
-        if constexpr (PRO) {   // delta = softplus(dt), as step_inputs_kernel
-          dlv[r] = softplus20(reinterpret_cast<const float*>(st + SL::oDL(r))[grp]);
+        if constexpr (PRO) {   // delta = softplus(dt + bias), as step_inputs_kernel
+          const float dtv = reinterpret_cast<const float*>(st + SL::oDL(r))[grp];
+          dlv[r] = softplus20(p.dt_bias != nullptr ? __fadd_rn(dtv, p.dt_bias[d]) : dtv);
         } else {
           dlv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + SL::oDL(r))[grp])
                          : reinterpret_cast<const float*>(st + SL::oDL(r))[grp];

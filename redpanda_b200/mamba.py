@@ -96,14 +96,14 @@ class Mamba3Block(nn.Module):
     # fold inside the step kernel (m3_step_gated_fused, bit-identical to the
     # two launches) for batches of at most fuse_step_max_batch rows, and runs
     # m3_step_inputs + m3_step_gated_ above that.  Measured on a B200 (the
-    # 12-layer config-3 stack replayed as a CUDA graph, per step): 340 vs 485 us
-    # at B=1, 825 vs 971 us at B=256, 1.80 vs 1.85 ms at B=1024, but 5.78 vs
-    # 5.54 ms at B=4096 and 11.4 vs 10.8 ms at B=8192 -- small batches are
+    # 12-layer config-3 stack replayed as a CUDA graph, per step): 390 vs 474 us
+    # at B=1, 872 vs 920 us at B=256, but 1.88 vs 1.79 ms at B=1024, 5.96 vs
+    # 5.44 ms at B=4096 and 11.8 vs 10.7 ms at B=8192 -- small batches are
     # launch-latency-bound and gain a launch per layer, large ones are
     # HBM-bound and lose more to the per-row-pair BCNorm and barrier in every
     # channel-tile CTA than the delta/Bc/Cc round trip costs.
     fuse_step = True
-    fuse_step_max_batch = 2048
+    fuse_step_max_batch = 512
 
     def __init__(self, config: MambaConfig):
         super().__init__()
@@ -230,6 +230,27 @@ class Mamba3Block(nn.Module):
         return self._selective_scan_trapezoidal(u, delta, A_real, A_imag, B, C, self.D,
                                                 return_state=return_state)
 
+    def _silu_x(self, xz):
+        """u = silu(x half of in_proj's output) (mamba.py:243, 452): fp32 rows in
+        one launch that reads the half in place (m3_silu, torch's rounding);
+        a bf16 layer's activations through torch."""
+        d_in = self.config.d_inner
+        if xz.dtype != torch.float32 or not xz.is_contiguous():
+            return F.silu(xz[..., :d_in])
+        rows = xz.numel() // (2 * d_in)
+        return S.m3_silu(xz.view(rows, 2 * d_in)[:, :d_in]).view(*xz.shape[:-1], d_in)
+
+    def _dt(self, x_dbl):
+        """(dt, bias) for the prologue kernels: fp32 layers take dt_proj without
+        its bias and add the bias inside m3_step_inputs / m3_step_gated_fused
+        (one fp32 add, as torch's matmul-then-add of a strided input); a bf16
+        layer's dt_proj output as autocast gives it, bias included."""
+        cfg = self.config
+        raw = x_dbl[..., :cfg.dt_rank]
+        if x_dbl.dtype != torch.float32 or _bf16_layer():
+            return self.dt_proj(raw), None
+        return F.linear(raw, self.dt_proj.weight), self.dt_proj.bias
+
     def _forward_inference(self, x, return_state, residual=None, state_out=None):
         """No-grad layer forward on the fused kernels (mamba.py:231-282): after
         the in_proj / x_proj / dt_proj GEMMs, softplus + BCNorm + MIMO fold of
@@ -239,16 +260,16 @@ class Mamba3Block(nn.Module):
         the final state (with ``return_state``)."""
         cfg = self.config
         n, p, d_in = cfg.d_state, cfg.mimo_p, cfg.d_inner
+        bf16 = _bf16_layer()
         xz = self.in_proj(x)
-        u = F.silu(xz[..., :d_in])
+        u = self._silu_x(xz)
         x_dbl = self.x_proj(u)
-        dt = self.dt_proj(x_dbl[..., :cfg.dt_rank])
+        dt, dt_bias = self._dt(x_dbl)
         lead = u.shape[:-1]
         rows = u.numel() // d_in
         bw = self.b_norm.weight if cfg.use_bcnorm else None
         cw = self.c_norm.weight if cfg.use_bcnorm else None
         eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
-        bf16 = _bf16_layer()
         coef = 2.0 if cfg.bidirectional else 1.0
         state = y = None
         if bf16:
@@ -258,7 +279,8 @@ class Mamba3Block(nn.Module):
                                      S.M3_DIR_BIDIR if cfg.bidirectional else S.M3_DIR_FWD)
         if y is None:
             delta, bc, cc = S.m3_step_inputs(dt.reshape(rows, d_in), x_dbl.reshape(rows, -1),
-                                             cfg.dt_rank, cfg.dt_rank + n * p, bw, cw, eps, n, p)
+                                             cfg.dt_rank, cfg.dt_rank + n * p, bw, cw, eps, n, p,
+                                             dt_bias=dt_bias)
             delta, bc, cc = delta.view(*lead, d_in), bc.view(*lead, n), cc.view(*lead, n)
             if bf16:
                 bf = torch.bfloat16
@@ -381,20 +403,21 @@ class Mamba3Block(nn.Module):
         cfg = self.config
         n, p = cfg.d_state, cfg.mimo_p
         xz = self.in_proj(x_t)
-        u = F.silu(xz[:, :cfg.d_inner])
+        u = self._silu_x(xz)
         x_dbl = self.x_proj(u)
-        dt = self.dt_proj(x_dbl[:, :cfg.dt_rank])
+        dt, dt_bias = self._dt(x_dbl)
         bw = self.b_norm.weight if cfg.use_bcnorm else None
         cw = self.c_norm.weight if cfg.use_bcnorm else None
         eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
         if self.fuse_step and x_t.shape[0] <= self.fuse_step_max_batch:
             out = S.m3_step_gated_fused_(state, dt, x_dbl, cfg.dt_rank, cfg.dt_rank + n * p,
                                          bw, cw, eps, p, u, self.step_params(),
-                                         cfg.n_rot_state, xz[:, cfg.d_inner:], self.D)
+                                         cfg.n_rot_state, xz[:, cfg.d_inner:], self.D,
+                                         dt_bias=dt_bias)
             if out is not None:
                 return out
         delta, bc, cc = S.m3_step_inputs(dt, x_dbl, cfg.dt_rank, cfg.dt_rank + n * p, bw, cw,
-                                         eps, n, p)
+                                         eps, n, p, dt_bias=dt_bias)
         return S.m3_step_gated_(state, delta, u, bc, cc, self.step_params(), cfg.n_rot_state,
                                 xz[:, cfg.d_inner:], self.D)
 

@@ -489,10 +489,13 @@ def m3_step_factored_(h, fac_prev, fac_next, delta_t, u_t, Bc_t, Cc_t, A_real, A
     return y
 
 
-def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mimo_p):
+def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mimo_p,
+                   dt_bias=None):
     """softplus(dt) and the BCNorm'ed, MIMO-folded B and C of one token, one launch.
 
-    dt: (B, D) float32, dt_proj output with its bias; x_dbl: (B, K) float32 rows
+    dt: (B, D) float32, dt_proj output with its bias, or without it when
+    ``dt_bias`` (D,) is given (added first, one fp32 rounding, as torch's
+    matmul followed by the bias add); x_dbl: (B, K) float32 rows
     of x_proj's output, B_raw at column ``off_b`` and C_raw at ``off_c``
     (N*p columns each); b_weight / c_weight: BCNorm weights (N*p,) or None
     (use_bcnorm=False).  Returns (delta (B, D), Bc (B, N), Cc (B, N)), float32:
@@ -513,13 +516,15 @@ def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mi
     if b_weight is not None:
         wb = b_weight.detach().to(torch.float32).contiguous()
         wc = c_weight.detach().to(torch.float32).contiguous()
+    bias = None if dt_bias is None else dt_bias.detach().to(torch.float32).contiguous()
     delta = torch.empty(B, D, device=dev, dtype=torch.float32)
     bc = torch.empty(B, n_state, device=dev, dtype=torch.float32)
     cc = torch.empty_like(bc)
     desc = StepDesc(B, D, n_state, 0, M3_F32, M3_F32)
     with torch.cuda.device(dev):
         _lib.check(lib.m3_step_inputs(desc, int(mimo_p), dt.data_ptr(), dt.stride(0),
-                                      x_dbl.data_ptr(), x_dbl.stride(0), int(off_b), int(off_c),
+                                      ctypes_ptr(bias), x_dbl.data_ptr(), x_dbl.stride(0),
+                                      int(off_b), int(off_c),
                                       ctypes_ptr(wb), ctypes_ptr(wc), float(eps),
                                       delta.data_ptr(), bc.data_ptr(), cc.data_ptr(),
                                       _stream(dev)))
@@ -645,14 +650,31 @@ def m3_step_gated_(state, delta_t, u_t, Bc_t, Cc_t, params, n_rot, z, d_skip):
 M3_ERR_UNSUPPORTED = 4
 
 
+def m3_silu(x):
+    """silu(x) = x / (1 + exp(-x)) over the rows of a (rows, D) float32 view
+    whose rows may be strided (the x half of in_proj's output, mamba.py:243,
+    452); returns a contiguous (rows, D) float32 tensor.  Same rounding as
+    torch's silu: x / (1 + exp(-x)) evaluated in fp32."""
+    lib = _lib.load()
+    dev = _require_cuda(x)
+    if x.dtype != torch.float32 or x.dim() != 2 or x.stride(-1) != 1:
+        raise ValueError("m3_silu: a (rows, D) float32 view with contiguous rows")
+    rows, D = x.shape
+    out = torch.empty(rows, D, device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        _lib.check(lib.m3_silu(rows, D, x.data_ptr(), x.stride(0), out.data_ptr(), _stream(dev)))
+    return out
+
+
 def m3_step_gated_fused_(state, dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, mimo_p,
-                         u_t, params, n_rot, z, d_skip):
+                         u_t, params, n_rot, z, d_skip, dt_bias=None):
     """:func:`m3_step_inputs` + :func:`m3_step_gated_` in ONE launch
     (mamba.py:455-497): the step kernel computes delta = softplus(dt) and the
     BCNorm'ed, MIMO-folded Bc/Cc of each row from the raw projections itself,
     with the same arithmetic, so state and output are bit-identical to the two
     launches.  ``dt`` (B, D) and ``x_dbl`` (B, ld) float32 rows (x_dbl may be
-    the full x_proj output, B_raw / C_raw at columns off_b / off_c).
+    the full x_proj output, B_raw / C_raw at columns off_b / off_c); ``dt_bias``
+    as for :func:`m3_step_inputs`.
 
     Returns the gated output (B, D) float32, or None when the fused kernel does
     not serve this shape or layout (nothing launched; the caller runs the two
@@ -675,6 +697,7 @@ def m3_step_gated_fused_(state, dt, x_dbl, off_b, off_c, b_weight, c_weight, eps
         raise ValueError("m3_step_gated_fused_: both BCNorm weights or neither")
     wb = None if b_weight is None else b_weight.detach().to(torch.float32).contiguous()
     wc = None if c_weight is None else c_weight.detach().to(torch.float32).contiguous()
+    bias = None if dt_bias is None else dt_bias.detach().to(torch.float32).contiguous()
     out = torch.empty(B, D, device=dev, dtype=torch.float32)
     desc = StepDesc(B, D, N, int(n_rot), dt_du, M3_F32)
     if len(state) == 2:
@@ -684,8 +707,8 @@ def m3_step_gated_fused_(state, dt, x_dbl, off_b, off_c, b_weight, c_weight, eps
     with torch.cuda.device(dev):
         rc = lib.m3_step_gated_fused(desc, int(mimo_p), h.data_ptr(), ctypes_ptr(dbu),
                                      ctypes_ptr(fa), ctypes_ptr(fb), dt.data_ptr(), dt.stride(0),
-                                     x_dbl.data_ptr(), x_dbl.stride(0), int(off_b), int(off_c),
-                                     ctypes_ptr(wb), ctypes_ptr(wc), float(eps), uu.data_ptr(),
+                                     ctypes_ptr(bias), x_dbl.data_ptr(), x_dbl.stride(0),
+                                     int(off_b), int(off_c), ctypes_ptr(wb), ctypes_ptr(wc), float(eps), uu.data_ptr(),
                                      ar.data_ptr(), ai.data_ptr(), tk.data_ptr(), z.data_ptr(),
                                      z.stride(0), ds.data_ptr(), out.data_ptr(), _stream(dev))
     if rc == M3_ERR_UNSUPPORTED:

@@ -119,16 +119,25 @@ def test_layer_entry_points_validate_before_device_work():
     buf = ctypes.create_string_buffer(4096)
     p = ctypes.cast(buf, ctypes.c_void_p).value    # host memory: never dereferenced
     d = _sdesc()
-    # m3_step_inputs(desc, p, dt, ld_dt, xbc, ld_x, off_b, off_c, wb, wc, eps, delta, Bc, Cc, s)
-    assert lib.m3_step_inputs(None, 2, p, 64, p, 72, 8, 40, None, None, 1e-5, p, p, p, None) == 1
-    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 32, p, 72, 8, 40, None, None, 1e-5, p, p, p,
-                              None) == 2          # ld_dt < d_inner
-    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 64, p, 60, 8, 40, None, None, 1e-5, p, p, p,
-                              None) == 2          # C_raw past the row
-    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 64, p, 72, 8, 40, p, None, 1e-5, p, p, p,
-                              None) == 1          # one BCNorm weight without the other
-    assert lib.m3_step_inputs(ctypes.byref(d), 0, p, 64, p, 72, 8, 40, None, None, 1e-5, p, p, p,
-                              None) == 2          # mimo_p = 0
+    # m3_step_inputs(desc, p, dt, ld_dt, dt_bias, xbc, ld_x, off_b, off_c, wb, wc, eps,
+    #                delta, Bc, Cc, s)
+    assert lib.m3_step_inputs(None, 2, p, 64, None, p, 72, 8, 40, None, None, 1e-5, p, p, p,
+                              None) == 1
+    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 32, None, p, 72, 8, 40, None, None, 1e-5,
+                              p, p, p, None) == 2          # ld_dt < d_inner
+    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 64, None, p, 60, 8, 40, None, None, 1e-5,
+                              p, p, p, None) == 2          # C_raw past the row
+    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 64, None, p, 72, 8, 40, p, None, 1e-5,
+                              p, p, p, None) == 1          # one BCNorm weight without the other
+    assert lib.m3_step_inputs(ctypes.byref(d), 0, p, 64, None, p, 72, 8, 40, None, None, 1e-5,
+                              p, p, p, None) == 2          # mimo_p = 0
+    assert lib.m3_step_inputs(ctypes.byref(d), 2, p, 64, p + 2, p, 72, 8, 40, None, None, 1e-5,
+                              p, p, p, None) == 5          # misaligned dt_bias
+    # m3_silu(rows, d, x, ld_x, out, s)
+    assert lib.m3_silu(0, 64, p, 64, p, None) == 2
+    assert lib.m3_silu(4, 64, p, 32, p, None) == 2       # ld_x < d
+    assert lib.m3_silu(4, 64, None, 64, p, None) == 1
+    assert lib.m3_silu(4, 64, p + 1, 64, p, None) == 5
     # m3_step_inputs_bwd: a BCNorm backward without a workspace
     args = [ctypes.byref(d), 2, p, 64, p, 72, 8, 40, p, p, 1e-5, p, p, p, p, p, p, p, None, 0,
             None]

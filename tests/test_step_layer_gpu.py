@@ -49,6 +49,28 @@ def test_step_inputs_match_torch(bcnorm, n, p):
     assert _rel(cc, craw.reshape(B, n, p).sum(-1)) <= TOL
 
 
+@pytest.mark.parametrize("D,pad", [(1024, 0), (96, 4), (90, 3)])
+def test_step_inputs_bias_and_silu(D, pad):
+    """m3_step_inputs with the dt_proj bias passed apart equals it on dt + bias
+    (torch's matmul-then-add), on the float4 and the scalar path; m3_silu on a
+    row-strided view equals torch's silu bit for bit."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    B, n, p, R = 19, 32, 2, 8
+    base = torch.randn(B, D + pad, device="cuda", generator=g) * 6
+    dt = base[:, :D]                                   # row stride D + pad
+    bias = torch.randn(D, device="cuda", generator=g)
+    x_dbl = torch.randn(B, R + 2 * n * p, device="cuda", generator=g)
+    wb = torch.rand(n * p, device="cuda", generator=g) + 0.5
+    wc = torch.rand(n * p, device="cuda", generator=g) + 0.5
+    ref = S.m3_step_inputs((dt + bias).contiguous(), x_dbl, R, R + n * p, wb, wc, 1e-5, n, p)
+    got = S.m3_step_inputs(dt, x_dbl, R, R + n * p, wb, wc, 1e-5, n, p, dt_bias=bias)
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+    xz = torch.randn(B, 2 * D + pad, device="cuda", generator=g) * 5
+    u = S.m3_silu(xz[:, :D])
+    assert u.is_contiguous() and torch.equal(u, F.silu(xz[:, :D]))
+
+
 @pytest.mark.parametrize("B,D,N,n_track", [(37, 256, 32, 8), (6, 40, 64, 16), (9, 128, 32, 16)])
 def test_gated_step_equals_step_and_torch_epilogue(B, D, N, n_track):
     """Same state bits as m3_step_ / m3_step_factored_; output (y + u*D)*silu(z)."""
@@ -110,21 +132,24 @@ def test_step_gated_fused_equals_inputs_then_gated(B, D, n_track, p, bcnorm):
     hf, df = h0.clone(), d0.clone()
     hfa, fa, fb = h0.clone(), fa0.clone(), torch.empty_like(fa0)
     hua, ua, ub = h0.clone(), fa0.clone(), torch.empty_like(fa0)
-    for _ in range(3):
+    bias = torch.randn(D, device="cuda", generator=g)
+    for it in range(3):
         dt = torch.randn(B, D, device="cuda", generator=g) * 2 - 3
         dt[:, ::17] += 24.0                                     # above the threshold
         x_dbl = torch.randn(B, R + 2 * N * p, device="cuda", generator=g)
         u = torch.randn(B, D, device="cuda", generator=g)
         z = torch.randn(B, 2 * D, device="cuda", generator=g)[:, D:]
-        delta, bc, cc = S.m3_step_inputs(dt, x_dbl, R, R + N * p, wb, wc, 1e-5, N, p)
+        db = bias if it == 1 else None                          # dt_proj bias passed apart
+        delta, bc, cc = S.m3_step_inputs(dt, x_dbl, R, R + N * p, wb, wc, 1e-5, N, p,
+                                         dt_bias=db)
         ref = S.m3_step_gated_((hu, du_), delta, u, bc, cc, params, n_rot, z, d_skip)
         out = S.m3_step_gated_fused_((hf, df), dt, x_dbl, R, R + N * p, wb, wc, 1e-5, p, u,
-                                     params, n_rot, z, d_skip)
+                                     params, n_rot, z, d_skip, dt_bias=db)
         assert out is not None, "the fused step kernel should serve this shape"
         assert torch.equal(out, ref) and torch.equal(hf, hu) and torch.equal(df, du_)
         ref_f = S.m3_step_gated_((hua, ua, ub), delta, u, bc, cc, params, n_rot, z, d_skip)
         out_f = S.m3_step_gated_fused_((hfa, fa, fb), dt, x_dbl, R, R + N * p, wb, wc, 1e-5, p,
-                                       u, params, n_rot, z, d_skip)
+                                       u, params, n_rot, z, d_skip, dt_bias=db)
         assert torch.equal(out_f, ref_f) and torch.equal(hfa, hua) and torch.equal(fb, ub)
         fa, fb = fb, fa
         ua, ub = ub, ua
