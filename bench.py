@@ -459,7 +459,8 @@ def run_m3(args):
     sweep_info = run_l_sweep(dev, args) if (args.sweep and rank == 0) else None
     configs_info = run_configs(dev, args, clocks) if (args.configs and rank == 0) else None
     eval_info = run_model_eval(dev, args) if (args.model_train and rank == 0) else None
-    node_info = run_search_nodes(dev, args) if (args.rollout and rank == 0) else None
+    node_info = (run_search_nodes(dev, args) if (args.rollout and args.search and rank == 0)
+                 else None)
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -1238,6 +1239,8 @@ def main():
                     help="sub-batches the end-to-end leg streams each step's rows in "
                          "(default 16: measured 130 ms/step at 8192 rows against 147 with 4 "
                          "and 137 with 8; the copies then run near the PCIe limit)")
+    ap.add_argument("--no-search", dest="search", action="store_false",
+                    help="skip the batch-1 search-node line")
     ap.add_argument("--batch", type=int, default=0,
                     help="rows per GPU (default: config 4's global 8192 rows split over "
                          "the GPUs; smaller values are for profiler captures only)")
