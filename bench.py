@@ -998,6 +998,18 @@ def run_search_nodes(dev, args):
                 dt = time.perf_counter() - t0
                 out[name] = {"us_per_node": dt / len(moves) * 1e6,
                              "nodes_per_s": len(moves) / dt}
+            # evaluate_lines_fast: 32 candidate lines of 8 moves from the board
+            # (search_mamba.py:178-219), eager vs stepping a captured graph
+            lines = torch.randint(0, 8192, (32, 8), device=dev, generator=g)
+            for name, graphed in (("lines_eager", False), ("lines_graph", True)):
+                sm.evaluate_lines_fast(board, lines, graphed=graphed)   # warm-up / capture
+                torch.cuda.synchronize(dev)
+                t0 = time.perf_counter()
+                for _ in range(5):
+                    sm.evaluate_lines_fast(board, lines, graphed=graphed)
+                torch.cuda.synchronize(dev)
+                out[name] = {"ms_per_call": (time.perf_counter() - t0) / 5 * 1e3,
+                             "lines": 32, "moves": 8}
         sm.release_graphs()
         # the backbone's step graph alone by batch, with the prologue inside the
         # step kernel and as its own launch (Mamba3Block.fuse_step)

@@ -59,6 +59,7 @@ class SearchMamba(nn.Module):
             nn.Linear(d, d), nn.GELU(), nn.Linear(d, eval_dim))
         self.apply(self._init_weights)
         self._node_graph = None
+        self._line_graphs = {}
 
     def _init_weights(self, m):
         if isinstance(m, nn.Linear):
@@ -102,16 +103,31 @@ class SearchMamba(nn.Module):
                 for h, dbu in cache]
 
     @torch.no_grad()
-    def evaluate_lines_fast(self, board_encoding, move_sequences, lengths=None):
+    def evaluate_lines_fast(self, board_encoding, move_sequences, lengths=None, graphed=False):
+        """search_mamba.py:178-219.  ``graphed``: the K lines step through a
+        captured CUDA graph of the whole backbone step (one launch per move;
+        the graph for K lines is captured on first use and kept, see
+        ``release_graphs``); same results up to rounding (the graph runs the
+        fused step layer, the eager path the step kernel and torch's gate)."""
         device = self._device()
         _, cache = self.prime_board(board_encoding.to(device))
         K, L = move_sequences.shape
         move_sequences = move_sequences.to(device)
-        cache = self._expand_cache(cache, K)
         hiddens = []
-        for t in range(L):
-            hidden, cache = self.backbone.step_(token_id=move_sequences[:, t], cache=cache)
-            hiddens.append(hidden)
+        if graphed:
+            g = self._line_graphs.get(K)
+            if g is None:
+                g = self._line_graphs[K] = StepGraph(self.backbone, K)
+            for (h, d), (h1, d1) in zip(g.cache, cache):   # broadcast the board's state
+                h.copy_(h1.expand_as(h))
+                d.copy_(d1.expand_as(d))
+            for t in range(L):
+                hiddens.append(g.step(move_sequences[:, t])[0].clone())
+        else:
+            cache = self._expand_cache(cache, K)
+            for t in range(L):
+                hidden, cache = self.backbone.step_(token_id=move_sequences[:, t], cache=cache)
+                hiddens.append(hidden)
         hiddens = torch.stack(hiddens, dim=1)
         if lengths is not None:
             idx = (lengths.to(device).clamp(min=1) - 1).view(K, 1, 1).expand(-1, 1, hiddens.shape[-1])
@@ -162,8 +178,10 @@ class SearchMamba(nn.Module):
         return value.item(), logits.clone(), g.snapshot()
 
     def release_graphs(self):
-        """Drop the captured node graph (it is captured again on next use)."""
+        """Drop the captured graphs (node evaluation, line batches); they are
+        captured again on next use -- call after changing the weights."""
         self._node_graph = None
+        self._line_graphs = {}
 
     def dynamics_rollout(self, board_encoding, move_tokens):
         """Training rollout (search_mamba.py:252-273) as one causal scan.

@@ -115,3 +115,23 @@ def test_search_eval_step_graphed_matches_eval_step():
     # the caller's cache is untouched
     for (a, b), (c, d) in zip(keep, cache):
         assert torch.equal(a, c) and torch.equal(b, d)
+
+
+def test_search_evaluate_lines_fast_graphed_matches_eager():
+    torch.manual_seed(4)
+    scfg = SearchMambaConfig(d_model=48, n_layer=3, d_state=32, n_track_state=8, mimo_p=2,
+                             vocab_size=300)
+    sm = SearchMamba(scfg, vocab_size=300).cuda().eval()
+    board = torch.randint(1, 300, (24,), device="cuda")
+    lines = torch.randint(1, 300, (5, 6), device="cuda")
+    lengths = torch.tensor([6, 1, 3, 6, 2], device="cuda")
+    with torch.no_grad():
+        eager = sm.evaluate_lines_fast(board, lines, lengths)
+        graphed = sm.evaluate_lines_fast(board, lines, lengths, graphed=True)
+        again = sm.evaluate_lines_fast(board, lines, lengths, graphed=True)   # reused graph
+        slow = sm.evaluate_lines(board, lines)
+    assert torch.allclose(eager, graphed, atol=1e-5)
+    assert torch.equal(graphed, again)
+    full = lengths == lines.shape[1]
+    assert torch.allclose(slow[full], graphed[full], atol=1e-4)
+    sm.release_graphs()
