@@ -63,8 +63,10 @@ class StepGraph:
                 run(scratch)
         torch.cuda.current_stream(dev).wait_stream(side)
         del scratch
+        # thread-local capture: CUDA calls from other threads of the process
+        # (NCCL's watchdog in a multi-GPU job) do not invalidate it
         self.graph = torch.cuda.CUDAGraph()
-        with torch.no_grad(), torch.cuda.graph(self.graph):
+        with torch.no_grad(), torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
             self.outputs = run(self.cache)
         self.hidden = self.outputs[0]
 
