@@ -20,6 +20,7 @@
  *   redpanda/engine/mamba.py:455-497        step inputs + step + gated output in one launch
  *                                           -> m3_step_gated_fused
  *   redpanda/engine/mamba.py:262-265        (y + u*D) * silu(z) after a scan -> m3_gate
+ *                                           and its autograd backward -> m3_gate_bwd
  *   redpanda/engine/mamba.py:243, 452       u = silu(x half of in_proj) -> m3_silu
  *
  * Shapes (B batch, L length, D = d_inner, N = d_state, n_rot rotational lanes,
@@ -322,10 +323,32 @@ M3_API int m3_gate(int64_t rows, int32_t d_inner, const float* y, const void* u,
 /* m3_gate with an element type per operand (M3_F32 or M3_BF16): y, u, z and
  * out of a bf16 layer (mamba.py:262-265 under the reference's autocast,
  * train.py:268; the bf16 Eval-Mamba forward, model.py:110-132).  Arithmetic is
- * fp32; out is rounded once.  out may equal y only when dtype_out == dtype_y. */
+ * fp32; out is rounded once.  out may equal y only when dtype_out == dtype_y.
+ * round_silu != 0 rounds silu(z) to bf16 when z is bf16, as torch's F.silu on a
+ * bf16 tensor does before the product (the training path's autograd formula,
+ * mamba.py:265). */
 M3_API int m3_gate_typed(int64_t rows, int32_t d_inner, const void* y, int32_t dtype_y,
             const void* u, int32_t dtype_u, const void* z, int32_t dtype_z, int64_t ld_z,
-            const float* d_skip, float coef, void* out, int32_t dtype_out, void* stream);
+            const float* d_skip, float coef, int32_t round_silu, void* out, int32_t dtype_out,
+            void* stream);
+
+/* Workspace bytes of m3_gate_bwd (the per-row-chunk partial sums of d d_skip). */
+M3_API size_t m3_gate_bwd_workspace_bytes(int64_t rows, int32_t d_inner);
+
+/* Backward of m3_gate_typed (the autograd of mamba.py:262-265 / 496-497 in one
+ * launch plus a fixed-order reduction): with a = y + coef*u*d_skip,
+ * s = silu(z) (rounded as in the forward), sig = 1/(1+exp(-z)) and g the
+ * gradient of out (rows, D) of dtype_g:
+ *   d_y = g*s,  d_u = (g*s*d_skip)*coef,  d_z = (g*a)*sig*(1 + z*(1 - sig)),
+ *   d_dskip = sum over rows of g*s*coef*u (deterministic)
+ * in fp32, each rounded once to its input's element type; d_y, d_u, d_z are
+ * (rows, D) contiguous, d_dskip (D,) float32.
+ *   workspace >= m3_gate_bwd_workspace_bytes(rows, d_inner) bytes */
+M3_API int m3_gate_bwd(int64_t rows, int32_t d_inner, const void* y, int32_t dtype_y,
+            const void* u, int32_t dtype_u, const void* z, int32_t dtype_z, int64_t ld_z,
+            const float* d_skip, float coef, int32_t round_silu, const void* g, int32_t dtype_g,
+            void* d_y, void* d_u, void* d_z, float* d_dskip, void* workspace,
+            size_t workspace_bytes, void* stream);
 
 /* Size of the scratch buffer built into the library for m3_scan_bwd_noalloc. */
 #define M3_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)

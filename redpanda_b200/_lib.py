@@ -69,7 +69,11 @@ SIGNATURES = {
     "m3_gate": (ctypes.c_int, [ctypes.c_int64, _I, _P, _P, _I, _P, ctypes.c_int64, _P,
                                ctypes.c_float, _P, _P]),
     "m3_gate_typed": (ctypes.c_int, [ctypes.c_int64, _I, _P, _I, _P, _I, _P, _I,
-                                     ctypes.c_int64, _P, ctypes.c_float, _P, _I, _P]),
+                                     ctypes.c_int64, _P, ctypes.c_float, _I, _P, _I, _P]),
+    "m3_gate_bwd_workspace_bytes": (_Z, [ctypes.c_int64, _I]),
+    "m3_gate_bwd": (ctypes.c_int, [ctypes.c_int64, _I, _P, _I, _P, _I, _P, _I, ctypes.c_int64,
+                                   _P, ctypes.c_float, _I, _P, _I, _P, _P, _P, _P, _P, _Z,
+                                   _P]),
     "m3_step_gated": (ctypes.c_int, [_S, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                      ctypes.c_int64, _P, _P, _P]),
     "m3_step_gated_fused": (ctypes.c_int, [_S, _I, _P, _P, _P, _P, _P, ctypes.c_int64, _P, _P,

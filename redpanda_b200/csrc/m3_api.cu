@@ -692,13 +692,14 @@ int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p, const float* dt
 int m3_gate(int64_t rows, int32_t d_inner, const float* y, const void* u, int32_t dtype_u,
             const float* z, int64_t ld_z, const float* d_skip, float coef, float* out,
             void* stream) {
-  return m3_gate_typed(rows, d_inner, y, M3_F32, u, dtype_u, z, M3_F32, ld_z, d_skip, coef,
+  return m3_gate_typed(rows, d_inner, y, M3_F32, u, dtype_u, z, M3_F32, ld_z, d_skip, coef, 0,
                        out, M3_F32, stream);
 }
 
 int m3_gate_typed(int64_t rows, int32_t d_inner, const void* y, int32_t dtype_y, const void* u,
                   int32_t dtype_u, const void* z, int32_t dtype_z, int64_t ld_z,
-                  const float* d_skip, float coef, void* out, int32_t dtype_out, void* stream) {
+                  const float* d_skip, float coef, int32_t round_silu, void* out,
+                  int32_t dtype_out, void* stream) {
   if (rows < 1 || d_inner < 1 || ld_z < d_inner) return M3_ERR_SHAPE;
   if (!dtype_ok(dtype_y) || !dtype_ok(dtype_u) || !dtype_ok(dtype_z) || !dtype_ok(dtype_out))
     return M3_ERR_DTYPE;
@@ -718,7 +719,46 @@ int m3_gate_typed(int64_t rows, int32_t d_inner, const void* y, int32_t dtype_y,
   p.d_skip = d_skip; p.coef = coef;
   p.out = out; p.out_bf16 = dtype_out == M3_BF16;
   p.rows = rows; p.D = d_inner;
+  p.round_silu = round_silu != 0;
   cudaError_t e = launch_gate(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
+size_t m3_gate_bwd_workspace_bytes(int64_t rows, int32_t d_inner) {
+  if (rows < 1 || d_inner < 1) return 0;
+  return (size_t)gate_bwd_row_ctas(rows, d_inner) * d_inner * sizeof(float);
+}
+
+int m3_gate_bwd(int64_t rows, int32_t d_inner, const void* y, int32_t dtype_y, const void* u,
+                int32_t dtype_u, const void* z, int32_t dtype_z, int64_t ld_z,
+                const float* d_skip, float coef, int32_t round_silu, const void* g,
+                int32_t dtype_g, void* d_y, void* d_u, void* d_z, float* d_dskip,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  if (rows < 1 || d_inner < 1 || ld_z < d_inner) return M3_ERR_SHAPE;
+  if (!dtype_ok(dtype_y) || !dtype_ok(dtype_u) || !dtype_ok(dtype_z) || !dtype_ok(dtype_g))
+    return M3_ERR_DTYPE;
+  if (!y || !u || !z || !d_skip || !g || !d_y || !d_u || !d_z || !d_dskip) return M3_ERR_NULL;
+  if (!workspace || workspace_bytes < m3_gate_bwd_workspace_bytes(rows, d_inner))
+    return M3_ERR_WORKSPACE;
+  if (!aligned(y, dsize(dtype_y)) || !aligned(u, dsize(dtype_u)) || !aligned(z, dsize(dtype_z)) ||
+      !aligned(g, dsize(dtype_g)) || !aligned(d_y, dsize(dtype_y)) ||
+      !aligned(d_u, dsize(dtype_u)) || !aligned(d_z, dsize(dtype_z)) || !aligned(d_skip, 4) ||
+      !aligned(d_dskip, 4) || !aligned(workspace, 4))
+    return M3_ERR_ALIGN;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  GateBwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.y = y; p.y_bf16 = dtype_y == M3_BF16;
+  p.u = u; p.u_bf16 = dtype_u == M3_BF16;
+  p.z = z; p.z_bf16 = dtype_z == M3_BF16; p.ld_z = ld_z;
+  p.d_skip = d_skip; p.coef = coef; p.round_silu = round_silu != 0;
+  p.g = g; p.g_bf16 = dtype_g == M3_BF16;
+  p.dy = d_y; p.du = d_u; p.dz = d_z;
+  p.part = static_cast<float*>(workspace); p.d_dskip = d_dskip;
+  p.rows = rows; p.D = d_inner;
+  p.gx = gate_bwd_row_ctas(rows, d_inner);
+  cudaError_t e = launch_gate_bwd(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 

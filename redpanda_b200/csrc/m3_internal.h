@@ -179,8 +179,25 @@ struct GateParams {
   const float* d_skip; float coef;
   void* out; int out_bf16;
   long long rows; int D;
+  int round_silu;                             // silu(z) rounded to bf16 when z is bf16
 };
 cudaError_t launch_gate(const GateParams& p, cudaStream_t s);
+
+// Backward of out = (y + coef*u*d_skip) * silu(z) over (rows, D).
+struct GateBwdParams {
+  const void* y; int y_bf16;
+  const void* u; int u_bf16;
+  const void* z; int z_bf16; long long ld_z;
+  const float* d_skip; float coef; int round_silu;
+  const void* g; int g_bf16;                  // (rows, D) gradient of out
+  void* dy; void* du; void* dz;               // (rows, D), element types of y, u, z
+  float* part;                                // (gx, D) partial sums of d d_skip
+  float* d_dskip;                             // (D,)
+  long long rows; int D;
+  int gx;                                     // CTAs along the rows
+};
+int gate_bwd_row_ctas(long long rows, int d);
+cudaError_t launch_gate_bwd(const GateBwdParams& p, cudaStream_t s);
 
 // device error word of the current device
 int* device_err_ptr();

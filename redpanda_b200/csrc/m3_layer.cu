@@ -69,8 +69,10 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) step_inputs_kernel(const Inp
 // out = (y + coef*(u*d_skip)) * silu(z) over (rows, D): each warp walks rows
 // (grid-stride), its lanes the channels, four at a time when VEC (D % 4 == 0,
 // 16-byte aligned rows of fp32 y, u, z and out).
-__device__ __forceinline__ float gate_one(float y, float u, float z, float ds, float coef) {
-  const float sz = __fdiv_rn(z, __fadd_rn(1.0f, expf(-z)));
+__device__ __forceinline__ float gate_one(float y, float u, float z, float ds, float coef,
+                                         bool round_silu = false) {
+  float sz = __fdiv_rn(z, __fadd_rn(1.0f, expf(-z)));
+  if (round_silu) sz = __bfloat162float(__float2bfloat16_rn(sz));
   return __fmul_rn(__fadd_rn(y, __fmul_rn(coef, __fmul_rn(u, ds))), sz);
 }
 
@@ -104,7 +106,8 @@ __global__ void gate_kernel(const GateParams p) {
       const size_t zrow = (size_t)r * p.ld_z;
       for (int d = lane; d < p.D; d += 32) {
         const float v = gate_one(ld(p.y, row + d, p.y_bf16), ld(p.u, row + d, p.u_bf16),
-                                 ld(p.z, zrow + d, p.z_bf16), p.d_skip[d], p.coef);
+                                 ld(p.z, zrow + d, p.z_bf16), p.d_skip[d], p.coef,
+                                 p.round_silu && p.z_bf16);
         if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[row + d] = __float2bfloat16_rn(v);
         else static_cast<float*>(p.out)[row + d] = v;
       }
@@ -239,10 +242,82 @@ cudaError_t launch_gate(const GateParams& p, cudaStream_t s) {
   if (grid > (long long)sms * 16) grid = (long long)sms * 16;
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   const bool vec = !p.u_bf16 && !p.y_bf16 && !p.z_bf16 && !p.out_bf16 && (p.D % 4) == 0 &&
+                   !p.round_silu &&
                    (p.ld_z % 4) == 0 && a16(p.y) && a16(p.u) &&
                    a16(p.z) && a16(p.d_skip) && a16(p.out);
   if (vec) gate_kernel<true><<<(unsigned)grid, 256, 0, s>>>(p);
   else gate_kernel<false><<<(unsigned)grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+// Backward of the gated output out = (y + coef*u*ds) * s, s = silu(z)
+// (mamba.py:262-265, 496-497), everything in fp32 and each gradient rounded once
+// to its input's element type:
+//   ga = g * s                     d y  = ga
+//   d u = (ga * ds) * coef         d ds = sum over rows of ga * (coef * u)
+//   d z = (g * a) * sig * (1 + z * (1 - sig)),  a = y + coef*u*ds, sig = 1/(1+exp(-z))
+// Thread = one channel, CTA (x, y) = rows chunk x of channel block y, so the
+// d ds partial of each (chunk, channel) is one sequential sum; gate_bwd_reduce
+// adds the chunks in order: deterministic.
+__global__ void __launch_bounds__(256) gate_bwd_kernel(const GateBwdParams p) {
+  const int d = blockIdx.y * 256 + threadIdx.x;
+  if (d >= p.D) return;   // no barrier in this kernel
+  const long long per = (p.rows + p.gx - 1) / p.gx;
+  const long long r0 = (long long)blockIdx.x * per;
+  const long long r1 = r0 + per < p.rows ? r0 + per : p.rows;
+  auto ld = [](const void* base, size_t i, int bf) {
+    return bf ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
+              : static_cast<const float*>(base)[i];
+  };
+  auto st = [](void* base, size_t i, float v, int bf) {
+    if (bf) static_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+    else static_cast<float*>(base)[i] = v;
+  };
+  const float ds = p.d_skip[d];
+  const bool rs = p.round_silu && p.z_bf16;
+  float acc = 0.f;
+#pragma unroll 4
+  for (long long r = r0; r < r1; ++r) {
+    const size_t i = (size_t)r * p.D + d;
+    const float y = ld(p.y, i, p.y_bf16), u = ld(p.u, i, p.u_bf16);
+    const float z = ld(p.z, (size_t)r * p.ld_z + d, p.z_bf16), g = ld(p.g, i, p.g_bf16);
+    const float e1 = __fadd_rn(1.0f, expf(-z));
+    float s = __fdiv_rn(z, e1);
+    if (rs) s = __bfloat162float(__float2bfloat16_rn(s));
+    const float sig = __fdiv_rn(1.0f, e1);
+    const float cu = __fmul_rn(p.coef, u);
+    const float a = __fadd_rn(y, __fmul_rn(p.coef, __fmul_rn(u, ds)));
+    const float ga = __fmul_rn(g, s);
+    st(p.dy, i, ga, p.y_bf16);
+    st(p.du, i, __fmul_rn(__fmul_rn(ga, ds), p.coef), p.u_bf16);
+    acc = __fmaf_rn(ga, cu, acc);
+    const float dsz = __fmul_rn(sig, __fadd_rn(1.0f, __fmul_rn(z, __fsub_rn(1.0f, sig))));
+    st(p.dz, i, __fmul_rn(__fmul_rn(g, a), dsz), p.z_bf16);
+  }
+  p.part[(size_t)blockIdx.x * p.D + d] = acc;
+}
+
+__global__ void gate_bwd_reduce(const float* part, int gx, int D, float* out) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  float s = part[d];
+  for (int x = 1; x < gx; ++x) s = __fadd_rn(s, part[(size_t)x * D + d]);
+  out[d] = s;
+}
+
+int gate_bwd_row_ctas(long long rows, int d) {
+  const int cb = (d + 255) / 256;
+  long long gx = (148LL * 4 + cb - 1) / cb;   // about four CTAs per SM of a 148-SM B200
+  if (gx > rows) gx = rows;
+  return gx < 1 ? 1 : (int)gx;
+}
+
+cudaError_t launch_gate_bwd(const GateBwdParams& p, cudaStream_t s) {
+  dim3 grid(p.gx, (p.D + 255) / 256);
+  gate_bwd_kernel<<<grid, 256, 0, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  gate_bwd_reduce<<<(p.D + 255) / 256, 256, 0, s>>>(p.part, p.gx, p.D, p.d_dskip);
   return cudaGetLastError();
 }
 

@@ -325,7 +325,7 @@ class Mamba3Block(nn.Module):
             y = self._fused_scan(x_branch, x_dbl, dt,
                                  S.M3_DIR_BIDIR if cfg.bidirectional else S.M3_DIR_FWD)
             if y is not None:
-                return self.out_proj((y + coef * x_branch * self.D) * F.silu(z))
+                return self.out_proj(self._gated(y, x_branch, z, coef))
         delta, bc, cc = self._ssm_inputs(x_branch, x_dbl, dt)
         yd = None
         if _bf16_layer():   # the kernels' bf16 configuration (autograd casts the grads back)
@@ -338,7 +338,14 @@ class Mamba3Block(nn.Module):
             y = S.m3_trapezoidal_scan(*args, y_dtype=yd)
         else:
             y = S.m3_bidir_scan(*args, y_dtype=yd)
-        return self.out_proj((y + coef * x_branch * self.D) * F.silu(z))
+        return self.out_proj(self._gated(y, x_branch, z, coef))
+
+    def _gated(self, y, u, z, coef):
+        """(y + coef*u*D) * silu(z) (mamba.py:262-265) with autograd, one launch
+        each way (S.gated_output); a bf16 layer gets its output in bf16, the
+        type autocast's out_proj casts it to anyway."""
+        return S.gated_output(y, u, z, self.D, coef,
+                              out_dtype=torch.bfloat16 if _bf16_layer() else None)
 
     def forward_with_state(self, x):
         """mamba.py:269-282: output and the (h_last, dBu_last) state."""

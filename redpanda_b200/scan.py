@@ -584,7 +584,7 @@ def step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mimo_
                                mimo_p)
 
 
-def m3_gate(y, u, z, d_skip, coef=1.0, out=None, out_dtype=None):
+def m3_gate(y, u, z, d_skip, coef=1.0, out=None, out_dtype=None, round_silu=False):
     """(y + coef*u*D) * silu(z) in one launch (mamba.py:262-265).
 
     y, u: (..., D) contiguous, float32 or bfloat16; z: (..., D) float32 or
@@ -606,9 +606,62 @@ def m3_gate(y, u, z, d_skip, coef=1.0, out=None, out_dtype=None):
     with torch.cuda.device(dev):
         _lib.check(lib.m3_gate_typed(rows, D, y.data_ptr(), _dt_code(y.dtype), u.data_ptr(),
                                      _dt_code(u.dtype), zz.data_ptr(), _dt_code(zz.dtype),
-                                     zz.stride(0), ds.data_ptr(), float(coef), out.data_ptr(),
-                                     _dt_code(out.dtype), _stream(dev)))
+                                     zz.stride(0), ds.data_ptr(), float(coef), int(round_silu),
+                                     out.data_ptr(), _dt_code(out.dtype), _stream(dev)))
     return out
+
+
+class _GateFn(torch.autograd.Function):
+    """out = (y + coef*u*D) * silu(z) (mamba.py:262-265, 496-497) with its
+    backward in one launch (m3_gate / m3_gate_bwd) instead of five elementwise
+    ops forward and about eight backward.  silu(z) of a bf16 z is rounded to
+    bf16 as F.silu does, so the forward equals torch's formula bit for bit;
+    the gradients are computed in fp32 and rounded once (torch rounds some
+    intermediates to bf16, so they agree to bf16 rounding)."""
+
+    @staticmethod
+    def forward(ctx, y, u, z, d_skip, coef, out_dtype):
+        y, u = y.contiguous(), u.contiguous()
+        out = m3_gate(y, u, z, d_skip, coef, out_dtype=out_dtype, round_silu=True)
+        ctx.save_for_backward(y, u, z, d_skip)
+        ctx.coef = float(coef)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        y, u, z, d_skip = ctx.saved_tensors
+        lib = _lib.load()
+        dev = y.device
+        D = y.shape[-1]
+        rows = y.numel() // D
+        zz = z.reshape(rows, D) if z.dim() > 2 else z
+        g = g.contiguous()
+        if g.dtype not in (torch.float32, torch.bfloat16):
+            g = g.float()
+        ds = d_skip.detach().to(torch.float32).contiguous()
+        dy = torch.empty_like(y)
+        du = torch.empty_like(u)
+        dz = torch.empty(z.shape, device=dev, dtype=z.dtype)
+        dds = torch.empty(D, device=dev, dtype=torch.float32)
+        nws = lib.m3_gate_bwd_workspace_bytes(rows, D)
+        ws = torch.empty(max(1, nws), device=dev, dtype=torch.uint8)
+        with torch.cuda.device(dev):
+            _lib.check(lib.m3_gate_bwd(rows, D, y.data_ptr(), _dt_code(y.dtype), u.data_ptr(),
+                                       _dt_code(u.dtype), zz.data_ptr(), _dt_code(zz.dtype),
+                                       zz.stride(0), ds.data_ptr(), ctx.coef, 1, g.data_ptr(),
+                                       _dt_code(g.dtype), dy.data_ptr(), du.data_ptr(),
+                                       dz.data_ptr(), dds.data_ptr(), ws.data_ptr(), nws,
+                                       _stream(dev)))
+        return dy, du, dz, dds.to(d_skip.dtype), None, None
+
+
+def gated_output(y, u, z, d_skip, coef=1.0, out_dtype=None):
+    """Differentiable (y + coef*u*d_skip) * silu(z) (mamba.py:262-265) on the
+    kernels; ``out_dtype`` defaults to torch's promotion of the operands."""
+    if out_dtype is None:
+        out_dtype = torch.promote_types(torch.promote_types(y.dtype, u.dtype),
+                                        torch.promote_types(z.dtype, d_skip.dtype))
+    return _GateFn.apply(y, u, z, d_skip, coef, out_dtype)
 
 
 def m3_step_gated_(state, delta_t, u_t, Bc_t, Cc_t, params, n_rot, z, d_skip):

@@ -143,6 +143,16 @@ def test_layer_entry_points_validate_before_device_work():
             None]
     assert lib.m3_step_inputs_bwd(*args) == 6
     assert lib.m3_step_inputs_bwd_workspace_bytes(ctypes.byref(d), 2) > 0
+    # m3_gate_bwd(rows, D, y, dty, u, dtu, z, dtz, ld_z, d_skip, coef, round, g, dtg,
+    #             d_y, d_u, d_z, d_dskip, ws, ws_bytes, s)
+    need = lib.m3_gate_bwd_workspace_bytes(64, 96)
+    assert need >= 96 * 4 and lib.m3_gate_bwd_workspace_bytes(0, 96) == 0
+    gb = [64, 96, p, 1, p, 1, p, 1, 192, p, 2.0, 1, p, 0, p, p, p, p, p, need, None]
+    assert lib.m3_gate_bwd(*(gb[:8] + [64] + gb[9:])) == 2                 # ld_z < D
+    assert lib.m3_gate_bwd(*(gb[:13] + [7] + gb[14:])) == 3                # dtype of g
+    assert lib.m3_gate_bwd(*(gb[:12] + [None] + gb[13:])) == 1             # no g
+    assert lib.m3_gate_bwd(*(gb[:19] + [need - 4] + gb[20:])) == 6         # workspace
+    assert lib.m3_gate_bwd(*(gb[:2] + [p + 1] + gb[3:])) == 5              # misaligned y
     # m3_gate(rows, D, y, u, dtype_u, z, ld_z, d_skip, coef, out, s)
     assert lib.m3_gate(0, 64, p, p, 0, p, 64, p, 1.0, p, None) == 2
     assert lib.m3_gate(4, 64, p, p, 0, p, 32, p, 1.0, p, None) == 2    # ld_z < D

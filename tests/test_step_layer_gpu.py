@@ -293,6 +293,43 @@ def test_inference_forward_equals_autograd_forward(bidir):
             assert _rel(h1, h2) <= 1e-5 and _rel(d1, d2) <= 1e-5
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("coef", [1.0, 2.0])
+def test_gated_output_fn_matches_torch_autograd(dtype, coef):
+    """S.gated_output (m3_gate forward, m3_gate_bwd backward) against torch's
+    autograd of (y + coef*u*D) * silu(z) with z a view of in_proj's output:
+    the forward bit for bit; the gradients within fp32 rounding (fp32) or
+    bf16 rounding (bf16: torch rounds some intermediates to bf16, the kernel
+    rounds each gradient once)."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    B, L, D = 3, 37, 96
+    xz0 = (torch.randn(B, L, 2 * D, device="cuda", generator=g) * 3).to(dtype)
+    y0 = torch.randn(B, L, D, device="cuda", generator=g).to(dtype)
+    u0 = torch.randn(B, L, D, device="cuda", generator=g).to(dtype)
+    d0 = torch.randn(D, device="cuda", generator=g)
+    go = torch.randn(B, L, D, device="cuda", generator=g)
+    leaves = []
+    for _ in range(2):
+        leaves.append([t.clone().requires_grad_() for t in (xz0, y0, u0, d0)])
+    (xa, ya, ua, da), (xb, yb, ub, db) = leaves
+    ref = (ya + coef * ua * da) * F.silu(xa[..., D:])
+    ref.backward(go)
+    out = S.gated_output(yb, ub, xb[..., D:], db, coef)
+    out.backward(go)
+    assert out.dtype == ref.dtype and torch.equal(out, ref)
+    tol = 1e-6 if dtype == torch.float32 else 1e-2
+    for a, b in ((xa, xb), (ya, yb), (ua, ub), (da, db)):
+        assert a.grad.dtype == b.grad.dtype
+        assert _rel(b.grad.float(), a.grad.float()) <= tol, (a.shape, _rel(b.grad, a.grad))
+    assert xb.grad[..., :D].abs().max().item() == 0.0
+    # deterministic: the d_skip reduction has a fixed order
+    first = db.grad.clone()
+    for t in leaves[1]:
+        t.grad = None
+    S.gated_output(yb, ub, xb[..., D:], db, coef).backward(go)
+    assert torch.equal(db.grad, first)
+
+
 @pytest.mark.parametrize("bcnorm", [True, False])
 def test_step_inputs_backward_matches_torch_autograd(bcnorm):
     """m3_step_inputs_bwd: the gradients torch's softplus / RMSNorm / sum give."""
