@@ -256,45 +256,109 @@ cudaError_t launch_gate(const GateParams& p, cudaStream_t s) {
 //   ga = g * s                     d y  = ga
 //   d u = (ga * ds) * coef         d ds = sum over rows of ga * (coef * u)
 //   d z = (g * a) * sig * (1 + z * (1 - sig)),  a = y + coef*u*ds, sig = 1/(1+exp(-z))
-// Thread = one channel, CTA (x, y) = rows chunk x of channel block y, so the
-// d ds partial of each (chunk, channel) is one sequential sum; gate_bwd_reduce
-// adds the chunks in order: deterministic.
-__global__ void __launch_bounds__(256) gate_bwd_kernel(const GateBwdParams p) {
-  const int d = blockIdx.y * 256 + threadIdx.x;
-  if (d >= p.D) return;   // no barrier in this kernel
+// A thread owns kGateVec consecutive channels (one 8- or 16-byte access per
+// operand and row), CTA (x, y) = rows chunk x of channel block y, so the d ds
+// partial of each (chunk, channel) is one sequential sum over the chunk's rows;
+// gate_bwd_reduce adds the chunks in order: deterministic.
+constexpr int kGateVec = 4;
+constexpr int kGateThreads = 128;
+
+template <int V>
+__device__ __forceinline__ void gate_ld(const void* base, size_t i, int bf, float (&v)[V]) {
+  if constexpr (V == 4) {   // one 8- or 16-byte access (the caller checked the alignment)
+    if (bf) {
+      const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(base) + i);
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+      const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + i);
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    }
+    return;
+  }
+  if (bf) {
+    const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(base) + i;
+#pragma unroll
+    for (int k = 0; k < V; ++k) v[k] = __bfloat162float(b[k]);
+  } else {
+    const float* f = static_cast<const float*>(base) + i;
+#pragma unroll
+    for (int k = 0; k < V; ++k) v[k] = f[k];
+  }
+}
+template <int V>
+__device__ __forceinline__ void gate_st(void* base, size_t i, int bf, const float (&v)[V]) {
+  if constexpr (V == 4) {
+    if (bf) {
+      const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+      const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+      uint2 w;
+      w.x = *reinterpret_cast<const uint32_t*>(&a);
+      w.y = *reinterpret_cast<const uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(base) + i) = w;
+    } else {
+      *reinterpret_cast<float4*>(static_cast<float*>(base) + i) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    return;
+  }
+  if (bf) {
+    __nv_bfloat16* b = static_cast<__nv_bfloat16*>(base) + i;
+#pragma unroll
+    for (int k = 0; k < V; ++k) b[k] = __float2bfloat16_rn(v[k]);
+  } else {
+    float* f = static_cast<float*>(base) + i;
+#pragma unroll
+    for (int k = 0; k < V; ++k) f[k] = v[k];
+  }
+}
+
+// VEC: kGateVec channels per thread (D % kGateVec == 0 and every row of every
+// operand aligned to kGateVec elements); otherwise one channel per thread.
+template <bool VEC>
+__global__ void __launch_bounds__(kGateThreads) gate_bwd_kernel(const GateBwdParams p) {
+  constexpr int V = VEC ? kGateVec : 1;
+  const int d0 = (blockIdx.y * kGateThreads + threadIdx.x) * V;
+  if (d0 >= p.D) return;   // no barrier in this kernel
   const long long per = (p.rows + p.gx - 1) / p.gx;
   const long long r0 = (long long)blockIdx.x * per;
   const long long r1 = r0 + per < p.rows ? r0 + per : p.rows;
-  auto ld = [](const void* base, size_t i, int bf) {
-    return bf ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
-              : static_cast<const float*>(base)[i];
-  };
-  auto st = [](void* base, size_t i, float v, int bf) {
-    if (bf) static_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
-    else static_cast<float*>(base)[i] = v;
-  };
-  const float ds = p.d_skip[d];
   const bool rs = p.round_silu && p.z_bf16;
-  float acc = 0.f;
-#pragma unroll 4
-  for (long long r = r0; r < r1; ++r) {
-    const size_t i = (size_t)r * p.D + d;
-    const float y = ld(p.y, i, p.y_bf16), u = ld(p.u, i, p.u_bf16);
-    const float z = ld(p.z, (size_t)r * p.ld_z + d, p.z_bf16), g = ld(p.g, i, p.g_bf16);
-    const float e1 = __fadd_rn(1.0f, expf(-z));
-    float s = __fdiv_rn(z, e1);
-    if (rs) s = __bfloat162float(__float2bfloat16_rn(s));
-    const float sig = __fdiv_rn(1.0f, e1);
-    const float cu = __fmul_rn(p.coef, u);
-    const float a = __fadd_rn(y, __fmul_rn(p.coef, __fmul_rn(u, ds)));
-    const float ga = __fmul_rn(g, s);
-    st(p.dy, i, ga, p.y_bf16);
-    st(p.du, i, __fmul_rn(__fmul_rn(ga, ds), p.coef), p.u_bf16);
-    acc = __fmaf_rn(ga, cu, acc);
-    const float dsz = __fmul_rn(sig, __fadd_rn(1.0f, __fmul_rn(z, __fsub_rn(1.0f, sig))));
-    st(p.dz, i, __fmul_rn(__fmul_rn(g, a), dsz), p.z_bf16);
+  float ds[V], acc[V];
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    ds[k] = p.d_skip[d0 + k];
+    acc[k] = 0.f;
   }
-  p.part[(size_t)blockIdx.x * p.D + d] = acc;
+#pragma unroll 2
+  for (long long r = r0; r < r1; ++r) {
+    const size_t i = (size_t)r * p.D + d0;
+    float y[V], u[V], z[V], g[V], oy[V], ou[V], oz[V];
+    gate_ld<V>(p.y, i, p.y_bf16, y);
+    gate_ld<V>(p.u, i, p.u_bf16, u);
+    gate_ld<V>(p.z, (size_t)r * p.ld_z + d0, p.z_bf16, z);
+    gate_ld<V>(p.g, i, p.g_bf16, g);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float e1 = __fadd_rn(1.0f, expf(-z[k]));
+      float s = __fdiv_rn(z[k], e1);
+      if (rs) s = __bfloat162float(__float2bfloat16_rn(s));
+      const float sig = __fdiv_rn(1.0f, e1);
+      const float a = __fadd_rn(y[k], __fmul_rn(p.coef, __fmul_rn(u[k], ds[k])));
+      const float ga = __fmul_rn(g[k], s);
+      oy[k] = ga;
+      ou[k] = __fmul_rn(__fmul_rn(ga, ds[k]), p.coef);
+      acc[k] = __fmaf_rn(ga, __fmul_rn(p.coef, u[k]), acc[k]);
+      const float dsz =
+          __fmul_rn(sig, __fadd_rn(1.0f, __fmul_rn(z[k], __fsub_rn(1.0f, sig))));
+      oz[k] = __fmul_rn(__fmul_rn(g[k], a), dsz);
+    }
+    gate_st<V>(p.dy, i, p.y_bf16, oy);
+    gate_st<V>(p.du, i, p.u_bf16, ou);
+    gate_st<V>(p.dz, i, p.z_bf16, oz);
+  }
+#pragma unroll
+  for (int k = 0; k < V; ++k) p.part[(size_t)blockIdx.x * p.D + d0 + k] = acc[k];
 }
 
 __global__ void gate_bwd_reduce(const float* part, int gx, int D, float* out) {
@@ -306,15 +370,23 @@ __global__ void gate_bwd_reduce(const float* part, int gx, int D, float* out) {
 }
 
 int gate_bwd_row_ctas(long long rows, int d) {
-  const int cb = (d + 255) / 256;
+  const int cb = (d + kGateThreads * kGateVec - 1) / (kGateThreads * kGateVec);
   long long gx = (148LL * 4 + cb - 1) / cb;   // about four CTAs per SM of a 148-SM B200
   if (gx > rows) gx = rows;
   return gx < 1 ? 1 : (int)gx;
 }
 
 cudaError_t launch_gate_bwd(const GateBwdParams& p, cudaStream_t s) {
-  dim3 grid(p.gx, (p.D + 255) / 256);
-  gate_bwd_kernel<<<grid, 256, 0, s>>>(p);
+  auto al = [](const void* q, int bf) {
+    return (reinterpret_cast<uintptr_t>(q) & (bf ? 2 * kGateVec - 1 : 4 * kGateVec - 1)) == 0;
+  };
+  const bool vec = p.D % kGateVec == 0 && p.ld_z % kGateVec == 0 && al(p.y, p.y_bf16) &&
+                   al(p.u, p.u_bf16) && al(p.z, p.z_bf16) && al(p.g, p.g_bf16) &&
+                   al(p.dy, p.y_bf16) && al(p.du, p.u_bf16) && al(p.dz, p.z_bf16);
+  const int per_block = kGateThreads * (vec ? kGateVec : 1);
+  dim3 grid(p.gx, (p.D + per_block - 1) / per_block);
+  if (vec) gate_bwd_kernel<true><<<grid, kGateThreads, 0, s>>>(p);
+  else gate_bwd_kernel<false><<<grid, kGateThreads, 0, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   gate_bwd_reduce<<<(p.D + 255) / 256, 256, 0, s>>>(p.part, p.gx, p.D, p.d_dskip);
