@@ -233,17 +233,19 @@ M3_API int m3_step_factored(const m3_step_desc* desc, float* h, const float* fac
  *   Bc, Cc (B, N) = sum over the p MIMO columns of BCNorm(B_raw), BCNorm(C_raw)
  * with BCNorm(x) = x * rsqrt(mean(x^2) + eps) * w over the N*p vector
  * (mamba.py:82-89, 297-299, 336-337).
- *   dt      (B, ld_dt) float32: dt_proj(dt_raw), with its bias or without it
+ *   dt      (B, ld_dt) desc->dtype_du: dt_proj(dt_raw), with its bias or without it
  *   dt_bias (D,) float32 dt_proj bias, added to dt first (one fp32 rounding, as
  *           torch's matmul-then-add), or NULL when dt includes it
- *   xbc     (B, ld_x)  float32: rows of x_proj's output; B_raw starts at column
- *           off_b and C_raw at off_c, N*p columns each
+ *   xbc     (B, ld_x) desc->dtype_bc: rows of x_proj's output; B_raw starts at
+ *           column off_b and C_raw at off_c, N*p columns each
  *   wb, wc  (N*p,) float32 BCNorm weights, or both NULL (use_bcnorm=False: plain sum)
- * desc->n_rot, dtype_du and dtype_bc are ignored; all outputs are float32. */
+ *   delta   (B, D) desc->dtype_du; Bc, Cc (B, N) desc->dtype_bc
+ * Arithmetic is fp32; a bf16 output is rounded once (the bits of the fp32
+ * result cast to bf16, as a bf16 layer's casts give).  desc->n_rot is ignored. */
 M3_API int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p,
-            const float* dt, int64_t ld_dt, const float* dt_bias, const float* xbc,
+            const void* dt, int64_t ld_dt, const float* dt_bias, const void* xbc,
             int64_t ld_x, int32_t off_b, int32_t off_c, const float* wb, const float* wc,
-            float eps, float* delta, float* Bc, float* Cc, void* stream);
+            float eps, void* delta, void* Bc, void* Cc, void* stream);
 
 /* u = silu(x) = x / (1 + exp(-x)) over (rows, d) of a row-strided x: the x half
  * of in_proj's output (mamba.py:243, 452), read in place; out (rows, d) float32
@@ -257,19 +259,20 @@ M3_API size_t m3_step_inputs_bwd_workspace_bytes(const m3_step_desc* desc, int32
 /* Backward of m3_step_inputs over desc->batch rows (the training-path prologue:
  * the gradients that torch's softplus, RMSNorm and sum backward give for
  * mamba.py:284-301 and 336-337):
- *   g_delta (rows, D), g_Bc, g_Cc (rows, N)  float32 upstream gradients
- *   d_dt    (rows, D) float32 = g_delta * softplus'(dt)
- *   d_xbc   (rows, ld_x) float32: columns [off_b, off_b + N*p) and
- *           [off_c, off_c + N*p) are written (the gradients of B_raw, C_raw);
- *           other columns are left untouched
+ *   dt, g_delta, d_dt       (rows, D) of desc->dtype_du; d_dt = g_delta * softplus'(dt)
+ *   xbc, d_xbc              (rows, ld_x) of desc->dtype_bc: columns [off_b, off_b + N*p)
+ *                           and [off_c, off_c + N*p) of d_xbc are written (the gradients
+ *                           of B_raw, C_raw); other columns are left untouched
+ *   g_Bc, g_Cc              (rows, N) of desc->dtype_bc: upstream gradients
  *   d_wb, d_wc (N*p,) float32 BCNorm weight gradients, reduced over the rows in a
  *           fixed order (bitwise reproducible); unused when wb == wc == NULL
- *   workspace >= m3_step_inputs_bwd_workspace_bytes(desc, mimo_p) bytes */
+ *   workspace >= m3_step_inputs_bwd_workspace_bytes(desc, mimo_p) bytes
+ * Arithmetic is fp32; bf16 gradients are rounded once. */
 M3_API int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p,
-            const float* dt, int64_t ld_dt, const float* xbc, int64_t ld_x,
+            const void* dt, int64_t ld_dt, const void* xbc, int64_t ld_x,
             int32_t off_b, int32_t off_c, const float* wb, const float* wc, float eps,
-            const float* g_delta, const float* g_Bc, const float* g_Cc,
-            float* d_dt, float* d_xbc, float* d_wb, float* d_wc,
+            const void* g_delta, const void* g_Bc, const void* g_Cc,
+            void* d_dt, void* d_xbc, float* d_wb, float* d_wc,
             void* workspace, size_t workspace_bytes, void* stream);
 
 /* m3_step (dbu != NULL) or m3_step_factored (fac_prev, fac_next != NULL, dbu

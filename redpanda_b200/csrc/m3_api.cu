@@ -605,20 +605,22 @@ int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* h, floa
                      track_p, out, stream, z, ld_z, d_skip, &pro);
 }
 
-int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const float* dt, int64_t ld_dt,
-                   const float* dt_bias, const float* xbc, int64_t ld_x, int32_t off_b,
-                   int32_t off_c, const float* wb, const float* wc, float eps, float* delta,
-                   float* Bc, float* Cc, void* stream) {
+int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const void* dt, int64_t ld_dt,
+                   const float* dt_bias, const void* xbc, int64_t ld_x, int32_t off_b,
+                   int32_t off_c, const float* wb, const float* wc, float eps, void* delta,
+                   void* Bc, void* Cc, void* stream) {
   if (!desc) return M3_ERR_NULL;
   const int64_t np = (int64_t)desc->d_state * mimo_p;
   if (desc->batch < 1 || desc->d_inner < 1 || desc->d_state < 1 || mimo_p < 1 ||
       ld_dt < desc->d_inner || off_b < 0 || off_c < 0 || off_b + np > ld_x ||
       off_c + np > ld_x || !(eps >= 0.f))
     return M3_ERR_SHAPE;
+  if (!dtype_ok(desc->dtype_du) || !dtype_ok(desc->dtype_bc)) return M3_ERR_DTYPE;
   if (!dt || !xbc || !delta || !Bc || !Cc || ((wb == nullptr) != (wc == nullptr)))
     return M3_ERR_NULL;
-  if (!aligned(dt, 4) || !aligned(xbc, 4) || !aligned(delta, 4) || !aligned(Bc, 4) ||
-      !aligned(Cc, 4) || (wb && (!aligned(wb, 4) || !aligned(wc, 4))) ||
+  const int esd = dsize(desc->dtype_du), esb = dsize(desc->dtype_bc);
+  if (!aligned(dt, esd) || !aligned(xbc, esb) || !aligned(delta, esd) || !aligned(Bc, esb) ||
+      !aligned(Cc, esb) || (wb && (!aligned(wb, 4) || !aligned(wc, 4))) ||
       (dt_bias && !aligned(dt_bias, 4)))
     return M3_ERR_ALIGN;
   int rc = check_device();
@@ -629,7 +631,9 @@ int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const float* dt, in
   p.xbc = xbc; p.ld_x = ld_x; p.off_b = off_b; p.off_c = off_c;
   p.wb = wb; p.wc = wc; p.eps = eps; p.delta = delta; p.Bc = Bc; p.Cc = Cc;
   p.B = desc->batch; p.D = desc->d_inner; p.N = desc->d_state; p.P = mimo_p;
-  p.vec4 = (desc->d_inner % 4) == 0 && ld_dt % 4 == 0 && aligned(dt, 16) &&
+  p.du_bf16 = desc->dtype_du == M3_BF16;
+  p.bc_bf16 = desc->dtype_bc == M3_BF16;
+  p.vec4 = !p.du_bf16 && (desc->d_inner % 4) == 0 && ld_dt % 4 == 0 && aligned(dt, 16) &&
            aligned(delta, 16) && (!dt_bias || aligned(dt_bias, 16));
   cudaError_t e = launch_step_inputs(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
@@ -655,11 +659,11 @@ size_t m3_step_inputs_bwd_workspace_bytes(const m3_step_desc* desc, int32_t mimo
   return (size_t)step_inputs_bwd_ctas(desc->batch) * 2 * np * sizeof(float);
 }
 
-int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p, const float* dt,
-                       int64_t ld_dt, const float* xbc, int64_t ld_x, int32_t off_b,
+int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p, const void* dt,
+                       int64_t ld_dt, const void* xbc, int64_t ld_x, int32_t off_b,
                        int32_t off_c, const float* wb, const float* wc, float eps,
-                       const float* g_delta, const float* g_Bc, const float* g_Cc,
-                       float* d_dt, float* d_xbc, float* d_wb, float* d_wc, void* workspace,
+                       const void* g_delta, const void* g_Bc, const void* g_Cc,
+                       void* d_dt, void* d_xbc, float* d_wb, float* d_wc, void* workspace,
                        size_t workspace_bytes, void* stream) {
   if (!desc) return M3_ERR_NULL;
   const int64_t np = (int64_t)desc->d_state * mimo_p;
@@ -670,8 +674,10 @@ int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p, const float* dt
   if (!dt || !xbc || !g_delta || !g_Bc || !g_Cc || !d_dt || !d_xbc ||
       ((wb == nullptr) != (wc == nullptr)) || (wb && (!d_wb || !d_wc)))
     return M3_ERR_NULL;
-  if (!aligned(dt, 4) || !aligned(xbc, 4) || !aligned(g_delta, 4) || !aligned(g_Bc, 4) ||
-      !aligned(g_Cc, 4) || !aligned(d_dt, 4) || !aligned(d_xbc, 4) ||
+  if (!dtype_ok(desc->dtype_du) || !dtype_ok(desc->dtype_bc)) return M3_ERR_DTYPE;
+  const int esd = dsize(desc->dtype_du), esb = dsize(desc->dtype_bc);
+  if (!aligned(dt, esd) || !aligned(xbc, esb) || !aligned(g_delta, esd) || !aligned(g_Bc, esb) ||
+      !aligned(g_Cc, esb) || !aligned(d_dt, esd) || !aligned(d_xbc, esb) ||
       (wb && (!aligned(wb, 4) || !aligned(wc, 4) || !aligned(d_wb, 4) || !aligned(d_wc, 4))))
     return M3_ERR_ALIGN;
   if (wb && (!workspace || workspace_bytes < m3_step_inputs_bwd_workspace_bytes(desc, mimo_p)))
@@ -685,6 +691,8 @@ int m3_step_inputs_bwd(const m3_step_desc* desc, int32_t mimo_p, const float* dt
   p.d_dt = d_dt; p.d_xbc = d_xbc; p.d_wb = d_wb; p.d_wc = d_wc;
   p.part_w = static_cast<float*>(workspace);
   p.rows = desc->batch; p.D = desc->d_inner; p.N = desc->d_state; p.P = mimo_p;
+  p.du_bf16 = desc->dtype_du == M3_BF16;
+  p.x_bf16 = p.gbc_bf16 = desc->dtype_bc == M3_BF16;
   cudaError_t e = launch_step_inputs_bwd(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }

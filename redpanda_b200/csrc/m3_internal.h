@@ -136,14 +136,16 @@ cudaError_t launch_bwd_reduce(const Tile& t, const ReduceParams& p, cudaStream_t
 cudaError_t launch_step(const Tile& t, const StepParams& p, cudaStream_t s);
 
 struct InputsParams {
-  const float* dt; long long ld_dt;       // (B, ld_dt): dt_proj output before softplus
+  const void* dt; long long ld_dt;        // (B, ld_dt): dt_proj output before softplus
   const float* dt_bias;                   // (D,) dt_proj bias added first, or nullptr
-  int vec4;                               // dt rows, bias and delta as float4 (aligned, D % 4 == 0)
-  const float* xbc; long long ld_x;       // (B, ld_x): row of x_proj output
+  int vec4;                               // fp32 dt rows, bias and delta as float4
+  const void* xbc; long long ld_x;        // (B, ld_x): row of x_proj output
   int off_b, off_c;                       // column offsets of B_raw and C_raw (N*p each)
   const float* wb; const float* wc;       // (N*p,) BCNorm weights
   float eps;
-  float* delta; float* Bc; float* Cc;     // (B, D), (B, N), (B, N)
+  void* delta; void* Bc; void* Cc;        // (B, D), (B, N), (B, N)
+  int du_bf16;                            // dt and delta are bf16 (else fp32)
+  int bc_bf16;                            // xbc, Bc and Cc are bf16 (else fp32)
   int B, D, N, P;
 };
 cudaError_t launch_step_inputs(const InputsParams& p, cudaStream_t s);
@@ -157,14 +159,16 @@ struct SiluParams {
 cudaError_t launch_silu(const SiluParams& p, cudaStream_t s);
 
 struct InputsBwdParams {
-  const float* dt; long long ld_dt;       // nullptr: skip the softplus part
+  const void* dt; long long ld_dt;        // nullptr: skip the softplus part
   const void* xbc; long long ld_x;        // float, or bf16 when x_bf16
-  int x_bf16;
+  int x_bf16;                             // xbc and d_xbc are bf16
+  int gbc_bf16;                           // g_Bc and g_Cc are bf16
+  int du_bf16;                            // dt, g_delta and d_dt are bf16
   int off_b, off_c;
   const float* wb; const float* wc;
   float eps;
-  const float* g_delta; const float* g_Bc; const float* g_Cc;   // (rows, D), (rows, N) x2
-  float* d_dt; void* d_xbc;                                     // (rows, D), (rows, ld_x)
+  const void* g_delta; const void* g_Bc; const void* g_Cc;      // (rows, D), (rows, N) x2
+  void* d_dt; void* d_xbc;                                      // (rows, D), (rows, ld_x)
   float* d_wb; float* d_wc;                                     // (N*P,) each
   float* part_w;                                                // [ctas][2][N*P]
   long long rows; int D, N, P;

@@ -30,9 +30,24 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) step_inputs_kernel(const Inp
   const int rows = min(kRowsPerCta, p.B - r0);
   if (warp >= rows) return;
   const size_t b = (size_t)(r0 + warp);
-  {   // softplus of this warp's row (after the dt_proj bias, when given)
-    const float* dt = p.dt + b * p.ld_dt;
-    float* delta = p.delta + b * p.D;
+  auto ldv = [](const void* base, size_t i, int bf) {
+    return bf ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
+              : static_cast<const float*>(base)[i];
+  };
+  auto stv = [](void* base, size_t i, float v, int bf) {
+    if (bf) static_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+    else static_cast<float*>(base)[i] = v;
+  };
+  if (p.du_bf16) {   // bf16 dt and delta: fp32 arithmetic, delta rounded once
+    const size_t i0 = b * p.ld_dt, o0 = b * p.D;
+    const float* bias = p.dt_bias;
+    for (int d = lane; d < p.D; d += 32) {
+      const float x = ldv(p.dt, i0 + d, 1);
+      stv(p.delta, o0 + d, softplus20(bias != nullptr ? __fadd_rn(x, bias[d]) : x), 1);
+    }
+  } else {   // softplus of this warp's row (after the dt_proj bias, when given)
+    const float* dt = static_cast<const float*>(p.dt) + b * p.ld_dt;
+    float* delta = static_cast<float*>(p.delta) + b * p.D;
     const float* bias = p.dt_bias;
     if (p.vec4) {
       const float4* dt4 = reinterpret_cast<const float4*>(dt);
@@ -53,16 +68,16 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) step_inputs_kernel(const Inp
     }
   }
   const int np = p.N * p.P;
-  const float* xb = p.xbc + b * p.ld_x + p.off_b;
-  const float* xc = p.xbc + b * p.ld_x + p.off_c;
+  const size_t xb = b * p.ld_x + p.off_b, xc = b * p.ld_x + p.off_c;
   const bool has_w = p.wb != nullptr;
-  auto ldb = [&](int k) { return xb[k]; };
-  auto ldc = [&](int k) { return xc[k]; };
+  const int xbf = p.bc_bf16;
+  auto ldb = [&](int k) { return ldv(p.xbc, xb + k, xbf); };
+  auto ldc = [&](int k) { return ldv(p.xbc, xc + k, xbf); };
   const float rb = bcnorm_scale(ldb, np, p.eps, has_w, lane);
   const float rc = bcnorm_scale(ldc, np, p.eps, has_w, lane);
   for (int n = lane; n < p.N; n += 32) {
-    p.Bc[b * p.N + n] = bcnorm_fold(ldb, n, p.P, rb, p.wb);
-    p.Cc[b * p.N + n] = bcnorm_fold(ldc, n, p.P, rc, p.wc);
+    stv(p.Bc, b * p.N + n, bcnorm_fold(ldb, n, p.P, rb, p.wb), xbf);
+    stv(p.Cc, b * p.N + n, bcnorm_fold(ldc, n, p.P, rc, p.wc), xbf);
   }
 }
 
@@ -147,29 +162,41 @@ __global__ void __launch_bounds__(256) step_inputs_bwd_kernel(const InputsBwdPar
   const int np = p.N * p.P;
   const XT* xbc = static_cast<const XT*>(p.xbc);
   XT* d_xbc = static_cast<XT*>(p.d_xbc);
+  auto ldv = [](const void* base, size_t i, int bf) {
+    return bf ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
+              : static_cast<const float*>(base)[i];
+  };
   float* wacc = s_w + (size_t)warp * 2 * np;
   for (int i = lane; i < 2 * np; i += 32) wacc[i] = 0.f;
   const long long nwarps = (long long)gridDim.x * 8;
   for (long long r = (long long)blockIdx.x * 8 + warp; r < p.rows; r += nwarps) {
     const size_t b = (size_t)r;
     if (p.dt != nullptr) {
-      for (int d = lane; d < p.D; d += 32)
-        p.d_dt[b * p.D + d] = softplus20_grad(p.g_delta[b * p.D + d], p.dt[b * p.ld_dt + d]);
+      const int bf = p.du_bf16;
+      for (int d = lane; d < p.D; d += 32) {
+        const float v = softplus20_grad(ldv(p.g_delta, b * p.D + d, bf),
+                                        ldv(p.dt, b * p.ld_dt + d, bf));
+        if (bf) static_cast<__nv_bfloat16*>(p.d_dt)[b * p.D + d] = __float2bfloat16_rn(v);
+        else static_cast<float*>(p.d_dt)[b * p.D + d] = v;
+      }
     }
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
       const size_t x0 = b * p.ld_x + (which ? p.off_c : p.off_b);
-      const float* gbc = (which ? p.g_Cc : p.g_Bc) + b * p.N;
+      const void* gsrc = which ? p.g_Cc : p.g_Bc;
+      const size_t g0 = b * p.N;
+      const int gbf = p.gbc_bf16;
+      auto gbc_at = [&](int n) { return ldv(gsrc, g0 + n, gbf); };
       const float* w = which ? p.wc : p.wb;
       if (w == nullptr) {   // no BCNorm: the fold is a plain sum
-        for (int i = lane; i < np; i += 32) stx(d_xbc, x0 + i, gbc[i / p.P]);
+        for (int i = lane; i < np; i += 32) stx(d_xbc, x0 + i, gbc_at(i / p.P));
         continue;
       }
       float ss = 0.f, sg = 0.f;
       for (int i = lane; i < np; i += 32) {
         const float xi = ldx(xbc, x0 + i);
         ss = __fmaf_rn(xi, xi, ss);
-        sg = __fmaf_rn(__fmul_rn(gbc[i / p.P], w[i]), xi, sg);
+        sg = __fmaf_rn(__fmul_rn(gbc_at(i / p.P), w[i]), xi, sg);
       }
 #pragma unroll
       for (int m = 16; m > 0; m >>= 1) {
@@ -181,7 +208,7 @@ __global__ void __launch_bounds__(256) step_inputs_bwd_kernel(const InputsBwdPar
       const float cs = __fmul_rn(coef, sg);
       float* wa = wacc + which * np;
       for (int i = lane; i < np; i += 32) {
-        const float xi = ldx(xbc, x0 + i), gy = gbc[i / p.P];
+        const float xi = ldx(xbc, x0 + i), gy = gbc_at(i / p.P);
         stx(d_xbc, x0 + i, __fsub_rn(__fmul_rn(rs, __fmul_rn(gy, w[i])), __fmul_rn(cs, xi)));
         wa[i] = __fmaf_rn(gy, __fmul_rn(xi, rs), wa[i]);
       }

@@ -489,26 +489,29 @@ def m3_step_factored_(h, fac_prev, fac_next, delta_t, u_t, Bc_t, Cc_t, A_real, A
     return y
 
 
+def _f32_or_bf16(t):
+    """t as float32 or bfloat16 (the element types the prologue kernels read)."""
+    return t if t.dtype in (torch.float32, torch.bfloat16) else t.float()
+
+
 def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mimo_p,
                    dt_bias=None):
     """softplus(dt) and the BCNorm'ed, MIMO-folded B and C of one token, one launch.
 
-    dt: (B, D) float32, dt_proj output with its bias, or without it when
-    ``dt_bias`` (D,) is given (added first, one fp32 rounding, as torch's
-    matmul followed by the bias add); x_dbl: (B, K) float32 rows
+    dt: (B, D) float32 or bfloat16, dt_proj output with its bias, or without it
+    when ``dt_bias`` (D,) is given (added first, one fp32 rounding, as torch's
+    matmul followed by the bias add); x_dbl: (B, K) float32 or bfloat16 rows
     of x_proj's output, B_raw at column ``off_b`` and C_raw at ``off_c``
     (N*p columns each); b_weight / c_weight: BCNorm weights (N*p,) or None
-    (use_bcnorm=False).  Returns (delta (B, D), Bc (B, N), Cc (B, N)), float32:
-    mamba.py:455-469 and 336-337 for one token.
+    (use_bcnorm=False).  Returns (delta (B, D) in dt's element type, Bc, Cc
+    (B, N) in x_dbl's): mamba.py:455-469 and 336-337 for one token.  The
+    arithmetic is fp32 (as torch autocast runs softplus and the RMSNorm,
+    train.py:268); a bf16 output is that result rounded once, the bits a bf16
+    layer's cast gives.
     """
     lib = _lib.load()
     dev = _require_cuda(dt, x_dbl)
-    # a bf16 layer's projections are widened first: the prologue computes in
-    # fp32, as torch autocast runs softplus and the RMSNorm (train.py:268)
-    if dt.dtype != torch.float32:
-        dt = dt.float()
-    if x_dbl.dtype != torch.float32:
-        x_dbl = x_dbl.float()
+    dt, x_dbl = _f32_or_bf16(dt), _f32_or_bf16(x_dbl)
     if dt.stride(-1) != 1 or x_dbl.stride(-1) != 1:
         raise ValueError("m3_step_inputs: rows of dt and x_dbl must be contiguous")
     B, D = dt.shape
@@ -517,10 +520,10 @@ def m3_step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mi
         wb = b_weight.detach().to(torch.float32).contiguous()
         wc = c_weight.detach().to(torch.float32).contiguous()
     bias = None if dt_bias is None else dt_bias.detach().to(torch.float32).contiguous()
-    delta = torch.empty(B, D, device=dev, dtype=torch.float32)
-    bc = torch.empty(B, n_state, device=dev, dtype=torch.float32)
+    delta = torch.empty(B, D, device=dev, dtype=dt.dtype)
+    bc = torch.empty(B, n_state, device=dev, dtype=x_dbl.dtype)
     cc = torch.empty_like(bc)
-    desc = StepDesc(B, D, n_state, 0, M3_F32, M3_F32)
+    desc = StepDesc(B, D, n_state, 0, _dt_code(dt.dtype), _dt_code(x_dbl.dtype))
     with torch.cuda.device(dev):
         _lib.check(lib.m3_step_inputs(desc, int(mimo_p), dt.data_ptr(), dt.stride(0),
                                       ctypes_ptr(bias), x_dbl.data_ptr(), x_dbl.stride(0),
@@ -552,11 +555,15 @@ class _StepInputsFn(torch.autograd.Function):
         lib = _lib.load()
         dev = dt.device
         rows, D = dt.shape
-        z = lambda g, shape: torch.zeros(shape, device=dev) if g is None else g.float().contiguous()  # noqa: E731
-        g_delta, g_bc, g_cc = z(g_delta, (rows, D)), z(g_bc, (rows, n)), z(g_cc, (rows, n))
-        d_dt = torch.empty(rows, D, device=dev, dtype=torch.float32)
+        def z(g, shape, dtype):   # an upstream gradient in the element type of its input
+            if g is None:
+                return torch.zeros(shape, device=dev, dtype=dtype)
+            return g.to(dtype).contiguous()
+        g_delta = z(g_delta, (rows, D), dt.dtype)
+        g_bc, g_cc = z(g_bc, (rows, n), x_dbl.dtype), z(g_cc, (rows, n), x_dbl.dtype)
+        d_dt = torch.empty(rows, D, device=dev, dtype=dt.dtype)
         d_x = torch.zeros_like(x_dbl)
-        desc = StepDesc(rows, D, n, 0, M3_F32, M3_F32)
+        desc = StepDesc(rows, D, n, 0, _dt_code(dt.dtype), _dt_code(x_dbl.dtype))
         d_wb = d_wc = ws = None
         if has_w:
             wb32, wc32 = wb.detach().float().contiguous(), wc.detach().float().contiguous()
@@ -577,9 +584,11 @@ class _StepInputsFn(torch.autograd.Function):
 
 
 def step_inputs(dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, n_state, mimo_p):
-    """Differentiable :func:`m3_step_inputs` over (rows, .) float32 tensors."""
-    dt = dt.float().contiguous()
-    x_dbl = x_dbl.float().contiguous()
+    """Differentiable :func:`m3_step_inputs` over (rows, .) float32 or bfloat16
+    tensors (a bf16 layer's projections stay bf16: the kernels read them and
+    write bf16 delta, Bc, Cc and gradients, each rounded once)."""
+    dt = _f32_or_bf16(dt).contiguous()
+    x_dbl = _f32_or_bf16(x_dbl).contiguous()
     return _StepInputsFn.apply(dt, x_dbl, b_weight, c_weight, off_b, off_c, eps, n_state,
                                mimo_p)
 
