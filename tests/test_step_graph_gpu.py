@@ -91,10 +91,13 @@ def test_step_graph_load_snapshot_reset():
         assert torch.equal(g.step(torch.tensor([9, 9, 9]))[0], h0)
 
 
-def test_search_eval_step_graphed_matches_eval_step():
+@pytest.mark.parametrize("shape", [dict(d_model=48, d_state=16, n_track_state=4),
+                                   dict(d_model=64, d_state=32, n_track_state=8)])
+def test_search_eval_step_graphed_matches_eval_step(shape):
+    """Two state layouts: 16 lanes (the step kernel's element-wise path) and 32
+    (the pipelined kernel with the prologue fused in, batch 1)."""
     torch.manual_seed(3)
-    scfg = SearchMambaConfig(d_model=48, n_layer=3, d_state=16, n_track_state=4, mimo_p=2,
-                             vocab_size=300)
+    scfg = SearchMambaConfig(n_layer=3, mimo_p=2, vocab_size=300, **shape)
     sm = SearchMamba(scfg, vocab_size=300).cuda().eval()
     board = torch.randint(1, 300, (30,), device="cuda")
     moves = [5, 17, 250, 3]
