@@ -23,9 +23,15 @@ from redpanda_b200.search_mamba import SearchMamba, SearchMambaConfig
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-FWD_TOL = 1e-5
-GRAD_TOL = 1e-4
-STEP_TOL = 1e-5
+# Bars about 3-30x above the largest errors measured on a B200 (GEMMs in fp32,
+# TF32 off): model forward 1.6e-7 and SearchMamba rollout 1.4e-6 (FWD_TOL),
+# parameter gradients 1.7e-5 (GRAD_TOL), step chains, caches and prime 8.2e-7,
+# SearchMamba node and line evaluations 1.8e-6 (STEP_TOL).  They are set this
+# close so that a regression in a prologue or gate kernel cannot hide under
+# GEMM rounding.
+FWD_TOL = 5e-6
+GRAD_TOL = 5e-5
+STEP_TOL = 5e-6
 
 
 def _rel(a, b):
@@ -77,19 +83,26 @@ def test_step_chain_and_prime_match_reference(name):
     c, m = _load(name)
     m.eval()
     ids = c["ids"].cuda()
+    errs = {}
     with torch.no_grad():
         cache, hs = None, []
         for t in range(ids.shape[1]):
             h, cache = m.step(token_id=ids[:, t], cache=cache)
             hs.append(h)
-        assert _rel(torch.stack(hs, 1), c["step_hidden"]) <= STEP_TOL
-        for (h1, d1), (h2, d2) in zip(cache, c["step_cache_last"]):
-            assert _rel(h1, h2) <= STEP_TOL and _rel(d1, d2) <= STEP_TOL
+        errs["step_hidden"] = _rel(torch.stack(hs, 1), c["step_hidden"])
+        for i, ((h1, d1), (h2, d2)) in enumerate(zip(cache, c["step_cache_last"])):
+            errs["cache_h%d" % i] = _rel(h1, h2)
+            errs["cache_dbu%d" % i] = _rel(d1, d2)
         k = c["prime_k"]
         fin, pc = m.prime_cache(ids[:, :k])
-        assert _rel(fin, c["prime_final"]) <= STEP_TOL
+        errs["prime_final"] = _rel(fin, c["prime_final"])
         nxt, _ = m.step(token_id=ids[:, k], cache=pc)
-        assert _rel(nxt, c["prime_next"]) <= STEP_TOL
+        errs["prime_next"] = _rel(nxt, c["prime_next"])
+    worst = max((e, k) for k, e in errs.items())
+    PARITY_TABLE.append((name, "step", "model", worst[0], float("nan"), float("nan"),
+                         ("ok" if worst[0] <= STEP_TOL else "FAIL") + " (worst: %s)" % worst[1]))
+    for k, e in errs.items():
+        assert e <= STEP_TOL, k
 
 
 def test_step_matches_forward_reference_gate():
@@ -143,7 +156,9 @@ def test_search_mamba_fast_line_eval_equals_slow():
     with torch.no_grad():
         slow = sm.evaluate_lines(board, lines)
         fast = sm.evaluate_lines_fast(board, lines)
-    assert torch.allclose(slow, fast, atol=1e-4)
+    PARITY_TABLE.append(("search_lines_fast_vs_slow", "lines", "model",
+                         (slow - fast).abs().max().item(), float("nan"), float("nan"), "abs"))
+    assert torch.allclose(slow, fast, atol=1e-5)   # measured 1.3e-6
 
 
 def test_search_mamba_dynamics_and_eval_step():
