@@ -1016,12 +1016,16 @@ def run_search_nodes(dev, args):
         from redpanda_b200.graphs import StepGraph
         from redpanda_b200.mamba import Mamba3Block
         sweep = {}
+        old_small = Mamba3Block.small_step_max_batch
         try:
-            for B in (1, 64, 256, 1024, 4096):
+            for B in (1, 8, 64, 256, 1024, 4096):
                 ids = torch.randint(0, 8192, (B, 16), device=dev, generator=g)
                 mv = torch.randint(0, 8192, (B,), device=dev, generator=g)
-                for fuse in (True, False):
+                variants = ([("small", True, old_small)] if B <= old_small else []) + \
+                    [("fused", True, 0), ("two_launch", False, 0)]
+                for vname, fuse, small in variants:
                     Mamba3Block.fuse_step = fuse
+                    Mamba3Block.small_step_max_batch = small
                     old_max = Mamba3Block.fuse_step_max_batch
                     Mamba3Block.fuse_step_max_batch = 1 << 30
                     with torch.no_grad():
@@ -1039,11 +1043,11 @@ def run_search_nodes(dev, args):
                         e1.record()
                         torch.cuda.synchronize(dev)
                     Mamba3Block.fuse_step_max_batch = old_max
-                    sweep[f"B{B}_{'fused' if fuse else 'two_launch'}"] = \
-                        e0.elapsed_time(e1) / n * 1e3
+                    sweep[f"B{B}_{vname}"] = e0.elapsed_time(e1) / n * 1e3
                     del gr
         finally:
             Mamba3Block.fuse_step = True
+            Mamba3Block.small_step_max_batch = old_small
         del sm
         torch.cuda.empty_cache()
         out["workload"] = ("a10 search node evaluation: 12-layer SearchMamba (d_model=512, "
@@ -1053,9 +1057,12 @@ def run_search_nodes(dev, args):
         out["speedup"] = out["eager"]["us_per_node"] / out["graph"]["us_per_node"]
         out["graph_step_us_by_batch"] = sweep
         out["graph_step_note"] = ("the backbone's 12-layer step as one CUDA graph, us per step "
-                                  "(CUDA events), prologue inside the step kernel vs its own "
-                                  "launch; step_fused_ takes the fused kernel up to "
-                                  "Mamba3Block.fuse_step_max_batch rows")
+                                  "(CUDA events): small = the small-batch layer (norm + "
+                                  "projections + step + residual in four launches per layer, "
+                                  "step_fused_'s path up to Mamba3Block.small_step_max_batch "
+                                  "rows); fused = cuBLAS projections with the prologue inside "
+                                  "the step kernel (up to Mamba3Block.fuse_step_max_batch rows); "
+                                  "two_launch = cuBLAS projections, prologue as its own launch")
         return out
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old_tf32

@@ -18,10 +18,13 @@
  *   redpanda/engine/mamba.py:455-469        step inputs (softplus, BCNorm, MIMO fold) -> m3_step_inputs
  *   redpanda/engine/mamba.py:490-497        step + gated output (y + u*D) * silu(z) -> m3_step_gated
  *   redpanda/engine/mamba.py:455-497        step inputs + step + gated output in one launch
- *                                           -> m3_step_gated_fused
+ *                                           -> m3_step_gated_fused (+ dt_proj: _proj)
  *   redpanda/engine/mamba.py:262-265        (y + u*D) * silu(z) after a scan -> m3_gate
  *                                           and its autograd backward -> m3_gate_bwd
  *   redpanda/engine/mamba.py:243, 452       u = silu(x half of in_proj) -> m3_silu
+ *   redpanda/engine/mamba.py:82-89, 450-452 RMSNorm + in_proj + silu, small batch -> m3_rows_linear
+ *   redpanda/engine/mamba.py:454, 463       x_proj + dt_proj product, small batch -> m3_xdt_proj
+ *   redpanda/engine/mamba.py:497, 591-595   out_proj + residual add, small batch -> m3_rows_linear
  *
  * Shapes (B batch, L length, D = d_inner, N = d_state, n_rot rotational lanes,
  * N - n_rot tracking lanes):
@@ -63,7 +66,8 @@ enum {
   M3_ERR_NULL = 1,         /* a required pointer is NULL */
   M3_ERR_SHAPE = 2,        /* a size is out of range */
   M3_ERR_DTYPE = 3,        /* unsupported element type */
-  M3_ERR_UNSUPPORTED = 4,  /* no kernel for this (d_state, n_rot) split */
+  M3_ERR_UNSUPPORTED = 4,  /* no compiled kernel serves this shape (a (d_state, n_rot)
+                              split, or a size past a kernel's stated limit) */
   M3_ERR_ALIGN = 5,        /* a pointer is not aligned to its element size */
   M3_ERR_WORKSPACE = 6,    /* workspace missing or too small */
   M3_ERR_LAUNCH = 7,       /* the CUDA launch failed (see cudaGetLastError) */
@@ -253,6 +257,39 @@ M3_API int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p,
 M3_API int m3_silu(int64_t rows, int32_t d, const float* x, int64_t ld_x, float* out,
             void* stream);
 
+/* Small-batch projections of the step layer (at most 8 rows; a search node or
+ * a few lines), fp32, for the launch-latency-bound regime where each
+ * projection is a matrix-vector product.  One warp per output column; sums in
+ * a fixed order (deterministic); weights (nn.Linear layout, (d_out, d_in)
+ * row-major) 16-byte aligned with d_in % 4 == 0.  rows > 8, or inputs past 48 KB
+ * of staged floats (8 rows x 1536, 4 x 3072, ...), return M3_ERR_UNSUPPORTED.
+ *
+ * m3_rows_linear: out = act(residual + (bias + xn W^T)) with
+ *   xn = x * rsqrt(mean(x^2) + eps) * norm_w    (RMSNorm, mamba.py:82-89) when
+ *        norm_w != NULL, else x;
+ *   columns [0, split) -> out0 (row stride ld0), silu applied when silu != 0
+ *        (the x half of in_proj, mamba.py:450-452); columns [split, d_out) ->
+ *        out1 (row stride ld1; the z half);
+ *   residual (rows, ld_r) or NULL, added last (mamba.py:595); it may be out0
+ *        itself (out_proj + residual in place), but no output may overlap x
+ *        (M3_ERR_ALIAS).
+ * Rounding differs from a cuBLAS GEMM only by the summation order. */
+M3_API int m3_rows_linear(int32_t rows, int32_t d_in, int32_t d_out, const float* x,
+            int64_t ld_x, const float* norm_w, float eps, const float* W,
+            const float* bias, const float* residual, int64_t ld_r, int32_t split,
+            int32_t silu, float* out0, int64_t ld0, float* out1, int64_t ld1,
+            void* stream);
+
+/* m3_xdt_proj: x_dbl = u W_x^T + b_x  (rows, n_x; mamba.py:454) and
+ * dt = x_dbl[:, :dt_rank] W_dt^T  (rows, d_inner; dt_proj without its bias,
+ * mamba.py:463 -- m3_step_gated_fused / m3_step_inputs add it) in one launch.
+ * u (rows, d_inner) contiguous; W_x (n_x, d_inner); b_x (n_x,) or NULL; W_dt
+ * (d_inner, dt_rank), dt_rank <= 64 (else M3_ERR_UNSUPPORTED).  u, x_dbl and dt
+ * must not overlap. */
+M3_API int m3_xdt_proj(int32_t rows, int32_t d_inner, int32_t n_x, int32_t dt_rank,
+            const float* u, const float* W_x, const float* b_x, const float* W_dt,
+            float* x_dbl, float* dt, void* stream);
+
 /* Workspace bytes of m3_step_inputs_bwd (the BCNorm weight-gradient partials). */
 M3_API size_t m3_step_inputs_bwd_workspace_bytes(const m3_step_desc* desc, int32_t mimo_p);
 
@@ -311,6 +348,21 @@ M3_API int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* 
             const float* wb, const float* wc, float eps, const void* u,
             const float* A_real_p, const float* A_imag_p, const float* track_p,
             const float* z, int64_t ld_z, const float* d_skip, float* out, void* stream);
+
+/* m3_step_gated_fused with dt_proj's product formed in the kernel too:
+ * dt = xbc[:, :dt_rank] W_dt^T (mamba.py:463, the dt_raw columns of x_proj's
+ * output times dt_proj's weight, W_dt (D, dt_rank) row-major float32,
+ * dt_rank <= 64), then delta = softplus(dt + dt_bias) and the rest as
+ * m3_step_gated_fused.  One launch for the whole step after x_proj; the dt sum
+ * runs in a fixed order (4 strided partials, then pairs), so results are
+ * deterministic but not the bits of a cuBLAS dt_proj. */
+M3_API int m3_step_gated_fused_proj(const m3_step_desc* desc, int32_t mimo_p, float* h,
+            float* dbu, const float* fac_prev, float* fac_next, const float* W_dt,
+            int32_t dt_rank, const float* dt_bias, const float* xbc, int64_t ld_x,
+            int32_t off_b, int32_t off_c, const float* wb, const float* wc, float eps,
+            const void* u, const float* A_real_p, const float* A_imag_p,
+            const float* track_p, const float* z, int64_t ld_z, const float* d_skip,
+            float* out, void* stream);
 
 /* The layer's gated activation after a scan (mamba.py:262-265), elementwise
  * over (rows, D) = (B*L, D):

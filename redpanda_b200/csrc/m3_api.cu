@@ -147,7 +147,7 @@ const char* m3_strerror(int code) {
     case M3_ERR_NULL: return "m3: a required pointer is NULL";
     case M3_ERR_SHAPE: return "m3: a size argument is out of range";
     case M3_ERR_DTYPE: return "m3: unsupported element type (float32 or bfloat16 only)";
-    case M3_ERR_UNSUPPORTED: return "m3: no compiled kernel for this (d_state, n_rot) split";
+    case M3_ERR_UNSUPPORTED: return "m3: no compiled kernel serves this shape";
     case M3_ERR_ALIGN: return "m3: a pointer is not aligned to its element size";
     case M3_ERR_WORKSPACE: return "m3: workspace missing or too small";
     case M3_ERR_LAUNCH: return "m3: CUDA kernel launch failed";
@@ -372,6 +372,7 @@ struct StepPro {
   int32_t off_b, off_c, P;
   const float* wb; const float* wc;
   float eps;
+  const float* wdt = nullptr; int32_t dt_rank = 0;   // dt formed in the kernel
 };
 
 static int step_common(const m3_step_desc* desc, float* h, float* dbu, const float* fac_prev,
@@ -434,6 +435,7 @@ static int step_common(const m3_step_desc* desc, float* h, float* dbu, const flo
     p.xbc = pro->xbc; p.ld_x = pro->ld_x;
     p.off_b = pro->off_b; p.off_c = pro->off_c; p.P = pro->P;
     p.wb = pro->wb; p.wc = pro->wc; p.eps = pro->eps;
+    p.wdt = pro->wdt; p.dt_rank = pro->dt_rank;
   }
   cudaError_t e = launch_step(t, p, static_cast<cudaStream_t>(stream));
   if (e == cudaErrorNotSupported) return M3_ERR_UNSUPPORTED;
@@ -605,6 +607,36 @@ int m3_step_gated_fused(const m3_step_desc* desc, int32_t mimo_p, float* h, floa
                      track_p, out, stream, z, ld_z, d_skip, &pro);
 }
 
+int m3_step_gated_fused_proj(const m3_step_desc* desc, int32_t mimo_p, float* h, float* dbu,
+                             const float* fac_prev, float* fac_next, const float* W_dt,
+                             int32_t dt_rank, const float* dt_bias, const float* xbc,
+                             int64_t ld_x, int32_t off_b, int32_t off_c, const float* wb,
+                             const float* wc, float eps, const void* u, const float* A_real_p,
+                             const float* A_imag_p, const float* track_p, const float* z,
+                             int64_t ld_z, const float* d_skip, float* out, void* stream) {
+  if (!desc || !z || !d_skip || !W_dt || !xbc) return M3_ERR_NULL;
+  if ((dbu != nullptr) == (fac_next != nullptr)) return M3_ERR_NULL;   // exactly one state form
+  if ((wb == nullptr) != (wc == nullptr)) return M3_ERR_NULL;
+  if (desc->dtype_bc != M3_F32) return M3_ERR_DTYPE;
+  const int64_t np = (int64_t)desc->d_state * mimo_p;
+  if (ld_z < desc->d_inner || mimo_p < 1 || dt_rank < 1 || dt_rank > ld_x || off_b < 0 ||
+      off_c < 0 || off_b + np > ld_x || off_c + np > ld_x || !(eps >= 0.f))
+    return M3_ERR_SHAPE;
+  if (!aligned(z, 4) || !aligned(d_skip, 4) || !aligned(W_dt, 4) || !aligned(xbc, 4) ||
+      (wb && (!aligned(wb, 4) || !aligned(wc, 4))) || (dt_bias && !aligned(dt_bias, 4)))
+    return M3_ERR_ALIGN;
+  if (dt_rank > kMaxDtRank || mimo_p > 2 || np % 4 != 0 || !aligned(xbc, 16) || ld_x % 4 != 0 ||
+      off_b % 4 != 0 || off_c % 4 != 0)
+    return M3_ERR_UNSUPPORTED;
+  StepPro pro{nullptr, 0, dt_bias, xbc, ld_x, off_b, off_c, mimo_p, wb, wc, eps};
+  pro.wdt = W_dt;
+  pro.dt_rank = dt_rank;
+  // delta/Bc/Cc are not read under the fused prologue; xbc stands in for the
+  // pointer checks (16-byte aligned)
+  return step_common(desc, h, dbu, fac_prev, fac_next, xbc, u, xbc, xbc, A_real_p, A_imag_p,
+                     track_p, out, stream, z, ld_z, d_skip, &pro);
+}
+
 int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const void* dt, int64_t ld_dt,
                    const float* dt_bias, const void* xbc, int64_t ld_x, int32_t off_b,
                    int32_t off_c, const float* wb, const float* wc, float eps, void* delta,
@@ -636,6 +668,76 @@ int m3_step_inputs(const m3_step_desc* desc, int32_t mimo_p, const void* dt, int
   p.vec4 = !p.du_bf16 && (desc->d_inner % 4) == 0 && ld_dt % 4 == 0 && aligned(dt, 16) &&
            aligned(delta, 16) && (!dt_bias || aligned(dt_bias, 16));
   cudaError_t e = launch_step_inputs(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
+namespace {
+// [a, a + an) and [b, b + bn) bytes intersect
+bool spans_overlap(const void* a, size_t an, const void* b, size_t bn) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return a && b && x < y + bn && y < x + an;
+}
+size_t rows_span(int64_t rows, int64_t ld, int64_t width) {
+  return (size_t)((rows - 1) * ld + width) * sizeof(float);
+}
+}  // namespace
+
+int m3_rows_linear(int32_t rows, int32_t d_in, int32_t d_out, const float* x, int64_t ld_x,
+                   const float* norm_w, float eps, const float* W, const float* bias,
+                   const float* residual, int64_t ld_r, int32_t split, int32_t silu,
+                   float* out0, int64_t ld0, float* out1, int64_t ld1, void* stream) {
+  if (rows < 1 || d_in < 4 || d_out < 1 || split < 0 || split > d_out) return M3_ERR_SHAPE;
+  if (rows > kSmallRows || d_in % 4 != 0 ||
+      (int64_t)small_rows_pad(rows) * d_in > kSmallStage)
+    return M3_ERR_UNSUPPORTED;
+  if (!x || !W || (split > 0 && !out0) || (split < d_out && !out1)) return M3_ERR_NULL;
+  if (ld_x < d_in || (residual && ld_r < d_out) || (split > 0 && ld0 < split) ||
+      (split < d_out && ld1 < d_out - split))
+    return M3_ERR_SHAPE;
+  if (!aligned(W, 16) || !aligned(x, 4) || (norm_w && !aligned(norm_w, 4)) ||
+      (bias && !aligned(bias, 4)) || (residual && !aligned(residual, 4)) ||
+      (out0 && !aligned(out0, 4)) || (out1 && !aligned(out1, 4)))
+    return M3_ERR_ALIGN;
+  // every CTA stages all of x before writing, but CTAs run in any order: the
+  // outputs must not overlap the input (the residual may be out0 itself)
+  const size_t xs = rows_span(rows, ld_x, d_in);
+  if ((split > 0 && spans_overlap(x, xs, out0, rows_span(rows, ld0, split))) ||
+      (split < d_out && spans_overlap(x, xs, out1, rows_span(rows, ld1, d_out - split))))
+    return M3_ERR_ALIAS;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  RowsLinearParams p;
+  memset(&p, 0, sizeof(p));
+  p.x = x; p.ld_x = ld_x; p.norm_w = norm_w; p.eps = eps; p.W = W; p.bias = bias;
+  p.residual = residual; p.ld_r = ld_r; p.out0 = out0; p.ld0 = ld0; p.out1 = out1; p.ld1 = ld1;
+  p.rows = rows; p.d_in = d_in; p.d_out = d_out; p.split = split; p.silu = silu != 0;
+  cudaError_t e = launch_rows_linear(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
+}
+
+int m3_xdt_proj(int32_t rows, int32_t d_inner, int32_t n_x, int32_t dt_rank, const float* u,
+                const float* W_x, const float* b_x, const float* W_dt, float* x_dbl, float* dt,
+                void* stream) {
+  if (rows < 1 || d_inner < 4 || dt_rank < 1 || n_x < dt_rank) return M3_ERR_SHAPE;
+  if (rows > kSmallRows || d_inner % 4 != 0 || dt_rank > kMaxDtRank ||
+      (int64_t)small_rows_pad(rows) * (d_inner + dt_rank) > kSmallStage)
+    return M3_ERR_UNSUPPORTED;
+  if (!u || !W_x || !W_dt || !x_dbl || !dt) return M3_ERR_NULL;
+  if (!aligned(W_x, 16) || !aligned(u, 4) || !aligned(W_dt, 4) || (b_x && !aligned(b_x, 4)) ||
+      !aligned(x_dbl, 4) || !aligned(dt, 4))
+    return M3_ERR_ALIGN;
+  const size_t us = (size_t)rows * d_inner * sizeof(float);
+  const size_t xs = (size_t)rows * n_x * sizeof(float);
+  if (spans_overlap(u, us, x_dbl, xs) || spans_overlap(u, us, dt, us) ||
+      spans_overlap(x_dbl, xs, dt, us))
+    return M3_ERR_ALIAS;
+  int rc = check_device();
+  if (rc != M3_OK) return rc;
+  XdtParams p;
+  memset(&p, 0, sizeof(p));
+  p.u = u; p.Wx = W_x; p.bx = b_x; p.Wdt = W_dt; p.x_dbl = x_dbl; p.dt = dt;
+  p.rows = rows; p.D = d_inner; p.n_x = n_x; p.r = dt_rank;
+  cudaError_t e = launch_xdt_proj(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 

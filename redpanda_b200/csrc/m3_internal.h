@@ -117,6 +117,9 @@ struct StepParams {
   int off_b, off_c, P;
   const float* wb; const float* wc;
   float eps;
+  // pro with the dt product: dt = xbc[:, :dt_rank] wdt^T computed in the
+  // kernel (dt_proj, wdt (D, dt_rank) row-major); `dt` is unused then
+  const float* wdt; int dt_rank;
 };
 
 struct ReduceParams {
@@ -202,6 +205,37 @@ struct GateBwdParams {
 };
 int gate_bwd_row_ctas(long long rows, int d);
 cudaError_t launch_gate_bwd(const GateBwdParams& p, cudaStream_t s);
+
+// Small-batch projections of the step layer (m3_gemv.cu): rows <= kSmallRows.
+constexpr int kSmallRows = 8;
+constexpr int kSmallStage = 12288;            // staged input floats per CTA (48 KB)
+int small_rows_pad(int rows);                 // rows rounded up to the compiled 1, 2, 4, 8
+constexpr int kMaxDtRank = 64;                // dt_rank limit of the small-batch dt product
+
+// out = act(residual + bias + norm(x) W^T), columns [0, split) to out0 (silu
+// when silu), [split, d_out) to out1.
+struct RowsLinearParams {
+  const float* x; long long ld_x;             // (rows, d_in)
+  const float* norm_w; float eps;             // RMSNorm weight or nullptr
+  const float* W;                             // (d_out, d_in) row-major
+  const float* bias;                          // (d_out,) or nullptr
+  const float* residual; long long ld_r;      // (rows, d_out) or nullptr
+  float* out0; long long ld0;
+  float* out1; long long ld1;
+  int rows, d_in, d_out, split, silu;
+};
+cudaError_t launch_rows_linear(const RowsLinearParams& p, cudaStream_t s);
+
+// x_dbl = u W_x^T + b_x and dt = x_dbl[:, :r] W_dt^T in one launch.
+struct XdtParams {
+  const float* u;                             // (rows, D) contiguous
+  const float* Wx; const float* bx;           // (n_x, D), (n_x,) or nullptr
+  const float* Wdt;                           // (D, r)
+  float* x_dbl;                               // (rows, n_x)
+  float* dt;                                  // (rows, D)
+  int rows, D, n_x, r;
+};
+cudaError_t launch_xdt_proj(const XdtParams& p, cudaStream_t s);
 
 // device error word of the current device
 int* device_err_ptr();

@@ -440,9 +440,11 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
   }
   __syncthreads();
 
-  // PRO: dt (fp32) and u, then the raw B and C rows instead of Bc and Cc
+  // PRO: dt (fp32; none when the kernel forms dt itself) and u, then the raw
+  // B and C rows instead of Bc and Cc
+  const bool dtproj = PRO && p.wdt != nullptr;
   const uint32_t row_tx = SL::kH + (FACT ? 32 * 4 + NP * 4 : SL::kH) +
-                          (PRO ? 32 * 4 + 32 * esd + 2 * np_raw * 4
+                          (PRO ? (dtproj ? 0 : 32 * 4) + 32 * esd + 2 * np_raw * 4
                                : 2 * 32 * esd + 2 * NP * esb);
   auto issue = [&](int i) {   // thread 0: stage the row pair pair0 + i
     const int s = i % kBulkStages;
@@ -467,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
         bulk_g2s(st + SL::oS2(r), p.dbu + (b * D + d0) * NP, SL::kH, &full[s]);
       }
       if constexpr (PRO) {
-        bulk_g2s(st + SL::oDL(r), p.dt + b * p.ld_dt + d0, 32 * 4, &full[s]);
+        if (!dtproj) bulk_g2s(st + SL::oDL(r), p.dt + b * p.ld_dt + d0, 32 * 4, &full[s]);
         bulk_g2s(st + SL::oU(r), (const char*)p.u + (b * D + d0) * esd, 32 * esd, &full[s]);
         bulk_g2s(st + SL::oRB(r), p.xbc + b * p.ld_x + p.off_b, np_raw * 4, &full[s]);
         bulk_g2s(st + SL::oRC(r), p.xbc + b * p.ld_x + p.off_c, np_raw * 4, &full[s]);
@@ -488,9 +490,28 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
   int fail_at = -1;
   for (int i = 0; i < n; ++i) {
     const int s = i % kBulkStages;
-    const bool ok = mbar_wait(&full[s], (uint32_t)((i / kBulkStages) & 1));
     const int b0 = 2 * (pair0 + i);
     const bool two = b0 + 1 < p.B;
+    // dtproj: dt of channel d for the pair's rows, x_proj's dt_raw columns
+    // times the channel's dt_proj row, the 4 quarters striding the dt_rank
+    // terms and summed in quad_sum's order; loaded and formed before the wait
+    // so their latency overlaps the stage's copies
+    float dtw[2] = {0.f, 0.f};
+    if (dtproj) {
+      const float* wr = p.wdt + (size_t)d * p.dt_rank;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float* xr = p.xbc + (size_t)(r == 1 && !two ? b0 : b0 + r) * p.ld_x;
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < kMaxDtRank / 4; ++k) {
+          const int j = q + 4 * k;
+          if (j < p.dt_rank) acc = __fmaf_rn(__ldg(wr + j), xr[j], acc);
+        }
+        dtw[r] = quad_sum(acc);
+      }
+    }
+    const bool ok = mbar_wait(&full[s], (uint32_t)((i / kBulkStages) & 1));
     if constexpr (PRO) {
       // Bc / Cc of the pair from the staged raw rows: warp w normalises and
       // folds (row w/2, B or C) exactly as step_inputs_kernel does (one warp
@@ -547,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
           if constexpr (T > 0) ld_vec<T, VT>(ds + 4 * R + q * T, dv[r] + R);
         }
         if constexpr (PRO) {   // delta = softplus(dt + bias), as step_inputs_kernel
-          const float dtv = reinterpret_cast<const float*>(st + SL::oDL(r))[grp];
+          const float dtv = dtproj ? dtw[r] : reinterpret_cast<const float*>(st + SL::oDL(r))[grp];
           dlv[r] = softplus20(p.dt_bias != nullptr ? __fadd_rn(dtv, p.dt_bias[d]) : dtv);
         } else {
           dlv[r] = bf_du ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + SL::oDL(r))[grp])

@@ -3,9 +3,10 @@
 Host-side mirror of ``redpanda/engine/mamba.py`` (the reference's backbone)
 with the same class names, constructor arguments, parameter names and
 initialisation, so a reference ``state_dict`` loads unchanged.  The
-projections (``in_proj``, ``x_proj``, ``dt_proj``, ``out_proj``), BCNorm and the
-gating stay plain PyTorch (cuBLAS GEMMs), exactly as in the reference; the
-recurrences go through :mod:`redpanda_b200.scan`:
+projections (``in_proj``, ``x_proj``, ``dt_proj``, ``out_proj``) are cuBLAS
+GEMMs, as in the reference, except in the small-batch lockstep step, where
+the library's matrix-vector kernels run them with the norm, silu and residual
+folded in; the recurrences go through :mod:`redpanda_b200.scan`:
 
 * causal scan (``_selective_scan_trapezoidal``, mamba.py:318-380) ->
   ``m3_trapezoidal_scan`` (forward + analytic backward)
@@ -104,6 +105,12 @@ class Mamba3Block(nn.Module):
     # channel-tile CTA than the delta/Bc/Cc round trip costs.
     fuse_step = True
     fuse_step_max_batch = 512
+    # Lockstep batches of at most this many rows (a search node, a few lines)
+    # run the whole step layer on the library's small-batch kernels, four
+    # launches per layer (``step_small_``): their projections are
+    # matrix-vector products, where launch latency, not arithmetic, sets the
+    # time.  0 disables it.
+    small_step_max_batch = 8
 
     def __init__(self, config: MambaConfig):
         super().__init__()
@@ -428,6 +435,64 @@ class Mamba3Block(nn.Module):
         return S.m3_step_gated_(state, delta, u, bc, cc, self.step_params(), cfg.n_rot_state,
                                 xz[:, cfg.d_inner:], self.D)
 
+    def small_step_ok(self, x):
+        """True when ``step_small_`` serves a lockstep batch ``x`` (B, d_model):
+        no autograd, fp32 outside autocast, B <= small_step_max_batch, and the
+        rows fit the kernels' staging (checked here so that a layer never
+        stops half way)."""
+        cfg = self.config
+        B = x.shape[0]
+        if not (self.fuse_step and 0 < B <= min(self.small_step_max_batch, S.SMALL_ROWS)):
+            return False
+        if torch.is_grad_enabled() or _bf16_layer() or x.dtype != torch.float32:
+            return False
+        pad = S.small_rows_pad(B)
+        return (cfg.d_model % 4 == 0 and cfg.d_inner % 4 == 0
+                and pad * cfg.d_model <= S.SMALL_STAGE
+                and pad * (cfg.d_inner + cfg.dt_rank) <= S.SMALL_STAGE
+                and all(w.dtype == torch.float32 and w.is_contiguous() for w in (
+                    self.in_proj.weight, self.x_proj.weight, self.dt_proj.weight,
+                    self.out_proj.weight)))
+
+    def step_small_(self, x, norm, state):
+        """One layer of the lockstep step for a small batch (``small_step_ok``),
+        in place on the residual stream ``x`` (B, d_model) float32 contiguous
+        and on ``state`` (as ``step_fused_``):
+
+        * RMSNorm + in_proj + silu of the x half (``m3_rows_linear``,
+          mamba.py:82-89, 450-452),
+        * x_proj (``m3_rows_linear``, mamba.py:454),
+        * dt_proj's product, softplus, BCNorm, MIMO fold, recurrence and the
+          gated output (``m3_step_gated_fused_proj``, mamba.py:455-497; where
+          that kernel does not serve the lane split, ``m3_xdt_proj`` then
+          ``m3_step_inputs`` + ``m3_step_gated``),
+        * out_proj + the residual add, written back into ``x``
+          (``m3_rows_linear``, mamba.py:497, 591-595).
+
+        Same arithmetic as ``step_fused_`` except the projections' summation
+        order (their products are not cuBLAS GEMMs here)."""
+        cfg = self.config
+        d_in, n, p = cfg.d_inner, cfg.d_state, cfg.mimo_p
+        u, z = S.m3_rows_linear(x, self.in_proj.weight, self.in_proj.bias, norm.weight,
+                                norm.eps, split=d_in, silu=True)
+        x_dbl, _ = S.m3_rows_linear(u, self.x_proj.weight, self.x_proj.bias)
+        bw = self.b_norm.weight if cfg.use_bcnorm else None
+        cw = self.c_norm.weight if cfg.use_bcnorm else None
+        eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
+        off_b, off_c = cfg.dt_rank, cfg.dt_rank + n * p
+        g = S.m3_step_gated_fused_proj_(state, self.dt_proj.weight, x_dbl, off_b, off_c, bw, cw,
+                                        eps, p, u, self.step_params(), cfg.n_rot_state, z,
+                                        self.D, dt_bias=self.dt_proj.bias)
+        if g is None:   # a lane split the fused kernel does not serve: dt, then two launches
+            x_dbl, dt = S.m3_xdt_proj(u, self.x_proj.weight, self.x_proj.bias,
+                                      self.dt_proj.weight)
+            delta, bc, cc = S.m3_step_inputs(dt, x_dbl, cfg.dt_rank, off_c, bw, cw, eps, n, p,
+                                             dt_bias=self.dt_proj.bias)
+            g = S.m3_step_gated_(state, delta, u, bc, cc, self.step_params(), cfg.n_rot_state,
+                                 z, self.D)
+        S.m3_rows_linear(g, self.out_proj.weight, self.out_proj.bias, residual=x, out0=x)
+        return x
+
     def step(self, x_t, state=None):
         """Functional O(1) step (mamba.py:427-498): returns (out, (h, dBu_t))."""
         cfg = self.config
@@ -517,9 +582,19 @@ class Mamba(nn.Module):
     def step_fused_(self, token_id=None, cache=None, input_embed=None, apply_final_norm=True):
         """Lockstep step of every layer on the fused step layer, in place on
         ``cache`` (entries (h, dBu) or (h, fac_prev, fac_next)); out_proj and
-        the residual add are one GEMM (addmm).  Returns (hidden, cache)."""
+        the residual add are one GEMM (addmm).  Batches of at most
+        ``Mamba3Block.small_step_max_batch`` rows run every layer on the
+        small-batch kernels instead (``Mamba3Block.step_small_``: norm,
+        projections, step and residual in four launches per layer).  Returns
+        (hidden, cache)."""
         assert not self.config.bidirectional, "step() requires a causal model"
         x = self._embed_step(token_id, input_embed)
+        if self.layers[0]["mixer"].small_step_ok(x):
+            # the small-batch layer updates the residual stream in place
+            x = x.clone() if input_embed is not None or not x.is_contiguous() else x
+            for i, layer in enumerate(self.layers):
+                layer["mixer"].step_small_(x, layer["norm"], cache[i])
+            return (self.norm_f(x) if apply_final_norm else x), cache
         for i, layer in enumerate(self.layers):
             mixer, norm = layer["mixer"], layer["norm"]
             g = mixer.step_fused_(norm(x), cache[i])

@@ -709,9 +709,6 @@ def m3_step_gated_(state, delta_t, u_t, Bc_t, Cc_t, params, n_rot, z, d_skip):
     return out
 
 
-M3_ERR_UNSUPPORTED = 4
-
-
 def m3_silu(x):
     """silu(x) = x / (1 + exp(-x)) over the rows of a (rows, D) float32 view
     whose rows may be strided (the x half of in_proj's output, mamba.py:243,
@@ -728,6 +725,93 @@ def m3_silu(x):
     return out
 
 
+SMALL_ROWS = 8          # row limit of the small-batch projection kernels
+SMALL_STAGE = 12288     # staged input floats per CTA of those kernels (rows padded to 1/2/4/8)
+
+
+def small_rows_pad(rows):
+    """Rows as the small-batch kernels stage them (1, 2, 4 or 8)."""
+    return 1 if rows <= 1 else 2 if rows <= 2 else 4 if rows <= 4 else 8
+
+
+def _f32_rows(t, name):
+    if t.dtype != torch.float32 or t.dim() != 2 or t.stride(-1) != 1:
+        raise ValueError(f"{name}: a (rows, n) float32 view with contiguous rows")
+    return t
+
+
+def m3_rows_linear(x, weight, bias=None, norm_weight=None, eps=0.0, residual=None,
+                   split=None, silu=False, out0=None, out1=None):
+    """Small-batch projection ``act(residual + (bias + norm(x) @ weight.T))``
+    in one launch (at most :data:`SMALL_ROWS` rows, fp32).
+
+    ``norm_weight``: apply the RMSNorm x * rsqrt(mean(x^2) + eps) * w first
+    (mamba.py:82-89).  Columns ``[0, split)`` are returned in ``out0`` (silu
+    applied when ``silu``: the x half of in_proj, mamba.py:450-452) and
+    ``[split, d_out)`` in ``out1`` (the z half); ``split`` defaults to d_out.
+    ``residual`` (rows, d_out) is added last (mamba.py:595) and may be passed as
+    ``out0`` to update it in place.  Returns (out0, out1) -- ``out1`` is None
+    when split == d_out -- or None when the shape is past the kernel's limits
+    (nothing launched)."""
+    lib = _lib.load()
+    dev = _require_cuda(x, weight)
+    _f32_rows(x, "m3_rows_linear")
+    rows, d_in = x.shape
+    d_out = weight.shape[0]
+    if weight.dtype != torch.float32 or not weight.is_contiguous() or weight.shape[1] != d_in:
+        return None
+    split = d_out if split is None else int(split)
+    if out0 is None and split > 0:
+        out0 = torch.empty(rows, split, device=dev, dtype=torch.float32)
+    if out1 is None and split < d_out:
+        out1 = torch.empty(rows, d_out - split, device=dev, dtype=torch.float32)
+    for t, nm in ((out0, "out0"), (out1, "out1"), (residual, "residual")):
+        if t is not None:
+            _f32_rows(t, "m3_rows_linear " + nm)
+    nw = None if norm_weight is None else norm_weight.detach().to(torch.float32).contiguous()
+    b = None if bias is None else bias.detach().to(torch.float32).contiguous()
+    with torch.cuda.device(dev):
+        rc = lib.m3_rows_linear(rows, d_in, d_out, x.data_ptr(), x.stride(0), ctypes_ptr(nw),
+                                float(eps), weight.data_ptr(), ctypes_ptr(b), ctypes_ptr(residual),
+                                0 if residual is None else residual.stride(0), split, int(bool(silu)),
+                                ctypes_ptr(out0), 0 if out0 is None else out0.stride(0),
+                                ctypes_ptr(out1), 0 if out1 is None else out1.stride(0),
+                                _stream(dev))
+    if rc == M3_ERR_UNSUPPORTED:
+        return None
+    _lib.check(rc)
+    return out0, out1
+
+
+def m3_xdt_proj(u, w_x, b_x, w_dt):
+    """Small-batch ``x_dbl = u @ w_x.T + b_x`` (mamba.py:454) and
+    ``dt = x_dbl[:, :dt_rank] @ w_dt.T`` (dt_proj without its bias,
+    mamba.py:463) in one launch; ``dt_rank`` = w_dt.shape[1].  Returns
+    (x_dbl, dt), or None when the shape is past the kernel's limits."""
+    lib = _lib.load()
+    dev = _require_cuda(u, w_x, w_dt)
+    _f32_rows(u, "m3_xdt_proj")
+    if not u.is_contiguous():
+        u = u.contiguous()
+    rows, d = u.shape
+    n_x, r = w_x.shape[0], w_dt.shape[1]
+    for w in (w_x, w_dt):
+        if w.dtype != torch.float32 or not w.is_contiguous():
+            return None
+    if w_x.shape[1] != d or w_dt.shape[0] != d:
+        raise ValueError("m3_xdt_proj: weight shapes do not match u")
+    b = None if b_x is None else b_x.detach().to(torch.float32).contiguous()
+    x_dbl = torch.empty(rows, n_x, device=dev, dtype=torch.float32)
+    dt = torch.empty(rows, d, device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        rc = lib.m3_xdt_proj(rows, d, n_x, r, u.data_ptr(), w_x.data_ptr(), ctypes_ptr(b),
+                             w_dt.data_ptr(), x_dbl.data_ptr(), dt.data_ptr(), _stream(dev))
+    if rc == M3_ERR_UNSUPPORTED:
+        return None
+    _lib.check(rc)
+    return x_dbl, dt
+
+
 def m3_step_gated_fused_(state, dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, mimo_p,
                          u_t, params, n_rot, z, d_skip, dt_bias=None):
     """:func:`m3_step_inputs` + :func:`m3_step_gated_` in ONE launch
@@ -741,13 +825,33 @@ def m3_step_gated_fused_(state, dt, x_dbl, off_b, off_c, b_weight, c_weight, eps
     Returns the gated output (B, D) float32, or None when the fused kernel does
     not serve this shape or layout (nothing launched; the caller runs the two
     launches)."""
+    if dt.dtype != torch.float32 or dt.stride(-1) != 1:
+        return None
+    return _step_gated_fused(state, dt, None, x_dbl, off_b, off_c, b_weight, c_weight, eps,
+                             mimo_p, u_t, params, n_rot, z, d_skip, dt_bias)
+
+
+def m3_step_gated_fused_proj_(state, w_dt, x_dbl, off_b, off_c, b_weight, c_weight, eps,
+                              mimo_p, u_t, params, n_rot, z, d_skip, dt_bias=None):
+    """:func:`m3_step_gated_fused_` with dt_proj's product formed in the step
+    kernel as well (mamba.py:463): dt = x_dbl[:, :r] @ w_dt.T, r =
+    w_dt.shape[1] <= 64, then softplus(dt + dt_bias).  The step after x_proj in
+    one launch; the dt sum's order is the kernel's own (4 strided partials,
+    then pairs).  Returns the gated output, or None when the kernel does not
+    serve the shape (nothing launched)."""
+    if w_dt.dtype != torch.float32 or not w_dt.is_contiguous():
+        return None
+    return _step_gated_fused(state, None, w_dt, x_dbl, off_b, off_c, b_weight, c_weight, eps,
+                             mimo_p, u_t, params, n_rot, z, d_skip, dt_bias)
+
+
+def _step_gated_fused(state, dt, w_dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, mimo_p,
+                      u_t, params, n_rot, z, d_skip, dt_bias):
     lib = _lib.load()
     h = state[0]
-    dev = _require_cuda(h, dt, x_dbl, u_t, z, d_skip)
+    dev = _require_cuda(h, dt, w_dt, x_dbl, u_t, z, d_skip)
     B, D, N = h.shape
-    if dt.dtype != torch.float32 or x_dbl.dtype != torch.float32:
-        return None
-    if dt.stride(-1) != 1 or x_dbl.stride(-1) != 1 or z.stride(-1) != 1:
+    if x_dbl.dtype != torch.float32 or x_dbl.stride(-1) != 1 or z.stride(-1) != 1:
         return None
     if z.dtype != torch.float32:
         z = z.float()
@@ -766,13 +870,19 @@ def m3_step_gated_fused_(state, dt, x_dbl, off_b, off_c, b_weight, c_weight, eps
         dbu, fa, fb = state[1], None, None
     else:
         dbu, fa, fb = None, state[1], state[2]
+    tail = (ctypes_ptr(bias), x_dbl.data_ptr(), x_dbl.stride(0), int(off_b), int(off_c),
+            ctypes_ptr(wb), ctypes_ptr(wc), float(eps), uu.data_ptr(), ar.data_ptr(),
+            ai.data_ptr(), tk.data_ptr(), z.data_ptr(), z.stride(0), ds.data_ptr(),
+            out.data_ptr(), _stream(dev))
     with torch.cuda.device(dev):
-        rc = lib.m3_step_gated_fused(desc, int(mimo_p), h.data_ptr(), ctypes_ptr(dbu),
-                                     ctypes_ptr(fa), ctypes_ptr(fb), dt.data_ptr(), dt.stride(0),
-                                     ctypes_ptr(bias), x_dbl.data_ptr(), x_dbl.stride(0),
-                                     int(off_b), int(off_c), ctypes_ptr(wb), ctypes_ptr(wc), float(eps), uu.data_ptr(),
-                                     ar.data_ptr(), ai.data_ptr(), tk.data_ptr(), z.data_ptr(),
-                                     z.stride(0), ds.data_ptr(), out.data_ptr(), _stream(dev))
+        if w_dt is None:
+            rc = lib.m3_step_gated_fused(desc, int(mimo_p), h.data_ptr(), ctypes_ptr(dbu),
+                                         ctypes_ptr(fa), ctypes_ptr(fb), dt.data_ptr(),
+                                         dt.stride(0), *tail)
+        else:
+            rc = lib.m3_step_gated_fused_proj(desc, int(mimo_p), h.data_ptr(), ctypes_ptr(dbu),
+                                              ctypes_ptr(fa), ctypes_ptr(fb), w_dt.data_ptr(),
+                                              w_dt.shape[1], *tail)
     if rc == M3_ERR_UNSUPPORTED:
         return None
     _lib.check(rc)

@@ -167,3 +167,58 @@ def test_layer_entry_points_validate_before_device_work():
     g[2] = p
     g[13] = 32
     assert lib.m3_step_gated(*g) == 2                                  # ld_z < D
+
+
+def test_small_batch_projections_validate_before_device_work():
+    """m3_rows_linear and m3_xdt_proj reject bad arguments, shapes past their
+    staging limits (M3_ERR_UNSUPPORTED) and overlapping buffers before any
+    device work."""
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(1 << 16)
+    p = (ctypes.cast(buf, ctypes.c_void_p).value + 15) & ~15   # host memory, never read
+    q = p + 8192
+    # m3_rows_linear(rows, d_in, d_out, x, ld_x, norm_w, eps, W, bias, residual, ld_r,
+    #                split, silu, out0, ld0, out1, ld1, s)
+    a = [2, 64, 96, p, 64, None, 1e-5, p + 4096, None, None, 0, 96, 0, q, 96, None, 0, None]
+
+    def rl(**kw):
+        names = ["rows", "d_in", "d_out", "x", "ld_x", "norm_w", "eps", "W", "bias",
+                 "residual", "ld_r", "split", "silu", "out0", "ld0", "out1", "ld1", "s"]
+        v = dict(zip(names, a))
+        v.update(kw)
+        return lib.m3_rows_linear(*[v[n] for n in names])
+
+    assert rl(rows=0) == 2
+    assert rl(rows=9) == 4                     # more rows than the kernels take
+    assert rl(d_in=66, ld_x=66) == 4           # d_in not a multiple of 4
+    assert rl(rows=8, d_in=2048, ld_x=2048) == 4   # 64 KB of staged input
+    assert rl(W=None) == 1
+    assert rl(W=p + 4100) == 5                 # weight rows not 16-byte aligned
+    assert rl(split=97) == 2
+    assert rl(split=64) == 1                   # columns past split need out1
+    assert rl(ld_x=32) == 2
+    assert rl(out0=p + 64) == 11               # output overlaps the staged input
+    # m3_xdt_proj(rows, d_inner, n_x, dt_rank, u, W_x, b_x, W_dt, x_dbl, dt, s)
+    x = [2, 64, 40, 8, p, p + 4096, None, p + 4096, q, q + 4096, None]
+    assert lib.m3_xdt_proj(*(x[:2] + [6] + x[3:])) == 2           # n_x < dt_rank
+    assert lib.m3_xdt_proj(*([9] + x[1:])) == 4
+    assert lib.m3_xdt_proj(*(x[:4] + [None] + x[5:])) == 1
+    assert lib.m3_xdt_proj(*(x[:5] + [p + 4100] + x[6:])) == 5    # misaligned W_x
+    assert lib.m3_xdt_proj(*(x[:9] + [q] + x[10:])) == 11          # dt overlaps x_dbl
+
+
+def test_step_gated_fused_proj_validates_before_device_work():
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(4096)
+    p = (ctypes.cast(buf, ctypes.c_void_p).value + 15) & ~15
+    d = _sdesc()
+    # (desc, mimo_p, h, dbu, fac_prev, fac_next, W_dt, dt_rank, dt_bias, xbc, ld_x, off_b,
+    #  off_c, wb, wc, eps, u, Ar, Ai, Tk, z, ld_z, d_skip, out, s)
+    a = [ctypes.byref(d), 2, p, p, None, None, p, 8, None, p, 72, 8, 40, None, None, 1e-5,
+         p, p, p, p, p, 64, p, p, None]
+    assert lib.m3_step_gated_fused_proj(*(a[:6] + [None] + a[7:])) == 1      # no W_dt
+    assert lib.m3_step_gated_fused_proj(*(a[:7] + [0] + a[8:])) == 2         # dt_rank 0
+    assert lib.m3_step_gated_fused_proj(*(a[:7] + [80] + a[8:])) == 2        # past the row
+    big = a[:7] + [68] + a[8:10] + [136] + a[11:]
+    assert lib.m3_step_gated_fused_proj(*big) == 4                           # dt_rank > 64
+    assert lib.m3_step_gated_fused_proj(*(a[:6] + [p + 2] + a[7:])) == 5     # misaligned W_dt
