@@ -273,12 +273,20 @@ M3_API int m3_silu(int64_t rows, int32_t d, const float* x, int64_t ld_x, float*
  *   residual (rows, ld_r) or NULL, added last (mamba.py:595); it may be out0
  *        itself (out_proj + residual in place), but no output may overlap x
  *        (M3_ERR_ALIAS).
- * Rounding differs from a cuBLAS GEMM only by the summation order. */
+ * Rounding differs from a cuBLAS GEMM only by the summation order.
+ *
+ * overlap != 0 (here, in m3_xdt_proj and in m3_step_gated_fused_proj): launch
+ * as a programmatic dependent launch, so that the kernel starts while the one
+ * ahead of it on the stream finishes (a chain of these calls, as one step
+ * layer makes, then pays one launch latency instead of one per call).
+ * m3_rows_linear reads the first part of its weight rows W before that kernel
+ * has completed: set overlap only when no kernel queued before the call
+ * writes W.  Everything else is read after it has completed. */
 M3_API int m3_rows_linear(int32_t rows, int32_t d_in, int32_t d_out, const float* x,
             int64_t ld_x, const float* norm_w, float eps, const float* W,
             const float* bias, const float* residual, int64_t ld_r, int32_t split,
             int32_t silu, float* out0, int64_t ld0, float* out1, int64_t ld1,
-            void* stream);
+            int32_t overlap, void* stream);
 
 /* m3_xdt_proj: x_dbl = u W_x^T + b_x  (rows, n_x; mamba.py:454) and
  * dt = x_dbl[:, :dt_rank] W_dt^T  (rows, d_inner; dt_proj without its bias,
@@ -288,7 +296,7 @@ M3_API int m3_rows_linear(int32_t rows, int32_t d_in, int32_t d_out, const float
  * must not overlap. */
 M3_API int m3_xdt_proj(int32_t rows, int32_t d_inner, int32_t n_x, int32_t dt_rank,
             const float* u, const float* W_x, const float* b_x, const float* W_dt,
-            float* x_dbl, float* dt, void* stream);
+            float* x_dbl, float* dt, int32_t overlap, void* stream);
 
 /* Workspace bytes of m3_step_inputs_bwd (the BCNorm weight-gradient partials). */
 M3_API size_t m3_step_inputs_bwd_workspace_bytes(const m3_step_desc* desc, int32_t mimo_p);
@@ -362,7 +370,7 @@ M3_API int m3_step_gated_fused_proj(const m3_step_desc* desc, int32_t mimo_p, fl
             int32_t off_b, int32_t off_c, const float* wb, const float* wc, float eps,
             const void* u, const float* A_real_p, const float* A_imag_p,
             const float* track_p, const float* z, int64_t ld_z, const float* d_skip,
-            float* out, void* stream);
+            float* out, int32_t overlap, void* stream);
 
 /* The layer's gated activation after a scan (mamba.py:262-265), elementwise
  * over (rows, D) = (B*L, D):

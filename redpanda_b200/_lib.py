@@ -64,8 +64,8 @@ SIGNATURES = {
     "m3_silu": (ctypes.c_int, [ctypes.c_int64, _I, _P, ctypes.c_int64, _P, _P]),
     "m3_rows_linear": (ctypes.c_int, [_I, _I, _I, _P, ctypes.c_int64, _P, ctypes.c_float, _P,
                                       _P, _P, ctypes.c_int64, _I, _I, _P, ctypes.c_int64, _P,
-                                      ctypes.c_int64, _P]),
-    "m3_xdt_proj": (ctypes.c_int, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
+                                      ctypes.c_int64, _I, _P]),
+    "m3_xdt_proj": (ctypes.c_int, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P]),
     "m3_step_inputs_bwd_workspace_bytes": (_Z, [_S, _I]),
     "m3_step_inputs_bwd": (ctypes.c_int, [_S, _I, _P, ctypes.c_int64, _P, ctypes.c_int64, _I,
                                           _I, _P, _P, ctypes.c_float, _P, _P, _P, _P, _P, _P,
@@ -85,7 +85,8 @@ SIGNATURES = {
                                            _P, _P, _P, _P, _P, ctypes.c_int64, _P, _P, _P]),
     "m3_step_gated_fused_proj": (ctypes.c_int, [_S, _I, _P, _P, _P, _P, _P, _I, _P, _P,
                                                 ctypes.c_int64, _I, _I, _P, _P, ctypes.c_float,
-                                                _P, _P, _P, _P, _P, ctypes.c_int64, _P, _P, _P]),
+                                                _P, _P, _P, _P, _P, ctypes.c_int64, _P, _P, _I,
+                                                _P]),
 }
 
 _lock = threading.Lock()

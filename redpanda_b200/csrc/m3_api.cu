@@ -373,6 +373,7 @@ struct StepPro {
   const float* wb; const float* wc;
   float eps;
   const float* wdt = nullptr; int32_t dt_rank = 0;   // dt formed in the kernel
+  int pdl = 0;                                        // programmatic dependent launch
 };
 
 static int step_common(const m3_step_desc* desc, float* h, float* dbu, const float* fac_prev,
@@ -435,7 +436,7 @@ static int step_common(const m3_step_desc* desc, float* h, float* dbu, const flo
     p.xbc = pro->xbc; p.ld_x = pro->ld_x;
     p.off_b = pro->off_b; p.off_c = pro->off_c; p.P = pro->P;
     p.wb = pro->wb; p.wc = pro->wc; p.eps = pro->eps;
-    p.wdt = pro->wdt; p.dt_rank = pro->dt_rank;
+    p.wdt = pro->wdt; p.dt_rank = pro->dt_rank; p.pdl = pro->pdl;
   }
   cudaError_t e = launch_step(t, p, static_cast<cudaStream_t>(stream));
   if (e == cudaErrorNotSupported) return M3_ERR_UNSUPPORTED;
@@ -613,7 +614,8 @@ int m3_step_gated_fused_proj(const m3_step_desc* desc, int32_t mimo_p, float* h,
                              int64_t ld_x, int32_t off_b, int32_t off_c, const float* wb,
                              const float* wc, float eps, const void* u, const float* A_real_p,
                              const float* A_imag_p, const float* track_p, const float* z,
-                             int64_t ld_z, const float* d_skip, float* out, void* stream) {
+                             int64_t ld_z, const float* d_skip, float* out, int32_t overlap,
+                             void* stream) {
   if (!desc || !z || !d_skip || !W_dt || !xbc) return M3_ERR_NULL;
   if ((dbu != nullptr) == (fac_next != nullptr)) return M3_ERR_NULL;   // exactly one state form
   if ((wb == nullptr) != (wc == nullptr)) return M3_ERR_NULL;
@@ -631,6 +633,7 @@ int m3_step_gated_fused_proj(const m3_step_desc* desc, int32_t mimo_p, float* h,
   StepPro pro{nullptr, 0, dt_bias, xbc, ld_x, off_b, off_c, mimo_p, wb, wc, eps};
   pro.wdt = W_dt;
   pro.dt_rank = dt_rank;
+  pro.pdl = overlap != 0;
   // delta/Bc/Cc are not read under the fused prologue; xbc stands in for the
   // pointer checks (16-byte aligned)
   return step_common(desc, h, dbu, fac_prev, fac_next, xbc, u, xbc, xbc, A_real_p, A_imag_p,
@@ -685,7 +688,8 @@ size_t rows_span(int64_t rows, int64_t ld, int64_t width) {
 int m3_rows_linear(int32_t rows, int32_t d_in, int32_t d_out, const float* x, int64_t ld_x,
                    const float* norm_w, float eps, const float* W, const float* bias,
                    const float* residual, int64_t ld_r, int32_t split, int32_t silu,
-                   float* out0, int64_t ld0, float* out1, int64_t ld1, void* stream) {
+                   float* out0, int64_t ld0, float* out1, int64_t ld1, int32_t overlap,
+                   void* stream) {
   if (rows < 1 || d_in < 4 || d_out < 1 || split < 0 || split > d_out) return M3_ERR_SHAPE;
   if (rows > kSmallRows || d_in % 4 != 0 ||
       (int64_t)small_rows_pad(rows) * d_in > kSmallStage)
@@ -711,13 +715,14 @@ int m3_rows_linear(int32_t rows, int32_t d_in, int32_t d_out, const float* x, in
   p.x = x; p.ld_x = ld_x; p.norm_w = norm_w; p.eps = eps; p.W = W; p.bias = bias;
   p.residual = residual; p.ld_r = ld_r; p.out0 = out0; p.ld0 = ld0; p.out1 = out1; p.ld1 = ld1;
   p.rows = rows; p.d_in = d_in; p.d_out = d_out; p.split = split; p.silu = silu != 0;
+  p.pdl = overlap != 0;
   cudaError_t e = launch_rows_linear(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
 
 int m3_xdt_proj(int32_t rows, int32_t d_inner, int32_t n_x, int32_t dt_rank, const float* u,
                 const float* W_x, const float* b_x, const float* W_dt, float* x_dbl, float* dt,
-                void* stream) {
+                int32_t overlap, void* stream) {
   if (rows < 1 || d_inner < 4 || dt_rank < 1 || n_x < dt_rank) return M3_ERR_SHAPE;
   if (rows > kSmallRows || d_inner % 4 != 0 || dt_rank > kMaxDtRank ||
       (int64_t)small_rows_pad(rows) * (d_inner + dt_rank) > kSmallStage)
@@ -737,6 +742,7 @@ int m3_xdt_proj(int32_t rows, int32_t d_inner, int32_t n_x, int32_t dt_rank, con
   memset(&p, 0, sizeof(p));
   p.u = u; p.Wx = W_x; p.bx = b_x; p.Wdt = W_dt; p.x_dbl = x_dbl; p.dt = dt;
   p.rows = rows; p.D = d_inner; p.n_x = n_x; p.r = dt_rank;
+  p.pdl = overlap != 0;
   cudaError_t e = launch_xdt_proj(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }

@@ -26,6 +26,7 @@
 #include <stdint.h>
 
 #include "m3_internal.h"
+#include "m3_pdl.cuh"
 
 namespace m3 {
 namespace {
@@ -46,23 +47,29 @@ __device__ __forceinline__ float silu_f(float z) {
 
 // Dot products of one weight row w (K floats, 16-byte aligned, K % 4 == 0)
 // with the RW staged rows of s; every lane returns the warp totals.  Each
-// lane issues its loads of the row in batches of kBatch 16-byte loads before
-// using them, so a row of up to kBatch * 512 bytes costs one memory latency.
+// lane loads the row in batches of kBatch 16-byte loads issued before they are
+// used, so a row of up to kBatch * 512 bytes costs one memory latency; `a`
+// holds the first batch on entry (load_batch), which lets a kernel issue it
+// before it waits for its inputs.
 constexpr int kBatch = 8;
+
+__device__ __forceinline__ void load_batch(const float* __restrict__ w, int K4, int k0,
+                                           float4 (&a)[kBatch]) {
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int j = 0; j < kBatch; ++j)
+    if (k0 + 32 * j < K4) a[j] = __ldg(w4 + k0 + 32 * j);
+}
 
 template <int RW>
 __device__ __forceinline__ void row_dots(const float* __restrict__ w, const float* s, int K,
-                                         int lane, float (&acc)[RW]) {
-  const float4* w4 = reinterpret_cast<const float4*>(w);
+                                         int lane, float4 (&a)[kBatch], float (&acc)[RW]) {
   const float4* s4 = reinterpret_cast<const float4*>(s);
   const int K4 = K >> 2;
 #pragma unroll
   for (int r = 0; r < RW; ++r) acc[r] = 0.f;
   for (int k0 = lane; k0 < K4; k0 += 32 * kBatch) {
-    float4 a[kBatch];
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j)
-      if (k0 + 32 * j < K4) a[j] = __ldg(w4 + k0 + 32 * j);
+    if (k0 != lane) load_batch(w, K4, k0, a);
 #pragma unroll
     for (int j = 0; j < kBatch; ++j) {
       if (k0 + 32 * j < K4) {
@@ -121,14 +128,23 @@ __device__ void stage_rows(float* s, const float* x, long long ld_x, int rows, i
 
 // out = act(residual + (bias + norm(x) W^T)); the residual is added last, as
 // the reference adds the layer's output to its input (mamba.py:595).
+// Launched as a programmatic dependent launch (p.pdl), the first batch of
+// each warp's weight row is loaded before the kernel waits for the kernel
+// ahead of it, so that load overlaps the previous layer's tail.
 template <int RW>
 __global__ void __launch_bounds__(kLinThreads) rows_linear_kernel(const RowsLinearParams p) {
   extern __shared__ __align__(16) float s_x[];   // [RW][d_in]
-  stage_rows<RW, kLinThreads>(s_x, p.x, p.ld_x, p.rows, p.d_in, p.norm_w, p.eps);
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int o = blockIdx.x * kLinWarps + warp; o < p.d_out; o += gridDim.x * kLinWarps) {
+  const int o0 = blockIdx.x * kLinWarps + warp;
+  float4 a[kBatch];
+  if (o0 < p.d_out) load_batch(p.W + (size_t)o0 * p.d_in, p.d_in >> 2, lane, a);
+  pdl_wait();
+  stage_rows<RW, kLinThreads>(s_x, p.x, p.ld_x, p.rows, p.d_in, p.norm_w, p.eps);
+  for (int o = o0; o < p.d_out; o += gridDim.x * kLinWarps) {
+    if (o != o0) load_batch(p.W + (size_t)o * p.d_in, p.d_in >> 2, lane, a);
     float acc[RW];
-    row_dots<RW>(p.W + (size_t)o * p.d_in, s_x, p.d_in, lane, acc);
+    row_dots<RW>(p.W + (size_t)o * p.d_in, s_x, p.d_in, lane, a, acc);
     float v = lane_row<RW>(acc, lane);
     if (lane < p.rows) {
       if (p.bias) v = __fadd_rn(v, p.bias[o]);
@@ -156,11 +172,15 @@ template <int RW>
 __global__ void __launch_bounds__(kXdtThreads) xdt_proj_kernel(const XdtParams p) {
   extern __shared__ __align__(16) float s_u[];   // [RW][D], then [RW][r] dt_raw
   float* s_raw = s_u + RW * p.D;
+  pdl_launch_dependents();
+  pdl_wait();
   stage_rows<RW, kXdtThreads>(s_u, p.u, p.D, p.rows, p.D, nullptr, 0.f);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float4 a[kBatch];
   for (int j = warp; j < p.r; j += kXdtWarps) {
     float acc[RW];
-    row_dots<RW>(p.Wx + (size_t)j * p.D, s_u, p.D, lane, acc);
+    load_batch(p.Wx + (size_t)j * p.D, p.D >> 2, lane, a);
+    row_dots<RW>(p.Wx + (size_t)j * p.D, s_u, p.D, lane, a, acc);
     float v = lane_row<RW>(acc, lane);
     if (p.bx) v = __fadd_rn(v, p.bx[j]);
     if (lane < RW) s_raw[lane * p.r + j] = v;
@@ -168,7 +188,8 @@ __global__ void __launch_bounds__(kXdtThreads) xdt_proj_kernel(const XdtParams p
   }
   for (int j = p.r + blockIdx.x * kXdtWarps + warp; j < p.n_x; j += gridDim.x * kXdtWarps) {
     float acc[RW];
-    row_dots<RW>(p.Wx + (size_t)j * p.D, s_u, p.D, lane, acc);
+    load_batch(p.Wx + (size_t)j * p.D, p.D >> 2, lane, a);
+    row_dots<RW>(p.Wx + (size_t)j * p.D, s_u, p.D, lane, a, acc);
     float v = lane_row<RW>(acc, lane);
     if (p.bx) v = __fadd_rn(v, p.bx[j]);
     if (lane < p.rows) p.x_dbl[(size_t)lane * p.n_x + j] = v;
@@ -204,8 +225,8 @@ template <int RW>
 cudaError_t rows_linear_impl(const RowsLinearParams& p, cudaStream_t s) {
   const int grid = (p.d_out + kLinWarps - 1) / kLinWarps;
   const size_t smem = (size_t)RW * p.d_in * sizeof(float);
-  rows_linear_kernel<RW><<<grid, kLinThreads, smem, s>>>(p);
-  return cudaGetLastError();
+  return launch_maybe_pdl(p.pdl != 0, rows_linear_kernel<RW>, dim3(grid), dim3(kLinThreads), smem,
+                          s, p);
 }
 
 template <int RW>
@@ -215,8 +236,8 @@ cudaError_t xdt_proj_impl(const XdtParams& p, cudaStream_t s) {
   int grid = g1 > g2 ? g1 : g2;
   grid = grid < 1 ? 1 : (grid > 64 ? 64 : grid);
   const size_t smem = (size_t)RW * (p.D + p.r) * sizeof(float);
-  xdt_proj_kernel<RW><<<grid, kXdtThreads, smem, s>>>(p);
-  return cudaGetLastError();
+  return launch_maybe_pdl(p.pdl != 0, xdt_proj_kernel<RW>, dim3(grid), dim3(kXdtThreads), smem,
+                          s, p);
 }
 
 }  // namespace

@@ -120,6 +120,7 @@ struct StepParams {
   // pro with the dt product: dt = xbc[:, :dt_rank] wdt^T computed in the
   // kernel (dt_proj, wdt (D, dt_rank) row-major); `dt` is unused then
   const float* wdt; int dt_rank;
+  int pdl;                                    // programmatic dependent launch (bulk kernel)
 };
 
 struct ReduceParams {
@@ -223,6 +224,7 @@ struct RowsLinearParams {
   float* out0; long long ld0;
   float* out1; long long ld1;
   int rows, d_in, d_out, split, silu;
+  int pdl;                                    // programmatic dependent launch
 };
 cudaError_t launch_rows_linear(const RowsLinearParams& p, cudaStream_t s);
 
@@ -234,6 +236,7 @@ struct XdtParams {
   float* x_dbl;                               // (rows, n_x)
   float* dt;                                  // (rows, D)
   int rows, D, n_x, r;
+  int pdl;                                    // programmatic dependent launch
 };
 cudaError_t launch_xdt_proj(const XdtParams& p, cudaStream_t s);
 

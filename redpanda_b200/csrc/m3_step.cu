@@ -27,6 +27,7 @@
 #include <string.h>
 
 #include "m3_common.cuh"
+#include "m3_pdl.cuh"
 #include "m3_internal.h"
 #include "m3_bulk.cuh"
 #include "m3_prologue.cuh"
@@ -401,6 +402,10 @@ __global__ void __launch_bounds__(kThreads, step_min_blocks(R + T))
   static_assert(!PRO || kThreads == 128, "the fused prologue uses one warp per (row, B|C)");
   constexpr int kBulkStages = bulk_stages(FACT);
   extern __shared__ __align__(128) unsigned char smem_raw[];
+  // launched as a programmatic dependent launch (p.pdl), the kernel starts
+  // while the one ahead of it finishes and waits here before reading anything
+  pdl_launch_dependents();
+  pdl_wait();
   // stage buffers (from the first 1 KB boundary when swizzled), then one
   // mbarrier per stage
   unsigned char* smem =
@@ -715,8 +720,8 @@ cudaError_t launch_step_bulk_kernel(const StepParams& p, cudaStream_t stream,
   const int per = (npairs + g - 1) / g;
   g = (npairs + per - 1) / per;
   dim3 grid(g, tiles);
-  kern<<<grid, kThreads, smem, stream>>>(p, per, mh, md);
-  return cudaGetLastError();
+  return launch_maybe_pdl(p.pdl != 0, kern, grid, dim3(kThreads), (size_t)smem, stream, p, per,
+                          mh, md);
 }
 
 

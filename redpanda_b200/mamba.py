@@ -473,24 +473,27 @@ class Mamba3Block(nn.Module):
         order (their products are not cuBLAS GEMMs here)."""
         cfg = self.config
         d_in, n, p = cfg.d_inner, cfg.d_state, cfg.mimo_p
+        # each launch may start while the one before it finishes (programmatic
+        # dependent launches; no kernel of the step writes a weight)
         u, z = S.m3_rows_linear(x, self.in_proj.weight, self.in_proj.bias, norm.weight,
-                                norm.eps, split=d_in, silu=True)
-        x_dbl, _ = S.m3_rows_linear(u, self.x_proj.weight, self.x_proj.bias)
+                                norm.eps, split=d_in, silu=True, overlap=True)
+        x_dbl, _ = S.m3_rows_linear(u, self.x_proj.weight, self.x_proj.bias, overlap=True)
         bw = self.b_norm.weight if cfg.use_bcnorm else None
         cw = self.c_norm.weight if cfg.use_bcnorm else None
         eps = self.b_norm.eps if cfg.use_bcnorm else 0.0
         off_b, off_c = cfg.dt_rank, cfg.dt_rank + n * p
         g = S.m3_step_gated_fused_proj_(state, self.dt_proj.weight, x_dbl, off_b, off_c, bw, cw,
                                         eps, p, u, self.step_params(), cfg.n_rot_state, z,
-                                        self.D, dt_bias=self.dt_proj.bias)
+                                        self.D, dt_bias=self.dt_proj.bias, overlap=True)
         if g is None:   # a lane split the fused kernel does not serve: dt, then two launches
             x_dbl, dt = S.m3_xdt_proj(u, self.x_proj.weight, self.x_proj.bias,
-                                      self.dt_proj.weight)
+                                      self.dt_proj.weight, overlap=True)
             delta, bc, cc = S.m3_step_inputs(dt, x_dbl, cfg.dt_rank, off_c, bw, cw, eps, n, p,
                                              dt_bias=self.dt_proj.bias)
             g = S.m3_step_gated_(state, delta, u, bc, cc, self.step_params(), cfg.n_rot_state,
                                  z, self.D)
-        S.m3_rows_linear(g, self.out_proj.weight, self.out_proj.bias, residual=x, out0=x)
+        S.m3_rows_linear(g, self.out_proj.weight, self.out_proj.bias, residual=x, out0=x,
+                         overlap=True)
         return x
 
     def step(self, x_t, state=None):

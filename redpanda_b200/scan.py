@@ -741,7 +741,7 @@ def _f32_rows(t, name):
 
 
 def m3_rows_linear(x, weight, bias=None, norm_weight=None, eps=0.0, residual=None,
-                   split=None, silu=False, out0=None, out1=None):
+                   split=None, silu=False, out0=None, out1=None, overlap=False):
     """Small-batch projection ``act(residual + (bias + norm(x) @ weight.T))``
     in one launch (at most :data:`SMALL_ROWS` rows, fp32).
 
@@ -752,7 +752,10 @@ def m3_rows_linear(x, weight, bias=None, norm_weight=None, eps=0.0, residual=Non
     ``residual`` (rows, d_out) is added last (mamba.py:595) and may be passed as
     ``out0`` to update it in place.  Returns (out0, out1) -- ``out1`` is None
     when split == d_out -- or None when the shape is past the kernel's limits
-    (nothing launched)."""
+    (nothing launched).  ``overlap``: launch as a programmatic dependent launch
+    that starts while the previous kernel on the stream finishes and reads the
+    first part of ``weight`` before that kernel completes (only when no queued
+    kernel writes the weight)."""
     lib = _lib.load()
     dev = _require_cuda(x, weight)
     _f32_rows(x, "m3_rows_linear")
@@ -776,14 +779,14 @@ def m3_rows_linear(x, weight, bias=None, norm_weight=None, eps=0.0, residual=Non
                                 0 if residual is None else residual.stride(0), split, int(bool(silu)),
                                 ctypes_ptr(out0), 0 if out0 is None else out0.stride(0),
                                 ctypes_ptr(out1), 0 if out1 is None else out1.stride(0),
-                                _stream(dev))
+                                int(bool(overlap)), _stream(dev))
     if rc == M3_ERR_UNSUPPORTED:
         return None
     _lib.check(rc)
     return out0, out1
 
 
-def m3_xdt_proj(u, w_x, b_x, w_dt):
+def m3_xdt_proj(u, w_x, b_x, w_dt, overlap=False):
     """Small-batch ``x_dbl = u @ w_x.T + b_x`` (mamba.py:454) and
     ``dt = x_dbl[:, :dt_rank] @ w_dt.T`` (dt_proj without its bias,
     mamba.py:463) in one launch; ``dt_rank`` = w_dt.shape[1].  Returns
@@ -805,7 +808,8 @@ def m3_xdt_proj(u, w_x, b_x, w_dt):
     dt = torch.empty(rows, d, device=dev, dtype=torch.float32)
     with torch.cuda.device(dev):
         rc = lib.m3_xdt_proj(rows, d, n_x, r, u.data_ptr(), w_x.data_ptr(), ctypes_ptr(b),
-                             w_dt.data_ptr(), x_dbl.data_ptr(), dt.data_ptr(), _stream(dev))
+                             w_dt.data_ptr(), x_dbl.data_ptr(), dt.data_ptr(), int(bool(overlap)),
+                             _stream(dev))
     if rc == M3_ERR_UNSUPPORTED:
         return None
     _lib.check(rc)
@@ -832,21 +836,24 @@ def m3_step_gated_fused_(state, dt, x_dbl, off_b, off_c, b_weight, c_weight, eps
 
 
 def m3_step_gated_fused_proj_(state, w_dt, x_dbl, off_b, off_c, b_weight, c_weight, eps,
-                              mimo_p, u_t, params, n_rot, z, d_skip, dt_bias=None):
+                              mimo_p, u_t, params, n_rot, z, d_skip, dt_bias=None,
+                              overlap=False):
     """:func:`m3_step_gated_fused_` with dt_proj's product formed in the step
     kernel as well (mamba.py:463): dt = x_dbl[:, :r] @ w_dt.T, r =
     w_dt.shape[1] <= 64, then softplus(dt + dt_bias).  The step after x_proj in
     one launch; the dt sum's order is the kernel's own (4 strided partials,
     then pairs).  Returns the gated output, or None when the kernel does not
-    serve the shape (nothing launched)."""
+    serve the shape (nothing launched).  ``overlap``: a programmatic dependent
+    launch (see :func:`m3_rows_linear`; this kernel reads nothing before the
+    previous kernel completes)."""
     if w_dt.dtype != torch.float32 or not w_dt.is_contiguous():
         return None
     return _step_gated_fused(state, None, w_dt, x_dbl, off_b, off_c, b_weight, c_weight, eps,
-                             mimo_p, u_t, params, n_rot, z, d_skip, dt_bias)
+                             mimo_p, u_t, params, n_rot, z, d_skip, dt_bias, overlap)
 
 
 def _step_gated_fused(state, dt, w_dt, x_dbl, off_b, off_c, b_weight, c_weight, eps, mimo_p,
-                      u_t, params, n_rot, z, d_skip, dt_bias):
+                      u_t, params, n_rot, z, d_skip, dt_bias, overlap=False):
     lib = _lib.load()
     h = state[0]
     dev = _require_cuda(h, dt, w_dt, x_dbl, u_t, z, d_skip)
@@ -882,7 +889,8 @@ def _step_gated_fused(state, dt, w_dt, x_dbl, off_b, off_c, b_weight, c_weight, 
         else:
             rc = lib.m3_step_gated_fused_proj(desc, int(mimo_p), h.data_ptr(), ctypes_ptr(dbu),
                                               ctypes_ptr(fa), ctypes_ptr(fb), w_dt.data_ptr(),
-                                              w_dt.shape[1], *tail)
+                                              w_dt.shape[1], *tail[:-1], int(bool(overlap)),
+                                              tail[-1])
     if rc == M3_ERR_UNSUPPORTED:
         return None
     _lib.check(rc)

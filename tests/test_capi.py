@@ -178,12 +178,13 @@ def test_small_batch_projections_validate_before_device_work():
     p = (ctypes.cast(buf, ctypes.c_void_p).value + 15) & ~15   # host memory, never read
     q = p + 8192
     # m3_rows_linear(rows, d_in, d_out, x, ld_x, norm_w, eps, W, bias, residual, ld_r,
-    #                split, silu, out0, ld0, out1, ld1, s)
-    a = [2, 64, 96, p, 64, None, 1e-5, p + 4096, None, None, 0, 96, 0, q, 96, None, 0, None]
+    #                split, silu, out0, ld0, out1, ld1, overlap, s)
+    a = [2, 64, 96, p, 64, None, 1e-5, p + 4096, None, None, 0, 96, 0, q, 96, None, 0, 0, None]
 
     def rl(**kw):
         names = ["rows", "d_in", "d_out", "x", "ld_x", "norm_w", "eps", "W", "bias",
-                 "residual", "ld_r", "split", "silu", "out0", "ld0", "out1", "ld1", "s"]
+                 "residual", "ld_r", "split", "silu", "out0", "ld0", "out1", "ld1", "overlap",
+                 "s"]
         v = dict(zip(names, a))
         v.update(kw)
         return lib.m3_rows_linear(*[v[n] for n in names])
@@ -198,8 +199,8 @@ def test_small_batch_projections_validate_before_device_work():
     assert rl(split=64) == 1                   # columns past split need out1
     assert rl(ld_x=32) == 2
     assert rl(out0=p + 64) == 11               # output overlaps the staged input
-    # m3_xdt_proj(rows, d_inner, n_x, dt_rank, u, W_x, b_x, W_dt, x_dbl, dt, s)
-    x = [2, 64, 40, 8, p, p + 4096, None, p + 4096, q, q + 4096, None]
+    # m3_xdt_proj(rows, d_inner, n_x, dt_rank, u, W_x, b_x, W_dt, x_dbl, dt, overlap, s)
+    x = [2, 64, 40, 8, p, p + 4096, None, p + 4096, q, q + 4096, 0, None]
     assert lib.m3_xdt_proj(*(x[:2] + [6] + x[3:])) == 2           # n_x < dt_rank
     assert lib.m3_xdt_proj(*([9] + x[1:])) == 4
     assert lib.m3_xdt_proj(*(x[:4] + [None] + x[5:])) == 1
@@ -213,9 +214,9 @@ def test_step_gated_fused_proj_validates_before_device_work():
     p = (ctypes.cast(buf, ctypes.c_void_p).value + 15) & ~15
     d = _sdesc()
     # (desc, mimo_p, h, dbu, fac_prev, fac_next, W_dt, dt_rank, dt_bias, xbc, ld_x, off_b,
-    #  off_c, wb, wc, eps, u, Ar, Ai, Tk, z, ld_z, d_skip, out, s)
+    #  off_c, wb, wc, eps, u, Ar, Ai, Tk, z, ld_z, d_skip, out, overlap, s)
     a = [ctypes.byref(d), 2, p, p, None, None, p, 8, None, p, 72, 8, 40, None, None, 1e-5,
-         p, p, p, p, p, 64, p, p, None]
+         p, p, p, p, p, 64, p, p, 0, None]
     assert lib.m3_step_gated_fused_proj(*(a[:6] + [None] + a[7:])) == 1      # no W_dt
     assert lib.m3_step_gated_fused_proj(*(a[:7] + [0] + a[8:])) == 2         # dt_rank 0
     assert lib.m3_step_gated_fused_proj(*(a[:7] + [80] + a[8:])) == 2        # past the row
