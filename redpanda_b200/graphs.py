@@ -20,6 +20,9 @@ next replay, which overwrites them.  The whole state lives in one flat buffer,
 so copying a cache in or out is a single copy.
 """
 
+import collections.abc
+import numbers
+
 import torch
 
 
@@ -45,6 +48,7 @@ class StepGraph:
         self.flat = torch.zeros(n_layer * 2 * self._per, device=dev, dtype=torch.float32)
         self.cache = self._views(self.flat)
         self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+        self._pinned = None     # host staging of per-row ids (step)
 
         def run(cache):
             h, _ = model.step_fused_(token_id=self.tokens, cache=cache,
@@ -91,10 +95,7 @@ class StepGraph:
 
     def snapshot(self):
         """A copy of the static state as a new cache (one copy of the flat buffer)."""
-        flat = self.flat.clone()
-        out = FlatCache(self._views(flat))
-        out.flat = flat
-        return out
+        return FlatCache(self.flat.clone(), self._views, len(self.cache))
 
     def reset_(self):
         """Zero state (the reference's ``init_cache``: no prefix)."""
@@ -102,13 +103,45 @@ class StepGraph:
 
     def step(self, token_id):
         """Advance the static state by one token per row; returns the captured
-        outputs (hidden state first), valid until the next call."""
-        tok = token_id if torch.is_tensor(token_id) else torch.as_tensor(token_id)
-        self.tokens.copy_(tok.reshape(-1).to(self.tokens.device), non_blocking=True)
+        outputs (hidden state first), valid until the next call.
+
+        ``token_id``: one id for every row (a Python or numpy integer: written
+        by a fill kernel, with no host-to-device copy and so no wait for the
+        GPU), or one per row as a tensor or sequence (a CUDA tensor is copied
+        on the device; host ids go through a pinned buffer, asynchronously)."""
+        if isinstance(token_id, numbers.Integral):
+            self.tokens.fill_(int(token_id))
+        elif torch.is_tensor(token_id) and token_id.is_cuda:
+            self.tokens.copy_(token_id.reshape(-1))
+        else:
+            tok = torch.as_tensor(token_id).reshape(-1)
+            if self._pinned is None:
+                self._pinned = torch.empty(self.batch, dtype=torch.long, pin_memory=True)
+                self._pinned_done = torch.cuda.Event()
+            self._pinned_done.synchronize()   # the last copy out of it has run
+            self._pinned.copy_(tok.expand(self.batch) if tok.numel() == 1 else tok)
+            self.tokens.copy_(self._pinned, non_blocking=True)
+            self._pinned_done.record()
         self.graph.replay()
         return self.outputs
 
 
-class FlatCache(list):
-    """A cache list whose (h, dBu) tensors are views of one buffer, ``flat``."""
-    flat = None
+class FlatCache(collections.abc.Sequence):
+    """A cache, (h, dBu) per layer, whose tensors are views of one buffer,
+    ``flat``.  The per-layer views are made on first access: a search that only
+    hands the cache back to :meth:`StepGraph.load_` (one copy of ``flat``)
+    never pays for them."""
+
+    def __init__(self, flat, views, n):
+        self.flat = flat
+        self._make = views
+        self._n = n
+        self._views = None
+
+    def __len__(self):
+        return self._n
+
+    def __getitem__(self, i):
+        if self._views is None:
+            self._views = self._make(self.flat)
+        return self._views[i]

@@ -89,6 +89,13 @@ def test_step_graph_load_snapshot_reset():
                               cache=[(torch.zeros_like(a), torch.zeros_like(b))
                                      for a, b in cache])
         assert torch.equal(g.step(torch.tensor([9, 9, 9]))[0], h0)
+        # the token forms: one Python int for every row (a fill kernel), a CUDA
+        # tensor, a host list (through the pinned buffer) give the same step
+        outs = []
+        for tok in (9, torch.full((3,), 9, device="cuda"), [9, 9, 9]):
+            g.reset_()
+            outs.append(g.step(tok)[0].clone())
+        assert all(torch.equal(o, h0) for o in outs)
 
 
 @pytest.mark.parametrize("shape", [dict(d_model=48, d_state=16, n_track_state=4),
