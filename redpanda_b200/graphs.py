@@ -145,3 +145,42 @@ class FlatCache(collections.abc.Sequence):
         if self._views is None:
             self._views = self._make(self.flat)
         return self._views[i]
+
+
+def _main():
+    """Time the config-3 backbone's step graph: ``python -m redpanda_b200.graphs
+    --batch 1``.  Reference initialisation, random move ids; prints the CUDA-event
+    time per replayed step."""
+    import argparse
+    from .mamba import Mamba, Mamba3Block, MambaConfig
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=str, default="1", help="comma-separated batch sizes")
+    ap.add_argument("--layers", type=int, default=12)
+    ap.add_argument("--small", type=int, default=Mamba3Block.small_step_max_batch,
+                    help="Mamba3Block.small_step_max_batch (0: cuBLAS projections)")
+    ap.add_argument("--steps", type=int, default=20)
+    args = ap.parse_args()
+    torch.manual_seed(0)
+    cfg = MambaConfig(d_model=512, n_layer=args.layers, d_state=32, n_track_state=8, mimo_p=2,
+                      vocab_size=8192)
+    model = Mamba(cfg).cuda().eval()
+    Mamba3Block.small_step_max_batch = args.small
+    for batch in (int(b) for b in args.batch.split(",")):
+        g = StepGraph(model, batch)
+        moves = torch.randint(0, cfg.vocab_size, (batch,), device="cuda")
+        for _ in range(3):
+            g.step(moves)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            g.step(moves)
+        e1.record()
+        torch.cuda.synchronize()
+        print(f"batch {batch}: {e0.elapsed_time(e1) / args.steps * 1e3:.1f} us per step "
+              f"(small_step_max_batch {args.small})", flush=True)
+
+
+if __name__ == "__main__":
+    _main()
