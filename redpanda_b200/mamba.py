@@ -447,7 +447,7 @@ class Mamba3Block(nn.Module):
         if torch.is_grad_enabled() or _bf16_layer() or x.dtype != torch.float32:
             return False
         pad = S.small_rows_pad(B)
-        return (cfg.d_model % 4 == 0 and cfg.d_inner % 4 == 0
+        return (cfg.d_model % 4 == 0 and cfg.d_inner % 4 == 0 and cfg.dt_rank <= S.SMALL_DT_RANK
                 and pad * cfg.d_model <= S.SMALL_STAGE
                 and pad * (cfg.d_inner + cfg.dt_rank) <= S.SMALL_STAGE
                 and all(w.dtype == torch.float32 and w.is_contiguous() for w in (

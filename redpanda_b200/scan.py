@@ -727,6 +727,7 @@ def m3_silu(x):
 
 SMALL_ROWS = 8          # row limit of the small-batch projection kernels
 SMALL_STAGE = 12288     # staged input floats per CTA of those kernels (rows padded to 1/2/4/8)
+SMALL_DT_RANK = 64      # dt_rank limit of the small-batch dt product
 
 
 def small_rows_pad(rows):

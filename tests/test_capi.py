@@ -223,3 +223,30 @@ def test_step_gated_fused_proj_validates_before_device_work():
     big = a[:7] + [68] + a[8:10] + [136] + a[11:]
     assert lib.m3_step_gated_fused_proj(*big) == 4                           # dt_rank > 64
     assert lib.m3_step_gated_fused_proj(*(a[:6] + [p + 2] + a[7:])) == 5     # misaligned W_dt
+
+
+def test_small_step_eligibility_is_host_logic():
+    """Which lockstep batches take the small-batch layer (decided on the host
+    before any launch, so a layer never stops half way)."""
+    import torch
+    from redpanda_b200.mamba import Mamba3Block, MambaConfig
+    blk = Mamba3Block(MambaConfig(d_model=512, n_layer=1, d_state=32, n_track_state=8,
+                                  mimo_p=2))
+    x1, x9 = torch.zeros(1, 512), torch.zeros(9, 512)
+    with torch.no_grad():
+        assert blk.small_step_ok(x1)
+        assert blk.small_step_ok(torch.zeros(8, 512))
+        assert not blk.small_step_ok(x9)                       # more rows than the kernels take
+        assert not blk.small_step_ok(x1.double())              # fp32 only
+    assert not blk.small_step_ok(x1)                           # autograd on: the training path
+    wide = Mamba3Block(MambaConfig(d_model=2048, n_layer=1, d_state=32, n_track_state=8,
+                                   mimo_p=2))
+    with torch.no_grad():
+        assert not wide.small_step_ok(torch.zeros(1, 2048))    # dt_rank 128 > 64
+    old = Mamba3Block.small_step_max_batch
+    Mamba3Block.small_step_max_batch = 0
+    try:
+        with torch.no_grad():
+            assert not blk.small_step_ok(x1)                   # switched off
+    finally:
+        Mamba3Block.small_step_max_batch = old
