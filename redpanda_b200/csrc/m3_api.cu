@@ -716,6 +716,7 @@ int m3_rows_linear(int32_t rows, int32_t d_in, int32_t d_out, const float* x, in
   p.residual = residual; p.ld_r = ld_r; p.out0 = out0; p.ld0 = ld0; p.out1 = out1; p.ld1 = ld1;
   p.rows = rows; p.d_in = d_in; p.d_out = d_out; p.split = split; p.silu = silu != 0;
   p.pdl = overlap != 0;
+  p.vec = aligned(x, 16) && ld_x % 4 == 0 && (!norm_w || aligned(norm_w, 16));
   cudaError_t e = launch_rows_linear(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }
@@ -743,6 +744,7 @@ int m3_xdt_proj(int32_t rows, int32_t d_inner, int32_t n_x, int32_t dt_rank, con
   p.u = u; p.Wx = W_x; p.bx = b_x; p.Wdt = W_dt; p.x_dbl = x_dbl; p.dt = dt;
   p.rows = rows; p.D = d_inner; p.n_x = n_x; p.r = dt_rank;
   p.pdl = overlap != 0;
+  p.vec = aligned(u, 16);
   cudaError_t e = launch_xdt_proj(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? M3_OK : M3_ERR_LAUNCH;
 }

@@ -100,15 +100,30 @@ __device__ __forceinline__ float lane_row(const float (&acc)[RW], int lane) {
 
 // Stage RW rows of x into s (rows past `rows` read zero), RMS-normalised when
 // norm_w is given: x * rsqrt(mean(x^2) + eps) * w  (mamba.py:88-89).  NT: the
-// CTA's threads.
+// CTA's threads.  vec (x rows and norm_w 16-byte aligned): one 16-byte load
+// per thread and row, every row's load issued before any is used.
 template <int RW, int NT>
 __device__ void stage_rows(float* s, const float* x, long long ld_x, int rows, int K,
-                           const float* norm_w, float eps) {
+                           const float* norm_w, float eps, bool vec) {
   __shared__ float s_rstd[RW];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < RW * K; i += NT) {
-    const int r = i / K, k = i - r * K;
-    s[i] = r < rows ? x[(size_t)r * ld_x + k] : 0.f;
+  const int K4 = K >> 2;
+  float4* s4 = reinterpret_cast<float4*>(s);
+  if (vec) {
+    for (int k = tid; k < K4; k += NT) {
+      float4 v[RW];
+#pragma unroll
+      for (int r = 0; r < RW; ++r)
+        v[r] = r < rows ? reinterpret_cast<const float4*>(x + (size_t)r * ld_x)[k]
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < RW; ++r) s4[r * K4 + k] = v[r];
+    }
+  } else {
+    for (int i = tid; i < RW * K; i += NT) {
+      const int r = i / K, k = i - r * K;
+      s[i] = r < rows ? x[(size_t)r * ld_x + k] : 0.f;
+    }
   }
   __syncthreads();
   if (norm_w == nullptr) return;
@@ -119,9 +134,25 @@ __device__ void stage_rows(float* s, const float* x, long long ld_x, int rows, i
     if (lane == 0) s_rstd[r] = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), eps));
   }
   __syncthreads();
-  for (int i = tid; i < RW * K; i += NT) {
-    const int r = i / K, k = i - r * K;
-    s[i] = __fmul_rn(__fmul_rn(s[i], s_rstd[r]), norm_w[k]);
+  if (vec) {
+    for (int k = tid; k < K4; k += NT) {
+      const float4 w = reinterpret_cast<const float4*>(norm_w)[k];
+#pragma unroll
+      for (int r = 0; r < RW; ++r) {
+        float4 v = s4[r * K4 + k];
+        const float rs = s_rstd[r];
+        v.x = __fmul_rn(__fmul_rn(v.x, rs), w.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, rs), w.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, rs), w.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, rs), w.w);
+        s4[r * K4 + k] = v;
+      }
+    }
+  } else {
+    for (int i = tid; i < RW * K; i += NT) {
+      const int r = i / K, k = i - r * K;
+      s[i] = __fmul_rn(__fmul_rn(s[i], s_rstd[r]), norm_w[k]);
+    }
   }
   __syncthreads();
 }
@@ -140,7 +171,7 @@ __global__ void __launch_bounds__(kLinThreads) rows_linear_kernel(const RowsLine
   float4 a[kBatch];
   if (o0 < p.d_out) load_batch(p.W + (size_t)o0 * p.d_in, p.d_in >> 2, lane, a);
   pdl_wait();
-  stage_rows<RW, kLinThreads>(s_x, p.x, p.ld_x, p.rows, p.d_in, p.norm_w, p.eps);
+  stage_rows<RW, kLinThreads>(s_x, p.x, p.ld_x, p.rows, p.d_in, p.norm_w, p.eps, p.vec != 0);
   for (int o = o0; o < p.d_out; o += gridDim.x * kLinWarps) {
     if (o != o0) load_batch(p.W + (size_t)o * p.d_in, p.d_in >> 2, lane, a);
     float acc[RW];
@@ -174,7 +205,7 @@ __global__ void __launch_bounds__(kXdtThreads) xdt_proj_kernel(const XdtParams p
   float* s_raw = s_u + RW * p.D;
   pdl_launch_dependents();
   pdl_wait();
-  stage_rows<RW, kXdtThreads>(s_u, p.u, p.D, p.rows, p.D, nullptr, 0.f);
+  stage_rows<RW, kXdtThreads>(s_u, p.u, p.D, p.rows, p.D, nullptr, 0.f, p.vec != 0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float4 a[kBatch];
   for (int j = warp; j < p.r; j += kXdtWarps) {

@@ -225,6 +225,7 @@ struct RowsLinearParams {
   float* out1; long long ld1;
   int rows, d_in, d_out, split, silu;
   int pdl;                                    // programmatic dependent launch
+  int vec;                                    // x rows and norm_w 16-byte aligned
 };
 cudaError_t launch_rows_linear(const RowsLinearParams& p, cudaStream_t s);
 
@@ -237,6 +238,7 @@ struct XdtParams {
   float* dt;                                  // (rows, D)
   int rows, D, n_x, r;
   int pdl;                                    // programmatic dependent launch
+  int vec;                                    // u 16-byte aligned
 };
 cudaError_t launch_xdt_proj(const XdtParams& p, cudaStream_t s);
 

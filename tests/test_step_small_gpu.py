@@ -58,6 +58,21 @@ def test_rows_linear_matches_float64(rows, norm, bias, resid, split):
     assert torch.equal(out0, again[0])                    # deterministic
 
 
+@pytest.mark.parametrize("rows", [1, 5])
+def test_rows_linear_unaligned_rows_match_aligned(rows):
+    """Input rows that are not 16-byte aligned take the element-wise staging;
+    same bits as the vector staging of the same values."""
+    g = torch.Generator("cuda").manual_seed(11)
+    buf = torch.randn(rows, 513, device="cuda", generator=g)
+    x_un = buf[:, 1:]                                  # 4-byte offset, row stride 513
+    x_al = x_un.contiguous()
+    W = torch.randn(256, 512, device="cuda", generator=g) / 512 ** 0.5
+    nw = torch.rand(512, device="cuda", generator=g) + 0.5
+    a = S.m3_rows_linear(x_un, W, None, nw, 1e-5, split=128, silu=True)
+    b = S.m3_rows_linear(x_al, W, None, nw, 1e-5, split=128, silu=True)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
 def test_rows_linear_residual_in_place():
     g = torch.Generator("cuda").manual_seed(9)
     x = torch.randn(3, 256, device="cuda", generator=g)
